@@ -1,0 +1,411 @@
+"""Benchmark: the ACT policy step on N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One policy replica per GPU (requests are independent: "replicas only", no
+collective in the step loop). Each timed step is one captured CUDA graph
+(frame normalize -> int8 ResNet-18 -> token assembly -> 4 encoder layers ->
+decoder -> head) on device-resident inputs, timed with CUDA events on the
+launching stream; L2 is flushed (256 MiB memset, outside the events) between
+steps. `value` = chunks/s of the whole job = N*K / max over ranks of the summed
+step time. `e2e` = the same metric through the C ABI (vla_act_predict) with
+host frames/state/actions, copies included, wall clock.
+
+Extra fields: per-step latency p50/p95, the W8A8 GEMM alone at the ACT FFN
+shape (602x3200x512; TOPS cold and L2-warm) as the
+roofline of the dominant kernel, the reference's own CPU implementation timed
+on this host as `cpu_baseline`, and SM clocks sampled during the timed region.
+
+--impl reference times the reference's CPU implementation (oracle/_ref, the
+reference's unmodified sources built here; all host threads) on the same
+workload and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ACT policy throughput (chunks/s, bs1 per replica); p50 chunk latency; int8 GEMM TOPS"
+INT8_MASK = 63
+GEMM_SHAPE = (602, 3200, 512)          # ACT encoder FFN w1: M x N x K
+GEMM_OPS = 2 * 602 * 3200 * 512        # 1,972,633,600 int8 ops per call
+# compulsory bytes of one dense_linear_i8 call: x fp32 + W int8 + out fp32 + scales/bias
+GEMM_BYTES = 602 * 512 * 4 + 3200 * 512 + 602 * 3200 * 4 + 3200 * 8 + 602 * 4
+
+
+def _env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), \
+        int(os.environ.get("WORLD_SIZE", "1"))
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def _traffic():
+    """dram bytes per GEMM launch from the committed ncu summary (profiles/), if any."""
+    p = os.path.join(ROOT, "profiles", "gemm_ffn_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.f:
+            return None
+        self.f.seek(0)
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------- CPU side
+
+_CPU_CHILD = r"""
+import json, os, sys, time
+sys.path.insert(0, %(root)r)
+import numpy as np
+from vla_simd_b200 import synth
+kind, budget, max_steps = %(kind)r, %(budget)f, %(max_steps)d
+f, s = synth.act_inputs(synth.ACT_BASELINE, seed=1)
+from oracle import oracle
+r = oracle.reference()
+if r is None:
+    print(json.dumps({"unavailable": "oracle/_ref/libvla_ref.so (the reference's own build) not present"}))
+    sys.exit(0)
+l = r.l
+h = l.vla_act_load(%(ckpt)r.encode())
+out = np.zeros((100, 6), np.float32)
+P = lambda a: a.ctypes.data_as(__import__("ctypes").c_void_p)
+for _ in range(2):
+    l.vla_act_predict(h, P(f), P(s), 1, P(out))
+times = []
+t_end = time.perf_counter() + budget
+while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+    t0 = time.perf_counter()
+    rc = l.vla_act_predict(h, P(f), P(s), 1, P(out))
+    times.append(time.perf_counter() - t0)
+    assert rc == 0
+l.vla_act_free(h)
+print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * float(np.median(times))}))
+"""
+
+
+def time_reference_cpu(ckpt: str, budget_s: float, max_steps: int):
+    """The reference's own ACT step (oracle/_ref) in a fresh process with all host cores."""
+    cores = cpu_cores()
+    env = dict(os.environ, ACT_INT8=str(INT8_MASK), OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close",
+               CUDA_VISIBLE_DEVICES="")
+    code = _CPU_CHILD % {"root": ROOT, "kind": "reference", "budget": budget_s, "max_steps": max_steps,
+                         "ckpt": ckpt}
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        return {"unavailable": f"reference CPU run failed: {r.stderr.strip().splitlines()[-1:]}"}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    if "unavailable" in d:
+        return d
+    d["cores"] = cores
+    d["chunks_per_s"] = d["steps"] / d["seconds"]
+    return d
+
+
+# ----------------------------------------------------------------- GPU side
+
+def time_gemm(torch, dev):
+    """The dominant op alone: quantize + tcgen05 W8A8 GEMM at the ACT FFN shape."""
+    from vla_simd_b200 import ops
+    M, N, K = GEMM_SHAPE
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to(dev)
+    W = torch.from_numpy((rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)).to(dev)
+    b = torch.from_numpy((rng.standard_normal(N, dtype=np.float32) * 0.01).astype(np.float32)).to(dev)
+    wq, ws = ops.pack_weights_i8(W)
+    xq, xs = ops.quantize_act_i8(x)
+    out = torch.empty((M, N), device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream()
+
+    def gemm():
+        ops.gemm_i8(xq, xs, wq, ws, K, bias=b, out=out)
+
+    for _ in range(10):
+        gemm()
+    # cold: L2 flushed before each launch
+    cold = []
+    for _ in range(50):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        gemm()
+        e1.record(st)
+        e1.synchronize()
+        cold.append(e0.elapsed_time(e1) * 1e-3)
+    # L2-warm: 200 back-to-back launches captured in one graph
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(200):
+            gemm()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(5):
+        g.replay()
+    e1.record(st)
+    e1.synchronize()
+    warm = e0.elapsed_time(e1) * 1e-3 / 1000
+    # fused quantize + GEMM (dense_linear_i8 entry point), cold
+    lin = []
+    for _ in range(30):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        ops.dense_linear_i8(x, wq, ws, b)
+        e1.record(st)
+        e1.synchronize()
+        lin.append(e0.elapsed_time(e1) * 1e-3)
+    del g
+    tc = statistics.median(cold)
+    return {"shape": "602x3200x512 (M x N x K)", "us_cold": tc * 1e6, "us_l2_warm": warm * 1e6,
+            "tops_cold": GEMM_OPS / tc / 1e12, "tops_l2_warm": GEMM_OPS / warm / 1e12,
+            "dense_linear_i8_us_cold": statistics.median(lin) * 1e6}
+
+
+def run_ours(args):
+    import torch
+    rank, local_rank, world = _env_rank()
+    os.environ["VLA_CUDA_DEVICE"] = str(local_rank)
+    os.environ["ACT_INT8"] = str(INT8_MASK)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from vla_simd_b200 import ActPolicy, synth
+
+    ckpt_root = tempfile.mkdtemp(prefix="vla_act_")
+    ckpt = synth.write_act_checkpoint(os.path.join(ckpt_root, "act"), synth.ACT_BASELINE, seed=0)
+    pol = ActPolicy(ckpt)
+    frames, state = synth.act_inputs(synth.ACT_BASELINE, seed=1 + rank)
+    # one C-ABI call leaves this observation resident in the policy's device
+    # input buffers; the timed steps then run on device-resident inputs
+    pol.predict(frames, state)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        pol.enqueue(stream.cuda_stream)
+    torch.cuda.synchronize()
+    kernels = pol.kernels_per_step
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            starts[i].record(stream)
+            pol.enqueue(stream.cuda_stream)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    step_s = [s.elapsed_time(e) * 1e-3 for s, e in zip(starts, ends)]
+    total = sum(step_s)
+    if dist:
+        t = torch.tensor([total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_max = float(t.item())
+    else:
+        total_max = total
+    value = world * args.steps / total_max
+
+    # e2e through the C ABI with host buffers (copies inside), wall clock
+    n_e2e = max(args.steps, 10)
+    for _ in range(3):
+        pol.predict(frames, state)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        pol.predict(frames, state)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * n_e2e / e2e_s, "unit": "chunks/s", "h2d_bytes_per_step": frames.nbytes + state.nbytes,
+           "d2h_bytes_per_step": 100 * 6 * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
+           "path": "vla_act_predict (C ABI), host uint8 frames + state -> host actions"}
+
+    gemm = time_gemm(torch, dev) if rank == 0 else None
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = time_reference_cpu(ckpt, budget_s=args.cpu_budget, max_steps=40)
+    pol.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    bf16_peak, hbm_peak, peak_kind = _peaks()
+    int8_peak = 2.0 * bf16_peak   # dense int8 runs at 2x the dense bf16 rate on B200
+    achieved = gemm["tops_l2_warm"]
+    roofline = {"kernel": "w8a8_umma_kernel (ACT FFN 602x3200x512, L2-warm, back-to-back)", "bound": "tensor",
+                "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS (int8)",
+                "frac": round(achieved / int8_peak, 4),
+                "peak_note": f"2x {peak_kind} bf16 dense ({bf16_peak} TFLOP/s, MEASURED_PEAKS.json)",
+                "traffic": _traffic(),
+                "cold": {"achieved_tops": round(gemm["tops_cold"], 2),
+                         "hbm_bound_us": round(GEMM_BYTES / (hbm_peak * 1e9) * 1e6, 3),
+                         "us": round(gemm["us_cold"], 3)}}
+    cpu_baseline = None
+    if cpu and "unavailable" not in cpu:
+        cpu_baseline = {"value": round(cpu["chunks_per_s"], 3), "unit": "chunks/s", "cores": cpu["cores"],
+                        "kind": "reference", "p50_ms": round(cpu["p50_ms"], 2),
+                        "sample": f"{cpu['steps']} ACT steps (same checkpoint, ACT_INT8=63) of the reference's "
+                                  f"own vla_act_predict, OMP_NUM_THREADS={cpu['cores']}"}
+    elif cpu:
+        cpu_baseline = {"unavailable": cpu["unavailable"]}
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
+        "data": "synthetic (seeded random-init ACT weights, uniform uint8 frames, N(0,1) state)",
+        "config": {"workload": "ACT policy step, BASELINE configs[1]: 2x480x640 uint8 frames -> ResNet-18 -> "
+                               "602-token 4-layer encoder, 1-layer decoder, 100x6 actions; bs1 per GPU",
+                   "int8_mask": INT8_MASK, "parallelism": f"replicas x{world} (no collective)",
+                   "l2": "flushed between steps (256 MiB memset outside the timed events)"},
+        "latency_ms": {"p50": round(1e3 * statistics.median(step_s), 4),
+                       "p95": round(1e3 * float(np.percentile(step_s, 95)), 4)},
+        "int8_gemm": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in gemm.items()},
+        "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
+        "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """Reference arm: the reference's own CPU implementation on this host (rank 0 only)."""
+    rank, _, world = _env_rank()
+    if rank != 0:
+        return
+    from vla_simd_b200 import synth
+    ckpt_root = tempfile.mkdtemp(prefix="vla_act_ref_")
+    ckpt = synth.write_act_checkpoint(os.path.join(ckpt_root, "act"), synth.ACT_BASELINE, seed=0)
+    steps = args.steps
+    cpu = time_reference_cpu(ckpt, budget_s=max(10.0, args.cpu_budget), max_steps=steps)
+    if "unavailable" in cpu:
+        print(json.dumps({"impl": "reference", "unavailable": cpu["unavailable"]}), flush=True)
+        return
+    v = cpu["chunks_per_s"]
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "chunks/s", "n_gpus": world,
+        "steps": cpu["steps"], "warmup": 2, "ms_per_step": round(1e3 * cpu["seconds"] / cpu["steps"], 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8) + fp32 (CPU)",
+        "data": "synthetic (seeded random-init ACT weights)",
+        "config": {"workload": "ACT policy step, BASELINE configs[1] (same checkpoint and inputs as ours)",
+                   "int8_mask": INT8_MASK, "parallelism": "CPU, OpenMP over all host cores"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "chunks/s", "cores": cpu["cores"], "kind": "reference",
+                         "sample": f"{cpu['steps']} steps of vla_act_predict from oracle/_ref"},
+        "e2e": {"value": round(v, 3), "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "latency_ms": {"p50": round(cpu["p50_ms"], 3)},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU steps")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

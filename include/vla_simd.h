@@ -1,0 +1,84 @@
+/*
+ * vla_simd.h - model-level C ABI of libvla_simd_b200.so, the B200 (sm_100a)
+ * backend of vla.simd. Same symbols, argument order and contracts as the
+ * reference's include/vla_simd.h, so its ctypes callers
+ * (vla_simd/policy_server.py:181-262, ActEngine at :276-307) load this library
+ * unchanged.
+ *
+ * Ownership
+ *   vla_act_load pairs with vla_act_free. Every other pointer - frames, state,
+ *   the actions output - is caller-owned HOST memory, borrowed for the duration
+ *   of the call. Weights live on the GPU from load to free.
+ *
+ * Errors
+ *   Fallible calls return vla_status (0 == VLA_OK); _load returns NULL. C++
+ *   exceptions never cross the boundary. CUDA failures (including a kernel's
+ *   bounded wait running out) are reported as VLA_ERR_DEVICE, a code this
+ *   backend appends after the reference's three.
+ *
+ * Threading
+ *   One handle is one inference at a time (it owns a stream, scratch buffers
+ *   and a captured CUDA graph). Load one handle per GPU for data parallelism;
+ *   VLA_CUDA_DEVICE (or the calling thread's current device) picks the GPU.
+ *
+ * Precision
+ *   ACT_INT8 selects the W8A8 layers exactly as in the reference
+ *   (1 enc attention, 2 enc w1, 4 enc w2, 8 image projection, 16 decoder,
+ *   32 backbone convs; ACT_I8_CONV_FROM / ACT_I8_CONV_TO, TCPU_I8_CLIP).
+ */
+
+#ifndef VLA_SIMD_H
+#define VLA_SIMD_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VLA_API __attribute__((visibility("default")))
+
+/* Kept at the reference's value: the additions below are new codes only, so a
+ * caller that checks vla_abi_version() == 1 (the reference server does) binds. */
+#define VLA_ABI_VERSION 1
+
+typedef enum {
+    VLA_OK            =  0,
+    VLA_ERR_ARG       = -1,  /* NULL handle, NULL buffer, or an out-of-range dimension */
+    VLA_ERR_SHAPE     = -2,  /* an argument disagrees with the loaded checkpoint */
+    VLA_ERR_EXCEPTION = -3,  /* a C++ exception was caught at the boundary */
+    VLA_ERR_DEVICE    = -4   /* a CUDA call or kernel failed (this backend only) */
+} vla_status;
+
+/* replaces reference include/vla_simd.h:60-62 (src/capi_version.cpp:14-15) */
+VLA_API int32_t vla_abi_version(void);
+VLA_API const char* vla_backend_name(void);   /* "cuda-sm100a" */
+VLA_API int32_t vla_int8_available(void);      /* 1 when an sm_100 device is visible */
+
+/* ---------------------------------------------------------------- ACT -----
+ * replaces reference include/vla_simd.h:66-81 (src/models/act/act_capi.cpp:20-54).
+ * model_dir: a converter directory (config.txt, backbone.meta/.bin, act.meta/.bin,
+ * stats.bin) as written by the reference's tools/convert_act.py. */
+
+VLA_API void* vla_act_load(const char* model_dir);
+VLA_API void  vla_act_free(void* h);
+
+/* 0 on a NULL handle. */
+VLA_API int32_t vla_act_chunk(void* h);
+VLA_API int32_t vla_act_action_dim(void* h);
+VLA_API int32_t vla_act_state_dim(void* h);
+VLA_API int32_t vla_act_n_cams(void* h);
+VLA_API int32_t vla_act_img_h(void* h);
+VLA_API int32_t vla_act_img_w(void* h);
+
+/* images: n_cams frames back to back, uint8 HWC at img_h x img_w, in the
+ * checkpoint's camera order. state [state_dim] in raw robot units.
+ * actions out [chunk*action_dim]. */
+VLA_API int32_t vla_act_predict(void* h, const uint8_t* images, const float* state,
+                                int32_t unnormalize, float* actions);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VLA_SIMD_H */

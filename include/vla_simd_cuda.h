@@ -1,0 +1,146 @@
+/*
+ * vla_simd_cuda.h - op-level C ABI of libvla_simd_b200.so: the B200 kernels
+ * behind the reference's portable op API (src/ops/quant_ops.h, lm_ops.h,
+ * conv_ops.h), so a TCPU_HAL_CUDA backend of the reference can define its
+ * tcpu:: functions on top of these.
+ *
+ * Two families:
+ *   vla_cuda_*  DEVICE pointers, an explicit cudaStream_t (passed as void*),
+ *               asynchronous; return vla_status (vla_simd.h).
+ *   vla_tcpu_*  HOST pointers with exactly the reference's tcpu:: argument
+ *               lists; synchronous (copy in, compute on the GPU, copy out).
+ *
+ * Device layout. Quantized activations and weights are row-major int8 with a
+ * leading dimension (bytes) that is a multiple of 16 (the TMA stride rule);
+ * vla_cuda_i8_ld(K) gives the smallest one. Bytes past K in a row are ignored
+ * by the GEMMs. The reference's CPU panel layout [N/16][Kp/4][16][4] exists
+ * only in the vla_tcpu_* shims.
+ *
+ * Numerics (all bit-identical to the reference CPU code on identical inputs):
+ *   scale = amax > 0 ? max(amax/127, FLT_MIN) : 1;  q = clamp(rne(x/scale*...), +-127)
+ *   out   = fma((float)acc * wscale[n], ascale[m], bias[n])
+ */
+
+#ifndef VLA_SIMD_CUDA_H
+#define VLA_SIMD_CUDA_H
+
+#include <stdint.h>
+#include "vla_simd.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Epilogue modes of vla_cuda_gemm_i8 (bit flags). */
+#define VLA_EPI_RELU      1   /* v < 0 ? 0 : v                       (tcpu::relu) */
+#define VLA_EPI_ADD       2   /* out = res + v                        (residual add) */
+#define VLA_EPI_ADD_RELU  4   /* v = v + res; v > 0 ? v : 0           (ResNet block tail) */
+#define VLA_EPI_ACC       8   /* write the raw int32 accumulators (out is int32_t*) */
+
+/* Smallest valid int8 row stride for K columns: K rounded up to 16. */
+VLA_API int64_t vla_cuda_i8_ld(int32_t K);
+
+/* Read and clear the device status word: 0 OK, 1 a kernel's bounded wait ran
+ * out (the kernel returned early), <0 the word could not be read. */
+VLA_API int32_t vla_cuda_device_status(void);
+
+/* replaces tcpu::quantize_act_i8 (src/ops/quant_ops.h:76):
+ * x [seq][K] fp32 -> xq [seq][ldq] int8 (zero past K) + ascale [seq]. */
+VLA_API int32_t vla_cuda_quantize_act_i8(const float* x, int8_t* xq, float* ascale,
+                                         int32_t seq, int32_t K, int64_t ldq, void* stream);
+
+/* replaces tcpu::pack_weights_i8 (src/ops/quant_ops.h:58) in the device layout:
+ * W [N][K] fp32 (device) -> Wq [N][ldw] int8 + wscale [N]. Same per-row math as
+ * the activation quantizer. */
+VLA_API int32_t vla_cuda_pack_weights_i8(const float* W, int8_t* Wq, float* wscale,
+                                         int32_t N, int32_t K, int64_t ldw, void* stream);
+
+/* replaces tcpu::dense_linear_i8_pre (src/ops/quant_ops.h:83-85):
+ * out [seq][N] = dequant(xq [seq][ldx] . Wq [N][ldw]^T) + bias. */
+VLA_API int32_t vla_cuda_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale,
+                                             const int8_t* Wq, const float* wscale, const float* bias,
+                                             int32_t seq, int32_t N, int32_t K,
+                                             int64_t ldx, int64_t ldw, void* stream);
+
+/* replaces tcpu::dense_linear_i8 (src/ops/quant_ops.h:69-71): quantize x per
+ * token into the caller-owned scratch (xq [seq][vla_cuda_i8_ld(K)], ascale
+ * [seq]), then the W8A8 GEMM. */
+VLA_API int32_t vla_cuda_dense_linear_i8(float* out, const float* x, const int8_t* Wq,
+                                         const float* wscale, const float* bias,
+                                         int32_t seq, int32_t N, int32_t K, int64_t ldw,
+                                         int8_t* xq_scratch, float* ascale_scratch, void* stream);
+
+/* The W8A8 GEMM with every option exposed (nn::Linear::forward / forward_add
+ * and the conv epilogues, src/nn/linear.cpp:121-185). ascale_per_row = 0 uses
+ * ascale[0] for every row. res/ldr feed VLA_EPI_ADD / VLA_EPI_ADD_RELU (res
+ * may alias out). amax (optional, zeroed by the caller) receives atomicMax of
+ * |out| as float bits, slot m / amax_rows. force_simt = 1 takes the CUDA-core
+ * kernel instead of the tensor-core one (same results). */
+VLA_API int32_t vla_cuda_gemm_i8(void* out, int64_t ldo, const int8_t* xq, int64_t ldx,
+                                 const float* ascale, int32_t ascale_per_row,
+                                 const int8_t* Wq, int64_t ldw, const float* wscale,
+                                 const float* bias, const float* res, int64_t ldr,
+                                 int32_t M, int32_t N, int32_t K, int32_t mode,
+                                 uint32_t* amax, int32_t amax_rows, int32_t force_simt,
+                                 void* stream);
+
+/* replaces tcpu::conv2d_i8 (src/ops/conv_ops.h, src/hal/common/conv.cpp:468-526)
+ * for F NHWC frames at once: per-frame per-tensor activation scale
+ * (absmax * clip / 127, TCPU_I8_CLIP semantics), int8 im2col, W8A8 GEMM.
+ * Wq [Cout][ldw] with K = k*k*Cin in (ky, kx, ci) order. Scratch (caller-owned):
+ * col [F*Ho*Wo][ldw] int8, rscale [F*Ho*Wo], amax [F] (zeroed here).
+ * mode/res as vla_cuda_gemm_i8 (ld of res = Cout). */
+VLA_API int32_t vla_cuda_conv2d_i8(float* out, const float* x, int32_t F, int32_t H, int32_t W,
+                                   int32_t Cin, const int8_t* Wq, int64_t ldw, const float* wscale,
+                                   const float* bias, int32_t Cout, int32_t k, int32_t stride,
+                                   int32_t pad, float clip, int32_t mode, const float* res,
+                                   int8_t* col_scratch, float* rscale_scratch, uint32_t* amax_scratch,
+                                   void* stream);
+
+/* replaces tcpu::layernorm (src/hal/common/norms.cpp:69-97); out may alias x. */
+VLA_API int32_t vla_cuda_layernorm(float* out, const float* x, const float* w, const float* b,
+                                   int32_t seq, int32_t hidden, float eps, void* stream);
+
+/* replaces tcpu::gqa_attention_masked / gqa_attention_dense (src/ops/lm_ops.h:21-35):
+ * Q [seq_q][n_q*head_dim], K/V [seq_k][n_kv*head_dim], out [seq_q][n_q*head_dim];
+ * mask [seq_q][seq_k] additive or NULL (dense). head_dim must be 64. */
+VLA_API int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* K, const float* V,
+                                       int32_t seq_q, int32_t seq_k, int32_t n_q, int32_t n_kv,
+                                       int32_t head_dim, float scale, const float* mask, void* stream);
+
+/* replaces tcpu::maxpool2d_relu (src/hal/common/conv.cpp:192-225), F frames. */
+VLA_API int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H, int32_t W,
+                                        int32_t C, int32_t k, int32_t stride, int32_t pad, void* stream);
+
+/* ------------------------------------------------ host-pointer tcpu shims */
+
+VLA_API int32_t vla_tcpu_int8_gemm_available(void);          /* src/ops/quant_ops.h:41 */
+VLA_API int32_t vla_tcpu_i8_kpad(int32_t K);                 /* :45 */
+VLA_API uint64_t vla_tcpu_packed_i8_words(int32_t N, int32_t K); /* :57 */
+/* :58, the reference's CPU panel layout + int32 row sums (load time, host) */
+VLA_API int32_t vla_tcpu_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K);
+/* :76 */
+VLA_API int32_t vla_tcpu_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int32_t seq, int32_t K);
+/* :83-85, Wq in the panel layout */
+VLA_API int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale,
+                                             const int8_t* Wq, const float* wscale, const float* bias,
+                                             int32_t seq, int32_t N, int32_t K);
+/* :69-71 */
+VLA_API int32_t vla_tcpu_dense_linear_i8(float* out, const float* x, const int8_t* Wq, const float* wscale,
+                                         const float* bias, int32_t seq, int32_t N, int32_t K,
+                                         int8_t* xq_scratch, float* ascale_scratch);
+
+/* ------------------------------------------- device-resident ACT stepping
+ * For throughput runs: inputs written straight into the handle's device
+ * buffers, the captured step enqueued on a caller stream, no host copies. */
+VLA_API int32_t vla_act_device_buffers(void* h, uint8_t** images, float** state, const float** actions);
+VLA_API int32_t vla_act_enqueue(void* h, void* stream, int32_t unnormalize);
+/* kernels in one captured step (0 before the first predict/enqueue) */
+VLA_API int32_t vla_act_kernels_per_step(void* h);
+VLA_API int32_t vla_act_int8_layers(void* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VLA_SIMD_CUDA_H */

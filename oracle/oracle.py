@@ -1,0 +1,260 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes loaders for the two CPU oracles.
+
+* ``restated()`` - this repository's C restatement of the reference's int8
+  algorithm (oracle/i8_oracle.c -> oracle/_build/libi8_oracle.so).
+* ``reference()`` - the reference's own sources compiled by oracle/Makefile
+  (oracle/_ref/libvla_ref.so): its tcpu:: int8 / attention / norm / conv ops
+  through ref_shim.cpp, and its full vla_act_* C ABI.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module; the library never does. The xorshift generator below restates the
+reference test's RNG (tests/test_ops.cpp:31-40) so parity cases use the same
+inputs as the reference's own op tests.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+RESTATED_SO = os.path.join(HERE, "_build", "libi8_oracle.so")
+REFERENCE_SO = os.path.join(HERE, "_ref", "libvla_ref.so")
+
+VP, I32, I64, F32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def build(reference: bool | None = None) -> None:
+    """make the restatement (always) and the reference build (when its sources exist)."""
+    targets = ["oracle"]
+    if reference is None:
+        reference = os.path.isdir(os.environ.get("VLA_REF_DIR", "/root/reference"))
+    if reference:
+        targets.append("ref")
+    env = dict(os.environ)
+    if "VLA_REF_DIR" in env:
+        env["REF"] = env["VLA_REF_DIR"]
+    subprocess.run(["make", "-s", "-j8", "-C", HERE, *targets], check=True, env=env)
+
+
+class Restated:
+    def __init__(self):
+        if not os.path.exists(RESTATED_SO):
+            build(reference=False)
+        l = ctypes.CDLL(RESTATED_SO)
+        l.or_i8_kpad.restype = I32
+        l.or_i8_kpad.argtypes = [I32]
+        l.or_row_scale.restype = F32
+        l.or_row_scale.argtypes = [F32]
+        l.or_quantize_rows.argtypes = [VP, I32, I32, VP, I64, VP]
+        l.or_pack_weights_i8.argtypes = [VP, VP, VP, I32, I32]
+        l.or_gemm_i8_acc.argtypes = [VP, VP, I64, VP, I64, I32, I32, I32]
+        l.or_dense_linear_i8_ref.argtypes = [VP, VP, I64, VP, VP, I64, VP, VP, I32, I32, I32]
+        l.or_quantize_span_i8.argtypes = [VP, VP, ctypes.c_size_t, F32]
+        l.or_tensor_scale.restype = F32
+        l.or_tensor_scale.argtypes = [VP, ctypes.c_size_t, F32]
+        l.or_conv2d_i8.argtypes = [VP, VP, VP, I64, VP, VP, I32, I32, I32, I32, I32, I32, I32, F32, VP, VP]
+        self.l = l
+
+    def quantize_rows(self, x, ld=None):
+        x = np.ascontiguousarray(x, np.float32)
+        rows, K = x.shape
+        ld = ld or K
+        q = np.zeros((rows, ld), np.int8)
+        s = np.zeros(rows, np.float32)
+        self.l.or_quantize_rows(_ptr(x), rows, K, _ptr(q), ld, _ptr(s))
+        return q, s
+
+    def pack_weights_panels(self, W):
+        W = np.ascontiguousarray(W, np.float32)
+        N, K = W.shape
+        Kp = self.l.or_i8_kpad(K)
+        buf = np.zeros(N * Kp + 4 * N, np.int8)
+        s = np.zeros(N, np.float32)
+        self.l.or_pack_weights_i8(_ptr(W), _ptr(buf), _ptr(s), N, K)
+        return buf, s
+
+    def gemm_acc(self, xq, wq, K):
+        M, N = xq.shape[0], wq.shape[0]
+        acc = np.zeros((M, N), np.int32)
+        self.l.or_gemm_i8_acc(_ptr(acc), _ptr(np.ascontiguousarray(xq)), xq.shape[1],
+                              _ptr(np.ascontiguousarray(wq)), wq.shape[1], M, N, K)
+        return acc
+
+    def dense_linear_i8_ref(self, xq, ascale, wq, wscale, bias, K):
+        M, N = xq.shape[0], wq.shape[0]
+        out = np.zeros((M, N), np.float32)
+        self.l.or_dense_linear_i8_ref(_ptr(out), _ptr(np.ascontiguousarray(xq)), xq.shape[1],
+                                      _ptr(np.ascontiguousarray(ascale, np.float32)),
+                                      _ptr(np.ascontiguousarray(wq)), wq.shape[1],
+                                      _ptr(np.ascontiguousarray(wscale, np.float32)),
+                                      _ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)), M, N, K)
+        return out
+
+    def conv2d_i8(self, x, wq, wscale, bias, Cout, k, stride, pad, clip=1.0):
+        x = np.ascontiguousarray(x, np.float32)
+        H, W, Cin = x.shape
+        Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+        out = np.zeros((Ho, Wo, Cout), np.float32)
+        xs = np.zeros(H * W * Cin, np.int8)
+        rs = np.zeros(k * k * Cin, np.int8)
+        self.l.or_conv2d_i8(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(wq)), wq.shape[1],
+                            _ptr(np.ascontiguousarray(wscale, np.float32)),
+                            _ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                            H, W, Cin, Cout, k, stride, pad, clip, _ptr(xs), _ptr(rs))
+        return out
+
+
+class Reference:
+    def __init__(self):
+        if not os.path.exists(REFERENCE_SO):
+            raise FileNotFoundError(REFERENCE_SO)
+        l = ctypes.CDLL(REFERENCE_SO)
+        l.ref_int8_gemm_available.restype = I32
+        l.ref_i8_kpad.restype = I32
+        l.ref_i8_kpad.argtypes = [I32]
+        l.ref_packed_i8_words.restype = ctypes.c_ulonglong
+        l.ref_packed_i8_words.argtypes = [I32, I32]
+        l.ref_pack_weights_i8.argtypes = [VP, VP, VP, I32, I32]
+        l.ref_quantize_act_i8.argtypes = [VP, VP, VP, I32, I32]
+        l.ref_dense_linear_i8.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, VP, VP]
+        l.ref_dense_linear_i8_pre.argtypes = [VP, VP, VP, VP, VP, VP, I32, I32, I32]
+        l.ref_dense_linear_i8_ref.argtypes = [VP, VP, VP, VP, VP, VP, I32, I32, I32]
+        l.ref_conv2d_i8.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, I32]
+        l.ref_layernorm.argtypes = [VP, VP, VP, VP, I32, I32, F32]
+        l.ref_gqa_attention_masked.argtypes = [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP]
+        l.ref_maxpool2d_relu.argtypes = [VP, VP, I32, I32, I32, I32, I32, I32]
+        l.ref_relu.argtypes = [VP, I32]
+        l.vla_act_load.restype = VP
+        l.vla_act_load.argtypes = [ctypes.c_char_p]
+        l.vla_act_free.argtypes = [VP]
+        for n in ("chunk", "action_dim", "state_dim", "n_cams", "img_h", "img_w"):
+            getattr(l, f"vla_act_{n}").restype = I32
+            getattr(l, f"vla_act_{n}").argtypes = [VP]
+        l.vla_act_predict.restype = I32
+        l.vla_act_predict.argtypes = [VP, VP, VP, I32, VP]
+        self.l = l
+
+    def kpad(self, K):
+        return self.l.ref_i8_kpad(K)
+
+    def pack_weights_i8(self, W):
+        W = np.ascontiguousarray(W, np.float32)
+        N, K = W.shape
+        words = self.l.ref_packed_i8_words(N, K)
+        buf = np.zeros(words * 4, np.int8)
+        s = np.zeros(N, np.float32)
+        self.l.ref_pack_weights_i8(_ptr(W), _ptr(buf), _ptr(s), N, K)
+        return buf, s
+
+    def quantize_act_i8(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        seq, K = x.shape
+        q = np.zeros((seq, self.kpad(K)), np.int8)
+        s = np.zeros(seq, np.float32)
+        self.l.ref_quantize_act_i8(_ptr(x), _ptr(q), _ptr(s), seq, K)
+        return q, s
+
+    def dense_linear_i8_ref(self, xq, ascale, panels, wscale, bias, N, K):
+        seq = xq.shape[0]
+        out = np.zeros((seq, N), np.float32)
+        self.l.ref_dense_linear_i8_ref(_ptr(out), _ptr(np.ascontiguousarray(xq)), _ptr(ascale), _ptr(panels),
+                                       _ptr(wscale), _ptr(bias), seq, N, K)
+        return out
+
+    def dense_linear_i8(self, x, panels, wscale, bias, N):
+        x = np.ascontiguousarray(x, np.float32)
+        seq, K = x.shape
+        out = np.zeros((seq, N), np.float32)
+        xq = np.zeros((seq, self.kpad(K)), np.int8)
+        s = np.zeros(seq, np.float32)
+        self.l.ref_dense_linear_i8(_ptr(out), _ptr(x), _ptr(panels), _ptr(wscale), _ptr(bias), seq, N, K, _ptr(xq),
+                                   _ptr(s))
+        return out
+
+    def conv2d_i8(self, x, panels, wscale, bias, Cout, k, stride, pad):
+        x = np.ascontiguousarray(x, np.float32)
+        H, W, Cin = x.shape
+        Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+        out = np.zeros((Ho, Wo, Cout), np.float32)
+        self.l.ref_conv2d_i8(_ptr(out), _ptr(x), _ptr(panels), _ptr(wscale), _ptr(bias), H, W, Cin, Cout, k, stride,
+                             pad)
+        return out
+
+    def layernorm(self, x, w, b, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        self.l.ref_layernorm(_ptr(out), _ptr(x), _ptr(w), _ptr(b), x.shape[0], x.shape[1], eps)
+        return out
+
+    def attention(self, Q, K, V, n_q, n_kv, head_dim, scale, mask=None):
+        seq_q, seq_k = Q.shape[0], K.shape[0]
+        out = np.zeros((seq_q, n_q * head_dim), np.float32)
+        self.l.ref_gqa_attention_masked(_ptr(out), _ptr(np.ascontiguousarray(Q)), _ptr(np.ascontiguousarray(K)),
+                                        _ptr(np.ascontiguousarray(V)), seq_q, seq_k, n_q, n_kv, head_dim, scale,
+                                        _ptr(mask))
+        return out
+
+    def maxpool2d_relu(self, x, k=3, stride=2, pad=1):
+        x = np.ascontiguousarray(x, np.float32)
+        H, W, C = x.shape
+        Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+        out = np.zeros((Ho, Wo, C), np.float32)
+        self.l.ref_maxpool2d_relu(_ptr(out), _ptr(x), H, W, C, k, stride, pad)
+        return out
+
+    # --- policy level (the reference's own vla_act_* ABI)
+    def act_predict(self, model_dir, frames, state, unnormalize=True):
+        h = self.l.vla_act_load(model_dir.encode())
+        if not h:
+            raise RuntimeError("reference vla_act_load failed")
+        try:
+            chunk, ad = self.l.vla_act_chunk(h), self.l.vla_act_action_dim(h)
+            out = np.zeros((chunk, ad), np.float32)
+            fr = np.ascontiguousarray(frames, np.uint8)
+            st = np.ascontiguousarray(state, np.float32)
+            rc = self.l.vla_act_predict(h, _ptr(fr), _ptr(st), 1 if unnormalize else 0, _ptr(out))
+            if rc != 0:
+                raise RuntimeError(f"reference vla_act_predict rc={rc}")
+            return out
+        finally:
+            self.l.vla_act_free(h)
+
+
+def restated() -> Restated:
+    return Restated()
+
+
+def reference() -> Reference | None:
+    """The compiled reference, or None when oracle/_ref was not built here."""
+    try:
+        return Reference()
+    except (FileNotFoundError, OSError):
+        return None
+
+
+class XorShift:
+    """The reference op tests' generator (tests/test_ops.cpp:31-35): 24-bit uniform floats."""
+
+    def __init__(self, seed: int = 0x243F6A8885A308D3):
+        self.state = seed & 0xFFFFFFFFFFFFFFFF
+
+    def uniform(self, n: int, lo: float = -1.0, hi: float = 1.0) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        s = self.state
+        M = 0xFFFFFFFFFFFFFFFF
+        lo32, span = np.float32(lo), np.float32(hi) - np.float32(lo)
+        for i in range(n):
+            s ^= (s << 13) & M
+            s ^= s >> 7
+            s ^= (s << 17) & M
+            r = np.float32((s >> 40) & 0xFFFFFF) / np.float32(16777216.0)
+            out[i] = lo32 + span * r
+        self.state = s
+        return out

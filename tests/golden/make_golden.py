@@ -1,0 +1,105 @@
+"""Regenerate the committed golden fixtures from the reference's OWN code.
+
+Needs oracle/_ref/libvla_ref.so (oracle/Makefile builds it from the reference
+checkout). Run from the repo root:  python tests/golden/make_golden.py
+
+* act_<cfg>_m<mask>.npy  - actions [chunk, action_dim] of the reference's
+  vla_act_predict (ACT_INT8=<mask>) on synth.write_act_checkpoint(seed=0) with
+  synth.act_inputs(seed=1); cfg small = synth.ACT_SMALL, base = ACT_BASELINE.
+* checkpoints.json       - sha256 of each synthetic checkpoint directory, so a
+  test notices if the writer ever stops reproducing the bytes the fixtures
+  were made from.
+* gemm.npz / gemm.json   - W8A8 linear cases (default_rng inputs): for small
+  shapes the full xq / ascale / int32 accumulators / fp32 outputs, for the
+  rest their sha256, all from the reference's quantize_act_i8,
+  pack_weights_i8 and dense_linear_i8_ref.
+"""
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle import oracle  # noqa: E402
+from vla_simd_b200 import synth  # noqa: E402
+
+ACT_CASES = [("small", synth.ACT_SMALL, 63), ("small", synth.ACT_SMALL, 0), ("small", synth.ACT_SMALL, 31),
+             ("small", synth.ACT_SMALL, 40), ("base", synth.ACT_BASELINE, 63)]
+GEMM_SHAPES = [(1, 16, 3), (7, 48, 64), (13, 64, 17), (257, 96, 48), (50, 768, 1027), (602, 3200, 512),
+               (602, 512, 3200), (300, 512, 512)]
+
+
+def dir_digest(d):
+    h = hashlib.sha256()
+    for name in sorted(os.listdir(d)):
+        h.update(name.encode())
+        with open(os.path.join(d, name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def gemm_inputs(seq, N, K, seed=11):
+    rng = np.random.default_rng(seed + seq * 7 + N * 13 + K)
+    x = rng.standard_normal((seq, K), dtype=np.float32)
+    W = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    b = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    return x, W, b
+
+
+def main():
+    ref = oracle.reference()
+    if ref is None:
+        sys.exit("oracle/_ref/libvla_ref.so missing: make -C oracle ref")
+    digests = {}
+    for cfg, shape, mask in ACT_CASES:
+        # the reference reads ACT_INT8 when it loads, so each mask runs in its own process
+        with tempfile.TemporaryDirectory() as d:
+            synth.write_act_checkpoint(d, shape, seed=0)
+            digests[cfg] = dir_digest(d)
+            code = ("import sys,numpy as np; sys.path.insert(0, %r); from oracle import oracle; "
+                    "from vla_simd_b200 import synth; r = oracle.reference(); "
+                    "f, s = synth.act_inputs(synth.%s, seed=1); "
+                    "np.save(%r, r.act_predict(%r, f, s))") % (
+                        ROOT, "ACT_SMALL" if cfg == "small" else "ACT_BASELINE",
+                        os.path.join(HERE, f"act_{cfg}_m{mask}.npy"), d)
+            env = dict(os.environ, ACT_INT8=str(mask))
+            subprocess.run([sys.executable, "-c", code], check=True, env=env)
+    with open(os.path.join(HERE, "checkpoints.json"), "w") as f:
+        json.dump(digests, f, indent=1, sort_keys=True)
+
+    arrays, meta = {}, {}
+    for seq, N, K in GEMM_SHAPES:
+        x, W, b = gemm_inputs(seq, N, K)
+        xq, xs = ref.quantize_act_i8(x)
+        panels, ws = ref.pack_weights_i8(W)
+        out = ref.dense_linear_i8_ref(xq, xs, panels, ws, b, N, K)
+        # int32 accumulators: the reference never exposes them; restate from its int8 operands
+        wq = np.zeros((N, K), np.int8)
+        Kp = ref.kpad(K)
+        pan = panels[:N * Kp].reshape(N // 16, Kp // 4, 16, 4)
+        wq[:, :] = pan.transpose(0, 2, 1, 3).reshape(N, Kp)[:, :K]
+        acc = (xq[:, :K].astype(np.int64) @ wq.astype(np.int64).T).astype(np.int32)
+        key = f"{seq}x{N}x{K}"
+        meta[key] = {"xq": sha(xq[:, :K]), "ascale": sha(xs), "wq": sha(wq), "wscale": sha(ws), "acc": sha(acc),
+                     "out": sha(out)}
+        if seq * N <= 20000:
+            arrays.update({f"{key}_xq": xq[:, :K], f"{key}_ascale": xs, f"{key}_acc": acc, f"{key}_out": out})
+    np.savez_compressed(os.path.join(HERE, "gemm.npz"), **arrays)
+    with open(os.path.join(HERE, "gemm.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+"""vla_simd_b200: the B200 (sm_100a) backend of vla.simd's W8A8 policy path.
+
+The product is ``libvla_simd_b200.so`` (CUDA kernels + the C ABI of
+``include/vla_simd.h`` and ``include/vla_simd_cuda.h``). This package only loads
+it with ctypes and mirrors the reference's Python-side interface:
+
+* :class:`ActPolicy` - the reference server's ``ActEngine`` binding
+  (vla_simd/policy_server.py:276-307): uint8 frames + state in, actions out.
+* ``ops`` - device-pointer wrappers over the op-level ABI taking torch CUDA
+  tensors (torch is only the allocator / stream provider here).
+
+There is no CPU fallback: importing works without a GPU, but every call needs
+the compiled library and a B200, and fails loudly otherwise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+__all__ = ["LIB_PATH", "lib", "ActPolicy", "VlaError"]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libvla_simd_b200.so")
+
+VLA_OK, VLA_ERR_ARG, VLA_ERR_SHAPE, VLA_ERR_EXCEPTION, VLA_ERR_DEVICE = 0, -1, -2, -3, -4
+EPI_RELU, EPI_ADD, EPI_ADD_RELU, EPI_ACC = 1, 2, 4, 8
+
+U8P = ctypes.POINTER(ctypes.c_uint8)
+F32P = ctypes.POINTER(ctypes.c_float)
+VP = ctypes.c_void_p
+I32, I64, F32 = ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+
+
+class VlaError(RuntimeError):
+    def __init__(self, what: str, code: int):
+        super().__init__(f"{what} failed with vla_status {code}")
+        self.code = code
+
+
+# name -> (restype, argtypes) for every symbol the two headers declare
+SIGNATURES = {
+    "vla_abi_version": (I32, []),
+    "vla_backend_name": (ctypes.c_char_p, []),
+    "vla_int8_available": (I32, []),
+    "vla_act_load": (VP, [ctypes.c_char_p]),
+    "vla_act_free": (None, [VP]),
+    "vla_act_chunk": (I32, [VP]),
+    "vla_act_action_dim": (I32, [VP]),
+    "vla_act_state_dim": (I32, [VP]),
+    "vla_act_n_cams": (I32, [VP]),
+    "vla_act_img_h": (I32, [VP]),
+    "vla_act_img_w": (I32, [VP]),
+    "vla_act_predict": (I32, [VP, U8P, F32P, I32, F32P]),
+    "vla_cuda_i8_ld": (I64, [I32]),
+    "vla_cuda_device_status": (I32, []),
+    "vla_cuda_quantize_act_i8": (I32, [VP, VP, VP, I32, I32, I64, VP]),
+    "vla_cuda_pack_weights_i8": (I32, [VP, VP, VP, I32, I32, I64, VP]),
+    "vla_cuda_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32, I64, I64, VP]),
+    "vla_cuda_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP, VP, VP]),
+    "vla_cuda_gemm_i8": (I32, [VP, I64, VP, I64, VP, I32, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I32,
+                               I32, VP]),
+    "vla_cuda_conv2d_i8": (I32, [VP, VP, I32, I32, I32, I32, VP, I64, VP, VP, I32, I32, I32, I32, F32, I32, VP, VP,
+                                 VP, VP, VP]),
+    "vla_cuda_layernorm": (I32, [VP, VP, VP, VP, I32, I32, F32, VP]),
+    "vla_cuda_gqa_attention": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP, VP]),
+    "vla_cuda_maxpool2d_relu": (I32, [VP, VP, I32, I32, I32, I32, I32, I32, I32, VP]),
+    "vla_tcpu_int8_gemm_available": (I32, []),
+    "vla_tcpu_i8_kpad": (I32, [I32]),
+    "vla_tcpu_packed_i8_words": (ctypes.c_uint64, [I32, I32]),
+    "vla_tcpu_pack_weights_i8": (I32, [VP, VP, VP, I32, I32]),
+    "vla_tcpu_quantize_act_i8": (I32, [VP, VP, VP, I32, I32]),
+    "vla_tcpu_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32]),
+    "vla_tcpu_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, VP, VP]),
+    "vla_act_device_buffers": (I32, [VP, VP, VP, VP]),
+    "vla_act_enqueue": (I32, [VP, VP, I32]),
+    "vla_act_kernels_per_step": (I32, [VP]),
+    "vla_act_int8_layers": (I32, [VP]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (built on first use if only the sources are present)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from . import build as _build
+            _build.build()
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != VLA_OK:
+        raise VlaError(what, code)
+
+
+class ActPolicy:
+    """ctypes binding of the ACT C ABI, shaped like the reference's ActEngine.
+
+    frames [n_cams, img_h, img_w, 3] uint8 + state [state_dim] (raw robot units)
+    -> actions [chunk, action_dim] float32 (robot units unless unnormalize=False).
+    """
+
+    def __init__(self, model_dir: str):
+        self.lib = lib()
+        self.h = self.lib.vla_act_load(model_dir.encode())
+        if not self.h:
+            raise RuntimeError(f"vla_act_load failed for {model_dir}")
+        for name in ("chunk", "action_dim", "state_dim", "n_cams", "img_h", "img_w"):
+            setattr(self, name, int(getattr(self.lib, f"vla_act_{name}")(self.h)))
+
+    def predict(self, frames: np.ndarray, state: np.ndarray, unnormalize: bool = True) -> np.ndarray:
+        frames = np.ascontiguousarray(frames, np.uint8)
+        if frames.shape != (self.n_cams, self.img_h, self.img_w, 3):
+            raise ValueError(f"frames {frames.shape} != {(self.n_cams, self.img_h, self.img_w, 3)}")
+        state = np.ascontiguousarray(np.asarray(state, np.float32).reshape(-1))
+        if state.size != self.state_dim:
+            raise ValueError(f"state has {state.size} values, the checkpoint wants {self.state_dim}")
+        out = np.empty((self.chunk, self.action_dim), np.float32)
+        rc = self.lib.vla_act_predict(self.h, frames.ctypes.data_as(U8P), state.ctypes.data_as(F32P),
+                                      1 if unnormalize else 0, out.ctypes.data_as(F32P))
+        check(rc, "vla_act_predict")
+        return out
+
+    def device_buffers(self):
+        img, st, act = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        check(self.lib.vla_act_device_buffers(self.h, ctypes.byref(img), ctypes.byref(st), ctypes.byref(act)),
+              "vla_act_device_buffers")
+        return img.value, st.value, act.value
+
+    def enqueue(self, stream_handle: int, unnormalize: bool = True) -> None:
+        check(self.lib.vla_act_enqueue(self.h, ctypes.c_void_p(stream_handle), 1 if unnormalize else 0),
+              "vla_act_enqueue")
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(self.lib.vla_act_kernels_per_step(self.h))
+
+    @property
+    def int8_layers(self) -> int:
+        return int(self.lib.vla_act_int8_layers(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.vla_act_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

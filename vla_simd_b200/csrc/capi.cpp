@@ -1,0 +1,362 @@
+// extern "C" boundary of libvla_simd_b200.so: include/vla_simd.h (model level)
+// and include/vla_simd_cuda.h (op level). Exceptions are fenced here, CUDA
+// errors map to VLA_ERR_DEVICE, argument checks to VLA_ERR_ARG.
+#include "../../include/vla_simd.h"
+#include "../../include/vla_simd_cuda.h"
+
+#include "act_policy.h"
+#include "gemm_i8.h"
+#include "host_quant.h"
+#include "nn.h"
+#include "quant.h"
+
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <vector>
+
+using vsb::ActPolicy;
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int32_t status_of(cudaError_t e) {
+    if (e == cudaSuccess) return VLA_OK;
+    if (e == cudaErrorInvalidValue) return VLA_ERR_ARG;
+    return VLA_ERR_DEVICE;
+}
+
+int64_t ld16(int64_t k) { return (k + 15) & ~int64_t(15); }
+
+bool k_ok(int32_t K) { return K > 0 && K <= INT_MAX / (255 * 127); }
+
+// Grow-only device workspace for the host-pointer shims (one per thread).
+struct Workspace {
+    void* p = nullptr;
+    size_t n = 0;
+    int dev = -1;
+    ~Workspace() {
+        if (p) cudaFree(p);
+    }
+    void* get(size_t bytes) {
+        int d = 0;
+        cudaGetDevice(&d);
+        if (p && (bytes > n || d != dev)) {
+            cudaFree(p);
+            p = nullptr;
+            n = 0;
+        }
+        if (!p) {
+            if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+            n = bytes;
+            dev = d;
+        }
+        return p;
+    }
+};
+thread_local Workspace g_ws;
+
+// carve 256-byte aligned pieces out of one allocation
+struct Carver {
+    char* base;
+    size_t off = 0;
+    template <class T>
+    T* take(size_t count) {
+        off = (off + 255) & ~size_t(255);
+        T* r = reinterpret_cast<T*>(base + off);
+        off += count * sizeof(T);
+        return r;
+    }
+};
+size_t carve_size(std::initializer_list<size_t> bytes) {
+    size_t s = 0;
+    for (size_t b : bytes) s += ((b + 255) & ~size_t(255)) + 256;
+    return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------ model level
+
+int32_t vla_abi_version(void) { return VLA_ABI_VERSION; }
+
+const char* vla_backend_name(void) { return "cuda-sm100a"; }
+
+int32_t vla_int8_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) return 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    return major == 10 ? 1 : 0;
+}
+
+void* vla_act_load(const char* model_dir) try {
+    if (!model_dir) return nullptr;
+    auto m = std::make_unique<ActPolicy>();
+    if (!m->load(model_dir)) {
+        std::fprintf(stderr, "vla_act_load: %s\n", m->error().c_str());
+        return nullptr;
+    }
+    return m.release();
+} catch (...) {
+    return nullptr;
+}
+
+void vla_act_free(void* h) { delete static_cast<ActPolicy*>(h); }
+
+int32_t vla_act_chunk(void* h) { return h ? static_cast<ActPolicy*>(h)->chunk() : 0; }
+int32_t vla_act_action_dim(void* h) { return h ? static_cast<ActPolicy*>(h)->action_dim() : 0; }
+int32_t vla_act_state_dim(void* h) { return h ? static_cast<ActPolicy*>(h)->state_dim() : 0; }
+int32_t vla_act_n_cams(void* h) { return h ? static_cast<ActPolicy*>(h)->n_cams() : 0; }
+int32_t vla_act_img_h(void* h) { return h ? static_cast<ActPolicy*>(h)->img_h() : 0; }
+int32_t vla_act_img_w(void* h) { return h ? static_cast<ActPolicy*>(h)->img_w() : 0; }
+
+int32_t vla_act_predict(void* h, const uint8_t* images, const float* state, int32_t unnormalize,
+                        float* actions) try {
+    if (!h || !images || !state || !actions) return VLA_ERR_ARG;
+    return static_cast<ActPolicy*>(h)->predict(images, state, unnormalize != 0, actions) == cudaSuccess
+               ? VLA_OK
+               : VLA_ERR_DEVICE;
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_act_device_buffers(void* h, uint8_t** images, float** state, const float** actions) {
+    if (!h) return VLA_ERR_ARG;
+    auto* m = static_cast<ActPolicy*>(h);
+    if (images) *images = m->device_images();
+    if (state) *state = m->device_state();
+    if (actions) *actions = m->device_actions();
+    return VLA_OK;
+}
+
+int32_t vla_act_enqueue(void* h, void* stream, int32_t unnormalize) try {
+    if (!h) return VLA_ERR_ARG;
+    return status_of(static_cast<ActPolicy*>(h)->enqueue_step(as_stream(stream), unnormalize != 0));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_act_kernels_per_step(void* h) { return h ? static_cast<ActPolicy*>(h)->kernels_per_step() : 0; }
+int32_t vla_act_int8_layers(void* h) { return h ? static_cast<ActPolicy*>(h)->int8_layers() : 0; }
+
+// --------------------------------------------------------------- op level
+
+int64_t vla_cuda_i8_ld(int32_t K) { return K > 0 ? ld16(K) : 0; }
+
+int32_t vla_cuda_device_status(void) { return vsb::device_status_take(); }
+
+int32_t vla_cuda_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int32_t seq, int32_t K, int64_t ldq,
+                                 void* stream) {
+    if (!x || !xq || !ascale || seq <= 0 || K <= 0 || ldq < K) return VLA_ERR_ARG;
+    return status_of(vsb::quantize_rows(x, K, nullptr, 0, seq, K, xq, ldq, ascale, nullptr, 0, nullptr,
+                                        as_stream(stream)));
+}
+
+int32_t vla_cuda_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K, int64_t ldw,
+                                 void* stream) {
+    if (!W || !Wq || !wscale || N <= 0 || K <= 0 || ldw < K) return VLA_ERR_ARG;
+    return status_of(vsb::quantize_rows(W, K, nullptr, 0, N, K, Wq, ldw, wscale, nullptr, 0, nullptr,
+                                        as_stream(stream)));
+}
+
+int32_t vla_cuda_gemm_i8(void* out, int64_t ldo, const int8_t* xq, int64_t ldx, const float* ascale,
+                         int32_t ascale_per_row, const int8_t* Wq, int64_t ldw, const float* wscale,
+                         const float* bias, const float* res, int64_t ldr, int32_t M, int32_t N, int32_t K,
+                         int32_t mode, uint32_t* amax, int32_t amax_rows, int32_t force_simt, void* stream) {
+    if (!out || !xq || !Wq || M <= 0 || N <= 0 || !k_ok(K) || ldx < K || ldw < K || ldo < N) return VLA_ERR_ARG;
+    if (!(mode & VLA_EPI_ACC) && (!ascale || !wscale)) return VLA_ERR_ARG;
+    if ((mode & (VLA_EPI_ADD | VLA_EPI_ADD_RELU)) && (!res || ldr < N)) return VLA_ERR_ARG;
+    if (mode & ~(VLA_EPI_RELU | VLA_EPI_ADD | VLA_EPI_ADD_RELU | VLA_EPI_ACC)) return VLA_ERR_ARG;
+    vsb::GemmI8Args a;
+    a.A = xq;
+    a.lda = ldx;
+    a.B = Wq;
+    a.ldb = ldw;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.out = out;
+    a.ldo = ldo;
+    a.ascale = ascale;
+    a.ascale_per_row = ascale_per_row != 0;
+    a.wscale = wscale;
+    a.bias = bias;
+    a.res = res;
+    a.ldr = ldr;
+    a.mode = mode;
+    a.amax = amax;
+    a.amax_rows = amax_rows > 0 ? amax_rows : 1;
+    a.force_simt = force_simt != 0;
+    return status_of(vsb::gemm_i8(a, as_stream(stream)));
+}
+
+int32_t vla_cuda_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
+                                     const float* wscale, const float* bias, int32_t seq, int32_t N, int32_t K,
+                                     int64_t ldx, int64_t ldw, void* stream) {
+    if (!ascale || !wscale) return VLA_ERR_ARG;
+    return vla_cuda_gemm_i8(out, N, xq, ldx, ascale, 1, Wq, ldw, wscale, bias, nullptr, 0, seq, N, K, 0, nullptr,
+                            1, 0, stream);
+}
+
+int32_t vla_cuda_dense_linear_i8(float* out, const float* x, const int8_t* Wq, const float* wscale,
+                                 const float* bias, int32_t seq, int32_t N, int32_t K, int64_t ldw,
+                                 int8_t* xq_scratch, float* ascale_scratch, void* stream) {
+    if (!out || !x || !xq_scratch || !ascale_scratch || seq <= 0 || !k_ok(K)) return VLA_ERR_ARG;
+    const int32_t r = vla_cuda_quantize_act_i8(x, xq_scratch, ascale_scratch, seq, K, ld16(K), stream);
+    if (r != VLA_OK) return r;
+    return vla_cuda_dense_linear_i8_pre(out, xq_scratch, ascale_scratch, Wq, wscale, bias, seq, N, K, ld16(K), ldw,
+                                        stream);
+}
+
+int32_t vla_cuda_conv2d_i8(float* out, const float* x, int32_t F, int32_t H, int32_t W, int32_t Cin,
+                           const int8_t* Wq, int64_t ldw, const float* wscale, const float* bias, int32_t Cout,
+                           int32_t k, int32_t stride, int32_t pad, float clip, int32_t mode, const float* res,
+                           int8_t* col_scratch, float* rscale_scratch, uint32_t* amax_scratch, void* stream) {
+    if (!out || !x || !Wq || !wscale || !col_scratch || !rscale_scratch || !amax_scratch) return VLA_ERR_ARG;
+    if (F <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || stride <= 0 || pad < 0) return VLA_ERR_ARG;
+    if (!(clip > 0.0f && clip <= 1.0f)) return VLA_ERR_ARG;
+    const int32_t K = k * k * Cin;
+    if (!k_ok(K) || ldw < K || (ldw & 15)) return VLA_ERR_ARG;
+    const int Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+    if (H + 2 * pad < k || W + 2 * pad < k || Ho <= 0 || Wo <= 0) return VLA_ERR_ARG;
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e = cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t) * F, st);
+    if (e == cudaSuccess) e = vsb::absmax_slots(x, (long long)F * H * W * Cin, (long long)H * W * Cin, amax_scratch, st);
+    if (e == cudaSuccess)
+        e = vsb::im2col_i8(x, F, H, W, Cin, k, stride, pad, Ho, Wo, ldw, amax_scratch, clip, col_scratch,
+                           rscale_scratch, st);
+    if (e != cudaSuccess) return status_of(e);
+    return vla_cuda_gemm_i8(out, Cout, col_scratch, ldw, rscale_scratch, 1, Wq, ldw, wscale, bias, res, Cout,
+                            F * Ho * Wo, Cout, K, mode, nullptr, 1, 0, stream);
+}
+
+int32_t vla_cuda_layernorm(float* out, const float* x, const float* w, const float* b, int32_t seq, int32_t hidden,
+                           float eps, void* stream) {
+    if (!out || !x || !w || seq <= 0 || hidden <= 0 || hidden > 2048) return VLA_ERR_ARG;
+    return status_of(vsb::layernorm(x, out, w, b, seq, hidden, eps, nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                                    as_stream(stream)));
+}
+
+int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* K, const float* V, int32_t seq_q,
+                               int32_t seq_k, int32_t n_q, int32_t n_kv, int32_t head_dim, float scale,
+                               const float* mask, void* stream) {
+    if (!out || !Q || !K || !V || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv || head_dim != 64)
+        return VLA_ERR_ARG;
+    return status_of(vsb::attention(Q, (long long)n_q * head_dim, K, (long long)n_kv * head_dim, V,
+                                    (long long)n_kv * head_dim, out, (long long)n_q * head_dim, seq_q, seq_k, n_q,
+                                    n_kv, head_dim, scale, mask, as_stream(stream)));
+}
+
+int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H, int32_t W, int32_t C, int32_t k,
+                                int32_t stride, int32_t pad, void* stream) {
+    if (!out || !x || F <= 0 || H <= 0 || W <= 0 || C <= 0 || k <= 0 || stride <= 0 || pad < 0) return VLA_ERR_ARG;
+    const int Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
+    if (Ho <= 0 || Wo <= 0) return VLA_ERR_ARG;
+    return status_of(vsb::maxpool_relu(x, out, F, H, W, C, k, stride, pad, Ho, Wo, nullptr, as_stream(stream)));
+}
+
+// ------------------------------------------------------ host-pointer shims
+
+int32_t vla_tcpu_int8_gemm_available(void) { return vla_int8_available(); }
+
+int32_t vla_tcpu_i8_kpad(int32_t K) { return (K + 3) & ~3; }
+
+uint64_t vla_tcpu_packed_i8_words(int32_t N, int32_t K) {
+    const uint64_t panel = (uint64_t)N * (uint64_t)vla_tcpu_i8_kpad(K);
+    return (panel + (uint64_t)N * 4) / 4;
+}
+
+int32_t vla_tcpu_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K) try {
+    if (!W || !Wq || !wscale || N <= 0 || N % 16 || K <= 0) return VLA_ERR_ARG;
+    const int Kp = vla_tcpu_i8_kpad(K), KG = Kp / 4;
+    std::vector<int8_t> rows((size_t)N * K);
+    vsb::quantize_rows_host(W, N, K, rows.data(), K, wscale);
+    std::memset(Wq, 0, (size_t)N * Kp);
+    int32_t* rowsum = reinterpret_cast<int32_t*>(Wq + (size_t)N * Kp);
+    for (int n = 0; n < N; ++n) {
+        int32_t s = 0;
+        for (int k = 0; k < K; ++k) {
+            const int8_t q = rows[(size_t)n * K + k];
+            Wq[((size_t)((n / 16) * KG + k / 4) * 16 + (n % 16)) * 4 + (k % 4)] = q;
+            s += q;
+        }
+        rowsum[n] = s;
+    }
+    return VLA_OK;
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_tcpu_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int32_t seq, int32_t K) try {
+    if (!x || !xq || !ascale || seq <= 0 || K <= 0) return VLA_ERR_ARG;
+    const int64_t ld = ld16(K);
+    const int Kp = vla_tcpu_i8_kpad(K);
+    void* base = g_ws.get(carve_size({sizeof(float) * (size_t)seq * K, (size_t)seq * ld, sizeof(float) * seq}));
+    if (!base) return VLA_ERR_DEVICE;
+    Carver c{static_cast<char*>(base)};
+    float* dx = c.take<float>((size_t)seq * K);
+    int8_t* dq = c.take<int8_t>((size_t)seq * ld);
+    float* ds = c.take<float>(seq);
+    cudaError_t e = cudaMemcpy(dx, x, sizeof(float) * (size_t)seq * K, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = vsb::quantize_rows(dx, K, nullptr, 0, seq, K, dq, ld, ds, nullptr, 0, nullptr, 0);
+    if (e == cudaSuccess) e = cudaMemcpy2D(xq, Kp, dq, ld, Kp, seq, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(ascale, ds, sizeof(float) * seq, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && vsb::device_status_take() != 0) e = cudaErrorLaunchFailure;
+    return status_of(e);
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
+                                     const float* wscale, const float* bias, int32_t seq, int32_t N,
+                                     int32_t K) try {
+    if (!out || !xq || !ascale || !Wq || !wscale || seq <= 0 || N <= 0 || N % 16 || !k_ok(K)) return VLA_ERR_ARG;
+    const int64_t ld = ld16(K);
+    const int Kp = vla_tcpu_i8_kpad(K);
+    const size_t panel_bytes = (size_t)N * Kp;
+    void* base = g_ws.get(carve_size({(size_t)seq * ld, sizeof(float) * seq, panel_bytes, (size_t)N * ld,
+                                      sizeof(float) * N, sizeof(float) * N, sizeof(float) * (size_t)seq * N}));
+    if (!base) return VLA_ERR_DEVICE;
+    Carver c{static_cast<char*>(base)};
+    int8_t* dq = c.take<int8_t>((size_t)seq * ld);
+    float* ds = c.take<float>(seq);
+    int8_t* dp = c.take<int8_t>(panel_bytes);
+    int8_t* dw = c.take<int8_t>((size_t)N * ld);
+    float* dws = c.take<float>(N);
+    float* db = c.take<float>(N);
+    float* dout = c.take<float>((size_t)seq * N);
+    cudaError_t e = cudaMemcpy2D(dq, ld, xq, Kp, Kp, seq, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(ds, ascale, sizeof(float) * seq, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dp, Wq, panel_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dws, wscale, sizeof(float) * N, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && bias) e = cudaMemcpy(db, bias, sizeof(float) * N, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = vsb::unpack_panels_i8(dp, N, K, dw, ld, 0);
+    if (e != cudaSuccess) return status_of(e);
+    const int32_t r = vla_cuda_gemm_i8(dout, N, dq, ld, ds, 1, dw, ld, dws, bias ? db : nullptr, nullptr, 0, seq, N,
+                                       K, 0, nullptr, 1, 0, nullptr);
+    if (r != VLA_OK) return r;
+    e = cudaMemcpy(out, dout, sizeof(float) * (size_t)seq * N, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && vsb::device_status_take() != 0) e = cudaErrorLaunchFailure;
+    return status_of(e);
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_tcpu_dense_linear_i8(float* out, const float* x, const int8_t* Wq, const float* wscale, const float* bias,
+                                 int32_t seq, int32_t N, int32_t K, int8_t* xq_scratch, float* ascale_scratch) {
+    if (!xq_scratch || !ascale_scratch) return VLA_ERR_ARG;
+    const int32_t r = vla_tcpu_quantize_act_i8(x, xq_scratch, ascale_scratch, seq, K);
+    if (r != VLA_OK) return r;
+    return vla_tcpu_dense_linear_i8_pre(out, xq_scratch, ascale_scratch, Wq, wscale, bias, seq, N, K);
+}
+
+}  // extern "C"

@@ -1,0 +1,375 @@
+// W8A8 GEMM for sm_100a: int8 x int8 -> int32 on the 5th-generation tensor
+// cores (tcgen05.mma kind::i8), accumulator in TMEM, operand tiles staged by TMA
+// with the 128-byte swizzle, and the reference's delayed-scaling epilogue fused:
+//
+//   out[m,n] = fma((float)acc[m,n] * s_w[n], s_a[m], bias[n])      (then ReLU /
+//              residual add / residual add + ReLU, optionally an absmax tap)
+//
+// which is, operation for operation, the epilogue of the reference's scalar
+// oracle dense_linear_i8_ref (src/hal/common/gemm_i8.cpp:278) and of its AVX-VNNI
+// kernel (src/hal/avx2/gemm_i8.cpp:101-104). Integer accumulation has no
+// rounding, so the int32 sums equal the reference's exactly; the fp32 epilogue
+// uses explicitly rounded intrinsics (__fmul_rn / __fmaf_rn) so nvcc cannot
+// contract the multiply into the fma and the outputs are bit-identical.
+//
+// Layout (device side, this library's own): A = activations int8 [M][lda],
+// B = weights int8 [N][ldb], both K-major (row-major over K); lda/ldb are
+// multiples of 16 bytes (TMA stride rule). Bytes past K in a row are never read:
+// the tensor maps' inner extent is K, so TMA zero-fills the k-tail.
+//
+// CTA = 128 threads, one 128 x BN output tile:
+//   thread 0   TMA producer (A and B k-blocks of 128 bytes, STAGES-deep ring)
+//   thread 32  MMA issuer (4 x tcgen05.mma K=32 per k-block), commits free ring
+//              slots back to the producer and finally signals the epilogue
+//   warps 0-3  epilogue: warp w reads TMEM lanes [32w, 32w+32) = tile rows
+//              32w..32w+31 with tcgen05.ld, applies the epilogue, stores fp32.
+#include "sm100.cuh"
+#include "gemm_i8.h"
+
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cfloat>
+#include <cstdio>
+#include <mutex>
+
+namespace vsb {
+
+namespace {
+
+constexpr int kBM = 128;          // UMMA M (one TMEM lane per tile row)
+constexpr int kBK = 128;          // bytes of K per pipeline stage (one SW128 atom row)
+constexpr int kUmmaK = 32;        // K per tcgen05.mma kind::i8
+constexpr int kThreads = 128;
+
+struct EpiParams {
+    void* out;                    // float* (or int32_t* with kEpiAcc)
+    long long ldo;
+    const float* res;             // residual, read before out is written (may alias out)
+    long long ldr;
+    const float* ascale;          // per-row activation scale, index m * as_stride
+    int as_stride;                // 1 = per row, 0 = one scale for every row
+    const float* wscale;          // [N]
+    const float* bias;            // [N] or null (then +0.0f, as the reference)
+    unsigned int* amax;           // optional absmax tap (float bits), slot m / amax_rows
+    int amax_rows;
+    int mode;
+    int M, N, K;
+    int vec_ok;                   // 16-byte aligned rows: float4 stores
+};
+
+__device__ __forceinline__ float epi_value(int32_t acc, float ws, float as, float b, int mode,
+                                           const float* resp) {
+    float v = __fmaf_rn(__fmul_rn(__int2float_rn(acc), ws), as, b);
+    if (mode & kEpiRelu) v = (v < 0.0f) ? 0.0f : v;                 // eltwise relu (eltwise.cpp:213-214)
+    if (mode & kEpiAdd) v = __fadd_rn(*resp, v);                      // x[i] += y[i]
+    if (mode & kEpiAddRelu) { v = __fadd_rn(v, *resp); v = v > 0.0f ? v : 0.0f; }  // resnet_backbone.cpp:293-295
+    return v;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                 const __grid_constant__ CUtensorMap tmap_b,
+                 const EpiParams p) {
+    constexpr int kABytes = kBM * kBK;
+    constexpr int kBBytes = BN * kBK;
+    constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    // SW128 tiles want 1024-byte alignment
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* s_ws = reinterpret_cast<float*>(tmem_slot + 4);
+    float* s_b = s_ws + BN;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN;
+    const int m0 = blockIdx.y * kBM;
+    const int nkb = (p.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(done, 1);
+        *s_consumed = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    for (int j = threadIdx.x; j < BN; j += kThreads) {
+        const int n = n0 + j;
+        s_ws[j] = n < p.N ? p.wscale[n] : 0.0f;
+        s_b[j] = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    int issued = 0;
+    if (threadIdx.x == 0) {
+        // ---- TMA producer
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % STAGES;
+            const int use = kb / STAGES;
+            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;
+            mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+            tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
+            tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
+            issued = kb + 1;
+        }
+    } else if (threadIdx.x == 32) {
+        // ---- MMA issuer
+        int kb = 0;
+        for (; kb < nkb; ++kb) {
+            const int s = kb % STAGES;
+            if (!mbar_wait(&full[s], (kb / STAGES) & 1)) break;
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(sA + s * kABytes);
+            const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+            #pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+                umma_s8(tmem_base, sw128_kmajor_desc(a_addr + k * kUmmaK),
+                        sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+            }
+            umma_commit(&empty[s]);
+            *s_consumed = kb + 1;
+        }
+        if (kb == nkb) umma_commit(done);
+    }
+    __syncwarp();
+
+    // ---- epilogue
+    const bool ok = mbar_wait(done, 0);
+    if (ok) {
+        tc_fence_after();
+        const int row = warp * 32 + lane;
+        const int m = m0 + row;
+        const bool row_ok = m < p.M;
+        const float as = row_ok ? p.ascale[(long long)m * p.as_stride] : 0.0f;
+        float tmax = 0.0f;
+        #pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t acc[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c * 32, acc);
+            tmem_ld_wait();
+            const int nb = n0 + c * 32;
+            if (!row_ok || nb >= p.N) continue;
+            if (p.mode & kEpiAcc) {
+                int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + nb;
+                #pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (nb + j < p.N) o[j] = static_cast<int32_t>(acc[j]);
+                continue;
+            }
+            float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + nb;
+            const float* r = p.res ? p.res + (long long)m * p.ldr + nb : nullptr;
+            if (p.vec_ok && nb + 32 <= p.N) {
+                #pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 rv = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (r) rv = *reinterpret_cast<const float4*>(r + j);
+                    float4 v;
+                    v.x = epi_value(static_cast<int32_t>(acc[j + 0]), s_ws[c * 32 + j + 0], as, s_b[c * 32 + j + 0], p.mode, &rv.x);
+                    v.y = epi_value(static_cast<int32_t>(acc[j + 1]), s_ws[c * 32 + j + 1], as, s_b[c * 32 + j + 1], p.mode, &rv.y);
+                    v.z = epi_value(static_cast<int32_t>(acc[j + 2]), s_ws[c * 32 + j + 2], as, s_b[c * 32 + j + 2], p.mode, &rv.z);
+                    v.w = epi_value(static_cast<int32_t>(acc[j + 3]), s_ws[c * 32 + j + 3], as, s_b[c * 32 + j + 3], p.mode, &rv.w);
+                    tmax = fmaxf(tmax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                    *reinterpret_cast<float4*>(o + j) = v;
+                }
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (nb + j >= p.N) continue;
+                    const float rv = r ? r[j] : 0.0f;
+                    const float v = epi_value(static_cast<int32_t>(acc[j]), s_ws[c * 32 + j], as, s_b[c * 32 + j], p.mode, &rv);
+                    tmax = fmaxf(tmax, fabsf(v));
+                    o[j] = v;
+                }
+            }
+        }
+        if (p.amax) {
+            // one atomic per warp when the warp's rows share a slot, else per row
+            const unsigned key = row_ok ? static_cast<unsigned>(m / p.amax_rows) : 0xFFFFFFFFu;
+            const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
+            if (__all_sync(0xFFFFFFFFu, key == k0)) {
+                float wm = tmax;
+                #pragma unroll
+                for (int off = 16; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
+                if (lane == 0 && k0 != 0xFFFFFFFFu) atomicMax(&p.amax[k0], __float_as_uint(wm));
+            } else if (row_ok) {
+                atomicMax(&p.amax[key], __float_as_uint(tmax));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // never leave the CTA with TMA writes still landing in its shared memory
+        for (int kb = *s_consumed; kb < issued; ++kb)
+            if (!mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1)) break;
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, BN);
+    }
+}
+
+// ------------------------------------------------------------------ SIMT path
+// Plain CUDA-core int8 GEMM (dp4a), used for operand strides TMA cannot
+// describe (lda/ldb not a multiple of 16) and as an independent GPU cross-check
+// of the tensor-core kernel in the tests. Same epilogue, bit for bit.
+__global__ void w8a8_simt_kernel(const int8_t* __restrict__ A, long long lda,
+                                 const int8_t* __restrict__ B, long long ldb, const EpiParams p) {
+    const int n = blockIdx.y * blockDim.x + threadIdx.x;
+    const int m = blockIdx.x;
+    if (n >= p.N || m >= p.M) return;
+    const int8_t* a = A + (long long)m * lda;
+    const int8_t* b = B + (long long)n * ldb;
+    int32_t acc = 0;
+    int k = 0;
+    if ((((uintptr_t)a | (uintptr_t)b) & 3) == 0) {
+        for (; k + 4 <= p.K; k += 4)
+            acc = __dp4a(*reinterpret_cast<const int*>(a + k), *reinterpret_cast<const int*>(b + k), acc);
+    }
+    for (; k < p.K; ++k) acc += static_cast<int32_t>(a[k]) * static_cast<int32_t>(b[k]);
+    if (p.mode & kEpiAcc) {
+        static_cast<int32_t*>(p.out)[(long long)m * p.ldo + n] = acc;
+        return;
+    }
+    const float rv = p.res ? p.res[(long long)m * p.ldr + n] : 0.0f;
+    const float v = epi_value(acc, p.wscale[n], p.ascale[(long long)m * p.as_stride],
+                              p.bias ? p.bias[n] : 0.0f, p.mode, &rv);
+    static_cast<float*>(p.out)[(long long)m * p.ldo + n] = v;
+    if (p.amax) atomicMax(&p.amax[m / p.amax_rows], __float_as_uint(fabsf(v)));
+}
+
+// ------------------------------------------------------------- tensor maps
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+}  // namespace
+
+bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, long long ld, int box_rows) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 15) || K <= 0 || rows <= 0) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+namespace {
+
+template <int BN, int STAGES>
+constexpr size_t umma_smem_bytes() {
+    return 1024 + STAGES * (kBM * kBK + BN * kBK) + (2 * STAGES + 1) * 8 + 16 + 2 * BN * 4;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, cudaStream_t st) {
+    constexpr size_t smem = umma_smem_bytes<BN, STAGES>();
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(w8a8_umma_kernel<BN, STAGES>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
+    w8a8_umma_kernel<BN, STAGES><<<grid, kThreads, smem, st>>>(ta, tb, p);
+    return cudaGetLastError();
+}
+
+EpiParams make_epi(const GemmI8Args& a) {
+    EpiParams p{};
+    p.out = a.out;
+    p.ldo = a.ldo;
+    p.res = a.res;
+    p.ldr = a.ldr;
+    p.ascale = a.ascale;
+    p.as_stride = a.ascale_per_row ? 1 : 0;
+    p.wscale = a.wscale;
+    p.bias = a.bias;
+    p.amax = a.amax;
+    p.amax_rows = a.amax_rows > 0 ? a.amax_rows : 1;
+    p.mode = a.mode;
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
+    p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 &&
+               (!a.res || ((rb & 15) == 0 && (a.ldr & 3) == 0));
+    return p;
+}
+
+}  // namespace
+
+int gemm_i8_pick_bn(int M, int N) {
+    // Fill the 148 SMs: prefer 128-wide tiles, fall back to 64 for narrow or
+    // few-row problems (conv stages with 64 output channels, short sequences).
+    const int mt = (M + kBM - 1) / kBM;
+    if (N <= 64) return 64;
+    if (mt * ((N + 127) / 128) < 120) return 64;
+    return 128;
+}
+
+cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, int bn,
+                         cudaStream_t st) {
+    const EpiParams p = make_epi(a);
+    if (bn == 64) return launch_umma<64, 4>(ta, tb, p, st);
+    if (bn == 256) return launch_umma<256, 4>(ta, tb, p, st);
+    return launch_umma<128, 3>(ta, tb, p, st);
+}
+
+cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
+    if (!a.force_simt) {
+        const int bn = gemm_i8_pick_bn(a.M, a.N);
+        CUtensorMap ta, tb;
+        if (make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) &&
+            make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, bn))
+            return gemm_i8_umma(a, ta, tb, bn, st);
+    }
+    const EpiParams p = make_epi(a);
+    if ((a.N + 127) / 128 > 65535) return cudaErrorInvalidValue;
+    dim3 grid(a.M, (a.N + 127) / 128);
+    w8a8_simt_kernel<<<grid, 128, 0, st>>>(a.A, a.lda, a.B, a.ldb, p);
+    return cudaGetLastError();
+}
+
+int device_status_take() {
+    int h = 0;
+    if (cudaMemcpyFromSymbol(&h, g_vsb_status, sizeof(int)) != cudaSuccess) return -1;
+    if (h) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_vsb_status, &z, sizeof(int));
+    }
+    return h;
+}
+
+}  // namespace vsb

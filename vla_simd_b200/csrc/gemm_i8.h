@@ -1,0 +1,50 @@
+// Host-side interface of the W8A8 GEMM (gemm_i8.cu).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace vsb {
+
+// Epilogue modes (bit flags). Without any flag: out = fma(acc*s_w, s_a, bias).
+enum : int {
+    kEpiRelu = 1,      // then v < 0 ? 0 : v            (tcpu::relu)
+    kEpiAdd = 2,       // then out = res + v            (residual x += y)
+    kEpiAddRelu = 4,   // then v = v + res; v > 0 ? v : 0 (ResNet block tail)
+    kEpiAcc = 8,       // write the raw int32 accumulators instead
+};
+
+struct GemmI8Args {
+    const int8_t* A = nullptr;   // [M][lda] quantized activations
+    long long lda = 0;
+    const int8_t* B = nullptr;   // [N][ldb] quantized weights (row n = output n)
+    long long ldb = 0;
+    int M = 0, N = 0, K = 0;
+    void* out = nullptr;         // float [M][ldo] (int32 with kEpiAcc)
+    long long ldo = 0;
+    const float* ascale = nullptr;
+    bool ascale_per_row = true;  // false: ascale[0] for every row
+    const float* wscale = nullptr;
+    const float* bias = nullptr;
+    const float* res = nullptr;  // kEpiAdd / kEpiAddRelu operand, may alias out
+    long long ldr = 0;
+    unsigned int* amax = nullptr;  // optional: atomicMax of |out| bits into amax[m / amax_rows]
+    int amax_rows = 1;
+    int mode = 0;
+    bool force_simt = false;     // route to the CUDA-core kernel (tests / odd strides)
+};
+
+// Launch on `st`. Tensor-core path when lda/ldb/A/B are 16-byte aligned,
+// otherwise the CUDA-core path (same results).
+cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st);
+
+// Pre-encoded variant for callers that keep tensor maps (the policy runtime).
+bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, long long ld, int box_rows);
+int gemm_i8_pick_bn(int M, int N);
+cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, int bn,
+                         cudaStream_t st);
+
+// Read and clear the device status word (0 = OK, see sm100.cuh).
+int device_status_take();
+
+}  // namespace vsb

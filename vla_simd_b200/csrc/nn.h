@@ -1,0 +1,35 @@
+// Host-side interface of the non-GEMM kernels (nn.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vsb {
+
+// out = LayerNorm(x) (may alias x). Optional fused per-row int8 outputs for the
+// next GEMM: q1/s1 quantize (out + addend) (or out when addend is null), q2/s2
+// quantize out. ldq = row stride of q1/q2.
+cudaError_t layernorm(const float* x, float* out, const float* w, const float* b, int M, int H, float eps,
+                      const float* addend, int8_t* q1, float* s1, int8_t* q2, float* s2, long long ldq,
+                      cudaStream_t st);
+
+// Multi-head attention, head_dim 64, rows of Q/K/V/O are tokens with the heads
+// side by side (token-major, [seq][heads*64] with leading dimensions).
+cudaError_t attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
+                      float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, int head_dim, float scale,
+                      const float* mask, cudaStream_t st);
+
+cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C, int k, int stride, int pad,
+                         int Ho, int Wo, unsigned int* amax, cudaStream_t st);
+
+cudaError_t normalize_frames(const uint8_t* img, float* out, int F, long long npx, const float* mean,
+                             const float* stdv, float eps, unsigned int* amax, cudaStream_t st);
+
+cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
+                       int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st);
+
+cudaError_t normalize_state(const float* s, const float* mean, const float* stdv, float eps, float* out, int n,
+                            cudaStream_t st);
+
+cudaError_t add_f32(const float* a, const float* b, float* out, long long n, cudaStream_t st);
+
+}  // namespace vsb

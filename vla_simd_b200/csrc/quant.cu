@@ -1,0 +1,241 @@
+// Symmetric int8 quantizers (memory-bound kernels).
+//
+// Row quantizer (activations per token, weights per output row): the same
+// arithmetic as the reference's quantize_act_i8 / pack_weights_i8
+// (src/hal/common/gemm_i8.cpp:49-54, :76, :150-152):
+//   s   = amax > 0 ? max(amax / 127, FLT_MIN) : 1
+//   q   = clamp(rne(x * (1/s)), -127, 127)
+// with IEEE division (__fdiv_rn) and an explicitly rounded multiply, so the
+// int8 values and scales are bit-identical to the CPU's.
+//
+// Per-tensor quantization for convolutions (src/hal/common/conv.cpp:444-466)
+// happens inside the im2col kernel: the producer of the conv input has already
+// accumulated its absmax (per frame) into a float-bits slot, so im2col reads
+// fp32, quantizes with the frame's scale and writes the int8 patch rows once.
+#include "sm100.cuh"
+#include "quant.h"
+
+#include <cfloat>
+
+namespace vsb {
+
+__device__ __forceinline__ float row_scale(float amax) {
+    return amax > 0.0f ? fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN) : 1.0f;
+}
+
+__device__ __forceinline__ int8_t q8(float v, float inv) {
+    int r = __float2int_rn(__fmul_rn(v, inv));
+    r = r > 127 ? 127 : r;
+    r = r < -127 ? -127 : r;
+    return static_cast<int8_t>(r);
+}
+
+// fp32 clamp first, then round: quantize_span_i8 (src/hal/common/gemm_i8.cpp:177-207),
+// where a clip factor < 1 lets x*inv exceed 127.
+__device__ __forceinline__ int8_t q8_span(float v, float inv) {
+    float t = __fmul_rn(v, inv);
+    t = fminf(fmaxf(t, -127.0f), 127.0f);
+    return static_cast<int8_t>(__float2int_rn(t));
+}
+
+// One warp per row. x [M][ldx] (+ optional addend [M][lda_] added first, in fp32,
+// like ActTransformer::encode's xq = x + pos). Writes q [M][ldq] (zero past K)
+// and scale [M]. A second output pair (q2/s2) quantizes x without the addend.
+__global__ void quantize_rows_kernel(const float* __restrict__ x, long long ldx,
+                                     const float* __restrict__ addend, long long lda_,
+                                     int M, int K,
+                                     int8_t* __restrict__ q, long long ldq, float* __restrict__ scale,
+                                     int8_t* __restrict__ q2, long long ldq2, float* __restrict__ scale2) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const float* xr = x + (long long)warp * ldx;
+    const float* ar = addend ? addend + (long long)warp * lda_ : nullptr;
+
+    float m1 = 0.0f, m2 = 0.0f;
+    for (int k = lane; k < K; k += 32) {
+        const float v = xr[k];
+        m2 = fmaxf(m2, fabsf(v));
+        if (ar) m1 = fmaxf(m1, fabsf(__fadd_rn(v, ar[k])));
+    }
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        m1 = fmaxf(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, off));
+        m2 = fmaxf(m2, __shfl_xor_sync(0xFFFFFFFFu, m2, off));
+    }
+    if (!ar) m1 = m2;
+    const float s1 = row_scale(m1), inv1 = __fdiv_rn(1.0f, s1);
+    int8_t* qr = q + (long long)warp * ldq;
+    for (int k = lane; k < ldq; k += 32)
+        qr[k] = k < K ? q8(ar ? __fadd_rn(xr[k], ar[k]) : xr[k], inv1) : 0;
+    if (lane == 0) scale[warp] = s1;
+    if (q2) {
+        const float s2 = row_scale(m2), inv2 = __fdiv_rn(1.0f, s2);
+        int8_t* qr2 = q2 + (long long)warp * ldq2;
+        for (int k = lane; k < ldq2; k += 32) qr2[k] = k < K ? q8(xr[k], inv2) : 0;
+        if (lane == 0) scale2[warp] = s2;
+    }
+}
+
+// im2col + per-tensor quantization. x: F frames of NHWC fp32 [H][W][C];
+// amax_bits[f] = float bits of frame f's absmax; clip = TCPU_I8_CLIP semantics.
+// col [F*Ho*Wo][ldc] int8, patch element order (ky, kx, ci) as the reference's
+// im2col_panel (src/hal/common/conv.cpp:142-156), zero for taps outside the
+// image and past K. rscale[row] = the frame's scale (one per output row, so the
+// GEMM epilogue reads a per-row scale).
+template <int VEC>
+__global__ void im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C,
+                                 int k, int stride, int pad, int Ho, int Wo, int K, long long ldc,
+                                 const unsigned int* __restrict__ amax_bits, float clip,
+                                 int8_t* __restrict__ col, float* __restrict__ rscale) {
+    const long long groups_per_row = ldc / VEC;
+    const long long total = (long long)F * Ho * Wo * groups_per_row;
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const long long row = t / groups_per_row;
+        const int g = static_cast<int>(t - row * groups_per_row);
+        const int npix = Ho * Wo;
+        const int f = static_cast<int>(row / npix);
+        const int pix = static_cast<int>(row - (long long)f * npix);
+        const int oy = pix / Wo, ox = pix - oy * Wo;
+        const float amax = __uint_as_float(amax_bits[f]);
+        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+        const float inv = __fdiv_rn(1.0f, s);
+        if (g == 0) rscale[row] = s;
+        const float* xf = x + (long long)f * H * W * C;
+        int8_t* dst = col + row * ldc + (long long)g * VEC;
+        const int k0 = g * VEC;
+        if (VEC == 16) {
+            // C % 16 == 0: the 16 elements share one tap
+            char4 out[4];
+            int8_t* ob = reinterpret_cast<int8_t*>(out);
+            if (k0 >= K) {
+                #pragma unroll
+                for (int i = 0; i < 16; ++i) ob[i] = 0;
+            } else {
+                const int tap = k0 / C, ci = k0 - tap * C;
+                const int ky = tap / k, kx = tap - ky * k;
+                const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+                if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
+                    #pragma unroll
+                    for (int i = 0; i < 16; ++i) ob[i] = 0;
+                } else {
+                    const float4* src = reinterpret_cast<const float4*>(xf + ((long long)iy * W + ix) * C + ci);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 v = src[i];
+                        ob[4 * i + 0] = q8_span(v.x, inv);
+                        ob[4 * i + 1] = q8_span(v.y, inv);
+                        ob[4 * i + 2] = q8_span(v.z, inv);
+                        ob[4 * i + 3] = q8_span(v.w, inv);
+                    }
+                }
+            }
+            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<int4*>(out);
+        } else {
+            #pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const int kk = k0 + i;
+                int8_t v = 0;
+                if (kk < K) {
+                    const int tap = kk / C, ci = kk - tap * C;
+                    const int ky = tap / k, kx = tap - ky * k;
+                    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+                    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                        v = q8_span(xf[((long long)iy * W + ix) * C + ci], inv);
+                }
+                dst[i] = v;
+            }
+        }
+    }
+}
+
+// Per-slot absmax of a contiguous tensor: slot = blockIdx.y covers elements
+// [slot*per_slot, (slot+1)*per_slot); one atomic per block.
+__global__ void absmax_kernel(const float* __restrict__ x, long long per_slot,
+                              unsigned int* __restrict__ amax_bits) {
+    const float* xs = x + (long long)blockIdx.y * per_slot;
+    float v = 0.0f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_slot;
+         i += (long long)gridDim.x * blockDim.x)
+        v = fmaxf(v, fabsf(xs[i]));
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    __shared__ float wmax[32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, wmax[w]);
+        atomicMax(&amax_bits[blockIdx.y], __float_as_uint(m));
+    }
+}
+
+// The reference's CPU panel layout [N/16][Kp/4][16][4] (src/hal/common/gemm_i8.cpp:30-43,
+// :79-84) -> device rows [N][ldw] (zero past K).
+__global__ void unpack_panels_kernel(const int8_t* __restrict__ panels, int N, int K, int8_t* __restrict__ rows,
+                                     long long ldw) {
+    const int Kp = (K + 3) & ~3, KG = Kp / 4;
+    const long long total = (long long)N * ldw;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int n = static_cast<int>(i / ldw);
+        const int k = static_cast<int>(i - (long long)n * ldw);
+        int8_t v = 0;
+        if (k < K) v = panels[((long long)((n / 16) * KG + k / 4) * 16 + (n % 16)) * 4 + (k % 4)];
+        rows[i] = v;
+    }
+}
+
+cudaError_t unpack_panels_i8(const int8_t* panels, int N, int K, int8_t* rows, long long ldw, cudaStream_t st) {
+    if (N <= 0 || K <= 0 || N % 16 || ldw < K) return cudaErrorInvalidValue;
+    const long long total = (long long)N * ldw;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    unpack_panels_kernel<<<(int)blocks, 256, 0, st>>>(panels, N, K, rows, ldw);
+    return cudaGetLastError();
+}
+
+cudaError_t quantize_rows(const float* x, long long ldx, const float* addend, long long ld_add, int M, int K,
+                          int8_t* q, long long ldq, float* scale, int8_t* q2, long long ldq2, float* scale2,
+                          cudaStream_t st) {
+    if (M <= 0 || K <= 0 || ldq < K || (q2 && ldq2 < K)) return cudaErrorInvalidValue;
+    const int threads = 256;
+    const int blocks = (M * 32 + threads - 1) / threads;
+    quantize_rows_kernel<<<blocks, threads, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+    return cudaGetLastError();
+}
+
+cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int stride, int pad, int Ho, int Wo,
+                      long long ldc, const unsigned int* amax_bits, float clip, int8_t* col, float* rscale,
+                      cudaStream_t st) {
+    const int K = k * k * C;
+    if (ldc < K || (ldc & 15)) return cudaErrorInvalidValue;
+    const bool v16 = (C % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(col) & 15) == 0);
+    const long long rows = (long long)F * Ho * Wo;
+    const long long total = rows * (ldc / (v16 ? 16 : 4));
+    const int threads = 256;
+    long long blocks = (total + threads - 1) / threads;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    if (v16)
+        im2col_i8_kernel<16><<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
+                                                              amax_bits, clip, col, rscale);
+    else
+        im2col_i8_kernel<4><<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
+                                                             amax_bits, clip, col, rscale);
+    return cudaGetLastError();
+}
+
+cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsigned int* amax_bits,
+                         cudaStream_t st) {
+    if (n <= 0 || per_slot <= 0 || n % per_slot) return cudaErrorInvalidValue;
+    const int threads = 256;
+    long long bx = (per_slot + threads - 1) / threads;
+    if (bx > 296) bx = 296;
+    dim3 grid((unsigned)bx, (unsigned)(n / per_slot));
+    absmax_kernel<<<grid, threads, 0, st>>>(x, per_slot, amax_bits);
+    return cudaGetLastError();
+}
+
+}  // namespace vsb

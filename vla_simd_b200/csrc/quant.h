@@ -1,0 +1,28 @@
+// Host-side interface of the quantization kernels (quant.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vsb {
+
+// Per-row symmetric int8 quantization of x [M][ldx] (K valid columns), optional
+// fp32 addend added first. q [M][ldq] is zero past K. Optional second output
+// q2/scale2 quantizes x itself (without the addend) in the same pass.
+cudaError_t quantize_rows(const float* x, long long ldx, const float* addend, long long ld_add, int M, int K,
+                          int8_t* q, long long ldq, float* scale, int8_t* q2, long long ldq2, float* scale2,
+                          cudaStream_t st);
+
+// int8 im2col of F NHWC frames with the per-frame per-tensor scale derived from
+// amax_bits[f] (float bits) and clip; col [F*Ho*Wo][ldc], rscale [F*Ho*Wo].
+cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int stride, int pad, int Ho, int Wo,
+                      long long ldc, const unsigned int* amax_bits, float clip, int8_t* col, float* rscale,
+                      cudaStream_t st);
+
+// atomicMax of |x| (float bits) per slot of per_slot consecutive elements.
+cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsigned int* amax_bits,
+                         cudaStream_t st);
+
+// Reference CPU panel layout [N/16][Kp/4][16][4] -> device rows [N][ldw].
+cudaError_t unpack_panels_i8(const int8_t* panels, int N, int K, int8_t* rows, long long ldw, cudaStream_t st);
+
+}  // namespace vsb

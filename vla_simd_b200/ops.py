@@ -1,0 +1,116 @@
+"""Op-level wrappers over include/vla_simd_cuda.h for torch CUDA tensors.
+
+Each function mirrors one reference op (src/ops/quant_ops.h, lm_ops.h,
+conv_ops.h) - same argument meaning, the outputs allocated here for
+convenience - and launches on torch's current stream. torch supplies device
+memory and the stream handle only; the compute is the library's kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import EPI_ACC, check, lib
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def i8_ld(K: int) -> int:
+    return int(lib().vla_cuda_i8_ld(K))
+
+
+def quantize_act_i8(x: torch.Tensor, ld: int | None = None):
+    """x [seq, K] fp32 -> (xq [seq, ld] int8, ascale [seq] fp32)."""
+    seq, K = x.shape
+    ld = ld or i8_ld(K)
+    xq = torch.empty((seq, ld), dtype=torch.int8, device=x.device)
+    s = torch.empty(seq, dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_quantize_act_i8(_p(x.contiguous()), _p(xq), _p(s), seq, K, ld, _stream()),
+          "vla_cuda_quantize_act_i8")
+    return xq, s
+
+
+def pack_weights_i8(W: torch.Tensor, ld: int | None = None):
+    """W [N, K] fp32 -> (Wq [N, ld] int8, wscale [N])."""
+    N, K = W.shape
+    ld = ld or i8_ld(K)
+    q = torch.empty((N, ld), dtype=torch.int8, device=W.device)
+    s = torch.empty(N, dtype=torch.float32, device=W.device)
+    check(lib().vla_cuda_pack_weights_i8(_p(W.contiguous()), _p(q), _p(s), N, K, ld, _stream()),
+          "vla_cuda_pack_weights_i8")
+    return q, s
+
+
+def gemm_i8(xq, ascale, Wq, wscale, K, bias=None, mode=0, res=None, out=None, amax=None, amax_rows=1,
+            force_simt=False, ascale_per_row=True):
+    """The W8A8 GEMM with its fused epilogue (vla_cuda_gemm_i8)."""
+    M, N = xq.shape[0], Wq.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.int32 if mode & EPI_ACC else torch.float32, device=xq.device)
+    ldr = res.stride(0) if res is not None else 0
+    check(lib().vla_cuda_gemm_i8(_p(out), out.stride(0), _p(xq), xq.stride(0), _p(ascale), 1 if ascale_per_row else 0,
+                                 _p(Wq), Wq.stride(0), _p(wscale), _p(bias), _p(res), ldr, M, N, K, mode, _p(amax),
+                                 amax_rows, 1 if force_simt else 0, _stream()), "vla_cuda_gemm_i8")
+    return out
+
+
+def dense_linear_i8(x, Wq, wscale, bias=None):
+    """tcpu::dense_linear_i8: fp32 x [seq, K] -> fp32 [seq, N], x quantized per token."""
+    seq, K = x.shape
+    N = Wq.shape[0]
+    out = torch.empty((seq, N), dtype=torch.float32, device=x.device)
+    xq = torch.empty((seq, i8_ld(K)), dtype=torch.int8, device=x.device)
+    s = torch.empty(seq, dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_dense_linear_i8(_p(out), _p(x.contiguous()), _p(Wq), _p(wscale), _p(bias), seq, N, K,
+                                         Wq.stride(0), _p(xq), _p(s), _stream()), "vla_cuda_dense_linear_i8")
+    return out
+
+
+def conv2d_i8(x, Wq, wscale, bias, Cout, k, stride, pad, clip=1.0, mode=0, res=None):
+    """tcpu::conv2d_i8 over F NHWC frames: x [F, H, W, Cin] -> [F, Ho, Wo, Cout]."""
+    F, H, W, Cin = x.shape
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    ldw = Wq.stride(0)
+    out = torch.empty((F, Ho, Wo, Cout), dtype=torch.float32, device=x.device)
+    col = torch.empty((F * Ho * Wo, ldw), dtype=torch.int8, device=x.device)
+    rs = torch.empty(F * Ho * Wo, dtype=torch.float32, device=x.device)
+    am = torch.zeros(F, dtype=torch.int32, device=x.device)
+    check(lib().vla_cuda_conv2d_i8(_p(out), _p(x.contiguous()), F, H, W, Cin, _p(Wq), ldw, _p(wscale), _p(bias), Cout,
+                                   k, stride, pad, clip, mode, _p(res), _p(col), _p(rs), _p(am), _stream()),
+          "vla_cuda_conv2d_i8")
+    return out
+
+
+def layernorm(x, w, b, eps=1e-5):
+    seq, H = x.shape
+    out = torch.empty_like(x)
+    check(lib().vla_cuda_layernorm(_p(out), _p(x.contiguous()), _p(w), _p(b), seq, H, eps, _stream()),
+          "vla_cuda_layernorm")
+    return out
+
+
+def gqa_attention(Q, K, V, n_q, n_kv, scale, mask=None, head_dim=64):
+    seq_q, seq_k = Q.shape[0], K.shape[0]
+    out = torch.empty((seq_q, n_q * head_dim), dtype=torch.float32, device=Q.device)
+    check(lib().vla_cuda_gqa_attention(_p(out), _p(Q.contiguous()), _p(K.contiguous()), _p(V.contiguous()), seq_q,
+                                       seq_k, n_q, n_kv, head_dim, scale, _p(mask), _stream()),
+          "vla_cuda_gqa_attention")
+    return out
+
+
+def maxpool2d_relu(x, k=3, stride=2, pad=1):
+    F, H, W, C = x.shape
+    Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    out = torch.empty((F, Ho, Wo, C), dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_maxpool2d_relu(_p(out), _p(x.contiguous()), F, H, W, C, k, stride, pad, _stream()),
+          "vla_cuda_maxpool2d_relu")
+    return out
+
+
+def device_status() -> int:
+    return int(lib().vla_cuda_device_status())
