@@ -108,6 +108,13 @@ VLA_API int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* 
                                        int32_t seq_q, int32_t seq_k, int32_t n_q, int32_t n_kv,
                                        int32_t head_dim, float scale, const float* mask, void* stream);
 
+/* replaces tcpu::dense_linear (src/ops/lm_ops.h, src/hal/avx2/gemm.cpp:98-122) for
+ * the small fp32 layers a policy keeps out of int8 (ACT's state projection and
+ * action head), in the reference's exact summation order:
+ * out [seq][N] = x [seq][K] . W [N][K]^T + bias. */
+VLA_API int32_t vla_cuda_dense_linear_f32(float* out, const float* x, const float* W, const float* bias,
+                                          int32_t seq, int32_t N, int32_t K, void* stream);
+
 /* replaces tcpu::maxpool2d_relu (src/hal/common/conv.cpp:192-225), F frames. */
 VLA_API int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H, int32_t W,
                                         int32_t C, int32_t k, int32_t stride, int32_t pad, void* stream);

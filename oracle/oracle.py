@@ -131,6 +131,7 @@ class Reference:
         l.ref_gqa_attention_masked.argtypes = [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP]
         l.ref_maxpool2d_relu.argtypes = [VP, VP, I32, I32, I32, I32, I32, I32]
         l.ref_relu.argtypes = [VP, I32]
+        l.ref_dense_linear.argtypes = [VP, VP, VP, VP, I32, I32, I32]
         l.vla_act_load.restype = VP
         l.vla_act_load.argtypes = [ctypes.c_char_p]
         l.vla_act_free.argtypes = [VP]
@@ -207,6 +208,14 @@ class Reference:
         Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
         out = np.zeros((Ho, Wo, C), np.float32)
         self.l.ref_maxpool2d_relu(_ptr(out), _ptr(x), H, W, C, k, stride, pad)
+        return out
+
+    def dense_linear(self, x, W, b):
+        x = np.ascontiguousarray(x, np.float32)
+        seq, K = x.shape
+        N = W.shape[0]
+        out = np.zeros((seq, N), np.float32)
+        self.l.ref_dense_linear(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(W, np.float32)), _ptr(b), seq, N, K)
         return out
 
     # --- policy level (the reference's own vla_act_* ABI)

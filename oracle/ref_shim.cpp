@@ -54,5 +54,8 @@ void ref_maxpool2d_relu(float* out, const float* x, int H, int W, int C, int k, 
     tcpu::maxpool2d_relu(out, x, H, W, C, k, stride, pad);
 }
 void ref_relu(float* x, int n) { tcpu::relu(x, n); }
+void ref_dense_linear(float* out, const float* x, const float* W, const float* bias, int seq, int N, int K) {
+    tcpu::dense_linear(out, x, W, bias, seq, N, K);
+}
 
 }  // extern "C"

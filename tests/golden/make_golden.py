@@ -32,6 +32,10 @@ from vla_simd_b200 import synth  # noqa: E402
 
 ACT_CASES = [("small", synth.ACT_SMALL, 63), ("small", synth.ACT_SMALL, 0), ("small", synth.ACT_SMALL, 31),
              ("small", synth.ACT_SMALL, 40), ("base", synth.ACT_BASELINE, 63)]
+# (seq_q, seq_k, n_q, n_kv): ACT encoder self, decoder self, decoder cross, GQA
+ATTN_CASES = [(602, 602, 8, 8), (100, 100, 8, 8), (100, 602, 8, 8), (50, 113, 15, 5), (3, 40, 4, 2)]
+LN_CASES = [(602, 512), (100, 512), (7, 960)]
+F32_LINEAR_CASES = [(1, 512, 6), (100, 6, 512), (5, 10, 37)]   # (seq, N, K): state_proj, head, odd
 GEMM_SHAPES = [(1, 16, 3), (7, 48, 64), (13, 64, 17), (257, 96, 48), (50, 768, 1027), (602, 3200, 512),
                (602, 512, 3200), (300, 512, 512)]
 
@@ -55,6 +59,35 @@ def gemm_inputs(seq, N, K, seed=11):
     W = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
     b = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
     return x, W, b
+
+
+def attn_inputs(sq, sk, nq, nkv, seed=21):
+    rng = np.random.default_rng(seed + sq + 3 * sk + 7 * nq)
+    Q = rng.standard_normal((sq, nq * 64), dtype=np.float32)
+    K = rng.standard_normal((sk, nkv * 64), dtype=np.float32)
+    V = rng.standard_normal((sk, nkv * 64), dtype=np.float32)
+    return Q, K, V
+
+
+def causal_mask(sq, sk):
+    i = np.arange(sq)[:, None]
+    j = np.arange(sk)[None, :]
+    return np.where(j > i + (sk - sq), -np.inf, 0.0).astype(np.float32)
+
+
+def ln_inputs(seq, H, seed=31):
+    rng = np.random.default_rng(seed + seq + H)
+    x = (rng.standard_normal((seq, H), dtype=np.float32) * np.float32(2.0) + np.float32(0.5)).astype(np.float32)
+    w = (1.0 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    b = (rng.standard_normal(H, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    return x, w, b
+
+
+def f32_linear_inputs(seq, N, K, seed=41):
+    rng = np.random.default_rng(seed + seq + N + K)
+    return (rng.standard_normal((seq, K), dtype=np.float32),
+            (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.05)).astype(np.float32),
+            rng.standard_normal(N, dtype=np.float32))
 
 
 def main():
@@ -95,6 +128,22 @@ def main():
                      "out": sha(out)}
         if seq * N <= 20000:
             arrays.update({f"{key}_xq": xq[:, :K], f"{key}_ascale": xs, f"{key}_acc": acc, f"{key}_out": out})
+    fp = {}
+    for sq, sk, nq, nkv in ATTN_CASES:
+        Q, K, V = attn_inputs(sq, sk, nq, nkv)
+        scale = np.float32(1.0) / np.sqrt(np.float32(64.0))
+        fp[f"attn_{sq}x{sk}x{nq}x{nkv}"] = sha(ref.attention(Q, K, V, nq, nkv, 64, scale))
+        fp[f"attn_causal_{sq}x{sk}x{nq}x{nkv}"] = sha(ref.attention(Q, K, V, nq, nkv, 64, scale,
+                                                                    causal_mask(sq, sk)))
+    for seq, H in LN_CASES:
+        x, w, b = ln_inputs(seq, H)
+        y = ref.layernorm(x, w, b, 1e-5)
+        fp[f"ln_{seq}x{H}"] = sha(y)
+        arrays[f"ln_{seq}x{H}"] = y
+    for seq, N, K in F32_LINEAR_CASES:
+        x, W, b = f32_linear_inputs(seq, N, K)
+        fp[f"f32lin_{seq}x{N}x{K}"] = sha(ref.dense_linear(x, W, b))
+    meta["fp32_ops"] = fp
     np.savez_compressed(os.path.join(HERE, "gemm.npz"), **arrays)
     with open(os.path.join(HERE, "gemm.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)

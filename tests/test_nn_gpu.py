@@ -154,3 +154,53 @@ def test_conv2d_i8_bit_exact(dev, restated, H, W, Cin, Cout, k, st, pd):
         want = restated.conv2d_i8(x[f], wqh, wsh, b, Cout, k, st, pd)
         assert np.array_equal(got[f].cpu().numpy().view(np.uint32), want.view(np.uint32))
     assert ops.device_status() == 0
+
+
+# ---- bit-exactness of the fp32 ops that feed int8 quantizers, against the
+# reference's own outputs (tests/golden/gemm.json, made by make_golden.py)
+
+def _golden():
+    import json
+    import os
+    import sys
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, here)
+    import make_golden
+    return make_golden, json.load(open(os.path.join(here, "gemm.json")))["fp32_ops"], here
+
+
+def test_attention_bit_exact_vs_reference(dev):
+    from vla_simd_b200 import ops
+    mg, fp, _ = _golden()
+    for sq, sk, nq, nkv in mg.ATTN_CASES:
+        Q, K, V = mg.attn_inputs(sq, sk, nq, nkv)
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(64.0)))
+        got = ops.gqa_attention(_t(Q, dev), _t(K, dev), _t(V, dev), nq, nkv, scale).cpu().numpy()
+        assert mg.sha(got) == fp[f"attn_{sq}x{sk}x{nq}x{nkv}"], (sq, sk, nq, nkv)
+        m = _t(mg.causal_mask(sq, sk), dev)
+        got = ops.gqa_attention(_t(Q, dev), _t(K, dev), _t(V, dev), nq, nkv, scale, mask=m).cpu().numpy()
+        assert mg.sha(got) == fp[f"attn_causal_{sq}x{sk}x{nq}x{nkv}"], ("causal", sq, sk, nq, nkv)
+
+
+def test_dense_linear_f32_bit_exact_vs_reference(dev):
+    from vla_simd_b200 import ops
+    mg, fp, _ = _golden()
+    for seq, N, K in mg.F32_LINEAR_CASES:
+        x, W, b = mg.f32_linear_inputs(seq, N, K)
+        got = ops.dense_linear_f32(_t(x, dev), _t(W, dev), _t(b, dev)).cpu().numpy()
+        assert mg.sha(got) == fp[f"f32lin_{seq}x{N}x{K}"], (seq, N, K)
+
+
+def test_layernorm_vs_reference_bits(dev):
+    """Double accumulation in a different order: identical bits except on
+    rare double->float rounding ties."""
+    import os
+    from vla_simd_b200 import ops
+    mg, fp, here = _golden()
+    z = np.load(os.path.join(here, "gemm.npz"))
+    for seq, H in mg.LN_CASES:
+        x, w, b = mg.ln_inputs(seq, H)
+        got = ops.layernorm(_t(x, dev), _t(w, dev), _t(b, dev), 1e-5).cpu().numpy()
+        want = z[f"ln_{seq}x{H}"]
+        diff = got.view(np.uint32) != want.view(np.uint32)
+        assert diff.mean() <= 1e-4 and np.abs(got - want).max() <= 1e-6

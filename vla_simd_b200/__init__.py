@@ -65,6 +65,7 @@ SIGNATURES = {
     "vla_cuda_layernorm": (I32, [VP, VP, VP, VP, I32, I32, F32, VP]),
     "vla_cuda_gqa_attention": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP, VP]),
     "vla_cuda_maxpool2d_relu": (I32, [VP, VP, I32, I32, I32, I32, I32, I32, I32, VP]),
+    "vla_cuda_dense_linear_f32": (I32, [VP, VP, VP, VP, I32, I32, I32, VP]),
     "vla_tcpu_int8_gemm_available": (I32, []),
     "vla_tcpu_i8_kpad": (I32, [I32]),
     "vla_tcpu_packed_i8_words": (ctypes.c_uint64, [I32, I32]),

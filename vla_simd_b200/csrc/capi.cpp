@@ -256,6 +256,12 @@ int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* K, const
                                     n_kv, head_dim, scale, mask, as_stream(stream)));
 }
 
+int32_t vla_cuda_dense_linear_f32(float* out, const float* x, const float* W, const float* bias, int32_t seq,
+                                  int32_t N, int32_t K, void* stream) {
+    if (!out || !x || !W || seq <= 0 || N <= 0 || K <= 0) return VLA_ERR_ARG;
+    return status_of(vsb::linear_f32(x, K, W, bias, out, N, seq, N, K, nullptr, nullptr, as_stream(stream)));
+}
+
 int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H, int32_t W, int32_t C, int32_t k,
                                 int32_t stride, int32_t pad, void* stream) {
     if (!out || !x || F <= 0 || H <= 0 || W <= 0 || C <= 0 || k <= 0 || stride <= 0 || pad < 0) return VLA_ERR_ARG;

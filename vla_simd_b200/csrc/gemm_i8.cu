@@ -17,12 +17,15 @@
 // multiples of 16 bytes (TMA stride rule). Bytes past K in a row are never read:
 // the tensor maps' inner extent is K, so TMA zero-fills the k-tail.
 //
-// CTA = 128 threads, one 128 x BN output tile:
-//   thread 0   TMA producer (A and B k-blocks of 128 bytes, STAGES-deep ring)
-//   thread 32  MMA issuer (4 x tcgen05.mma K=32 per k-block), commits free ring
-//              slots back to the producer and finally signals the epilogue
-//   warps 0-3  epilogue: warp w reads TMEM lanes [32w, 32w+32) = tile rows
-//              32w..32w+31 with tcgen05.ld, applies the epilogue, stores fp32.
+// CTA = 192 threads (6 warps, specialized), one 128 x BN output tile:
+//   warp 0     lane 0: TMA producer (A and B k-blocks of 128 bytes, STAGES ring)
+//   warp 1     TMEM allocation; lane 0: MMA issuer (4 x tcgen05.mma K=32 per
+//              k-block), commits free ring slots back to the producer and
+//              finally signals the epilogue
+//   warps 2-5  epilogue: warp w reads TMEM lanes [32(w%4), +32) = tile rows
+//              32(w%4).. with tcgen05.ld, applies the epilogue, stores fp32.
+// Only the epilogue warps wait on the accumulator barrier; the producer and
+// MMA warps never share a warp with a spinning waiter.
 #include "sm100.cuh"
 #include "gemm_i8.h"
 
@@ -39,7 +42,7 @@ namespace {
 constexpr int kBM = 128;          // UMMA M (one TMEM lane per tile row)
 constexpr int kBK = 128;          // bytes of K per pipeline stage (one SW128 atom row)
 constexpr int kUmmaK = 32;        // K per tcgen05.mma kind::i8
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;
 
 struct EpiParams {
     void* out;                    // float* (or int32_t* with kEpiAcc)
@@ -114,93 +117,144 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t tmem_base = *tmem_slot;
 
     int issued = 0;
-    if (threadIdx.x == 0) {
-        // ---- TMA producer
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % STAGES;
-            const int use = kb / STAGES;
-            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;
-            mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
-            tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
-            tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
-            issued = kb + 1;
-        }
-    } else if (threadIdx.x == 32) {
-        // ---- MMA issuer
-        int kb = 0;
-        for (; kb < nkb; ++kb) {
-            const int s = kb % STAGES;
-            if (!mbar_wait(&full[s], (kb / STAGES) & 1)) break;
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(sA + s * kABytes);
-            const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-            #pragma unroll
-            for (int k = 0; k < kBK / kUmmaK; ++k) {
-                umma_s8(tmem_base, sw128_kmajor_desc(a_addr + k * kUmmaK),
-                        sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                const int use = kb / STAGES;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;
+                mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
+                tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
+                issued = kb + 1;
             }
-            umma_commit(&empty[s]);
-            *s_consumed = kb + 1;
         }
-        if (kb == nkb) umma_commit(done);
-    }
-    __syncwarp();
-
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            int kb = 0;
+            for (; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                if (!mbar_wait(&full[s], (kb / STAGES) & 1)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + s * kABytes);
+                const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+                #pragma unroll
+                for (int k = 0; k < kBK / kUmmaK; ++k) {
+                    umma_s8(tmem_base, sw128_kmajor_desc(a_addr + k * kUmmaK),
+                            sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+                }
+                umma_commit(&empty[s]);
+                *s_consumed = kb + 1;
+            }
+            if (kb == nkb) umma_commit(done);
+        }
+        __syncwarp();
+    } else {
     // ---- epilogue
-    const bool ok = mbar_wait(done, 0);
+    // Phase A (thread = tile row, as TMEM hands it out): 32 accumulators of a
+    // 32-column chunk -> v = fma(acc*s_w, s_a, b) (or the raw int32 bits) into
+    // this warp's 32 x 33 shared staging tile. Phase B (coalesced): lane l
+    // covers columns 4*(l%8)..+3 of rows l/8 + 4i, so each store instruction
+    // writes four whole 128-byte row segments; the residual is read the same
+    // way. The staging tiles reuse the A ring (every MMA has completed).
+    // warp-uniform: the epilogue's tcgen05.ld and shuffles need every lane
+    const int quarter = warp & 3;   // TMEM lanes a warp may read: 32 * (warp id % 4)
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(done, 0));
     if (ok) {
         tc_fence_after();
-        const int row = warp * 32 + lane;
-        const int m = m0 + row;
-        const bool row_ok = m < p.M;
-        const float as = row_ok ? p.ascale[(long long)m * p.as_stride] : 0.0f;
-        float tmax = 0.0f;
+        float* stg = reinterpret_cast<float*>(sA) + quarter * (32 * 33);
+        const int row = quarter * 32 + lane;
+        const int m_row = m0 + row;
+        const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
+        const bool acc_mode = (p.mode & kEpiAcc) != 0;
+        const int cq = (lane & 7) * 4;       // phase B column offset in the chunk
+        const int rq = lane >> 3;            // phase B first row (0..3)
+        float tmax = 0.0f;                   // |out| max of this thread's tile row
         #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             uint32_t acc[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c * 32, acc);
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
             tmem_ld_wait();
-            const int nb = n0 + c * 32;
-            if (!row_ok || nb >= p.N) continue;
-            if (p.mode & kEpiAcc) {
-                int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + nb;
+            if (n0 + c * 32 >= p.N) continue;            // warp-uniform
+            #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                float v;
+                if (acc_mode) {
+                    v = __int_as_float(static_cast<int32_t>(acc[j]));
+                } else {
+                    v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_ws[c * 32 + j]), as,
+                                  s_b[c * 32 + j]);
+                    if (p.mode & kEpiRelu) v = (v < 0.0f) ? 0.0f : v;   // tcpu::relu (eltwise.cpp:213-214)
+                }
+                stg[lane * 33 + j] = v;
+            }
+            __syncwarp();
+            const int n = n0 + c * 32 + cq;
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = rq + 4 * i;
+                const int m = m0 + quarter * 32 + r;
+                if (m >= p.M || n >= p.N) continue;
+                float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
+                const bool full4 = n + 4 <= p.N;
+                if (acc_mode) {
+                    int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (n + e < p.N) o[e] = __float_as_int(v[e]);
+                    continue;
+                }
+                if (p.mode & (kEpiAdd | kEpiAddRelu)) {
+                    const float* rr = p.res + (long long)m * p.ldr + n;
+                    float rv[4];
+                    if (p.vec_ok && full4) {
+                        const float4 t = *reinterpret_cast<const float4*>(rr);
+                        rv[0] = t.x; rv[1] = t.y; rv[2] = t.z; rv[3] = t.w;
+                    } else {
+                        #pragma unroll
+                        for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
+                    }
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (p.mode & kEpiAdd) v[e] = __fadd_rn(rv[e], v[e]);             // x[i] += y[i]
+                        if (p.mode & kEpiAddRelu) {                                        // resnet_backbone.cpp:293-295
+                            v[e] = __fadd_rn(v[e], rv[e]);
+                            v[e] = v[e] > 0.0f ? v[e] : 0.0f;
+                        }
+                    }
+                    if (p.amax) {
+                        #pragma unroll
+                        for (int e = 0; e < 4; ++e) stg[r * 33 + cq + e] = v[e];
+                    }
+                }
+                float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
+                if (p.vec_ok && full4) {
+                    *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+                } else {
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (n + e < p.N) o[e] = v[e];
+                }
+            }
+            if (p.amax) {
+                // final values are back in the staging tile: per-row max, thread = row
+                __syncwarp();
                 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (nb + j < p.N) o[j] = static_cast<int32_t>(acc[j]);
-                continue;
+                    if (n0 + c * 32 + j < p.N) tmax = fmaxf(tmax, fabsf(stg[lane * 33 + j]));
             }
-            float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + nb;
-            const float* r = p.res ? p.res + (long long)m * p.ldr + nb : nullptr;
-            if (p.vec_ok && nb + 32 <= p.N) {
-                #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    float4 rv = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (r) rv = *reinterpret_cast<const float4*>(r + j);
-                    float4 v;
-                    v.x = epi_value(static_cast<int32_t>(acc[j + 0]), s_ws[c * 32 + j + 0], as, s_b[c * 32 + j + 0], p.mode, &rv.x);
-                    v.y = epi_value(static_cast<int32_t>(acc[j + 1]), s_ws[c * 32 + j + 1], as, s_b[c * 32 + j + 1], p.mode, &rv.y);
-                    v.z = epi_value(static_cast<int32_t>(acc[j + 2]), s_ws[c * 32 + j + 2], as, s_b[c * 32 + j + 2], p.mode, &rv.z);
-                    v.w = epi_value(static_cast<int32_t>(acc[j + 3]), s_ws[c * 32 + j + 3], as, s_b[c * 32 + j + 3], p.mode, &rv.w);
-                    tmax = fmaxf(tmax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                    *reinterpret_cast<float4*>(o + j) = v;
-                }
-            } else {
-                #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (nb + j >= p.N) continue;
-                    const float rv = r ? r[j] : 0.0f;
-                    const float v = epi_value(static_cast<int32_t>(acc[j]), s_ws[c * 32 + j], as, s_b[c * 32 + j], p.mode, &rv);
-                    tmax = fmaxf(tmax, fabsf(v));
-                    o[j] = v;
-                }
-            }
+            __syncwarp();
         }
         if (p.amax) {
             // one atomic per warp when the warp's rows share a slot, else per row
-            const unsigned key = row_ok ? static_cast<unsigned>(m / p.amax_rows) : 0xFFFFFFFFu;
+            const bool row_ok = m_row < p.M;
+            const unsigned key = row_ok ? static_cast<unsigned>(m_row / p.amax_rows) : 0xFFFFFFFFu;
             const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
-            if (__all_sync(0xFFFFFFFFu, key == k0)) {
-                float wm = tmax;
+            if (__all_sync(0xFFFFFFFFu, key == k0 || key == 0xFFFFFFFFu)) {
+                float wm = row_ok ? tmax : 0.0f;    // rows past M hold bias-only values
                 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
                 if (lane == 0 && k0 != 0xFFFFFFFFu) atomicMax(&p.amax[k0], __float_as_uint(wm));
@@ -209,6 +263,8 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
         }
     }
+
+    }   // epilogue warps
 
     tc_fence_before();
     __syncthreads();
@@ -330,17 +386,18 @@ EpiParams make_epi(const GemmI8Args& a) {
 }  // namespace
 
 int gemm_i8_pick_bn(int M, int N) {
-    // Fill the 148 SMs: prefer 128-wide tiles, fall back to 64 for narrow or
-    // few-row problems (conv stages with 64 output channels, short sequences).
+    // Fill the 148 SMs: the widest N tile that still yields ~0.8 waves of CTAs,
+    // else the narrowest (the 602-row transformer GEMMs, the deep conv stages).
     const int mt = (M + kBM - 1) / kBM;
-    if (N <= 64) return 64;
-    if (mt * ((N + 127) / 128) < 120) return 64;
-    return 128;
+    for (int bn : {128, 64, 32})
+        if (N > bn / 2 && mt * ((N + bn - 1) / bn) >= 120) return bn;
+    return 32;
 }
 
 cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, int bn,
                          cudaStream_t st) {
     const EpiParams p = make_epi(a);
+    if (bn == 32) return launch_umma<32, 4>(ta, tb, p, st);
     if (bn == 64) return launch_umma<64, 4>(ta, tb, p, st);
     if (bn == 256) return launch_umma<256, 4>(ta, tb, p, st);
     return launch_umma<128, 3>(ta, tb, p, st);
@@ -348,12 +405,17 @@ cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUten
 
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
-    if (!a.force_simt) {
+    const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
+                        (a.lda & 15) == 0 && (a.ldb & 15) == 0;
+    if (!a.force_simt && tma_ok) {
+        // operands TMA can describe always take the tensor-core kernel; a tensor
+        // map the driver refuses is an error, never a silent detour
         const int bn = gemm_i8_pick_bn(a.M, a.N);
         CUtensorMap ta, tb;
-        if (make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) &&
-            make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, bn))
-            return gemm_i8_umma(a, ta, tb, bn, st);
+        if (!make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) ||
+            !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, bn))
+            return cudaErrorInvalidConfiguration;
+        return gemm_i8_umma(a, ta, tb, bn, st);
     }
     const EpiParams p = make_epi(a);
     if ((a.N + 127) / 128 > 65535) return cudaErrorInvalidValue;

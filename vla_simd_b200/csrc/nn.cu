@@ -43,17 +43,102 @@ __device__ __forceinline__ float warp_max_f(float v) {
 //
 // Optional fused outputs, each a per-row int8 quantization of the normalized
 // row for the next W8A8 GEMM: q1 of (out + addend) and q2 of out.
+template <int V4>
+__global__ void __launch_bounds__(64)
+layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const float* __restrict__ w,
+                 const float* __restrict__ b, int M, int H, float eps, const float* __restrict__ addend,
+                 int8_t* __restrict__ q1, float* __restrict__ s1, int8_t* __restrict__ q2, float* __restrict__ s2,
+                 long long ldq) {
+    // one warp per row (two rows per 64-thread block, so a 602-row input spans
+    // every SM); lane l holds float4 groups l, l+32, ... (H % 4 == 0)
+    const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const int H4 = H >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * H);
+    float4 v[V4];
+    double sum = 0.0;
+    #pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        const int g = lane + 32 * i;
+        v[i] = g < H4 ? xr[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        sum += (double)v[i].x + (double)v[i].y + (double)v[i].z + (double)v[i].w;
+    }
+    const double mean = warp_sum_d(sum) / H;
+    double var = 0.0;
+    #pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        if (lane + 32 * i < H4) {
+            const double dx = (double)v[i].x - mean, dy = (double)v[i].y - mean;
+            const double dz = (double)v[i].z - mean, dw = (double)v[i].w - mean;
+            var += dx * dx + dy * dy + dz * dz + dw * dw;
+        }
+    }
+    var = warp_sum_d(var);
+    const float inv = (float)(1.0 / sqrt(var / H + (double)eps));
+    float4* orow = reinterpret_cast<float4*>(out + (long long)row * H);
+    const float4* ar = addend ? reinterpret_cast<const float4*>(addend + (long long)row * H) : nullptr;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* b4 = b ? reinterpret_cast<const float4*>(b) : nullptr;
+    float am1 = 0.0f, am2 = 0.0f;
+    float4 a[V4];
+    #pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        const int g = lane + 32 * i;
+        if (g < H4) {
+            const float4 ww = w4[g];
+            const float4 bb = b4 ? b4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float* e = reinterpret_cast<float*>(&v[i]);
+            const float* we = reinterpret_cast<const float*>(&ww);
+            const float* be = reinterpret_cast<const float*>(&bb);
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float xc = (float)((double)e[c] - mean);
+                e[c] = b4 ? __fmaf_rn(__fmul_rn(xc, inv), we[c], be[c]) : __fmul_rn(__fmul_rn(xc, inv), we[c]);
+                am2 = fmaxf(am2, fabsf(e[c]));
+            }
+            orow[g] = v[i];
+            if (ar) {
+                const float4 t = ar[g];
+                a[i] = make_float4(__fadd_rn(v[i].x, t.x), __fadd_rn(v[i].y, t.y), __fadd_rn(v[i].z, t.z),
+                                   __fadd_rn(v[i].w, t.w));
+                am1 = fmaxf(am1, fmaxf(fmaxf(fabsf(a[i].x), fabsf(a[i].y)), fmaxf(fabsf(a[i].z), fabsf(a[i].w))));
+            }
+        }
+    }
+    auto store_q = [&](int8_t* qbase, float* sbase, float m, bool use_a) {
+        m = warp_max_f(m);
+        const float sc = nn_row_scale(m), iv = __fdiv_rn(1.0f, sc);
+        char4* qr = reinterpret_cast<char4*>(qbase + (long long)row * ldq);
+        #pragma unroll
+        for (int i = 0; i < V4; ++i) {
+            const int g = lane + 32 * i;
+            if (g < H4) {
+                const float4 t = use_a ? a[i] : v[i];
+                qr[g] = make_char4(nn_q8(t.x, iv), nn_q8(t.y, iv), nn_q8(t.z, iv), nn_q8(t.w, iv));
+            }
+        }
+        for (long long h = H + 4 * lane; h < ldq; h += 128)
+            *reinterpret_cast<char4*>(qbase + (long long)row * ldq + h) = make_char4(0, 0, 0, 0);
+        if (lane == 0) sbase[row] = sc;
+    };
+    if (q1) store_q(q1, s1, ar ? am1 : am2, ar != nullptr);
+    if (q2) store_q(q2, s2, am2, false);
+}
+
+// Scalar twin of layernorm_kernel for rows that are not float4-shaped
+// (H % 4 != 0 or unaligned pointers): lane l holds elements l, l+32, ...
 template <int VPL>
-__global__ void layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const float* __restrict__ w,
-                                 const float* __restrict__ b, int M, int H, float eps,
-                                 const float* __restrict__ addend,
-                                 int8_t* __restrict__ q1, float* __restrict__ s1,
-                                 int8_t* __restrict__ q2, float* __restrict__ s2, long long ldq) {
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__global__ void __launch_bounds__(64)
+layernorm_scalar_kernel(const float* __restrict__ x, float* __restrict__ out, const float* __restrict__ w,
+                        const float* __restrict__ b, int M, int H, float eps, const float* __restrict__ addend,
+                        int8_t* __restrict__ q1, float* __restrict__ s1, int8_t* __restrict__ q2,
+                        float* __restrict__ s2, long long ldq) {
+    const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
     const float* xr = x + (long long)row * H;
-    float v[VPL];
+    float v[VPL], a[VPL];
     double sum = 0.0;
     #pragma unroll
     for (int i = 0; i < VPL; ++i) {
@@ -64,53 +149,43 @@ __global__ void layernorm_kernel(const float* __restrict__ x, float* __restrict_
     const double mean = warp_sum_d(sum) / H;
     double var = 0.0;
     #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-        const int h = lane + 32 * i;
-        if (h < H) {
+    for (int i = 0; i < VPL; ++i)
+        if (lane + 32 * i < H) {
             const double d = (double)v[i] - mean;
             var += d * d;
         }
-    }
     var = warp_sum_d(var);
     const float inv = (float)(1.0 / sqrt(var / H + (double)eps));
-    float* orow = out + (long long)row * H;
     float am1 = 0.0f, am2 = 0.0f;
-    const float* ar = addend ? addend + (long long)row * H : nullptr;
     #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const int h = lane + 32 * i;
+        a[i] = 0.0f;
         if (h < H) {
             const float xc = (float)((double)v[i] - mean);
-            const float y = b ? __fmaf_rn(__fmul_rn(xc, inv), w[h], b[h]) : __fmul_rn(__fmul_rn(xc, inv), w[h]);
-            v[i] = y;
-            orow[h] = y;
-            am2 = fmaxf(am2, fabsf(y));
-            if (ar) am1 = fmaxf(am1, fabsf(__fadd_rn(y, ar[h])));
+            v[i] = b ? __fmaf_rn(__fmul_rn(xc, inv), w[h], b[h]) : __fmul_rn(__fmul_rn(xc, inv), w[h]);
+            out[(long long)row * H + h] = v[i];
+            am2 = fmaxf(am2, fabsf(v[i]));
+            if (addend) {
+                a[i] = __fadd_rn(v[i], addend[(long long)row * H + h]);
+                am1 = fmaxf(am1, fabsf(a[i]));
+            }
         }
     }
-    if (q1) {
-        const float m = warp_max_f(ar ? am1 : am2);
+    for (int pass = 0; pass < 2; ++pass) {
+        int8_t* qb = pass == 0 ? q1 : q2;
+        if (!qb) continue;
+        const bool use_a = pass == 0 && addend;
+        const float m = warp_max_f(use_a ? am1 : am2);
         const float sc = nn_row_scale(m), iv = __fdiv_rn(1.0f, sc);
-        int8_t* qr = q1 + (long long)row * ldq;
+        int8_t* qr = qb + (long long)row * ldq;
         #pragma unroll
         for (int i = 0; i < VPL; ++i) {
             const int h = lane + 32 * i;
-            if (h < H) qr[h] = nn_q8(ar ? __fadd_rn(v[i], ar[h]) : v[i], iv);
+            if (h < H) qr[h] = nn_q8(use_a ? a[i] : v[i], iv);
         }
-        for (int h = H + lane; h < ldq; h += 32) qr[h] = 0;
-        if (lane == 0) s1[row] = sc;
-    }
-    if (q2) {
-        const float m = warp_max_f(am2);
-        const float sc = nn_row_scale(m), iv = __fdiv_rn(1.0f, sc);
-        int8_t* qr = q2 + (long long)row * ldq;
-        #pragma unroll
-        for (int i = 0; i < VPL; ++i) {
-            const int h = lane + 32 * i;
-            if (h < H) qr[h] = nn_q8(v[i], iv);
-        }
-        for (int h = H + lane; h < ldq; h += 32) qr[h] = 0;
-        if (lane == 0) s2[row] = sc;
+        for (long long h = H + lane; h < ldq; h += 32) qr[h] = 0;
+        if (lane == 0) (pass == 0 ? s1 : s2)[row] = sc;
     }
 }
 
@@ -118,167 +193,268 @@ cudaError_t layernorm(const float* x, float* out, const float* w, const float* b
                       const float* addend, int8_t* q1, float* s1, int8_t* q2, float* s2, long long ldq,
                       cudaStream_t st) {
     if (M <= 0 || H <= 0 || H > 2048 || ((q1 || q2) && ldq < H)) return cudaErrorInvalidValue;
-    const int threads = 256;
-    const int blocks = (M * 32 + threads - 1) / threads;
-    if (H <= 512)
-        layernorm_kernel<16><<<blocks, threads, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
-    else if (H <= 1024)
-        layernorm_kernel<32><<<blocks, threads, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
-    else
-        layernorm_kernel<64><<<blocks, threads, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+    const uintptr_t f16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                          reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b) |
+                          reinterpret_cast<uintptr_t>(addend);
+    const uintptr_t q4 = reinterpret_cast<uintptr_t>(q1) | reinterpret_cast<uintptr_t>(q2);
+    const bool vec = (H % 4 == 0) && (f16 & 15) == 0 && (q4 & 3) == 0 && (ldq % 4 == 0);
+    const int blocks = (M + 1) / 2;
+    if (vec) {
+        if (H <= 512)
+            layernorm_kernel<4><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+        else if (H <= 1024)
+            layernorm_kernel<8><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+        else
+            layernorm_kernel<16><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+    } else {
+        if (H <= 512)
+            layernorm_scalar_kernel<16><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+        else if (H <= 1024)
+            layernorm_scalar_kernel<32><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+        else
+            layernorm_scalar_kernel<64><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+    }
     return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- attention
-// softmax(Q K^T * scale + mask) V per head, fp32 throughout, flash-style
-// (online max / sum over 64-key tiles, scores never leave shared memory).
-// Semantics of the reference's gqa_attention_masked / _dense
-// (src/hal/avx2/attn.cpp:266-447, src/hal/common/attn.cpp:22-41): grouped KV
-// heads (kv = h / (n_q / n_kv)), an optional additive mask [seq_q][seq_k] whose
-// -inf / lowest entries block a key, and a fully-blocked row -> the uniform mean
-// of V over all seq_k keys.
+// softmax(Q K^T * scale + mask) V per head, fp32, reproducing the reference
+// x86 kernel's arithmetic (src/hal/avx2/attn.cpp:54-94, :134-162, :210-251)
+// operation for operation, so the int8 quantizers that follow see the same
+// bits as on the CPU:
+//   score[j] = (fma chain over d = 0..63 of q[d]*k[d], from 0) * scale
+//              (+ mask[j] for j below the row bound; -inf past it)
+//   e[j]     = cephes_exp(score[j] - max)   (0 where score - max <= -87)
+//   sum      = 8 lane sums (lane l adds e[l], e[l+8], ... in order), combined
+//              ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))    (hsum8, simd.h:52-59)
+//   p[j]     = e[j] * (1/sum)
+//   out[d]   = fma chain over keys j = 0.. of p[j]*v[j][d], from 0
+// A row whose every score is blocked (max <= lowest) gets the uniform mean of V
+// (attn_uniform_row, :45-52). Grouped KV heads: kv = h / (n_q / n_kv).
 //
-// CTA = 128 threads = 32 queries x 64 keys per tile of one head; thread (ty, tx)
-// owns query rows 4ty..4ty+3 and key columns tx, tx+16, tx+32, tx+48 of the
-// score tile, and output dims tx, tx+16, tx+32, tx+48 of those rows.
-constexpr int kAttQ = 32;
-constexpr int kAttK = 64;
+// CTA = one head x QT queries (32, or 16 for long key rows), 256 threads, the
+// whole score rows in shared memory (row stride = 8 banks apart). Three phases,
+// each a register-tiled loop whose per-output accumulation order is the
+// reference's:
+//   scores  thread = QT/8 queries x 2 keys of a 64-key tile; per d one 16-byte
+//           Q^T load (broadcast) + one 8-byte K^T load feed QT/4 fmas
+//   softmax 8 threads per row; thread t owns keys j = t (mod 8), i.e. exactly
+//           the reference's AVX lane t: its max, exp, and in-order lane sum
+//   A*V     thread = QT/16 queries x 4 dims; keys streamed in order through
+//           64-key V tiles, one 16-byte V load per key
 constexpr int kAttD = 64;
+constexpr int kAttKT = 64;   // keys per shared K^T / V tile
+constexpr int kAttThreads = 256;
 
-__global__ void __launch_bounds__(128)
+// The reference's Cephes-style exp (src/hal/avx2/simd.h:72-95), lane for lane.
+__device__ __forceinline__ float ref_exp(float x) {
+    const bool keep = !(x <= -87.0f);
+    x = (88.3762626647949f < x) ? 88.3762626647949f : x;
+    x = (-88.3762626647950f > x) ? -88.3762626647950f : x;
+    float fx = __fmaf_rn(x, 1.44269504088896341f, 0.5f);
+    fx = floorf(fx);
+    x = __fmaf_rn(-fx, 0.693359375f, x);
+    x = __fmaf_rn(-fx, -2.12194440e-4f, x);
+    float y = 1.9875691500e-4f;
+    y = __fmaf_rn(y, x, 1.3981999507e-3f);
+    y = __fmaf_rn(y, x, 8.3334519073e-3f);
+    y = __fmaf_rn(y, x, 4.1665795894e-2f);
+    y = __fmaf_rn(y, x, 1.6666665459e-1f);
+    y = __fmaf_rn(y, x, 5.0000001201e-1f);
+    y = __fmaf_rn(y, __fmul_rn(x, x), __fadd_rn(x, 1.0f));
+    const int n = __float2int_rn(fx);
+    y = __fmul_rn(y, __int_as_float((n + 127) << 23));
+    return keep ? y : 0.0f;
+}
+
+__host__ __device__ constexpr int att_row_stride(int seq_k) {
+    // ceil8(seq_k), rounded to whole bank rows, plus 8 so consecutive rows
+    // start 8 banks apart (the softmax phase reads 4 rows per warp)
+    return (((seq_k + 7) & ~7) + 31) / 32 * 32 + 8;
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kAttThreads)
 attention_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                  const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
                  int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
-    // dynamic shared memory (49.4 KB): Q tile, K^T tile (padded against bank
-    // conflicts on the transposed store), V tile, probabilities
-    extern __shared__ float att_smem[];
-    float (*sQ)[kAttD] = reinterpret_cast<float (*)[kAttD]>(att_smem);
-    float (*sKt)[kAttK + 1] = reinterpret_cast<float (*)[kAttK + 1]>(att_smem + kAttQ * kAttD);
-    float (*sV)[kAttD] = reinterpret_cast<float (*)[kAttD]>(att_smem + kAttQ * kAttD + kAttD * (kAttK + 1));
-    float (*sP)[kAttK] = reinterpret_cast<float (*)[kAttK]>(att_smem + kAttQ * kAttD + kAttD * (kAttK + 1) + kAttK * kAttD);
+    constexpr int QPT = QT / 8;      // queries per thread, score phase
+    constexpr int QPT2 = QT / 16;    // queries per thread, A*V phase
+    extern __shared__ __align__(16) float att_smem[];
+    const int ss = att_row_stride(seq_k);
+    const int skp = (seq_k + 7) & ~7;
+    float* sS = att_smem;                         // [QT][ss] scores -> probabilities
+    float* sQt = sS + QT * ss;                    // Q^T [64][QT]
+    float* sT = sQt + kAttD * QT;                 // K^T [64][64] or V [64][64]
 
     const int h = blockIdx.y;
     const int kvh = h / (n_q / n_kv);
-    const int q0 = blockIdx.x * kAttQ;
+    const int q0 = blockIdx.x * QT;
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;   // ty 0..7
+    const float NINF = __int_as_float(0xff800000);
 
-    for (int i = tid; i < kAttQ * kAttD; i += 128) {
-        const int r = i / kAttD, d = i - r * kAttD;
-        const int q = q0 + r;
-        sQ[r][d] = q < seq_q ? Q[(long long)q * ldq + (long long)h * kAttD + d] : 0.0f;
+    for (int i = tid; i < QT * kAttD; i += kAttThreads) {
+        const int q = i % QT, d = i / QT;
+        sQt[d * QT + q] = (q0 + q) < seq_q ? Q[(long long)(q0 + q) * ldq + (long long)h * kAttD + d] : 0.0f;
     }
 
-    float m_i[4], l_i[4], acc[4][4];
-    #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        m_i[r] = -INFINITY;
-        l_i[r] = 0.0f;
-        #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
-    }
-
-    for (int k0 = 0; k0 < seq_k; k0 += kAttK) {
-        __syncthreads();
-        for (int i = tid; i < kAttK * kAttD; i += 128) {
-            const int r = i / kAttD, d = i - r * kAttD;
-            const int kk = k0 + r;
-            sKt[d][r] = kk < seq_k ? K[(long long)kk * ldk + (long long)kvh * kAttD + d] : 0.0f;
-            sV[r][d] = kk < seq_k ? V[(long long)kk * ldv + (long long)kvh * kAttD + d] : 0.0f;
-        }
-        __syncthreads();
-
-        float s[4][4];
-        #pragma unroll
-        for (int r = 0; r < 4; ++r)
+    // ---- scores: thread (tq, tk) -> queries QPT*tq.., keys 2tk, 2tk+1 of the tile
+    {
+        const int tq = tid >> 5, tk = tid & 31;
+        for (int k0 = 0; k0 < seq_k; k0 += kAttKT) {
+            __syncthreads();
+            // K^T tile: consecutive threads take consecutive keys (conflict-free stores)
+            for (int i = tid; i < kAttKT * (kAttD / 4); i += kAttThreads) {
+                const int key = i % kAttKT, dg = i / kAttKT;
+                const int kk = k0 + key;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (kk < seq_k)
+                    v = *reinterpret_cast<const float4*>(K + (long long)kk * ldk + (long long)kvh * kAttD + dg * 4);
+                sT[(dg * 4 + 0) * kAttKT + key] = v.x;
+                sT[(dg * 4 + 1) * kAttKT + key] = v.y;
+                sT[(dg * 4 + 2) * kAttKT + key] = v.z;
+                sT[(dg * 4 + 3) * kAttKT + key] = v.w;
+            }
+            __syncthreads();
+            float acc[QPT][2];
             #pragma unroll
-            for (int c = 0; c < 4; ++c) s[r][c] = 0.0f;
-        #pragma unroll 8
-        for (int d = 0; d < kAttD; ++d) {
-            float qv[4], kv[4];
-            #pragma unroll
-            for (int r = 0; r < 4; ++r) qv[r] = sQ[4 * ty + r][d];
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) kv[c] = sKt[d][tx + 16 * c];
-            #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int a = 0; a < QPT; ++a) { acc[a][0] = 0.0f; acc[a][1] = 0.0f; }
+            #pragma unroll 4
+            for (int d = 0; d < kAttD; ++d) {
+                float qv[QPT];
                 #pragma unroll
-                for (int c = 0; c < 4; ++c) s[r][c] = fmaf(qv[r], kv[c], s[r][c]);
-        }
-
-        #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int q = q0 + 4 * ty + r;
-            float tmax = -INFINITY;
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int kk = k0 + tx + 16 * c;
-                float v = s[r][c] * scale;
-                if (kk >= seq_k) v = -INFINITY;
-                else if (mask && q < seq_q) {
-                    const float mv = mask[(long long)q * seq_k + kk];
-                    v = (mv <= -FLT_MAX) ? -INFINITY : v + mv;
+                for (int a = 0; a < QPT; a += 2) {
+                    const float2 t = *reinterpret_cast<const float2*>(sQt + d * QT + QPT * tq + a);
+                    qv[a] = t.x;
+                    qv[a + 1] = t.y;
                 }
-                s[r][c] = v;
-                tmax = fmaxf(tmax, v);
-            }
-            // the 16 threads of a row are lanes (ty&1)*16 .. +15 of one warp
-            #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xFFFFFFFFu, tmax, off));
-            const float m_new = fmaxf(m_i[r], tmax);
-            const float alpha = (m_i[r] == -INFINITY) ? 0.0f : expf(m_i[r] - m_new);
-            float psum = 0.0f;
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float pv = (m_new == -INFINITY) ? 0.0f : expf(s[r][c] - m_new);
-                sP[4 * ty + r][tx + 16 * c] = pv;
-                psum += pv;
-            }
-            #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xFFFFFFFFu, psum, off);
-            l_i[r] = l_i[r] * alpha + psum;
-            m_i[r] = m_new;
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) acc[r][c] *= alpha;
-        }
-        __syncwarp();
-        // sP rows 4ty..4ty+3 are written and read by the same 16 threads
-        // (half of one warp), so a warp barrier is enough here.
-        const int kn = min(kAttK, seq_k - k0);
-        for (int j = 0; j < kn; ++j) {
-            float pv[4];
-            #pragma unroll
-            for (int r = 0; r < 4; ++r) pv[r] = sP[4 * ty + r][j];
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float vv = sV[j][tx + 16 * c];
+                const float2 kv = *reinterpret_cast<const float2*>(sT + d * kAttKT + 2 * tk);
                 #pragma unroll
-                for (int r = 0; r < 4; ++r) acc[r][c] = fmaf(pv[r], vv, acc[r][c]);
+                for (int a = 0; a < QPT; ++a) {
+                    acc[a][0] = __fmaf_rn(qv[a], kv.x, acc[a][0]);
+                    acc[a][1] = __fmaf_rn(qv[a], kv.y, acc[a][1]);
+                }
+            }
+            const int kk = k0 + 2 * tk;
+            if (kk < skp) {
+                #pragma unroll
+                for (int a = 0; a < QPT; ++a)
+                    *reinterpret_cast<float2*>(sS + (QPT * tq + a) * ss + kk) =
+                        make_float2(__fmul_rn(acc[a][0], scale), __fmul_rn(acc[a][1], scale));
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- softmax rows: 8 threads per row, thread t = the reference's lane t
+    {
+        const int r = tid >> 3, t = tid & 7;
+        if (r < QT) {
+            const int q = q0 + r;
+            float* srow = sS + r * ss;
+            const float* mrow = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
+            // row bound: trailing `lowest` mask entries block keys (hal::row_bound).
+            // The shuffle is outside any row-dependent branch: every lane of
+            // the warp reaches it (rows past seq_q have no mask row).
+            int last = seq_k - 1;
+            if (mrow) {
+                last = -1;
+                for (int j = t; j < seq_k; j += 8)
+                    if (mrow[j] != -FLT_MAX) last = j;
+            }
+            #pragma unroll
+            for (int off = 4; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
+            const int jmax = last + 1;
+            float mx = NINF;
+            for (int j = t; j < skp; j += 8) {
+                float v = srow[j];
+                if (j >= jmax) v = NINF;
+                else if (mrow) v = __fadd_rn(v, mrow[j]);
+                srow[j] = v;
+                mx = fmaxf(mx, v);
+            }
+            #pragma unroll
+            for (int off = 4; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+            const bool degenerate = !(mx > -FLT_MAX);
+            float lane_sum = 0.0f;
+            if (!degenerate) {
+                for (int j = t; j < skp; j += 8) {
+                    const float e = ref_exp(__fsub_rn(srow[j], mx));
+                    srow[j] = e;
+                    lane_sum = __fadd_rn(lane_sum, e);
+                }
+            }
+            float l[8];
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, lane_sum, (threadIdx.x & 24) | i);
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[1], l[5])),
+                                        __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
+            if (degenerate) {
+                // fully blocked row: uniform weights over every key (attn_uniform_row)
+                const float u = __fdiv_rn(1.0f, (float)seq_k);
+                for (int j = t; j < skp; j += 8) srow[j] = j < seq_k ? u : 0.0f;
+            } else {
+                const float inv = __fdiv_rn(1.0f, sum);
+                for (int j = t; j < skp; j += 8) srow[j] = __fmul_rn(srow[j], inv);
             }
         }
     }
 
-    // fully-blocked rows: uniform mean of V over every key
+    // ---- A*V: thread (tq2, td) -> queries QPT2*tq2.., dims 4td..4td+3, keys in order
+    const int tq2 = tid >> 4, td = tid & 15;
+    float o[QPT2][4];
     #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int q = q0 + 4 * ty + r;
-        if (q >= seq_q) continue;
-        float* o = O + (long long)q * ldo + (long long)h * kAttD;
-        if (m_i[r] == -INFINITY) {
-            const float u = __fdiv_rn(1.0f, (float)seq_k);
+    for (int a = 0; a < QPT2; ++a)
+        #pragma unroll
+        for (int c = 0; c < 4; ++c) o[a][c] = 0.0f;
+    for (int k0 = 0; k0 < seq_k; k0 += kAttKT) {
+        __syncthreads();
+        for (int i = tid; i < kAttKT * (kAttD / 4); i += kAttThreads) {
+            const int key = i / (kAttD / 4), dg = i % (kAttD / 4);
+            const int kk = k0 + key;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (kk < seq_k)
+                v = *reinterpret_cast<const float4*>(V + (long long)kk * ldv + (long long)kvh * kAttD + dg * 4);
+            *reinterpret_cast<float4*>(sT + key * kAttD + dg * 4) = v;
+        }
+        __syncthreads();
+        const int kn = min(kAttKT, seq_k - k0);
+        for (int j = 0; j < kn; ++j) {
+            const float4 vv = *reinterpret_cast<const float4*>(sT + j * kAttD + 4 * td);
             #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int d = tx + 16 * c;
-                float a = 0.0f;
-                for (int kk = 0; kk < seq_k; ++kk) a = fmaf(u, V[(long long)kk * ldv + (long long)kvh * kAttD + d], a);
-                o[d] = a;
+            for (int a = 0; a < QPT2; ++a) {
+                const float pv = sS[(QPT2 * tq2 + a) * ss + k0 + j];
+                o[a][0] = __fmaf_rn(pv, vv.x, o[a][0]);
+                o[a][1] = __fmaf_rn(pv, vv.y, o[a][1]);
+                o[a][2] = __fmaf_rn(pv, vv.z, o[a][2]);
+                o[a][3] = __fmaf_rn(pv, vv.w, o[a][3]);
             }
-        } else {
-            const float invl = __fdiv_rn(1.0f, l_i[r]);
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) o[tx + 16 * c] = acc[r][c] * invl;
         }
     }
+    #pragma unroll
+    for (int a = 0; a < QPT2; ++a) {
+        const int q = q0 + QPT2 * tq2 + a;
+        if (q < seq_q)
+            *reinterpret_cast<float4*>(O + (long long)q * ldo + (long long)h * kAttD + 4 * td) =
+                make_float4(o[a][0], o[a][1], o[a][2], o[a][3]);
+    }
+}
+
+template <int QT>
+cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                             long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                             float scale, const float* mask, size_t smem, cudaStream_t st) {
+    static int configured = 0;
+    if ((int)smem > configured) {
+        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = (int)smem;
+    }
+    dim3 grid((seq_q + QT - 1) / QT, n_q);
+    attention_kernel<QT><<<grid, kAttThreads, smem, st>>>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv,
+                                                          scale, mask);
+    return cudaGetLastError();
 }
 
 cudaError_t attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
@@ -286,16 +462,18 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
                       const float* mask, cudaStream_t st) {
     if (head_dim != kAttD || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv)
         return cudaErrorInvalidValue;
-    constexpr size_t smem = sizeof(float) * (kAttQ * kAttD + kAttD * (kAttK + 1) + kAttK * kAttD + kAttQ * kAttK);
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
-    dim3 grid((seq_q + kAttQ - 1) / kAttQ, n_q);
-    attention_kernel<<<grid, 128, smem, st>>>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask);
-    return cudaGetLastError();
+    // 16-byte vector loads of Q/K/V/O rows
+    if (((ldq | ldk | ldv | ldo) & 3) ||
+        ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V) |
+          reinterpret_cast<uintptr_t>(O)) & 15))
+        return cudaErrorInvalidValue;
+    const size_t ss = (size_t)att_row_stride(seq_k);
+    auto need = [&](int qt) { return sizeof(float) * (qt * ss + (size_t)kAttD * qt + (size_t)kAttKT * kAttD); };
+    if (need(32) <= 112 * 1024)   // two CTAs per SM
+        return launch_attention<32>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(32), st);
+    if (need(16) <= 220 * 1024)
+        return launch_attention<16>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(16), st);
+    return cudaErrorInvalidValue;   // > ~3400 keys: not a shape any policy here has
 }
 
 // --------------------------------------------------------- max-pool + ReLU
@@ -304,17 +482,19 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
 // next conv's per-tensor quantization.
 __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restrict__ out, int F, int H, int W, int C,
                                     int k, int stride, int pad, int Ho, int Wo, unsigned int* __restrict__ amax) {
-    const long long total = (long long)F * Ho * Wo * C;
+    // blockIdx.y = frame, so a block's absmax goes to one slot: reduce in the
+    // block, then one atomic per block
+    const int f = blockIdx.y;
     const long long per_frame = (long long)Ho * Wo * C;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int f = static_cast<int>(i / per_frame);
-        const long long r = i - f * per_frame;
+    const float* xf = x + (long long)f * H * W * C;
+    float* of = out + (long long)f * per_frame;
+    float bmax = 0.0f;
+    for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < per_frame;
+         r += (long long)gridDim.x * blockDim.x) {
         const int c = static_cast<int>(r % C);
         const int pix = static_cast<int>(r / C);
         const int oy = pix / Wo, ox = pix - oy * Wo;
         float o = -INFINITY;
-        const float* xf = x + (long long)f * H * W * C;
         for (int ky = 0; ky < k; ++ky) {
             const int iy = oy * stride - pad + ky;
             if (iy < 0 || iy >= H) continue;
@@ -326,18 +506,30 @@ __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restri
             }
         }
         if (!(o > 0.0f)) o = 0.0f;
-        out[i] = o;
-        if (amax) atomicMax(&amax[f], __float_as_uint(o));
+        of[r] = o;
+        bmax = fmaxf(bmax, o);
+    }
+    if (amax) {
+        bmax = warp_max_f(bmax);
+        __shared__ float wm[32];
+        if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = bmax;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = 0.0f;
+            for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, wm[i]);
+            atomicMax(&amax[f], __float_as_uint(m));
+        }
     }
 }
 
 cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C, int k, int stride, int pad,
                          int Ho, int Wo, unsigned int* amax, cudaStream_t st) {
-    const long long total = (long long)F * Ho * Wo * C;
-    if (total <= 0) return cudaErrorInvalidValue;
-    long long blocks = (total + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    maxpool_relu_kernel<<<(int)blocks, 256, 0, st>>>(x, out, F, H, W, C, k, stride, pad, Ho, Wo, amax);
+    const long long per_frame = (long long)Ho * Wo * C;
+    if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
+    long long bx = (per_frame + 255) / 256;
+    if (bx > 148 * 8) bx = 148 * 8;
+    maxpool_relu_kernel<<<dim3((unsigned)bx, (unsigned)F), 256, 0, st>>>(x, out, F, H, W, C, k, stride, pad, Ho, Wo,
+                                                                        amax);
     return cudaGetLastError();
 }
 
@@ -347,72 +539,125 @@ cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C,
 __global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* __restrict__ out, int F, long long npx,
                                         const float* __restrict__ mean, const float* __restrict__ stdv, float eps,
                                         unsigned int* __restrict__ amax) {
+    const int f = blockIdx.y;
     const long long per_frame = npx * 3;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < F * per_frame;
+    const uint8_t* src = img + (long long)f * per_frame;
+    float* dst = out + (long long)f * per_frame;
+    float bmax = 0.0f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_frame;
          i += (long long)gridDim.x * blockDim.x) {
-        const int f = static_cast<int>(i / per_frame);
-        const int c = static_cast<int>((i - f * per_frame) % 3);
-        const float p = __fdiv_rn((float)img[i], 255.0f);
+        const int c = static_cast<int>(i % 3);
+        const float p = __fdiv_rn((float)src[i], 255.0f);
         const float v = __fdiv_rn(__fsub_rn(p, mean[f * 3 + c]), __fadd_rn(stdv[f * 3 + c], eps));
-        out[i] = v;
-        if (amax) {
-            float a = fabsf(v);
-            // frames are whole blocks apart only by chance: reduce per warp when uniform
-            const unsigned fk = static_cast<unsigned>(f);
-            const unsigned msk = __activemask();
-            const unsigned f0 = __shfl_sync(msk, fk, __ffs(msk) - 1);
-            if (msk == 0xFFFFFFFFu && __all_sync(msk, fk == f0)) {
-                a = warp_max_f(a);
-                if ((threadIdx.x & 31) == 0) atomicMax(&amax[f], __float_as_uint(a));
-            } else {
-                atomicMax(&amax[f], __float_as_uint(a));
-            }
+        dst[i] = v;
+        bmax = fmaxf(bmax, fabsf(v));
+    }
+    if (amax) {
+        bmax = warp_max_f(bmax);
+        __shared__ float wm[32];
+        if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = bmax;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = 0.0f;
+            for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, wm[i]);
+            atomicMax(&amax[f], __float_as_uint(m));
         }
     }
 }
 
 cudaError_t normalize_frames(const uint8_t* img, float* out, int F, long long npx, const float* mean,
                              const float* stdv, float eps, unsigned int* amax, cudaStream_t st) {
-    const long long total = (long long)F * npx * 3;
-    if (total <= 0) return cudaErrorInvalidValue;
-    long long blocks = (total + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    normalize_frames_kernel<<<(int)blocks, 256, 0, st>>>(img, out, F, npx, mean, stdv, eps, amax);
+    const long long per_frame = npx * 3;
+    if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
+    long long bx = (per_frame + 255) / 256;
+    if (bx > 148 * 8) bx = 148 * 8;
+    normalize_frames_kernel<<<dim3((unsigned)bx, (unsigned)F), 256, 0, st>>>(img, out, F, npx, mean, stdv, eps, amax);
     return cudaGetLastError();
 }
 
 // ------------------------------------------------------ small fp32 linears
-// out[m][n] = bias[n] + sum_k x[m][k] * W[n][k], one warp per output, k in
-// order per lane then a fixed tree: fp32 dense_linear (src/hal/avx2/gemm.cpp:98-122)
-// up to summation order. Optional elementwise affine on the result
-// (out = out*post_mul[n] + post_add[n]: ACT's action unnormalization).
+// The reference's fp32 dense_linear (src/hal/avx2/gemm.cpp:98-122), reproduced
+// per output: outputs in a whole block of 4 take mm_block4's order (two 8-lane
+// accumulators over 16-wide k steps, an 8-wide step into the first, hsum8 of
+// their sum, scalar fma tail; :33-86), the rest simd_dot's (four 8-lane chains
+// over 32-wide steps; simd.h:12-40); then + bias. One thread per output - these
+// are ACT's K=6 state projection and N=6 action head, where exact replication
+// costs nothing. Optional post affine (action unnormalization):
+// out = fma(out, post_mul[n], post_add[n]).
+__device__ __forceinline__ float hsum8_ref(const float (&a)[8]) {
+    return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])),
+                     __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
+}
+
 __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ W,
                                   const float* __restrict__ bias, float* __restrict__ out, long long ldo,
                                   int M, int N, int K, const float* __restrict__ post_mul,
                                   const float* __restrict__ post_add) {
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (gw >= M * N) return;
-    const int m = gw / N, n = gw - m * N;
+    const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (gid >= (long long)M * N) return;
+    const int m = static_cast<int>(gid / N), n = static_cast<int>(gid - (long long)m * N);
     const float* xr = x + (long long)m * ldx;
     const float* wr = W + (long long)n * K;
-    float a = 0.0f;
-    for (int k = lane; k < K; k += 32) a = fmaf(xr[k], wr[k], a);
-    #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, off);
-    if (lane == 0) {
-        float v = a + (bias ? bias[n] : 0.0f);
-        if (post_mul) v = fmaf(v, post_mul[n], post_add[n]);
-        out[(long long)m * ldo + n] = v;
+    float s;
+    int k = 0;
+    const bool block4 = n < N - N % 4;
+    if (block4) {
+        float a[8], b[8];
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) { a[l] = 0.0f; b[l] = 0.0f; }
+        for (; k + 16 <= K; k += 16) {
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) {
+                a[l] = __fmaf_rn(xr[k + l], wr[k + l], a[l]);
+                b[l] = __fmaf_rn(xr[k + 8 + l], wr[k + 8 + l], b[l]);
+            }
+        }
+        for (; k + 8 <= K; k += 8) {
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) a[l] = __fmaf_rn(xr[k + l], wr[k + l], a[l]);
+        }
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) a[l] = __fadd_rn(a[l], b[l]);
+        s = hsum8_ref(a);
+    } else {
+        float c0[8], c1[8], c2[8], c3[8];
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) { c0[l] = 0.0f; c1[l] = 0.0f; c2[l] = 0.0f; c3[l] = 0.0f; }
+        for (; k + 32 <= K; k += 32) {
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) {
+                c0[l] = __fmaf_rn(xr[k + l], wr[k + l], c0[l]);
+                c1[l] = __fmaf_rn(xr[k + 8 + l], wr[k + 8 + l], c1[l]);
+                c2[l] = __fmaf_rn(xr[k + 16 + l], wr[k + 16 + l], c2[l]);
+                c3[l] = __fmaf_rn(xr[k + 24 + l], wr[k + 24 + l], c3[l]);
+            }
+        }
+        for (; k + 8 <= K; k += 8) {
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) c0[l] = __fmaf_rn(xr[k + l], wr[k + l], c0[l]);
+        }
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) c0[l] = __fadd_rn(__fadd_rn(c0[l], c1[l]), __fadd_rn(c2[l], c3[l]));
+        s = hsum8_ref(c0);
     }
+    // scalar tails: mm_block4's is contracted to fma by the reference's
+    // -ffp-contract=fast build, simd_dot's stays a rounded multiply then add
+    // (both established against the compiled reference on odd K)
+    if (block4)
+        for (; k < K; ++k) s = __fmaf_rn(xr[k], wr[k], s);
+    else
+        for (; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], wr[k]));
+    float v = bias ? __fadd_rn(s, bias[n]) : s;
+    if (post_mul) v = __fmaf_rn(v, post_mul[n], post_add[n]);
+    out[(long long)m * ldo + n] = v;
 }
 
 cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
-    const long long threads = (long long)M * N * 32;
-    linear_f32_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, ldx, W, bias, out, ldo, M, N, K, post_mul,
-                                                                      post_add);
+    const long long total = (long long)M * N;
+    linear_f32_kernel<<<(int)((total + 127) / 128), 128, 0, st>>>(x, ldx, W, bias, out, ldo, M, N, K, post_mul,
+                                                                   post_add);
     return cudaGetLastError();
 }
 

@@ -38,25 +38,38 @@ __device__ __forceinline__ int8_t q8_span(float v, float inv) {
     return static_cast<int8_t>(__float2int_rn(t));
 }
 
-// One warp per row. x [M][ldx] (+ optional addend [M][lda_] added first, in fp32,
-// like ActTransformer::encode's xq = x + pos). Writes q [M][ldq] (zero past K)
-// and scale [M]. A second output pair (q2/s2) quantizes x without the addend.
-__global__ void quantize_rows_kernel(const float* __restrict__ x, long long ldx,
-                                     const float* __restrict__ addend, long long lda_,
-                                     int M, int K,
-                                     int8_t* __restrict__ q, long long ldq, float* __restrict__ scale,
-                                     int8_t* __restrict__ q2, long long ldq2, float* __restrict__ scale2) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// One warp per row (two rows per 64-thread block). x [M][ldx] (+ optional
+// addend [M][lda_] added first, in fp32, like ActTransformer::encode's
+// xq = x + pos). Writes q [M][ldq] (zero past K) and scale [M]. A second output
+// pair (q2/s2) quantizes x without the addend in the same pass. float4 loads /
+// 4-byte int8 stores when every row is 16-byte aligned and K % 4 == 0.
+template <bool VEC>
+__global__ void __launch_bounds__(64)
+quantize_rows_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ addend, long long lda_,
+                     int M, int K, int8_t* __restrict__ q, long long ldq, float* __restrict__ scale,
+                     int8_t* __restrict__ q2, long long ldq2, float* __restrict__ scale2) {
+    const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (warp >= M) return;
-    const float* xr = x + (long long)warp * ldx;
-    const float* ar = addend ? addend + (long long)warp * lda_ : nullptr;
-
+    if (row >= M) return;
+    const float* xr = x + (long long)row * ldx;
+    const float* ar = addend ? addend + (long long)row * lda_ : nullptr;
     float m1 = 0.0f, m2 = 0.0f;
-    for (int k = lane; k < K; k += 32) {
-        const float v = xr[k];
-        m2 = fmaxf(m2, fabsf(v));
-        if (ar) m1 = fmaxf(m1, fabsf(__fadd_rn(v, ar[k])));
+    if (VEC) {
+        for (int k = 4 * lane; k < K; k += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + k);
+            m2 = fmaxf(m2, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            if (ar) {
+                const float4 t = *reinterpret_cast<const float4*>(ar + k);
+                m1 = fmaxf(m1, fmaxf(fmaxf(fabsf(__fadd_rn(v.x, t.x)), fabsf(__fadd_rn(v.y, t.y))),
+                                     fmaxf(fabsf(__fadd_rn(v.z, t.z)), fabsf(__fadd_rn(v.w, t.w)))));
+            }
+        }
+    } else {
+        for (int k = lane; k < K; k += 32) {
+            const float v = xr[k];
+            m2 = fmaxf(m2, fabsf(v));
+            if (ar) m1 = fmaxf(m1, fabsf(__fadd_rn(v, ar[k])));
+        }
     }
     #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -65,15 +78,35 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, long long ldx,
     }
     if (!ar) m1 = m2;
     const float s1 = row_scale(m1), inv1 = __fdiv_rn(1.0f, s1);
-    int8_t* qr = q + (long long)warp * ldq;
-    for (int k = lane; k < ldq; k += 32)
-        qr[k] = k < K ? q8(ar ? __fadd_rn(xr[k], ar[k]) : xr[k], inv1) : 0;
-    if (lane == 0) scale[warp] = s1;
-    if (q2) {
-        const float s2 = row_scale(m2), inv2 = __fdiv_rn(1.0f, s2);
-        int8_t* qr2 = q2 + (long long)warp * ldq2;
-        for (int k = lane; k < ldq2; k += 32) qr2[k] = k < K ? q8(xr[k], inv2) : 0;
-        if (lane == 0) scale2[warp] = s2;
+    const float s2 = row_scale(m2), inv2 = __fdiv_rn(1.0f, s2);
+    int8_t* qr = q + (long long)row * ldq;
+    int8_t* qr2 = q2 ? q2 + (long long)row * ldq2 : nullptr;
+    if (VEC) {
+        for (int k = 4 * lane; k < K; k += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + k);
+            if (ar) {
+                const float4 t = *reinterpret_cast<const float4*>(ar + k);
+                *reinterpret_cast<char4*>(qr + k) =
+                    make_char4(q8(__fadd_rn(v.x, t.x), inv1), q8(__fadd_rn(v.y, t.y), inv1),
+                               q8(__fadd_rn(v.z, t.z), inv1), q8(__fadd_rn(v.w, t.w), inv1));
+            } else {
+                *reinterpret_cast<char4*>(qr + k) = make_char4(q8(v.x, inv1), q8(v.y, inv1), q8(v.z, inv1), q8(v.w, inv1));
+            }
+            if (qr2)
+                *reinterpret_cast<char4*>(qr2 + k) = make_char4(q8(v.x, inv2), q8(v.y, inv2), q8(v.z, inv2), q8(v.w, inv2));
+        }
+        for (long long k = K + 4 * lane; k < ldq; k += 128) *reinterpret_cast<char4*>(qr + k) = make_char4(0, 0, 0, 0);
+        if (qr2)
+            for (long long k = K + 4 * lane; k < ldq2; k += 128) *reinterpret_cast<char4*>(qr2 + k) = make_char4(0, 0, 0, 0);
+    } else {
+        for (long long k = lane; k < ldq; k += 32)
+            qr[k] = k < K ? q8(ar ? __fadd_rn(xr[k], ar[k]) : xr[k], inv1) : 0;
+        if (qr2)
+            for (long long k = lane; k < ldq2; k += 32) qr2[k] = k < K ? q8(xr[k], inv2) : 0;
+    }
+    if (lane == 0) {
+        scale[row] = s1;
+        if (scale2) scale2[row] = s2;
     }
 }
 
@@ -132,20 +165,44 @@ __global__ void im2col_i8_kernel(const float* __restrict__ x, int F, int H, int 
                 }
             }
             *reinterpret_cast<int4*>(dst) = *reinterpret_cast<int4*>(out);
+        }
+    }
+}
+
+// im2col for small channel counts (the 3-channel stem): one thread per (output
+// row, kernel tap) copies that tap's C contiguous NHWC values; the extra tap
+// k*k zero-fills the row's padding [K, ldc).
+__global__ void im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride,
+                                      int pad, int Ho, int Wo, int K, long long ldc,
+                                      const unsigned int* __restrict__ amax_bits, float clip,
+                                      int8_t* __restrict__ col, float* __restrict__ rscale) {
+    const int taps = k * k + 1;
+    const long long total = (long long)F * Ho * Wo * taps;
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const long long row = t / taps;
+        const int tap = static_cast<int>(t - row * taps);
+        const int npix = Ho * Wo;
+        const int f = static_cast<int>(row / npix);
+        const int pix = static_cast<int>(row - (long long)f * npix);
+        const float amax = __uint_as_float(amax_bits[f]);
+        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+        int8_t* dst = col + row * ldc;
+        if (tap == k * k) {
+            for (long long i = K; i < ldc; ++i) dst[i] = 0;
+            rscale[row] = s;
+            continue;
+        }
+        const float inv = __fdiv_rn(1.0f, s);
+        const int oy = pix / Wo, ox = pix - oy * Wo;
+        const int ky = tap / k, kx = tap - ky * k;
+        const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+        int8_t* d = dst + tap * C;
+        if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
+            for (int c = 0; c < C; ++c) d[c] = 0;
         } else {
-            #pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                const int kk = k0 + i;
-                int8_t v = 0;
-                if (kk < K) {
-                    const int tap = kk / C, ci = kk - tap * C;
-                    const int ky = tap / k, kx = tap - ky * k;
-                    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-                    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
-                        v = q8_span(xf[((long long)iy * W + ix) * C + ci], inv);
-                }
-                dst[i] = v;
-            }
+            const float* src = x + (((long long)f * H + iy) * W + ix) * C;
+            for (int c = 0; c < C; ++c) d[c] = q8_span(src[c], inv);
         }
     }
 }
@@ -200,9 +257,15 @@ cudaError_t quantize_rows(const float* x, long long ldx, const float* addend, lo
                           int8_t* q, long long ldq, float* scale, int8_t* q2, long long ldq2, float* scale2,
                           cudaStream_t st) {
     if (M <= 0 || K <= 0 || ldq < K || (q2 && ldq2 < K)) return cudaErrorInvalidValue;
-    const int threads = 256;
-    const int blocks = (M * 32 + threads - 1) / threads;
-    quantize_rows_kernel<<<blocks, threads, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+    const uintptr_t fa = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(addend);
+    const uintptr_t qa = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(q2);
+    const bool vec = (K % 4 == 0) && (fa & 15) == 0 && (qa & 3) == 0 && (ldx % 4 == 0) &&
+                     (!addend || ld_add % 4 == 0) && (ldq % 4 == 0) && (!q2 || ldq2 % 4 == 0);
+    const int blocks = (M + 1) / 2;
+    if (vec)
+        quantize_rows_kernel<true><<<blocks, 64, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+    else
+        quantize_rows_kernel<false><<<blocks, 64, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
     return cudaGetLastError();
 }
 
@@ -214,7 +277,7 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
     const bool v16 = (C % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(col) & 15) == 0);
     const long long rows = (long long)F * Ho * Wo;
-    const long long total = rows * (ldc / (v16 ? 16 : 4));
+    const long long total = v16 ? rows * (ldc / 16) : rows * (k * k + 1);
     const int threads = 256;
     long long blocks = (total + threads - 1) / threads;
     if (blocks > 148 * 64) blocks = 148 * 64;
@@ -222,8 +285,8 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
         im2col_i8_kernel<16><<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
                                                               amax_bits, clip, col, rscale);
     else
-        im2col_i8_kernel<4><<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
-                                                             amax_bits, clip, col, rscale);
+        im2col_i8_taps_kernel<<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
+                                                               amax_bits, clip, col, rscale);
     return cudaGetLastError();
 }
 

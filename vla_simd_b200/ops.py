@@ -112,5 +112,15 @@ def maxpool2d_relu(x, k=3, stride=2, pad=1):
     return out
 
 
+def dense_linear_f32(x, W, bias=None):
+    """tcpu::dense_linear (fp32), the reference's summation order."""
+    seq, K = x.shape
+    N = W.shape[0]
+    out = torch.empty((seq, N), dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_dense_linear_f32(_p(out), _p(x.contiguous()), _p(W.contiguous()), _p(bias), seq, N, K,
+                                          _stream()), "vla_cuda_dense_linear_f32")
+    return out
+
+
 def device_status() -> int:
     return int(lib().vla_cuda_device_status())
