@@ -548,6 +548,7 @@ cudaError_t ActPolicy::run_linear(const DevLinear& l, const float* x_f32, const 
         a.mode = mode;
         a.amax = amax;
         a.amax_rows = amax_rows;
+        a.static_weights = true;   // uploaded once at load
         (void)tmap_a;
         return gemm_i8(a, st);
     }
@@ -580,6 +581,7 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
         a.mode = mode;
         a.amax = amax_out;
         a.amax_rows = Ho * Wo;
+        a.static_weights = true;
         return gemm_i8(a, st);
     }
     VSB_TRY(im2col_f32(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, d_col_f_, st));
@@ -659,7 +661,7 @@ cudaError_t ActPolicy::run_decoder(cudaStream_t st, bool unnormalize) {
     // cross-attention keys / values: q(enc + pos) is in qa, q(enc) in qb
     // (last encoder LN2). With one decoder layer they are used once; with
     // more, each layer projects them with its own weights.
-    VSB_TRY(cudaMemsetAsync(d_dx_, 0, sizeof(float) * C * d, st));   // queries start at zero
+    // (queries start at zero: d_dx_ was cleared by the step prologue)
     for (const DecLayerDev& l : dec_) {
         if (!l.c_wk.int8) VSB_TRY(add_f32(d_x_, d_pos_, d_xp_, (long long)T * d, st));   // fp32 keys read enc + pos
         VSB_TRY(run_linear(l.c_wk, d_xp_, d_qea_, d_sea_, nullptr, T, d_ck_, d, 0, nullptr, 0, st));
@@ -699,11 +701,11 @@ cudaError_t ActPolicy::run_decoder(cudaStream_t st, bool unnormalize) {
 
 cudaError_t ActPolicy::forward(cudaStream_t st, bool unnormalize) {
     const int d = cfg_.dim;
-    VSB_TRY(cudaMemsetAsync(d_amax_, 0, sizeof(unsigned int) * n_amax_, st));
+    // absmax slots and decoder queries zeroed, latent token placed, state normalized
+    VSB_TRY(act_prologue(d_amax_, n_amax_, d_dx_, (long long)cfg_.chunk * d, d_x_, d_latent_, d, d_state_,
+                         d_state_mean_, d_state_std_, norm_eps_, d_state_n_, cfg_.state_dim, st));
     VSB_TRY(run_backbone(st));
     // tokens: [latent | state_proj(state_norm) | img_proj(features per camera)]
-    VSB_TRY(cudaMemcpyAsync(d_x_, d_latent_, sizeof(float) * d, cudaMemcpyDeviceToDevice, st));
-    VSB_TRY(normalize_state(d_state_, d_state_mean_, d_state_std_, norm_eps_, d_state_n_, cfg_.state_dim, st));
     VSB_TRY(linear_f32(d_state_n_, cfg_.state_dim, state_proj_.W, state_proj_.bias, d_x_ + d, d, 1, d,
                        cfg_.state_dim, nullptr, nullptr, st));
     const int img_rows = n_cams_ * fh_ * fw_;

@@ -4,6 +4,7 @@
 // ReLU, absmax tap). Summation order differs from the CPU's packed kernels, so
 // these layers match the reference to fp32 rounding, not bit for bit.
 #include "sm100.cuh"
+#include "launch.cuh"
 #include "f32.h"
 #include "gemm_i8.h"
 
@@ -17,6 +18,8 @@ gemm_f32_kernel(const float* __restrict__ A, long long lda, const float* __restr
                 const float* __restrict__ bias, float* __restrict__ out, long long ldo,
                 const float* __restrict__ res, long long ldr, int M, int N, int K, int mode,
                 unsigned int* __restrict__ amax, int amax_rows) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     __shared__ float sA[kFK][kFT + 4];
     __shared__ float sW[kFK][kFT + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -67,13 +70,19 @@ cudaError_t gemm_f32(const float* A, long long lda, const float* W, long long ld
                      unsigned int* amax, int amax_rows, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
     dim3 grid((N + kFT - 1) / kFT, (M + kFT - 1) / kFT);
-    gemm_f32_kernel<<<grid, 256, 0, st>>>(A, lda, W, ldw, bias, out, ldo, res, ldr, M, N, K, mode, amax,
+    {
+        const cudaError_t le_ = launch_k(gemm_f32_kernel, grid, 256, 0, st,
+                                         A, lda, W, ldw, bias, out, ldo, res, ldr, M, N, K, mode, amax,
                                           amax_rows > 0 ? amax_rows : 1);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
 __global__ void im2col_f32_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride, int pad,
                                   int Ho, int Wo, int K, float* __restrict__ col) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const long long total = (long long)F * Ho * Wo * K;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
          t += (long long)gridDim.x * blockDim.x) {
@@ -98,7 +107,11 @@ cudaError_t im2col_f32(const float* x, int F, int H, int W, int C, int k, int st
     if (total <= 0) return cudaErrorInvalidValue;
     long long blocks = (total + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
-    im2col_f32_kernel<<<(int)blocks, 256, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, k * k * C, col);
+    {
+        const cudaError_t le_ = launch_k(im2col_f32_kernel, (int)blocks, 256, 0, st,
+                                         x, F, H, W, C, k, stride, pad, Ho, Wo, k * k * C, col);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@
 // Only the epilogue warps wait on the accumulator barrier; the producer and
 // MMA warps never share a warp with a spinning waiter.
 #include "sm100.cuh"
+#include "launch.cuh"
 #include "gemm_i8.h"
 
 #include <cuda_runtime.h>
@@ -58,6 +59,8 @@ struct EpiParams {
     int mode;
     int M, N, K;
     int vec_ok;                   // 16-byte aligned rows: float4 stores
+    int static_weights;           // B / wscale / bias never written by a kernel:
+                                  // safe to read before the predecessor finishes
 };
 
 __device__ __forceinline__ float epi_value(int32_t acc, float ws, float as, float b, int mode,
@@ -96,6 +99,8 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int n0 = blockIdx.x * BN;
     const int m0 = blockIdx.y * kBM;
     const int nkb = (p.K + kBK - 1) / kBK;
+    // weights that a predecessor kernel may still be writing: wait up front
+    if (!p.static_weights) pdl_wait();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -115,15 +120,28 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above touched only on-chip state and constant weights; let the
+    // next kernel in the stream start its own setup.
+    pdl_trigger();
 
     int issued = 0;
     if (warp == 0) {
         if (lane == 0) {
-            // ---- TMA producer
-            for (int kb = 0; kb < nkb; ++kb) {
+            // ---- TMA producer. The weight halves of the first ring slots do not
+            // depend on earlier kernels: issue them before waiting for the
+            // predecessor, then the activation halves.
+            const int pre = nkb < STAGES ? nkb : STAGES;
+            for (int kb = 0; kb < pre; ++kb) {
+                mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
+                tma_load_2d(sB + kb * kBBytes, &tmap_b, &full[kb], kb * kBK, n0);
+            }
+            pdl_wait();
+            for (int kb = 0; kb < pre; ++kb) tma_load_2d(sA + kb * kABytes, &tmap_a, &full[kb], kb * kBK, m0);
+            issued = pre;
+            for (int kb = pre; kb < nkb; ++kb) {
                 const int s = kb % STAGES;
                 const int use = kb / STAGES;
-                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;
+                if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
                 mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
                 tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
                 tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
@@ -163,6 +181,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // warp-uniform: the epilogue's tcgen05.ld and shuffles need every lane
     const int quarter = warp & 3;   // TMEM lanes a warp may read: 32 * (warp id % 4)
     const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(done, 0));
+    pdl_wait();   // activation scales / residual / output: predecessor data
     if (ok) {
         tc_fence_after();
         float* stg = reinterpret_cast<float*>(sA) + quarter * (32 * 33);
@@ -285,6 +304,8 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // of the tensor-core kernel in the tests. Same epilogue, bit for bit.
 __global__ void w8a8_simt_kernel(const int8_t* __restrict__ A, long long lda,
                                  const int8_t* __restrict__ B, long long ldb, const EpiParams p) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int n = blockIdx.y * blockDim.x + threadIdx.x;
     const int m = blockIdx.x;
     if (n >= p.N || m >= p.M) return;
@@ -357,7 +378,11 @@ cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiP
         configured = true;
     }
     dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
-    w8a8_umma_kernel<BN, STAGES><<<grid, kThreads, smem, st>>>(ta, tb, p);
+    {
+        const cudaError_t le_ = launch_k(w8a8_umma_kernel<BN, STAGES>, grid, kThreads, smem, st,
+                                         ta, tb, p);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -377,6 +402,7 @@ EpiParams make_epi(const GemmI8Args& a) {
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
+    p.static_weights = a.static_weights ? 1 : 0;
     const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
     p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 &&
                (!a.res || ((rb & 15) == 0 && (a.ldr & 3) == 0));
@@ -420,7 +446,11 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     const EpiParams p = make_epi(a);
     if ((a.N + 127) / 128 > 65535) return cudaErrorInvalidValue;
     dim3 grid(a.M, (a.N + 127) / 128);
-    w8a8_simt_kernel<<<grid, 128, 0, st>>>(a.A, a.lda, a.B, a.ldb, p);
+    {
+        const cudaError_t le_ = launch_k(w8a8_simt_kernel, grid, 128, 0, st,
+                                         a.A, a.lda, a.B, a.ldb, p);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

@@ -32,6 +32,8 @@ struct GemmI8Args {
     int amax_rows = 1;
     int mode = 0;
     bool force_simt = false;     // route to the CUDA-core kernel (tests / odd strides)
+    bool static_weights = false; // B/wscale/bias are load-time constants: the kernel may
+                                 // fetch them before its predecessor in the stream ends
 };
 
 // Launch on `st`. Tensor-core path when lda/ldb/A/B are 16-byte aligned,

@@ -1,0 +1,29 @@
+// Kernel launch with programmatic dependent launch (see pdl_wait / pdl_trigger
+// in sm100.cuh). Captured into a CUDA graph, consecutive launches become
+// programmatic edges, so a kernel's launch, on-chip setup and weight loads
+// overlap its predecessor's tail.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace vsb {
+
+// Set to false (VLA_CUDA_PDL=0) to launch plainly, for A/B timing.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace vsb

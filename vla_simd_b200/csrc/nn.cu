@@ -3,12 +3,22 @@
 // ReLU, camera-frame normalization, and the two tiny fp32 linears ACT keeps in
 // full precision (state projection K=6, action head N=6).
 #include "sm100.cuh"
+#include "launch.cuh"
 #include "nn.h"
 
 #include <cfloat>
 #include <cmath>
+#include <cstdlib>
 
 namespace vsb {
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("VLA_CUDA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 __device__ __forceinline__ float nn_row_scale(float amax) {
     return amax > 0.0f ? fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN) : 1.0f;
@@ -49,6 +59,8 @@ layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const flo
                  const float* __restrict__ b, int M, int H, float eps, const float* __restrict__ addend,
                  int8_t* __restrict__ q1, float* __restrict__ s1, int8_t* __restrict__ q2, float* __restrict__ s2,
                  long long ldq) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     // one warp per row (two rows per 64-thread block, so a 602-row input spans
     // every SM); lane l holds float4 groups l, l+32, ... (H % 4 == 0)
     const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
@@ -134,6 +146,8 @@ layernorm_scalar_kernel(const float* __restrict__ x, float* __restrict__ out, co
                         const float* __restrict__ b, int M, int H, float eps, const float* __restrict__ addend,
                         int8_t* __restrict__ q1, float* __restrict__ s1, int8_t* __restrict__ q2,
                         float* __restrict__ s2, long long ldq) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -201,18 +215,42 @@ cudaError_t layernorm(const float* x, float* out, const float* w, const float* b
     const int blocks = (M + 1) / 2;
     if (vec) {
         if (H <= 512)
-            layernorm_kernel<4><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_kernel<4>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
         else if (H <= 1024)
-            layernorm_kernel<8><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_kernel<8>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
         else
-            layernorm_kernel<16><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_kernel<16>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
     } else {
         if (H <= 512)
-            layernorm_scalar_kernel<16><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_scalar_kernel<16>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
         else if (H <= 1024)
-            layernorm_scalar_kernel<32><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_scalar_kernel<32>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
         else
-            layernorm_scalar_kernel<64><<<blocks, 64, 0, st>>>(x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+            {
+                const cudaError_t le_ = launch_k(layernorm_scalar_kernel<64>, blocks, 64, 0, st,
+                                                 x, out, w, b, M, H, eps, addend, q1, s1, q2, s2, ldq);
+                if (le_ != cudaSuccess) return le_;
+            }
     }
     return cudaGetLastError();
 }
@@ -278,6 +316,8 @@ __global__ void __launch_bounds__(kAttThreads)
 attention_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                  const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
                  int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     constexpr int QPT = QT / 8;      // queries per thread, score phase
     constexpr int QPT2 = QT / 16;    // queries per thread, A*V phase
     extern __shared__ __align__(16) float att_smem[];
@@ -452,8 +492,12 @@ cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long
         configured = (int)smem;
     }
     dim3 grid((seq_q + QT - 1) / QT, n_q);
-    attention_kernel<QT><<<grid, kAttThreads, smem, st>>>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv,
+    {
+        const cudaError_t le_ = launch_k(attention_kernel<QT>, grid, kAttThreads, smem, st,
+                                         Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv,
                                                           scale, mask);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -482,6 +526,8 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
 // next conv's per-tensor quantization.
 __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restrict__ out, int F, int H, int W, int C,
                                     int k, int stride, int pad, int Ho, int Wo, unsigned int* __restrict__ amax) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     // blockIdx.y = frame, so a block's absmax goes to one slot: reduce in the
     // block, then one atomic per block
     const int f = blockIdx.y;
@@ -528,8 +574,12 @@ cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C,
     if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
     long long bx = (per_frame + 255) / 256;
     if (bx > 148 * 8) bx = 148 * 8;
-    maxpool_relu_kernel<<<dim3((unsigned)bx, (unsigned)F), 256, 0, st>>>(x, out, F, H, W, C, k, stride, pad, Ho, Wo,
+    {
+        const cudaError_t le_ = launch_k(maxpool_relu_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st,
+                                         x, out, F, H, W, C, k, stride, pad, Ho, Wo,
                                                                         amax);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -539,6 +589,8 @@ cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C,
 __global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* __restrict__ out, int F, long long npx,
                                         const float* __restrict__ mean, const float* __restrict__ stdv, float eps,
                                         unsigned int* __restrict__ amax) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int f = blockIdx.y;
     const long long per_frame = npx * 3;
     const uint8_t* src = img + (long long)f * per_frame;
@@ -571,7 +623,11 @@ cudaError_t normalize_frames(const uint8_t* img, float* out, int F, long long np
     if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
     long long bx = (per_frame + 255) / 256;
     if (bx > 148 * 8) bx = 148 * 8;
-    normalize_frames_kernel<<<dim3((unsigned)bx, (unsigned)F), 256, 0, st>>>(img, out, F, npx, mean, stdv, eps, amax);
+    {
+        const cudaError_t le_ = launch_k(normalize_frames_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st,
+                                         img, out, F, npx, mean, stdv, eps, amax);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -593,6 +649,8 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
                                   const float* __restrict__ bias, float* __restrict__ out, long long ldo,
                                   int M, int N, int K, const float* __restrict__ post_mul,
                                   const float* __restrict__ post_add) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (gid >= (long long)M * N) return;
     const int m = static_cast<int>(gid / N), n = static_cast<int>(gid - (long long)m * N);
@@ -656,28 +714,48 @@ cudaError_t linear_f32(const float* x, long long ldx, const float* W, const floa
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
     const long long total = (long long)M * N;
-    linear_f32_kernel<<<(int)((total + 127) / 128), 128, 0, st>>>(x, ldx, W, bias, out, ldo, M, N, K, post_mul,
+    {
+        const cudaError_t le_ = launch_k(linear_f32_kernel, (int)((total + 127) / 128), 128, 0, st,
+                                         x, ldx, W, bias, out, ldo, M, N, K, post_mul,
                                                                    post_add);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
-// (state - mean) / (std + eps): ActModel::predict (src/models/act/act_model.cpp:151-153)
-__global__ void normalize_state_kernel(const float* __restrict__ s, const float* __restrict__ mean,
-                                       const float* __restrict__ stdv, float eps, float* __restrict__ out, int n) {
-    const int i = threadIdx.x;
-    if (i < n) out[i] = __fdiv_rn(__fsub_rn(s[i], mean[i]), __fadd_rn(stdv[i], eps));
+// First kernel of an ACT step: zero the per-frame absmax slots and the decoder
+// queries, place the latent token, and normalize the state,
+// (state - mean) / (std + eps) as ActModel::predict (src/models/act/act_model.cpp:151-153).
+// Doing this in a kernel keeps the captured step a single chain of kernels.
+__global__ void act_prologue_kernel(unsigned int* __restrict__ zero_u32, int n_zero_u32, float* __restrict__ zero_f32,
+                                    long long n_zero_f32, float* __restrict__ tok0, const float* __restrict__ latent,
+                                    int d, const float* __restrict__ state, const float* __restrict__ mean,
+                                    const float* __restrict__ stdv, float eps, float* __restrict__ state_n, int n) {
+    pdl_wait();     // the previous step may still read these buffers
+    pdl_trigger();
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = tid; i < n_zero_u32; i += stride) zero_u32[i] = 0u;
+    for (long long i = tid; i < n_zero_f32; i += stride) zero_f32[i] = 0.0f;
+    for (long long i = tid; i < d; i += stride) tok0[i] = latent[i];
+    for (long long i = tid; i < n; i += stride)
+        state_n[i] = __fdiv_rn(__fsub_rn(state[i], mean[i]), __fadd_rn(stdv[i], eps));
 }
 
-cudaError_t normalize_state(const float* s, const float* mean, const float* stdv, float eps, float* out, int n,
-                            cudaStream_t st) {
-    if (n <= 0 || n > 1024) return cudaErrorInvalidValue;
-    normalize_state_kernel<<<1, 1024, 0, st>>>(s, mean, stdv, eps, out, n);
+cudaError_t act_prologue(unsigned int* zero_u32, int n_zero_u32, float* zero_f32, long long n_zero_f32, float* tok0,
+                         const float* latent, int d, const float* state, const float* mean, const float* stdv,
+                         float eps, float* state_n, int n, cudaStream_t st) {
+    const cudaError_t le_ = launch_k(act_prologue_kernel, 64, 256, 0, st, zero_u32, n_zero_u32, zero_f32, n_zero_f32,
+                                     tok0, latent, d, state, mean, stdv, eps, state_n, n);
+    if (le_ != cudaSuccess) return le_;
     return cudaGetLastError();
 }
 
 // out = a + b, elementwise (fp32 inputs of fp32-path q/k projections)
 __global__ void add_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
                                long long n) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = __fadd_rn(a[i], b[i]);
 }
@@ -686,7 +764,11 @@ cudaError_t add_f32(const float* a, const float* b, float* out, long long n, cud
     if (n <= 0) return cudaErrorInvalidValue;
     long long blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    add_f32_kernel<<<(int)blocks, 256, 0, st>>>(a, b, out, n);
+    {
+        const cudaError_t le_ = launch_k(add_f32_kernel, (int)blocks, 256, 0, st,
+                                         a, b, out, n);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

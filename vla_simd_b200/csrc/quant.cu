@@ -13,6 +13,7 @@
 // accumulated its absmax (per frame) into a float-bits slot, so im2col reads
 // fp32, quantizes with the frame's scale and writes the int8 patch rows once.
 #include "sm100.cuh"
+#include "launch.cuh"
 #include "quant.h"
 
 #include <cfloat>
@@ -48,6 +49,8 @@ __global__ void __launch_bounds__(64)
 quantize_rows_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ addend, long long lda_,
                      int M, int K, int8_t* __restrict__ q, long long ldq, float* __restrict__ scale,
                      int8_t* __restrict__ q2, long long ldq2, float* __restrict__ scale2) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int row = blockIdx.x * 2 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -121,6 +124,8 @@ __global__ void im2col_i8_kernel(const float* __restrict__ x, int F, int H, int 
                                  int k, int stride, int pad, int Ho, int Wo, int K, long long ldc,
                                  const unsigned int* __restrict__ amax_bits, float clip,
                                  int8_t* __restrict__ col, float* __restrict__ rscale) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const long long groups_per_row = ldc / VEC;
     const long long total = (long long)F * Ho * Wo * groups_per_row;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
@@ -176,6 +181,8 @@ __global__ void im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H,
                                       int pad, int Ho, int Wo, int K, long long ldc,
                                       const unsigned int* __restrict__ amax_bits, float clip,
                                       int8_t* __restrict__ col, float* __restrict__ rscale) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int taps = k * k + 1;
     const long long total = (long long)F * Ho * Wo * taps;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
@@ -211,6 +218,8 @@ __global__ void im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H,
 // [slot*per_slot, (slot+1)*per_slot); one atomic per block.
 __global__ void absmax_kernel(const float* __restrict__ x, long long per_slot,
                               unsigned int* __restrict__ amax_bits) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const float* xs = x + (long long)blockIdx.y * per_slot;
     float v = 0.0f;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_slot;
@@ -232,6 +241,8 @@ __global__ void absmax_kernel(const float* __restrict__ x, long long per_slot,
 // :79-84) -> device rows [N][ldw] (zero past K).
 __global__ void unpack_panels_kernel(const int8_t* __restrict__ panels, int N, int K, int8_t* __restrict__ rows,
                                      long long ldw) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
     const int Kp = (K + 3) & ~3, KG = Kp / 4;
     const long long total = (long long)N * ldw;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -249,7 +260,11 @@ cudaError_t unpack_panels_i8(const int8_t* panels, int N, int K, int8_t* rows, l
     const long long total = (long long)N * ldw;
     long long blocks = (total + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    unpack_panels_kernel<<<(int)blocks, 256, 0, st>>>(panels, N, K, rows, ldw);
+    {
+        const cudaError_t le_ = launch_k(unpack_panels_kernel, (int)blocks, 256, 0, st,
+                                         panels, N, K, rows, ldw);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -263,9 +278,17 @@ cudaError_t quantize_rows(const float* x, long long ldx, const float* addend, lo
                      (!addend || ld_add % 4 == 0) && (ldq % 4 == 0) && (!q2 || ldq2 % 4 == 0);
     const int blocks = (M + 1) / 2;
     if (vec)
-        quantize_rows_kernel<true><<<blocks, 64, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+        {
+            const cudaError_t le_ = launch_k(quantize_rows_kernel<true>, blocks, 64, 0, st,
+                                             x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+            if (le_ != cudaSuccess) return le_;
+        }
     else
-        quantize_rows_kernel<false><<<blocks, 64, 0, st>>>(x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+        {
+            const cudaError_t le_ = launch_k(quantize_rows_kernel<false>, blocks, 64, 0, st,
+                                             x, ldx, addend, ld_add, M, K, q, ldq, scale, q2, ldq2, scale2);
+            if (le_ != cudaSuccess) return le_;
+        }
     return cudaGetLastError();
 }
 
@@ -282,11 +305,19 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
     long long blocks = (total + threads - 1) / threads;
     if (blocks > 148 * 64) blocks = 148 * 64;
     if (v16)
-        im2col_i8_kernel<16><<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
+        {
+            const cudaError_t le_ = launch_k(im2col_i8_kernel<16>, (int)blocks, threads, 0, st,
+                                             x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
                                                               amax_bits, clip, col, rscale);
+            if (le_ != cudaSuccess) return le_;
+        }
     else
-        im2col_i8_taps_kernel<<<(int)blocks, threads, 0, st>>>(x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
+        {
+            const cudaError_t le_ = launch_k(im2col_i8_taps_kernel, (int)blocks, threads, 0, st,
+                                             x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
                                                                amax_bits, clip, col, rscale);
+            if (le_ != cudaSuccess) return le_;
+        }
     return cudaGetLastError();
 }
 
@@ -297,7 +328,11 @@ cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsign
     long long bx = (per_slot + threads - 1) / threads;
     if (bx > 296) bx = 296;
     dim3 grid((unsigned)bx, (unsigned)(n / per_slot));
-    absmax_kernel<<<grid, threads, 0, st>>>(x, per_slot, amax_bits);
+    {
+        const cudaError_t le_ = launch_k(absmax_kernel, grid, threads, 0, st,
+                                         x, per_slot, amax_bits);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

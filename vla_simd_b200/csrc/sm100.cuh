@@ -41,6 +41,18 @@ __device__ __forceinline__ void record_status(int code) {
     atomicCAS(&g_vsb_status, 0, code);
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Every kernel of the library is launched with programmatic stream
+// serialization (launch.cuh): it may start while the previous kernel in the
+// stream is still running. pdl_wait() blocks the calling thread until that
+// kernel has completed and its memory is visible; each kernel calls it before
+// touching anything a predecessor writes or reads (only constant weights and
+// on-chip setup come before it). pdl_trigger() lets the next kernel be
+// scheduled; it is safe anywhere, since a dependent only starts once every CTA
+// of this grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ----------------------------------------------------------------- mbarrier --
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
