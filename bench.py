@@ -242,6 +242,57 @@ def time_gemm(torch, dev, n_cold=30, n_warm_graph=50, n_lin=10):
             "dense_linear_i8_us_cold": statistics.median(lin) * 1e6}
 
 
+def run_op(name: str, iters: int = 20):
+    """One op at its ACT-step shape, timed alone (also the small cases ncu captures use)."""
+    import torch
+    from vla_simd_b200 import EPI_ADD, EPI_RELU, ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rnd = lambda *sh, s=1.0: (torch.randn(*sh, generator=g) * s).to(dev)  # noqa: E731
+    T, d, ff = 602, 512, 3200
+    if name == "attention":
+        qk, v = rnd(T, 2 * d), rnd(T, d)
+        fn = lambda: ops.gqa_attention(qk[:, :d], qk[:, d:], v, 8, 8, 0.125)  # noqa: E731
+        work = 4 * 8 * T * T * 64
+    elif name in ("gemm_qkv", "gemm_w1", "gemm_w2"):
+        M, N, K, mode = {"gemm_qkv": (T, 512, d, 0), "gemm_w1": (T, ff, d, EPI_RELU),
+                         "gemm_w2": (T, d, ff, EPI_ADD)}[name]
+        wq, ws = ops.pack_weights_i8(rnd(N, K, s=0.02))
+        xq, xs = ops.quantize_act_i8(rnd(M, K))
+        b, res = rnd(N), rnd(M, N)
+        fn = lambda: ops.gemm_i8(xq, xs, wq, ws, K, bias=b, mode=mode, res=res if mode == EPI_ADD else None)  # noqa
+        work = 2 * M * N * K
+    elif name == "layernorm":
+        x, w, b = rnd(T, d), rnd(d), rnd(d)
+        fn = lambda: ops.layernorm(x, w, b)  # noqa: E731
+        work = 2 * T * d * 4
+    elif name == "quantize":
+        x = rnd(T, ff)
+        fn = lambda: ops.quantize_act_i8(x)  # noqa: E731
+        work = T * ff * 5
+    elif name == "conv_layer1":
+        x = rnd(2, 120, 160, 64)
+        wq, ws = ops.pack_weights_i8(rnd(64, 9 * 64, s=0.05))
+        b = rnd(64)
+        fn = lambda: ops.conv2d_i8(x, wq, ws, b, 64, 3, 1, 1, mode=EPI_RELU)  # noqa: E731
+        work = 2 * 2 * 120 * 160 * 64 * 576
+    else:
+        raise SystemExit(f"unknown --op {name}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    print(json.dumps({"op": name, "us_per_call": round(us, 3), "work_per_call": work,
+                      "rate_per_s": work / us * 1e6}), flush=True)
+
+
 def run_ours(args):
     import torch
     rank, local_rank, world = _env_rank()
@@ -400,9 +451,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default=None, help="time one op at its ACT shape (attention, gemm_qkv, gemm_w1, "
+                                               "gemm_w2, layernorm, quantize, conv_layer1)")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
     args = ap.parse_args()
+    if args.op:
+        run_op(args.op)
+        return
     if args.gemm_only:
         import torch
         torch.cuda.set_device(0)

@@ -162,6 +162,10 @@ bool ActPolicy::load_config(const std::string& dir) {
         fail("bad config.txt values");
         return false;
     }
+    if (n_cams_ > 8) {   // the conv kernels batch the cameras as up to 8 frames
+        fail("more than 8 cameras");
+        return false;
+    }
     return true;
 }
 

@@ -17,13 +17,16 @@
 // multiples of 16 bytes (TMA stride rule). Bytes past K in a row are never read:
 // the tensor maps' inner extent is K, so TMA zero-fills the k-tail.
 //
-// CTA = 192 threads (6 warps, specialized), one 128 x BN output tile:
+// Persistent CTA = 320 threads (10 warps, specialized) looping over 128 x BN
+// output tiles, accumulators double-buffered in TMEM so one tile's epilogue
+// overlaps the next tile's loads and MMAs:
 //   warp 0     lane 0: TMA producer (A and B k-blocks of 128 bytes, STAGES ring)
 //   warp 1     TMEM allocation; lane 0: MMA issuer (4 x tcgen05.mma K=32 per
 //              k-block), commits free ring slots back to the producer and
 //              finally signals the epilogue
-//   warps 2-5  epilogue: warp w reads TMEM lanes [32(w%4), +32) = tile rows
-//              32(w%4).. with tcgen05.ld, applies the epilogue, stores fp32.
+//   warps 2-9  epilogue: warp w reads TMEM lanes [32(w%4), +32) = tile rows
+//              32(w%4).., the column chunks c with c % 2 == (w-2)/4, with
+//              tcgen05.ld, applies the epilogue, stores fp32.
 // Only the epilogue warps wait on the accumulator barrier; the producer and
 // MMA warps never share a warp with a spinning waiter.
 #include "sm100.cuh"
@@ -43,7 +46,7 @@ namespace {
 constexpr int kBM = 128;          // UMMA M (one TMEM lane per tile row)
 constexpr int kBK = 128;          // bytes of K per pipeline stage (one SW128 atom row)
 constexpr int kUmmaK = 32;        // K per tcgen05.mma kind::i8
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
 struct EpiParams {
     void* out;                    // float* (or int32_t* with kEpiAcc)
@@ -80,210 +83,234 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     constexpr int kABytes = kBM * kBK;
     constexpr int kBBytes = BN * kBK;
     constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
+    constexpr int kStg = 32 * 33;   // floats: one epilogue warp's 32 x 32 staging tile, padded
+    constexpr int kEpiWarps = 8;
 
     extern __shared__ uint8_t smem_raw[];
     // SW128 tiles want 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * kABytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+    float* stg_all = reinterpret_cast<float*>(sB + STAGES * kBBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + kEpiWarps * kStg);
     uint64_t* empty = full + STAGES;
-    uint64_t* done = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + STAGES;     // [2]: accumulator buffer ready for the epilogue
+    uint64_t* acc_empty = acc_full + 2;      // [2]: epilogue done reading the buffer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* s_ws = reinterpret_cast<float*>(tmem_slot + 4);
-    float* s_b = s_ws + BN;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * kBM;
+    const int n_tn = (p.N + BN - 1) / BN;
+    const int n_tiles = n_tn * ((p.M + kBM - 1) / kBM);
     const int nkb = (p.K + kBK - 1) / kBK;
     // weights that a predecessor kernel may still be writing: wait up front
     if (!p.static_weights) pdl_wait();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
         *s_consumed = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
-    for (int j = threadIdx.x; j < BN; j += kThreads) {
-        const int n = n0 + j;
-        s_ws[j] = n < p.N ? p.wscale[n] : 0.0f;
-        s_b[j] = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
-    }
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Everything above touched only on-chip state and constant weights; let the
-    // next kernel in the stream start its own setup.
+    // Everything above touched only on-chip state (and constant weights); let
+    // the next kernel in the stream start its own setup.
     pdl_trigger();
 
     int issued = 0;
     if (warp == 0) {
         if (lane == 0) {
-            // ---- TMA producer. The weight halves of the first ring slots do not
-            // depend on earlier kernels: issue them before waiting for the
-            // predecessor, then the activation halves.
+            // ---- TMA producer: tiles t = blockIdx.x, +gridDim.x, ...; one ring
+            // of STAGES k-block slots shared across tiles. The weight halves of
+            // the first slots go out before waiting for the predecessor kernel.
             const int pre = nkb < STAGES ? nkb : STAGES;
-            for (int kb = 0; kb < pre; ++kb) {
-                mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
-                tma_load_2d(sB + kb * kBBytes, &tmap_b, &full[kb], kb * kBK, n0);
+            {
+                const int n0 = (blockIdx.x % n_tn) * BN;
+                for (int kb = 0; kb < pre; ++kb) {
+                    mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
+                    tma_load_2d(sB + kb * kBBytes, &tmap_b, &full[kb], kb * kBK, n0);
+                }
             }
             pdl_wait();
-            for (int kb = 0; kb < pre; ++kb) tma_load_2d(sA + kb * kABytes, &tmap_a, &full[kb], kb * kBK, m0);
-            issued = pre;
-            for (int kb = pre; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                const int use = kb / STAGES;
-                if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
-                mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
-                tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
-                tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
-                issued = kb + 1;
+            int it = 0;
+            bool fail = false;
+            for (int t = blockIdx.x; t < n_tiles && !fail; t += gridDim.x) {
+                const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it < pre) {   // first tile's weights already in flight
+                        tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
+                    } else {
+                        const int use = it / STAGES;   // > 0 unless the ring is longer than the first tile
+                        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) { fail = true; break; }
+                        mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                        tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
+                        tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
+                    }
+                    issued = it + 1;
+                }
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---- MMA issuer
-            int kb = 0;
-            for (; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                if (!mbar_wait(&full[s], (kb / STAGES) & 1)) break;
+            // ---- MMA issuer: tile i accumulates into TMEM buffer i % 2
+            int it = 0, i = 0;
+            bool fail = false;
+            for (int t = blockIdx.x; t < n_tiles && !fail; t += gridDim.x, ++i) {
+                const int buf = i & 1, ub = i >> 1;
+                if (ub > 0 && !mbar_wait(&acc_empty[buf], (ub - 1) & 1)) break;
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(sA + s * kABytes);
-                const uint32_t b_addr = smem_u32(sB + s * kBBytes);
-                #pragma unroll
-                for (int k = 0; k < kBK / kUmmaK; ++k) {
-                    umma_s8(tmem_base, sw128_kmajor_desc(a_addr + k * kUmmaK),
-                            sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1)) { fail = true; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * kABytes);
+                    const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+                    #pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k) {
+                        umma_s8(d_tmem, sw128_kmajor_desc(a_addr + k * kUmmaK),
+                                sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+                    }
+                    umma_commit(&empty[s]);
+                    *s_consumed = it + 1;
                 }
-                umma_commit(&empty[s]);
-                *s_consumed = kb + 1;
+                if (!fail) umma_commit(&acc_full[buf]);
             }
-            if (kb == nkb) umma_commit(done);
         }
         __syncwarp();
     } else {
-    // ---- epilogue
-    // Phase A (thread = tile row, as TMEM hands it out): 32 accumulators of a
-    // 32-column chunk -> v = fma(acc*s_w, s_a, b) (or the raw int32 bits) into
-    // this warp's 32 x 33 shared staging tile. Phase B (coalesced): lane l
-    // covers columns 4*(l%8)..+3 of rows l/8 + 4i, so each store instruction
-    // writes four whole 128-byte row segments; the residual is read the same
-    // way. The staging tiles reuse the A ring (every MMA has completed).
-    // warp-uniform: the epilogue's tcgen05.ld and shuffles need every lane
-    const int quarter = warp & 3;   // TMEM lanes a warp may read: 32 * (warp id % 4)
-    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(done, 0));
-    pdl_wait();   // activation scales / residual / output: predecessor data
-    if (ok) {
-        tc_fence_after();
-        float* stg = reinterpret_cast<float*>(sA) + quarter * (32 * 33);
-        const int row = quarter * 32 + lane;
-        const int m_row = m0 + row;
-        const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
+        // ---- epilogue (warps 2-9). Per 32-column chunk: phase A (thread = tile
+        // row, as TMEM hands it out) turns the accumulators into
+        // v = fma(acc*s_w, s_a, b) (or raw int32 bits) in this warp's staging
+        // tile; phase B (coalesced) - lane l covers columns 4*(l%8)..+3 of rows
+        // l/8 + 4i - adds the residual and stores, four whole 128-byte row
+        // segments per instruction. Column scales and biases reach the lanes by
+        // shuffle from one load per lane.
+        const int quarter = warp & 3;   // TMEM lanes this warp may read: 32 * (warp id % 4)
+        const int half = (warp - 2) >> 2;   // which column chunks: c % 2 == half
+        float* stg = stg_all + (warp - 2) * kStg;
         const bool acc_mode = (p.mode & kEpiAcc) != 0;
-        const int cq = (lane & 7) * 4;       // phase B column offset in the chunk
-        const int rq = lane >> 3;            // phase B first row (0..3)
-        float tmax = 0.0f;                   // |out| max of this thread's tile row
-        #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            uint32_t acc[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
-            tmem_ld_wait();
-            if (n0 + c * 32 >= p.N) continue;            // warp-uniform
-            #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                float v;
-                if (acc_mode) {
-                    v = __int_as_float(static_cast<int32_t>(acc[j]));
-                } else {
-                    v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_ws[c * 32 + j]), as,
-                                  s_b[c * 32 + j]);
-                    if (p.mode & kEpiRelu) v = (v < 0.0f) ? 0.0f : v;   // tcpu::relu (eltwise.cpp:213-214)
-                }
-                stg[lane * 33 + j] = v;
-            }
-            __syncwarp();
-            const int n = n0 + c * 32 + cq;
-            #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = rq + 4 * i;
-                const int m = m0 + quarter * 32 + r;
-                if (m >= p.M || n >= p.N) continue;
-                float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
-                const bool full4 = n + 4 <= p.N;
-                if (acc_mode) {
-                    int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
-                    #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (n + e < p.N) o[e] = __float_as_int(v[e]);
-                    continue;
-                }
-                if (p.mode & (kEpiAdd | kEpiAddRelu)) {
-                    const float* rr = p.res + (long long)m * p.ldr + n;
-                    float rv[4];
-                    if (p.vec_ok && full4) {
-                        const float4 t = *reinterpret_cast<const float4*>(rr);
-                        rv[0] = t.x; rv[1] = t.y; rv[2] = t.z; rv[3] = t.w;
+        const int cq = (lane & 7) * 4;
+        const int rq = lane >> 3;
+        pdl_wait();   // activation scales / residual / output: predecessor data
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            const int buf = i & 1;
+            // warp-uniform: the tcgen05.ld and shuffles below need every lane
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (i >> 1) & 1))) break;
+            tc_fence_after();
+            const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
+            const int m_row = m0 + quarter * 32 + lane;
+            const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
+            float tmax = 0.0f;
+            #pragma unroll 1
+            for (int c = half; c < BN / 32; c += 2) {
+                uint32_t acc[32];
+                tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
+                const int ncol = n0 + c * 32 + lane;
+                const float my_ws = ncol < p.N ? p.wscale[ncol] : 0.0f;
+                const float my_b = (p.bias && ncol < p.N) ? p.bias[ncol] : 0.0f;
+                tmem_ld_wait();
+                if (n0 + c * 32 >= p.N) continue;            // warp-uniform
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float ws = __shfl_sync(0xFFFFFFFFu, my_ws, j);
+                    const float bj = __shfl_sync(0xFFFFFFFFu, my_b, j);
+                    float v;
+                    if (acc_mode) {
+                        v = __int_as_float(static_cast<int32_t>(acc[j]));
                     } else {
-                        #pragma unroll
-                        for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
+                        v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), ws), as, bj);
+                        if (p.mode & kEpiRelu) v = (v < 0.0f) ? 0.0f : v;   // tcpu::relu (eltwise.cpp:213-214)
                     }
-                    #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (p.mode & kEpiAdd) v[e] = __fadd_rn(rv[e], v[e]);             // x[i] += y[i]
-                        if (p.mode & kEpiAddRelu) {                                        // resnet_backbone.cpp:293-295
-                            v[e] = __fadd_rn(v[e], rv[e]);
-                            v[e] = v[e] > 0.0f ? v[e] : 0.0f;
+                    stg[lane * 33 + j] = v;
+                }
+                __syncwarp();
+                const int n = n0 + c * 32 + cq;
+                #pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8) {
+                    const int r = rq + 4 * r8;
+                    const int m = m0 + quarter * 32 + r;
+                    if (m >= p.M || n >= p.N) continue;
+                    float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
+                    const bool full4 = n + 4 <= p.N;
+                    if (acc_mode) {
+                        int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
+                        #pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (n + e < p.N) o[e] = __float_as_int(v[e]);
+                        continue;
+                    }
+                    if (p.mode & (kEpiAdd | kEpiAddRelu)) {
+                        const float* rr = p.res + (long long)m * p.ldr + n;
+                        float rv[4];
+                        if (p.vec_ok && full4) {
+                            const float4 tt = *reinterpret_cast<const float4*>(rr);
+                            rv[0] = tt.x; rv[1] = tt.y; rv[2] = tt.z; rv[3] = tt.w;
+                        } else {
+                            #pragma unroll
+                            for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
+                        }
+                        #pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (p.mode & kEpiAdd) v[e] = __fadd_rn(rv[e], v[e]);             // x[i] += y[i]
+                            if (p.mode & kEpiAddRelu) {                                        // resnet_backbone.cpp:293-295
+                                v[e] = __fadd_rn(v[e], rv[e]);
+                                v[e] = v[e] > 0.0f ? v[e] : 0.0f;
+                            }
+                        }
+                        if (p.amax) {
+                            #pragma unroll
+                            for (int e = 0; e < 4; ++e) stg[r * 33 + cq + e] = v[e];
                         }
                     }
-                    if (p.amax) {
+                    float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
+                    if (p.vec_ok && full4) {
+                        *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+                    } else {
                         #pragma unroll
-                        for (int e = 0; e < 4; ++e) stg[r * 33 + cq + e] = v[e];
+                        for (int e = 0; e < 4; ++e)
+                            if (n + e < p.N) o[e] = v[e];
                     }
                 }
-                float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
-                if (p.vec_ok && full4) {
-                    *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
-                } else {
+                if (p.amax) {
+                    // final values are back in the staging tile: per-row max, thread = row
+                    __syncwarp();
                     #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (n + e < p.N) o[e] = v[e];
+                    for (int j = 0; j < 32; ++j)
+                        if (n0 + c * 32 + j < p.N) tmax = fmaxf(tmax, fabsf(stg[lane * 33 + j]));
                 }
-            }
-            if (p.amax) {
-                // final values are back in the staging tile: per-row max, thread = row
                 __syncwarp();
-                #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (n0 + c * 32 + j < p.N) tmax = fmaxf(tmax, fabsf(stg[lane * 33 + j]));
             }
+            // this tile's TMEM buffer may be reused by the MMA warp
+            tc_fence_before();
             __syncwarp();
-        }
-        if (p.amax) {
-            // one atomic per warp when the warp's rows share a slot, else per row
-            const bool row_ok = m_row < p.M;
-            const unsigned key = row_ok ? static_cast<unsigned>(m_row / p.amax_rows) : 0xFFFFFFFFu;
-            const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
-            if (__all_sync(0xFFFFFFFFu, key == k0 || key == 0xFFFFFFFFu)) {
-                float wm = row_ok ? tmax : 0.0f;    // rows past M hold bias-only values
-                #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
-                if (lane == 0 && k0 != 0xFFFFFFFFu) atomicMax(&p.amax[k0], __float_as_uint(wm));
-            } else if (row_ok) {
-                atomicMax(&p.amax[key], __float_as_uint(tmax));
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (p.amax) {
+                // one atomic per warp when the warp's rows share a slot, else per row
+                const bool row_ok = m_row < p.M;
+                const unsigned key = row_ok ? static_cast<unsigned>(m_row / p.amax_rows) : 0xFFFFFFFFu;
+                const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
+                if (__all_sync(0xFFFFFFFFu, key == k0 || key == 0xFFFFFFFFu)) {
+                    float wm = row_ok ? tmax : 0.0f;    // rows past M hold bias-only values
+                    #pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
+                    if (lane == 0 && k0 != 0xFFFFFFFFu) atomicMax(&p.amax[k0], __float_as_uint(wm));
+                } else if (row_ok) {
+                    atomicMax(&p.amax[key], __float_as_uint(tmax));
+                }
             }
         }
     }
-
-    }   // epilogue warps
 
     tc_fence_before();
     __syncthreads();
@@ -294,7 +321,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, BN);
+        tmem_dealloc(tmem_base, 2 * BN);
     }
 }
 
@@ -364,25 +391,39 @@ namespace {
 
 template <int BN, int STAGES>
 constexpr size_t umma_smem_bytes() {
-    return 1024 + STAGES * (kBM * kBK + BN * kBK) + (2 * STAGES + 1) * 8 + 16 + 2 * BN * 4;
+    return 1024 + STAGES * (kBM * kBK + BN * kBK) + 8 * 32 * 33 * 4 + (2 * STAGES + 4) * 8 + 16;
 }
 
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// Persistent launch: at most (SMs x resident CTAs) CTAs, each looping over
+// output tiles t = blockIdx.x, +gridDim.x, ...
 template <int BN, int STAGES>
 cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, cudaStream_t st) {
     constexpr size_t smem = umma_smem_bytes<BN, STAGES>();
-    static bool configured = false;
-    if (!configured) {
+    static int per_sm = 0;
+    if (!per_sm) {
         const cudaError_t e = cudaFuncSetAttribute(w8a8_umma_kernel<BN, STAGES>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        configured = true;
+        int occ = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w8a8_umma_kernel<BN, STAGES>, kThreads, smem);
+        per_sm = occ > 0 ? occ : 1;
     }
-    dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
-    {
-        const cudaError_t le_ = launch_k(w8a8_umma_kernel<BN, STAGES>, grid, kThreads, smem, st,
-                                         ta, tb, p);
-        if (le_ != cudaSuccess) return le_;
-    }
+    const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + kBM - 1) / kBM);
+    const long long cap = (long long)sm_count() * per_sm;
+    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    const cudaError_t le_ = launch_k(w8a8_umma_kernel<BN, STAGES>, grid, kThreads, smem, st, ta, tb, p);
+    if (le_ != cudaSuccess) return le_;
     return cudaGetLastError();
 }
 

@@ -649,75 +649,72 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
                                   const float* __restrict__ bias, float* __restrict__ out, long long ldo,
                                   int M, int N, int K, const float* __restrict__ post_mul,
                                   const float* __restrict__ post_add) {
+    // one warp per output; the reference's independent lane accumulators are
+    // spread over the warp's lanes, then combined in its order
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (gid >= (long long)M * N) return;
-    const int m = static_cast<int>(gid / N), n = static_cast<int>(gid - (long long)m * N);
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    if (w >= (long long)M * N) return;
+    const int m = static_cast<int>(w / N), n = static_cast<int>(w - (long long)m * N);
     const float* xr = x + (long long)m * ldx;
     const float* wr = W + (long long)n * K;
-    float s;
-    int k = 0;
     const bool block4 = n < N - N % 4;
+    float acc = 0.0f;
+    int kend;
     if (block4) {
-        float a[8], b[8];
-        #pragma unroll
-        for (int l = 0; l < 8; ++l) { a[l] = 0.0f; b[l] = 0.0f; }
-        for (; k + 16 <= K; k += 16) {
-            #pragma unroll
-            for (int l = 0; l < 8; ++l) {
-                a[l] = __fmaf_rn(xr[k + l], wr[k + l], a[l]);
-                b[l] = __fmaf_rn(xr[k + 8 + l], wr[k + 8 + l], b[l]);
-            }
+        // lanes 0-7: a[l] (k % 16 == l), lanes 8-15: b[l-8] (k % 16 == l); 16-wide steps
+        const int K16 = K & ~15;
+        if (lane < 16)
+            for (int k = 0; k < K16; k += 16) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        kend = K16;
+        if (K - K16 >= 8) {                      // one 8-wide step into a
+            if (lane < 8) acc = __fmaf_rn(xr[K16 + lane], wr[K16 + lane], acc);
+            kend = K16 + 8;
         }
-        for (; k + 8 <= K; k += 8) {
-            #pragma unroll
-            for (int l = 0; l < 8; ++l) a[l] = __fmaf_rn(xr[k + l], wr[k + l], a[l]);
-        }
-        #pragma unroll
-        for (int l = 0; l < 8; ++l) a[l] = __fadd_rn(a[l], b[l]);
-        s = hsum8_ref(a);
+        // t[l] = a[l] + b[l]
+        const float other = __shfl_down_sync(0xFFFFFFFFu, acc, 8);
+        acc = __fadd_rn(acc, other);
     } else {
-        float c0[8], c1[8], c2[8], c3[8];
-        #pragma unroll
-        for (int l = 0; l < 8; ++l) { c0[l] = 0.0f; c1[l] = 0.0f; c2[l] = 0.0f; c3[l] = 0.0f; }
-        for (; k + 32 <= K; k += 32) {
-            #pragma unroll
-            for (int l = 0; l < 8; ++l) {
-                c0[l] = __fmaf_rn(xr[k + l], wr[k + l], c0[l]);
-                c1[l] = __fmaf_rn(xr[k + 8 + l], wr[k + 8 + l], c1[l]);
-                c2[l] = __fmaf_rn(xr[k + 16 + l], wr[k + 16 + l], c2[l]);
-                c3[l] = __fmaf_rn(xr[k + 24 + l], wr[k + 24 + l], c3[l]);
-            }
-        }
-        for (; k + 8 <= K; k += 8) {
-            #pragma unroll
-            for (int l = 0; l < 8; ++l) c0[l] = __fmaf_rn(xr[k + l], wr[k + l], c0[l]);
-        }
-        #pragma unroll
-        for (int l = 0; l < 8; ++l) c0[l] = __fadd_rn(__fadd_rn(c0[l], c1[l]), __fadd_rn(c2[l], c3[l]));
-        s = hsum8_ref(c0);
+        // lanes 8j+l: chain j of lane l, 32-wide steps; then 8-wide steps into chain 0
+        const int K32 = K & ~31;
+        for (int k = 0; k < K32; k += 32) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        kend = K32;
+        for (; kend + 8 <= K; kend += 8)
+            if (lane < 8) acc = __fmaf_rn(xr[kend + lane], wr[kend + lane], acc);
+        // c0[l] = (acc0[l] + acc1[l]) + (acc2[l] + acc3[l])
+        const float a1 = __shfl_down_sync(0xFFFFFFFFu, acc, 8);
+        const float a2 = __shfl_down_sync(0xFFFFFFFFu, acc, 16);
+        const float a3 = __shfl_down_sync(0xFFFFFFFFu, acc, 24);
+        acc = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
     }
-    // scalar tails: mm_block4's is contracted to fma by the reference's
-    // -ffp-contract=fast build, simd_dot's stays a rounded multiply then add
-    // (both established against the compiled reference on odd K)
-    if (block4)
-        for (; k < K; ++k) s = __fmaf_rn(xr[k], wr[k], s);
-    else
-        for (; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], wr[k]));
-    float v = bias ? __fadd_rn(s, bias[n]) : s;
-    if (post_mul) v = __fmaf_rn(v, post_mul[n], post_add[n]);
-    out[(long long)m * ldo + n] = v;
+    // hsum8 over lanes 0..7: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+    float l[8];
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, acc, i);
+    if (lane == 0) {
+        float s = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[1], l[5])),
+                            __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
+        // scalar tails: mm_block4's is contracted to fma by the reference's
+        // -ffp-contract=fast build, simd_dot's stays a rounded multiply then add
+        // (both established against the compiled reference on odd K)
+        if (block4)
+            for (int k = kend; k < K; ++k) s = __fmaf_rn(xr[k], wr[k], s);
+        else
+            for (int k = kend; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], wr[k]));
+        float v = bias ? __fadd_rn(s, bias[n]) : s;
+        if (post_mul) v = __fmaf_rn(v, post_mul[n], post_add[n]);
+        out[(long long)m * ldo + n] = v;
+    }
 }
 
 cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
-    const long long total = (long long)M * N;
+    const long long threads = (long long)M * N * 32;
     {
-        const cudaError_t le_ = launch_k(linear_f32_kernel, (int)((total + 127) / 128), 128, 0, st,
-                                         x, ldx, W, bias, out, ldo, M, N, K, post_mul,
-                                                                   post_add);
+        const cudaError_t le_ = launch_k(linear_f32_kernel, (int)((threads + 255) / 256), 256, 0, st,
+                                         x, ldx, W, bias, out, ldo, M, N, K, post_mul, post_add);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

@@ -119,97 +119,86 @@ quantize_rows_kernel(const float* __restrict__ x, long long ldx, const float* __
 // im2col_panel (src/hal/common/conv.cpp:142-156), zero for taps outside the
 // image and past K. rscale[row] = the frame's scale (one per output row, so the
 // GEMM epilogue reads a per-row scale).
-template <int VEC>
-__global__ void im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C,
-                                 int k, int stride, int pad, int Ho, int Wo, int K, long long ldc,
-                                 const unsigned int* __restrict__ amax_bits, float clip,
-                                 int8_t* __restrict__ col, float* __restrict__ rscale) {
+// C % 16 == 0: one thread per 16-byte group of an output row (16 channels of
+// one tap); 32-bit index math; the per-frame scale computed once per block.
+__global__ void __launch_bounds__(256)
+im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride, int pad, int Ho,
+                 int Wo, int K, int ldc, const unsigned int* __restrict__ amax_bits, float clip,
+                 int8_t* __restrict__ col, float* __restrict__ rscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    const long long groups_per_row = ldc / VEC;
-    const long long total = (long long)F * Ho * Wo * groups_per_row;
-    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
-         t += (long long)gridDim.x * blockDim.x) {
-        const long long row = t / groups_per_row;
-        const int g = static_cast<int>(t - row * groups_per_row);
-        const int npix = Ho * Wo;
-        const int f = static_cast<int>(row / npix);
-        const int pix = static_cast<int>(row - (long long)f * npix);
-        const int oy = pix / Wo, ox = pix - oy * Wo;
-        const float amax = __uint_as_float(amax_bits[f]);
+    __shared__ float s_inv[8], s_scale[8];
+    if (threadIdx.x < F && threadIdx.x < 8) {
+        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
         const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        const float inv = __fdiv_rn(1.0f, s);
-        if (g == 0) rscale[row] = s;
-        const float* xf = x + (long long)f * H * W * C;
-        int8_t* dst = col + row * ldc + (long long)g * VEC;
-        const int k0 = g * VEC;
-        if (VEC == 16) {
-            // C % 16 == 0: the 16 elements share one tap
-            char4 out[4];
-            int8_t* ob = reinterpret_cast<int8_t*>(out);
-            if (k0 >= K) {
+        s_scale[threadIdx.x] = s;
+        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
+    }
+    __syncthreads();
+    const int groups = ldc >> 4;
+    const int cg = C >> 4;                       // 16-channel groups per tap
+    const int npix = Ho * Wo;
+    const int total = F * npix * groups;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int row = t / groups;
+        const int g = t - row * groups;
+        const int f = row / npix;
+        const int pix = row - f * npix;
+        const float inv = s_inv[f];
+        if (g == 0) rscale[row] = s_scale[f];
+        char4 out[4] = {make_char4(0, 0, 0, 0), make_char4(0, 0, 0, 0), make_char4(0, 0, 0, 0),
+                        make_char4(0, 0, 0, 0)};
+        if (g * 16 < K) {
+            const int oy = pix / Wo, ox = pix - oy * Wo;
+            const int tap = g / cg, ci = (g - tap * cg) * 16;
+            const int ky = tap / k, kx = tap - ky * k;
+            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
+                const float4* src = reinterpret_cast<const float4*>(x + (((long long)f * H + iy) * W + ix) * C + ci);
                 #pragma unroll
-                for (int i = 0; i < 16; ++i) ob[i] = 0;
-            } else {
-                const int tap = k0 / C, ci = k0 - tap * C;
-                const int ky = tap / k, kx = tap - ky * k;
-                const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-                if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
-                    #pragma unroll
-                    for (int i = 0; i < 16; ++i) ob[i] = 0;
-                } else {
-                    const float4* src = reinterpret_cast<const float4*>(xf + ((long long)iy * W + ix) * C + ci);
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float4 v = src[i];
-                        ob[4 * i + 0] = q8_span(v.x, inv);
-                        ob[4 * i + 1] = q8_span(v.y, inv);
-                        ob[4 * i + 2] = q8_span(v.z, inv);
-                        ob[4 * i + 3] = q8_span(v.w, inv);
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    const float4 v = src[i];
+                    out[i] = make_char4(q8_span(v.x, inv), q8_span(v.y, inv), q8_span(v.z, inv), q8_span(v.w, inv));
                 }
             }
-            *reinterpret_cast<int4*>(dst) = *reinterpret_cast<int4*>(out);
         }
+        reinterpret_cast<int4*>(col + (long long)row * ldc)[g] = *reinterpret_cast<int4*>(out);
     }
 }
 
-// im2col for small channel counts (the 3-channel stem): one thread per (output
-// row, kernel tap) copies that tap's C contiguous NHWC values; the extra tap
-// k*k zero-fills the row's padding [K, ldc).
-__global__ void im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride,
-                                      int pad, int Ho, int Wo, int K, long long ldc,
-                                      const unsigned int* __restrict__ amax_bits, float clip,
-                                      int8_t* __restrict__ col, float* __restrict__ rscale) {
+// im2col for small channel counts (the 3-channel stem): one warp per output
+// row; lane l copies the C contiguous NHWC values of taps l, l+32, ...; lane
+// work past the k*k taps zero-fills the row's padding [K, ldc).
+__global__ void __launch_bounds__(256)
+im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride, int pad, int Ho,
+                      int Wo, int K, long long ldc, const unsigned int* __restrict__ amax_bits, float clip,
+                      int8_t* __restrict__ col, float* __restrict__ rscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    const int taps = k * k + 1;
-    const long long total = (long long)F * Ho * Wo * taps;
-    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
-         t += (long long)gridDim.x * blockDim.x) {
-        const long long row = t / taps;
-        const int tap = static_cast<int>(t - row * taps);
+    const int lane = threadIdx.x & 31;
+    const int rows = F * Ho * Wo;
+    const int taps = k * k;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += (gridDim.x * blockDim.x) >> 5) {
         const int npix = Ho * Wo;
-        const int f = static_cast<int>(row / npix);
-        const int pix = static_cast<int>(row - (long long)f * npix);
+        const int f = row / npix;
+        const int pix = row - f * npix;
+        const int oy = pix / Wo, ox = pix - oy * Wo;
         const float amax = __uint_as_float(amax_bits[f]);
         const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        int8_t* dst = col + row * ldc;
-        if (tap == k * k) {
-            for (long long i = K; i < ldc; ++i) dst[i] = 0;
-            rscale[row] = s;
-            continue;
-        }
         const float inv = __fdiv_rn(1.0f, s);
-        const int oy = pix / Wo, ox = pix - oy * Wo;
-        const int ky = tap / k, kx = tap - ky * k;
-        const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-        int8_t* d = dst + tap * C;
-        if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
-            for (int c = 0; c < C; ++c) d[c] = 0;
-        } else {
-            const float* src = x + (((long long)f * H + iy) * W + ix) * C;
-            for (int c = 0; c < C; ++c) d[c] = q8_span(src[c], inv);
+        if (lane == 0) rscale[row] = s;
+        int8_t* dst = col + (long long)row * ldc;
+        for (long long i = K + lane; i < ldc; i += 32) dst[i] = 0;
+        for (int tap = lane; tap < taps; tap += 32) {
+            const int ky = tap / k, kx = tap - ky * k;
+            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+            int8_t* d = dst + tap * C;
+            if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
+                for (int c = 0; c < C; ++c) d[c] = 0;
+            } else {
+                const float* src = x + (((long long)f * H + iy) * W + ix) * C;
+                for (int c = 0; c < C; ++c) d[c] = q8_span(src[c], inv);
+            }
         }
     }
 }
@@ -296,28 +285,26 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
                       long long ldc, const unsigned int* amax_bits, float clip, int8_t* col, float* rscale,
                       cudaStream_t st) {
     const int K = k * k * C;
-    if (ldc < K || (ldc & 15)) return cudaErrorInvalidValue;
+    if (ldc < K || (ldc & 15) || F > 8 || (long long)F * H * W * C >= (1LL << 31) ||
+        (long long)F * Ho * Wo * (ldc / 16) >= (1LL << 31))
+        return cudaErrorInvalidValue;
     const bool v16 = (C % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(col) & 15) == 0);
     const long long rows = (long long)F * Ho * Wo;
-    const long long total = v16 ? rows * (ldc / 16) : rows * (k * k + 1);
     const int threads = 256;
-    long long blocks = (total + threads - 1) / threads;
-    if (blocks > 148 * 64) blocks = 148 * 64;
-    if (v16)
-        {
-            const cudaError_t le_ = launch_k(im2col_i8_kernel<16>, (int)blocks, threads, 0, st,
-                                             x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
-                                                              amax_bits, clip, col, rscale);
-            if (le_ != cudaSuccess) return le_;
-        }
-    else
-        {
-            const cudaError_t le_ = launch_k(im2col_i8_taps_kernel, (int)blocks, threads, 0, st,
-                                             x, F, H, W, C, k, stride, pad, Ho, Wo, K, ldc,
-                                                               amax_bits, clip, col, rscale);
-            if (le_ != cudaSuccess) return le_;
-        }
+    if (v16) {
+        long long blocks = (rows * (ldc / 16) + threads - 1) / threads;
+        if (blocks > 148 * 32) blocks = 148 * 32;
+        const cudaError_t le_ = launch_k(im2col_i8_kernel, (int)blocks, threads, 0, st, x, F, H, W, C, k, stride, pad,
+                                         Ho, Wo, K, (int)ldc, amax_bits, clip, col, rscale);
+        if (le_ != cudaSuccess) return le_;
+    } else {
+        long long blocks = (rows * 32 + threads - 1) / threads;
+        if (blocks > 148 * 16) blocks = 148 * 16;
+        const cudaError_t le_ = launch_k(im2col_i8_taps_kernel, (int)blocks, threads, 0, st, x, F, H, W, C, k, stride,
+                                         pad, Ho, Wo, K, ldc, amax_bits, clip, col, rscale);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
