@@ -70,6 +70,24 @@ VLA_API int32_t vla_cuda_dense_linear_i8(float* out, const float* x, const int8_
                                          int32_t seq, int32_t N, int32_t K, int64_t ldw,
                                          int8_t* xq_scratch, float* ascale_scratch, void* stream);
 
+/* No counterpart in the reference: this backend's addition for callers that
+ * cannot allocate device memory (a real-time control loop, where cudaMalloc /
+ * cudaFree may synchronize the device and stall for an unbounded time, or a
+ * host framework that owns all GPU memory through its own pool). Same result
+ * as vla_cuda_dense_linear_i8, but the quantization scratch is a fixed 2 MiB
+ * array in GPU global memory that the library reserves on every GPU it runs on
+ * until the process exits; nothing is allocated or freed. Limit:
+ * seq * ceil16(K) rounded up to 256 bytes, plus 4 * seq, at most 2 MiB (e.g.
+ * 602 x 3200); larger calls return VLA_ERR_SHAPE with a message on stderr.
+ * The first call on each device looks up the array's device address, so make
+ * that first call before any stream capture. All calls share the one array:
+ * calls that overlap on the GPU (different streams, or different host threads
+ * on the same device) race; serialize them. */
+VLA_API int32_t vla_cuda_dense_linear_i8_noalloc(float* out, const float* x, const int8_t* Wq,
+                                                 const float* wscale, const float* bias,
+                                                 int32_t seq, int32_t N, int32_t K, int64_t ldw,
+                                                 void* stream);
+
 /* The W8A8 GEMM with every option exposed (nn::Linear::forward / forward_add
  * and the conv epilogues, src/nn/linear.cpp:121-185). ascale_per_row = 0 uses
  * ascale[0] for every row. res/ldr feed VLA_EPI_ADD / VLA_EPI_ADD_RELU (res

@@ -58,6 +58,7 @@ SIGNATURES = {
     "vla_cuda_pack_weights_i8": (I32, [VP, VP, VP, I32, I32, I64, VP]),
     "vla_cuda_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32, I64, I64, VP]),
     "vla_cuda_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP, VP, VP]),
+    "vla_cuda_dense_linear_i8_noalloc": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP]),
     "vla_cuda_gemm_i8": (I32, [VP, I64, VP, I64, VP, I32, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I32,
                                I32, VP]),
     "vla_cuda_conv2d_i8": (I32, [VP, VP, I32, I32, I32, I32, VP, I64, VP, VP, I32, I32, I32, I32, F32, I32, VP, VP,

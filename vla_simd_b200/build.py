@@ -26,7 +26,7 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-
                      "-Xptxas", "-warn-spills"]
 CXX_FLAGS = ["-std=c++17", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
 
-CUDA_SOURCES = ["kernels.cu"]
+CUDA_SOURCES = ["kernels.cu", "no_alloc.cu"]
 CXX_SOURCES = ["act_policy.cpp", "host_quant.cpp", "capi.cpp"]
 
 
