@@ -270,19 +270,17 @@ cudaError_t layernorm(const float* x, float* out, const float* w, const float* b
 // A row whose every score is blocked (max <= lowest) gets the uniform mean of V
 // (attn_uniform_row, :45-52). Grouped KV heads: kv = h / (n_q / n_kv).
 //
-// CTA = one head x QT queries (32, or 16 for long key rows), 256 threads, the
-// whole score rows in shared memory (row stride = 8 banks apart). Three phases,
-// each a register-tiled loop whose per-output accumulation order is the
-// reference's:
-//   scores  thread = QT/8 queries x 2 keys of a 64-key tile; per d one 16-byte
-//           Q^T load (broadcast) + one 8-byte K^T load feed QT/4 fmas
+// CTA = one head x QT queries, NT threads (16 x 128 at ACT shapes), the whole
+// score rows in shared memory (row stride = 8 banks apart). Three phases, each
+// a register-tiled loop whose per-output accumulation order is the reference's:
+//   scores  thread = QT/(NT/32) queries x 2 keys of a 64-key tile; per d the
+//           queries' Q^T values (broadcast) + one 8-byte K^T load feed the fmas
 //   softmax 8 threads per row; thread t owns keys j = t (mod 8), i.e. exactly
 //           the reference's AVX lane t: its max, exp, and in-order lane sum
-//   A*V     thread = QT/16 queries x 4 dims; keys streamed in order through
+//   A*V     thread = QT/(NT/16) queries x 4 dims; keys streamed in order through
 //           64-key V tiles, one 16-byte V load per key
 constexpr int kAttD = 64;
 constexpr int kAttKT = 64;   // keys per shared K^T / V tile
-constexpr int kAttThreads = 256;
 
 // The reference's Cephes-style exp (src/hal/avx2/simd.h:72-95), lane for lane.
 __device__ __forceinline__ float ref_exp(float x) {
@@ -311,15 +309,17 @@ __host__ __device__ constexpr int att_row_stride(int seq_k) {
     return (((seq_k + 7) & ~7) + 31) / 32 * 32 + 8;
 }
 
-template <int QT>
-__global__ void __launch_bounds__(kAttThreads)
+template <int QT, int NT>
+__global__ void __launch_bounds__(NT)
 attention_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                  const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
                  int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    constexpr int QPT = QT / 8;      // queries per thread, score phase
-    constexpr int QPT2 = QT / 16;    // queries per thread, A*V phase
+    constexpr int QPT = QT / (NT / 32);    // queries per thread, score phase
+    constexpr int QPT2 = QT / (NT / 16);   // queries per thread, A*V phase
+    static_assert(QPT >= 2 && QPT % 2 == 0 && QPT2 >= 1, "attention tile shape");
+    static_assert(NT >= 64 && (QT % (NT / 8) == 0 || NT / 8 >= QT), "softmax row groups");
     extern __shared__ __align__(16) float att_smem[];
     const int ss = att_row_stride(seq_k);
     const int skp = (seq_k + 7) & ~7;
@@ -333,7 +333,7 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
     const int tid = threadIdx.x;
     const float NINF = __int_as_float(0xff800000);
 
-    for (int i = tid; i < QT * kAttD; i += kAttThreads) {
+    for (int i = tid; i < QT * kAttD; i += NT) {
         const int q = i % QT, d = i / QT;
         sQt[d * QT + q] = (q0 + q) < seq_q ? Q[(long long)(q0 + q) * ldq + (long long)h * kAttD + d] : 0.0f;
     }
@@ -344,7 +344,7 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
         for (int k0 = 0; k0 < seq_k; k0 += kAttKT) {
             __syncthreads();
             // K^T tile: consecutive threads take consecutive keys (conflict-free stores)
-            for (int i = tid; i < kAttKT * (kAttD / 4); i += kAttThreads) {
+            for (int i = tid; i < kAttKT * (kAttD / 4); i += NT) {
                 const int key = i % kAttKT, dg = i / kAttKT;
                 const int kk = k0 + key;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -388,8 +388,8 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
 
     // ---- softmax rows: 8 threads per row, thread t = the reference's lane t
     {
-        const int r = tid >> 3, t = tid & 7;
-        if (r < QT) {
+        const int t = tid & 7;
+        for (int r = tid >> 3; r < QT; r += NT / 8) {   // rows of 8 threads (whole warps leave together)
             const int q = q0 + r;
             float* srow = sS + r * ss;
             const float* mrow = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
@@ -449,7 +449,7 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
         for (int c = 0; c < 4; ++c) o[a][c] = 0.0f;
     for (int k0 = 0; k0 < seq_k; k0 += kAttKT) {
         __syncthreads();
-        for (int i = tid; i < kAttKT * (kAttD / 4); i += kAttThreads) {
+        for (int i = tid; i < kAttKT * (kAttD / 4); i += NT) {
             const int key = i / (kAttD / 4), dg = i % (kAttD / 4);
             const int kk = k0 + key;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -480,20 +480,20 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
     }
 }
 
-template <int QT>
+template <int QT, int NT>
 cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                              long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
                              float scale, const float* mask, size_t smem, cudaStream_t st) {
     static int configured = 0;
     if ((int)smem > configured) {
-        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)smem);
         if (e != cudaSuccess) return e;
         configured = (int)smem;
     }
     dim3 grid((seq_q + QT - 1) / QT, n_q);
     {
-        const cudaError_t le_ = launch_k(attention_kernel<QT>, grid, kAttThreads, smem, st,
+        const cudaError_t le_ = launch_k(attention_kernel<QT, NT>, grid, NT, smem, st,
                                          Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv,
                                                           scale, mask);
         if (le_ != cudaSuccess) return le_;
@@ -513,11 +513,13 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
         return cudaErrorInvalidValue;
     const size_t ss = (size_t)att_row_stride(seq_k);
     auto need = [&](int qt) { return sizeof(float) * (qt * ss + (size_t)kAttD * qt + (size_t)kAttKT * kAttD); };
-    if (need(32) <= 112 * 1024)   // two CTAs per SM
-        return launch_attention<32>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(32), st);
-    if (need(16) <= 220 * 1024)
-        return launch_attention<16>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(16), st);
-    return cudaErrorInvalidValue;   // > ~3400 keys: not a shape any policy here has
+    // 16 queries x 128 threads per CTA: measured fastest among 8..32 queries x
+    // 64..512 threads at the ACT shapes (more work per thread beats more warps)
+    if (need(16) <= 200 * 1024)
+        return launch_attention<16, 128>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(16), st);
+    if (need(8) <= 220 * 1024)
+        return launch_attention<8, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(8), st);
+    return cudaErrorInvalidValue;   // > ~13000 keys: not a shape any policy here has
 }
 
 // --------------------------------------------------------- max-pool + ReLU
