@@ -123,6 +123,22 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
+def max_over_ranks(seconds: float, dist=None, device=None) -> float:
+    """The job's time for a timed region: the slowest rank's (max-reduce), or
+    the local time on one process. Runs outside the timed region."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return seconds
+    import torch
+    t = torch.tensor([seconds], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_value(steps_per_rank: int, world: int, seconds_max: float) -> float:
+    """Whole-job chunks/s: every rank's steps over the slowest rank's time."""
+    return world * steps_per_rank / seconds_max
+
+
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -339,14 +355,8 @@ def run_ours(args):
     if dist:
         dist.barrier()
     step_s = [s.elapsed_time(e) * 1e-3 for s, e in zip(starts, ends)]
-    total = sum(step_s)
-    if dist:
-        t = torch.tensor([total], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_max = float(t.item())
-    else:
-        total_max = total
-    value = world * args.steps / total_max
+    total_max = max_over_ranks(sum(step_s), dist, dev)
+    value = job_value(args.steps, world, total_max)
 
     # e2e through the C ABI with host buffers (copies inside), wall clock
     n_e2e = max(args.steps, 10)
@@ -357,12 +367,8 @@ def run_ours(args):
     t0 = time.perf_counter()
     for _ in range(n_e2e):
         pol.predict(frames, state)
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = {"value": world * n_e2e / e2e_s, "unit": "chunks/s", "h2d_bytes_per_step": frames.nbytes + state.nbytes,
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    e2e = {"value": job_value(n_e2e, world, e2e_s), "unit": "chunks/s", "h2d_bytes_per_step": frames.nbytes + state.nbytes,
            "d2h_bytes_per_step": 100 * 6 * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
            "path": "vla_act_predict (C ABI), host uint8 frames + state -> host actions"}
 

@@ -1,5 +1,5 @@
 // Thin inline-PTX layer for the sm_100a features the kernels use: mbarriers,
-// TMA tile loads (no cluster multicast anywhere in this library), tcgen05 MMA /
+// TMA tile loads (each CTA loads its own tiles), tcgen05 MMA /
 // TMEM allocation / TMEM loads, and bounded waits.
 //
 // Every wait on an mbarrier is bounded by wall time (%globaltimer). A wait that
