@@ -20,7 +20,7 @@
 // Persistent CTA = 320 threads (10 warps, specialized) looping over 128 x BN
 // output tiles, accumulators double-buffered in TMEM so one tile's epilogue
 // overlaps the next tile's loads and MMAs:
-//   warp 0     lane 0: TMA producer (A and B k-blocks of 128 bytes, STAGES ring)
+//   warp 0     lane 0: TMA producer (A and B k-blocks of 128 bytes, `stages`-deep ring)
 //   warp 1     TMEM allocation; lane 0: MMA issuer (4 x tcgen05.mma K=32 per
 //              k-block), commits free ring slots back to the producer and
 //              finally signals the epilogue
@@ -35,8 +35,10 @@
 
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <cfloat>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace vsb {
@@ -75,11 +77,11 @@ __device__ __forceinline__ float epi_value(int32_t acc, float ws, float as, floa
     return v;
 }
 
-template <int BN, int STAGES>
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b,
-                 const EpiParams p) {
+                 const EpiParams p, const int stages) {
     constexpr int kABytes = kBM * kBK;
     constexpr int kBBytes = BN * kBK;
     constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
@@ -90,11 +92,11 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // SW128 tiles want 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * kABytes;
-    float* stg_all = reinterpret_cast<float*>(sB + STAGES * kBBytes);
+    uint8_t* sB = smem + stages * kABytes;
+    float* stg_all = reinterpret_cast<float*>(sB + stages * kBBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + kEpiWarps * kStg);
-    uint64_t* empty = full + STAGES;
-    uint64_t* acc_full = empty + STAGES;     // [2]: accumulator buffer ready for the epilogue
+    uint64_t* empty = full + stages;
+    uint64_t* acc_full = empty + stages;     // [2]: accumulator buffer ready for the epilogue
     uint64_t* acc_empty = acc_full + 2;      // [2]: epilogue done reading the buffer
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -108,7 +110,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (!p.static_weights) pdl_wait();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
         *s_consumed = 0;
         fence_mbar_init();
@@ -128,9 +130,9 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer: tiles t = blockIdx.x, +gridDim.x, ...; one ring
-            // of STAGES k-block slots shared across tiles. The weight halves of
+            // of `stages` k-block slots shared across tiles. The weight halves of
             // the first slots go out before waiting for the predecessor kernel.
-            const int pre = nkb < STAGES ? nkb : STAGES;
+            const int pre = nkb < stages ? nkb : stages;
             {
                 const int n0 = (blockIdx.x % n_tn) * BN;
                 for (int kb = 0; kb < pre; ++kb) {
@@ -144,11 +146,11 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             for (int t = blockIdx.x; t < n_tiles && !fail; t += gridDim.x) {
                 const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % STAGES;
+                    const int s = it % stages;
                     if (it < pre) {   // first tile's weights already in flight
                         tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
                     } else {
-                        const int use = it / STAGES;   // > 0 unless the ring is longer than the first tile
+                        const int use = it / stages;   // > 0 unless the ring is longer than the first tile
                         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) { fail = true; break; }
                         mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
                         tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
@@ -170,8 +172,8 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * BN;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    if (!mbar_wait(&full[s], (it / STAGES) & 1)) { fail = true; break; }
+                    const int s = it % stages;
+                    if (!mbar_wait(&full[s], (it / stages) & 1)) { fail = true; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kABytes);
                     const uint32_t b_addr = smem_u32(sB + s * kBBytes);
@@ -202,29 +204,64 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int cq = (lane & 7) * 4;
         const int rq = lane >> 3;
         pdl_wait();   // activation scales / residual / output: predecessor data
+        constexpr int kChunks = (BN / 32 + 1) / 2;   // column chunks per warp: c = half, half + 2, ...
+        // residual of chunk c for this lane's 8 rows x 4 columns (phase B layout)
+        auto load_res = [&](float4 (&rv)[8], int m0, int n0, int c) {
+            const int n = n0 + c * 32 + cq;
+            const bool full4 = n + 4 <= p.N;
+            #pragma unroll
+            for (int r8 = 0; r8 < 8; ++r8) {
+                const int m = m0 + quarter * 32 + rq + 4 * r8;
+                rv[r8] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (m >= p.M || n >= p.N) continue;
+                const float* rr = p.res + (long long)m * p.ldr + n;
+                if (p.vec_ok && full4) {
+                    rv[r8] = *reinterpret_cast<const float4*>(rr);
+                } else {
+                    float* t = reinterpret_cast<float*>(&rv[r8]);
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e) t[e] = n + e < p.N ? rr[e] : 0.0f;
+                }
+            }
+        };
+        const bool has_res = (p.mode & (kEpiAdd | kEpiAddRelu)) != 0;
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int buf = i & 1;
+            const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
+            const int m_row = m0 + quarter * 32 + lane;
+            // Everything the epilogue reads besides the accumulators is fetched
+            // before waiting for them, so its latency hides behind the MMAs:
+            // row scale, column scales / biases of every chunk, first residual.
+            // (Each lane later writes only elements it read here or reads
+            // itself, so a residual aliasing out is never read after a store.)
+            const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
+            float my_ws[kChunks], my_b[kChunks];
+            #pragma unroll
+            for (int ci = 0; ci < kChunks; ++ci) {
+                const int ncol = n0 + (half + 2 * ci) * 32 + lane;
+                const bool ok = half + 2 * ci < BN / 32 && ncol < p.N;
+                my_ws[ci] = ok ? p.wscale[ncol] : 0.0f;
+                my_b[ci] = (ok && p.bias) ? p.bias[ncol] : 0.0f;
+            }
+            float4 rv[8];
+            if (has_res && half < BN / 32) load_res(rv, m0, n0, half);
             // warp-uniform: the tcgen05.ld and shuffles below need every lane
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (i >> 1) & 1))) break;
             tc_fence_after();
-            const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
-            const int m_row = m0 + quarter * 32 + lane;
-            const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
             float tmax = 0.0f;
-            #pragma unroll 1
-            for (int c = half; c < BN / 32; c += 2) {
+            #pragma unroll
+            for (int ci = 0; ci < kChunks; ++ci) {
+                const int c = half + 2 * ci;
+                if (c >= BN / 32) break;
                 uint32_t acc[32];
                 tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
-                const int ncol = n0 + c * 32 + lane;
-                const float my_ws = ncol < p.N ? p.wscale[ncol] : 0.0f;
-                const float my_b = (p.bias && ncol < p.N) ? p.bias[ncol] : 0.0f;
                 tmem_ld_wait();
                 if (n0 + c * 32 >= p.N) continue;            // warp-uniform
                 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const float ws = __shfl_sync(0xFFFFFFFFu, my_ws, j);
-                    const float bj = __shfl_sync(0xFFFFFFFFu, my_b, j);
+                    const float ws = __shfl_sync(0xFFFFFFFFu, my_ws[ci], j);
+                    const float bj = __shfl_sync(0xFFFFFFFFu, my_b[ci], j);
                     float v;
                     if (acc_mode) {
                         v = __int_as_float(static_cast<int32_t>(acc[j]));
@@ -236,13 +273,17 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 }
                 __syncwarp();
                 const int n = n0 + c * 32 + cq;
+                const bool full4 = n + 4 <= p.N;
+                // next chunk's residual goes out before this chunk's stores
+                // (different columns, so no aliasing hazard)
+                float4 rn[8];
+                if (has_res && ci + 1 < kChunks && c + 2 < BN / 32) load_res(rn, m0, n0, c + 2);
                 #pragma unroll
                 for (int r8 = 0; r8 < 8; ++r8) {
                     const int r = rq + 4 * r8;
                     const int m = m0 + quarter * 32 + r;
                     if (m >= p.M || n >= p.N) continue;
                     float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
-                    const bool full4 = n + 4 <= p.N;
                     if (acc_mode) {
                         int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
                         #pragma unroll
@@ -250,21 +291,13 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                             if (n + e < p.N) o[e] = __float_as_int(v[e]);
                         continue;
                     }
-                    if (p.mode & (kEpiAdd | kEpiAddRelu)) {
-                        const float* rr = p.res + (long long)m * p.ldr + n;
-                        float rv[4];
-                        if (p.vec_ok && full4) {
-                            const float4 tt = *reinterpret_cast<const float4*>(rr);
-                            rv[0] = tt.x; rv[1] = tt.y; rv[2] = tt.z; rv[3] = tt.w;
-                        } else {
-                            #pragma unroll
-                            for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
-                        }
+                    if (has_res) {
+                        const float* rvv = reinterpret_cast<const float*>(&rv[r8]);
                         #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            if (p.mode & kEpiAdd) v[e] = __fadd_rn(rv[e], v[e]);             // x[i] += y[i]
-                            if (p.mode & kEpiAddRelu) {                                        // resnet_backbone.cpp:293-295
-                                v[e] = __fadd_rn(v[e], rv[e]);
+                            if (p.mode & kEpiAdd) v[e] = __fadd_rn(rvv[e], v[e]);             // x[i] += y[i]
+                            if (p.mode & kEpiAddRelu) {                                         // resnet_backbone.cpp:293-295
+                                v[e] = __fadd_rn(v[e], rvv[e]);
                                 v[e] = v[e] > 0.0f ? v[e] : 0.0f;
                             }
                         }
@@ -281,6 +314,10 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         for (int e = 0; e < 4; ++e)
                             if (n + e < p.N) o[e] = v[e];
                     }
+                }
+                if (has_res && ci + 1 < kChunks) {
+                    #pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) rv[r8] = rn[r8];
                 }
                 if (p.amax) {
                     // final values are back in the staging tile: per-row max, thread = row
@@ -317,11 +354,239 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (threadIdx.x == 0) {
         // never leave the CTA with TMA writes still landing in its shared memory
         for (int kb = *s_consumed; kb < issued; ++kb)
-            if (!mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1)) break;
+            if (!mbar_wait(&full[kb % stages], (kb / stages) & 1)) break;
     }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, 2 * BN);
+    }
+}
+
+// -------------------------------------------------------- split-K (cluster)
+// For GEMMs with few output tiles and a long K (the deep conv stages, the FFN
+// down-projection) one tile per SM leaves most SMs idle and each busy one
+// streaming every k-block alone. Here the `splits` CTAs of a thread-block
+// cluster (grid = splits x tiles, cluster = splits x 1) take the same 128 x BN
+// tile over disjoint k-block ranges, each into its own TMEM accumulator. The
+// int32 partial tiles then go to shared memory and are summed through
+// distributed shared memory - integer addition, so the sums are exact and
+// equal to the single-pass accumulators whatever the order - and each CTA
+// finishes the tile rows r = rank, rank + splits, ... through the same fp32
+// epilogue as the persistent kernel (bit-identical outputs).
+//   warp 0 lane 0: TMA producer; warp 1: TMEM + MMA issuer;
+//   warps 2-9: TMEM -> shared partial tile, then the cross-CTA sum + epilogue.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b,
+                   const EpiParams p, const int stages) {
+    constexpr int kABytes = kBM * kBK;
+    constexpr int kBBytes = BN * kBK;
+    constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
+    constexpr int kPS = BN + 4;           // partial tile row stride (int32): 16-byte rows, conflict-free v4
+    constexpr int kC4 = BN / 4;           // 4-column groups per row
+    constexpr int kRPP = 256 / kC4;       // tile rows per pass of the 256 epilogue threads
+    // the host guarantees kBM * kPS * 4 <= stages * (kABytes + kBBytes): the
+    // partial tile overlays the stage ring
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + stages * kABytes;
+    int32_t* part = reinterpret_cast<int32_t*>(smem);    // [kBM][kPS], once the ring is idle
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * kBBytes);
+    uint64_t* empty = full + stages;
+    uint64_t* acc_full = empty + stages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    unsigned int* s_amax = reinterpret_cast<unsigned int*>(tmem_slot + 2);   // [4]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int splits = gridDim.x;
+    const int rank = blockIdx.x;          // cluster (splits, 1, 1): rank in the cluster
+    const int n_tn = (p.N + BN - 1) / BN;
+    const int m0 = (blockIdx.y / n_tn) * kBM, n0 = (blockIdx.y % n_tn) * BN;
+    const int nkb = (p.K + kBK - 1) / kBK;
+    const int kb0 = static_cast<int>((long long)nkb * rank / splits);
+    const int my_kb = static_cast<int>((long long)nkb * (rank + 1) / splits) - kb0;   // >= 1: splits <= nkb
+    if (!p.static_weights) pdl_wait();
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(acc_full, 1);
+        *s_consumed = 0;
+        for (int i = 0; i < 4; ++i) s_amax[i] = 0u;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
+
+    int issued = 0;
+    if (warp == 0) {
+        if (lane == 0) {
+            const int pre = my_kb < stages ? my_kb : stages;
+            for (int i = 0; i < pre; ++i) {     // weights first: load-time constants
+                mbar_arrive_expect_tx(&full[i], kABytes + kBBytes);
+                tma_load_2d(sB + i * kBBytes, &tmap_b, &full[i], (kb0 + i) * kBK, n0);
+            }
+            pdl_wait();
+            for (int i = 0; i < my_kb; ++i) {
+                const int s = i % stages;
+                if (i >= pre) {
+                    if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) break;
+                    mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                    tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], (kb0 + i) * kBK, n0);
+                }
+                tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], (kb0 + i) * kBK, m0);
+                issued = i + 1;
+            }
+            if (issued < pre) issued = pre;     // the weight halves went out regardless
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool fail = false;
+            for (int i = 0; i < my_kb; ++i) {
+                const int s = i % stages;
+                if (!mbar_wait(&full[s], (i / stages) & 1)) { fail = true; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + s * kABytes);
+                const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+                #pragma unroll
+                for (int k = 0; k < kBK / kUmmaK; ++k)
+                    umma_s8(tmem_base, sw128_kmajor_desc(a_addr + k * kUmmaK),
+                            sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (i | k) != 0);
+                umma_commit(&empty[s]);
+                *s_consumed = i + 1;
+            }
+            if (!fail) umma_commit(acc_full);
+        }
+        __syncwarp();
+    } else {
+        pdl_wait();                 // activation scales / residual: predecessor data
+        mbar_wait(acc_full, 0);     // a timeout is recorded in the status word
+        tc_fence_after();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // the partial tile overlays the ring: no TMA write may still be landing
+        for (int i = *s_consumed; i < issued; ++i)
+            if (!mbar_wait(&full[i % stages], (i / stages) & 1)) break;
+    }
+    __syncthreads();
+
+    // ---- phase 1: this CTA's partial accumulators -> shared [row][col] int32
+    if (warp >= 2) {
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        #pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+            uint32_t acc[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
+            tmem_ld_wait();
+            int4* dst = reinterpret_cast<int4*>(part + row * kPS + c * 32);
+            #pragma unroll
+            for (int j = 0; j < 8; ++j)
+                dst[j] = make_int4(static_cast<int>(acc[4 * j]), static_cast<int>(acc[4 * j + 1]),
+                                   static_cast<int>(acc[4 * j + 2]), static_cast<int>(acc[4 * j + 3]));
+        }
+    }
+    tc_fence_before();
+    cluster_sync();      // every partial tile of the cluster is in shared memory
+
+    // ---- phase 2: sum the cluster's partials for rows rank, rank + splits, ...
+    if (warp >= 2) {
+        const int et = threadIdx.x - 64;
+        const int q = et % kC4, rsub = et / kC4;
+        const int n = n0 + 4 * q;
+        const bool acc_mode = (p.mode & kEpiAcc) != 0;
+        const bool has_res = (p.mode & (kEpiAdd | kEpiAddRelu)) != 0;
+        const bool vec = p.vec_ok && n + 4 <= p.N;
+        float ws[4], bb[4];
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const bool ok = n + e < p.N;
+            ws[e] = ok ? p.wscale[n + e] : 0.0f;
+            bb[e] = (ok && p.bias) ? p.bias[n + e] : 0.0f;
+        }
+        const uint32_t part_s = smem_u32(part);
+        const unsigned key0 = p.amax ? static_cast<unsigned>(m0 / p.amax_rows) : 0u;
+        unsigned cur_key = 0xFFFFFFFFu;
+        float cur_max = 0.0f;
+        auto flush = [&]() {
+            if (cur_key == 0xFFFFFFFFu) return;
+            if (cur_key - key0 < 4u) atomicMax(&s_amax[cur_key - key0], __float_as_uint(cur_max));
+            else atomicMax(&p.amax[cur_key], __float_as_uint(cur_max));
+        };
+        for (int j = rsub; rank + splits * j < kBM; j += kRPP) {
+            const int r = rank + splits * j;
+            const int m = m0 + r;
+            if (m >= p.M || n >= p.N) continue;
+            const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
+            int4 sum = make_int4(0, 0, 0, 0);
+            for (int src = 0; src < splits; ++src) {
+                const int4 v = dsmem_ld_v4(dsmem_map(off, static_cast<uint32_t>(src)));
+                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            }
+            const int32_t a4[4] = {sum.x, sum.y, sum.z, sum.w};
+            if (acc_mode) {
+                int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
+                #pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (n + e < p.N) o[e] = a4[e];
+                continue;
+            }
+            float rv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (has_res) {
+                const float* rr = p.res + (long long)m * p.ldr + n;
+                if (vec) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(rr);
+                    rv[0] = t4.x; rv[1] = t4.y; rv[2] = t4.z; rv[3] = t4.w;
+                } else {
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
+                }
+            }
+            const float as = p.ascale[(long long)m * p.as_stride];
+            float v[4];
+            float lmax = 0.0f;
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                v[e] = epi_value(a4[e], ws[e], as, bb[e], p.mode, &rv[e]);
+                if (n + e < p.N) lmax = fmaxf(lmax, fabsf(v[e]));
+            }
+            float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
+            if (vec) {
+                *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                #pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (n + e < p.N) o[e] = v[e];
+            }
+            if (p.amax) {
+                const unsigned key = static_cast<unsigned>(m / p.amax_rows);
+                if (key != cur_key) { flush(); cur_key = key; cur_max = 0.0f; }
+                cur_max = fmaxf(cur_max, lmax);
+            }
+        }
+        if (p.amax) {
+            flush();
+            asm volatile("bar.sync 1, 256;" ::: "memory");     // epilogue warps only
+            if (et < 4 && s_amax[et] != 0u) atomicMax(&p.amax[key0 + et], s_amax[et]);
+        }
+    }
+    cluster_sync();      // no CTA leaves while another still reads its partial tile
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, BN);
     }
 }
 
@@ -389,9 +654,32 @@ bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, lo
 
 namespace {
 
-template <int BN, int STAGES>
-constexpr size_t umma_smem_bytes() {
-    return 1024 + STAGES * (kBM * kBK + BN * kBK) + 8 * 32 * 33 * 4 + (2 * STAGES + 4) * 8 + 16;
+constexpr size_t kMaxDynSmem = 227 * 1024;   // per-CTA dynamic shared memory limit (sm_100)
+
+constexpr size_t umma_smem_bytes(int bn, int stages) {
+    return 1024 + (size_t)stages * (kBM * kBK + bn * kBK) + 8 * 32 * 33 * 4 + (2 * stages + 4) * 8 + 16;
+}
+
+constexpr size_t splitk_smem_bytes(int bn, int stages) {
+    return 1024 + (size_t)stages * (kBM * kBK + bn * kBK) + (2 * stages + 1) * 8 + 32;
+}
+
+// deepest ring that fits (capped at 8 stages)
+constexpr int umma_max_stages(int bn) {
+    int s = 8;
+    while (s > 2 && umma_smem_bytes(bn, s) > kMaxDynSmem) --s;
+    return s;
+}
+constexpr int splitk_max_stages(int bn) {
+    int s = 8;
+    while (s > 2 && splitk_smem_bytes(bn, s) > kMaxDynSmem) --s;
+    return s;
+}
+// the split-K partial tile [128][bn + 4] int32 overlays the ring
+constexpr int splitk_min_stages(int bn) {
+    int s = 2;
+    while ((size_t)s * (kBM * kBK + bn * kBK) < (size_t)kBM * (bn + 4) * 4) ++s;
+    return s;
 }
 
 int sm_count() {
@@ -405,25 +693,106 @@ int sm_count() {
     return n;
 }
 
+// cudaFuncSetAttribute is per device: one bit per device that has it. Every
+// GEMM kernel may use up to the full dynamic shared memory; occupancy still
+// follows the size each launch asks for.
+template <typename Kern>
+cudaError_t set_smem_attr_once(Kern kernel, std::atomic<unsigned long long>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxDynSmem));
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
+template <int BN>
+cudaError_t umma_ready() {
+    static std::atomic<unsigned long long> done{0};
+    return set_smem_attr_once(w8a8_umma_kernel<BN>, done);
+}
+template <int BN>
+cudaError_t splitk_ready() {
+    static std::atomic<unsigned long long> done{0};
+    return set_smem_attr_once(w8a8_splitk_kernel<BN>, done);
+}
+
 // Persistent launch: at most (SMs x resident CTAs) CTAs, each looping over
 // output tiles t = blockIdx.x, +gridDim.x, ...
-template <int BN, int STAGES>
-cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, cudaStream_t st) {
-    constexpr size_t smem = umma_smem_bytes<BN, STAGES>();
-    static int per_sm = 0;
-    if (!per_sm) {
-        const cudaError_t e = cudaFuncSetAttribute(w8a8_umma_kernel<BN, STAGES>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        int occ = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w8a8_umma_kernel<BN, STAGES>, kThreads, smem);
-        per_sm = occ > 0 ? occ : 1;
+template <int BN>
+cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int stages,
+                        cudaStream_t st) {
+    const size_t smem = umma_smem_bytes(BN, stages);
+    cudaError_t e = umma_ready<BN>();
+    if (e != cudaSuccess) return e;
+    static std::atomic<int> per_sm[9];     // resident CTAs per SM (registers and shared memory), by stages
+    int occ = per_sm[stages].load(std::memory_order_relaxed);
+    if (!occ) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w8a8_umma_kernel<BN>, kThreads, smem);
+        if (occ <= 0) occ = 1;
+        per_sm[stages].store(occ, std::memory_order_relaxed);
     }
     const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + kBM - 1) / kBM);
-    const long long cap = (long long)sm_count() * per_sm;
+    const long long cap = (long long)sm_count() * occ;
     const int grid = static_cast<int>(tiles < cap ? tiles : cap);
-    const cudaError_t le_ = launch_k(w8a8_umma_kernel<BN, STAGES>, grid, kThreads, smem, st, ta, tb, p);
-    if (le_ != cudaSuccess) return le_;
+    e = launch_k(w8a8_umma_kernel<BN>, grid, kThreads, smem, st, ta, tb, p, stages);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// How many clusters of `splits` split-K CTAs can be resident at once (the
+// GPCs' SM counts, not just the SM total, bound this: a cluster lives in one
+// GPC). Cached per device, cluster size and ring depth.
+template <int BN>
+int splitk_max_clusters(int splits, int stages) {
+    static std::atomic<int> cache[64][9][9];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || splits < 2 || splits > 8 || stages < 2 || stages > 8) return 0;
+    dev &= 63;
+    int v = cache[dev][splits][stages].load(std::memory_order_relaxed);
+    if (v) return v;
+    if (splitk_ready<BN>() != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = splitk_smem_bytes(BN, stages);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&v, w8a8_splitk_kernel<BN>, &cfg) != cudaSuccess || v <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    cache[dev][splits][stages].store(v, std::memory_order_relaxed);
+    return v;
+}
+
+int splitk_clusters(int bn, int splits, int stages) {
+    switch (bn) {
+        case 32: return splitk_max_clusters<32>(splits, stages);
+        case 64: return splitk_max_clusters<64>(splits, stages);
+        case 256: return splitk_max_clusters<256>(splits, stages);
+        default: return splitk_max_clusters<128>(splits, stages);
+    }
+}
+
+// Split-K launch: grid (splits, tiles), clusters of `splits` CTAs.
+template <int BN>
+cudaError_t launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int splits, int stages,
+                          cudaStream_t st) {
+    cudaError_t e = splitk_ready<BN>();
+    if (e != cudaSuccess) return e;
+    const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + kBM - 1) / kBM);
+    if (tiles > 65535 || splits < 2 || splits > 8) return cudaErrorInvalidValue;
+    e = launch_k_cluster(w8a8_splitk_kernel<BN>, dim3(splits, (unsigned)tiles), kThreads, dim3(splits, 1, 1),
+                         splitk_smem_bytes(BN, stages), st, ta, tb, p, stages);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -452,22 +821,81 @@ EpiParams make_epi(const GemmI8Args& a) {
 
 }  // namespace
 
-int gemm_i8_pick_bn(int M, int N) {
-    // Fill the 148 SMs: the widest N tile that still yields ~0.8 waves of CTAs,
-    // else the narrowest (the 602-row transformer GEMMs, the deep conv stages).
+GemmPlan gemm_i8_plan(int M, int N, int K) {
+    GemmPlan plan;
+    const int nkb = (K + kBK - 1) / kBK;
+    // VLA_GEMM_PLAN=<bn>:<splits>[:<stages>] forces one plan (tuning and tests)
+    if (const char* e = std::getenv("VLA_GEMM_PLAN")) {
+        int bn = 0, sp = 0, stg = 0;
+        const int n = std::sscanf(e, "%d:%d:%d", &bn, &sp, &stg);
+        if (n >= 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) && sp >= 1 && sp <= 8) {
+            plan.bn = bn;
+            plan.splits = sp <= nkb ? sp : nkb;
+            const int lo = plan.splits > 1 ? splitk_min_stages(bn) : 2;
+            const int hi = plan.splits > 1 ? splitk_max_stages(bn) : umma_max_stages(bn);
+            plan.stages = n == 3 ? (stg < lo ? lo : stg > hi ? hi : stg) : (plan.splits > 1 ? (lo > 4 ? lo : 4) : hi);
+            return plan;
+        }
+    }
+    // Cost model (relative units), fitted to device timings of every plan on
+    // the ACT policy's GEMM shapes (graph-replayed launches on cold data):
+    //   rounds x (k-blocks per CTA x bytes per k-block + output tile bytes)
+    //   + for split K: a fixed cluster cost + the partial-tile exchange.
+    // rounds = how many times the slowest SM runs a work unit.
+    const int sms = sm_count();
     const int mt = (M + kBM - 1) / kBM;
-    for (int bn : {128, 64, 32})
-        if (N > bn / 2 && mt * ((N + bn - 1) / bn) >= 120) return bn;
-    return 32;
+    double best = 1e30;
+    for (int bn : {32, 64, 128}) {
+        const long long tiles = (long long)mt * ((N + bn - 1) / bn);
+        for (int sp = 1; sp <= 8 && sp <= nkb; ++sp) {
+            long long slots;
+            int stages;
+            if (sp == 1) {
+                stages = 4;
+                slots = sms;               // one persistent CTA per SM (register bound)
+            } else {
+                stages = splitk_min_stages(bn) > 4 ? splitk_min_stages(bn) : 4;
+                if (tiles > 65535) continue;
+                slots = (long long)splitk_clusters(bn, sp, stages) * sp;
+                if (slots <= 0) continue;
+            }
+            const long long units = tiles * sp;
+            const long long rounds = (units + slots - 1) / slots;
+            const int kbc = (nkb + sp - 1) / sp;
+            double cost = (double)rounds * ((double)kbc * (kBM * kBK + bn * kBK) + 4.0 * kBM * bn);
+            if (sp > 1) cost += 31250.0 + 2.0 * 4.0 * kBM * bn * (sp - 1) / sp;
+            if (cost < best) {
+                best = cost;
+                plan.bn = bn;
+                plan.splits = sp;
+                plan.stages = stages;
+            }
+        }
+    }
+    return plan;
 }
 
-cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, int bn,
+cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, const GemmPlan& plan,
                          cudaStream_t st) {
     const EpiParams p = make_epi(a);
-    if (bn == 32) return launch_umma<32, 4>(ta, tb, p, st);
-    if (bn == 64) return launch_umma<64, 4>(ta, tb, p, st);
-    if (bn == 256) return launch_umma<256, 4>(ta, tb, p, st);
-    return launch_umma<128, 3>(ta, tb, p, st);
+    const int bn = plan.bn;
+    if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return cudaErrorInvalidValue;
+    if (plan.splits > 1) {
+        if (plan.stages < splitk_min_stages(bn) || plan.stages > splitk_max_stages(bn)) return cudaErrorInvalidValue;
+        switch (bn) {
+            case 32: return launch_splitk<32>(ta, tb, p, plan.splits, plan.stages, st);
+            case 64: return launch_splitk<64>(ta, tb, p, plan.splits, plan.stages, st);
+            case 256: return launch_splitk<256>(ta, tb, p, plan.splits, plan.stages, st);
+            default: return launch_splitk<128>(ta, tb, p, plan.splits, plan.stages, st);
+        }
+    }
+    if (plan.stages < 2 || plan.stages > umma_max_stages(bn)) return cudaErrorInvalidValue;
+    switch (bn) {
+        case 32: return launch_umma<32>(ta, tb, p, plan.stages, st);
+        case 64: return launch_umma<64>(ta, tb, p, plan.stages, st);
+        case 256: return launch_umma<256>(ta, tb, p, plan.stages, st);
+        default: return launch_umma<128>(ta, tb, p, plan.stages, st);
+    }
 }
 
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
@@ -477,12 +905,12 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (!a.force_simt && tma_ok) {
         // operands TMA can describe always take the tensor-core kernel; a tensor
         // map the driver refuses is an error, never a silent detour
-        const int bn = gemm_i8_pick_bn(a.M, a.N);
+        const GemmPlan plan = gemm_i8_plan(a.M, a.N, a.K);
         CUtensorMap ta, tb;
         if (!make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) ||
-            !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, bn))
+            !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, plan.bn))
             return cudaErrorInvalidConfiguration;
-        return gemm_i8_umma(a, ta, tb, bn, st);
+        return gemm_i8_umma(a, ta, tb, plan, st);
     }
     const EpiParams p = make_epi(a);
     if ((a.N + 127) / 128 > 65535) return cudaErrorInvalidValue;

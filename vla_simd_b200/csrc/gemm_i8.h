@@ -40,10 +40,19 @@ struct GemmI8Args {
 // otherwise the CUDA-core path (same results).
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st);
 
-// Pre-encoded variant for callers that keep tensor maps (the policy runtime).
+// Launch plan: output tile width BN (the B tensor map's box rows), the
+// number of CTAs of a cluster that split K for one tile (1 = persistent
+// kernel) and the depth of the shared-memory k-block ring.
+struct GemmPlan {
+    int bn = 128;
+    int splits = 1;
+    int stages = 4;
+};
+GemmPlan gemm_i8_plan(int M, int N, int K);
+
+// Pre-encoded variant for callers that keep tensor maps (box rows of tb = plan.bn).
 bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, long long ld, int box_rows);
-int gemm_i8_pick_bn(int M, int N);
-cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, int bn,
+cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, const GemmPlan& plan,
                          cudaStream_t st);
 
 // Read and clear the device status word (0 = OK, see sm100.cuh).

@@ -480,6 +480,247 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
     }
 }
 
+// ---- register-tiled variant (the default wherever its score rows fit)
+// CTA = one head x QP = 8*QPT query rows, 256 threads (two warps per SM
+// sub-partition), K and V streamed through 128-key tiles. Warp w, lane l:
+//   scores  rows 4*QPT*(w&1) + QPT*(l/8) + a (a < QPT), keys 32*(w/2) + l%8 + 8i
+//           (i < 4) of the tile: per 4 dims, QPT 16-byte Q loads (4 distinct
+//           addresses per warp) and 4 16-byte K loads (8 consecutive rows)
+//           feed 16*QPT fmas, one shared-memory wavefront per load;
+//   softmax warp w takes rows w, w+8, ...: row bound, masked max, exp and the
+//           final scaling are elementwise over all 32 lanes; only the
+//           reference's 8 in-order lane sums run 8 lanes per row;
+//   A*V     the same rows, dims 16*(w/2) + 2*(l%8) + {0,1}: per 4 keys, QPT
+//           16-byte probability loads and 4 8-byte V loads feed 8*QPT fmas.
+// K/V rows are 68 floats apart in shared memory (conflict-free 16-byte
+// loads); tiles are double-buffered with cp.async. Every per-output
+// accumulation runs in the reference's order (d = 0..63 for a score, keys in
+// order for an output), so the results are the reference's bits.
+constexpr int kAttRS = 68;   // floats per Q / K / V row in shared memory
+constexpr int kAttTK = 128;  // keys per K / V tile
+
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(smem_u32(sdst)), "l"(gsrc), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+__host__ __device__ constexpr size_t att_tiled_smem(int qp, int seq_k) {
+    return sizeof(float) * ((size_t)qp * att_row_stride(seq_k) + (size_t)qp * kAttRS + 2 * kAttTK * kAttRS);
+}
+
+template <int QPT>
+__global__ void __launch_bounds__(256, 1)
+attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
+                       const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
+                       int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
+    constexpr int QP = 8 * QPT;
+    constexpr int kTile = kAttTK * kAttRS;
+    extern __shared__ __align__(16) float att_smem[];
+    const int ss = att_row_stride(seq_k);
+    const int skp = (seq_k + 7) & ~7;
+    float* sS = att_smem;               // [QP][ss] scores -> probabilities
+    float* sQ = sS + QP * ss;           // [QP][kAttRS]
+    float* sKV = sQ + QP * kAttRS;      // [2][kAttTK][kAttRS] K tiles, then V tiles
+
+    const int h = blockIdx.y;
+    const int kvh = h / (n_q / n_kv);
+    const int q0 = blockIdx.x * QP;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane & 7;
+    const int r0 = (warp & 1) * (4 * QPT) + (lane >> 3) * QPT;   // this thread's first row
+    const int c0 = (warp >> 1) * 32;                              // key offset (scores) in the tile
+    const int d0 = (warp >> 1) * 16 + 2 * g;                      // first of two output dims
+    const float NINF = __int_as_float(0xff800000);
+    const float* Kh = K + (long long)kvh * kAttD;
+    const float* Vh = V + (long long)kvh * kAttD;
+    const int ntiles = (seq_k + kAttTK - 1) / kAttTK;
+
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+
+    // kAttTK rows x 16 chunks of 16 bytes; rows past seq_k are zero-filled
+    auto load_tile = [&](const float* base, long long ld, int k0, float* dst) {
+        for (int i = tid; i < kAttTK * 16; i += 256) {
+            const int r = i >> 4, c = i & 15;
+            const bool ok = k0 + r < seq_k;
+            cp_async16(dst + r * kAttRS + c * 4, base + (long long)(ok ? k0 + r : 0) * ld + c * 4, ok ? 16 : 0);
+        }
+    };
+    for (int i = tid; i < QP * 16; i += 256) {
+        const int r = i >> 4, c = i & 15;
+        const bool ok = q0 + r < seq_q;
+        cp_async16(sQ + r * kAttRS + c * 4, Q + (long long)(ok ? q0 + r : 0) * ldq + (long long)h * kAttD + c * 4,
+                   ok ? 16 : 0);
+    }
+    load_tile(Kh, ldk, 0, sKV);
+    cp_async_commit();
+
+    // ---- scores
+    for (int t = 0; t < ntiles; ++t) {
+        const float* cur = sKV + (t & 1) * kTile + (c0 + g) * kAttRS;
+        if (t + 1 < ntiles) load_tile(Kh, ldk, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
+        cp_async_commit();
+        cp_async_wait_prev();           // tile t (and Q) have landed
+        __syncthreads();
+        float acc[QPT][4];
+        #pragma unroll
+        for (int a = 0; a < QPT; ++a)
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) acc[a][i] = 0.0f;
+        #pragma unroll 2
+        for (int d = 0; d < kAttD; d += 4) {
+            float4 qv[QPT], kv[4];
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a) qv[a] = *reinterpret_cast<const float4*>(sQ + (r0 + a) * kAttRS + d);
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) kv[i] = *reinterpret_cast<const float4*>(cur + 8 * i * kAttRS + d);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a)
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[a][i] = __fmaf_rn(qv[a].x, kv[i].x, acc[a][i]);
+                    acc[a][i] = __fmaf_rn(qv[a].y, kv[i].y, acc[a][i]);
+                    acc[a][i] = __fmaf_rn(qv[a].z, kv[i].z, acc[a][i]);
+                    acc[a][i] = __fmaf_rn(qv[a].w, kv[i].w, acc[a][i]);
+                }
+        }
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int key = t * kAttTK + c0 + g + 8 * i;
+            if (key < skp) {
+                #pragma unroll
+                for (int a = 0; a < QPT; ++a) sS[(r0 + a) * ss + key] = __fmul_rn(acc[a][i], scale);
+            }
+        }
+        __syncthreads();                // the buffer is refilled two tiles on
+    }
+    load_tile(Vh, ldv, 0, sKV);         // V tile 0 streams in during the softmax
+    cp_async_commit();
+
+    // ---- softmax: warp w takes rows w, w + 8, ...
+    for (int r = warp; r < QP; r += 8) {
+        const int q = q0 + r;
+        float* srow = sS + r * ss;
+        const float* mrow = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
+        // row bound: trailing `lowest` mask entries block keys (hal::row_bound)
+        int jmax = seq_k;
+        if (mrow) {
+            int last = -1;
+            for (int j = lane; j < seq_k; j += 32)
+                if (mrow[j] != -FLT_MAX) last = j;
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
+            jmax = last + 1;
+        }
+        float mx = NINF;
+        for (int j = lane; j < skp; j += 32) {
+            float v = srow[j];
+            if (j >= jmax) v = NINF;
+            else if (mrow) v = __fadd_rn(v, mrow[j]);
+            srow[j] = v;
+            mx = fmaxf(mx, v);
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+        if (mx > -FLT_MAX) {
+            for (int j = lane; j < skp; j += 32) srow[j] = ref_exp(__fsub_rn(srow[j], mx));
+        } else {
+            // fully blocked row: uniform weights over every key (attn_uniform_row);
+            // a negative row max marks it for the scaling pass below
+            const float u = __fdiv_rn(1.0f, (float)seq_k);
+            for (int j = lane; j < skp; j += 32) srow[j] = j < seq_k ? u : 0.0f;
+        }
+        __syncwarp();
+        // the reference's 8 lane sums (lane t adds e[t], e[t+8], ... in order),
+        // combined ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+        float lane_sum = 0.0f;
+        if (lane < 8)
+            for (int j = lane; j < skp; j += 8) lane_sum = __fadd_rn(lane_sum, srow[j]);
+        float l[8];
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, lane_sum, i);
+        if (mx > -FLT_MAX) {
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[1], l[5])),
+                                        __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
+            const float inv = __fdiv_rn(1.0f, sum);
+            for (int j = lane; j < skp; j += 32) srow[j] = __fmul_rn(srow[j], inv);
+        }
+    }
+
+    // ---- A*V
+    float o[QPT][2];
+    #pragma unroll
+    for (int a = 0; a < QPT; ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
+    for (int t = 0; t < ntiles; ++t) {
+        const float* cur = sKV + (t & 1) * kTile + d0;
+        if (t + 1 < ntiles) load_tile(Vh, ldv, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
+        cp_async_commit();
+        cp_async_wait_prev();
+        __syncthreads();                // also: the softmax is done before tile 0
+        const int k0 = t * kAttTK;
+        const int kn = min(kAttTK, seq_k - k0);
+        const float* prow = sS + r0 * ss + k0;
+        int j = 0;
+        #pragma unroll 2
+        for (; j + 4 <= kn; j += 4) {
+            float4 pv[QPT];
+            float2 vv[4];
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a) pv[a] = *reinterpret_cast<const float4*>(prow + a * ss + j);
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) vv[i] = *reinterpret_cast<const float2*>(cur + (j + i) * kAttRS);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a) {
+                const float pa[4] = {pv[a].x, pv[a].y, pv[a].z, pv[a].w};
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    o[a][0] = __fmaf_rn(pa[i], vv[i].x, o[a][0]);
+                    o[a][1] = __fmaf_rn(pa[i], vv[i].y, o[a][1]);
+                }
+            }
+        }
+        for (; j < kn; ++j) {           // ragged tail: exactly seq_k keys enter each chain
+            const float2 vv = *reinterpret_cast<const float2*>(cur + j * kAttRS);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a) {
+                const float pa = prow[a * ss + j];
+                o[a][0] = __fmaf_rn(pa, vv.x, o[a][0]);
+                o[a][1] = __fmaf_rn(pa, vv.y, o[a][1]);
+            }
+        }
+        __syncthreads();
+    }
+    #pragma unroll
+    for (int a = 0; a < QPT; ++a) {
+        const int q = q0 + r0 + a;
+        if (q < seq_q)
+            *reinterpret_cast<float2*>(O + (long long)q * ldo + (long long)h * kAttD + d0) =
+                make_float2(o[a][0], o[a][1]);
+    }
+}
+
+template <int QPT>
+cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                                   long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                                   float scale, const float* mask, cudaStream_t st) {
+    const size_t smem = att_tiled_smem(8 * QPT, seq_k);
+    static int configured = 0;
+    if ((int)smem > configured) {
+        const cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel<QPT>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = (int)smem;
+    }
+    dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q);
+    const cudaError_t e = launch_k(attention_tiled_kernel<QPT>, grid, 256, smem, st, Q, ldq, K, ldk, V, ldv, O, ldo,
+                                   seq_q, seq_k, n_q, n_kv, scale, mask);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 template <int QT, int NT>
 cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                              long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
@@ -513,12 +754,38 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
         return cudaErrorInvalidValue;
     const size_t ss = (size_t)att_row_stride(seq_k);
     auto need = [&](int qt) { return sizeof(float) * (qt * ss + (size_t)kAttD * qt + (size_t)kAttKT * kAttD); };
+    // Register-tiled kernel: the query tile (8, 16 or 40 rows) that gives the
+    // busiest SM the fewest rows (ceil(CTAs / SMs) x rows; ties to the larger
+    // tile, which reuses each K/V tile more). 602 queries x 8 heads: 40 rows,
+    // 128 CTAs in one wave; the decoder's 100 queries: 8 rows, 104 CTAs.
+    if (att_tiled_smem(8, seq_k) <= 227 * 1024) {
+        int best_qpt = 0;
+        long long best_rows = 0;
+        for (int qpt : {5, 2, 1}) {
+            if (att_tiled_smem(8 * qpt, seq_k) > 227 * 1024) continue;
+            const long long ctas = (long long)((seq_q + 8 * qpt - 1) / (8 * qpt)) * n_q;
+            const long long rows = (ctas + 147) / 148 * 8 * qpt;
+            if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
+        }
+        if (best_qpt == 5)
+            return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
+        if (best_qpt == 2)
+            return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
+        return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
+    }
+    // Longer key ranges (> ~1100 keys): score rows of fewer queries per CTA.
     // 16 queries x 128 threads per CTA: measured fastest among 8..32 queries x
-    // 64..512 threads at the ACT shapes (more work per thread beats more warps)
-    if (need(16) <= 200 * 1024)
+    // 64..512 threads at the ACT encoder shape (more work per thread beats
+    // more warps). Fewer queries (the decoder's 100) would leave most SMs idle
+    // with 16 per CTA: narrower query tiles until the grid covers the SMs.
+    const long long ctas16 = (long long)((seq_q + 15) / 16) * n_q;
+    const long long ctas8 = (long long)((seq_q + 7) / 8) * n_q;
+    if (ctas16 >= 148 && need(16) <= 200 * 1024)
         return launch_attention<16, 128>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(16), st);
-    if (need(8) <= 220 * 1024)
+    if (ctas8 >= 148 && need(8) <= 220 * 1024)
         return launch_attention<8, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(8), st);
+    if (need(4) <= 220 * 1024)
+        return launch_attention<4, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(4), st);
     return cudaErrorInvalidValue;   // > ~13000 keys: not a shape any policy here has
 }
 
