@@ -288,7 +288,15 @@ __device__ __forceinline__ float ref_exp(float x) {
     x = (88.3762626647949f < x) ? 88.3762626647949f : x;
     x = (-88.3762626647950f > x) ? -88.3762626647950f : x;
     float fx = __fmaf_rn(x, 1.44269504088896341f, 0.5f);
-    fx = floorf(fx);
+    // floor(fx) for |fx| < 2^22 (here |fx| <= 128) in plain fp32 adds: adding
+    // and removing 1.5 * 2^23 rounds to the nearest integer exactly, then step
+    // down if that went up. Equal to floorf, but on the fma pipe instead of
+    // the narrow conversion unit (this exp runs once per attention score).
+    constexpr float kRound = 12582912.0f;   // 1.5 * 2^23, bits 0x4B400000
+    {
+        const float r = __fsub_rn(__fadd_rn(fx, kRound), kRound);
+        fx = r > fx ? __fsub_rn(r, 1.0f) : r;
+    }
     x = __fmaf_rn(-fx, 0.693359375f, x);
     x = __fmaf_rn(-fx, -2.12194440e-4f, x);
     float y = 1.9875691500e-4f;
@@ -298,7 +306,7 @@ __device__ __forceinline__ float ref_exp(float x) {
     y = __fmaf_rn(y, x, 1.6666665459e-1f);
     y = __fmaf_rn(y, x, 5.0000001201e-1f);
     y = __fmaf_rn(y, __fmul_rn(x, x), __fadd_rn(x, 1.0f));
-    const int n = __float2int_rn(fx);
+    const int n = __float_as_int(__fadd_rn(fx, kRound)) - 0x4B400000;   // (int)fx: fx is an integer
     y = __fmul_rn(y, __int_as_float((n + 127) << 23));
     return keep ? y : 0.0f;
 }
@@ -487,10 +495,10 @@ attention_kernel(const float* __restrict__ Q, long long ldq, const float* __rest
 //           (i < 4) of the tile: per 4 dims, QPT 16-byte Q loads (4 distinct
 //           addresses per warp) and 4 16-byte K loads (8 consecutive rows)
 //           feed 16*QPT fmas, one shared-memory wavefront per load;
-//   softmax warp w takes rows w, w+8, ...: row bound, masked max, exp and the
+//   softmax warp w takes rows QPT*w ..: row bound, masked max, exp and the
 //           final scaling are elementwise over all 32 lanes; only the
 //           reference's 8 in-order lane sums run 8 lanes per row;
-//   A*V     the same rows, dims 16*(w/2) + 2*(l%8) + {0,1}: per 4 keys, QPT
+//   A*V     the score phase's rows, dims 16*(w/2) + 2*(l%8) + {0,1}: per 4 keys, QPT
 //           16-byte probability loads and 4 8-byte V loads feed 8*QPT fmas.
 // K/V rows are 68 floats apart in shared memory (conflict-free 16-byte
 // loads); tiles are double-buffered with cp.async. Every per-output
@@ -577,15 +585,24 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             for (int a = 0; a < QPT; ++a) qv[a] = *reinterpret_cast<const float4*>(sQ + (r0 + a) * kAttRS + d);
             #pragma unroll
             for (int i = 0; i < 4; ++i) kv[i] = *reinterpret_cast<const float4*>(cur + 8 * i * kAttRS + d);
+            // d, d+1, d+2, d+3 in order per accumulator; consecutive fmas
+            // touch different accumulators (no dependent back-to-back issue)
             #pragma unroll
             for (int a = 0; a < QPT; ++a)
                 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[a][i] = __fmaf_rn(qv[a].x, kv[i].x, acc[a][i]);
-                    acc[a][i] = __fmaf_rn(qv[a].y, kv[i].y, acc[a][i]);
-                    acc[a][i] = __fmaf_rn(qv[a].z, kv[i].z, acc[a][i]);
-                    acc[a][i] = __fmaf_rn(qv[a].w, kv[i].w, acc[a][i]);
-                }
+                for (int i = 0; i < 4; ++i) acc[a][i] = __fmaf_rn(qv[a].x, kv[i].x, acc[a][i]);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a)
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) acc[a][i] = __fmaf_rn(qv[a].y, kv[i].y, acc[a][i]);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a)
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) acc[a][i] = __fmaf_rn(qv[a].z, kv[i].z, acc[a][i]);
+            #pragma unroll
+            for (int a = 0; a < QPT; ++a)
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) acc[a][i] = __fmaf_rn(qv[a].w, kv[i].w, acc[a][i]);
         }
         #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -600,53 +617,126 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
     load_tile(Vh, ldv, 0, sKV);         // V tile 0 streams in during the softmax
     cp_async_commit();
 
-    // ---- softmax: warp w takes rows w, w + 8, ...
-    for (int r = warp; r < QP; r += 8) {
-        const int q = q0 + r;
-        float* srow = sS + r * ss;
-        const float* mrow = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
-        // row bound: trailing `lowest` mask entries block keys (hal::row_bound)
-        int jmax = seq_k;
-        if (mrow) {
-            int last = -1;
-            for (int j = lane; j < seq_k; j += 32)
-                if (mrow[j] != -FLT_MAX) last = j;
-            #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
-            jmax = last + 1;
+    // ---- softmax: warp w takes rows QPT*w + k (k < QPT), processed together
+    // so every pass has QPT independent chains in flight
+    {
+        float* srow[QPT];
+        const float* mrow[QPT];
+        int jmax[QPT];
+        float mx[QPT];
+        #pragma unroll
+        for (int k = 0; k < QPT; ++k) {
+            const int r = QPT * warp + k;
+            const int q = q0 + r;
+            srow[k] = sS + r * ss;
+            mrow[k] = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
+            // row bound: trailing `lowest` mask entries block keys (hal::row_bound)
+            int last = seq_k - 1;
+            if (mrow[k]) {
+                last = -1;
+                for (int j = lane; j < seq_k; j += 32)
+                    if (mrow[k][j] != -FLT_MAX) last = j;
+                #pragma unroll
+                for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
+            }
+            jmax[k] = last + 1;
+            mx[k] = NINF;
         }
-        float mx = NINF;
-        for (int j = lane; j < skp; j += 32) {
-            float v = srow[j];
-            if (j >= jmax) v = NINF;
-            else if (mrow) v = __fadd_rn(v, mrow[j]);
-            srow[j] = v;
-            mx = fmaxf(mx, v);
+        // Each pass loads all of an iteration's elements before storing any:
+        // the row pointers may alias as far as the compiler knows, so a
+        // load-compute-store sequence per element would serialize on the
+        // shared-memory latency (and on the exp chain).
+        // (branch-free bodies: selects, so the QPT rows' chains interleave)
+        if (mask) {
+            for (int j = lane; j < skp; j += 32) {
+                float v[QPT];
+                #pragma unroll
+                for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
+                #pragma unroll
+                for (int k = 0; k < QPT; ++k) {
+                    const float mv = (mrow[k] && j < jmax[k]) ? mrow[k][j] : 0.0f;
+                    v[k] = j >= jmax[k] ? NINF : (mrow[k] ? __fadd_rn(v[k], mv) : v[k]);
+                    mx[k] = fmaxf(mx[k], v[k]);
+                }
+                #pragma unroll
+                for (int k = 0; k < QPT; ++k) srow[k][j] = v[k];
+            }
+        } else {
+            for (int j = lane; j < skp; j += 32) {
+                float v[QPT];
+                #pragma unroll
+                for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
+                #pragma unroll
+                for (int k = 0; k < QPT; ++k) {
+                    v[k] = j >= seq_k ? NINF : v[k];
+                    mx[k] = fmaxf(mx[k], v[k]);
+                }
+                if (j >= seq_k) {
+                    #pragma unroll
+                    for (int k = 0; k < QPT; ++k) srow[k][j] = NINF;
+                }
+            }
         }
         #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
-        if (mx > -FLT_MAX) {
-            for (int j = lane; j < skp; j += 32) srow[j] = ref_exp(__fsub_rn(srow[j], mx));
-        } else {
-            // fully blocked row: uniform weights over every key (attn_uniform_row);
-            // a negative row max marks it for the scaling pass below
-            const float u = __fdiv_rn(1.0f, (float)seq_k);
-            for (int j = lane; j < skp; j += 32) srow[j] = j < seq_k ? u : 0.0f;
+        for (int k = 0; k < QPT; ++k)
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xFFFFFFFFu, mx[k], off));
+        const float u = __fdiv_rn(1.0f, (float)seq_k);
+        for (int j = lane; j < skp; j += 32) {
+            float v[QPT];
+            #pragma unroll
+            for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
+            #pragma unroll
+            for (int k = 0; k < QPT; ++k) {
+                // a fully blocked row (max <= lowest) takes uniform weights over
+                // every key (attn_uniform_row); the scaling pass leaves it alone.
+                // The exp is computed either way (no branch), then selected.
+                const float e = ref_exp(__fsub_rn(v[k], mx[k]));
+                v[k] = mx[k] > -FLT_MAX ? e : (j < seq_k ? u : 0.0f);
+            }
+            #pragma unroll
+            for (int k = 0; k < QPT; ++k) srow[k][j] = v[k];
         }
         __syncwarp();
-        // the reference's 8 lane sums (lane t adds e[t], e[t+8], ... in order),
-        // combined ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
-        float lane_sum = 0.0f;
-        if (lane < 8)
-            for (int j = lane; j < skp; j += 8) lane_sum = __fadd_rn(lane_sum, srow[j]);
-        float l[8];
+        // the reference's 8 lane sums: lane t adds e[t], e[t+8], ... in order,
+        // combined ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)). Lane l runs sum
+        // (l % 8) of rows k = l/8, l/8 + 4 (two chains per lane).
+        const int t = lane & 7, kk = lane >> 3;
+        float s0 = 0.0f, s1 = 0.0f;
+        const float* rowa = kk < QPT ? sS + (QPT * warp + kk) * ss : nullptr;
+        const float* rowb = kk + 4 < QPT ? sS + (QPT * warp + kk + 4) * ss : nullptr;
+        if (rowa && rowb) {
+            #pragma unroll 4
+            for (int j = t; j < skp; j += 8) { s0 = __fadd_rn(s0, rowa[j]); s1 = __fadd_rn(s1, rowb[j]); }
+        } else if (rowa) {
+            #pragma unroll 8
+            for (int j = t; j < skp; j += 8) s0 = __fadd_rn(s0, rowa[j]);
+        }
+        float inv[QPT];
         #pragma unroll
-        for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, lane_sum, i);
-        if (mx > -FLT_MAX) {
+        for (int k = 0; k < QPT; ++k) {
+            float l[8];
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, k < 4 ? s0 : s1, 8 * (k & 3) + i);
             const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[1], l[5])),
                                         __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
-            const float inv = __fdiv_rn(1.0f, sum);
-            for (int j = lane; j < skp; j += 32) srow[j] = __fmul_rn(srow[j], inv);
+            inv[k] = __fdiv_rn(1.0f, sum);
+        }
+        for (int j = lane; j < skp; j += 64) {
+            const bool two = j + 32 < skp;
+            float v[QPT], w[QPT];
+            #pragma unroll
+            for (int k = 0; k < QPT; ++k) {
+                v[k] = srow[k][j];
+                w[k] = two ? srow[k][j + 32] : 0.0f;
+            }
+            #pragma unroll
+            for (int k = 0; k < QPT; ++k) {
+                if (mx[k] > -FLT_MAX) {
+                    srow[k][j] = __fmul_rn(v[k], inv[k]);
+                    if (two) srow[k][j + 32] = __fmul_rn(w[k], inv[k]);
+                }
+            }
         }
     }
 
@@ -672,15 +762,15 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             for (int a = 0; a < QPT; ++a) pv[a] = *reinterpret_cast<const float4*>(prow + a * ss + j);
             #pragma unroll
             for (int i = 0; i < 4; ++i) vv[i] = *reinterpret_cast<const float2*>(cur + (j + i) * kAttRS);
+            // keys j..j+3 in order per output; 2*QPT independent chains per key
             #pragma unroll
-            for (int a = 0; a < QPT; ++a) {
-                const float pa[4] = {pv[a].x, pv[a].y, pv[a].z, pv[a].w};
+            for (int i = 0; i < 4; ++i)
                 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    o[a][0] = __fmaf_rn(pa[i], vv[i].x, o[a][0]);
-                    o[a][1] = __fmaf_rn(pa[i], vv[i].y, o[a][1]);
+                for (int a = 0; a < QPT; ++a) {
+                    const float pa = i == 0 ? pv[a].x : i == 1 ? pv[a].y : i == 2 ? pv[a].z : pv[a].w;
+                    o[a][0] = __fmaf_rn(pa, vv[i].x, o[a][0]);
+                    o[a][1] = __fmaf_rn(pa, vv[i].y, o[a][1]);
                 }
-            }
         }
         for (; j < kn; ++j) {           // ragged tail: exactly seq_k keys enter each chain
             const float2 vv = *reinterpret_cast<const float2*>(cur + j * kAttRS);
