@@ -564,6 +564,31 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
                                 cudaStream_t st) {
     const int Ho = conv_out(H, c.k, c.stride, c.pad), Wo = conv_out(W, c.k, c.stride, c.pad);
     const int rows = F * Ho * Wo;
+    if (c.lin.int8 && conv_i8_implicit_supported(c.cin, c.k, c.stride)) {
+        // stride-1 convs over >= 64 channels: quantize the input once, then the
+        // tensor-core GEMM gathers the taps itself (no im2col matrix)
+        VSB_TRY(quantize_frames_i8(in, F, (long long)H * W * c.cin, amax_in, i8_clip_, d_col_, d_col_scale_, st));
+        ConvI8Args a;
+        a.x = d_col_;
+        a.F = F;
+        a.H = H;
+        a.W = W;
+        a.C = c.cin;
+        a.k = c.k;
+        a.pad = c.pad;
+        a.Wq = c.lin.Wq;
+        a.ldw = c.lin.ldw;
+        a.N = c.cout;
+        a.fscale = d_col_scale_;
+        a.wscale = c.lin.wscale;
+        a.bias = c.lin.bias;
+        a.out = out;
+        a.res = res;
+        a.amax = amax_out;
+        a.mode = mode;
+        a.static_weights = true;
+        return conv_i8_implicit(a, st);
+    }
     if (c.lin.int8) {
         VSB_TRY(im2col_i8(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, c.lin.ldw, amax_in, i8_clip_, d_col_,
                           d_col_scale_, st));

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -231,6 +232,30 @@ int32_t vla_cuda_conv2d_i8(float* out, const float* x, int32_t F, int32_t H, int
     cudaStream_t st = as_stream(stream);
     cudaError_t e = cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t) * F, st);
     if (e == cudaSuccess) e = vsb::absmax_slots(x, (long long)F * H * W * Cin, (long long)H * W * Cin, amax_scratch, st);
+    if (e == cudaSuccess && vsb::conv_i8_implicit_supported(Cin, k, stride) && !std::getenv("VLA_CONV_IM2COL")) {
+        // stride 1, >= 64 channels: quantized NHWC input (fits col_scratch: F*H*W*Cin <= the
+        // im2col matrix), taps gathered by the GEMM itself; VLA_CONV_IM2COL=1 keeps im2col
+        e = vsb::quantize_frames_i8(x, F, (long long)H * W * Cin, amax_scratch, clip, col_scratch, rscale_scratch, st);
+        if (e != cudaSuccess) return status_of(e);
+        vsb::ConvI8Args a;
+        a.x = col_scratch;
+        a.F = F;
+        a.H = H;
+        a.W = W;
+        a.C = Cin;
+        a.k = k;
+        a.pad = pad;
+        a.Wq = Wq;
+        a.ldw = ldw;
+        a.N = Cout;
+        a.fscale = rscale_scratch;
+        a.wscale = wscale;
+        a.bias = bias;
+        a.out = out;
+        a.res = res;
+        a.mode = mode;
+        return status_of(vsb::conv_i8_implicit(a, st));
+    }
     if (e == cudaSuccess)
         e = vsb::im2col_i8(x, F, H, W, Cin, k, stride, pad, Ho, Wo, ldw, amax_scratch, clip, col_scratch,
                            rscale_scratch, st);

@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 #include <atomic>
 #include <cfloat>
+#include <climits>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -66,7 +67,58 @@ struct EpiParams {
     int vec_ok;                   // 16-byte aligned rows: float4 stores
     int static_weights;           // B / wscale / bias never written by a kernel:
                                   // safe to read before the predecessor finishes
+    int m_tiles;                  // 128-row M tiles
+    // Implicit convolution (conv_bw > 0). A is an int8 NHWC tensor [F][H][W][C]
+    // read through a 4D tensor map; M tile mt is the output patch (frame f,
+    // tile row ty, tile column tx) of conv_bh x conv_bw pixels, tile row r the
+    // pixel (ty*conv_bh + r / conv_bw, tx*conv_bw + r % conv_bw). K runs over
+    // (ky, kx, channel block): k-block kb = tap * conv_cb + channel block.
+    // ascale is per frame.
+    int conv_bw, conv_bh, conv_tx, conv_ty, conv_ho, conv_wo, conv_k, conv_pad, conv_cb;
 };
+
+// Output row (index into out / res, and the absmax slot numerator) of tile
+// row r of M tile mt; -1 where the tile row maps to no output.
+__device__ __forceinline__ int out_row(const EpiParams& p, int mt, int r) {
+    if (!p.conv_bw) {
+        const int m = mt * kBM + r;
+        return m < p.M ? m : -1;
+    }
+    const int per_f = p.conv_ty * p.conv_tx;
+    const int f = mt / per_f, rem = mt - f * per_f;
+    const int ty = rem / p.conv_tx, tx = rem - ty * p.conv_tx;
+    const int ly = r / p.conv_bw, lx = r - ly * p.conv_bw;
+    const int oy = ty * p.conv_bh + ly, ox = tx * p.conv_bw + lx;
+    if (ly >= p.conv_bh || oy >= p.conv_ho || ox >= p.conv_wo) return -1;
+    return (f * p.conv_ho + oy) * p.conv_wo + ox;
+}
+
+// activation scale of output row m
+__device__ __forceinline__ float row_ascale(const EpiParams& p, int m) {
+    return p.conv_bw ? p.ascale[m / (p.conv_ho * p.conv_wo)] : p.ascale[(long long)m * p.as_stride];
+}
+
+// The A operand of M tile mt, k-block kb (KBB bytes of K) -> shared memory.
+template <int KBB>
+__device__ __forceinline__ void load_a(const EpiParams& p, const CUtensorMap* ta, void* dst, uint64_t* bar, int mt,
+                                       int kb) {
+    if (!p.conv_bw) {
+        tma_load_2d(dst, ta, bar, kb * KBB, mt * kBM);
+        return;
+    }
+    const int per_f = p.conv_ty * p.conv_tx;
+    const int f = mt / per_f, rem = mt - f * per_f;
+    const int ty = rem / p.conv_tx, tx = rem - ty * p.conv_tx;
+    const int tap = kb / p.conv_cb, cb = kb - tap * p.conv_cb;
+    const int ky = tap / p.conv_k, kx = tap - ky * p.conv_k;
+    tma_load_4d(dst, ta, bar, cb * KBB, tx * p.conv_bw - p.conv_pad + kx, ty * p.conv_bh - p.conv_pad + ky, f);
+}
+
+template <int KBB>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+    if constexpr (KBB == 128) return sw128_kmajor_desc(saddr);
+    else return sw64_kmajor_desc(saddr);
+}
 
 __device__ __forceinline__ float epi_value(int32_t acc, float ws, float as, float b, int mode,
                                            const float* resp) {
@@ -77,13 +129,13 @@ __device__ __forceinline__ float epi_value(int32_t acc, float ws, float as, floa
     return v;
 }
 
-template <int BN>
+template <int BN, int KBB>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b,
                  const EpiParams p, const int stages) {
-    constexpr int kABytes = kBM * kBK;
-    constexpr int kBBytes = BN * kBK;
+    constexpr int kABytes = kBM * KBB;
+    constexpr int kBBytes = BN * KBB;
     constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
     constexpr int kStg = 32 * 33;   // floats: one epilogue warp's 32 x 32 staging tile, padded
     constexpr int kEpiWarps = 8;
@@ -104,8 +156,10 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int n_tn = (p.N + BN - 1) / BN;
-    const int n_tiles = n_tn * ((p.M + kBM - 1) / kBM);
-    const int nkb = (p.K + kBK - 1) / kBK;
+    const int n_tiles = n_tn * p.m_tiles;
+    const int nkb = (p.K + KBB - 1) / KBB;
+    // bytes one k-block brings in: a conv patch box may be under 128 rows
+    const uint32_t stage_tx = (p.conv_bw ? KBB * p.conv_bw * p.conv_bh : kABytes) + kBBytes;
     // weights that a predecessor kernel may still be writing: wait up front
     if (!p.static_weights) pdl_wait();
 
@@ -136,25 +190,25 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             {
                 const int n0 = (blockIdx.x % n_tn) * BN;
                 for (int kb = 0; kb < pre; ++kb) {
-                    mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
-                    tma_load_2d(sB + kb * kBBytes, &tmap_b, &full[kb], kb * kBK, n0);
+                    mbar_arrive_expect_tx(&full[kb], stage_tx);
+                    tma_load_2d(sB + kb * kBBytes, &tmap_b, &full[kb], kb * KBB, n0);
                 }
             }
             pdl_wait();
             int it = 0;
             bool fail = false;
             for (int t = blockIdx.x; t < n_tiles && !fail; t += gridDim.x) {
-                const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
+                const int mt = t / n_tn, n0 = (t % n_tn) * BN;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % stages;
                     if (it < pre) {   // first tile's weights already in flight
-                        tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
+                        load_a<KBB>(p, &tmap_a, sA + s * kABytes, &full[s], mt, kb);
                     } else {
                         const int use = it / stages;   // > 0 unless the ring is longer than the first tile
                         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) { fail = true; break; }
-                        mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
-                        tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, m0);
-                        tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * kBK, n0);
+                        mbar_arrive_expect_tx(&full[s], stage_tx);
+                        load_a<KBB>(p, &tmap_a, sA + s * kABytes, &full[s], mt, kb);
+                        tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], kb * KBB, n0);
                     }
                     issued = it + 1;
                 }
@@ -178,9 +232,9 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const uint32_t a_addr = smem_u32(sA + s * kABytes);
                     const uint32_t b_addr = smem_u32(sB + s * kBBytes);
                     #pragma unroll
-                    for (int k = 0; k < kBK / kUmmaK; ++k) {
-                        umma_s8(d_tmem, sw128_kmajor_desc(a_addr + k * kUmmaK),
-                                sw128_kmajor_desc(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
+                    for (int k = 0; k < KBB / kUmmaK; ++k) {
+                        umma_s8(d_tmem, kmajor_desc<KBB>(a_addr + k * kUmmaK),
+                                kmajor_desc<KBB>(b_addr + k * kUmmaK), kIdesc, (kb | k) != 0);
                     }
                     umma_commit(&empty[s]);
                     *s_consumed = it + 1;
@@ -206,14 +260,14 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
         pdl_wait();   // activation scales / residual / output: predecessor data
         constexpr int kChunks = (BN / 32 + 1) / 2;   // column chunks per warp: c = half, half + 2, ...
         // residual of chunk c for this lane's 8 rows x 4 columns (phase B layout)
-        auto load_res = [&](float4 (&rv)[8], int m0, int n0, int c) {
+        auto load_res = [&](float4 (&rv)[8], const int (&mrow)[8], int n0, int c) {
             const int n = n0 + c * 32 + cq;
             const bool full4 = n + 4 <= p.N;
             #pragma unroll
             for (int r8 = 0; r8 < 8; ++r8) {
-                const int m = m0 + quarter * 32 + rq + 4 * r8;
+                const int m = mrow[r8];
                 rv[r8] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (m >= p.M || n >= p.N) continue;
+                if (m < 0 || n >= p.N) continue;
                 const float* rr = p.res + (long long)m * p.ldr + n;
                 if (p.vec_ok && full4) {
                     rv[r8] = *reinterpret_cast<const float4*>(rr);
@@ -228,14 +282,17 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int buf = i & 1;
-            const int m0 = (t / n_tn) * kBM, n0 = (t % n_tn) * BN;
-            const int m_row = m0 + quarter * 32 + lane;
+            const int mt = t / n_tn, n0 = (t % n_tn) * BN;
+            const int m_row = out_row(p, mt, quarter * 32 + lane);     // phase A row (thread = row)
+            int mrow[8];                                                // phase B rows of this lane
+            #pragma unroll
+            for (int r8 = 0; r8 < 8; ++r8) mrow[r8] = out_row(p, mt, quarter * 32 + rq + 4 * r8);
             // Everything the epilogue reads besides the accumulators is fetched
             // before waiting for them, so its latency hides behind the MMAs:
             // row scale, column scales / biases of every chunk, first residual.
             // (Each lane later writes only elements it read here or reads
             // itself, so a residual aliasing out is never read after a store.)
-            const float as = m_row < p.M ? p.ascale[(long long)m_row * p.as_stride] : 0.0f;
+            const float as = m_row >= 0 ? row_ascale(p, m_row) : 0.0f;
             float my_ws[kChunks], my_b[kChunks];
             #pragma unroll
             for (int ci = 0; ci < kChunks; ++ci) {
@@ -245,7 +302,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 my_b[ci] = (ok && p.bias) ? p.bias[ncol] : 0.0f;
             }
             float4 rv[8];
-            if (has_res && half < BN / 32) load_res(rv, m0, n0, half);
+            if (has_res && half < BN / 32) load_res(rv, mrow, n0, half);
             // warp-uniform: the tcgen05.ld and shuffles below need every lane
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (i >> 1) & 1))) break;
             tc_fence_after();
@@ -277,12 +334,12 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 // next chunk's residual goes out before this chunk's stores
                 // (different columns, so no aliasing hazard)
                 float4 rn[8];
-                if (has_res && ci + 1 < kChunks && c + 2 < BN / 32) load_res(rn, m0, n0, c + 2);
+                if (has_res && ci + 1 < kChunks && c + 2 < BN / 32) load_res(rn, mrow, n0, c + 2);
                 #pragma unroll
                 for (int r8 = 0; r8 < 8; ++r8) {
                     const int r = rq + 4 * r8;
-                    const int m = m0 + quarter * 32 + r;
-                    if (m >= p.M || n >= p.N) continue;
+                    const int m = mrow[r8];
+                    if (m < 0 || n >= p.N) continue;
                     float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
                     if (acc_mode) {
                         int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
@@ -334,7 +391,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
             if (p.amax) {
                 // one atomic per warp when the warp's rows share a slot, else per row
-                const bool row_ok = m_row < p.M;
+                const bool row_ok = m_row >= 0;
                 const unsigned key = row_ok ? static_cast<unsigned>(m_row / p.amax_rows) : 0xFFFFFFFFu;
                 const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
                 if (__all_sync(0xFFFFFFFFu, key == k0 || key == 0xFFFFFFFFu)) {
@@ -406,8 +463,9 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int splits = gridDim.x;
     const int rank = blockIdx.x;          // cluster (splits, 1, 1): rank in the cluster
     const int n_tn = (p.N + BN - 1) / BN;
-    const int m0 = (blockIdx.y / n_tn) * kBM, n0 = (blockIdx.y % n_tn) * BN;
+    const int mt = blockIdx.y / n_tn, n0 = (blockIdx.y % n_tn) * BN;
     const int nkb = (p.K + kBK - 1) / kBK;
+    const uint32_t stage_tx = (p.conv_bw ? kBK * p.conv_bw * p.conv_bh : kABytes) + kBBytes;
     const int kb0 = static_cast<int>((long long)nkb * rank / splits);
     const int my_kb = static_cast<int>((long long)nkb * (rank + 1) / splits) - kb0;   // >= 1: splits <= nkb
     if (!p.static_weights) pdl_wait();
@@ -433,7 +491,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (lane == 0) {
             const int pre = my_kb < stages ? my_kb : stages;
             for (int i = 0; i < pre; ++i) {     // weights first: load-time constants
-                mbar_arrive_expect_tx(&full[i], kABytes + kBBytes);
+                mbar_arrive_expect_tx(&full[i], stage_tx);
                 tma_load_2d(sB + i * kBBytes, &tmap_b, &full[i], (kb0 + i) * kBK, n0);
             }
             pdl_wait();
@@ -441,10 +499,10 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 const int s = i % stages;
                 if (i >= pre) {
                     if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1)) break;
-                    mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
                     tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], (kb0 + i) * kBK, n0);
                 }
-                tma_load_2d(sA + s * kABytes, &tmap_a, &full[s], (kb0 + i) * kBK, m0);
+                load_a<kBK>(p, &tmap_a, sA + s * kABytes, &full[s], mt, kb0 + i);
                 issued = i + 1;
             }
             if (issued < pre) issued = pre;     // the weight halves went out regardless
@@ -518,7 +576,8 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             bb[e] = (ok && p.bias) ? p.bias[n + e] : 0.0f;
         }
         const uint32_t part_s = smem_u32(part);
-        const unsigned key0 = p.amax ? static_cast<unsigned>(m0 / p.amax_rows) : 0u;
+        // tile row 0 always maps to an output row (the tile's origin)
+        const unsigned key0 = p.amax ? static_cast<unsigned>(out_row(p, mt, 0) / p.amax_rows) : 0u;
         unsigned cur_key = 0xFFFFFFFFu;
         float cur_max = 0.0f;
         auto flush = [&]() {
@@ -528,8 +587,8 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         };
         for (int j = rsub; rank + splits * j < kBM; j += kRPP) {
             const int r = rank + splits * j;
-            const int m = m0 + r;
-            if (m >= p.M || n >= p.N) continue;
+            const int m = out_row(p, mt, r);
+            if (m < 0 || n >= p.N) continue;
             const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
             int4 sum = make_int4(0, 0, 0, 0);
             for (int src = 0; src < splits; ++src) {
@@ -555,7 +614,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
                 }
             }
-            const float as = p.ascale[(long long)m * p.as_stride];
+            const float as = row_ascale(p, m);
             float v[4];
             float lmax = 0.0f;
             #pragma unroll
@@ -654,10 +713,47 @@ bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, lo
 
 namespace {
 
+// 4D map over an int8 NHWC tensor [F][H][W][C]: box {kbb channels, bw, bh, 1},
+// swizzled like the K-major operand tiles the MMA reads (128- or 64-byte rows).
+bool make_tmap_nhwc_i8(CUtensorMap* map, const void* base, int F, int H, int W, int C, int kbb, int bw, int bh) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || C % kbb || (kbb != 64 && kbb != 128)) return false;
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(F)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W) * C,
+                                   static_cast<cuuint64_t>(H) * W * C};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(kbb), static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh),
+                               1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          kbb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// 2D K-major weight map with kbb-byte k-blocks (the 64-byte form for 64-channel convs)
+bool make_tmap_i8_kmajor_kb(CUtensorMap* map, const void* base, int rows, int K, long long ld, int box_rows,
+                            int kbb) {
+    if (kbb == 128) return make_tmap_i8_kmajor(map, base, rows, K, ld, box_rows);
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 15) || K <= 0 || rows <= 0) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kbb), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 constexpr size_t kMaxDynSmem = 227 * 1024;   // per-CTA dynamic shared memory limit (sm_100)
 
-constexpr size_t umma_smem_bytes(int bn, int stages) {
-    return 1024 + (size_t)stages * (kBM * kBK + bn * kBK) + 8 * 32 * 33 * 4 + (2 * stages + 4) * 8 + 16;
+constexpr size_t umma_smem_bytes(int bn, int stages, int kbb = kBK) {
+    return 1024 + (size_t)stages * (kBM * kbb + bn * kbb) + 8 * 32 * 33 * 4 + (2 * stages + 4) * 8 + 16;
 }
 
 constexpr size_t splitk_smem_bytes(int bn, int stages) {
@@ -708,10 +804,10 @@ cudaError_t set_smem_attr_once(Kern kernel, std::atomic<unsigned long long>& don
     return e;
 }
 
-template <int BN>
+template <int BN, int KBB>
 cudaError_t umma_ready() {
     static std::atomic<unsigned long long> done{0};
-    return set_smem_attr_once(w8a8_umma_kernel<BN>, done);
+    return set_smem_attr_once(w8a8_umma_kernel<BN, KBB>, done);
 }
 template <int BN>
 cudaError_t splitk_ready() {
@@ -721,23 +817,23 @@ cudaError_t splitk_ready() {
 
 // Persistent launch: at most (SMs x resident CTAs) CTAs, each looping over
 // output tiles t = blockIdx.x, +gridDim.x, ...
-template <int BN>
+template <int BN, int KBB = kBK>
 cudaError_t launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int stages,
                         cudaStream_t st) {
-    const size_t smem = umma_smem_bytes(BN, stages);
-    cudaError_t e = umma_ready<BN>();
+    const size_t smem = umma_smem_bytes(BN, stages, KBB);
+    cudaError_t e = umma_ready<BN, KBB>();
     if (e != cudaSuccess) return e;
     static std::atomic<int> per_sm[9];     // resident CTAs per SM (registers and shared memory), by stages
     int occ = per_sm[stages].load(std::memory_order_relaxed);
     if (!occ) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w8a8_umma_kernel<BN>, kThreads, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, w8a8_umma_kernel<BN, KBB>, kThreads, smem);
         if (occ <= 0) occ = 1;
         per_sm[stages].store(occ, std::memory_order_relaxed);
     }
-    const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + kBM - 1) / kBM);
+    const long long tiles = (long long)((p.N + BN - 1) / BN) * p.m_tiles;
     const long long cap = (long long)sm_count() * occ;
     const int grid = static_cast<int>(tiles < cap ? tiles : cap);
-    e = launch_k(w8a8_umma_kernel<BN>, grid, kThreads, smem, st, ta, tb, p, stages);
+    e = launch_k(w8a8_umma_kernel<BN, KBB>, grid, kThreads, smem, st, ta, tb, p, stages);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -788,7 +884,7 @@ cudaError_t launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
                           cudaStream_t st) {
     cudaError_t e = splitk_ready<BN>();
     if (e != cudaSuccess) return e;
-    const long long tiles = (long long)((p.N + BN - 1) / BN) * ((p.M + kBM - 1) / kBM);
+    const long long tiles = (long long)((p.N + BN - 1) / BN) * p.m_tiles;
     if (tiles > 65535 || splits < 2 || splits > 8) return cudaErrorInvalidValue;
     e = launch_k_cluster(w8a8_splitk_kernel<BN>, dim3(splits, (unsigned)tiles), kThreads, dim3(splits, 1, 1),
                          splitk_smem_bytes(BN, stages), st, ta, tb, p, stages);
@@ -813,6 +909,7 @@ EpiParams make_epi(const GemmI8Args& a) {
     p.N = a.N;
     p.K = a.K;
     p.static_weights = a.static_weights ? 1 : 0;
+    p.m_tiles = (a.M + kBM - 1) / kBM;
     const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
     p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 &&
                (!a.res || ((rb & 15) == 0 && (a.ldr & 3) == 0));
@@ -921,6 +1018,97 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
+}
+
+bool conv_i8_implicit_supported(int C, int k, int stride) {
+    return stride == 1 && k >= 1 && C > 0 && C % 64 == 0;
+}
+
+cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st) {
+    if (!a.x || !a.Wq || !a.fscale || !a.wscale || !a.out || a.F <= 0 || a.H <= 0 || a.W <= 0 || a.N <= 0 ||
+        a.pad < 0 || !conv_i8_implicit_supported(a.C, a.k, 1))
+        return cudaErrorInvalidValue;
+    const int Ho = a.H + 2 * a.pad - a.k + 1, Wo = a.W + 2 * a.pad - a.k + 1;
+    const long long K = (long long)a.k * a.k * a.C;
+    if (Ho <= 0 || Wo <= 0 || K > INT_MAX / (255 * 127) || a.ldw < K || (a.ldw & 15) ||
+        (long long)a.F * Ho * Wo >= (1LL << 31) || (long long)a.F * a.H * a.W * a.C >= (1LL << 40))
+        return cudaErrorInvalidValue;
+    // Output patch per 128-row tile: the width (power of two, or the whole
+    // row) giving the fewest tiles; ties to the wider patch.
+    int bw = 0, bh = 0;
+    long long best = 0;
+    for (int cw : {Wo, 128, 64, 32, 16, 8, 4, 2, 1}) {
+        if (cw <= 0 || cw > 128) continue;
+        const int ch = 128 / cw;
+        const long long tiles = (long long)((Wo + cw - 1) / cw) * ((Ho + ch - 1) / ch);
+        if (!bw || tiles < best) { best = tiles; bw = cw; bh = ch; }
+    }
+    const int kbb = a.C % 128 == 0 ? 128 : 64;
+    EpiParams p{};
+    p.out = a.out;
+    p.ldo = a.N;
+    p.res = a.res;
+    p.ldr = a.N;
+    p.ascale = a.fscale;
+    p.wscale = a.wscale;
+    p.bias = a.bias;
+    p.amax = a.amax;
+    p.amax_rows = Ho * Wo;
+    p.mode = a.mode;
+    p.M = a.F * Ho * Wo;
+    p.N = a.N;
+    p.K = static_cast<int>(K);
+    p.static_weights = a.static_weights ? 1 : 0;
+    const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
+    p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.N & 3) == 0 && (!a.res || (rb & 15) == 0);
+    p.conv_bw = bw;
+    p.conv_bh = bh;
+    p.conv_tx = (Wo + bw - 1) / bw;
+    p.conv_ty = (Ho + bh - 1) / bh;
+    p.conv_ho = Ho;
+    p.conv_wo = Wo;
+    p.conv_k = a.k;
+    p.conv_pad = a.pad;
+    p.conv_cb = a.C / kbb;
+    p.m_tiles = a.F * p.conv_ty * p.conv_tx;
+    GemmPlan plan;
+    if (kbb == 64) {
+        // 64-channel inputs: 64-byte k-blocks (one tap each), persistent kernel
+        plan.bn = a.N >= 64 ? 64 : 32;
+        plan.splits = 1;
+        plan.stages = 8;
+        if (const char* e = std::getenv("VLA_GEMM_PLAN")) {
+            int bn = 0, sp = 0;
+            if (std::sscanf(e, "%d:%d", &bn, &sp) >= 1 && (bn == 32 || bn == 64)) plan.bn = bn;
+        }
+    } else {
+        plan = gemm_i8_plan(p.m_tiles * kBM, a.N, static_cast<int>(K));
+    }
+    CUtensorMap ta, tb;
+    if (!make_tmap_nhwc_i8(&ta, a.x, a.F, a.H, a.W, a.C, kbb, bw, bh) ||
+        !make_tmap_i8_kmajor_kb(&tb, a.Wq, a.N, static_cast<int>(K), a.ldw, plan.bn, kbb))
+        return cudaErrorInvalidConfiguration;
+    if (kbb == 64) {
+        if (plan.bn == 32) return launch_umma<32, 64>(ta, tb, p, plan.stages, st);
+        return launch_umma<64, 64>(ta, tb, p, plan.stages, st);
+    }
+    if (plan.splits > 1) {
+        if (plan.stages < splitk_min_stages(plan.bn) || plan.stages > splitk_max_stages(plan.bn))
+            return cudaErrorInvalidValue;
+        switch (plan.bn) {
+            case 32: return launch_splitk<32>(ta, tb, p, plan.splits, plan.stages, st);
+            case 64: return launch_splitk<64>(ta, tb, p, plan.splits, plan.stages, st);
+            case 256: return launch_splitk<256>(ta, tb, p, plan.splits, plan.stages, st);
+            default: return launch_splitk<128>(ta, tb, p, plan.splits, plan.stages, st);
+        }
+    }
+    if (plan.stages < 2 || plan.stages > umma_max_stages(plan.bn)) return cudaErrorInvalidValue;
+    switch (plan.bn) {
+        case 32: return launch_umma<32>(ta, tb, p, plan.stages, st);
+        case 64: return launch_umma<64>(ta, tb, p, plan.stages, st);
+        case 256: return launch_umma<256>(ta, tb, p, plan.stages, st);
+        default: return launch_umma<128>(ta, tb, p, plan.stages, st);
+    }
 }
 
 int device_status_take() {

@@ -55,6 +55,31 @@ bool make_tmap_i8_kmajor(CUtensorMap* map, const void* base, int rows, int K, lo
 cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUtensorMap& tb, const GemmPlan& plan,
                          cudaStream_t st);
 
+// Implicit-GEMM convolution, stride 1, on the same tensor-core kernels: the
+// A operand is read straight from an int8 NHWC tensor by 4D TMA tile loads
+// (one per filter tap and channel block; out-of-image taps read zeros), so no
+// im2col matrix is written. x = int8 [F][H][W][C] quantized with the per-frame
+// scales fscale[F]; weights [N][ldw] over K = k*k*C in (ky, kx, c) order;
+// out = fp32 NHWC [F][Ho][Wo][N], the gemm_i8 epilogue (mode, residual of the
+// same shape, absmax slot = frame). Requires C % 64 == 0.
+struct ConvI8Args {
+    const int8_t* x = nullptr;
+    int F = 0, H = 0, W = 0, C = 0, k = 0, pad = 0;
+    const int8_t* Wq = nullptr;
+    long long ldw = 0;
+    int N = 0;
+    const float* fscale = nullptr;
+    const float* wscale = nullptr;
+    const float* bias = nullptr;
+    float* out = nullptr;
+    const float* res = nullptr;
+    unsigned int* amax = nullptr;
+    int mode = 0;
+    bool static_weights = false;
+};
+bool conv_i8_implicit_supported(int C, int k, int stride);
+cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st);
+
 // Read and clear the device status word (0 = OK, see sm100.cuh).
 int device_status_take();
 

@@ -884,35 +884,51 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
 // ReLU `!(o > 0) -> 0`. F frames of NHWC. Optional per-frame absmax tap for the
 // next conv's per-tensor quantization.
 __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restrict__ out, int F, int H, int W, int C,
-                                    int k, int stride, int pad, int Ho, int Wo, unsigned int* __restrict__ amax) {
+                                    int k, int stride, int pad, int Ho, int Wo, int vw, unsigned int* __restrict__ amax) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     // blockIdx.y = frame, so a block's absmax goes to one slot: reduce in the
-    // block, then one atomic per block
+    // block, then one atomic per block. Thread = vw (4 or 1) channels of one
+    // output pixel (4: C % 4 == 0 and 16-byte aligned tensors); 32-bit index
+    // math.
     const int f = blockIdx.y;
-    const long long per_frame = (long long)Ho * Wo * C;
+    const int cg = C / vw;
+    const int per_frame = Ho * Wo * cg;
     const float* xf = x + (long long)f * H * W * C;
-    float* of = out + (long long)f * per_frame;
+    float* of = out + (long long)f * Ho * Wo * C;
     float bmax = 0.0f;
-    for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < per_frame;
-         r += (long long)gridDim.x * blockDim.x) {
-        const int c = static_cast<int>(r % C);
-        const int pix = static_cast<int>(r / C);
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < per_frame; r += gridDim.x * blockDim.x) {
+        const int pix = r / cg;
+        const int c = (r - pix * cg) * vw;
         const int oy = pix / Wo, ox = pix - oy * Wo;
-        float o = -INFINITY;
+        float o[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         for (int ky = 0; ky < k; ++ky) {
             const int iy = oy * stride - pad + ky;
             if (iy < 0 || iy >= H) continue;
             for (int kx = 0; kx < k; ++kx) {
                 const int ix = ox * stride - pad + kx;
                 if (ix < 0 || ix >= W) continue;
-                const float v = xf[((long long)iy * W + ix) * C + c];
-                o = v > o ? v : o;
+                const float* src = xf + (iy * W + ix) * C + c;
+                if (vw == 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(src);
+                    o[0] = v.x > o[0] ? v.x : o[0];
+                    o[1] = v.y > o[1] ? v.y : o[1];
+                    o[2] = v.z > o[2] ? v.z : o[2];
+                    o[3] = v.w > o[3] ? v.w : o[3];
+                } else {
+                    const float v = *src;
+                    o[0] = v > o[0] ? v : o[0];
+                }
             }
         }
-        if (!(o > 0.0f)) o = 0.0f;
-        of[r] = o;
-        bmax = fmaxf(bmax, o);
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (!(o[e] > 0.0f)) o[e] = 0.0f;
+            bmax = fmaxf(bmax, o[e]);
+        }
+        float* dst = of + pix * C + c;
+        if (vw == 4) *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        else *dst = o[0];
     }
     if (amax) {
         bmax = warp_max_f(bmax);
@@ -929,14 +945,16 @@ __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restri
 
 cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C, int k, int stride, int pad,
                          int Ho, int Wo, unsigned int* amax, cudaStream_t st) {
-    const long long per_frame = (long long)Ho * Wo * C;
-    if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
+    if (F <= 0 || Ho <= 0 || Wo <= 0 || C <= 0 || (long long)H * W * C >= (1LL << 31) ||
+        (long long)Ho * Wo * C >= (1LL << 31))
+        return cudaErrorInvalidValue;
+    const bool vec = C % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    const long long per_frame = (long long)Ho * Wo * (vec ? C / 4 : C);
     long long bx = (per_frame + 255) / 256;
     if (bx > 148 * 8) bx = 148 * 8;
     {
         const cudaError_t le_ = launch_k(maxpool_relu_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st,
-                                         x, out, F, H, W, C, k, stride, pad, Ho, Wo,
-                                                                        amax);
+                                         x, out, F, H, W, C, k, stride, pad, Ho, Wo, vec ? 4 : 1, amax);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
@@ -945,23 +963,30 @@ cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C,
 // --------------------------------------------------- camera frame normalize
 // uint8 HWC -> (p/255 - mean[c]) / (std[c] + eps), per camera f
 // (src/models/act/act_model.cpp:116-121). mean/std are [F][3]. Per-frame absmax tap.
-__global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* __restrict__ out, int F, long long npx,
+__global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* __restrict__ out, int F, int npx,
                                         const float* __restrict__ mean, const float* __restrict__ stdv, float eps,
                                         unsigned int* __restrict__ amax) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
+    // thread = one pixel of frame blockIdx.y (its 3 interleaved channels)
     const int f = blockIdx.y;
-    const long long per_frame = npx * 3;
-    const uint8_t* src = img + (long long)f * per_frame;
-    float* dst = out + (long long)f * per_frame;
+    const uint8_t* src = img + (long long)f * npx * 3;
+    float* dst = out + (long long)f * npx * 3;
+    float mu[3], den[3];
+    #pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        mu[c] = mean[f * 3 + c];
+        den[c] = __fadd_rn(stdv[f * 3 + c], eps);
+    }
     float bmax = 0.0f;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_frame;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int c = static_cast<int>(i % 3);
-        const float p = __fdiv_rn((float)src[i], 255.0f);
-        const float v = __fdiv_rn(__fsub_rn(p, mean[f * 3 + c]), __fadd_rn(stdv[f * 3 + c], eps));
-        dst[i] = v;
-        bmax = fmaxf(bmax, fabsf(v));
+    for (int px = blockIdx.x * blockDim.x + threadIdx.x; px < npx; px += gridDim.x * blockDim.x) {
+        #pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float p = __fdiv_rn((float)src[3 * px + c], 255.0f);
+            const float v = __fdiv_rn(__fsub_rn(p, mu[c]), den[c]);
+            dst[3 * px + c] = v;
+            bmax = fmaxf(bmax, fabsf(v));
+        }
     }
     if (amax) {
         bmax = warp_max_f(bmax);
@@ -978,13 +1003,12 @@ __global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* 
 
 cudaError_t normalize_frames(const uint8_t* img, float* out, int F, long long npx, const float* mean,
                              const float* stdv, float eps, unsigned int* amax, cudaStream_t st) {
-    const long long per_frame = npx * 3;
-    if (per_frame <= 0 || F <= 0) return cudaErrorInvalidValue;
-    long long bx = (per_frame + 255) / 256;
+    if (npx <= 0 || F <= 0 || npx * 3 >= (1LL << 31)) return cudaErrorInvalidValue;
+    long long bx = (npx + 255) / 256;
     if (bx > 148 * 8) bx = 148 * 8;
     {
         const cudaError_t le_ = launch_k(normalize_frames_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st,
-                                         img, out, F, npx, mean, stdv, eps, amax);
+                                         img, out, F, (int)npx, mean, stdv, eps, amax);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

@@ -166,41 +166,102 @@ im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k,
     }
 }
 
-// im2col for small channel counts (the 3-channel stem): one warp per output
-// row; lane l copies the C contiguous NHWC values of taps l, l+32, ...; lane
-// work past the k*k taps zero-fills the row's padding [K, ldc).
+// im2col for channel counts that are not a multiple of 16 (the 3-channel
+// stem): one thread per 16-byte group of an output row, like the kernel
+// above, but element by element: the group's first patch element e = 16g is
+// split into (tap, channel) once, then (ky, kx, ci) advance incrementally.
+// One 16-byte store per thread (a row's groups are consecutive threads).
 __global__ void __launch_bounds__(256)
-im2col_i8_taps_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride, int pad, int Ho,
-                      int Wo, int K, long long ldc, const unsigned int* __restrict__ amax_bits, float clip,
-                      int8_t* __restrict__ col, float* __restrict__ rscale) {
+im2col_i8_bytes_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k, int stride, int pad, int Ho,
+                       int Wo, int K, int ldc, const unsigned int* __restrict__ amax_bits, float clip,
+                       int8_t* __restrict__ col, float* __restrict__ rscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int rows = F * Ho * Wo;
-    const int taps = k * k;
-    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += (gridDim.x * blockDim.x) >> 5) {
-        const int npix = Ho * Wo;
+    __shared__ float s_inv[8], s_scale[8];
+    if (threadIdx.x < F && threadIdx.x < 8) {
+        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
+        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+        s_scale[threadIdx.x] = s;
+        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
+    }
+    __syncthreads();
+    const int groups = ldc >> 4;
+    const int npix = Ho * Wo;
+    const int total = F * npix * groups;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int row = t / groups;
+        const int g = t - row * groups;
         const int f = row / npix;
         const int pix = row - f * npix;
+        const float inv = s_inv[f];
+        if (g == 0) rscale[row] = s_scale[f];
         const int oy = pix / Wo, ox = pix - oy * Wo;
-        const float amax = __uint_as_float(amax_bits[f]);
-        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        const float inv = __fdiv_rn(1.0f, s);
-        if (lane == 0) rscale[row] = s;
-        int8_t* dst = col + (long long)row * ldc;
-        for (long long i = K + lane; i < ldc; i += 32) dst[i] = 0;
-        for (int tap = lane; tap < taps; tap += 32) {
-            const int ky = tap / k, kx = tap - ky * k;
-            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-            int8_t* d = dst + tap * C;
-            if (iy < 0 || iy >= H || ix < 0 || ix >= W) {
-                for (int c = 0; c < C; ++c) d[c] = 0;
-            } else {
-                const float* src = x + (((long long)f * H + iy) * W + ix) * C;
-                for (int c = 0; c < C; ++c) d[c] = q8_span(src[c], inv);
+        const int e0 = 16 * g;
+        int tap = e0 / C;
+        int ci = e0 - tap * C;
+        int ky = tap / k, kx = tap - ky * k;
+        const float* xf = x + (long long)f * H * W * C;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            if (e0 + i < K) {
+                const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+                int8_t q = 0;
+                if (iy >= 0 && iy < H && ix >= 0 && ix < W) q = q8_span(xf[((long long)iy * W + ix) * C + ci], inv);
+                w[i >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (i & 3));
+                if (++ci == C) {
+                    ci = 0;
+                    if (++kx == k) { kx = 0; ++ky; }
+                }
             }
         }
+        reinterpret_cast<int4*>(col + (long long)row * ldc)[g] =
+            make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]), static_cast<int>(w[2]), static_cast<int>(w[3]));
     }
+}
+
+// Per-frame quantization for the implicit-GEMM convolution: F frames of
+// per_frame contiguous floats (NHWC) -> int8 with the scale the im2col path
+// uses (frame absmax slot -> s = max(amax * clip / 127, FLT_MIN), 1 if the
+// frame is all zero), fscale[f] = s. blockIdx.y = frame; 4 floats per thread
+// when per_frame % 4 == 0.
+__global__ void quantize_frames_i8_kernel(const float* __restrict__ x, long long per_frame,
+                                          const unsigned int* __restrict__ amax_bits, float clip,
+                                          int8_t* __restrict__ q, float* __restrict__ fscale, int vec) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    const int f = blockIdx.y;
+    const float amax = __uint_as_float(amax_bits[f]);
+    const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, s);
+    if (blockIdx.x == 0 && threadIdx.x == 0) fscale[f] = s;
+    const float* xf = x + (long long)f * per_frame;
+    int8_t* qf = q + (long long)f * per_frame;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    if (vec) {
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; 4 * i < per_frame; i += stride) {
+            const float4 v = reinterpret_cast<const float4*>(xf)[i];
+            reinterpret_cast<char4*>(qf)[i] =
+                make_char4(q8_span(v.x, inv), q8_span(v.y, inv), q8_span(v.z, inv), q8_span(v.w, inv));
+        }
+    } else {
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_frame; i += stride)
+            qf[i] = q8_span(xf[i], inv);
+    }
+}
+
+cudaError_t quantize_frames_i8(const float* x, int F, long long per_frame, const unsigned int* amax_bits, float clip,
+                               int8_t* q, float* fscale, cudaStream_t st) {
+    if (F <= 0 || per_frame <= 0 || F > 65535) return cudaErrorInvalidValue;
+    const int vec = per_frame % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                    ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
+    const long long items = vec ? per_frame / 4 : per_frame;
+    long long bx = (items + 255) / 256;
+    if (bx > 148 * 4) bx = 148 * 4;
+    const cudaError_t e = launch_k(quantize_frames_i8_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st, x,
+                                   per_frame, amax_bits, clip, q, fscale, vec);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
 }
 
 // Per-slot absmax of a contiguous tensor: slot = blockIdx.y covers elements
@@ -299,10 +360,11 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
                                          Ho, Wo, K, (int)ldc, amax_bits, clip, col, rscale);
         if (le_ != cudaSuccess) return le_;
     } else {
-        long long blocks = (rows * 32 + threads - 1) / threads;
-        if (blocks > 148 * 16) blocks = 148 * 16;
-        const cudaError_t le_ = launch_k(im2col_i8_taps_kernel, (int)blocks, threads, 0, st, x, F, H, W, C, k, stride,
-                                         pad, Ho, Wo, K, ldc, amax_bits, clip, col, rscale);
+        if ((reinterpret_cast<uintptr_t>(col) & 15)) return cudaErrorInvalidValue;
+        long long blocks = (rows * (ldc / 16) + threads - 1) / threads;
+        if (blocks > 148 * 32) blocks = 148 * 32;
+        const cudaError_t le_ = launch_k(im2col_i8_bytes_kernel, (int)blocks, threads, 0, st, x, F, H, W, C, k,
+                                         stride, pad, Ho, Wo, K, (int)ldc, amax_bits, clip, col, rscale);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

@@ -18,6 +18,12 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
                       long long ldc, const unsigned int* amax_bits, float clip, int8_t* col, float* rscale,
                       cudaStream_t st);
 
+// Per-frame int8 quantization of F frames of per_frame floats with the scale
+// im2col_i8 uses (from amax_bits[f] and clip): q has x's layout, fscale [F].
+// The input of the implicit-GEMM convolution.
+cudaError_t quantize_frames_i8(const float* x, int F, long long per_frame, const unsigned int* amax_bits, float clip,
+                               int8_t* q, float* fscale, cudaStream_t st);
+
 // atomicMax of |x| (float bits) per slot of per_slot consecutive elements.
 cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsigned int* amax_bits,
                          cudaStream_t st);

@@ -121,6 +121,19 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// 4D tile load (implicit convolution: box {channels, W, H, 1} of an NHWC
+// tensor); x = channel offset, a multiple of 16 bytes. Coordinates past the
+// tensor (conv padding) read zeros.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z, int32_t w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
+           "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05 --
 
 // Allocate `ncols` TMEM columns (power of two >= 32); the base address is
@@ -153,6 +166,16 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
          | (static_cast<uint64_t>(1024u >> 4) << 32)
          | (static_cast<uint64_t>(1u) << 46)
          | (static_cast<uint64_t>(2u) << 61);
+}
+
+// The same for the 64-byte swizzle (CU_TENSOR_MAP_SWIZZLE_64B): rows of 64
+// bytes, 8-row atoms 512 bytes apart, layout type 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t sw64_kmajor_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4)
+         | (static_cast<uint64_t>(1u) << 16)
+         | (static_cast<uint64_t>(512u >> 4) << 32)
+         | (static_cast<uint64_t>(1u) << 46)
+         | (static_cast<uint64_t>(4u) << 61);
 }
 
 // Instruction descriptor, kind::i8: signed A and B, int32 accumulator, both
