@@ -114,6 +114,59 @@ __device__ __forceinline__ void load_a(const EpiParams& p, const CUtensorMap* ta
     tma_load_4d(dst, ta, bar, cb * KBB, tx * p.conv_bw - p.conv_pad + kx, ty * p.conv_bh - p.conv_pad + ky, f);
 }
 
+// Phase B of the persistent epilogue for one 32-column chunk: lane (rq, cq)
+// finishes columns cq..cq+3 of tile rows rq + 4*r8 from the raw int32
+// accumulators in its warp's staging tile (rows kStgLd words apart):
+// v = fma(acc*s_w, s_a, b), then ReLU / residual add / add + ReLU, stores, and
+// the per-row |v| maximum for the absmax tap. MODE is the epilogue flag set
+// (-1: read it at run time); the 32 element computations are straight-line
+// code without per-row branches, so they interleave; only stores are predicated.
+constexpr int kStgLd = 36;   // words per staging row: 16-byte aligned, conflict-free per quarter warp
+
+template <int MODE, bool AMAX>
+__device__ __forceinline__ void epi_rows(const EpiParams& p, const float* stg, int rq, int cq, const int (&mrow)[8],
+                                         const float (&asr)[8], const float (&ws)[4], const float (&bb)[4],
+                                         const float4 (&rv)[8], int n, bool full4, float (&rmax)[8]) {
+    const int mode = MODE >= 0 ? MODE : p.mode;
+    float v[8][4];
+    #pragma unroll
+    for (int r8 = 0; r8 < 8; ++r8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(stg + (rq + 4 * r8) * kStgLd + cq);
+        const int32_t a4[4] = {static_cast<int32_t>(raw.x), static_cast<int32_t>(raw.y), static_cast<int32_t>(raw.z),
+                               static_cast<int32_t>(raw.w)};
+        const float* rvv = reinterpret_cast<const float*>(&rv[r8]);
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float t = __fmaf_rn(__fmul_rn(__int2float_rn(a4[e]), ws[e]), asr[r8], bb[e]);
+            if (mode & kEpiRelu) t = (t < 0.0f) ? 0.0f : t;            // tcpu::relu (eltwise.cpp:213-214)
+            if (mode & kEpiAdd) t = __fadd_rn(rvv[e], t);               // x[i] += y[i]
+            if (mode & kEpiAddRelu) {                                   // resnet_backbone.cpp:293-295
+                t = __fadd_rn(t, rvv[e]);
+                t = t > 0.0f ? t : 0.0f;
+            }
+            v[r8][e] = t;
+        }
+    }
+    #pragma unroll
+    for (int r8 = 0; r8 < 8; ++r8) {
+        const int m = mrow[r8];
+        const bool row_ok = m >= 0 && n < p.N;
+        if (AMAX) {
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) rmax[r8] = fmaxf(rmax[r8], (row_ok && n + e < p.N) ? fabsf(v[r8][e]) : 0.0f);
+        }
+        if (!row_ok) continue;
+        float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
+        if (p.vec_ok && full4) {
+            *reinterpret_cast<float4*>(o) = make_float4(v[r8][0], v[r8][1], v[r8][2], v[r8][3]);
+        } else {
+            #pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (n + e < p.N) o[e] = v[r8][e];
+        }
+    }
+}
+
 template <int KBB>
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
     if constexpr (KBB == 128) return sw128_kmajor_desc(saddr);
@@ -137,7 +190,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
     constexpr int kABytes = kBM * KBB;
     constexpr int kBBytes = BN * KBB;
     constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, BN);
-    constexpr int kStg = 32 * 33;   // floats: one epilogue warp's 32 x 32 staging tile, padded
+    constexpr int kStg = 32 * kStgLd;   // one epilogue warp's 32 x 32 staging tile
     constexpr int kEpiWarps = 8;
 
     extern __shared__ uint8_t smem_raw[];
@@ -245,12 +298,13 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
         __syncwarp();
     } else {
         // ---- epilogue (warps 2-9). Per 32-column chunk: phase A (thread = tile
-        // row, as TMEM hands it out) turns the accumulators into
-        // v = fma(acc*s_w, s_a, b) (or raw int32 bits) in this warp's staging
-        // tile; phase B (coalesced) - lane l covers columns 4*(l%8)..+3 of rows
-        // l/8 + 4i - adds the residual and stores, four whole 128-byte row
-        // segments per instruction. Column scales and biases reach the lanes by
-        // shuffle from one load per lane.
+        // row, as TMEM hands it out) parks the raw int32 accumulators in this
+        // warp's staging tile (16-byte stores, rows 36 words apart); phase B
+        // (coalesced) - lane l owns columns 4*(l%8)..+3 of rows l/8 + 4i -
+        // applies v = fma(acc*s_w, s_a, b), ReLU / residual, and stores four
+        // whole 128-byte row segments per instruction. A lane's 4 column scales
+        // and biases are one vector load per chunk, its 8 row scales one load
+        // each per tile: no shuffles.
         const int quarter = warp & 3;   // TMEM lanes this warp may read: 32 * (warp id % 4)
         const int half = (warp - 2) >> 2;   // which column chunks: c % 2 == half
         float* stg = stg_all + (warp - 2) * kStg;
@@ -278,129 +332,134 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 }
             }
         };
+        // column scales / biases of chunk c for this lane's 4 columns
+        auto load_cols = [&](float (&ws)[4], float (&bb)[4], int n0, int c) {
+            const int n = n0 + c * 32 + cq;
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const bool ok = c < BN / 32 && n + e < p.N;
+                ws[e] = ok ? p.wscale[n + e] : 0.0f;
+                bb[e] = (ok && p.bias) ? p.bias[n + e] : 0.0f;
+            }
+        };
         const bool has_res = (p.mode & (kEpiAdd | kEpiAddRelu)) != 0;
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int buf = i & 1;
             const int mt = t / n_tn, n0 = (t % n_tn) * BN;
-            const int m_row = out_row(p, mt, quarter * 32 + lane);     // phase A row (thread = row)
             int mrow[8];                                                // phase B rows of this lane
+            float asr[8];                                               // and their activation scales
             #pragma unroll
-            for (int r8 = 0; r8 < 8; ++r8) mrow[r8] = out_row(p, mt, quarter * 32 + rq + 4 * r8);
+            for (int r8 = 0; r8 < 8; ++r8) {
+                mrow[r8] = out_row(p, mt, quarter * 32 + rq + 4 * r8);
+                asr[r8] = (mrow[r8] >= 0 && !acc_mode) ? row_ascale(p, mrow[r8]) : 0.0f;
+            }
             // Everything the epilogue reads besides the accumulators is fetched
-            // before waiting for them, so its latency hides behind the MMAs:
-            // row scale, column scales / biases of every chunk, first residual.
+            // before waiting for them, so its latency hides behind the MMAs.
             // (Each lane later writes only elements it read here or reads
             // itself, so a residual aliasing out is never read after a store.)
-            const float as = m_row >= 0 ? row_ascale(p, m_row) : 0.0f;
-            float my_ws[kChunks], my_b[kChunks];
-            #pragma unroll
-            for (int ci = 0; ci < kChunks; ++ci) {
-                const int ncol = n0 + (half + 2 * ci) * 32 + lane;
-                const bool ok = half + 2 * ci < BN / 32 && ncol < p.N;
-                my_ws[ci] = ok ? p.wscale[ncol] : 0.0f;
-                my_b[ci] = (ok && p.bias) ? p.bias[ncol] : 0.0f;
-            }
+            float ws[4], bb[4];
+            if (!acc_mode) load_cols(ws, bb, n0, half);
             float4 rv[8];
             if (has_res && half < BN / 32) load_res(rv, mrow, n0, half);
-            // warp-uniform: the tcgen05.ld and shuffles below need every lane
+            // warp-uniform: the tcgen05.ld below needs every lane
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (i >> 1) & 1))) break;
             tc_fence_after();
-            float tmax = 0.0f;
+            float rmax[8];                                              // |out| per phase B row (absmax tap)
+            #pragma unroll
+            for (int r8 = 0; r8 < 8; ++r8) rmax[r8] = 0.0f;
             #pragma unroll
             for (int ci = 0; ci < kChunks; ++ci) {
                 const int c = half + 2 * ci;
                 if (c >= BN / 32) break;
+                if (n0 + c * 32 >= p.N) break;                          // warp-uniform; later chunks too
                 uint32_t acc[32];
                 tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, acc);
                 tmem_ld_wait();
-                if (n0 + c * 32 >= p.N) continue;            // warp-uniform
                 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float ws = __shfl_sync(0xFFFFFFFFu, my_ws[ci], j);
-                    const float bj = __shfl_sync(0xFFFFFFFFu, my_b[ci], j);
-                    float v;
-                    if (acc_mode) {
-                        v = __int_as_float(static_cast<int32_t>(acc[j]));
-                    } else {
-                        v = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), ws), as, bj);
-                        if (p.mode & kEpiRelu) v = (v < 0.0f) ? 0.0f : v;   // tcpu::relu (eltwise.cpp:213-214)
-                    }
-                    stg[lane * 33 + j] = v;
-                }
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<uint4*>(stg + lane * kStgLd + j) = make_uint4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
                 __syncwarp();
                 const int n = n0 + c * 32 + cq;
                 const bool full4 = n + 4 <= p.N;
-                // next chunk's residual goes out before this chunk's stores
+                // the next chunk's operands go out before this chunk's stores
                 // (different columns, so no aliasing hazard)
                 float4 rn[8];
-                if (has_res && ci + 1 < kChunks && c + 2 < BN / 32) load_res(rn, mrow, n0, c + 2);
-                #pragma unroll
-                for (int r8 = 0; r8 < 8; ++r8) {
-                    const int r = rq + 4 * r8;
-                    const int m = mrow[r8];
-                    if (m < 0 || n >= p.N) continue;
-                    float v[4] = {stg[r * 33 + cq], stg[r * 33 + cq + 1], stg[r * 33 + cq + 2], stg[r * 33 + cq + 3]};
-                    if (acc_mode) {
+                float wn[4], bn[4];
+                const bool more = ci + 1 < kChunks && c + 2 < BN / 32;
+                if (more && !acc_mode) load_cols(wn, bn, n0, c + 2);
+                if (more && has_res) load_res(rn, mrow, n0, c + 2);
+                // Straight-line over all 8 rows x 4 columns (no per-row
+                // branches, mode flags as selects): one basic block, so the 32
+                // independent element chains interleave; only the stores are
+                // predicated.
+                if (acc_mode) {
+                    #pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) {
+                        const uint4 raw = *reinterpret_cast<const uint4*>(stg + (rq + 4 * r8) * kStgLd + cq);
+                        const int m = mrow[r8];
+                        if (m < 0 || n >= p.N) continue;
+                        const uint32_t a4[4] = {raw.x, raw.y, raw.z, raw.w};
                         int32_t* o = static_cast<int32_t*>(p.out) + (long long)m * p.ldo + n;
                         #pragma unroll
                         for (int e = 0; e < 4; ++e)
-                            if (n + e < p.N) o[e] = __float_as_int(v[e]);
-                        continue;
+                            if (n + e < p.N) o[e] = static_cast<int32_t>(a4[e]);
                     }
+                } else {
+                    // mode and absmax tap as template flags: each instance
+                    // carries only its own operations (see epi_rows)
+                    const int mode = p.mode & (kEpiRelu | kEpiAdd | kEpiAddRelu);
+                    const bool am = p.amax != nullptr;
+                    #define VSB_EPI(M) (am ? epi_rows<M, true>(p, stg, rq, cq, mrow, asr, ws, bb, rv, n, full4, rmax) \
+                                           : epi_rows<M, false>(p, stg, rq, cq, mrow, asr, ws, bb, rv, n, full4, rmax))
+                    if (mode == 0) VSB_EPI(0);
+                    else if (mode == kEpiRelu) VSB_EPI(kEpiRelu);
+                    else if (mode == kEpiAdd) VSB_EPI(kEpiAdd);
+                    else if (mode == kEpiAddRelu) VSB_EPI(kEpiAddRelu);
+                    else VSB_EPI(-1);
+                    #undef VSB_EPI
+                }
+                if (more) {
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e) { ws[e] = wn[e]; bb[e] = bn[e]; }
                     if (has_res) {
-                        const float* rvv = reinterpret_cast<const float*>(&rv[r8]);
                         #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (p.mode & kEpiAdd) v[e] = __fadd_rn(rvv[e], v[e]);             // x[i] += y[i]
-                            if (p.mode & kEpiAddRelu) {                                         // resnet_backbone.cpp:293-295
-                                v[e] = __fadd_rn(v[e], rvv[e]);
-                                v[e] = v[e] > 0.0f ? v[e] : 0.0f;
-                            }
-                        }
-                        if (p.amax) {
-                            #pragma unroll
-                            for (int e = 0; e < 4; ++e) stg[r * 33 + cq + e] = v[e];
-                        }
-                    }
-                    float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
-                    if (p.vec_ok && full4) {
-                        *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
-                    } else {
-                        #pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            if (n + e < p.N) o[e] = v[e];
+                        for (int r8 = 0; r8 < 8; ++r8) rv[r8] = rn[r8];
                     }
                 }
-                if (has_res && ci + 1 < kChunks) {
-                    #pragma unroll
-                    for (int r8 = 0; r8 < 8; ++r8) rv[r8] = rn[r8];
-                }
-                if (p.amax) {
-                    // final values are back in the staging tile: per-row max, thread = row
-                    __syncwarp();
-                    #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (n0 + c * 32 + j < p.N) tmax = fmaxf(tmax, fabsf(stg[lane * 33 + j]));
-                }
-                __syncwarp();
+                __syncwarp();                                           // staging tile reused by the next chunk
             }
             // this tile's TMEM buffer may be reused by the MMA warp
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
             if (p.amax) {
-                // one atomic per warp when the warp's rows share a slot, else per row
-                const bool row_ok = m_row >= 0;
-                const unsigned key = row_ok ? static_cast<unsigned>(m_row / p.amax_rows) : 0xFFFFFFFFu;
-                const unsigned k0 = __shfl_sync(0xFFFFFFFFu, key, 0);
-                if (__all_sync(0xFFFFFFFFu, key == k0 || key == 0xFFFFFFFFu)) {
-                    float wm = row_ok ? tmax : 0.0f;    // rows past M hold bias-only values
+                // one atomic per warp when the warp's rows share a slot, else one
+                // per row (its 8 lanes reduced first); rows past M count nothing
+                unsigned key[8];
+                bool same = true;
+                const unsigned first = mrow[0] >= 0 ? static_cast<unsigned>(mrow[0] / p.amax_rows) : 0xFFFFFFFFu;
+                #pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8) {
+                    key[r8] = mrow[r8] >= 0 ? static_cast<unsigned>(mrow[r8] / p.amax_rows) : 0xFFFFFFFFu;
+                    same = same && (key[r8] == first || key[r8] == 0xFFFFFFFFu);
+                }
+                const unsigned k0 = __shfl_sync(0xFFFFFFFFu, first, 0);
+                if (__all_sync(0xFFFFFFFFu, same && (first == k0 || first == 0xFFFFFFFFu))) {
+                    float wm = 0.0f;
+                    #pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) wm = fmaxf(wm, rmax[r8]);
                     #pragma unroll
                     for (int off = 16; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
                     if (lane == 0 && k0 != 0xFFFFFFFFu) atomicMax(&p.amax[k0], __float_as_uint(wm));
-                } else if (row_ok) {
-                    atomicMax(&p.amax[key], __float_as_uint(tmax));
+                } else {
+                    #pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) {
+                        float wm = rmax[r8];
+                        #pragma unroll
+                        for (int off = 4; off > 0; off >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xFFFFFFFFu, wm, off));
+                        if ((lane & 7) == 0 && key[r8] != 0xFFFFFFFFu) atomicMax(&p.amax[key[r8]], __float_as_uint(wm));
+                    }
                 }
             }
         }
@@ -753,7 +812,7 @@ bool make_tmap_i8_kmajor_kb(CUtensorMap* map, const void* base, int rows, int K,
 constexpr size_t kMaxDynSmem = 227 * 1024;   // per-CTA dynamic shared memory limit (sm_100)
 
 constexpr size_t umma_smem_bytes(int bn, int stages, int kbb = kBK) {
-    return 1024 + (size_t)stages * (kBM * kbb + bn * kbb) + 8 * 32 * 33 * 4 + (2 * stages + 4) * 8 + 16;
+    return 1024 + (size_t)stages * (kBM * kbb + bn * kbb) + 8 * 32 * 36 * 4 + (2 * stages + 4) * 8 + 16;
 }
 
 constexpr size_t splitk_smem_bytes(int bn, int stages) {

@@ -25,10 +25,12 @@ __device__ __forceinline__ float nn_row_scale(float amax) {
 }
 
 __device__ __forceinline__ int8_t nn_q8(float v, float inv) {
-    int r = __float2int_rn(__fmul_rn(v, inv));
-    r = r > 127 ? 127 : r;
-    r = r < -127 ? -127 : r;
-    return static_cast<int8_t>(r);
+    // round, then clamp to +-127; the same as clamping in fp32 first (x.5 at
+    // the edge rounds outward either way), which keeps the rounding in the
+    // exact small-range form. NaN quantizes to 0 as a plain conversion would.
+    float t = __fmul_rn(v, inv);
+    t = t != t ? 0.0f : fminf(fmaxf(t, -127.0f), 127.0f);
+    return static_cast<int8_t>(f2i_rn_small(t));
 }
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -982,7 +984,7 @@ __global__ void normalize_frames_kernel(const uint8_t* __restrict__ img, float* 
     for (int px = blockIdx.x * blockDim.x + threadIdx.x; px < npx; px += gridDim.x * blockDim.x) {
         #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            const float p = __fdiv_rn((float)src[3 * px + c], 255.0f);
+            const float p = __fdiv_rn(i2f_small(src[3 * px + c]), 255.0f);
             const float v = __fdiv_rn(__fsub_rn(p, mu[c]), den[c]);
             dst[3 * px + c] = v;
             bmax = fmaxf(bmax, fabsf(v));

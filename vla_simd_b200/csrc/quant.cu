@@ -25,10 +25,12 @@ __device__ __forceinline__ float row_scale(float amax) {
 }
 
 __device__ __forceinline__ int8_t q8(float v, float inv) {
-    int r = __float2int_rn(__fmul_rn(v, inv));
-    r = r > 127 ? 127 : r;
-    r = r < -127 ? -127 : r;
-    return static_cast<int8_t>(r);
+    // round, then clamp to +-127; the same as clamping in fp32 first (x.5 at
+    // the edge rounds outward either way), which keeps the rounding in the
+    // exact small-range form. NaN quantizes to 0 as a plain conversion would.
+    float t = __fmul_rn(v, inv);
+    t = t != t ? 0.0f : fminf(fmaxf(t, -127.0f), 127.0f);
+    return static_cast<int8_t>(f2i_rn_small(t));
 }
 
 // fp32 clamp first, then round: quantize_span_i8 (src/hal/common/gemm_i8.cpp:177-207),
@@ -36,7 +38,7 @@ __device__ __forceinline__ int8_t q8(float v, float inv) {
 __device__ __forceinline__ int8_t q8_span(float v, float inv) {
     float t = __fmul_rn(v, inv);
     t = fminf(fmaxf(t, -127.0f), 127.0f);
-    return static_cast<int8_t>(__float2int_rn(t));
+    return static_cast<int8_t>(f2i_rn_small(t));
 }
 
 // One warp per row (two rows per 64-thread block). x [M][ldx] (+ optional

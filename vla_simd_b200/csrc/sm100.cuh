@@ -41,6 +41,24 @@ __device__ __forceinline__ void record_status(int code) {
     atomicCAS(&g_vsb_status, 0, code);
 }
 
+// ------------------------------------------------------- exact conversions
+// Small-range int <-> float conversions as two fma-pipe / integer operations
+// instead of the conversion unit (the int8 quantizers round every element).
+// Both are exact: adding 1.5 * 2^23 to a float rounds it to the nearest (even)
+// integer, and an integer placed in the low mantissa bits of 1.5 * 2^23 reads
+// back exactly.
+constexpr float kRoundConst = 12582912.0f;   // 1.5 * 2^23, bits 0x4B400000
+
+// round-to-nearest-even float -> int, for |x| <= 2^22 (callers clamp first)
+__device__ __forceinline__ int f2i_rn_small(float x) {
+    return __float_as_int(__fadd_rn(x, kRoundConst)) - 0x4B400000;
+}
+
+// small non-negative or signed int (|x| < 2^22) -> float, exact
+__device__ __forceinline__ float i2f_small(int x) {
+    return __fsub_rn(__int_as_float(x + 0x4B400000), kRoundConst);
+}
+
 // ------------------------------------------------ programmatic dependent launch
 // Every kernel of the library is launched with programmatic stream
 // serialization (launch.cuh): it may start while the previous kernel in the
