@@ -258,6 +258,54 @@ def time_gemm(torch, dev, n_cold=30, n_warm_graph=50, n_lin=10):
             "dense_linear_i8_us_cold": statistics.median(lin) * 1e6}
 
 
+def run_gemm_msweep():
+    """The W8A8 GEMM at the FFN shape for M = 602 x {1, 8, 32, 128} (batched
+    policies), back-to-back launches in a CUDA graph. Per M: time per call,
+    int8 TOPS against the measured tensor peak, and the compulsory-bytes
+    roofline (int8 A and W, fp32 out, scales) against measured HBM bandwidth."""
+    import torch
+    from vla_simd_b200 import ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    N, K = GEMM_SHAPE[1], GEMM_SHAPE[2]
+    bf16_peak, hbm, peak_kind = _peaks()
+    peak_tops = 2.0 * bf16_peak
+    st = torch.cuda.Stream()
+    for mult in (1, 8, 32, 128):
+        M = GEMM_SHAPE[0] * mult
+        g = torch.Generator(device="cpu").manual_seed(M)
+        xq = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g).to(dev)
+        wq = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g).to(dev)
+        xs, ws = torch.rand(M, device=dev) * 1e-3, torch.rand(N, device=dev) * 1e-3
+        b, out = torch.rand(N, device=dev), torch.empty(M, N, device=dev)
+        with torch.cuda.stream(st):
+            ops.gemm_i8(xq, xs, wq, ws, K, bias=b, out=out)
+        torch.cuda.synchronize()
+        reps = max(4, 200 // mult)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            for _ in range(reps):
+                ops.gemm_i8(xq, xs, wq, ws, K, bias=b, out=out)
+        ts = []
+        for r in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(st):
+                e0.record(st)
+                gr.replay()
+                e1.record(st)
+            torch.cuda.synchronize()
+            if r:
+                ts.append(e0.elapsed_time(e1) * 1e-3 / reps)
+        del gr
+        t = statistics.median(ts)
+        ops_ = 2.0 * M * N * K
+        nbytes = M * K + N * K + 4.0 * M * N + 4.0 * (M + 2 * N)
+        print(json.dumps({"op": "gemm_i8", "M": M, "N": N, "K": K, "us_per_call": round(t * 1e6, 2),
+                          "tops": round(ops_ / t / 1e12, 1), "tensor_frac": round(ops_ / t / 1e12 / peak_tops, 4),
+                          "hbm_gbs_compulsory": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4),
+                          "peak_source": peak_kind}), flush=True)
+
+
 def run_op(name: str, iters: int = 20):
     """One op at its ACT-step shape, timed alone (also the small cases ncu captures use)."""
     import torch
@@ -267,6 +315,8 @@ def run_op(name: str, iters: int = 20):
     g = torch.Generator(device="cpu").manual_seed(0)
     rnd = lambda *sh, s=1.0: (torch.randn(*sh, generator=g) * s).to(dev)  # noqa: E731
     T, d, ff = 602, 512, 3200
+    if name == "gemm_msweep":
+        return run_gemm_msweep()
     if name == "attention":
         qk, v = rnd(T, 2 * d), rnd(T, d)
         fn = lambda: ops.gqa_attention(qk[:, :d], qk[:, d:], v, 8, 8, 0.125)  # noqa: E731
@@ -458,7 +508,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default=None, help="time one op at its ACT shape (attention, gemm_qkv, gemm_w1, "
-                                               "gemm_w2, layernorm, quantize, conv_layer1)")
+                                               "gemm_w2, layernorm, quantize, conv_layer1), or gemm_msweep "
+                                               "(the FFN GEMM at M = 602 x {1, 8, 32, 128})")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
     args = ap.parse_args()

@@ -121,9 +121,11 @@ __device__ __forceinline__ void load_a(const EpiParams& p, const CUtensorMap* ta
 // the per-row |v| maximum for the absmax tap. MODE is the epilogue flag set
 // (-1: read it at run time); the 32 element computations are straight-line
 // code without per-row branches, so they interleave; only stores are predicated.
+// Five instances in all (one per mode): the absmax upkeep is a uniform branch,
+// not a template flag, to keep the kernel's code within the instruction cache.
 constexpr int kStgLd = 36;   // words per staging row: 16-byte aligned, conflict-free per quarter warp
 
-template <int MODE, bool AMAX>
+template <int MODE>
 __device__ __forceinline__ void epi_rows(const EpiParams& p, const float* stg, int rq, int cq, const int (&mrow)[8],
                                          const float (&asr)[8], const float (&ws)[4], const float (&bb)[4],
                                          const float4 (&rv)[8], int n, bool full4, float (&rmax)[8]) {
@@ -147,14 +149,18 @@ __device__ __forceinline__ void epi_rows(const EpiParams& p, const float* stg, i
             v[r8][e] = t;
         }
     }
+    if (p.amax) {
+        #pragma unroll
+        for (int r8 = 0; r8 < 8; ++r8) {
+            const bool row_ok = mrow[r8] >= 0 && n < p.N;
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) rmax[r8] = fmaxf(rmax[r8], (row_ok && n + e < p.N) ? fabsf(v[r8][e]) : 0.0f);
+        }
+    }
     #pragma unroll
     for (int r8 = 0; r8 < 8; ++r8) {
         const int m = mrow[r8];
         const bool row_ok = m >= 0 && n < p.N;
-        if (AMAX) {
-            #pragma unroll
-            for (int e = 0; e < 4; ++e) rmax[r8] = fmaxf(rmax[r8], (row_ok && n + e < p.N) ? fabsf(v[r8][e]) : 0.0f);
-        }
         if (!row_ok) continue;
         float* o = static_cast<float*>(p.out) + (long long)m * p.ldo + n;
         if (p.vec_ok && full4) {
@@ -368,8 +374,8 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             float rmax[8];                                              // |out| per phase B row (absmax tap)
             #pragma unroll
             for (int r8 = 0; r8 < 8; ++r8) rmax[r8] = 0.0f;
-            #pragma unroll
-            for (int ci = 0; ci < kChunks; ++ci) {
+            #pragma unroll 1
+            for (int ci = 0; ci < kChunks; ++ci) {                      // rolled: one copy of the chunk code
                 const int c = half + 2 * ci;
                 if (c >= BN / 32) break;
                 if (n0 + c * 32 >= p.N) break;                          // warp-uniform; later chunks too
@@ -406,12 +412,10 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
                             if (n + e < p.N) o[e] = static_cast<int32_t>(a4[e]);
                     }
                 } else {
-                    // mode and absmax tap as template flags: each instance
-                    // carries only its own operations (see epi_rows)
+                    // the mode as a template flag: each instance carries only
+                    // its own operations (see epi_rows)
                     const int mode = p.mode & (kEpiRelu | kEpiAdd | kEpiAddRelu);
-                    const bool am = p.amax != nullptr;
-                    #define VSB_EPI(M) (am ? epi_rows<M, true>(p, stg, rq, cq, mrow, asr, ws, bb, rv, n, full4, rmax) \
-                                           : epi_rows<M, false>(p, stg, rq, cq, mrow, asr, ws, bb, rv, n, full4, rmax))
+                    #define VSB_EPI(M) epi_rows<M>(p, stg, rq, cq, mrow, asr, ws, bb, rv, n, full4, rmax)
                     if (mode == 0) VSB_EPI(0);
                     else if (mode == kEpiRelu) VSB_EPI(kEpiRelu);
                     else if (mode == kEpiAdd) VSB_EPI(kEpiAdd);
