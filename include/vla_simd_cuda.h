@@ -137,6 +137,56 @@ VLA_API int32_t vla_cuda_dense_linear_f32(float* out, const float* x, const floa
 VLA_API int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H, int32_t W,
                                         int32_t C, int32_t k, int32_t stride, int32_t pad, void* stream);
 
+/* ---------------- lm / conv ops of the other policy families (device pointers)
+ * The reference's formulas in its order (see the notes per op): bit-identical
+ * where it is deterministic fp arithmetic, within its own tests' tolerances
+ * where it calls libm. */
+
+/* replaces tcpu::rmsnorm (src/ops/lm_ops.h:21; src/hal/common/norms.cpp:19-35):
+ * x, out [seq][hidden], w [hidden]; hidden <= 6144. Bit-identical. */
+VLA_API int32_t vla_cuda_rmsnorm(float* out, const float* x, const float* w, int32_t seq, int32_t hidden,
+                                 float eps, void* stream);
+
+/* replaces tcpu::rope_neox (src/ops/lm_ops.h:26; norms.cpp:37-67), in place:
+ * x [seq][n_heads][head_dim], pos [seq] int32 (device). Double trig. */
+VLA_API int32_t vla_cuda_rope_neox(float* x, const int32_t* pos, int32_t seq, int32_t n_heads,
+                                   int32_t head_dim, float base, void* stream);
+
+/* replace tcpu::silu_gate / silu / gelu_tanh / gelu_erf / relu / mish
+ * (src/ops/lm_ops.h:55-79; src/hal/common/eltwise.cpp): the reference's SIMD
+ * bodies with its Cephes exp for every element. out may alias x (in place). */
+VLA_API int32_t vla_cuda_silu_gate(float* out, const float* g, const float* u, int64_t n, void* stream);
+VLA_API int32_t vla_cuda_silu(float* out, const float* x, int64_t n, void* stream);
+VLA_API int32_t vla_cuda_gelu_tanh(float* out, const float* x, int64_t n, void* stream);
+VLA_API int32_t vla_cuda_gelu_erf(float* out, const float* x, int64_t n, void* stream);
+VLA_API int32_t vla_cuda_relu(float* out, const float* x, int64_t n, void* stream);
+VLA_API int32_t vla_cuda_mish(float* out, const float* x, int64_t n, void* stream);
+
+/* replaces tcpu::groupnorm (src/ops/conv_ops.h:91; src/hal/common/conv.cpp:227-318):
+ * x, out [n_pixels][C] (channels last), scale/bias [C], C % groups == 0.
+ * scratch: vla_cuda_groupnorm_scratch_bytes(C) caller-owned device bytes, 8-byte aligned. */
+VLA_API uint64_t vla_cuda_groupnorm_scratch_bytes(int32_t C);
+VLA_API int32_t vla_cuda_groupnorm(float* out, const float* x, const float* scale, const float* bias,
+                                   int32_t n_pixels, int32_t C, int32_t groups, float eps, int32_t fuse_relu,
+                                   void* scratch, void* stream);
+
+/* replaces tcpu::spatial_softmax (src/ops/conv_ops.h:83; conv.cpp:397-422):
+ * x [n_pixels][C], grid [n_pixels][2] -> out [C][2] expected coordinates. */
+VLA_API int32_t vla_cuda_spatial_softmax(float* out, const float* x, const float* grid, int32_t n_pixels,
+                                         int32_t C, void* stream);
+
+/* replaces tcpu::im2col1d (src/ops/conv_ops.h:65; conv.cpp:334-347):
+ * x [T][Cin] -> col [Tout][k*Cin] (caller-owned). */
+VLA_API int32_t vla_cuda_im2col1d(float* col, const float* x, int32_t T, int32_t Cin, int32_t k,
+                                  int32_t stride, int32_t pad, int32_t Tout, void* stream);
+
+/* replaces tcpu::conv_transpose1d (src/ops/conv_ops.h:74; conv.cpp:349-395):
+ * x [T][Cin], W [Cin][k][Cout], bias [Cout] or NULL -> out [(T-1)*stride-2*pad+k][Cout].
+ * Bit-identical (the reference's accumulation order per output). */
+VLA_API int32_t vla_cuda_conv_transpose1d(float* out, const float* x, const float* W, const float* bias,
+                                          int32_t T, int32_t Cin, int32_t Cout, int32_t k, int32_t stride,
+                                          int32_t pad, void* stream);
+
 /* ------------------------------------------------ host-pointer tcpu shims */
 
 VLA_API int32_t vla_tcpu_int8_gemm_available(void);          /* src/ops/quant_ops.h:41 */

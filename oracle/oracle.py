@@ -132,6 +132,15 @@ class Reference:
         l.ref_maxpool2d_relu.argtypes = [VP, VP, I32, I32, I32, I32, I32, I32]
         l.ref_relu.argtypes = [VP, I32]
         l.ref_dense_linear.argtypes = [VP, VP, VP, VP, I32, I32, I32]
+        l.ref_rmsnorm.argtypes = [VP, VP, VP, I32, I32, F32]
+        l.ref_rope_neox.argtypes = [VP, VP, I32, I32, I32, F32]
+        l.ref_silu_gate.argtypes = [VP, VP, VP, I32]
+        for n in ("silu", "gelu_tanh", "gelu_erf", "mish"):
+            getattr(l, f"ref_{n}").argtypes = [VP, I32]
+        l.ref_groupnorm.argtypes = [VP, VP, VP, VP, I32, I32, I32, F32, I32]
+        l.ref_spatial_softmax.argtypes = [VP, VP, VP, I32, I32]
+        l.ref_im2col1d.argtypes = [VP, VP, I32, I32, I32, I32, I32, I32]
+        l.ref_conv_transpose1d.argtypes = [VP, VP, VP, VP, I32, I32, I32, I32, I32, I32]
         l.vla_act_load.restype = VP
         l.vla_act_load.argtypes = [ctypes.c_char_p]
         l.vla_act_free.argtypes = [VP]
@@ -216,6 +225,61 @@ class Reference:
         N = W.shape[0]
         out = np.zeros((seq, N), np.float32)
         self.l.ref_dense_linear(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(W, np.float32)), _ptr(b), seq, N, K)
+        return out
+
+    # --- lm / conv ops of the other policy families (src/ops/lm_ops.h, conv_ops.h)
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        self.l.ref_rmsnorm(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), x.shape[0], x.shape[1], eps)
+        return out
+
+    def rope_neox(self, x, pos, n_heads, head_dim, base):
+        x = np.array(x, np.float32, copy=True, order="C")
+        pos = np.ascontiguousarray(pos, np.int32)
+        self.l.ref_rope_neox(_ptr(x), _ptr(pos), x.shape[0], n_heads, head_dim, base)
+        return x
+
+    def activation(self, name, x, u=None):
+        x = np.array(x, np.float32, copy=True, order="C").ravel()
+        if name == "silu_gate":
+            out = np.zeros_like(x)
+            self.l.ref_silu_gate(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(u, np.float32).ravel()), x.size)
+            return out
+        getattr(self.l, f"ref_{name}")(_ptr(x), x.size)
+        return x
+
+    def groupnorm(self, x, scale, bias, groups, eps, fuse_relu=False):
+        x = np.ascontiguousarray(x, np.float32)
+        P, C = x.shape
+        out = np.zeros_like(x)
+        self.l.ref_groupnorm(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(scale, np.float32)),
+                             _ptr(np.ascontiguousarray(bias, np.float32)), P, C, groups, eps, 1 if fuse_relu else 0)
+        return out
+
+    def spatial_softmax(self, x, grid):
+        x = np.ascontiguousarray(x, np.float32)
+        P, C = x.shape
+        out = np.zeros((C, 2), np.float32)
+        self.l.ref_spatial_softmax(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(grid, np.float32)), P, C)
+        return out
+
+    def im2col1d(self, x, k, stride, pad):
+        x = np.ascontiguousarray(x, np.float32)
+        T, Cin = x.shape
+        Tout = (T + 2 * pad - k) // stride + 1
+        col = np.zeros((Tout, k * Cin), np.float32)
+        self.l.ref_im2col1d(_ptr(col), _ptr(x), T, Cin, k, stride, pad, Tout)
+        return col
+
+    def conv_transpose1d(self, x, W, b, k, stride, pad):
+        x = np.ascontiguousarray(x, np.float32)
+        T, Cin = x.shape
+        Cout = W.shape[-1]
+        Tout = (T - 1) * stride - 2 * pad + k
+        out = np.zeros((Tout, Cout), np.float32)
+        self.l.ref_conv_transpose1d(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(W, np.float32)),
+                                    _ptr(b) if b is not None else None, T, Cin, Cout, k, stride, pad)
         return out
 
     # --- policy level (the reference's own vla_act_* ABI)

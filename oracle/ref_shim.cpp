@@ -58,4 +58,35 @@ void ref_dense_linear(float* out, const float* x, const float* W, const float* b
     tcpu::dense_linear(out, x, W, bias, seq, N, K);
 }
 
+// lm_ops.h norms / positional / activations
+void ref_rmsnorm(float* out, const float* x, const float* w, int seq, int hidden, float eps) {
+    tcpu::rmsnorm(out, x, w, seq, hidden, eps);
+}
+void ref_rope_neox(float* x, const int* pos, int seq, int n_heads, int head_dim, float base) {
+    tcpu::rope_neox(x, pos, seq, n_heads, head_dim, base);
+}
+void ref_silu_gate(float* out, const float* g, const float* u, int n) { tcpu::silu_gate(out, g, u, n); }
+void ref_silu(float* x, int n) { tcpu::silu(x, n); }
+void ref_gelu_tanh(float* x, int n) { tcpu::gelu_tanh(x, n); }
+void ref_gelu_erf(float* x, int n) { tcpu::gelu_erf(x, n); }
+void ref_mish(float* x, int n) { tcpu::mish(x, n); }
+
+// conv_ops.h 1D / diffusion-policy ops
+void ref_groupnorm(float* out, const float* x, const float* scale, const float* bias, int n_pixels, int C,
+                   int groups, float eps, int fuse_relu) {
+    tcpu::groupnorm(out, x, scale, bias, n_pixels, C, groups, eps, fuse_relu != 0);
+}
+void ref_spatial_softmax(float* out, const float* x, const float* grid, int n_pixels, int C) {
+    tcpu::spatial_softmax(out, x, grid, n_pixels, C);
+}
+void ref_im2col1d(float* col, const float* x, int T, int Cin, int k, int stride, int pad, int Tout) {
+    std::vector<float> v;
+    tcpu::im2col1d(v, x, T, Cin, k, stride, pad, Tout);
+    for (size_t i = 0; i < (size_t)Tout * k * Cin; ++i) col[i] = v[i];
+}
+void ref_conv_transpose1d(float* out, const float* x, const float* W, const float* bias, int T, int Cin, int Cout,
+                          int k, int stride, int pad) {
+    tcpu::conv_transpose1d(out, x, W, bias, T, Cin, Cout, k, stride, pad);
+}
+
 }  // extern "C"

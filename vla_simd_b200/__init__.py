@@ -66,6 +66,19 @@ SIGNATURES = {
     "vla_cuda_layernorm": (I32, [VP, VP, VP, VP, I32, I32, F32, VP]),
     "vla_cuda_gqa_attention": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP, VP]),
     "vla_cuda_maxpool2d_relu": (I32, [VP, VP, I32, I32, I32, I32, I32, I32, I32, VP]),
+    "vla_cuda_rmsnorm": (I32, [VP, VP, VP, I32, I32, F32, VP]),
+    "vla_cuda_rope_neox": (I32, [VP, VP, I32, I32, I32, F32, VP]),
+    "vla_cuda_silu_gate": (I32, [VP, VP, VP, I64, VP]),
+    "vla_cuda_silu": (I32, [VP, VP, I64, VP]),
+    "vla_cuda_gelu_tanh": (I32, [VP, VP, I64, VP]),
+    "vla_cuda_gelu_erf": (I32, [VP, VP, I64, VP]),
+    "vla_cuda_relu": (I32, [VP, VP, I64, VP]),
+    "vla_cuda_mish": (I32, [VP, VP, I64, VP]),
+    "vla_cuda_groupnorm_scratch_bytes": (ctypes.c_uint64, [I32]),
+    "vla_cuda_groupnorm": (I32, [VP, VP, VP, VP, I32, I32, I32, F32, I32, VP, VP]),
+    "vla_cuda_spatial_softmax": (I32, [VP, VP, VP, I32, I32, VP]),
+    "vla_cuda_im2col1d": (I32, [VP, VP, I32, I32, I32, I32, I32, I32, VP]),
+    "vla_cuda_conv_transpose1d": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, VP]),
     "vla_cuda_dense_linear_f32": (I32, [VP, VP, VP, VP, I32, I32, I32, VP]),
     "vla_tcpu_int8_gemm_available": (I32, []),
     "vla_tcpu_i8_kpad": (I32, [I32]),

@@ -7,6 +7,7 @@
 #include "act_policy.h"
 #include "gemm_i8.h"
 #include "host_quant.h"
+#include "lm_ops.h"
 #include "nn.h"
 #include "quant.h"
 
@@ -293,6 +294,74 @@ int32_t vla_cuda_maxpool2d_relu(float* out, const float* x, int32_t F, int32_t H
     const int Ho = (H + 2 * pad - k) / stride + 1, Wo = (W + 2 * pad - k) / stride + 1;
     if (Ho <= 0 || Wo <= 0) return VLA_ERR_ARG;
     return status_of(vsb::maxpool_relu(x, out, F, H, W, C, k, stride, pad, Ho, Wo, nullptr, as_stream(stream)));
+}
+
+// ------------------------------------------- lm / conv ops (other policies)
+
+int32_t vla_cuda_rmsnorm(float* out, const float* x, const float* w, int32_t seq, int32_t hidden, float eps,
+                         void* stream) {
+    if (!out || !x || !w || seq <= 0 || hidden <= 0 || hidden > 6144) return VLA_ERR_ARG;
+    return status_of(vsb::rmsnorm(x, w, out, seq, hidden, eps, as_stream(stream)));
+}
+
+int32_t vla_cuda_rope_neox(float* x, const int32_t* pos, int32_t seq, int32_t n_heads, int32_t head_dim, float base,
+                           void* stream) {
+    if (!x || !pos || seq <= 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2) return VLA_ERR_ARG;
+    return status_of(vsb::rope_neox(x, pos, seq, n_heads, head_dim, base, as_stream(stream)));
+}
+
+static int32_t act_call(int kind, float* out, const float* x, const float* u, int64_t n, void* stream) {
+    if (!out || !x || n <= 0) return VLA_ERR_ARG;
+    return status_of(vsb::activation(kind, out, x, u, n, as_stream(stream)));
+}
+int32_t vla_cuda_silu_gate(float* out, const float* g, const float* u, int64_t n, void* stream) {
+    if (!u) return VLA_ERR_ARG;
+    return act_call(vsb::kActSiluGate, out, g, u, n, stream);
+}
+int32_t vla_cuda_silu(float* out, const float* x, int64_t n, void* stream) {
+    return act_call(vsb::kActSilu, out, x, nullptr, n, stream);
+}
+int32_t vla_cuda_gelu_tanh(float* out, const float* x, int64_t n, void* stream) {
+    return act_call(vsb::kActGeluTanh, out, x, nullptr, n, stream);
+}
+int32_t vla_cuda_gelu_erf(float* out, const float* x, int64_t n, void* stream) {
+    return act_call(vsb::kActGeluErf, out, x, nullptr, n, stream);
+}
+int32_t vla_cuda_relu(float* out, const float* x, int64_t n, void* stream) {
+    return act_call(vsb::kActRelu, out, x, nullptr, n, stream);
+}
+int32_t vla_cuda_mish(float* out, const float* x, int64_t n, void* stream) {
+    return act_call(vsb::kActMish, out, x, nullptr, n, stream);
+}
+
+uint64_t vla_cuda_groupnorm_scratch_bytes(int32_t C) { return C > 0 ? vsb::groupnorm_scratch_bytes(C) : 0; }
+
+int32_t vla_cuda_groupnorm(float* out, const float* x, const float* scale, const float* bias, int32_t n_pixels,
+                           int32_t C, int32_t groups, float eps, int32_t fuse_relu, void* scratch, void* stream) {
+    if (!out || !x || !scale || !bias || !scratch || n_pixels <= 0 || C <= 0 || groups <= 0 || C % groups)
+        return VLA_ERR_ARG;
+    return status_of(vsb::groupnorm(x, scale, bias, out, n_pixels, C, groups, eps, fuse_relu != 0, scratch,
+                                    as_stream(stream)));
+}
+
+int32_t vla_cuda_spatial_softmax(float* out, const float* x, const float* grid, int32_t n_pixels, int32_t C,
+                                 void* stream) {
+    if (!out || !x || !grid || n_pixels <= 0 || C <= 0) return VLA_ERR_ARG;
+    return status_of(vsb::spatial_softmax(x, grid, out, n_pixels, C, as_stream(stream)));
+}
+
+int32_t vla_cuda_im2col1d(float* col, const float* x, int32_t T, int32_t Cin, int32_t k, int32_t stride, int32_t pad,
+                          int32_t Tout, void* stream) {
+    if (!col || !x || T <= 0 || Cin <= 0 || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0) return VLA_ERR_ARG;
+    return status_of(vsb::im2col1d(x, col, T, Cin, k, stride, pad, Tout, as_stream(stream)));
+}
+
+int32_t vla_cuda_conv_transpose1d(float* out, const float* x, const float* W, const float* bias, int32_t T,
+                                  int32_t Cin, int32_t Cout, int32_t k, int32_t stride, int32_t pad, void* stream) {
+    if (!out || !x || !W || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || stride <= 0 || pad < 0 ||
+        (T - 1) * stride - 2 * pad + k <= 0)
+        return VLA_ERR_ARG;
+    return status_of(vsb::conv_transpose1d(x, W, bias, out, T, Cin, Cout, k, stride, pad, as_stream(stream)));
 }
 
 // ------------------------------------------------------ host-pointer shims

@@ -5,3 +5,4 @@
 #include "quant.cu"
 #include "nn.cu"
 #include "f32.cu"
+#include "lm_ops.cu"

@@ -122,5 +122,77 @@ def dense_linear_f32(x, W, bias=None):
     return out
 
 
+# ---- lm / conv ops of the other policy families (src/ops/lm_ops.h, conv_ops.h)
+
+def rmsnorm(x, w, eps=1e-6):
+    """tcpu::rmsnorm: sequential double sum of squares per row."""
+    seq, hidden = x.shape
+    out = torch.empty_like(x)
+    check(lib().vla_cuda_rmsnorm(_p(out), _p(x.contiguous()), _p(w.contiguous()), seq, hidden, eps, _stream()),
+          "vla_cuda_rmsnorm")
+    return out
+
+
+def rope_neox(x, pos, n_heads, head_dim, base=10000.0):
+    """tcpu::rope_neox on a copy of x [seq, n_heads*head_dim]; pos int32 [seq]."""
+    y = x.contiguous().clone()
+    check(lib().vla_cuda_rope_neox(_p(y), _p(pos.to(torch.int32).contiguous()), y.shape[0], n_heads, head_dim, base,
+                                   _stream()), "vla_cuda_rope_neox")
+    return y
+
+
+def activation(name, x, u=None):
+    """tcpu::{silu_gate, silu, gelu_tanh, gelu_erf, relu, mish}; returns a new tensor."""
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    fn = getattr(lib(), f"vla_cuda_{name}")
+    if name == "silu_gate":
+        rc = fn(_p(out), _p(x), _p(u.contiguous()), x.numel(), _stream())
+    else:
+        rc = fn(_p(out), _p(x), x.numel(), _stream())
+    check(rc, f"vla_cuda_{name}")
+    return out
+
+
+def groupnorm(x, scale, bias, groups, eps=1e-5, fuse_relu=False):
+    """tcpu::groupnorm over x [n_pixels, C] (channels last)."""
+    P, C = x.shape
+    out = torch.empty_like(x)
+    scratch = torch.empty(int(lib().vla_cuda_groupnorm_scratch_bytes(C)), dtype=torch.uint8, device=x.device)
+    check(lib().vla_cuda_groupnorm(_p(out), _p(x.contiguous()), _p(scale.contiguous()), _p(bias.contiguous()), P, C,
+                                   groups, eps, 1 if fuse_relu else 0, _p(scratch), _stream()), "vla_cuda_groupnorm")
+    return out
+
+
+def spatial_softmax(x, grid):
+    """tcpu::spatial_softmax: x [n_pixels, C], grid [n_pixels, 2] -> [C, 2]."""
+    P, C = x.shape
+    out = torch.empty((C, 2), dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_spatial_softmax(_p(out), _p(x.contiguous()), _p(grid.contiguous()), P, C, _stream()),
+          "vla_cuda_spatial_softmax")
+    return out
+
+
+def im2col1d(x, k, stride, pad):
+    """tcpu::im2col1d: x [T, Cin] -> [Tout, k*Cin]."""
+    T, Cin = x.shape
+    Tout = (T + 2 * pad - k) // stride + 1
+    col = torch.empty((Tout, k * Cin), dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_im2col1d(_p(col), _p(x.contiguous()), T, Cin, k, stride, pad, Tout, _stream()),
+          "vla_cuda_im2col1d")
+    return col
+
+
+def conv_transpose1d(x, W, bias, k, stride, pad):
+    """tcpu::conv_transpose1d: x [T, Cin], W [Cin, k, Cout] -> [(T-1)*stride-2*pad+k, Cout]."""
+    T, Cin = x.shape
+    Cout = W.shape[-1]
+    Tout = (T - 1) * stride - 2 * pad + k
+    out = torch.empty((Tout, Cout), dtype=torch.float32, device=x.device)
+    check(lib().vla_cuda_conv_transpose1d(_p(out), _p(x.contiguous()), _p(W.contiguous()), _p(bias), T, Cin, Cout, k,
+                                          stride, pad, _stream()), "vla_cuda_conv_transpose1d")
+    return out
+
+
 def device_status() -> int:
     return int(lib().vla_cuda_device_status())
