@@ -59,7 +59,10 @@ quantize_rows_kernel(const float* __restrict__ x, long long ldx, const float* __
     const float* xr = x + (long long)row * ldx;
     const float* ar = addend ? addend + (long long)row * lda_ : nullptr;
     float m1 = 0.0f, m2 = 0.0f;
+    // unrolled so several rows' loads are in flight (a 3200-wide row is 25
+    // vector loads per lane)
     if (VEC) {
+        #pragma unroll 8
         for (int k = 4 * lane; k < K; k += 128) {
             const float4 v = *reinterpret_cast<const float4*>(xr + k);
             m2 = fmaxf(m2, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
@@ -87,6 +90,7 @@ quantize_rows_kernel(const float* __restrict__ x, long long ldx, const float* __
     int8_t* qr = q + (long long)row * ldq;
     int8_t* qr2 = q2 ? q2 + (long long)row * ldq2 : nullptr;
     if (VEC) {
+        #pragma unroll 4
         for (int k = 4 * lane; k < K; k += 128) {
             const float4 v = *reinterpret_cast<const float4*>(xr + k);
             if (ar) {
@@ -203,19 +207,28 @@ im2col_i8_bytes_kernel(const float* __restrict__ x, int F, int H, int W, int C, 
         int ci = e0 - tap * C;
         int ky = tap / k, kx = tap - ky * k;
         const float* xf = x + (long long)f * H * W * C;
+        // all 16 gathers first (addresses and predicates, then the loads),
+        // so they are in flight together; then quantize and pack
+        int off[16];
+        bool ok[16];
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+            ok[i] = e0 + i < K && iy >= 0 && iy < H && ix >= 0 && ix < W;
+            off[i] = (iy * W + ix) * C + ci;
+            if (++ci == C) {
+                ci = 0;
+                if (++kx == k) { kx = 0; ++ky; }
+            }
+        }
+        float v[16];
+        #pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = ok[i] ? xf[off[i]] : 0.0f;
         uint32_t w[4] = {0u, 0u, 0u, 0u};
         #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            if (e0 + i < K) {
-                const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-                int8_t q = 0;
-                if (iy >= 0 && iy < H && ix >= 0 && ix < W) q = q8_span(xf[((long long)iy * W + ix) * C + ci], inv);
-                w[i >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (i & 3));
-                if (++ci == C) {
-                    ci = 0;
-                    if (++kx == k) { kx = 0; ++ky; }
-                }
-            }
+            const int8_t q = ok[i] ? q8_span(v[i], inv) : 0;
+            w[i >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (i & 3));
         }
         reinterpret_cast<int4*>(col + (long long)row * ldc)[g] =
             make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]), static_cast<int>(w[2]), static_cast<int>(w[3]));
