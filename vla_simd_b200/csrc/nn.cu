@@ -904,22 +904,44 @@ __global__ void maxpool_relu_kernel(const float* __restrict__ x, float* __restri
         const int c = (r - pix * cg) * vw;
         const int oy = pix / Wo, ox = pix - oy * Wo;
         float o[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        for (int ky = 0; ky < k; ++ky) {
-            const int iy = oy * stride - pad + ky;
-            if (iy < 0 || iy >= H) continue;
-            for (int kx = 0; kx < k; ++kx) {
-                const int ix = ox * stride - pad + kx;
-                if (ix < 0 || ix >= W) continue;
-                const float* src = xf + (iy * W + ix) * C + c;
-                if (vw == 4) {
-                    const float4 v = *reinterpret_cast<const float4*>(src);
-                    o[0] = v.x > o[0] ? v.x : o[0];
-                    o[1] = v.y > o[1] ? v.y : o[1];
-                    o[2] = v.z > o[2] ? v.z : o[2];
-                    o[3] = v.w > o[3] ? v.w : o[3];
-                } else {
-                    const float v = *src;
-                    o[0] = v > o[0] ? v : o[0];
+        if (k == 3 && vw == 4) {
+            // the ACT stem pool: all 9 taps' loads issued before the maxima
+            // (out-of-image taps predicated off and kept at -inf)
+            float4 t[9];
+            #pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+                #pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+                    const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+                    t[ky * 3 + kx] = in ? *reinterpret_cast<const float4*>(xf + (iy * W + ix) * C + c)
+                                        : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                }
+            #pragma unroll
+            for (int i = 0; i < 9; ++i) {     // taps in the reference's (ky, kx) order
+                o[0] = t[i].x > o[0] ? t[i].x : o[0];
+                o[1] = t[i].y > o[1] ? t[i].y : o[1];
+                o[2] = t[i].z > o[2] ? t[i].z : o[2];
+                o[3] = t[i].w > o[3] ? t[i].w : o[3];
+            }
+        } else {
+            for (int ky = 0; ky < k; ++ky) {
+                const int iy = oy * stride - pad + ky;
+                if (iy < 0 || iy >= H) continue;
+                for (int kx = 0; kx < k; ++kx) {
+                    const int ix = ox * stride - pad + kx;
+                    if (ix < 0 || ix >= W) continue;
+                    const float* src = xf + (iy * W + ix) * C + c;
+                    if (vw == 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(src);
+                        o[0] = v.x > o[0] ? v.x : o[0];
+                        o[1] = v.y > o[1] ? v.y : o[1];
+                        o[2] = v.z > o[2] ? v.z : o[2];
+                        o[3] = v.w > o[3] ? v.w : o[3];
+                    } else {
+                        const float v = *src;
+                        o[0] = v > o[0] ? v : o[0];
+                    }
                 }
             }
         }

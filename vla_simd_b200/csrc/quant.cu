@@ -152,22 +152,20 @@ im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k,
         const int pix = row - f * npix;
         const float inv = s_inv[f];
         if (g == 0) rscale[row] = s_scale[f];
-        char4 out[4] = {make_char4(0, 0, 0, 0), make_char4(0, 0, 0, 0), make_char4(0, 0, 0, 0),
-                        make_char4(0, 0, 0, 0)};
-        if (g * 16 < K) {
-            const int oy = pix / Wo, ox = pix - oy * Wo;
-            const int tap = g / cg, ci = (g - tap * cg) * 16;
-            const int ky = tap / k, kx = tap - ky * k;
-            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
-            if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
-                const float4* src = reinterpret_cast<const float4*>(x + (((long long)f * H + iy) * W + ix) * C + ci);
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 v = src[i];
-                    out[i] = make_char4(q8_span(v.x, inv), q8_span(v.y, inv), q8_span(v.z, inv), q8_span(v.w, inv));
-                }
-            }
-        }
+        char4 out[4];
+        const int oy = pix / Wo, ox = pix - oy * Wo;
+        const int tap = g / cg, ci = (g - tap * cg) * 16;
+        const int ky = tap / k, kx = tap - ky * k;
+        const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+        const bool in = g * 16 < K && iy >= 0 && iy < H && ix >= 0 && ix < W;
+        const float4* src = reinterpret_cast<const float4*>(x + (((long long)f * H + (in ? iy : 0)) * W +
+                                                                 (in ? ix : 0)) * C + (in ? ci : 0));
+        float4 v[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = in ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)   // zero taps (padding, past K) quantize to 0
+            out[i] = make_char4(q8_span(v[i].x, inv), q8_span(v[i].y, inv), q8_span(v[i].z, inv), q8_span(v[i].w, inv));
         reinterpret_cast<int4*>(col + (long long)row * ldc)[g] = *reinterpret_cast<int4*>(out);
     }
 }
@@ -246,14 +244,20 @@ __global__ void quantize_frames_i8_kernel(const float* __restrict__ x, long long
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     const int f = blockIdx.y;
-    const float amax = __uint_as_float(amax_bits[f]);
-    const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-    const float inv = __fdiv_rn(1.0f, s);
-    if (blockIdx.x == 0 && threadIdx.x == 0) fscale[f] = s;
+    __shared__ float s_inv;
+    if (threadIdx.x == 0) {   // the frame's scale once per block
+        const float amax = __uint_as_float(amax_bits[f]);
+        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+        s_inv = __fdiv_rn(1.0f, s);
+        if (blockIdx.x == 0) fscale[f] = s;
+    }
+    __syncthreads();
+    const float inv = s_inv;
     const float* xf = x + (long long)f * per_frame;
     int8_t* qf = q + (long long)f * per_frame;
     const long long stride = (long long)gridDim.x * blockDim.x;
     if (vec) {
+        #pragma unroll 4
         for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; 4 * i < per_frame; i += stride) {
             const float4 v = reinterpret_cast<const float4*>(xf)[i];
             reinterpret_cast<char4*>(qf)[i] =
