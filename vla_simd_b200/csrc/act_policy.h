@@ -104,6 +104,9 @@ class ActPolicy {
     cudaError_t run_backbone(cudaStream_t st);
     cudaError_t run_encoder(cudaStream_t st);
     cudaError_t run_decoder(cudaStream_t st, bool unnormalize);
+    cudaError_t decoder_self_block(const DecLayerDev& l, cudaStream_t st);
+    cudaError_t decoder_cross_queries(const DecLayerDev& l, float* q, cudaStream_t st);
+    cudaError_t dec0_consts(cudaStream_t st);
     template <class T> T* dalloc(size_t n);
     void fail(const std::string& m) { if (err_.empty()) err_ = m; }
 
@@ -151,12 +154,17 @@ class ActPolicy {
     int8_t *d_qea_ = nullptr, *d_qeb_ = nullptr;   // q(enc + pos), q(enc) for cross-attention
     float *d_sea_ = nullptr, *d_seb_ = nullptr;
     float *d_sa_ = nullptr, *d_sb_ = nullptr, *d_satt_ = nullptr, *d_sff_ = nullptr;
+    // decoder layer 0 on its (always zero) queries, evaluated once at load
+    float *d_dec_x0_ = nullptr, *d_dec_q0_ = nullptr;
+    bool dec0_ready_ = false;
     long long ldq_ = 0, ldqff_ = 0;
 
     std::vector<void*> allocs_;
-    uint8_t* h_img_pinned_ = nullptr;
+    size_t state_off_ = 0;                  // d_state_ = d_img_u8_ + state_off_ (one input buffer)
     float* h_state_pinned_ = nullptr;
     float* h_actions_pinned_ = nullptr;
+    int* h_status_pinned_ = nullptr;        // device status word, read back with the actions
+    int* d_status_ = nullptr;               // its device address
     cudaStream_t stream_ = nullptr;
     cudaGraphExec_t graph_[2] = {nullptr, nullptr};
     bool use_graph_ = true;

@@ -1174,6 +1174,11 @@ cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st) {
     }
 }
 
+void* device_status_address() {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_vsb_status) == cudaSuccess ? p : nullptr;
+}
+
 int device_status_take() {
     int h = 0;
     if (cudaMemcpyFromSymbol(&h, g_vsb_status, sizeof(int)) != cudaSuccess) return -1;

@@ -82,5 +82,7 @@ cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st);
 
 // Read and clear the device status word (0 = OK, see sm100.cuh).
 int device_status_take();
+// Device address of the status word on the current device (for asynchronous reads).
+void* device_status_address();
 
 }  // namespace vsb

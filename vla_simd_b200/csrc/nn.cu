@@ -1132,7 +1132,8 @@ cudaError_t linear_f32(const float* x, long long ldx, const float* W, const floa
 // (state - mean) / (std + eps) as ActModel::predict (src/models/act/act_model.cpp:151-153).
 // Doing this in a kernel keeps the captured step a single chain of kernels.
 __global__ void act_prologue_kernel(unsigned int* __restrict__ zero_u32, int n_zero_u32, float* __restrict__ zero_f32,
-                                    long long n_zero_f32, float* __restrict__ tok0, const float* __restrict__ latent,
+                                    long long n_zero_f32, const float* __restrict__ init_f32,
+                                    float* __restrict__ tok0, const float* __restrict__ latent,
                                     int d, const float* __restrict__ state, const float* __restrict__ mean,
                                     const float* __restrict__ stdv, float eps, float* __restrict__ state_n, int n) {
     pdl_wait();     // the previous step may still read these buffers
@@ -1140,17 +1141,17 @@ __global__ void act_prologue_kernel(unsigned int* __restrict__ zero_u32, int n_z
     const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = tid; i < n_zero_u32; i += stride) zero_u32[i] = 0u;
-    for (long long i = tid; i < n_zero_f32; i += stride) zero_f32[i] = 0.0f;
+    for (long long i = tid; i < n_zero_f32; i += stride) zero_f32[i] = init_f32 ? init_f32[i] : 0.0f;
     for (long long i = tid; i < d; i += stride) tok0[i] = latent[i];
     for (long long i = tid; i < n; i += stride)
         state_n[i] = __fdiv_rn(__fsub_rn(state[i], mean[i]), __fadd_rn(stdv[i], eps));
 }
 
-cudaError_t act_prologue(unsigned int* zero_u32, int n_zero_u32, float* zero_f32, long long n_zero_f32, float* tok0,
-                         const float* latent, int d, const float* state, const float* mean, const float* stdv,
-                         float eps, float* state_n, int n, cudaStream_t st) {
+cudaError_t act_prologue(unsigned int* zero_u32, int n_zero_u32, float* zero_f32, long long n_zero_f32,
+                         const float* init_f32, float* tok0, const float* latent, int d, const float* state,
+                         const float* mean, const float* stdv, float eps, float* state_n, int n, cudaStream_t st) {
     const cudaError_t le_ = launch_k(act_prologue_kernel, 64, 256, 0, st, zero_u32, n_zero_u32, zero_f32, n_zero_f32,
-                                     tok0, latent, d, state, mean, stdv, eps, state_n, n);
+                                     init_f32, tok0, latent, d, state, mean, stdv, eps, state_n, n);
     if (le_ != cudaSuccess) return le_;
     return cudaGetLastError();
 }

@@ -27,11 +27,11 @@ cudaError_t normalize_frames(const uint8_t* img, float* out, int F, long long np
 cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st);
 
-// First kernel of an ACT step: zero absmax slots and the decoder queries, copy
-// the latent token, normalize the state.
-cudaError_t act_prologue(unsigned int* zero_u32, int n_zero_u32, float* zero_f32, long long n_zero_f32, float* tok0,
-                         const float* latent, int d, const float* state, const float* mean, const float* stdv,
-                         float eps, float* state_n, int n, cudaStream_t st);
+// First kernel of an ACT step: zero absmax slots, set the decoder state
+// (init_f32, or zeros when null), copy the latent token, normalize the state.
+cudaError_t act_prologue(unsigned int* zero_u32, int n_zero_u32, float* zero_f32, long long n_zero_f32,
+                         const float* init_f32, float* tok0, const float* latent, int d, const float* state,
+                         const float* mean, const float* stdv, float eps, float* state_n, int n, cudaStream_t st);
 
 cudaError_t add_f32(const float* a, const float* b, float* out, long long n, cudaStream_t st);
 
