@@ -106,6 +106,9 @@ ActPolicy::~ActPolicy() {
     for (auto& g : graph_)
         if (g) cudaGraphExecDestroy(g);
     if (stream_) cudaStreamDestroy(stream_);
+    if (side_) cudaStreamDestroy(side_);
+    if (ev_fork_) cudaEventDestroy(ev_fork_);
+    if (ev_join_) cudaEventDestroy(ev_join_);
     for (void* p : allocs_) cudaFree(p);
     if (h_state_pinned_) cudaFreeHost(h_state_pinned_);
     if (h_actions_pinned_) cudaFreeHost(h_actions_pinned_);
@@ -416,6 +419,14 @@ bool ActPolicy::alloc_buffers() {
     const int sh = conv_out(img_h_, stem_k_, stem_stride_, stem_pad_), sw = conv_out(img_w_, stem_k_, stem_stride_, stem_pad_);
     size_t max_act = (size_t)F * sh * sw * stem_out_;
     size_t max_col_i8 = 0, max_col_f = 0, max_rows = 0;
+    size_t max_col_side = 0, max_rows_side = 0;   // downsample convs, run beside conv1
+    auto visit_side = [&](const DevConv& c, int H, int W) {
+        if (!c.lin.int8) return;
+        const int Ho = conv_out(H, c.k, c.stride, c.pad), Wo = conv_out(W, c.k, c.stride, c.pad);
+        const size_t rows = (size_t)F * Ho * Wo;
+        max_rows_side = std::max(max_rows_side, std::max(rows, (size_t)F));
+        max_col_side = std::max(max_col_side, std::max(rows * (size_t)c.lin.ldw, (size_t)F * H * W * c.cin));
+    };
     auto visit = [&](const DevConv& c, int H, int W) {
         const int Ho = conv_out(H, c.k, c.stride, c.pad), Wo = conv_out(W, c.k, c.stride, c.pad);
         const size_t rows = (size_t)F * Ho * Wo;
@@ -430,7 +441,10 @@ bool ActPolicy::alloc_buffers() {
         visit(b.conv1, h, w);
         const int oh = conv_out(h, 3, b.conv1.stride, 1), ow = conv_out(w, 3, b.conv1.stride, 1);
         visit(b.conv2, oh, ow);
-        if (b.has_down) visit(b.down, h, w);
+        if (b.has_down) {
+            visit(b.down, h, w);
+            visit_side(b.down, h, w);
+        }
         h = oh;
         w = ow;
     }
@@ -450,6 +464,10 @@ bool ActPolicy::alloc_buffers() {
     if (max_col_i8) d_col_ = dalloc<int8_t>(max_col_i8);
     if (max_col_f) d_col_f_ = dalloc<float>(max_col_f);
     d_col_scale_ = dalloc<float>(max_rows);
+    if (max_col_side) {
+        d_col2_ = dalloc<int8_t>(max_col_side);
+        d_col_scale2_ = dalloc<float>(max_rows_side);
+    }
     n_amax_ = (2 + 2 * static_cast<int>(blocks_.size())) * F;
     d_amax_ = dalloc<unsigned int>(n_amax_);
     return err_.empty();
@@ -513,7 +531,13 @@ bool ActPolicy::load(const std::string& dir) {
     d_dec_q0_ = dalloc<float>((size_t)C * d);
     if (!err_.empty()) return false;
 
-    if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) { fail("stream"); return false; }
+    if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming) != cudaSuccess) {
+        fail("streams / events");
+        return false;
+    }
     if (cudaMallocHost(&h_state_pinned_, sizeof(float) * cfg_.state_dim) != cudaSuccess ||
         cudaMallocHost(&h_actions_pinned_, sizeof(float) * cfg_.chunk * cfg_.action_dim) != cudaSuccess ||
         cudaMallocHost(&h_status_pinned_, sizeof(int)) != cudaSuccess) {
@@ -571,15 +595,18 @@ cudaError_t ActPolicy::run_linear(const DevLinear& l, const float* x_f32, const 
 
 cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H, int W, float* out, int mode,
                                 const float* res, const unsigned int* amax_in, unsigned int* amax_out,
-                                cudaStream_t st) {
+                                cudaStream_t st, bool side) {
     const int Ho = conv_out(H, c.k, c.stride, c.pad), Wo = conv_out(W, c.k, c.stride, c.pad);
     const int rows = F * Ho * Wo;
+    // a conv running beside another (a downsample next to conv1) has its own scratch
+    int8_t* col = side ? d_col2_ : d_col_;
+    float* col_scale = side ? d_col_scale2_ : d_col_scale_;
     if (c.lin.int8 && conv_i8_implicit_supported(c.cin, c.k, c.stride)) {
         // stride-1 convs over >= 64 channels: quantize the input once, then the
         // tensor-core GEMM gathers the taps itself (no im2col matrix)
-        VSB_TRY(quantize_frames_i8(in, F, (long long)H * W * c.cin, amax_in, i8_clip_, d_col_, d_col_scale_, st));
+        VSB_TRY(quantize_frames_i8(in, F, (long long)H * W * c.cin, amax_in, i8_clip_, col, col_scale, st));
         ConvI8Args a;
-        a.x = d_col_;
+        a.x = col;
         a.F = F;
         a.H = H;
         a.W = W;
@@ -589,7 +616,7 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
         a.Wq = c.lin.Wq;
         a.ldw = c.lin.ldw;
         a.N = c.cout;
-        a.fscale = d_col_scale_;
+        a.fscale = col_scale;
         a.wscale = c.lin.wscale;
         a.bias = c.lin.bias;
         a.out = out;
@@ -600,10 +627,10 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
         return conv_i8_implicit(a, st);
     }
     if (c.lin.int8) {
-        VSB_TRY(im2col_i8(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, c.lin.ldw, amax_in, i8_clip_, d_col_,
-                          d_col_scale_, st));
+        VSB_TRY(im2col_i8(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, c.lin.ldw, amax_in, i8_clip_, col,
+                          col_scale, st));
         GemmI8Args a;
-        a.A = d_col_;
+        a.A = col;
         a.lda = c.lin.ldw;
         a.B = c.lin.Wq;
         a.ldb = c.lin.ldw;
@@ -612,7 +639,7 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
         a.K = c.lin.K;
         a.out = out;
         a.ldo = c.cout;
-        a.ascale = d_col_scale_;
+        a.ascale = col_scale;
         a.wscale = c.lin.wscale;
         a.bias = c.lin.bias;
         a.res = res;
@@ -626,6 +653,17 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
     VSB_TRY(im2col_f32(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, d_col_f_, st));
     return gemm_f32(d_col_f_, c.lin.K, c.lin.W, c.lin.K, c.lin.bias, out, c.cout, res, c.cout, rows, c.cout,
                     c.lin.K, mode, amax_out, Ho * Wo, st);
+}
+
+cudaStream_t ActPolicy::fork(cudaStream_t st) {
+    if (cudaEventRecord(ev_fork_, st) != cudaSuccess || cudaStreamWaitEvent(side_, ev_fork_, 0) != cudaSuccess)
+        return nullptr;
+    return side_;
+}
+
+cudaError_t ActPolicy::join(cudaStream_t st) {
+    VSB_TRY(cudaEventRecord(ev_join_, side_));
+    return cudaStreamWaitEvent(st, ev_join_, 0);
 }
 
 cudaError_t ActPolicy::run_backbone(cudaStream_t st) {
@@ -648,11 +686,17 @@ cudaError_t ActPolicy::run_backbone(cudaStream_t st) {
         unsigned int* out_slot = mid_slot + F;
         const int oh = conv_out(h, 3, blk.conv1.stride, 1), ow = conv_out(w, 3, blk.conv1.stride, 1);
         const float* idn = b;
+        // the downsample conv runs beside conv1 (both read the block input; it
+        // has its own scratch); conv2 waits for both
+        const bool side = blk.has_down && blk.down.lin.int8 && d_col2_;
         if (blk.has_down) {
-            VSB_TRY(run_conv(blk.down, b, F, h, w, d_bres_, 0, nullptr, in_slot, nullptr, st));
+            cudaStream_t ds = side ? fork(st) : st;
+            if (!ds) return cudaErrorUnknown;
+            VSB_TRY(run_conv(blk.down, b, F, h, w, d_bres_, 0, nullptr, in_slot, nullptr, ds, side));
             idn = d_bres_;
         }
         VSB_TRY(run_conv(blk.conv1, b, F, h, w, a, kEpiRelu, nullptr, in_slot, mid_slot, st));
+        if (side) VSB_TRY(join(st));
         VSB_TRY(run_conv(blk.conv2, a, F, oh, ow, c, kEpiAddRelu, idn, mid_slot, out_slot, st));
         std::swap(b, c);
         h = oh;
@@ -672,8 +716,13 @@ cudaError_t ActPolicy::run_encoder(cudaStream_t st) {
         const EncLayerDev& l = enc_[li];
         const bool last = li + 1 == enc_.size();
         if (!l.wqk.int8) VSB_TRY(add_f32(d_x_, d_pos_, d_xp_, (long long)T * d, st));   // fp32 q/k read x + pos
-        VSB_TRY(run_linear(l.wqk, d_xp_, d_qa_, d_sa_, nullptr, T, d_qk_, 2 * d, 0, nullptr, 0, st));
-        VSB_TRY(run_linear(l.wv, d_x_, d_qb_, d_sb_, nullptr, T, d_v_, d, 0, nullptr, 0, st));
+        {   // V beside Q/K (separate inputs and outputs); attention waits for both
+            cudaStream_t sv = fork(st);
+            if (!sv) return cudaErrorUnknown;
+            VSB_TRY(run_linear(l.wv, d_x_, d_qb_, d_sb_, nullptr, T, d_v_, d, 0, nullptr, 0, sv));
+            VSB_TRY(run_linear(l.wqk, d_xp_, d_qa_, d_sa_, nullptr, T, d_qk_, 2 * d, 0, nullptr, 0, st));
+            VSB_TRY(join(st));
+        }
         VSB_TRY(attention(d_qk_, 2 * d, d_qk_ + d, 2 * d, d_v_, d, d_att_, d, T, T, cfg_.heads, cfg_.heads,
                           cfg_.head_dim, scale, nullptr, st));
         if (l.wo.int8) {
@@ -708,8 +757,13 @@ cudaError_t ActPolicy::run_decoder(cudaStream_t st, bool unnormalize) {
     for (size_t li = 0; li < dec_.size(); ++li) {
         const DecLayerDev& l = dec_[li];
         if (!l.c_wk.int8) VSB_TRY(add_f32(d_x_, d_pos_, d_xp_, (long long)T * d, st));   // fp32 keys read enc + pos
-        VSB_TRY(run_linear(l.c_wk, d_xp_, d_qea_, d_sea_, nullptr, T, d_ck_, d, 0, nullptr, 0, st));
-        VSB_TRY(run_linear(l.c_wv, d_x_, d_qeb_, d_seb_, nullptr, T, d_cv_, d, 0, nullptr, 0, st));
+        {   // cross V beside cross K
+            cudaStream_t sv = fork(st);
+            if (!sv) return cudaErrorUnknown;
+            VSB_TRY(run_linear(l.c_wv, d_x_, d_qeb_, d_seb_, nullptr, T, d_cv_, d, 0, nullptr, 0, sv));
+            VSB_TRY(run_linear(l.c_wk, d_xp_, d_qea_, d_sea_, nullptr, T, d_ck_, d, 0, nullptr, 0, st));
+            VSB_TRY(join(st));
+        }
         const float* cq = d_qk_;
         if (li == 0 && dec0_ready_) {
             cq = d_dec_q0_;

@@ -97,9 +97,15 @@ class ActPolicy {
                            const CUtensorMap* tmap_a, int M, float* out, long long ldo, int mode,
                            const float* res, long long ldr, cudaStream_t st, unsigned int* amax = nullptr,
                            int amax_rows = 1);
+    // Independent kernel pairs of the step run on `st` and a side stream:
+    // fork() returns the side stream, ordered after everything issued on st so
+    // far; join() orders st after everything issued on the side stream. In a
+    // captured step they become parallel branches of the graph.
+    cudaStream_t fork(cudaStream_t st);
+    cudaError_t join(cudaStream_t st);
     cudaError_t run_conv(const DevConv& c, const float* in, int F, int H, int W, float* out, int mode,
                          const float* res, const unsigned int* amax_in, unsigned int* amax_out,
-                         cudaStream_t st);
+                         cudaStream_t st, bool side = false);
     cudaError_t enqueue_on_device(cudaStream_t st, bool unnormalize);
     cudaError_t run_backbone(cudaStream_t st);
     cudaError_t run_encoder(cudaStream_t st);
@@ -143,6 +149,8 @@ class ActPolicy {
     float* d_actions_ = nullptr;
     float *d_img_f_ = nullptr, *d_ba_ = nullptr, *d_bb_ = nullptr, *d_bc_ = nullptr, *d_bres_ = nullptr;
     int8_t* d_col_ = nullptr;
+    int8_t* d_col2_ = nullptr;              // scratch of the conv on the side stream
+    float* d_col_scale2_ = nullptr;
     float* d_col_f_ = nullptr;
     float* d_col_scale_ = nullptr;
     unsigned int* d_amax_ = nullptr;
@@ -166,6 +174,8 @@ class ActPolicy {
     int* h_status_pinned_ = nullptr;        // device status word, read back with the actions
     int* d_status_ = nullptr;               // its device address
     cudaStream_t stream_ = nullptr;
+    cudaStream_t side_ = nullptr;
+    cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
     cudaGraphExec_t graph_[2] = {nullptr, nullptr};
     bool use_graph_ = true;
 };
