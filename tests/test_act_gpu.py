@@ -58,6 +58,24 @@ def test_graph_equals_eager(tmp_path, monkeypatch):
     assert np.array_equal(ga, gb)
 
 
+@pytest.mark.parametrize("shape", ["small", "baseline"])
+def test_conv_forms_are_bit_identical(tmp_path, monkeypatch, shape):
+    """Implicit-GEMM convs and the space-to-depth stem (stride-2 7x7 over 3
+    channels as 4x1 taps over 64 channels) give the explicit im2col + GEMM
+    path's bits for the whole step."""
+    sh = synth.ACT_SMALL if shape == "small" else synth.ACT_BASELINE
+    f, s = synth.act_inputs(sh, seed=1)
+    monkeypatch.setenv("VLA_CONV_IM2COL", "1")
+    a = _policy(tmp_path, sh, 63, monkeypatch)
+    want = a.predict(f, s)
+    a.close()
+    monkeypatch.delenv("VLA_CONV_IM2COL")
+    b = _policy(tmp_path, sh, 63, monkeypatch)
+    got = b.predict(f, s)
+    b.close()
+    assert np.array_equal(got, want)
+
+
 def test_unnormalize_flag(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.ACT_SMALL, 63, monkeypatch)
     f, s = synth.act_inputs(synth.ACT_SMALL, seed=1)

@@ -217,7 +217,19 @@ bool ActPolicy::load_backbone(const std::string& dir, bool int8) {
         const float* b = take(cout);
         if (!take.ok) { fail("backbone.bin too short"); return false; }
         c.cin = cin; c.cout = cout; c.k = k; c.stride = stride; c.pad = pad;
-        return upload_linear(c.lin, w, b, cout, k * k * cin, q);
+        if (!upload_linear(c.lin, w, b, cout, k * k * cin, q)) return false;
+        if (c.lin.int8 && s2d_conv_supported(cin, k, stride)) {
+            // the same int8 weights (quantization is deterministic), re-indexed
+            // for the space-to-depth form of the conv
+            std::vector<int8_t> wq((size_t)cout * c.lin.ldw), ws2d((size_t)cout * 64 * ((k + 1) / 2));
+            std::vector<float> sc(cout);
+            quantize_rows_host(w, cout, k * k * cin, wq.data(), c.lin.ldw, sc.data());
+            s2d_repack_weights_host(wq.data(), cout, k, cin, c.lin.ldw, ws2d.data());
+            c.Wq_s2d = dalloc<int8_t>(ws2d.size());
+            if (!c.Wq_s2d) return false;
+            cudaMemcpy(c.Wq_s2d, ws2d.data(), ws2d.size(), cudaMemcpyHostToDevice);
+        }
+        return true;
     };
     if (!make_conv(stem_, stem_out_, stem_k_, in_ch, stem_stride_, stem_pad_, want(0))) return false;
     blocks_.resize(bm.size());
@@ -433,6 +445,7 @@ bool ActPolicy::alloc_buffers() {
         max_rows = std::max(max_rows, rows);
         max_act = std::max(max_act, rows * c.cout);
         if (c.lin.int8) max_col_i8 = std::max(max_col_i8, rows * (size_t)c.lin.ldw);
+        if (c.Wq_s2d) max_col_i8 = std::max(max_col_i8, (size_t)F * (Ho + (c.k + 1) / 2 - 1) * Wo * 64);
         else max_col_f = std::max(max_col_f, rows * (size_t)c.lin.K);
     };
     visit(stem_, img_h_, img_w_);
@@ -484,6 +497,7 @@ bool ActPolicy::load(const std::string& dir) {
     cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_);
     if (major != 10) { fail("needs an sm_100 (B200) device"); return false; }
     use_graph_ = env_int("VLA_CUDA_GRAPH", 1) != 0;
+    explicit_convs_ = env_int("VLA_CONV_IM2COL", 0) != 0;
     i8_clip_ = env_clip();
     const int mask = env_int("ACT_INT8", 0);
 
@@ -601,7 +615,34 @@ cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H,
     // a conv running beside another (a downsample next to conv1) has its own scratch
     int8_t* col = side ? d_col2_ : d_col_;
     float* col_scale = side ? d_col_scale2_ : d_col_scale_;
-    if (c.lin.int8 && conv_i8_implicit_supported(c.cin, c.k, c.stride)) {
+    if (c.lin.int8 && c.Wq_s2d && !explicit_convs_) {
+        // stride-2 conv over a few channels as a stride-1 conv of ceil(k/2) x 1
+        // taps over 64 space-to-depth channels (same int32 sums as im2col)
+        const int kt = (c.k + 1) / 2;
+        VSB_TRY(s2d_quantize_i8(in, F, H, W, c.cin, c.k, c.pad, Ho, Wo, amax_in, i8_clip_, col, col_scale, st));
+        ConvI8Args a;
+        a.x = col;
+        a.F = F;
+        a.H = Ho + kt - 1;
+        a.W = Wo;
+        a.C = 64;
+        a.k = kt;
+        a.kw = 1;
+        a.pad = 0;
+        a.Wq = c.Wq_s2d;
+        a.ldw = 64LL * kt;
+        a.N = c.cout;
+        a.fscale = col_scale;
+        a.wscale = c.lin.wscale;
+        a.bias = c.lin.bias;
+        a.out = out;
+        a.res = res;
+        a.amax = amax_out;
+        a.mode = mode;
+        a.static_weights = true;
+        return conv_i8_implicit(a, st);
+    }
+    if (c.lin.int8 && !explicit_convs_ && conv_i8_implicit_supported(c.cin, c.k, c.stride)) {
         // stride-1 convs over >= 64 channels: quantize the input once, then the
         // tensor-core GEMM gathers the taps itself (no im2col matrix)
         VSB_TRY(quantize_frames_i8(in, F, (long long)H * W * c.cin, amax_in, i8_clip_, col, col_scale, st));

@@ -31,6 +31,9 @@ struct DevLinear {
 struct DevConv {
     int cin = 0, cout = 0, k = 0, stride = 1, pad = 0;
     DevLinear lin;             // N = cout, K = k*k*cin in (ky, kx, ci) order
+    // stride-2 convs over <= 4 channels (the stem): lin.Wq re-indexed for the
+    // space-to-depth form, [cout][64 * ceil(k/2)]
+    int8_t* Wq_s2d = nullptr;
 };
 
 struct DevBlock {
@@ -178,6 +181,7 @@ class ActPolicy {
     cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
     cudaGraphExec_t graph_[2] = {nullptr, nullptr};
     bool use_graph_ = true;
+    bool explicit_convs_ = false;   // VLA_CONV_IM2COL: im2col + GEMM for every int8 conv
 };
 
 }  // namespace vsb

@@ -75,6 +75,7 @@ struct EpiParams {
     // (ky, kx, channel block): k-block kb = tap * conv_cb + channel block.
     // ascale is per frame.
     int conv_bw, conv_bh, conv_tx, conv_ty, conv_ho, conv_wo, conv_k, conv_pad, conv_cb;
+    int conv_kw;                  // filter width (conv_k = height)
 };
 
 // Output row (index into out / res, and the absmax slot numerator) of tile
@@ -110,7 +111,7 @@ __device__ __forceinline__ void load_a(const EpiParams& p, const CUtensorMap* ta
     const int f = mt / per_f, rem = mt - f * per_f;
     const int ty = rem / p.conv_tx, tx = rem - ty * p.conv_tx;
     const int tap = kb / p.conv_cb, cb = kb - tap * p.conv_cb;
-    const int ky = tap / p.conv_k, kx = tap - ky * p.conv_k;
+    const int ky = tap / p.conv_kw, kx = tap - ky * p.conv_kw;
     tma_load_4d(dst, ta, bar, cb * KBB, tx * p.conv_bw - p.conv_pad + kx, ty * p.conv_bh - p.conv_pad + ky, f);
 }
 
@@ -1091,8 +1092,9 @@ cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st) {
     if (!a.x || !a.Wq || !a.fscale || !a.wscale || !a.out || a.F <= 0 || a.H <= 0 || a.W <= 0 || a.N <= 0 ||
         a.pad < 0 || !conv_i8_implicit_supported(a.C, a.k, 1))
         return cudaErrorInvalidValue;
-    const int Ho = a.H + 2 * a.pad - a.k + 1, Wo = a.W + 2 * a.pad - a.k + 1;
-    const long long K = (long long)a.k * a.k * a.C;
+    const int kw = a.kw > 0 ? a.kw : a.k;
+    const int Ho = a.H + 2 * a.pad - a.k + 1, Wo = a.W + 2 * a.pad - kw + 1;
+    const long long K = (long long)a.k * kw * a.C;
     if (Ho <= 0 || Wo <= 0 || K > INT_MAX / (255 * 127) || a.ldw < K || (a.ldw & 15) ||
         (long long)a.F * Ho * Wo >= (1LL << 31) || (long long)a.F * a.H * a.W * a.C >= (1LL << 40))
         return cudaErrorInvalidValue;
@@ -1131,6 +1133,7 @@ cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st) {
     p.conv_ho = Ho;
     p.conv_wo = Wo;
     p.conv_k = a.k;
+    p.conv_kw = kw;
     p.conv_pad = a.pad;
     p.conv_cb = a.C / kbb;
     p.m_tiles = a.F * p.conv_ty * p.conv_tx;

@@ -61,10 +61,12 @@ cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUten
 // im2col matrix is written. x = int8 [F][H][W][C] quantized with the per-frame
 // scales fscale[F]; weights [N][ldw] over K = k*k*C in (ky, kx, c) order;
 // out = fp32 NHWC [F][Ho][Wo][N], the gemm_i8 epilogue (mode, residual of the
-// same shape, absmax slot = frame). Requires C % 64 == 0.
+// same shape, absmax slot = frame). Requires C % 64 == 0. The filter is k x kw
+// (kw = 0: square); weights' K order (ky, kx, c).
 struct ConvI8Args {
     const int8_t* x = nullptr;
     int F = 0, H = 0, W = 0, C = 0, k = 0, pad = 0;
+    int kw = 0;
     const int8_t* Wq = nullptr;
     long long ldw = 0;
     int N = 0;

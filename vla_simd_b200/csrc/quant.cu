@@ -283,6 +283,107 @@ cudaError_t quantize_frames_i8(const float* x, int F, long long per_frame, const
     return cudaGetLastError();
 }
 
+// Space-to-depth quantization for a stride-2 convolution over C <= 4
+// channels (the 7x7/2 stem). With ky = 2t + dy and kx = 2u + dx the stride-2
+// conv is a stride-1 conv of kt = ceil(k/2) rows and one column over
+//   q[f][by][ox][u*16 + (dy*2 + dx)*C + c] = quant(x[f][2by + dy - pad][2(ox + u) + dx - pad][c])
+// (zero outside the image, in bytes 4C..15 of a group and in groups u >= kt),
+// 64 channels per pixel, by in [0, Hb = Ho + kt - 1). The weights are
+// re-indexed the same way once at load, so every int32 sum, and the output,
+// is the im2col path's. One thread per 16-byte group (a pixel's u), scale as
+// im2col_i8 (frame absmax slot, clip), fscale [F] = the frame scales.
+template <int C>
+__global__ void __launch_bounds__(256)
+s2d_quantize_i8_kernel(const float* __restrict__ x, int F, int H, int W, int pad, int Hb, int Wo, int kt,
+                       const unsigned int* __restrict__ amax_bits, float clip, int8_t* __restrict__ q,
+                       float* __restrict__ fscale) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    __shared__ float s_inv[8];
+    if (threadIdx.x < F && threadIdx.x < 8) {
+        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
+        const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
+        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
+        if (blockIdx.x == 0) fscale[threadIdx.x] = s;
+    }
+    __syncthreads();
+    const int total = F * Hb * Wo * 4;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int u = t & 3;
+        const int pix = t >> 2;
+        const int ox = pix % Wo, r = pix / Wo;
+        const int by = r % Hb, f = r / Hb;
+        const float inv = s_inv[f];
+        const int iy0 = 2 * by - pad, ix0 = 2 * (ox + u) - pad;
+        const float* xf = x + (long long)f * H * W * C;
+        // all loads first (predicated), then quantize and pack
+        float v[4 * C];
+        bool ok[4 * C];
+        #pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            const int iy = iy0 + (d >> 1), ix = ix0 + (d & 1);
+            const bool in = u < kt && iy >= 0 && iy < H && ix >= 0 && ix < W;
+            #pragma unroll
+            for (int c = 0; c < C; ++c) {
+                ok[d * C + c] = in;
+                v[d * C + c] = in ? xf[(iy * W + ix) * C + c] : 0.0f;
+            }
+        }
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        #pragma unroll
+        for (int i = 0; i < 4 * C; ++i) {
+            const int8_t b = ok[i] ? q8_span(v[i], inv) : 0;
+            w[i >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(b)) << (8 * (i & 3));
+        }
+        reinterpret_cast<int4*>(q)[t] =
+            make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]), static_cast<int>(w[2]), static_cast<int>(w[3]));
+    }
+}
+
+cudaError_t s2d_quantize_i8(const float* x, int F, int H, int W, int C, int k, int pad, int Ho, int Wo,
+                            const unsigned int* amax_bits, float clip, int8_t* q, float* fscale, cudaStream_t st) {
+    const int kt = (k + 1) / 2;
+    const int Hb = Ho + kt - 1;
+    if (!s2d_conv_supported(C, k, 2) || F <= 0 || F > 8 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || pad < 0 ||
+        (reinterpret_cast<uintptr_t>(q) & 15) || (long long)F * Hb * Wo * 4 >= (1LL << 31) ||
+        (long long)H * W * C >= (1LL << 31))
+        return cudaErrorInvalidValue;
+    const long long total = (long long)F * Hb * Wo * 4;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    cudaError_t e = cudaSuccess;
+    switch (C) {
+        case 1: e = launch_k(s2d_quantize_i8_kernel<1>, (int)blocks, 256, 0, st, x, F, H, W, pad, Hb, Wo, kt, amax_bits,
+                             clip, q, fscale); break;
+        case 2: e = launch_k(s2d_quantize_i8_kernel<2>, (int)blocks, 256, 0, st, x, F, H, W, pad, Hb, Wo, kt, amax_bits,
+                             clip, q, fscale); break;
+        case 3: e = launch_k(s2d_quantize_i8_kernel<3>, (int)blocks, 256, 0, st, x, F, H, W, pad, Hb, Wo, kt, amax_bits,
+                             clip, q, fscale); break;
+        default: e = launch_k(s2d_quantize_i8_kernel<4>, (int)blocks, 256, 0, st, x, F, H, W, pad, Hb, Wo, kt,
+                              amax_bits, clip, q, fscale); break;
+    }
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+bool s2d_conv_supported(int C, int k, int stride) {
+    return stride == 2 && C >= 1 && C <= 4 && k >= 1 && k <= 8;
+}
+
+void s2d_repack_weights_host(const int8_t* Wq, int N, int k, int C, long long ldw, int8_t* out) {
+    const int kt = (k + 1) / 2;
+    const long long ldo = 64LL * kt;
+    for (int o = 0; o < N; ++o) {
+        int8_t* row = out + (long long)o * ldo;
+        for (long long j = 0; j < ldo; ++j) row[j] = 0;
+        for (int ky = 0; ky < k; ++ky)
+            for (int kx = 0; kx < k; ++kx)
+                for (int c = 0; c < C; ++c)
+                    row[(ky >> 1) * 64 + (kx >> 1) * 16 + ((ky & 1) * 2 + (kx & 1)) * C + c] =
+                        Wq[(long long)o * ldw + ((long long)ky * k + kx) * C + c];
+    }
+}
+
 // Per-slot absmax of a contiguous tensor: slot = blockIdx.y covers elements
 // [slot*per_slot, (slot+1)*per_slot); one atomic per block.
 __global__ void absmax_kernel(const float* __restrict__ x, long long per_slot,

@@ -24,6 +24,17 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
 cudaError_t quantize_frames_i8(const float* x, int F, long long per_frame, const unsigned int* amax_bits, float clip,
                                int8_t* q, float* fscale, cudaStream_t st);
 
+// Stride-2 convolution over C <= 4 channels with a k <= 8 filter as a
+// stride-1 conv of kt = ceil(k/2) rows and 1 column over 64 channels
+// (space to depth): s2d_quantize_i8 writes the int8 input
+// q [F][Ho + kt - 1][Wo][64] and fscale [F] (scale as im2col_i8), and
+// s2d_repack_weights_host re-indexes packed weights Wq [N][ldw] (K order
+// ky, kx, c) into [N][64 * kt] (zero for the taps the conv does not have).
+bool s2d_conv_supported(int C, int k, int stride);
+cudaError_t s2d_quantize_i8(const float* x, int F, int H, int W, int C, int k, int pad, int Ho, int Wo,
+                            const unsigned int* amax_bits, float clip, int8_t* q, float* fscale, cudaStream_t st);
+void s2d_repack_weights_host(const int8_t* Wq, int N, int k, int C, long long ldw, int8_t* out);
+
 // atomicMax of |x| (float bits) per slot of per_slot consecutive elements.
 cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsigned int* amax_bits,
                          cudaStream_t st);
