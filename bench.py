@@ -471,6 +471,152 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+_DP_CPU_CHILD = r"""
+import ctypes, json, os, sys, time
+sys.path.insert(0, %(root)r)
+import numpy as np
+from vla_simd_b200 import synth
+budget, max_steps = %(budget)f, %(max_steps)d
+f, s, n = synth.dp_inputs(synth.DP_BASELINE, seed=1)
+from oracle import oracle
+r = oracle.reference()
+if r is None:
+    print(json.dumps({"unavailable": "oracle/_ref/libvla_ref.so (the reference's own build) not present"}))
+    sys.exit(0)
+l = r.l
+l.vla_diffusion_load.restype = ctypes.c_void_p
+l.vla_diffusion_load.argtypes = [ctypes.c_char_p]
+l.vla_diffusion_predict.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int32] + [ctypes.c_void_p] * 2
+l.vla_diffusion_free.argtypes = [ctypes.c_void_p]
+h = l.vla_diffusion_load(%(ckpt)r.encode())
+out = np.zeros((synth.DP_BASELINE.n_action_steps, synth.DP_BASELINE.action_dim), np.float32)
+P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+l.vla_diffusion_predict(h, P(f), P(s), 1, P(out), P(n))
+times = []
+t_end = time.perf_counter() + budget
+while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+    t0 = time.perf_counter()
+    rc = l.vla_diffusion_predict(h, P(f), P(s), 1, P(out), P(n))
+    times.append(time.perf_counter() - t0)
+    assert rc == 0
+l.vla_diffusion_free(h)
+print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * float(np.median(times))}))
+"""
+
+DP_MASK = 3   # DIFFUSION_INT8: U-Net GEMMs and backbone convs in W8A8
+
+
+def time_reference_dp_cpu(ckpt: str, budget_s: float, max_steps: int):
+    """The reference's own Diffusion Policy query (oracle/_ref) in a fresh process, all host cores."""
+    cores = cpu_cores()
+    env = dict(os.environ, DIFFUSION_INT8=str(DP_MASK), OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close",
+               CUDA_VISIBLE_DEVICES="")
+    code = _DP_CPU_CHILD % {"root": ROOT, "budget": budget_s, "max_steps": max_steps, "ckpt": ckpt}
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        return {"unavailable": f"reference CPU run failed: {r.stderr.strip().splitlines()[-1:]}"}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    if "unavailable" in d:
+        return d
+    d["cores"] = cores
+    d["chunks_per_s"] = d["steps"] / d["seconds"]
+    return d
+
+
+def run_dp(args):
+    """Diffusion Policy: one query batch per step, every
+    query its own observation history and noise, DDIM 10; replicas per GPU."""
+    import torch
+    rank, local_rank, world = _env_rank()
+    os.environ["VLA_CUDA_DEVICE"] = str(local_rank)
+    os.environ["DIFFUSION_INT8"] = str(DP_MASK)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from vla_simd_b200 import DiffusionPolicy, synth
+    B = args.batch
+    ckpt_root = tempfile.mkdtemp(prefix="vla_dp_")
+    ckpt = synth.write_dp_checkpoint(os.path.join(ckpt_root, "dp"), synth.DP_BASELINE, seed=0)
+    pol = DiffusionPolicy(ckpt, max_batch=B)
+    frames, state, noise = synth.dp_inputs(synth.DP_BASELINE, seed=1 + rank, batch=B)
+    pol.predict_batch(frames, state, noise)   # leaves the batch resident in the device input buffers
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        pol.enqueue(B, stream.cuda_stream)
+    torch.cuda.synchronize()
+    kernels = pol.kernels_per_step
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            starts[i].record(stream)
+            pol.enqueue(B, stream.cuda_stream)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    step_s = [s_.elapsed_time(e_) * 1e-3 for s_, e_ in zip(starts, ends)]
+    total_max = max_over_ranks(sum(step_s), dist, dev)
+    value = job_value(args.steps * B, world, total_max)
+    n_e2e = max(args.steps, 10)
+    for _ in range(2):
+        pol.predict_batch(frames, state, noise)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        pol.predict_batch(frames, state, noise)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    e2e = {"value": job_value(n_e2e * B, world, e2e_s), "unit": "chunks/s",
+           "h2d_bytes_per_step": frames.nbytes + state.nbytes + noise.nbytes,
+           "d2h_bytes_per_step": B * pol.chunk * pol.action_dim * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
+           "path": "vla_diffusion_predict_batch (C ABI), host frames + state + noise -> host actions"}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = time_reference_dp_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
+    pol.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu_baseline = None
+    if cpu and "unavailable" not in cpu:
+        cpu_baseline = {"value": round(cpu["chunks_per_s"], 3), "unit": "chunks/s", "cores": cpu["cores"],
+                        "kind": "reference", "p50_ms": round(cpu["p50_ms"], 2),
+                        "sample": f"{cpu['steps']} single queries (same checkpoint, DIFFUSION_INT8={DP_MASK}) of "
+                                  f"the reference's own vla_diffusion_predict, OMP_NUM_THREADS={cpu['cores']}"}
+    elif cpu:
+        cpu_baseline = {"unavailable": cpu["unavailable"]}
+    print(json.dumps({
+        "metric": "Diffusion Policy throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
+        "data": "synthetic (seeded random-init DP weights, uniform uint8 frames, N(0,1) state and noise)",
+        "config": {"workload": "Diffusion Policy, BASELINE configs[2]: 2-frame history of 96x96 frames "
+                               "center-cropped to 84x84 -> ResNet-18 (GroupNorm) + spatial softmax; U-Net "
+                               "(512, 1024, 2048) k5 GN8 FiLM, horizon 16, action 2, DDIM 10",
+                   "batch_per_gpu": B, "int8_mask": DP_MASK, "parallelism": f"replicas x{world} (no collective)",
+                   "l2": "flushed between steps (256 MiB memset outside the timed events)"},
+        "latency_ms": {"p50": round(1e3 * statistics.median(step_s), 4),
+                       "p95": round(1e3 * float(np.percentile(step_s, 95)), 4)},
+        "cpu_baseline": cpu_baseline, "e2e": e2e, "gpu_launches": kernels * args.steps,
+        "kernels_per_step": kernels, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_reference(args):
     """Reference arm: the reference's own CPU implementation on this host (rank 0 only)."""
     rank, _, world = _env_rank()
@@ -510,6 +656,9 @@ def main():
     ap.add_argument("--op", default=None, help="time one op at its ACT shape (attention, gemm_qkv, gemm_w1, "
                                                "gemm_w2, layernorm, quantize, conv_layer1), or gemm_msweep "
                                                "(the FFN GEMM at M = 602 x {1, 8, 32, 128})")
+    ap.add_argument("--model", choices=["act", "dp"], default="act",
+                    help="act: the ACT step (the headline line); dp: Diffusion Policy (BASELINE configs[2])")
+    ap.add_argument("--batch", type=int, default=1, help="queries per step per GPU (--model dp)")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
     args = ap.parse_args()
@@ -522,7 +671,9 @@ def main():
         print(json.dumps({"int8_gemm": time_gemm(torch, torch.device("cuda", 0), n_cold=5, n_warm_graph=5,
                                                  n_lin=2)}), flush=True)
         return
-    if args.impl == "reference":
+    if args.model == "dp" and args.impl != "reference":
+        run_dp(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

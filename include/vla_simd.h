@@ -77,6 +77,33 @@ VLA_API int32_t vla_act_img_w(void* h);
 VLA_API int32_t vla_act_predict(void* h, const uint8_t* images, const float* state,
                                 int32_t unnormalize, float* actions);
 
+/* ---------------------------------------------------- Diffusion Policy -----
+ * replaces reference include/vla_simd.h:258-280 (src/models/diffusion/diffusion_capi.cpp:23-72).
+ * model_dir: a converter directory (diffusion.meta, rgb_encoder{i}_backbone.meta/.bin,
+ * rgb_encoder{i}.bin, unet.bin, stats.bin) as written by tools/convert_diffusion.py.
+ * DIFFUSION_INT8 (bit 1 U-Net GEMMs, bit 2 backbone convs), DP_STEPS and
+ * DP_SCHEDULER keep the reference's meaning. */
+VLA_API void* vla_diffusion_load(const char* model_dir);
+VLA_API void  vla_diffusion_free(void* h);
+
+VLA_API int32_t vla_diffusion_chunk(void* h);        /* n_action_steps */
+VLA_API int32_t vla_diffusion_horizon(void* h);
+VLA_API int32_t vla_diffusion_action_dim(void* h);
+VLA_API int32_t vla_diffusion_state_dim(void* h);
+VLA_API int32_t vla_diffusion_n_cams(void* h);
+VLA_API int32_t vla_diffusion_n_obs_steps(void* h);
+VLA_API int32_t vla_diffusion_img_h(void* h);
+VLA_API int32_t vla_diffusion_img_w(void* h);
+VLA_API int32_t vla_diffusion_num_steps(void* h);
+VLA_API int32_t vla_diffusion_is_ddim(void* h);
+
+/* frames [n_obs_steps, n_cams, img_h, img_w, 3] uint8, oldest first; state
+ * [n_obs_steps, state_dim]; noise [1 + num_steps, horizon, action_dim] or NULL
+ * (the sampler then starts from zeros); actions out [chunk, action_dim]. */
+VLA_API int32_t vla_diffusion_predict(void* h, const uint8_t* frames, const float* state,
+                                      int32_t unnormalize, float* actions,
+                                      const float* noise);
+
 #ifdef __cplusplus
 }
 #endif

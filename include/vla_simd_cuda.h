@@ -214,6 +214,47 @@ VLA_API int32_t vla_act_enqueue(void* h, void* stream, int32_t unnormalize);
 VLA_API int32_t vla_act_kernels_per_step(void* h);
 VLA_API int32_t vla_act_int8_layers(void* h);
 
+/* The W8A8 GEMM of vla_cuda_gemm_i8 (same epilogues, same results) for at
+ * most 128 rows and a long K, with K split over independent CTAs whose int32
+ * partial tiles are summed in a caller workspace: ws (ws_elems int32) and
+ * counters (n_counters, zero before the first call; every call leaves them
+ * zero). Weight-streaming shapes - a batch-1 policy's layers - spread over all
+ * SMs this way. Shapes that gain nothing take the ordinary kernels. Calls that
+ * may overlap on the GPU need separate workspaces. No counterpart in the
+ * reference (its GEMM is one CPU kernel, src/hal/avx2/gemm_i8.cpp:123-159). */
+VLA_API int32_t vla_cuda_gemm_i8_splitk(void* out, int64_t ldo, const int8_t* xq, int64_t ldx,
+                                        const float* ascale, const int8_t* Wq, int64_t ldw,
+                                        const float* wscale, const float* bias, const float* res,
+                                        int64_t ldr, int32_t M, int32_t N, int32_t K, int32_t mode,
+                                        int32_t* ws, int64_t ws_elems, uint32_t* counters,
+                                        int32_t n_counters, void* stream);
+
+/* ------------------------------------------- batched Diffusion Policy
+ * No counterpart in the reference, whose vla_diffusion_predict serves one query
+ * (src/models/diffusion/diffusion_capi.cpp:57-72): a handle loaded with
+ * max_batch serves up to that many independent queries in one call, each
+ * with its own GroupNorm statistics and quantization scales, so every query's
+ * actions equal a single-query predict of it. Arrays gain a leading batch axis:
+ * frames [batch][n_obs_steps*n_cams][img_h][img_w][3], state [batch][n_obs_steps][state_dim],
+ * noise [batch][1 + num_steps][horizon][action_dim] or NULL, actions [batch][chunk][action_dim]. */
+VLA_API void* vla_diffusion_load_batch(const char* model_dir, int32_t max_batch);
+VLA_API int32_t vla_diffusion_predict_batch(void* h, int32_t batch, const uint8_t* frames, const float* state,
+                                            int32_t unnormalize, float* actions, const float* noise);
+/* device-resident stepping for throughput runs (as vla_act_device_buffers / vla_act_enqueue) */
+VLA_API int32_t vla_diffusion_device_buffers(void* h, uint8_t** frames, float** state, float** noise,
+                                             const float** actions);
+VLA_API int32_t vla_diffusion_enqueue(void* h, int32_t batch, void* stream, int32_t unnormalize);
+VLA_API int32_t vla_diffusion_kernels_per_step(void* h);
+VLA_API int32_t vla_diffusion_int8_layers(void* h);
+/* Parity taps, no counterpart in the reference's ABI (its intermediates are
+ * not exposed): after a predict, copy to `out` (capacity `cap` floats) the last
+ * batch's global conditioning vector [batch][n_obs_steps*(state_dim + n_cams*2*keypoints)],
+ * or, for a handle loaded with VLA_DP_DEBUG_STAGE = s, the first encoder's map
+ * after ResNet stage s (0 stem + GroupNorm, 1 max-pool, 2 + i block i) for all
+ * of its frames. Return the element count, or -1. */
+VLA_API int64_t vla_diffusion_global_cond(void* h, float* out, int64_t cap);
+VLA_API int64_t vla_diffusion_debug_map(void* h, float* out, int64_t cap);
+
 #ifdef __cplusplus
 }
 #endif

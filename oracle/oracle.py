@@ -300,6 +300,59 @@ class Reference:
             self.l.vla_act_free(h)
 
 
+    def dp_predict(self, model_dir, frames, state, noise, unnormalize=True):
+        """The reference's vla_diffusion_predict (src/models/diffusion/diffusion_capi.cpp:57-72)
+        on one query: frames [n_obs*n_cams, H, W, 3] uint8, state [n_obs, state_dim],
+        noise [1 + steps, horizon, action_dim]; returns actions [n_action_steps, action_dim]."""
+        l = self.l
+        l.vla_diffusion_load.restype = VP
+        l.vla_diffusion_load.argtypes = [ctypes.c_char_p]
+        l.vla_diffusion_free.argtypes = [VP]
+        for name in ("chunk", "action_dim"):
+            getattr(l, f"vla_diffusion_{name}").argtypes = [VP]
+        l.vla_diffusion_predict.argtypes = [VP, VP, VP, I32, VP, VP]
+        h = l.vla_diffusion_load(model_dir.encode())
+        if not h:
+            raise RuntimeError("reference vla_diffusion_load failed")
+        try:
+            out = np.zeros((l.vla_diffusion_chunk(h), l.vla_diffusion_action_dim(h)), np.float32)
+            fr = np.ascontiguousarray(frames, np.uint8)
+            st = np.ascontiguousarray(state, np.float32)
+            nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+            rc = l.vla_diffusion_predict(h, _ptr(fr), _ptr(st), 1 if unnormalize else 0, _ptr(out), _ptr(nz))
+            if rc != 0:
+                raise RuntimeError(f"reference vla_diffusion_predict rc={rc}")
+            return out
+        finally:
+            l.vla_diffusion_free(h)
+
+
+    def dp_global_cond(self, model_dir, frames, state):
+        """The global conditioning vector the reference builds for one DP query (ref_dp_shim.cpp)."""
+        l = self.l
+        l.ref_dp_global_cond.argtypes = [ctypes.c_char_p, VP, VP, VP]
+        l.ref_dp_global_cond.restype = I32
+        st = np.ascontiguousarray(state, np.float32)
+        out = np.zeros(1 << 16, np.float32)
+        rc = l.ref_dp_global_cond(model_dir.encode(), _ptr(np.ascontiguousarray(frames, np.uint8)), _ptr(st),
+                                  _ptr(out))
+        if rc != 0:
+            raise RuntimeError("ref_dp_global_cond failed")
+        return out
+
+    def dp_backbone_stage(self, model_dir, frames, s, cam, stage):
+        """One ResNet stage map of frame (s, cam) in the reference's DP encoder (ref_dp_shim.cpp)."""
+        l = self.l
+        l.ref_dp_backbone_stage.argtypes = [ctypes.c_char_p, VP, I32, I32, I32, VP, I64]
+        l.ref_dp_backbone_stage.restype = I64
+        out = np.zeros(1 << 24, np.float32)
+        n = l.ref_dp_backbone_stage(model_dir.encode(), _ptr(np.ascontiguousarray(frames, np.uint8)), s, cam,
+                                    stage, _ptr(out), out.size)
+        if n < 0:
+            raise RuntimeError("ref_dp_backbone_stage failed")
+        return out[:n].copy()
+
+
 def restated() -> Restated:
     return Restated()
 

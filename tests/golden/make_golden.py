@@ -6,6 +6,13 @@ checkout). Run from the repo root:  python tests/golden/make_golden.py
 * act_<cfg>_m<mask>.npy  - actions [chunk, action_dim] of the reference's
   vla_act_predict (ACT_INT8=<mask>) on synth.write_act_checkpoint(seed=0) with
   synth.act_inputs(seed=1); cfg small = synth.ACT_SMALL, base = ACT_BASELINE.
+* dp_<cfg>_m<mask>[_<variant>].npy - actions [chunk, action_dim] of the
+  reference's vla_diffusion_predict (DIFFUSION_INT8=<mask>) on
+  synth.write_dp_checkpoint(seed=0) with synth.dp_inputs(seed=1); variant
+  ddpm = DP_SCHEDULER=DDPM (DP_STEPS=10), nonoise = a NULL noise pointer. The
+  reference runs with OMP_NUM_THREADS=1: its GroupNorm splits the pixel sums
+  per thread when a map has fewer than 16 channels per thread, so one thread
+  is the order-defined result.
 * checkpoints.json       - sha256 of each synthetic checkpoint directory, so a
   test notices if the writer ever stops reproducing the bytes the fixtures
   were made from.
@@ -36,6 +43,10 @@ ACT_CASES = [("small", synth.ACT_SMALL, 63), ("small", synth.ACT_SMALL, 0), ("sm
 ATTN_CASES = [(602, 602, 8, 8), (100, 100, 8, 8), (100, 602, 8, 8), (50, 113, 15, 5), (3, 40, 4, 2)]
 LN_CASES = [(602, 512), (100, 512), (7, 960)]
 F32_LINEAR_CASES = [(1, 512, 6), (100, 6, 512), (5, 10, 37)]   # (seq, N, K): state_proj, head, odd
+# (cfg, shape name, DIFFUSION_INT8, variant)
+DP_CASES = [("small", "DP_SMALL", 3, ""), ("small", "DP_SMALL", 0, ""), ("small", "DP_SMALL", 1, ""),
+            ("small", "DP_SMALL", 3, "ddpm"), ("small", "DP_SMALL", 3, "nonoise"), ("base", "DP_BASELINE", 3, ""),
+            ("base", "DP_BASELINE", 0, "")]
 GEMM_SHAPES = [(1, 16, 3), (7, 48, 64), (13, 64, 17), (257, 96, 48), (50, 768, 1027), (602, 3200, 512),
                (602, 512, 3200), (300, 512, 512)]
 
@@ -90,11 +101,41 @@ def f32_linear_inputs(seq, N, K, seed=41):
             rng.standard_normal(N, dtype=np.float32))
 
 
+def dp_fixture_name(cfg, mask, variant):
+    return f"dp_{cfg}_m{mask}" + (f"_{variant}" if variant else "") + ".npy"
+
+
+def make_dp(digests):
+    for cfg, shape_name, mask, variant in DP_CASES:
+        with tempfile.TemporaryDirectory() as d:
+            synth.write_dp_checkpoint(d, getattr(synth, shape_name), seed=0)
+            digests["dp_" + cfg] = dir_digest(d)
+            code = ("import sys,numpy as np; sys.path.insert(0, %r); from oracle import oracle; "
+                    "from vla_simd_b200 import synth; r = oracle.reference(); sh = synth.%s; "
+                    "import dataclasses; sh = dataclasses.replace(sh, num_inference_steps=%d); "
+                    "f, s, n = synth.dp_inputs(sh, seed=1); "
+                    "np.save(%r, r.dp_predict(%r, f, s, %s))") % (
+                        ROOT, shape_name, 10, os.path.join(HERE, dp_fixture_name(cfg, mask, variant)), d,
+                        "None" if variant == "nonoise" else "n")
+            env = dict(os.environ, DIFFUSION_INT8=str(mask), OMP_NUM_THREADS="1")
+            if variant == "ddpm":
+                env.update(DP_SCHEDULER="DDPM", DP_STEPS="10")
+            subprocess.run([sys.executable, "-c", code], check=True, env=env)
+
+
 def main():
     ref = oracle.reference()
     if ref is None:
         sys.exit("oracle/_ref/libvla_ref.so missing: make -C oracle ref")
     digests = {}
+    if "--dp" in sys.argv:   # only the Diffusion Policy fixtures
+        path = os.path.join(HERE, "checkpoints.json")
+        digests = json.load(open(path))
+        make_dp(digests)
+        with open(path, "w") as f:
+            json.dump(digests, f, indent=1, sort_keys=True)
+        return
+    make_dp(digests)
     for cfg, shape, mask in ACT_CASES:
         # the reference reads ACT_INT8 when it loads, so each mask runs in its own process
         with tempfile.TemporaryDirectory() as d:

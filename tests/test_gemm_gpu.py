@@ -172,3 +172,42 @@ def test_host_pointer_shims_take_the_reference_panel_layout(restated):
     assert np.array_equal(xq, q_ref) and np.array_equal(xs, s_ref)
     wq, wsr = restated.quantize_rows(W)
     assert _bits_equal(out, restated.dense_linear_i8_ref(q_ref[:, :K], s_ref, wq, wsr, b, K))
+
+
+SPLITK_SHAPES = [(16, 2048, 10240), (16, 512, 2560), (8, 1024, 5120), (4, 1024, 20480), (128, 384, 4096),
+                 (1, 64, 1000), (77, 4096, 4096), (16, 16, 130)]
+
+
+@pytest.mark.parametrize("M,N,K", SPLITK_SHAPES)
+def test_splitk_workspace_gemm_matches_oracle(dev, restated, M, N, K):
+    """K split over independent CTAs (workspace reduction): the same int32 sums
+    and fp32 outputs as the oracle and the ordinary kernels, every epilogue; the
+    counters are left zero, so a second call gives the same bits."""
+    import torch
+    from vla_simd_b200 import EPI_ACC, EPI_ADD, EPI_RELU, ops
+    rng = np.random.default_rng(M * 31 + N * 7 + K)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    W = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    b = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    wq, ws = ops.pack_weights_i8(_t(W, dev))
+    xq, xs = ops.quantize_act_i8(_t(x, dev))
+    work = torch.empty(148 * 128 * 128, dtype=torch.int32, device=dev)
+    counters = torch.zeros(4096, dtype=torch.int32, device=dev)
+    acc = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, mode=EPI_ACC)
+    out = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev))
+    relu = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev), mode=EPI_RELU)
+    add = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev), mode=EPI_ADD, res=_t(r, dev))
+    again = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert int(counters.abs().sum().item()) == 0, "arrival counters not reset"
+    xqh, xsh = restated.quantize_rows(x)
+    wqh, wsh = restated.quantize_rows(W)
+    assert np.array_equal(acc.cpu().numpy(), restated.gemm_acc(xqh, wqh, K))
+    want = restated.dense_linear_i8_ref(xqh, xsh, wqh, wsh, b, K)
+    assert _bits_equal(out.cpu().numpy(), want)
+    assert _bits_equal(again.cpu().numpy(), want)
+    assert _bits_equal(relu.cpu().numpy(), ops.gemm_i8(xq, xs, wq, ws, K, bias=_t(b, dev), mode=EPI_RELU).cpu().numpy())
+    assert _bits_equal(add.cpu().numpy(),
+                       ops.gemm_i8(xq, xs, wq, ws, K, bias=_t(b, dev), mode=EPI_ADD, res=_t(r, dev)).cpu().numpy())

@@ -38,9 +38,13 @@ def test_small_fixture_arrays_are_consistent():
         assert sha(z[f"{key}_acc"]) == GEMM[key]["acc"]
 
 
-@pytest.mark.parametrize("cfg,shape", [("small", synth.ACT_SMALL), ("base", synth.ACT_BASELINE)])
+@pytest.mark.parametrize("cfg,shape", [("small", synth.ACT_SMALL), ("base", synth.ACT_BASELINE),
+                                       ("dp_small", synth.DP_SMALL), ("dp_base", synth.DP_BASELINE)])
 def test_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
-    d = synth.write_act_checkpoint(str(tmp_path / cfg), shape, seed=0)
+    if cfg.startswith("dp_"):
+        d = synth.write_dp_checkpoint(str(tmp_path / cfg), shape, seed=0)
+    else:
+        d = synth.write_act_checkpoint(str(tmp_path / cfg), shape, seed=0)
     assert dir_digest(d) == json.load(open(os.path.join(HERE, "checkpoints.json")))[cfg]
 
 
@@ -50,3 +54,12 @@ def test_reference_policy_fixture_is_current(tmp_path, reference, monkeypatch):
     f, s = synth.act_inputs(synth.ACT_SMALL, seed=1)
     got = reference.act_predict(d, f, s)
     assert np.array_equal(got, np.load(os.path.join(HERE, "act_small_m63.npy")))
+
+
+def test_reference_dp_fixture_is_current(tmp_path, reference, monkeypatch):
+    monkeypatch.setenv("DIFFUSION_INT8", "3")
+    monkeypatch.setenv("OMP_NUM_THREADS", "1")
+    d = synth.write_dp_checkpoint(str(tmp_path / "dp"), synth.DP_SMALL, seed=0)
+    f, s, n = synth.dp_inputs(synth.DP_SMALL, seed=1)
+    got = reference.dp_predict(d, f, s, n)
+    assert np.array_equal(got, np.load(os.path.join(HERE, "dp_small_m3.npy")))

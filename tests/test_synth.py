@@ -41,3 +41,29 @@ def test_reference_loads_and_runs_synthetic_checkpoint(tmp_path, reference, monk
     frames, state = synth.act_inputs(synth.ACT_SMALL, seed=1)
     a = reference.act_predict(d, frames, state)
     assert a.shape == (synth.ACT_SMALL.chunk, synth.ACT_SMALL.action_dim) and np.isfinite(a).all()
+
+
+def test_dp_writer_is_deterministic(tmp_path):
+    a = synth.write_dp_checkpoint(str(tmp_path / "a"), synth.DP_SMALL, seed=5)
+    b = synth.write_dp_checkpoint(str(tmp_path / "b"), synth.DP_SMALL, seed=5)
+    assert _digest(a) == _digest(b)
+
+
+def test_dp_baseline_shape_sizes(tmp_path):
+    d = synth.write_dp_checkpoint(str(tmp_path / "dp"), synth.DP_BASELINE, seed=0)
+    # conditional U-Net (512, 1024, 2048), kernel 5: ~256M parameters
+    n_unet = os.path.getsize(os.path.join(d, "unet.bin")) // 4
+    assert 240_000_000 < n_unet < 270_000_000
+    assert synth.DP_BASELINE.cond_dim == 128 + (2 + 64) * 2
+    frames, state, noise = synth.dp_inputs(synth.DP_BASELINE)
+    assert frames.shape == (2, 96, 96, 3) and state.shape == (2, 2) and noise.shape == (11, 16, 2)
+    fb, sb, nb = synth.dp_inputs(synth.DP_SMALL, batch=3)
+    assert fb.shape[0] == sb.shape[0] == nb.shape[0] == 3
+
+
+def test_reference_runs_synthetic_dp_checkpoint(tmp_path, reference, monkeypatch):
+    monkeypatch.setenv("DIFFUSION_INT8", "3")
+    d = synth.write_dp_checkpoint(str(tmp_path / "dp"), synth.DP_SMALL, seed=0)
+    frames, state, noise = synth.dp_inputs(synth.DP_SMALL, seed=1)
+    a = reference.dp_predict(d, frames, state, noise)
+    assert a.shape == (synth.DP_SMALL.n_action_steps, synth.DP_SMALL.action_dim) and np.isfinite(a).all()

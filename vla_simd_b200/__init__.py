@@ -6,6 +6,9 @@ it with ctypes and mirrors the reference's Python-side interface:
 
 * :class:`ActPolicy` - the reference server's ``ActEngine`` binding
   (vla_simd/policy_server.py:276-307): uint8 frames + state in, actions out.
+* :class:`DiffusionPolicy` - the ``vla_diffusion_*`` ABI: an observation
+  history (frames + states) and the sampler's noise in, an action chunk out;
+  optionally a batch of independent queries per call.
 * ``ops`` - device-pointer wrappers over the op-level ABI taking torch CUDA
   tensors (torch is only the allocator / stream provider here).
 
@@ -19,7 +22,7 @@ import os
 
 import numpy as np
 
-__all__ = ["LIB_PATH", "lib", "ActPolicy", "VlaError"]
+__all__ = ["LIB_PATH", "lib", "ActPolicy", "DiffusionPolicy", "VlaError"]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libvla_simd_b200.so")
 
@@ -61,6 +64,8 @@ SIGNATURES = {
     "vla_cuda_dense_linear_i8_noalloc": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP]),
     "vla_cuda_gemm_i8": (I32, [VP, I64, VP, I64, VP, I32, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I32,
                                I32, VP]),
+    "vla_cuda_gemm_i8_splitk": (I32, [VP, I64, VP, I64, VP, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I64, VP,
+                                      I32, VP]),
     "vla_cuda_conv2d_i8": (I32, [VP, VP, I32, I32, I32, I32, VP, I64, VP, VP, I32, I32, I32, I32, F32, I32, VP, VP,
                                  VP, VP, VP]),
     "vla_cuda_layernorm": (I32, [VP, VP, VP, VP, I32, I32, F32, VP]),
@@ -87,6 +92,27 @@ SIGNATURES = {
     "vla_tcpu_quantize_act_i8": (I32, [VP, VP, VP, I32, I32]),
     "vla_tcpu_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32]),
     "vla_tcpu_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, VP, VP]),
+    "vla_diffusion_load": (VP, [ctypes.c_char_p]),
+    "vla_diffusion_load_batch": (VP, [ctypes.c_char_p, I32]),
+    "vla_diffusion_free": (None, [VP]),
+    "vla_diffusion_chunk": (I32, [VP]),
+    "vla_diffusion_horizon": (I32, [VP]),
+    "vla_diffusion_action_dim": (I32, [VP]),
+    "vla_diffusion_state_dim": (I32, [VP]),
+    "vla_diffusion_n_cams": (I32, [VP]),
+    "vla_diffusion_n_obs_steps": (I32, [VP]),
+    "vla_diffusion_img_h": (I32, [VP]),
+    "vla_diffusion_img_w": (I32, [VP]),
+    "vla_diffusion_num_steps": (I32, [VP]),
+    "vla_diffusion_is_ddim": (I32, [VP]),
+    "vla_diffusion_predict": (I32, [VP, U8P, F32P, I32, F32P, F32P]),
+    "vla_diffusion_predict_batch": (I32, [VP, I32, U8P, F32P, I32, F32P, F32P]),
+    "vla_diffusion_device_buffers": (I32, [VP, VP, VP, VP, VP]),
+    "vla_diffusion_enqueue": (I32, [VP, I32, VP, I32]),
+    "vla_diffusion_kernels_per_step": (I32, [VP]),
+    "vla_diffusion_int8_layers": (I32, [VP]),
+    "vla_diffusion_global_cond": (I64, [VP, F32P, I64]),
+    "vla_diffusion_debug_map": (I64, [VP, F32P, I64]),
     "vla_act_device_buffers": (I32, [VP, VP, VP, VP]),
     "vla_act_enqueue": (I32, [VP, VP, I32]),
     "vla_act_kernels_per_step": (I32, [VP]),
@@ -166,6 +192,108 @@ class ActPolicy:
     def close(self) -> None:
         if self.h:
             self.lib.vla_act_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DiffusionPolicy:
+    """ctypes binding of the Diffusion Policy C ABI (include/vla_simd.h, the
+    reference's vla_diffusion_* at src/models/diffusion/diffusion_capi.cpp:23-72).
+
+    frames [n_obs_steps * n_cams, img_h, img_w, 3] uint8 (oldest step first,
+    cameras inside a step), state [n_obs_steps, state_dim], noise
+    [1 + num_steps, horizon, action_dim] (None: start from zeros) ->
+    actions [chunk, action_dim]. With max_batch > 1, predict_batch takes the
+    same arrays with a leading batch axis.
+    """
+
+    def __init__(self, model_dir: str, max_batch: int = 1):
+        self.lib = lib()
+        self.h = (self.lib.vla_diffusion_load(model_dir.encode()) if max_batch == 1
+                  else self.lib.vla_diffusion_load_batch(model_dir.encode(), int(max_batch)))
+        if not self.h:
+            raise RuntimeError(f"vla_diffusion_load failed for {model_dir}")
+        self.max_batch = int(max_batch)
+        for name in ("chunk", "horizon", "action_dim", "state_dim", "n_cams", "n_obs_steps", "img_h", "img_w",
+                     "num_steps", "is_ddim"):
+            setattr(self, name, int(getattr(self.lib, f"vla_diffusion_{name}")(self.h)))
+
+    def _args(self, frames, state, noise, lead):
+        frames = np.ascontiguousarray(frames, np.uint8)
+        want = lead + (self.n_obs_steps * self.n_cams, self.img_h, self.img_w, 3)
+        if frames.shape != want:
+            raise ValueError(f"frames {frames.shape} != {want}")
+        state = np.ascontiguousarray(np.asarray(state, np.float32))
+        if state.size != int(np.prod(lead, dtype=np.int64)) * self.n_obs_steps * self.state_dim:
+            raise ValueError(f"state has {state.size} values")
+        nz = None
+        if noise is not None:
+            nz = np.ascontiguousarray(np.asarray(noise, np.float32))
+            if nz.size != int(np.prod(lead, dtype=np.int64)) * (1 + self.num_steps) * self.horizon * self.action_dim:
+                raise ValueError(f"noise has {nz.size} values")
+        return frames, state, nz
+
+    def predict(self, frames, state, noise=None, unnormalize: bool = True) -> np.ndarray:
+        frames, state, nz = self._args(frames, state, noise, ())
+        out = np.empty((self.chunk, self.action_dim), np.float32)
+        rc = self.lib.vla_diffusion_predict(self.h, frames.ctypes.data_as(U8P), state.ctypes.data_as(F32P),
+                                            1 if unnormalize else 0, out.ctypes.data_as(F32P),
+                                            None if nz is None else nz.ctypes.data_as(F32P))
+        check(rc, "vla_diffusion_predict")
+        return out
+
+    def predict_batch(self, frames, state, noise=None, unnormalize: bool = True) -> np.ndarray:
+        b = int(np.asarray(frames).shape[0])
+        frames, state, nz = self._args(frames, state, noise, (b,))
+        out = np.empty((b, self.chunk, self.action_dim), np.float32)
+        rc = self.lib.vla_diffusion_predict_batch(self.h, b, frames.ctypes.data_as(U8P), state.ctypes.data_as(F32P),
+                                                  1 if unnormalize else 0, out.ctypes.data_as(F32P),
+                                                  None if nz is None else nz.ctypes.data_as(F32P))
+        check(rc, "vla_diffusion_predict_batch")
+        return out
+
+    def device_buffers(self):
+        fr, st, nz, act = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        check(self.lib.vla_diffusion_device_buffers(self.h, ctypes.byref(fr), ctypes.byref(st), ctypes.byref(nz),
+                                                    ctypes.byref(act)), "vla_diffusion_device_buffers")
+        return fr.value, st.value, nz.value, act.value
+
+    def enqueue(self, batch: int, stream_handle: int, unnormalize: bool = True) -> None:
+        check(self.lib.vla_diffusion_enqueue(self.h, int(batch), ctypes.c_void_p(stream_handle),
+                                             1 if unnormalize else 0), "vla_diffusion_enqueue")
+
+    def global_cond(self) -> np.ndarray:
+        """The last query batch's global conditioning vectors (a parity tap)."""
+        out = np.empty(self.max_batch * 4096 * 16, np.float32)
+        n = int(self.lib.vla_diffusion_global_cond(self.h, out.ctypes.data_as(F32P), out.size))
+        if n < 0:
+            raise RuntimeError("vla_diffusion_global_cond failed")
+        return out[:n].copy()
+
+    def debug_map(self, cap: int = 1 << 24) -> np.ndarray:
+        """The first encoder's map after the ResNet stage VLA_DP_DEBUG_STAGE names (a parity tap)."""
+        out = np.empty(cap, np.float32)
+        n = int(self.lib.vla_diffusion_debug_map(self.h, out.ctypes.data_as(F32P), out.size))
+        if n < 0:
+            raise RuntimeError("vla_diffusion_debug_map failed")
+        return out[:n].copy()
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(self.lib.vla_diffusion_kernels_per_step(self.h))
+
+    @property
+    def int8_layers(self) -> int:
+        return int(self.lib.vla_diffusion_int8_layers(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.vla_diffusion_free(self.h)
             self.h = None
 
     def __del__(self):

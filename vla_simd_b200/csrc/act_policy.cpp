@@ -117,32 +117,7 @@ ActPolicy::~ActPolicy() {
 }
 
 bool ActPolicy::upload_linear(DevLinear& l, const float* W, const float* b, int N, int K, bool int8) {
-    l.N = N;
-    l.K = K;
-    // nn::Linear::init_int8's conditions (src/nn/linear.cpp:67): N % 16 and the
-    // int32 headroom bound on K; a layer that fails them stays fp32.
-    l.int8 = int8 && N % 16 == 0 && K > 0 && K <= INT_MAX / (255 * 127);
-    l.bias = dalloc<float>(N);
-    if (!l.bias) return false;
-    if (b) cudaMemcpy(l.bias, b, sizeof(float) * N, cudaMemcpyHostToDevice);
-    else cudaMemset(l.bias, 0, sizeof(float) * N);
-    if (l.int8) {
-        l.ldw = round16(K);
-        std::vector<int8_t> q((size_t)N * l.ldw);
-        std::vector<float> s(N);
-        quantize_rows_host(W, N, K, q.data(), l.ldw, s.data());
-        l.Wq = dalloc<int8_t>(q.size());
-        l.wscale = dalloc<float>(N);
-        if (!l.Wq || !l.wscale) return false;
-        cudaMemcpy(l.Wq, q.data(), q.size(), cudaMemcpyHostToDevice);
-        cudaMemcpy(l.wscale, s.data(), sizeof(float) * N, cudaMemcpyHostToDevice);
-        n_int8_++;
-    } else {
-        l.W = dalloc<float>((size_t)N * K);
-        if (!l.W) return false;
-        cudaMemcpy(l.W, W, sizeof(float) * (size_t)N * K, cudaMemcpyHostToDevice);
-    }
-    return true;
+    return vsb::upload_linear(l, W, b, N, K, int8, [this](size_t n) -> void* { return dalloc<char>(n); }, &n_int8_);
 }
 
 bool ActPolicy::load_config(const std::string& dir) {
@@ -216,20 +191,8 @@ bool ActPolicy::load_backbone(const std::string& dir, bool int8) {
         const float* w = take((size_t)cout * k * k * cin);
         const float* b = take(cout);
         if (!take.ok) { fail("backbone.bin too short"); return false; }
-        c.cin = cin; c.cout = cout; c.k = k; c.stride = stride; c.pad = pad;
-        if (!upload_linear(c.lin, w, b, cout, k * k * cin, q)) return false;
-        if (c.lin.int8 && s2d_conv_supported(cin, k, stride)) {
-            // the same int8 weights (quantization is deterministic), re-indexed
-            // for the space-to-depth form of the conv
-            std::vector<int8_t> wq((size_t)cout * c.lin.ldw), ws2d((size_t)cout * 64 * ((k + 1) / 2));
-            std::vector<float> sc(cout);
-            quantize_rows_host(w, cout, k * k * cin, wq.data(), c.lin.ldw, sc.data());
-            s2d_repack_weights_host(wq.data(), cout, k, cin, c.lin.ldw, ws2d.data());
-            c.Wq_s2d = dalloc<int8_t>(ws2d.size());
-            if (!c.Wq_s2d) return false;
-            cudaMemcpy(c.Wq_s2d, ws2d.data(), ws2d.size(), cudaMemcpyHostToDevice);
-        }
-        return true;
+        return make_dev_conv(c, w, b, cout, k, cin, stride, pad, q,
+                             [this](size_t n) -> void* { return dalloc<char>(n); }, &n_int8_);
     };
     if (!make_conv(stem_, stem_out_, stem_k_, in_ch, stem_stride_, stem_pad_, want(0))) return false;
     blocks_.resize(bm.size());
@@ -610,90 +573,12 @@ cudaError_t ActPolicy::run_linear(const DevLinear& l, const float* x_f32, const 
 cudaError_t ActPolicy::run_conv(const DevConv& c, const float* in, int F, int H, int W, float* out, int mode,
                                 const float* res, const unsigned int* amax_in, unsigned int* amax_out,
                                 cudaStream_t st, bool side) {
-    const int Ho = conv_out(H, c.k, c.stride, c.pad), Wo = conv_out(W, c.k, c.stride, c.pad);
-    const int rows = F * Ho * Wo;
     // a conv running beside another (a downsample next to conv1) has its own scratch
-    int8_t* col = side ? d_col2_ : d_col_;
-    float* col_scale = side ? d_col_scale2_ : d_col_scale_;
-    if (c.lin.int8 && c.Wq_s2d && !explicit_convs_) {
-        // stride-2 conv over a few channels as a stride-1 conv of ceil(k/2) x 1
-        // taps over 64 space-to-depth channels (same int32 sums as im2col)
-        const int kt = (c.k + 1) / 2;
-        VSB_TRY(s2d_quantize_i8(in, F, H, W, c.cin, c.k, c.pad, Ho, Wo, amax_in, i8_clip_, col, col_scale, st));
-        ConvI8Args a;
-        a.x = col;
-        a.F = F;
-        a.H = Ho + kt - 1;
-        a.W = Wo;
-        a.C = 64;
-        a.k = kt;
-        a.kw = 1;
-        a.pad = 0;
-        a.Wq = c.Wq_s2d;
-        a.ldw = 64LL * kt;
-        a.N = c.cout;
-        a.fscale = col_scale;
-        a.wscale = c.lin.wscale;
-        a.bias = c.lin.bias;
-        a.out = out;
-        a.res = res;
-        a.amax = amax_out;
-        a.mode = mode;
-        a.static_weights = true;
-        return conv_i8_implicit(a, st);
-    }
-    if (c.lin.int8 && !explicit_convs_ && conv_i8_implicit_supported(c.cin, c.k, c.stride)) {
-        // stride-1 convs over >= 64 channels: quantize the input once, then the
-        // tensor-core GEMM gathers the taps itself (no im2col matrix)
-        VSB_TRY(quantize_frames_i8(in, F, (long long)H * W * c.cin, amax_in, i8_clip_, col, col_scale, st));
-        ConvI8Args a;
-        a.x = col;
-        a.F = F;
-        a.H = H;
-        a.W = W;
-        a.C = c.cin;
-        a.k = c.k;
-        a.pad = c.pad;
-        a.Wq = c.lin.Wq;
-        a.ldw = c.lin.ldw;
-        a.N = c.cout;
-        a.fscale = col_scale;
-        a.wscale = c.lin.wscale;
-        a.bias = c.lin.bias;
-        a.out = out;
-        a.res = res;
-        a.amax = amax_out;
-        a.mode = mode;
-        a.static_weights = true;
-        return conv_i8_implicit(a, st);
-    }
-    if (c.lin.int8) {
-        VSB_TRY(im2col_i8(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, c.lin.ldw, amax_in, i8_clip_, col,
-                          col_scale, st));
-        GemmI8Args a;
-        a.A = col;
-        a.lda = c.lin.ldw;
-        a.B = c.lin.Wq;
-        a.ldb = c.lin.ldw;
-        a.M = rows;
-        a.N = c.cout;
-        a.K = c.lin.K;
-        a.out = out;
-        a.ldo = c.cout;
-        a.ascale = col_scale;
-        a.wscale = c.lin.wscale;
-        a.bias = c.lin.bias;
-        a.res = res;
-        a.ldr = c.cout;
-        a.mode = mode;
-        a.amax = amax_out;
-        a.amax_rows = Ho * Wo;
-        a.static_weights = true;
-        return gemm_i8(a, st);
-    }
-    VSB_TRY(im2col_f32(in, F, H, W, c.cin, c.k, c.stride, c.pad, Ho, Wo, d_col_f_, st));
-    return gemm_f32(d_col_f_, c.lin.K, c.lin.W, c.lin.K, c.lin.bias, out, c.cout, res, c.cout, rows, c.cout,
-                    c.lin.K, mode, amax_out, Ho * Wo, st);
+    ConvScratch s;
+    s.col = side ? d_col2_ : d_col_;
+    s.col_scale = side ? d_col_scale2_ : d_col_scale_;
+    s.col_f = d_col_f_;
+    return conv2d_dev(c, in, F, H, W, out, mode, res, amax_in, amax_out, i8_clip_, explicit_convs_, s, st);
 }
 
 cudaStream_t ActPolicy::fork(cudaStream_t st) {

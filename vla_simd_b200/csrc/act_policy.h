@@ -11,30 +11,13 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "conv_exec.h"
+
 #include <cstdint>
 #include <string>
 #include <vector>
 
 namespace vsb {
-
-// A dense layer in whichever representation the int8 mask picked.
-struct DevLinear {
-    int N = 0, K = 0;
-    bool int8 = false;
-    int8_t* Wq = nullptr;      // [N][ldw] int8 (int8 layers)
-    long long ldw = 0;
-    float* wscale = nullptr;   // [N]
-    float* W = nullptr;        // [N][K] fp32 (fp32 layers)
-    float* bias = nullptr;     // [N]
-};
-
-struct DevConv {
-    int cin = 0, cout = 0, k = 0, stride = 1, pad = 0;
-    DevLinear lin;             // N = cout, K = k*k*cin in (ky, kx, ci) order
-    // stride-2 convs over <= 4 channels (the stem): lin.Wq re-indexed for the
-    // space-to-depth form, [cout][64 * ceil(k/2)]
-    int8_t* Wq_s2d = nullptr;
-};
 
 struct DevBlock {
     DevConv conv1, conv2, down;

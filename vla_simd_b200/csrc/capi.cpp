@@ -5,6 +5,7 @@
 #include "../../include/vla_simd_cuda.h"
 
 #include "act_policy.h"
+#include "dp_policy.h"
 #include "gemm_i8.h"
 #include "host_quant.h"
 #include "lm_ops.h"
@@ -14,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -21,6 +23,7 @@
 #include <vector>
 
 using vsb::ActPolicy;
+using vsb::DpPolicy;
 
 namespace {
 
@@ -150,6 +153,91 @@ int32_t vla_act_enqueue(void* h, void* stream, int32_t unnormalize) try {
 int32_t vla_act_kernels_per_step(void* h) { return h ? static_cast<ActPolicy*>(h)->kernels_per_step() : 0; }
 int32_t vla_act_int8_layers(void* h) { return h ? static_cast<ActPolicy*>(h)->int8_layers() : 0; }
 
+// ---------------------------------------------------- Diffusion Policy
+
+void* vla_diffusion_load_batch(const char* model_dir, int32_t max_batch) try {
+    if (!model_dir || max_batch < 1) return nullptr;
+    auto m = std::make_unique<DpPolicy>();
+    if (!m->load(model_dir, max_batch)) {
+        std::fprintf(stderr, "vla_diffusion_load: %s\n", m->error().c_str());
+        return nullptr;
+    }
+    return m.release();
+} catch (...) {
+    return nullptr;
+}
+
+void* vla_diffusion_load(const char* model_dir) { return vla_diffusion_load_batch(model_dir, 1); }
+
+void vla_diffusion_free(void* h) { delete static_cast<DpPolicy*>(h); }
+
+#define VSB_DP_GET(name, expr)                          \
+    int32_t vla_diffusion_##name(void* h) {             \
+        if (!h) return VLA_ERR_ARG;                     \
+        const DpPolicy* m = static_cast<DpPolicy*>(h);  \
+        return static_cast<int32_t>(expr);              \
+    }
+VSB_DP_GET(chunk, m->config().n_action_steps)
+VSB_DP_GET(horizon, m->config().horizon)
+VSB_DP_GET(action_dim, m->config().action_dim)
+VSB_DP_GET(state_dim, m->config().state_dim)
+VSB_DP_GET(n_cams, m->config().n_cams)
+VSB_DP_GET(n_obs_steps, m->config().n_obs)
+VSB_DP_GET(img_h, m->config().img_h)
+VSB_DP_GET(img_w, m->config().img_w)
+VSB_DP_GET(num_steps, m->num_steps())
+VSB_DP_GET(is_ddim, m->config().ddim ? 1 : 0)
+VSB_DP_GET(kernels_per_step, m->kernels_per_step())
+VSB_DP_GET(int8_layers, m->int8_layers())
+#undef VSB_DP_GET
+
+int32_t vla_diffusion_predict_batch(void* h, int32_t batch, const uint8_t* frames, const float* state,
+                                    int32_t unnormalize, float* actions, const float* noise) try {
+    if (!h || !frames || !state || !actions) return VLA_ERR_ARG;
+    auto* m = static_cast<DpPolicy*>(h);
+    if (batch < 1 || batch > m->max_batch()) return VLA_ERR_SHAPE;
+    return status_of(m->predict(batch, frames, state, noise, unnormalize != 0, actions));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_diffusion_predict(void* h, const uint8_t* frames, const float* state, int32_t unnormalize,
+                              float* actions, const float* noise) {
+    return vla_diffusion_predict_batch(h, 1, frames, state, unnormalize, actions, noise);
+}
+
+int64_t vla_diffusion_global_cond(void* h, float* out, int64_t cap) try {
+    return h ? static_cast<DpPolicy*>(h)->global_cond(out, cap) : -1;
+} catch (...) {
+    return -1;
+}
+
+int64_t vla_diffusion_debug_map(void* h, float* out, int64_t cap) try {
+    return h ? static_cast<DpPolicy*>(h)->debug_map(out, cap) : -1;
+} catch (...) {
+    return -1;
+}
+
+int32_t vla_diffusion_device_buffers(void* h, uint8_t** frames, float** state, float** noise,
+                                     const float** actions) {
+    if (!h) return VLA_ERR_ARG;
+    auto* m = static_cast<DpPolicy*>(h);
+    if (frames) *frames = m->device_frames();
+    if (state) *state = m->device_state();
+    if (noise) *noise = m->device_noise();
+    if (actions) *actions = m->device_actions();
+    return VLA_OK;
+}
+
+int32_t vla_diffusion_enqueue(void* h, int32_t batch, void* stream, int32_t unnormalize) try {
+    if (!h) return VLA_ERR_ARG;
+    auto* m = static_cast<DpPolicy*>(h);
+    if (batch < 1 || batch > m->max_batch()) return VLA_ERR_SHAPE;
+    return status_of(m->enqueue(batch, as_stream(stream), unnormalize != 0));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
 // --------------------------------------------------------------- op level
 
 int64_t vla_cuda_i8_ld(int32_t K) { return K > 0 ? ld16(K) : 0; }
@@ -198,6 +286,40 @@ int32_t vla_cuda_gemm_i8(void* out, int64_t ldo, const int8_t* xq, int64_t ldx, 
     a.amax = amax;
     a.amax_rows = amax_rows > 0 ? amax_rows : 1;
     a.force_simt = force_simt != 0;
+    return status_of(vsb::gemm_i8(a, as_stream(stream)));
+}
+
+int32_t vla_cuda_gemm_i8_splitk(void* out, int64_t ldo, const int8_t* xq, int64_t ldx, const float* ascale,
+                                const int8_t* Wq, int64_t ldw, const float* wscale, const float* bias,
+                                const float* res, int64_t ldr, int32_t M, int32_t N, int32_t K, int32_t mode,
+                                int32_t* ws, int64_t ws_elems, uint32_t* counters, int32_t n_counters,
+                                void* stream) {
+    if (!out || !xq || !Wq || M <= 0 || M > 128 || N <= 0 || !k_ok(K) || ldx < K || ldw < K || ldo < N ||
+        !ws || ws_elems <= 0 || !counters || n_counters <= 0)
+        return VLA_ERR_ARG;
+    if (!(mode & VLA_EPI_ACC) && (!ascale || !wscale)) return VLA_ERR_ARG;
+    if ((mode & (VLA_EPI_ADD | VLA_EPI_ADD_RELU)) && (!res || ldr < N)) return VLA_ERR_ARG;
+    if (mode & ~(VLA_EPI_RELU | VLA_EPI_ADD | VLA_EPI_ADD_RELU | VLA_EPI_ACC)) return VLA_ERR_ARG;
+    vsb::GemmI8Args a;
+    a.A = xq;
+    a.lda = ldx;
+    a.B = Wq;
+    a.ldb = ldw;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.out = out;
+    a.ldo = ldo;
+    a.ascale = ascale;
+    a.wscale = wscale;
+    a.bias = bias;
+    a.res = res;
+    a.ldr = ldr;
+    a.mode = mode;
+    a.splitk_ws = ws;
+    a.splitk_ws_elems = ws_elems;
+    a.splitk_counters = counters;
+    a.splitk_counters_n = n_counters;
     return status_of(vsb::gemm_i8(a, as_stream(stream)));
 }
 

@@ -1,0 +1,907 @@
+// Diffusion Policy kernels: observation preprocessing, GroupNorm over batched
+// samples with fused Mish / FiLM / residual / ReLU epilogues, the 1D im2col of
+// the conditional U-Net fused with its per-row int8 quantization, the cond
+// encoder input, and the DDIM / DDPM reverse step. Compiled into kernels.cu
+// after nn.cu and lm_ops.cu (ref_exp, nn_row_scale, nn_q8, warp_max_f).
+//
+// Arithmetic follows the reference build (-mavx2 -mfma -ffp-contract=fast):
+// the contractions below (fma in GroupNorm's apply, FiLM, the scheduler step
+// and the action unnormalization) are the ones its compiler emitted.
+#include "sm100.cuh"
+#include "launch.cuh"
+#include "dp.h"
+
+namespace vsb {
+
+namespace {
+
+// Mish as the reference's 8-lane body (src/hal/common/eltwise.cpp:224-243):
+// v * m / (m + 2), m = e(e + 2), e = exp(min(v, 20)) with its Cephes exp.
+__device__ __forceinline__ float mish_lanes(float v) {
+    const float e = ref_exp(fminf(v, 20.0f));
+    const float m = __fmul_rn(e, __fadd_rn(e, 2.0f));
+    return __fmul_rn(v, __fdiv_rn(m, __fadd_rn(m, 2.0f)));
+}
+
+// The host C library's expf (glibc 2.39 on x86-64, the build the reference
+// links), restated from its published algorithm (ARM optimized-routines expf):
+// x*32/ln2 = k + r rounded with the 1.5*2^52 shift, exp(x) = 2^(k/32) *
+// (1 + c2 r + c1 r^2 + c0 r^3) in double, the 2^(i/32) table entries the
+// correctly rounded doubles with the exponent bits of i/32 removed, and the
+// fused multiply-adds of its FMA build. Identical to that expf on every
+// float (checked over all 2^32 inputs against the host library); the
+// spatial softmax needs it because its output feeds int8 quantizers, where
+// one ulp can move a rounding decision.
+__constant__ unsigned long long kExp2Tab32[32] = {
+    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
+    0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
+    0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
+    0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL,
+    0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL,
+    0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
+    0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
+    0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
+
+__device__ __forceinline__ float libm_expf(float x) {
+    if (x != x) return x + x;
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   // overflow: +inf
+    if (x < -0x1.9fe368p6f) return 0.0f;                        // underflow
+    const double xd = static_cast<double>(x);
+    const double inv_ln2_32 = 0x1.71547652b82fep+5, shift = 0x1.8p+52;
+    double kd = __fma_rn(inv_ln2_32, xd, shift);
+    const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2_32, xd, -kd);
+    const double s = __longlong_as_double(static_cast<long long>(kExp2Tab32[ki & 31] + (ki << 47)));
+    const double z = __fma_rn(0x1.c6af84b912394p-20, r, 0x1.ebfce50fac4f3p-13);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(0x1.62e42ff0c52d6p-6, r, 1.0);
+    y = __fma_rn(z, r2, y);
+    return __double2float_rn(__dmul_rn(y, s));
+}
+
+__device__ __forceinline__ float block_max_256(float v, float* sh) {
+    v = warp_max_f(v);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+        m = warp_max_f(m);
+        if (threadIdx.x == 0) sh[0] = m;
+    }
+    __syncthreads();
+    const float r = sh[0];
+    __syncthreads();
+    return r;
+}
+
+__device__ __forceinline__ double block_sum_d(double v, double* sh) {
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double s = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, off));
+        if (threadIdx.x == 0) sh[0] = s;
+    }
+    __syncthreads();
+    const double r = sh[0];
+    __syncthreads();
+    return r;
+}
+
+long long grid_cap(long long n, int threads, long long cap) {
+    long long b = (n + threads - 1) / threads;
+    if (b < 1) b = 1;
+    return b > cap ? cap : b;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ preprocessing
+__global__ void dp_preprocess_kernel(const uint8_t* __restrict__ frames, int B, int S, int N, int H, int W, int top,
+                                     int left, int oh, int ow, const float* __restrict__ mean,
+                                     const float* __restrict__ stdv, float eps, float* __restrict__ out,
+                                     unsigned int* __restrict__ amax, int Fr, long long run_stride) {
+    pdl_wait();     // the previous step may still read these buffers
+    pdl_trigger();
+    const int i = blockIdx.y;            // input frame (b, s, c)
+    const int c = i % N, bs = i / N;
+    const int o = c * (B * S) + bs;      // camera-major output frame
+    const uint8_t* src = frames + (long long)i * H * W * 3;
+    float* dst = out + (long long)o * oh * ow * 3;
+    float mu[3], den[3];
+    #pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+        mu[ch] = mean[c * 3 + ch];
+        den[ch] = __fadd_rn(stdv[c * 3 + ch], eps);
+    }
+    float bmax = 0.0f;
+    const int npx = oh * ow;
+    for (int px = blockIdx.x * blockDim.x + threadIdx.x; px < npx; px += gridDim.x * blockDim.x) {
+        const int y = px / ow, x = px - y * ow;
+        const uint8_t* s = src + ((long long)(y + top) * W + left + x) * 3;
+        #pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            const float v = __fdiv_rn(__fsub_rn(__fdiv_rn(i2f_small(s[ch]), 255.0f), mu[ch]), den[ch]);
+            dst[3 * px + ch] = v;
+            bmax = fmaxf(bmax, fabsf(v));
+        }
+    }
+    __shared__ float sh[32];
+    bmax = block_max_256(bmax, sh);
+    if (threadIdx.x == 0 && amax) atomicMax(&amax[(long long)(o / Fr) * run_stride + o % Fr], __float_as_uint(bmax));
+}
+
+cudaError_t dp_preprocess(const uint8_t* frames, int B, int S, int N, int H, int W, int top, int left, int oh, int ow,
+                          const float* mean, const float* stdv, float eps, float* out, unsigned int* amax, int Fr,
+                          long long run_stride, cudaStream_t st) {
+    if (B <= 0 || S <= 0 || N <= 0 || oh <= 0 || ow <= 0 || top < 0 || left < 0 || top + oh > H || left + ow > W ||
+        (long long)B * S * N > 65535 || Fr <= 0)
+        return cudaErrorInvalidValue;
+    const long long bx = grid_cap((long long)oh * ow, 256, 64);
+    const cudaError_t e = launch_k(dp_preprocess_kernel, dim3((unsigned)bx, (unsigned)(B * S * N)), 256, 0, st, frames,
+                                   B, S, N, H, W, top, left, oh, ow, mean, stdv, eps, out, amax, Fr, run_stride);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- GroupNorm
+// Block = one (group, sample). Per channel: shift K = its first pixel, S1 =
+// sum(x - K), S2 = sum((x - K)^2) in double over pixel slices, then the slices
+// in order; per group: mean = sum(S1 + np*K)/n, ss = sum(S2 + 2dk*S1 +
+// np*dk^2) (dk = K - mean) as block reductions, inv = 1/sqrt(ss/n + eps);
+// A = inv*scale, B = bias - mean*inv*scale (the reference's formulas,
+// src/hal/common/conv.cpp:236-301). The sums are regrouped for parallelism;
+// in double that moves A and B by far less than a float ulp.
+__global__ void __launch_bounds__(256)
+gn_affine_kernel(const float* __restrict__ x, int npx, int C, long long ld, int groups, float eps,
+                 const float* __restrict__ scale, const float* __restrict__ bias, float* __restrict__ A,
+                 float* __restrict__ B) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    extern __shared__ double gsm[];
+    __shared__ double red[32];
+    const int g = blockIdx.x, f = blockIdx.y;
+    const int gc = C / groups, c0 = g * gc;
+    const int nsl = gc >= 256 ? 1 : 256 / gc;       // pixel slices per channel
+    double* p1 = gsm;                                // [nsl][gc]
+    double* p2 = gsm + (size_t)nsl * gc;
+    const float* xf = x + (long long)f * npx * ld + c0;
+    for (int it = threadIdx.x; it < gc * nsl; it += blockDim.x) {
+        const int cl = it % gc, sl = it / gc;
+        const double K = (double)xf[cl];
+        double s1 = 0.0, s2 = 0.0;
+        for (int p = sl; p < npx; p += nsl) {
+            const double d = __dsub_rn((double)xf[(long long)p * ld + cl], K);
+            s1 = __dadd_rn(s1, d);
+            s2 = __fma_rn(d, d, s2);
+        }
+        p1[it] = s1;
+        p2[it] = s2;
+    }
+    __syncthreads();
+    const double np = (double)npx, n = np * gc;
+    double t1 = 0.0;
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        double s1 = p1[cl], s2 = p2[cl];
+        for (int sl = 1; sl < nsl; ++sl) {
+            s1 = __dadd_rn(s1, p1[sl * gc + cl]);
+            s2 = __dadd_rn(s2, p2[sl * gc + cl]);
+        }
+        p1[cl] = s1;
+        p2[cl] = s2;
+        t1 = __dadd_rn(t1, __fma_rn(np, (double)xf[cl], s1));
+    }
+    const double mean = __ddiv_rn(block_sum_d(t1, red), n);
+    double t2 = 0.0;
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        const double dk = __dsub_rn((double)xf[cl], mean);
+        const double t = __fma_rn(__dmul_rn(2.0, dk), p1[cl], p2[cl]);
+        t2 = __dadd_rn(t2, __fma_rn(__dmul_rn(np, dk), dk, t));
+    }
+    const double ss = block_sum_d(t2, red);
+    const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, n), (double)eps)));
+    const double mi = __dmul_rn(mean, inv);
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        const int c = c0 + cl;
+        A[(long long)f * C + c] = (float)__dmul_rn(inv, (double)scale[c]);
+        B[(long long)f * C + c] = (float)__fma_rn(-mi, (double)scale[c], (double)bias[c]);
+    }
+}
+
+cudaError_t gn_affine(const float* x, int F, int npx, int C, long long ld, int groups, float eps, const float* scale,
+                      const float* bias, float* A, float* B, cudaStream_t st) {
+    if (F <= 0 || npx <= 0 || C <= 0 || groups <= 0 || C % groups || ld < C || F > 65535) return cudaErrorInvalidValue;
+    const int gc = C / groups;
+    const int nsl = gc >= 256 ? 1 : 256 / gc;
+    const size_t smem = (size_t)2 * nsl * gc * sizeof(double);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(gn_affine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    const cudaError_t e = launch_k(gn_affine_kernel, dim3((unsigned)groups, (unsigned)F), 256, smem, st, x, npx, C, ld,
+                                   groups, eps, scale, bias, A, B);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256)
+gn_apply_kernel(const float* __restrict__ x, const float* __restrict__ A, const float* __restrict__ B,
+                float* __restrict__ out, int npx, int C, long long ld, int epi, const float* __restrict__ res,
+                unsigned int* __restrict__ amax) {
+    pdl_wait();     // A / B and x come from earlier kernels in the stream
+    pdl_trigger();
+    const int f = blockIdx.y;
+    const long long base = (long long)f * npx * ld;
+    const float* Af = A + (long long)f * C;
+    const float* Bf = B + (long long)f * C;
+    const long long total = (long long)npx * C;
+    float bmax = 0.0f;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const int p = static_cast<int>(e / C), c = static_cast<int>(e - (long long)p * C);
+        const long long i = base + (long long)p * ld + c;
+        float v = __fmaf_rn(x[i], Af[c], Bf[c]);
+        if (epi & kGnMish) v = mish_lanes(v);
+        if (epi & kGnAdd) {
+            v = __fadd_rn(v, res[i]);
+            if (epi & kGnRelu) v = v > 0.0f ? v : 0.0f;        // relu(c + identity), resnet block tail
+        } else if (epi & kGnRelu) {
+            v = v < 0.0f ? 0.0f : v;                           // groupnorm(..., fuse_relu)
+        }
+        out[i] = v;
+        bmax = fmaxf(bmax, fabsf(v));
+    }
+    if (amax) {
+        __shared__ float sh[32];
+        bmax = block_max_256(bmax, sh);
+        if (threadIdx.x == 0) atomicMax(&amax[f], __float_as_uint(bmax));
+    }
+}
+
+cudaError_t gn_apply(const float* x, const float* A, const float* B, float* out, int F, int npx, int C, long long ld,
+                     int epi, const float* res, unsigned int* amax, cudaStream_t st) {
+    if (F <= 0 || npx <= 0 || C <= 0 || ld < C || F > 65535 || ((epi & kGnAdd) && !res)) return cudaErrorInvalidValue;
+    const long long bx = grid_cap((long long)npx * C, 256, (148 * 8 + F - 1) / F);
+    const cudaError_t e = launch_k(gn_apply_kernel, dim3((unsigned)bx, (unsigned)F), 256, 0, st, x, A, B, out, npx, C,
+                                   ld, epi, res, amax);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// --------------------------------------------------- 1D im2col + quantize
+// Block = one output row (sample f, time ot): the k*C fp32 patch values are
+// formed once in shared memory (zero for taps outside [0, T)), then the row
+// absmax, scale and int8 codes exactly as quantize_act_i8. Q8 = false writes
+// the fp32 row to colf [F*Tout][k*C] instead (fp32 layers).
+template <bool Q8>
+__global__ void __launch_bounds__(256)
+im2col1d_kernel(const float* __restrict__ x, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
+                const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ film,
+                long long ld_film, int film_scale, int8_t* __restrict__ q, long long ldq,
+                float* __restrict__ scale, float* __restrict__ colf) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    extern __shared__ float row[];
+    __shared__ float sh[32];
+    const int r = blockIdx.x;
+    const int f = r / Tout, ot = r - f * Tout;
+    const int K = k * C;
+    const float* xf = x + (long long)f * T * ldx;
+    const float* Af = A ? A + (long long)f * C : nullptr;
+    const float* Bf = B ? B + (long long)f * C : nullptr;
+    const float* ff = film ? film + (long long)f * ld_film : nullptr;
+    float m = 0.0f;
+    for (int e = threadIdx.x; e < K; e += blockDim.x) {
+        const int kt = e / C, c = e - kt * C;
+        const int t = ot * stride - pad + kt;
+        float v = 0.0f;
+        if (t >= 0 && t < T) {
+            v = xf[(long long)t * ldx + c];
+            if (Af) {
+                v = mish_lanes(__fmaf_rn(v, Af[c], Bf[c]));
+                if (ff) v = film_scale ? __fmaf_rn(ff[c], v, ff[C + c]) : __fadd_rn(v, ff[c]);
+            }
+        }
+        if (!Q8) {
+            colf[(long long)r * K + e] = v;
+            continue;
+        }
+        row[e] = v;
+        m = fmaxf(m, fabsf(v));
+    }
+    if (!Q8) return;
+    m = block_max_256(m, sh);    // (its barriers also order the row writes)
+    const float s = nn_row_scale(m), inv = __fdiv_rn(1.0f, s);
+    int8_t* qr = q + (long long)r * ldq;
+    for (int e4 = 4 * threadIdx.x; e4 < ldq; e4 += 4 * blockDim.x) {
+        char4 o;
+        o.x = e4 + 0 < K ? nn_q8(row[e4 + 0], inv) : 0;
+        o.y = e4 + 1 < K ? nn_q8(row[e4 + 1], inv) : 0;
+        o.z = e4 + 2 < K ? nn_q8(row[e4 + 2], inv) : 0;
+        o.w = e4 + 3 < K ? nn_q8(row[e4 + 3], inv) : 0;
+        *reinterpret_cast<char4*>(qr + e4) = o;
+    }
+    if (threadIdx.x == 0) scale[r] = s;
+}
+
+cudaError_t im2col1d_q8(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
+                        const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
+                        int8_t* q, long long ldq, float* scale, cudaStream_t st) {
+    const long long K = (long long)k * C;
+    if (F <= 0 || T <= 0 || C <= 0 || ldx < C || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0 || ldq < K ||
+        (ldq & 15) || (reinterpret_cast<uintptr_t>(q) & 15) || (A && !B) || (film && !A) ||
+        (long long)F * Tout > 2147483647LL)
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)K * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(im2col1d_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    const cudaError_t e = launch_k(im2col1d_kernel<true>, (unsigned)(F * Tout), 256, smem, st, x, T, C, ldx, k, stride,
+                                   pad, Tout, A, B, film, ld_film, film_scale ? 1 : 0, q, ldq, scale,
+                                   static_cast<float*>(nullptr));
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
+                          const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
+                          float* colf, cudaStream_t st) {
+    if (F <= 0 || T <= 0 || C <= 0 || ldx < C || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0 || (A && !B) ||
+        (film && !A) || (long long)F * Tout > 2147483647LL)
+        return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(im2col1d_kernel<false>, (unsigned)(F * Tout), 256, 0, st, x, T, C, ldx, k, stride,
+                                   pad, Tout, A, B, film, ld_film, film_scale ? 1 : 0, static_cast<int8_t*>(nullptr),
+                                   0LL, static_cast<float*>(nullptr), colf);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------ conv_transpose1d
+// Per output (sample, ot, co): bias, then x[t][ci] * W[ci][kt][co] for kt from
+// k-1 down to 0, ci in order, zero inputs skipped (src/hal/common/conv.cpp:349-395).
+// That order is kept: every output is one fma chain. CTA = 32 output channels x
+// 8 thread rows, a thread owns outputs ot = ty + 8i (OPT independent chains);
+// the chains advance tap slot by tap slot (the j-th valid kt of each output,
+// descending), and inside a slot over 32-channel chunks of ci whose x and W
+// values are staged in shared memory, the next chunk's loads issued before
+// the current chunk's fmas. Optional per-row absmax of the output (atomicMax).
+constexpr int kCtCo = 32, kCtCi = 32, kCtRows = 8, kCtMaxK = 4;
+
+template <int OPT>
+__global__ void __launch_bounds__(256)
+conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                              const float* __restrict__ bias, float* __restrict__ out, int T, int Cin, int Cout,
+                              int k, int stride, int pad, int Tout, int slots, unsigned int* __restrict__ rowmax) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    extern __shared__ float ct_smem[];
+    float* sW = ct_smem;                          // [2][kCtCi][k][kCtCo]
+    float* sx = ct_smem + 2 * kCtCi * k * kCtCo;  // [2][T][kCtCi]
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int co0 = blockIdx.x * kCtCo, f = blockIdx.y;
+    const int co = co0 + tx;
+    const float* xf = x + (long long)f * T * Cin;
+    float acc[OPT];
+    int ot[OPT];
+    #pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+        ot[i] = ty + kCtRows * i;
+        acc[i] = (bias && co < Cout) ? bias[co] : 0.0f;
+    }
+    const int nchunk = (Cin + kCtCi - 1) / kCtCi;
+    const int wlen = kCtCi * k * kCtCo, xlen = T * kCtCi;
+    for (int j = 0; j < slots; ++j) {
+        // this slot's tap and input row per output (-1: none)
+        int kt_i[OPT], t_i[OPT];
+        #pragma unroll
+        for (int i = 0; i < OPT; ++i) {
+            kt_i[i] = -1;
+            t_i[i] = 0;
+            if (ot[i] >= Tout) continue;
+            int seen = 0;
+            for (int kt = k - 1; kt >= 0; --kt) {
+                const int num = ot[i] + pad - kt;
+                if (num < 0 || num % stride) continue;
+                const int t = num / stride;
+                if (t >= T) continue;
+                if (seen++ == j) { kt_i[i] = kt; t_i[i] = t; break; }
+            }
+        }
+        // chunk 0 into buffer 0
+        for (int e = threadIdx.x; e < wlen; e += blockDim.x) {
+            const int cc = e % kCtCo, r = e / kCtCo, kt = r % k, ci = r / k;
+            sW[e] = (ci < Cin && co0 + cc < Cout) ? W[((long long)ci * k + kt) * Cout + co0 + cc] : 0.0f;
+        }
+        for (int e = threadIdx.x; e < xlen; e += blockDim.x) {
+            const int ci = e % kCtCi, t = e / kCtCi;
+            sx[e] = ci < Cin ? xf[(long long)t * Cin + ci] : 0.0f;
+        }
+        __syncthreads();
+        for (int c = 0; c < nchunk; ++c) {
+            const int cur = c & 1, nxt = cur ^ 1;
+            // the next chunk's values in flight while this chunk computes
+            constexpr int kPre = (kCtCi * kCtMaxK * kCtCo + 255) / 256;
+            float wv[kPre], xv[4];
+            const bool more = c + 1 < nchunk;
+            const int ci1 = (c + 1) * kCtCi;
+            if (more) {
+                #pragma unroll
+                for (int u = 0; u < kPre; ++u) {
+                    const int e = threadIdx.x + u * 256;
+                    wv[u] = 0.0f;
+                    if (e < wlen) {
+                        const int cc = e % kCtCo, r = e / kCtCo, kt = r % k, ci = ci1 + r / k;
+                        if (ci < Cin && co0 + cc < Cout) wv[u] = W[((long long)ci * k + kt) * Cout + co0 + cc];
+                    }
+                }
+                #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = threadIdx.x + u * 256;
+                    xv[u] = 0.0f;
+                    if (e < xlen) {
+                        const int ci = ci1 + e % kCtCi, t = e / kCtCi;
+                        if (ci < Cin) xv[u] = xf[(long long)t * Cin + ci];
+                    }
+                }
+            }
+            const float* w = sW + cur * wlen;
+            const float* xs = sx + cur * xlen;
+            const int cmax = min(kCtCi, Cin - c * kCtCi);
+            #pragma unroll
+            for (int i = 0; i < OPT; ++i) {
+                if (kt_i[i] < 0) continue;
+                const float* xr = xs + t_i[i] * kCtCi;
+                const float* wr = w + kt_i[i] * kCtCo + tx;
+                for (int ci = 0; ci < cmax; ++ci) {
+                    const float v = xr[ci];
+                    if (v == 0.0f) continue;
+                    acc[i] = __fmaf_rn(v, wr[ci * k * kCtCo], acc[i]);
+                }
+            }
+            if (more) {
+                float* wn = sW + nxt * wlen;
+                float* xn = sx + nxt * xlen;
+                #pragma unroll
+                for (int u = 0; u < kPre; ++u) {
+                    const int e = threadIdx.x + u * 256;
+                    if (e < wlen) wn[e] = wv[u];
+                }
+                #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = threadIdx.x + u * 256;
+                    if (e < xlen) xn[e] = xv[u];
+                }
+            }
+            __syncthreads();
+        }
+    }
+    #pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+        if (ot[i] >= Tout) continue;
+        if (co < Cout) out[((long long)f * Tout + ot[i]) * Cout + co] = acc[i];
+        if (rowmax) {
+            float m = co < Cout ? fabsf(acc[i]) : 0.0f;
+            m = warp_max_f(m);
+            if (tx == 0) atomicMax(&rowmax[f * Tout + ot[i]], __float_as_uint(m));
+        }
+    }
+}
+
+template <int OPT>
+cudaError_t launch_convt(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
+                         int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax, cudaStream_t st) {
+    const int slots = (k + stride - 1) / stride;
+    const size_t smem = sizeof(float) * (2 * kCtCi * k * kCtCo + 2 * T * kCtCi);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(conv_transpose1d_tiled_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        attr = true;
+    }
+    return launch_k(conv_transpose1d_tiled_kernel<OPT>, dim3((unsigned)((Cout + kCtCo - 1) / kCtCo), (unsigned)F), 256,
+                    smem, st, x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
+}
+
+cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
+                               int Cout, int k, int stride, int pad, unsigned int* rowmax, cudaStream_t st) {
+    const int Tout = (T - 1) * stride - 2 * pad + k;
+    // staged rows: T * kCtCi x values in at most 4 loads per thread; k <= kCtMaxK taps
+    if (F <= 0 || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || k > kCtMaxK || stride <= 0 || pad < 0 || Tout <= 0 ||
+        Tout > 8 * kCtRows || T * kCtCi > 4 * 256 || F > 65535)
+        return cudaErrorInvalidValue;
+    cudaError_t e;
+    if (Tout <= kCtRows) e = launch_convt<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else if (Tout <= 2 * kCtRows) e = launch_convt<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else if (Tout <= 4 * kCtRows) e = launch_convt<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else e = launch_convt<8>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// --------------------------------------------------- U-Net GroupNorm + Mish
+// Block = one (group, sample) of x [F][T][C]: the group's statistics exactly
+// as gn_affine_kernel (per channel over the T time steps, then the group), then
+// v = mish(fma(x, A, B)) and the epilogue: FiLM fma(sc, v, bi) (film_scale) or
+// v + film (bias only), or + res; out may alias x. rowmax (optional): atomicMax
+// of each time step's |out| over this group's channels (the next conv's row
+// quantization reads it).
+__global__ void __launch_bounds__(256)
+unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float* __restrict__ scale,
+               const float* __restrict__ bias, int epi, const float* __restrict__ film, long long ld_film,
+               const float* res, float* out, unsigned int* __restrict__ rowmax) {
+    pdl_wait();     // x comes from the GEMM before
+    pdl_trigger();
+    extern __shared__ float ug_smem[];
+    __shared__ double red[32];
+    const int g = blockIdx.x, f = blockIdx.y;
+    const int gc = C / groups, c0 = g * gc;
+    float* sA = ug_smem;                                            // [gc]
+    float* sB = ug_smem + gc;                                       // [gc]
+    unsigned int* srm = reinterpret_cast<unsigned int*>(ug_smem + 2 * gc);   // [T]
+    const float* xf = x + (long long)f * T * C + c0;
+    const double np = (double)T, n = np * gc;
+    // per channel: shifted sums over the T steps (first step as the shift)
+    double t1 = 0.0;
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        const double K = (double)xf[cl];
+        double s1 = 0.0;
+        for (int p = 0; p < T; ++p) s1 = __dadd_rn(s1, __dsub_rn((double)xf[(long long)p * C + cl], K));
+        t1 = __dadd_rn(t1, __fma_rn(np, K, s1));
+    }
+    const double mean = __ddiv_rn(block_sum_d(t1, red), n);
+    double t2 = 0.0;
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        const double K = (double)xf[cl];
+        double s1 = 0.0, s2 = 0.0;
+        for (int p = 0; p < T; ++p) {
+            const double d = __dsub_rn((double)xf[(long long)p * C + cl], K);
+            s1 = __dadd_rn(s1, d);
+            s2 = __fma_rn(d, d, s2);
+        }
+        const double dk = __dsub_rn(K, mean);
+        const double t = __fma_rn(__dmul_rn(2.0, dk), s1, s2);
+        t2 = __dadd_rn(t2, __fma_rn(__dmul_rn(np, dk), dk, t));
+    }
+    const double ss = block_sum_d(t2, red);
+    const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, n), (double)eps)));
+    const double mi = __dmul_rn(mean, inv);
+    for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
+        sA[cl] = (float)__dmul_rn(inv, (double)scale[c0 + cl]);
+        sB[cl] = (float)__fma_rn(-mi, (double)scale[c0 + cl], (double)bias[c0 + cl]);
+    }
+    for (int p = threadIdx.x; p < T; p += blockDim.x) srm[p] = 0u;
+    __syncthreads();
+    const float* ff = film ? film + (long long)f * ld_film : nullptr;
+    for (int e = threadIdx.x; e < T * gc; e += blockDim.x) {
+        const int p = e / gc, cl = e - p * gc, c = c0 + cl;
+        const long long i = ((long long)f * T + p) * C + c;
+        float v = mish_lanes(__fmaf_rn(x[i], sA[cl], sB[cl]));
+        if (epi == kUgFilmScale) v = __fmaf_rn(ff[c], v, ff[C + c]);
+        else if (epi == kUgFilmBias) v = __fadd_rn(v, ff[c]);
+        else if (epi == kUgRes) v = __fadd_rn(v, res[i]);
+        out[i] = v;
+        if (rowmax) atomicMax(&srm[p], __float_as_uint(fabsf(v)));
+    }
+    if (rowmax) {
+        __syncthreads();
+        for (int p = threadIdx.x; p < T; p += blockDim.x)
+            if (srm[p]) atomicMax(&rowmax[f * T + p], srm[p]);
+    }
+}
+
+cudaError_t unet_gn(const float* x, int F, int T, int C, int groups, float eps, const float* scale,
+                    const float* bias, int epi, const float* film, long long ld_film, const float* res, float* out,
+                    unsigned int* rowmax, cudaStream_t st) {
+    if (F <= 0 || T <= 0 || C <= 0 || groups <= 0 || C % groups || F > 65535 ||
+        ((epi == kUgFilmScale || epi == kUgFilmBias) && !film) || (epi == kUgRes && !res))
+        return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (2 * (size_t)(C / groups) + T);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(unet_gn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    const cudaError_t e = launch_k(unet_gn_kernel, dim3((unsigned)groups, (unsigned)F), 256, smem, st, x, T, C, groups,
+                                   eps, scale, bias, epi, film, ld_film, res, out, rowmax);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ------------------------------------------- 1D im2col + row quantization
+// Thread = 4 output bytes of one im2col row (sample f, time ot). The row's
+// absmax is the max of its taps' per-time-step absmax (rowmax [F][T], float
+// bits; zero taps add nothing), so every thread forms its row scale from at
+// most k values and quantizes its 4 elements independently: the same int8
+// codes and scale as quantize_act_i8 of the fp32 im2col row. rowmax may be null
+// for narrow rows (k*C <= 64): the thread then scans the row itself.
+__global__ void __launch_bounds__(256)
+im2col1d_q8w_kernel(const float* __restrict__ x, int T, int C, int k, int stride, int pad, int Tout,
+                    const unsigned int* __restrict__ rowmax, int8_t* __restrict__ q, long long ldq,
+                    float* __restrict__ scale, long long rows) {
+    pdl_wait();     // x and rowmax come from earlier kernels in the stream
+    pdl_trigger();
+    const long long g4n = ldq >> 2, total = rows * g4n;
+    const int K = k * C;
+    for (long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x; tid < total;
+         tid += (long long)gridDim.x * blockDim.x) {
+        const long long r = tid / g4n;
+        const int g4 = static_cast<int>(tid - r * g4n);
+        const int f = static_cast<int>(r / Tout), ot = static_cast<int>(r - (long long)f * Tout);
+        const float* xf = x + (long long)f * T * C;
+        float m = 0.0f;
+        if (rowmax) {
+            unsigned int mb = 0u;
+            for (int kt = 0; kt < k; ++kt) {
+                const int t = ot * stride - pad + kt;
+                if (t >= 0 && t < T) mb = max(mb, rowmax[f * T + t]);
+            }
+            m = __uint_as_float(mb);
+        } else {
+            for (int e = 0; e < K; ++e) {
+                const int kt = e / C, t = ot * stride - pad + kt;
+                if (t >= 0 && t < T) m = fmaxf(m, fabsf(xf[(long long)t * C + (e - kt * C)]));
+            }
+        }
+        const float s = nn_row_scale(m), inv = __fdiv_rn(1.0f, s);
+        if (g4 == 0) scale[r] = s;
+        int8_t b[4];
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = 4 * g4 + u;
+            float v = 0.0f;
+            if (e < K) {
+                const int kt = e / C, t = ot * stride - pad + kt;
+                if (t >= 0 && t < T) v = xf[(long long)t * C + (e - kt * C)];
+            }
+            b[u] = e < K ? nn_q8(v, inv) : 0;
+        }
+        *reinterpret_cast<char4*>(q + r * ldq + 4 * g4) = make_char4(b[0], b[1], b[2], b[3]);
+    }
+}
+
+cudaError_t im2col1d_q8w(const float* x, int F, int T, int C, int k, int stride, int pad, int Tout,
+                         const unsigned int* rowmax, int8_t* q, long long ldq, float* scale, cudaStream_t st) {
+    if (F <= 0 || T <= 0 || C <= 0 || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0 || ldq < (long long)k * C ||
+        (ldq & 15) || (reinterpret_cast<uintptr_t>(q) & 15) || (!rowmax && (long long)k * C > 64))
+        return cudaErrorInvalidValue;
+    const long long rows = (long long)F * Tout;
+    const cudaError_t e = launch_k(im2col1d_q8w_kernel, (unsigned)grid_cap(rows * (ldq >> 2), 256, 148 * 8), 256, 0,
+                                   st, x, T, C, k, stride, pad, Tout, rowmax, q, ldq, scale, rows);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// cat [F*T][C1 + C2] = [a | b] per row, with the row's absmax (float bits) into rowmax.
+__global__ void __launch_bounds__(256)
+concat_rows_kernel(const float* __restrict__ a, int C1, const float* __restrict__ b, int C2, float* __restrict__ cat,
+                   unsigned int* __restrict__ rowmax) {
+    pdl_wait();     // inputs come from earlier kernels in the stream
+    pdl_trigger();
+    __shared__ float sh[32];
+    const long long r = blockIdx.x;
+    const int Cc = C1 + C2;
+    float m = 0.0f;
+    for (int c = threadIdx.x; c < Cc; c += blockDim.x) {
+        const float v = c < C1 ? a[r * C1 + c] : b[r * C2 + (c - C1)];
+        cat[r * Cc + c] = v;
+        m = fmaxf(m, fabsf(v));
+    }
+    m = block_max_256(m, sh);
+    if (threadIdx.x == 0 && rowmax) rowmax[r] = __float_as_uint(m);
+}
+
+// --------------------------------------------------- cond encoder input
+// gm = mish([stepfeat | gcond]) per step and query. Mish's 8-lane body covers
+// the first CD - CD % 8 elements (mish_lanes, exact); the last CD % 8 are the
+// reference's scalar libm tail, whose values arrive precomputed in tail
+// [B][CD % 8] (evaluated with the host's libm, see DpPolicy::forward).
+__global__ void dp_cond_input_kernel(const float* __restrict__ stepfeat, int n_steps, int D,
+                                     const float* __restrict__ gcond, const float* __restrict__ tail, int B, int CD,
+                                     float* __restrict__ gm) {
+    pdl_wait();     // gcond comes from the encoders of this step
+    pdl_trigger();
+    const long long total = (long long)n_steps * B * CD;
+    const int nt = CD % 8, lanes_end = CD - nt;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / CD;
+        const int j = static_cast<int>(i - r * CD);
+        const int step = static_cast<int>(r / B), b = static_cast<int>(r - (long long)step * B);
+        if (j < lanes_end) {
+            const float v = j < D ? stepfeat[(long long)step * D + j] : gcond[(long long)b * (CD - D) + (j - D)];
+            gm[i] = mish_lanes(v);
+        } else {
+            gm[i] = tail[(long long)b * nt + (j - lanes_end)];
+        }
+    }
+}
+
+cudaError_t dp_cond_input(const float* stepfeat, int n_steps, int D, const float* gcond, const float* tail, int B,
+                          int CD, float* gm, cudaStream_t st) {
+    if (n_steps <= 0 || D <= 0 || B <= 0 || CD <= D || CD - CD % 8 < D || (CD % 8 && !tail))
+        return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(dp_cond_input_kernel, (unsigned)grid_cap((long long)n_steps * B * CD, 256, 148 * 4),
+                                   256, 0, st, stepfeat, n_steps, D, gcond, tail, B, CD, gm);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------- step prologue
+__global__ void dp_prologue_kernel(unsigned int* __restrict__ zero, int n_zero, const float* __restrict__ state, int B,
+                                   int S, int sd, const float* __restrict__ smin, const float* __restrict__ smax,
+                                   float eps, float* __restrict__ gcond, int per_step, const float* __restrict__ noise,
+                                   long long noise_stride, int HA, float* __restrict__ sample) {
+    pdl_wait();     // the previous step may still read these buffers
+    pdl_trigger();
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = tid; i < n_zero; i += stride) zero[i] = 0u;
+    // 2 (state - min) / d - 1, d = max - min (eps when 0): diffusion_model.cpp:203-207
+    for (long long i = tid; i < (long long)B * S * sd; i += stride) {
+        const int j = static_cast<int>(i % sd);
+        const long long bs = i / sd;
+        const int s = static_cast<int>(bs % S), b = static_cast<int>(bs / S);
+        const float den = __fsub_rn(smax[j], smin[j]);
+        const float d = den == 0.0f ? eps : den;
+        const float t = __fsub_rn(state[i], smin[j]);
+        gcond[(long long)b * S * per_step + (long long)s * per_step + j] =
+            __fsub_rn(__fdiv_rn(__fadd_rn(t, t), d), 1.0f);
+    }
+    for (long long i = tid; i < (long long)B * HA; i += stride) {
+        const long long b = i / HA;
+        sample[i] = noise[b * noise_stride + (i - b * HA)];
+    }
+}
+
+cudaError_t dp_prologue(unsigned int* zero, int n_zero, const float* state, int B, int S, int sd, const float* smin,
+                        const float* smax, float eps, float* gcond, int per_step, const float* noise,
+                        long long noise_stride, int HA, float* sample, cudaStream_t st) {
+    if (B <= 0 || S <= 0 || sd <= 0 || HA <= 0) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(dp_prologue_kernel, 32, 256, 0, st, zero, n_zero, state, B, S, sd, smin, smax, eps,
+                                   gcond, per_step, noise, noise_stride, HA, sample);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------- reverse step
+__global__ void dp_sched_step_kernel(float* __restrict__ sample, const float* __restrict__ eps,
+                                     const float* __restrict__ noise, long long noise_stride, int HA, long long n,
+                                     DdStepConsts c) {
+    pdl_wait();     // eps comes from the U-Net's last kernel
+    pdl_trigger();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const double s = (double)sample[i], e = (double)eps[i];
+        double x0 = __ddiv_rn(__fma_rn(-c.sqrt_bp, e, s), c.sqrt_ap);
+        if (c.clip) {
+            x0 = (c.lo < x0) ? x0 : c.lo;    // std::max(lo, x0)
+            x0 = (x0 < c.hi) ? x0 : c.hi;    // std::min(hi, .)
+        }
+        double v;
+        if (!c.ddpm) {
+            v = __fma_rn(x0, c.a, __dmul_rn(c.b, e));
+        } else {
+            v = __fma_rn(x0, c.a, __dmul_rn(c.b, s));
+            if (noise) {
+                const long long b = i / HA;
+                v = __fma_rn(c.var, (double)noise[b * noise_stride + (i - b * HA)], v);
+            }
+        }
+        sample[i] = __double2float_rn(v);
+    }
+}
+
+cudaError_t dp_sched_step(float* sample, const float* eps, const float* noise, long long noise_stride, int B, int HA,
+                          const DdStepConsts& c, cudaStream_t st) {
+    if (B <= 0 || HA <= 0) return cudaErrorInvalidValue;
+    const long long n = (long long)B * HA;
+    const cudaError_t e = launch_k(dp_sched_step_kernel, (unsigned)grid_cap(n, 256, 148), 256, 0, st, sample, eps,
+                                   noise, noise_stride, HA, n, c);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ actions
+__global__ void dp_actions_kernel(const float* __restrict__ sample, int B, int horizon, int A, int start, int n_act,
+                                  const float* __restrict__ amin, const float* __restrict__ amax, float eps,
+                                  float* __restrict__ actions) {
+    pdl_wait();     // sample comes from the last reverse step
+    pdl_trigger();
+    const long long total = (long long)B * n_act * A;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int a = static_cast<int>(i % A);
+        const long long bt = i / A;
+        const int t = static_cast<int>(bt % n_act), b = static_cast<int>(bt / n_act);
+        const float s = sample[((long long)b * horizon + start + t) * A + a];
+        if (amin) {
+            const float den = __fsub_rn(amax[a], amin[a]);
+            const float d = den == 0.0f ? eps : den;
+            actions[i] = __fmaf_rn(__fmul_rn(__fadd_rn(s, 1.0f), 0.5f), d, amin[a]);
+        } else {
+            actions[i] = s;
+        }
+    }
+}
+
+cudaError_t dp_actions(const float* sample, int B, int horizon, int A, int start, int n_act, const float* amin,
+                       const float* amax, float eps, float* actions, cudaStream_t st) {
+    if (B <= 0 || A <= 0 || n_act <= 0 || start < 0 || start + n_act > horizon) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(dp_actions_kernel, (unsigned)grid_cap((long long)B * n_act * A, 256, 64), 256, 0,
+                                   st, sample, B, horizon, A, start, n_act, amin, amax, eps, actions);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------- spatial softmax
+// Per (frame, channel): max shift, then exp / sum / expected (x, y) in pixel
+// order with the coordinate products fused (src/hal/common/conv.cpp:397-422),
+// exp the host library's (libm_expf).
+__global__ void spatial_softmax_f_kernel(const float* __restrict__ x, const float* __restrict__ grid,
+                                         float* __restrict__ out, int F, int npx, int C) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)F * C) return;
+    const int f = static_cast<int>(i / C), c = static_cast<int>(i - (long long)f * C);
+    const float* xf = x + (long long)f * npx * C;
+    float m = -INFINITY;
+    for (int p = 0; p < npx; ++p) {
+        const float v = xf[(long long)p * C + c];
+        if (v > m) m = v;
+    }
+    float sum = 0.0f, ex = 0.0f, ey = 0.0f;
+    for (int p = 0; p < npx; ++p) {
+        const float e = libm_expf(__fsub_rn(xf[(long long)p * C + c], m));
+        sum = __fadd_rn(sum, e);
+        ex = __fmaf_rn(e, grid[2 * p], ex);
+        ey = __fmaf_rn(e, grid[2 * p + 1], ey);
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    out[(long long)f * 2 * C + 2 * c] = __fmul_rn(ex, inv);
+    out[(long long)f * 2 * C + 2 * c + 1] = __fmul_rn(ey, inv);
+}
+
+cudaError_t concat_channels(const float* a, int C1, const float* b, int C2, float* cat, int F, int T,
+                            unsigned int* rowmax, cudaStream_t st) {
+    if (F <= 0 || T <= 0 || C1 <= 0 || C2 <= 0 || (long long)F * T > 2147483647LL) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(concat_rows_kernel, (unsigned)(F * T), 256, 0, st, a, C1, b, C2, cat, rowmax);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+cudaError_t spatial_softmax_f(const float* x, const float* grid, float* out, int F, int npx, int C, cudaStream_t st) {
+    if (F <= 0 || npx <= 0 || C <= 0) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(spatial_softmax_f_kernel, (unsigned)(((long long)F * C + 127) / 128), 128, 0, st, x,
+                                   grid, out, F, npx, C);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+__global__ void relu_rows_kernel(float* __restrict__ x, int M, int N, long long ld) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    const long long total = (long long)M * N;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / N;
+        float* p = x + r * ld + (i - r * N);
+        const float v = *p;
+        *p = v < 0.0f ? 0.0f : v;   // tcpu::relu (src/hal/common/eltwise.cpp:209-215)
+    }
+}
+
+cudaError_t relu_rows(float* x, int M, int N, long long ld, cudaStream_t st) {
+    if (M <= 0 || N <= 0 || ld < N) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(relu_rows_kernel, (unsigned)grid_cap((long long)M * N, 256, 148), 256, 0, st, x, M,
+                                   N, ld);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+}  // namespace vsb

@@ -50,6 +50,7 @@ constexpr int kBM = 128;          // UMMA M (one TMEM lane per tile row)
 constexpr int kBK = 128;          // bytes of K per pipeline stage (one SW128 atom row)
 constexpr int kUmmaK = 32;        // K per tcgen05.mma kind::i8
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kMaxGlobalSplits = 64;   // K splits over independent CTAs (workspace reduction)
 
 struct EpiParams {
     void* out;                    // float* (or int32_t* with kEpiAcc)
@@ -76,6 +77,10 @@ struct EpiParams {
     // ascale is per frame.
     int conv_bw, conv_bh, conv_tx, conv_ty, conv_ho, conv_wo, conv_k, conv_pad, conv_cb;
     int conv_kw;                  // filter width (conv_k = height)
+    // split K over independent CTAs (w8a8_splitk_kernel<BN, true>): partial
+    // int32 tiles [tile][split][M][BN] in ws, arrivals counted per tile
+    int32_t* ws;
+    unsigned int* counters;
 };
 
 // Output row (index into out / res, and the absmax slot numerator) of tile
@@ -496,7 +501,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
 // epilogue as the persistent kernel (bit-identical outputs).
 //   warp 0 lane 0: TMA producer; warp 1: TMEM + MMA issuer;
 //   warps 2-9: TMEM -> shared partial tile, then the cross-CTA sum + epilogue.
-template <int BN>
+template <int BN, bool GLOBAL>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
@@ -521,11 +526,12 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
     unsigned int* s_amax = reinterpret_cast<unsigned int*>(tmem_slot + 2);   // [4]
+    volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 6);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int splits = gridDim.x;
-    const int rank = blockIdx.x;          // cluster (splits, 1, 1): rank in the cluster
+    const int rank = blockIdx.x;          // cluster (splits, 1, 1): rank in the cluster (GLOBAL: in the grid row)
     const int n_tn = (p.N + BN - 1) / BN;
     const int mt = blockIdx.y / n_tn, n0 = (blockIdx.y % n_tn) * BN;
     const int nkb = (p.K + kBK - 1) / kBK;
@@ -622,9 +628,30 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
     }
     tc_fence_before();
-    cluster_sync();      // every partial tile of the cluster is in shared memory
+    if (!GLOBAL) {
+        cluster_sync();      // every partial tile of the cluster is in shared memory
+    } else {
+        // the rows with an output go to this split's workspace slice; the CTA
+        // that arrives last for the tile (counter) sums the slices in phase 2
+        __syncthreads();
+        if (warp >= 2) {
+            int32_t* wsl = p.ws + ((long long)blockIdx.y * splits + rank) * p.M * BN;
+            for (int idx = threadIdx.x - 64; idx < kBM * kC4; idx += 256) {
+                const int r = idx / kC4, q = idx - r * kC4;
+                if (r >= p.M) break;
+                *reinterpret_cast<int4*>(wsl + (long long)r * BN + 4 * q) =
+                    *reinterpret_cast<const int4*>(part + r * kPS + 4 * q);
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) *s_last = atomicAdd(&p.counters[blockIdx.y], 1u) == static_cast<unsigned>(splits - 1);
+        __syncthreads();
+        if (*s_last) __threadfence();
+    }
 
     // ---- phase 2: sum the cluster's partials for rows rank, rank + splits, ...
+    // (GLOBAL: the last-arriving CTA sums every split's slice for all rows)
     if (warp >= 2) {
         const int et = threadIdx.x - 64;
         const int q = et % kC4, rsub = et / kC4;
@@ -649,15 +676,25 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (cur_key - key0 < 4u) atomicMax(&s_amax[cur_key - key0], __float_as_uint(cur_max));
             else atomicMax(&p.amax[cur_key], __float_as_uint(cur_max));
         };
-        for (int j = rsub; rank + splits * j < kBM; j += kRPP) {
-            const int r = rank + splits * j;
+        const int r_first = GLOBAL ? 0 : rank, r_step = GLOBAL ? 1 : splits;
+        const bool reduce_here = !GLOBAL || *s_last;
+        for (int j = rsub; reduce_here && r_first + r_step * j < kBM; j += kRPP) {
+            const int r = r_first + r_step * j;
             const int m = out_row(p, mt, r);
             if (m < 0 || n >= p.N) continue;
-            const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
             int4 sum = make_int4(0, 0, 0, 0);
-            for (int src = 0; src < splits; ++src) {
-                const int4 v = dsmem_ld_v4(dsmem_map(off, static_cast<uint32_t>(src)));
-                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            if (GLOBAL) {
+                const int32_t* src0 = p.ws + (long long)blockIdx.y * splits * p.M * BN + (long long)r * BN + 4 * q;
+                for (int src = 0; src < splits; ++src) {
+                    const int4 v = __ldcg(reinterpret_cast<const int4*>(src0 + (long long)src * p.M * BN));
+                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+                }
+            } else {
+                const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
+                for (int src = 0; src < splits; ++src) {
+                    const int4 v = dsmem_ld_v4(dsmem_map(off, static_cast<uint32_t>(src)));
+                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+                }
             }
             const int32_t a4[4] = {sum.x, sum.y, sum.z, sum.w};
             if (acc_mode) {
@@ -706,7 +743,11 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (et < 4 && s_amax[et] != 0u) atomicMax(&p.amax[key0 + et], s_amax[et]);
         }
     }
-    cluster_sync();      // no CTA leaves while another still reads its partial tile
+    if (!GLOBAL) {
+        cluster_sync();      // no CTA leaves while another still reads its partial tile
+    } else if (threadIdx.x == 0 && *s_last) {
+        p.counters[blockIdx.y] = 0u;     // ready for the next launch (stream-ordered after this one)
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, BN);
@@ -873,10 +914,10 @@ cudaError_t umma_ready() {
     static std::atomic<unsigned long long> done{0};
     return set_smem_attr_once(w8a8_umma_kernel<BN, KBB>, done);
 }
-template <int BN>
+template <int BN, bool GLOBAL = false>
 cudaError_t splitk_ready() {
     static std::atomic<unsigned long long> done{0};
-    return set_smem_attr_once(w8a8_splitk_kernel<BN>, done);
+    return set_smem_attr_once(w8a8_splitk_kernel<BN, GLOBAL>, done);
 }
 
 // Persistent launch: at most (SMs x resident CTAs) CTAs, each looping over
@@ -925,7 +966,7 @@ int splitk_max_clusters(int splits, int stages) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&v, w8a8_splitk_kernel<BN>, &cfg) != cudaSuccess || v <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&v, w8a8_splitk_kernel<BN, false>, &cfg) != cudaSuccess || v <= 0) {
         cudaGetLastError();
         return 0;
     }
@@ -950,8 +991,25 @@ cudaError_t launch_splitk(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     if (e != cudaSuccess) return e;
     const long long tiles = (long long)((p.N + BN - 1) / BN) * p.m_tiles;
     if (tiles > 65535 || splits < 2 || splits > 8) return cudaErrorInvalidValue;
-    e = launch_k_cluster(w8a8_splitk_kernel<BN>, dim3(splits, (unsigned)tiles), kThreads, dim3(splits, 1, 1),
+    e = launch_k_cluster(w8a8_splitk_kernel<BN, false>, dim3(splits, (unsigned)tiles), kThreads, dim3(splits, 1, 1),
                          splitk_smem_bytes(BN, stages), st, ta, tb, p, stages);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// Split-K over independent CTAs: grid (splits, tiles), no clusters; partial
+// tiles meet in the caller's workspace (p.ws / p.counters).
+template <int BN>
+cudaError_t launch_splitk_global(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int splits,
+                                 int stages, cudaStream_t st) {
+    cudaError_t e = splitk_ready<BN, true>();
+    if (e != cudaSuccess) return e;
+    const long long tiles = (long long)((p.N + BN - 1) / BN) * p.m_tiles;
+    if (tiles > 65535 || splits < 2 || splits > kMaxGlobalSplits || !p.ws || !p.counters || p.m_tiles != 1 ||
+        p.conv_bw)
+        return cudaErrorInvalidValue;
+    e = launch_k(w8a8_splitk_kernel<BN, true>, dim3(splits, (unsigned)tiles), kThreads, splitk_smem_bytes(BN, stages),
+                 st, ta, tb, p, stages);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -1041,6 +1099,18 @@ cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUten
     const EpiParams p = make_epi(a);
     const int bn = plan.bn;
     if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return cudaErrorInvalidValue;
+    if (plan.global) {
+        if (plan.stages < splitk_min_stages(bn) || plan.stages > splitk_max_stages(bn)) return cudaErrorInvalidValue;
+        EpiParams pg = p;
+        pg.ws = a.splitk_ws;
+        pg.counters = a.splitk_counters;
+        switch (bn) {
+            case 32: return launch_splitk_global<32>(ta, tb, pg, plan.splits, plan.stages, st);
+            case 64: return launch_splitk_global<64>(ta, tb, pg, plan.splits, plan.stages, st);
+            case 256: return launch_splitk_global<256>(ta, tb, pg, plan.splits, plan.stages, st);
+            default: return launch_splitk_global<128>(ta, tb, pg, plan.splits, plan.stages, st);
+        }
+    }
     if (plan.splits > 1) {
         if (plan.stages < splitk_min_stages(bn) || plan.stages > splitk_max_stages(bn)) return cudaErrorInvalidValue;
         switch (bn) {
@@ -1059,6 +1129,27 @@ cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUten
     }
 }
 
+bool gemm_i8_skinny_plan(const GemmI8Args& a, GemmPlan* plan) {
+    // one 128-row M tile and a long K: the weights are the traffic. Spread the
+    // (N tile, k-block) work over one CTA per SM, K split across independent
+    // CTAs whose int32 partials meet in the caller's workspace.
+    if (!a.splitk_ws || !a.splitk_counters || a.M > kBM || std::getenv("VLA_GEMM_PLAN")) return false;
+    const int nkb = (a.K + kBK - 1) / kBK;
+    const int bn = a.N >= 1024 ? 128 : a.N >= 256 ? 64 : 32;
+    const int n_tiles = (a.N + bn - 1) / bn;
+    int splits = sm_count() / n_tiles;
+    if (splits > nkb) splits = nkb;
+    if (splits > kMaxGlobalSplits) splits = kMaxGlobalSplits;
+    if (nkb < 4 || splits < 2 || n_tiles > a.splitk_counters_n ||
+        (long long)n_tiles * splits * a.M * bn > a.splitk_ws_elems)
+        return false;
+    plan->bn = bn;
+    plan->splits = splits;
+    plan->stages = splitk_max_stages(bn);
+    plan->global = true;
+    return true;
+}
+
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
@@ -1066,7 +1157,8 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (!a.force_simt && tma_ok) {
         // operands TMA can describe always take the tensor-core kernel; a tensor
         // map the driver refuses is an error, never a silent detour
-        const GemmPlan plan = gemm_i8_plan(a.M, a.N, a.K);
+        GemmPlan plan = gemm_i8_plan(a.M, a.N, a.K);
+        gemm_i8_skinny_plan(a, &plan);
         CUtensorMap ta, tb;
         if (!make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) ||
             !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, plan.bn))

@@ -34,6 +34,15 @@ struct GemmI8Args {
     bool force_simt = false;     // route to the CUDA-core kernel (tests / odd strides)
     bool static_weights = false; // B/wscale/bias are load-time constants: the kernel may
                                  // fetch them before its predecessor in the stream ends
+    // Optional split-K workspace for M <= 128 (one row tile) with a long K: K
+    // is then split over independent CTAs whose int32 partial tiles are summed
+    // by the last one to finish a tile (exact: integer sums). counters
+    // [splitk_counters_n] must be zero when first used; every launch leaves them
+    // zero again. Calls that may run at the same time need separate workspaces.
+    int32_t* splitk_ws = nullptr;
+    long long splitk_ws_elems = 0;
+    unsigned int* splitk_counters = nullptr;
+    int splitk_counters_n = 0;
 };
 
 // Launch on `st`. Tensor-core path when lda/ldb/A/B are 16-byte aligned,
@@ -47,6 +56,7 @@ struct GemmPlan {
     int bn = 128;
     int splits = 1;
     int stages = 4;
+    bool global = false;   // split K over independent CTAs (needs GemmI8Args::splitk_ws)
 };
 GemmPlan gemm_i8_plan(int M, int N, int K);
 

@@ -6,3 +6,4 @@
 #include "nn.cu"
 #include "f32.cu"
 #include "lm_ops.cu"
+#include "dp.cu"

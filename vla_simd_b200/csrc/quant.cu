@@ -133,12 +133,12 @@ im2col_i8_kernel(const float* __restrict__ x, int F, int H, int W, int C, int k,
                  int8_t* __restrict__ col, float* __restrict__ rscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    __shared__ float s_inv[8], s_scale[8];
-    if (threadIdx.x < F && threadIdx.x < 8) {
-        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
+    __shared__ float s_inv[kMaxConvFrames], s_scale[kMaxConvFrames];
+    for (int i = threadIdx.x; i < F; i += blockDim.x) {
+        const float amax = __uint_as_float(amax_bits[i]);
         const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        s_scale[threadIdx.x] = s;
-        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
+        s_scale[i] = s;
+        s_inv[i] = __fdiv_rn(1.0f, s);
     }
     __syncthreads();
     const int groups = ldc >> 4;
@@ -181,12 +181,12 @@ im2col_i8_bytes_kernel(const float* __restrict__ x, int F, int H, int W, int C, 
                        int8_t* __restrict__ col, float* __restrict__ rscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    __shared__ float s_inv[8], s_scale[8];
-    if (threadIdx.x < F && threadIdx.x < 8) {
-        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
+    __shared__ float s_inv[kMaxConvFrames], s_scale[kMaxConvFrames];
+    for (int i = threadIdx.x; i < F; i += blockDim.x) {
+        const float amax = __uint_as_float(amax_bits[i]);
         const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        s_scale[threadIdx.x] = s;
-        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
+        s_scale[i] = s;
+        s_inv[i] = __fdiv_rn(1.0f, s);
     }
     __syncthreads();
     const int groups = ldc >> 4;
@@ -299,12 +299,12 @@ s2d_quantize_i8_kernel(const float* __restrict__ x, int F, int H, int W, int pad
                        float* __restrict__ fscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    __shared__ float s_inv[8];
-    if (threadIdx.x < F && threadIdx.x < 8) {
-        const float amax = __uint_as_float(amax_bits[threadIdx.x]);
+    __shared__ float s_inv[kMaxConvFrames];
+    for (int i = threadIdx.x; i < F; i += blockDim.x) {
+        const float amax = __uint_as_float(amax_bits[i]);
         const float s = amax > 0.0f ? fmaxf(__fdiv_rn(__fmul_rn(amax, clip), 127.0f), FLT_MIN) : 1.0f;
-        s_inv[threadIdx.x] = __fdiv_rn(1.0f, s);
-        if (blockIdx.x == 0) fscale[threadIdx.x] = s;
+        s_inv[i] = __fdiv_rn(1.0f, s);
+        if (blockIdx.x == 0) fscale[i] = s;
     }
     __syncthreads();
     const int total = F * Hb * Wo * 4;
@@ -344,7 +344,7 @@ cudaError_t s2d_quantize_i8(const float* x, int F, int H, int W, int C, int k, i
                             const unsigned int* amax_bits, float clip, int8_t* q, float* fscale, cudaStream_t st) {
     const int kt = (k + 1) / 2;
     const int Hb = Ho + kt - 1;
-    if (!s2d_conv_supported(C, k, 2) || F <= 0 || F > 8 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || pad < 0 ||
+    if (!s2d_conv_supported(C, k, 2) || F <= 0 || F > kMaxConvFrames || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || pad < 0 ||
         (reinterpret_cast<uintptr_t>(q) & 15) || (long long)F * Hb * Wo * 4 >= (1LL << 31) ||
         (long long)H * W * C >= (1LL << 31))
         return cudaErrorInvalidValue;
@@ -466,7 +466,7 @@ cudaError_t im2col_i8(const float* x, int F, int H, int W, int C, int k, int str
                       long long ldc, const unsigned int* amax_bits, float clip, int8_t* col, float* rscale,
                       cudaStream_t st) {
     const int K = k * k * C;
-    if (ldc < K || (ldc & 15) || F > 8 || (long long)F * H * W * C >= (1LL << 31) ||
+    if (ldc < K || (ldc & 15) || F <= 0 || F > kMaxConvFrames || (long long)F * H * W * C >= (1LL << 31) ||
         (long long)F * Ho * Wo * (ldc / 16) >= (1LL << 31))
         return cudaErrorInvalidValue;
     const bool v16 = (C % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&

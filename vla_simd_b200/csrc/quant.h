@@ -5,6 +5,10 @@
 
 namespace vsb {
 
+// Most frames one im2col / space-to-depth launch quantizes (per-frame scales
+// are staged in shared memory).
+constexpr int kMaxConvFrames = 256;
+
 // Per-row symmetric int8 quantization of x [M][ldx] (K valid columns), optional
 // fp32 addend added first. q [M][ldq] is zero past K. Optional second output
 // q2/scale2 quantizes x itself (without the addend) in the same pass.

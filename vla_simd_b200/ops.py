@@ -59,6 +59,19 @@ def gemm_i8(xq, ascale, Wq, wscale, K, bias=None, mode=0, res=None, out=None, am
     return out
 
 
+def gemm_i8_splitk(xq, ascale, Wq, wscale, K, ws, counters, bias=None, mode=0, res=None, out=None):
+    """The W8A8 GEMM with K split over independent CTAs (vla_cuda_gemm_i8_splitk):
+    M <= 128 rows; ws int32 and counters int32 (zeroed) are the caller's workspace."""
+    M, N = xq.shape[0], Wq.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.int32 if mode & EPI_ACC else torch.float32, device=xq.device)
+    ldr = res.stride(0) if res is not None else 0
+    check(lib().vla_cuda_gemm_i8_splitk(_p(out), out.stride(0), _p(xq), xq.stride(0), _p(ascale), _p(Wq), Wq.stride(0),
+                                        _p(wscale), _p(bias), _p(res), ldr, M, N, K, mode, _p(ws), ws.numel(),
+                                        _p(counters), counters.numel(), _stream()), "vla_cuda_gemm_i8_splitk")
+    return out
+
+
 def dense_linear_i8(x, Wq, wscale, bias=None):
     """tcpu::dense_linear_i8: fp32 x [seq, K] -> fp32 [seq, N], x quantized per token."""
     seq, K = x.shape

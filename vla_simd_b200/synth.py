@@ -156,3 +156,178 @@ def act_inputs(shape: ActShape = ACT_BASELINE, seed: int = 1):
     frames = rng.integers(0, 256, size=(shape.n_cams, shape.img_h, shape.img_w, 3), dtype=np.uint8)
     state = rng.standard_normal(shape.state_dim, dtype=np.float32)
     return frames, state
+
+
+# ---------------------------------------------------------------------------
+# Diffusion Policy (the reference's src/models/diffusion), random-init.
+#
+#     diffusion.meta                 shapes + sampler settings
+#                                    (src/models/diffusion/diffusion_model.cpp:25-88)
+#     rgb_encoder{i}_backbone.meta   ResNet-18 table + gn_group_size
+#     rgb_encoder{i}_backbone.bin    stem W, GroupNorm scale/shift, then per block
+#                                    conv1 W + GN, conv2 W + GN, (down W + GN); no conv
+#                                    bias (src/models/act/resnet_backbone.cpp:100-150)
+#     rgb_encoder{i}.bin             1x1 keypoint conv [K, C] + bias, output linear
+#                                    [2K, 2K] + bias (src/models/diffusion/rgb_encoder.cpp:45-56)
+#     unet.bin                       DPUNet1d::load order (src/models/diffusion/unet1d.cpp:18-33)
+#     stats.bin                      state min/max, action min/max, per-camera image
+#                                    mean/std (diffusion_model.cpp:123-141)
+
+@dataclasses.dataclass(frozen=True)
+class DpShape:
+    n_obs_steps: int = 2
+    n_cams: int = 1
+    img_h: int = 96
+    img_w: int = 96
+    crop_h: int = 84
+    crop_w: int = 84
+    state_dim: int = 2
+    action_dim: int = 2
+    horizon: int = 16
+    n_action_steps: int = 8
+    num_keypoints: int = 32
+    kernel_size: int = 5
+    n_groups: int = 8
+    step_embed_dim: int = 128
+    film_scale: bool = True
+    separate_encoders: bool = True
+    down_dims: tuple = (512, 1024, 2048)
+    num_train_timesteps: int = 100
+    num_inference_steps: int = 10
+    scheduler: str = "DDIM"
+    beta_schedule: str = "squaredcos_cap_v2"
+    clip_sample: bool = True
+    stem_out: int = 64
+    widths: tuple = (64, 128, 256, 512)
+    gn_group_size: int = 16
+
+    @property
+    def cond_dim(self) -> int:
+        return self.step_embed_dim + (self.state_dim + self.n_cams * 2 * self.num_keypoints) * self.n_obs_steps
+
+
+# ResNet-18 + GroupNorm + spatial softmax on a 2-frame
+# history of 84x84 crops (96x96 frames, center-cropped as PushT), 2-dim state and
+# action, U-Net (512, 1024, 2048), kernel 5, 8 groups, FiLM, horizon 16, DDIM 10.
+DP_BASELINE = DpShape()
+# reduced DP for fast tests: two cameras with separate encoders, narrow widths
+DP_SMALL = DpShape(n_cams=2, img_h=40, img_w=48, crop_h=32, crop_w=40, state_dim=3, action_dim=4, horizon=16,
+                   n_action_steps=6, num_keypoints=8, down_dims=(64, 128, 256), step_embed_dim=32,
+                   stem_out=16, widths=(16, 32, 48, 64))
+
+
+def write_dp_checkpoint(out_dir: str, shape: DpShape = DP_BASELINE, seed: int = 0) -> str:
+    """Write a random-init Diffusion Policy checkpoint directory; returns out_dir."""
+    os.makedirs(out_dir, exist_ok=True)
+    rng = np.random.default_rng(seed)
+    s = shape
+
+    def normal(shape_, std):
+        return (rng.standard_normal(shape_, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+    def save(name, parts):
+        np.concatenate([p.reshape(-1) for p in parts]).astype(np.float32).tofile(os.path.join(out_dir, name))
+
+    def gn(c):
+        return [(1.0 + normal((c,), 0.05)).astype(np.float32), normal((c,), 0.05)]
+
+    n_enc = s.n_cams if s.separate_encoders else 1
+    ashape = ActShape(stem_out=s.stem_out, widths=s.widths)
+    for e in range(n_enc):
+        parts = []
+        k = 7
+        parts += [normal((s.stem_out, k, k, 3), np.sqrt(2.0 / (k * k * 3)))] + gn(s.stem_out)
+        meta = ["in_ch 3", f"stem_out {s.stem_out}", f"stem_k {k}", "stem_stride 2", f"stem_pad {k // 2}",
+                "pool_k 3", "pool_stride 2", "pool_pad 1"]
+        for cin, cout, stride, has_down in _block_table(ashape):
+            parts += [normal((cout, 3, 3, cin), np.sqrt(2.0 / (9 * cin)))] + gn(cout)
+            parts += [normal((cout, 3, 3, cout), np.sqrt(1.0 / (9 * cout)))] + gn(cout)
+            if has_down:
+                parts += [normal((cout, 1, 1, cin), np.sqrt(1.0 / cin))] + gn(cout)
+            meta.append(f"block {cin} {cout} {stride} {has_down}")
+        meta.append(f"gn_group_size {s.gn_group_size}")
+        with open(os.path.join(out_dir, f"rgb_encoder{e}_backbone.meta"), "w") as f:
+            f.write("\n".join(meta) + "\n")
+        save(f"rgb_encoder{e}_backbone.bin", parts)
+        C, K = s.widths[-1], s.num_keypoints
+        save(f"rgb_encoder{e}.bin", [normal((K, C), np.sqrt(1.0 / C)), normal((K,), 0.05),
+                                     normal((2 * K, 2 * K), np.sqrt(1.0 / (2 * K))), normal((2 * K,), 0.05)])
+
+    # ---- conditional U-Net, DPUNet1d::load order
+    A, D, CD, k = s.action_dim, s.step_embed_dim, s.cond_dim, s.kernel_size
+    parts = []
+
+    def lin(n, kk, std=None):
+        parts.extend([normal((n, kk), np.sqrt(1.0 / kk) if std is None else std), normal((n,), 0.02)])
+
+    def conv_block(cin, cout):
+        lin(cout, k * cin)
+        parts.extend(gn(cout))
+
+    def res_block(cin, cout):
+        conv_block(cin, cout)
+        lin(2 * cout if s.film_scale else cout, CD, 0.5 / np.sqrt(CD))
+        conv_block(cout, cout)
+        if cin != cout:
+            lin(cout, cin)
+
+    lin(4 * D, D)
+    lin(D, 4 * D)
+    in_out = [(A, s.down_dims[0])] + [(s.down_dims[i], s.down_dims[i + 1]) for i in range(len(s.down_dims) - 1)]
+    for i, (ci, co) in enumerate(in_out):
+        res_block(ci, co)
+        res_block(co, co)
+        if i + 1 < len(in_out):
+            lin(co, 3 * co)
+    mid = s.down_dims[-1]
+    res_block(mid, mid)
+    res_block(mid, mid)
+    for ind in range(len(in_out) - 1):
+        dim_out, dim_in = in_out[len(in_out) - 1 - ind]
+        res_block(dim_in * 2, dim_out)
+        res_block(dim_out, dim_out)
+        parts.extend([normal((dim_out, 4, dim_out), np.sqrt(1.0 / (2 * dim_out))), normal((dim_out,), 0.02)])
+    conv_block(s.down_dims[0], s.down_dims[0])
+    lin(A, s.down_dims[0])
+    save("unet.bin", parts)
+
+    # ---- stats: MIN_MAX state / action (non-degenerate), MEAN_STD images
+    smin = normal((s.state_dim,), 1.0) - 2.0
+    amin = normal((s.action_dim,), 1.0) - 2.0
+    stats = [smin, (smin + rng.uniform(1.0, 4.0, s.state_dim)).astype(np.float32),
+             amin, (amin + rng.uniform(1.0, 4.0, s.action_dim)).astype(np.float32)]
+    for _ in range(s.n_cams):
+        stats.append(rng.uniform(0.4, 0.6, 3).astype(np.float32))
+        stats.append(rng.uniform(0.2, 0.3, 3).astype(np.float32))
+    save("stats.bin", stats)
+
+    meta = [f"n_obs_steps {s.n_obs_steps}", f"n_cams {s.n_cams}", f"img_h {s.img_h}", f"img_w {s.img_w}",
+            f"crop_h {s.crop_h}", f"crop_w {s.crop_w}", "resize_h 0", "resize_w 0",
+            f"state_dim {s.state_dim}", f"action_dim {s.action_dim}", f"horizon {s.horizon}",
+            f"n_action_steps {s.n_action_steps}", f"num_keypoints {s.num_keypoints}",
+            f"kernel_size {s.kernel_size}", f"n_groups {s.n_groups}", f"step_embed_dim {s.step_embed_dim}",
+            f"film_scale {int(s.film_scale)}", f"separate_encoders {int(s.separate_encoders)}",
+            "down_dims " + " ".join(str(d) for d in s.down_dims),
+            f"num_train_timesteps {s.num_train_timesteps}", f"num_inference_steps {s.num_inference_steps}",
+            "beta_start 0.0001", "beta_end 0.02", f"beta_schedule {s.beta_schedule}", "prediction_type epsilon",
+            f"clip_sample {int(s.clip_sample)}", "clip_sample_range 1.0", f"scheduler {s.scheduler}",
+            "gn_eps 1e-5"] + [f"cam observation.images.cam{c}" for c in range(s.n_cams)]
+    with open(os.path.join(out_dir, "diffusion.meta"), "w") as f:
+        f.write("\n".join(meta) + "\n")
+    with open(os.path.join(out_dir, "config.txt"), "w") as f:
+        f.write("".join(f"cam{c} cam{c}\n" for c in range(s.n_cams)))
+    return out_dir
+
+
+def dp_inputs(shape: DpShape = DP_BASELINE, seed: int = 1, batch: int = 0):
+    """Seeded DP query: frames [n_obs_steps * n_cams, H, W, 3] uint8 ~ U{0..255}
+    (obs-major, then camera), state [n_obs_steps, state_dim] in the stats' range,
+    noise [1 + num_inference_steps, horizon, action_dim] ~ N(0, 1). With batch > 0
+    each array gains a leading batch axis."""
+    rng = np.random.default_rng(seed)
+    s = shape
+    lead = (batch,) if batch else ()
+    frames = rng.integers(0, 256, size=lead + (s.n_obs_steps * s.n_cams, s.img_h, s.img_w, 3), dtype=np.uint8)
+    state = rng.standard_normal(lead + (s.n_obs_steps, s.state_dim), dtype=np.float32)
+    noise = rng.standard_normal(lead + (1 + s.num_inference_steps, s.horizon, s.action_dim), dtype=np.float32)
+    return frames, state, noise
