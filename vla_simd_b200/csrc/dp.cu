@@ -367,28 +367,35 @@ cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, in
 // ------------------------------------------------------ conv_transpose1d
 // Per output (sample, ot, co): bias, then x[t][ci] * W[ci][kt][co] for kt from
 // k-1 down to 0, ci in order, zero inputs skipped (src/hal/common/conv.cpp:349-395).
-// That order is kept: every output is one fma chain. CTA = 32 output channels x
-// 8 thread rows, a thread owns outputs ot = ty + 8i (OPT independent chains);
-// the chains advance tap slot by tap slot (the j-th valid kt of each output,
-// descending), and inside a slot over 32-channel chunks of ci whose x and W
-// values are staged in shared memory, the next chunk's loads issued before
-// the current chunk's fmas. Optional per-row absmax of the output (atomicMax).
-constexpr int kCtCo = 32, kCtCi = 32, kCtRows = 8, kCtMaxK = 4;
+// That order is kept: every output is one fma chain, advanced tap slot by tap
+// slot (the j-th valid kt of the output, descending), and inside a slot over
+// ci. CTA = 8 output channels x 16 thread rows, a thread owns outputs
+// ot = row + 16i (OPT chains); ci advances in chunks of kCtCi whose W [kCtCi][k][8]
+// and x [T][kCtCi] values stream through a cp.async ring of kCtStages chunks,
+// so many weight bytes are in flight per SM while the chains run. Optional
+// per-row absmax of the output (atomicMax).
+constexpr int kCtCo = 8, kCtCi = 128, kCtRows = 16, kCtMaxK = 4, kCtStages = 4;
+constexpr int kCtXs = kCtCi + 4;   // x row stride in shared memory: 16-byte rows, distinct banks per row
+
+__host__ __device__ constexpr size_t convt_stage_floats(int k, int T) {
+    return (size_t)kCtCi * k * kCtCo + (size_t)T * kCtXs;
+}
 
 template <int OPT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128)
 conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restrict__ W,
                               const float* __restrict__ bias, float* __restrict__ out, int T, int Cin, int Cout,
                               int k, int stride, int pad, int Tout, int slots, unsigned int* __restrict__ rowmax) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    extern __shared__ float ct_smem[];
-    float* sW = ct_smem;                          // [2][kCtCi][k][kCtCo]
-    float* sx = ct_smem + 2 * kCtCi * k * kCtCo;  // [2][T][kCtCi]
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    extern __shared__ __align__(16) float ct_smem[];
+    const int tx = threadIdx.x & (kCtCo - 1), ty = threadIdx.x / kCtCo;
     const int co0 = blockIdx.x * kCtCo, f = blockIdx.y;
     const int co = co0 + tx;
     const float* xf = x + (long long)f * T * Cin;
+    const size_t stage_fl = convt_stage_floats(k, T);
+    const int nchunk = (Cin + kCtCi - 1) / kCtCi;
+    const int iters = slots * nchunk;           // (slot, chunk) in chain order
     float acc[OPT];
     int ot[OPT];
     #pragma unroll
@@ -396,101 +403,82 @@ conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restri
         ot[i] = ty + kCtRows * i;
         acc[i] = (bias && co < Cout) ? bias[co] : 0.0f;
     }
-    const int nchunk = (Cin + kCtCi - 1) / kCtCi;
-    const int wlen = kCtCi * k * kCtCo, xlen = T * kCtCi;
-    for (int j = 0; j < slots; ++j) {
-        // this slot's tap and input row per output (-1: none)
-        int kt_i[OPT], t_i[OPT];
-        #pragma unroll
-        for (int i = 0; i < OPT; ++i) {
-            kt_i[i] = -1;
-            t_i[i] = 0;
-            if (ot[i] >= Tout) continue;
-            int seen = 0;
-            for (int kt = k - 1; kt >= 0; --kt) {
-                const int num = ot[i] + pad - kt;
-                if (num < 0 || num % stride) continue;
-                const int t = num / stride;
-                if (t >= T) continue;
-                if (seen++ == j) { kt_i[i] = kt; t_i[i] = t; break; }
-            }
+    // cp.async of chunk c (ci block) into ring stage s: W rows (ci, kt) of 8
+    // floats (two 16-byte pieces) and x rows t of kCtCi floats; zero past Cin
+    auto issue = [&](int it, int stg) {
+        const int c = it % nchunk;
+        float* sW = ct_smem + (size_t)stg * stage_fl;
+        float* sx = sW + (size_t)kCtCi * k * kCtCo;
+        const int ci0 = c * kCtCi;
+        for (int e = threadIdx.x; e < kCtCi * k * 2; e += blockDim.x) {
+            const int half = e & 1, r = e >> 1, kt = r % k, ci = ci0 + r / k;
+            const bool ok = ci < Cin;
+            cp_async16(sW + (size_t)r * kCtCo + half * 4,
+                       W + ((long long)(ok ? ci : 0) * k + kt) * Cout + co0 + half * 4, ok ? 16 : 0);
         }
-        // chunk 0 into buffer 0
-        for (int e = threadIdx.x; e < wlen; e += blockDim.x) {
-            const int cc = e % kCtCo, r = e / kCtCo, kt = r % k, ci = r / k;
-            sW[e] = (ci < Cin && co0 + cc < Cout) ? W[((long long)ci * k + kt) * Cout + co0 + cc] : 0.0f;
+        for (int e = threadIdx.x; e < T * (kCtCi / 4); e += blockDim.x) {
+            const int t = e / (kCtCi / 4), q = e - t * (kCtCi / 4), ci = ci0 + 4 * q;
+            const bool ok = ci < Cin;
+            cp_async16(sx + (size_t)t * kCtXs + 4 * q, xf + (long long)t * Cin + (ok ? ci : 0), ok ? 16 : 0);
         }
-        for (int e = threadIdx.x; e < xlen; e += blockDim.x) {
-            const int ci = e % kCtCi, t = e / kCtCi;
-            sx[e] = ci < Cin ? xf[(long long)t * Cin + ci] : 0.0f;
-        }
-        __syncthreads();
-        for (int c = 0; c < nchunk; ++c) {
-            const int cur = c & 1, nxt = cur ^ 1;
-            // the next chunk's values in flight while this chunk computes
-            constexpr int kPre = (kCtCi * kCtMaxK * kCtCo + 255) / 256;
-            float wv[kPre], xv[4];
-            const bool more = c + 1 < nchunk;
-            const int ci1 = (c + 1) * kCtCi;
-            if (more) {
-                #pragma unroll
-                for (int u = 0; u < kPre; ++u) {
-                    const int e = threadIdx.x + u * 256;
-                    wv[u] = 0.0f;
-                    if (e < wlen) {
-                        const int cc = e % kCtCo, r = e / kCtCo, kt = r % k, ci = ci1 + r / k;
-                        if (ci < Cin && co0 + cc < Cout) wv[u] = W[((long long)ci * k + kt) * Cout + co0 + cc];
-                    }
-                }
-                #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int e = threadIdx.x + u * 256;
-                    xv[u] = 0.0f;
-                    if (e < xlen) {
-                        const int ci = ci1 + e % kCtCi, t = e / kCtCi;
-                        if (ci < Cin) xv[u] = xf[(long long)t * Cin + ci];
-                    }
-                }
-            }
-            const float* w = sW + cur * wlen;
-            const float* xs = sx + cur * xlen;
-            const int cmax = min(kCtCi, Cin - c * kCtCi);
+    };
+    for (int s0 = 0; s0 < kCtStages - 1; ++s0) {
+        if (s0 < iters) issue(s0, s0);
+        cp_async_commit();
+    }
+    int cur_slot = -1;
+    int kt_i[OPT], t_i[OPT];
+    for (int it = 0; it < iters; ++it) {
+        const int j = it / nchunk, c = it - j * nchunk;
+        if (j != cur_slot) {      // this slot's tap and input row per output (-1: none)
+            cur_slot = j;
             #pragma unroll
             for (int i = 0; i < OPT; ++i) {
-                if (kt_i[i] < 0) continue;
-                const float* xr = xs + t_i[i] * kCtCi;
-                const float* wr = w + kt_i[i] * kCtCo + tx;
-                for (int ci = 0; ci < cmax; ++ci) {
-                    const float v = xr[ci];
-                    if (v == 0.0f) continue;
-                    acc[i] = __fmaf_rn(v, wr[ci * k * kCtCo], acc[i]);
+                kt_i[i] = -1;
+                t_i[i] = 0;
+                if (ot[i] >= Tout) continue;
+                int seen = 0;
+                for (int kt = k - 1; kt >= 0; --kt) {
+                    const int num = ot[i] + pad - kt;
+                    if (num < 0 || num % stride) continue;
+                    const int t = num / stride;
+                    if (t >= T) continue;
+                    if (seen++ == j) { kt_i[i] = kt; t_i[i] = t; break; }
                 }
             }
-            if (more) {
-                float* wn = sW + nxt * wlen;
-                float* xn = sx + nxt * xlen;
-                #pragma unroll
-                for (int u = 0; u < kPre; ++u) {
-                    const int e = threadIdx.x + u * 256;
-                    if (e < wlen) wn[e] = wv[u];
-                }
-                #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int e = threadIdx.x + u * 256;
-                    if (e < xlen) xn[e] = xv[u];
-                }
+        }
+        asm volatile("cp.async.wait_group %0;" :: "n"(kCtStages - 2) : "memory");
+        __syncthreads();
+        // refill the stage the previous iteration read (every thread is past it)
+        if (it + kCtStages - 1 < iters) issue(it + kCtStages - 1, (it + kCtStages - 1) % kCtStages);
+        cp_async_commit();
+        const float* sW = ct_smem + (size_t)(it % kCtStages) * stage_fl;
+        const float* sx = sW + (size_t)kCtCi * k * kCtCo;
+        const int cmax = min(kCtCi, Cin - c * kCtCi);
+        #pragma unroll
+        for (int i = 0; i < OPT; ++i) {
+            if (kt_i[i] < 0) continue;
+            const float* xr = sx + (size_t)t_i[i] * kCtXs;
+            const float* wr = sW + (size_t)kt_i[i] * kCtCo + tx;
+            for (int ci = 0; ci < cmax; ++ci) {
+                const float v = xr[ci];
+                if (v == 0.0f) continue;
+                acc[i] = __fmaf_rn(v, wr[(size_t)ci * k * kCtCo], acc[i]);
             }
-            __syncthreads();
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     #pragma unroll
     for (int i = 0; i < OPT; ++i) {
-        if (ot[i] >= Tout) continue;
-        if (co < Cout) out[((long long)f * Tout + ot[i]) * Cout + co] = acc[i];
+        const bool valid = ot[i] < Tout && co < Cout;
+        if (valid) out[((long long)f * Tout + ot[i]) * Cout + co] = acc[i];
         if (rowmax) {
-            float m = co < Cout ? fabsf(acc[i]) : 0.0f;
-            m = warp_max_f(m);
-            if (tx == 0) atomicMax(&rowmax[f * Tout + ot[i]], __float_as_uint(m));
+            // the 8 channels of this row sit in 8 consecutive lanes; every lane
+            // of the warp takes part in the shuffles
+            float m = valid ? fabsf(acc[i]) : 0.0f;
+            #pragma unroll
+            for (int off = 4; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+            if (tx == 0 && ot[i] < Tout) atomicMax(&rowmax[f * Tout + ot[i]], __float_as_uint(m));
         }
     }
 }
@@ -499,29 +487,30 @@ template <int OPT>
 cudaError_t launch_convt(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
                          int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax, cudaStream_t st) {
     const int slots = (k + stride - 1) / stride;
-    const size_t smem = sizeof(float) * (2 * kCtCi * k * kCtCo + 2 * T * kCtCi);
+    const size_t smem = sizeof(float) * kCtStages * convt_stage_floats(k, T);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(conv_transpose1d_tiled_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              200 * 1024);
         attr = true;
     }
-    return launch_k(conv_transpose1d_tiled_kernel<OPT>, dim3((unsigned)((Cout + kCtCo - 1) / kCtCo), (unsigned)F), 256,
-                    smem, st, x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
+    return launch_k(conv_transpose1d_tiled_kernel<OPT>, dim3((unsigned)(Cout / kCtCo), (unsigned)F), 128, smem, st,
+                    x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
 }
 
 cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
                                int Cout, int k, int stride, int pad, unsigned int* rowmax, cudaStream_t st) {
     const int Tout = (T - 1) * stride - 2 * pad + k;
-    // staged rows: T * kCtCi x values in at most 4 loads per thread; k <= kCtMaxK taps
+    // 16-byte cp.async rows: Cin and Cout multiples of 4 / 8 and aligned bases
     if (F <= 0 || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || k > kCtMaxK || stride <= 0 || pad < 0 || Tout <= 0 ||
-        Tout > 8 * kCtRows || T * kCtCi > 4 * 256 || F > 65535)
+        Tout > 4 * kCtRows || Cin % 4 || Cout % kCtCo || F > 65535 ||
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W)) & 15))
         return cudaErrorInvalidValue;
     cudaError_t e;
     if (Tout <= kCtRows) e = launch_convt<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
     else if (Tout <= 2 * kCtRows) e = launch_convt<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
-    else if (Tout <= 4 * kCtRows) e = launch_convt<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
-    else e = launch_convt<8>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else e = launch_convt<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -543,26 +532,43 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
     __shared__ double red[32];
     const int g = blockIdx.x, f = blockIdx.y;
     const int gc = C / groups, c0 = g * gc;
-    float* sA = ug_smem;                                            // [gc]
-    float* sB = ug_smem + gc;                                       // [gc]
-    unsigned int* srm = reinterpret_cast<unsigned int*>(ug_smem + 2 * gc);   // [T]
+    float* sx = ug_smem;                                            // [T][gc]: the group's tile
+    float* sA = ug_smem + (size_t)T * gc;                           // [gc]
+    float* sB = sA + gc;                                            // [gc]
+    unsigned int* srm = reinterpret_cast<unsigned int*>(sB + gc);   // [T]
     const float* xf = x + (long long)f * T * C + c0;
+    // the tile in one sweep (all loads in flight), statistics from shared memory
+    if ((gc & 3) == 0 && (C & 3) == 0 && (c0 & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int g4 = gc >> 2;
+        for (int e = threadIdx.x; e < T * g4; e += blockDim.x) {
+            const int p = e / g4, q = e - p * g4;
+            *reinterpret_cast<float4*>(sx + (size_t)p * gc + 4 * q) =
+                *reinterpret_cast<const float4*>(xf + (long long)p * C + 4 * q);
+        }
+    } else {
+        for (int e = threadIdx.x; e < T * gc; e += blockDim.x) {
+            const int p = e / gc, cl = e - p * gc;
+            sx[e] = xf[(long long)p * C + cl];
+        }
+    }
+    for (int p = threadIdx.x; p < T; p += blockDim.x) srm[p] = 0u;
+    __syncthreads();
     const double np = (double)T, n = np * gc;
     // per channel: shifted sums over the T steps (first step as the shift)
     double t1 = 0.0;
     for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
-        const double K = (double)xf[cl];
+        const double K = (double)sx[cl];
         double s1 = 0.0;
-        for (int p = 0; p < T; ++p) s1 = __dadd_rn(s1, __dsub_rn((double)xf[(long long)p * C + cl], K));
+        for (int p = 0; p < T; ++p) s1 = __dadd_rn(s1, __dsub_rn((double)sx[(size_t)p * gc + cl], K));
         t1 = __dadd_rn(t1, __fma_rn(np, K, s1));
     }
     const double mean = __ddiv_rn(block_sum_d(t1, red), n);
     double t2 = 0.0;
     for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
-        const double K = (double)xf[cl];
+        const double K = (double)sx[cl];
         double s1 = 0.0, s2 = 0.0;
         for (int p = 0; p < T; ++p) {
-            const double d = __dsub_rn((double)xf[(long long)p * C + cl], K);
+            const double d = __dsub_rn((double)sx[(size_t)p * gc + cl], K);
             s1 = __dadd_rn(s1, d);
             s2 = __fma_rn(d, d, s2);
         }
@@ -577,18 +583,31 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
         sA[cl] = (float)__dmul_rn(inv, (double)scale[c0 + cl]);
         sB[cl] = (float)__fma_rn(-mi, (double)scale[c0 + cl], (double)bias[c0 + cl]);
     }
-    for (int p = threadIdx.x; p < T; p += blockDim.x) srm[p] = 0u;
     __syncthreads();
     const float* ff = film ? film + (long long)f * ld_film : nullptr;
-    for (int e = threadIdx.x; e < T * gc; e += blockDim.x) {
-        const int p = e / gc, cl = e - p * gc, c = c0 + cl;
-        const long long i = ((long long)f * T + p) * C + c;
-        float v = mish_lanes(__fmaf_rn(x[i], sA[cl], sB[cl]));
-        if (epi == kUgFilmScale) v = __fmaf_rn(ff[c], v, ff[C + c]);
-        else if (epi == kUgFilmBias) v = __fadd_rn(v, ff[c]);
-        else if (epi == kUgRes) v = __fadd_rn(v, res[i]);
-        out[i] = v;
-        if (rowmax) atomicMax(&srm[p], __float_as_uint(fabsf(v)));
+    // a warp's 32 consecutive elements share a time step when gc % 32 == 0:
+    // one shared-memory atomic per warp then, else one per element
+    const bool warp_rows = (gc & 31) == 0;
+    for (int e0 = 0; e0 < T * gc; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        float m = 0.0f;
+        int p = 0;
+        if (e < T * gc) {
+            p = e / gc;
+            const int cl = e - p * gc, c = c0 + cl;
+            const long long i = ((long long)f * T + p) * C + c;
+            float v = mish_lanes(__fmaf_rn(sx[e], sA[cl], sB[cl]));
+            if (epi == kUgFilmScale) v = __fmaf_rn(ff[c], v, ff[C + c]);
+            else if (epi == kUgFilmBias) v = __fadd_rn(v, ff[c]);
+            else if (epi == kUgRes) v = __fadd_rn(v, res[i]);
+            out[i] = v;
+            m = fabsf(v);
+            if (rowmax && !warp_rows) atomicMax(&srm[p], __float_as_uint(m));
+        }
+        if (rowmax && warp_rows) {   // every lane takes part (blockDim and T*gc are multiples of 32)
+            m = warp_max_f(m);
+            if ((threadIdx.x & 31) == 0 && e < T * gc) atomicMax(&srm[p], __float_as_uint(m));
+        }
     }
     if (rowmax) {
         __syncthreads();
@@ -603,7 +622,7 @@ cudaError_t unet_gn(const float* x, int F, int T, int C, int groups, float eps, 
     if (F <= 0 || T <= 0 || C <= 0 || groups <= 0 || C % groups || F > 65535 ||
         ((epi == kUgFilmScale || epi == kUgFilmBias) && !film) || (epi == kUgRes && !res))
         return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (2 * (size_t)(C / groups) + T);
+    const size_t smem = sizeof(float) * ((size_t)T * (C / groups) + 2 * (size_t)(C / groups) + T);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr = false;
     if (!attr) {
@@ -626,7 +645,7 @@ cudaError_t unet_gn(const float* x, int F, int T, int C, int groups, float eps, 
 __global__ void __launch_bounds__(256)
 im2col1d_q8w_kernel(const float* __restrict__ x, int T, int C, int k, int stride, int pad, int Tout,
                     const unsigned int* __restrict__ rowmax, int8_t* __restrict__ q, long long ldq,
-                    float* __restrict__ scale, long long rows) {
+                    float* __restrict__ scale, long long rows, int vec4) {
     pdl_wait();     // x and rowmax come from earlier kernels in the stream
     pdl_trigger();
     const long long g4n = ldq >> 2, total = rows * g4n;
@@ -654,15 +673,29 @@ im2col1d_q8w_kernel(const float* __restrict__ x, int T, int C, int k, int stride
         const float s = nn_row_scale(m), inv = __fdiv_rn(1.0f, s);
         if (g4 == 0) scale[r] = s;
         int8_t b[4];
-        #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = 4 * g4 + u;
-            float v = 0.0f;
+        if (vec4) {   // C % 4 == 0: the 4 elements are 4 channels of one tap
+            const int e = 4 * g4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (e < K) {
                 const int kt = e / C, t = ot * stride - pad + kt;
-                if (t >= 0 && t < T) v = xf[(long long)t * C + (e - kt * C)];
+                if (t >= 0 && t < T) v = *reinterpret_cast<const float4*>(xf + (long long)t * C + (e - kt * C));
             }
-            b[u] = e < K ? nn_q8(v, inv) : 0;
+            const bool in = e < K;
+            b[0] = in ? nn_q8(v.x, inv) : 0;
+            b[1] = in ? nn_q8(v.y, inv) : 0;
+            b[2] = in ? nn_q8(v.z, inv) : 0;
+            b[3] = in ? nn_q8(v.w, inv) : 0;
+        } else {
+            #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = 4 * g4 + u;
+                float v = 0.0f;
+                if (e < K) {
+                    const int kt = e / C, t = ot * stride - pad + kt;
+                    if (t >= 0 && t < T) v = xf[(long long)t * C + (e - kt * C)];
+                }
+                b[u] = e < K ? nn_q8(v, inv) : 0;
+            }
         }
         *reinterpret_cast<char4*>(q + r * ldq + 4 * g4) = make_char4(b[0], b[1], b[2], b[3]);
     }
@@ -674,8 +707,9 @@ cudaError_t im2col1d_q8w(const float* x, int F, int T, int C, int k, int stride,
         (ldq & 15) || (reinterpret_cast<uintptr_t>(q) & 15) || (!rowmax && (long long)k * C > 64))
         return cudaErrorInvalidValue;
     const long long rows = (long long)F * Tout;
+    const int vec4 = (C % 4 == 0) && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const cudaError_t e = launch_k(im2col1d_q8w_kernel, (unsigned)grid_cap(rows * (ldq >> 2), 256, 148 * 8), 256, 0,
-                                   st, x, T, C, k, stride, pad, Tout, rowmax, q, ldq, scale, rows);
+                                   st, x, T, C, k, stride, pad, Tout, rowmax, q, ldq, scale, rows, vec4);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -611,7 +611,8 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncthreads();
 
     // ---- phase 1: this CTA's partial accumulators -> shared [row][col] int32
-    if (warp >= 2) {
+    // (a plain GEMM's quadrants past the last row hold nothing anyone reads)
+    if (warp >= 2 && (p.conv_bw || mt * kBM + (warp & 3) * 32 < p.M)) {
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
@@ -643,11 +644,16 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     *reinterpret_cast<const int4*>(part + r * kPS + 4 * q);
             }
         }
-        __threadfence();
+        // one thread publishes the CTA's writes (the barrier orders them before
+        // its fence) and counts the arrival; the last arrival acquires the others'
         __syncthreads();
-        if (threadIdx.x == 0) *s_last = atomicAdd(&p.counters[blockIdx.y], 1u) == static_cast<unsigned>(splits - 1);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const bool last = atomicAdd(&p.counters[blockIdx.y], 1u) == static_cast<unsigned>(splits - 1);
+            if (last) __threadfence();
+            *s_last = last ? 1 : 0;
+        }
         __syncthreads();
-        if (*s_last) __threadfence();
     }
 
     // ---- phase 2: sum the cluster's partials for rows rank, rank + splits, ...
@@ -684,10 +690,17 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (m < 0 || n >= p.N) continue;
             int4 sum = make_int4(0, 0, 0, 0);
             if (GLOBAL) {
+                // eight slices' loads in flight at a time (integer sums: any order)
                 const int32_t* src0 = p.ws + (long long)blockIdx.y * splits * p.M * BN + (long long)r * BN + 4 * q;
-                for (int src = 0; src < splits; ++src) {
-                    const int4 v = __ldcg(reinterpret_cast<const int4*>(src0 + (long long)src * p.M * BN));
-                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+                const long long sl = (long long)p.M * BN;
+                for (int s0 = 0; s0 < splits; s0 += 8) {
+                    int4 v[8];
+                    #pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        v[u] = s0 + u < splits ? __ldcg(reinterpret_cast<const int4*>(src0 + (s0 + u) * sl))
+                                               : make_int4(0, 0, 0, 0);
+                    #pragma unroll
+                    for (int u = 0; u < 8; ++u) { sum.x += v[u].x; sum.y += v[u].y; sum.z += v[u].z; sum.w += v[u].w; }
                 }
             } else {
                 const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
@@ -1138,7 +1151,7 @@ bool gemm_i8_skinny_plan(const GemmI8Args& a, GemmPlan* plan) {
     const int bn = a.N >= 1024 ? 128 : a.N >= 256 ? 64 : 32;
     const int n_tiles = (a.N + bn - 1) / bn;
     int splits = sm_count() / n_tiles;
-    if (splits > nkb) splits = nkb;
+    if (splits > nkb / 2) splits = nkb / 2;      // at least two k-blocks per CTA
     if (splits > kMaxGlobalSplits) splits = kMaxGlobalSplits;
     if (nkb < 4 || splits < 2 || n_tiles > a.splitk_counters_n ||
         (long long)n_tiles * splits * a.M * bn > a.splitk_ws_elems)
