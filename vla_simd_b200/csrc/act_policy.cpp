@@ -2,6 +2,8 @@
 // buffer planning, and the kernel sequence of one step.
 #include "act_policy.h"
 
+#include "model_files.h"
+
 #include "f32.h"
 #include "gemm_i8.h"
 #include "host_quant.h"
@@ -43,18 +45,6 @@ bool shape_fits(std::initializer_list<int> dims) {
         if (c > INT_MAX) return false;
     }
     return true;
-}
-
-bool read_floats(const std::string& path, std::vector<float>& out) {
-    std::ifstream f(path, std::ios::binary);
-    if (!f) return false;
-    f.seekg(0, std::ios::end);
-    const std::streamoff end = f.tellg();
-    f.seekg(0);
-    if (end < 0 || end % 4) return false;
-    out.resize(static_cast<size_t>(end) / 4);
-    f.read(reinterpret_cast<char*>(out.data()), end);
-    return static_cast<bool>(f);
 }
 
 // Cursor over a float arena in the converter's order (src/models/arena.h:61-72).
@@ -120,9 +110,10 @@ bool ActPolicy::upload_linear(DevLinear& l, const float* W, const float* b, int 
     return vsb::upload_linear(l, W, b, N, K, int8, [this](size_t n) -> void* { return dalloc<char>(n); }, &n_int8_);
 }
 
-bool ActPolicy::load_config(const std::string& dir) {
-    std::ifstream f(dir + "/config.txt");
-    if (!f) { fail("cannot open config.txt"); return false; }
+bool ActPolicy::load_config(const ModelFiles& files) {
+    std::string text;
+    if (!files.read("config.txt", text)) { fail("cannot open config.txt"); return false; }
+    std::istringstream f(text);
     std::string line;
     while (std::getline(f, line)) {
         std::istringstream ss(line);
@@ -147,9 +138,10 @@ bool ActPolicy::load_config(const std::string& dir) {
     return true;
 }
 
-bool ActPolicy::load_backbone(const std::string& dir, bool int8) {
-    std::ifstream meta(dir + "/backbone.meta");
-    if (!meta) { fail("cannot open backbone.meta"); return false; }
+bool ActPolicy::load_backbone(const ModelFiles& files, bool int8) {
+    std::string meta_text;
+    if (!files.read("backbone.meta", meta_text)) { fail("cannot open backbone.meta"); return false; }
+    std::istringstream meta(meta_text);
     struct BM { int cin, cout, stride, has_down; };
     std::vector<BM> bm;
     int in_ch = 3, gn = 0;
@@ -178,7 +170,7 @@ bool ActPolicy::load_backbone(const std::string& dir, bool int8) {
         return false;
     }
     std::vector<float> data;
-    if (!read_floats(dir + "/backbone.bin", data)) { fail("cannot read backbone.bin"); return false; }
+    if (!files.read_floats("backbone.bin", data)) { fail("cannot read backbone.bin"); return false; }
     Cursor take{data};
     // ACT_I8_CONV_FROM / ACT_I8_CONV_TO (src/models/act/act_model.cpp:57-65,
     // src/models/act/resnet_backbone.cpp:171-188): stage 0 = stem, i+1 = block i.
@@ -218,9 +210,10 @@ bool ActPolicy::load_backbone(const std::string& dir, bool int8) {
     return true;
 }
 
-bool ActPolicy::load_transformer(const std::string& dir, int mask) {
-    std::ifstream meta(dir + "/act.meta");
-    if (!meta) { fail("cannot open act.meta"); return false; }
+bool ActPolicy::load_transformer(const ModelFiles& files, int mask) {
+    std::string meta_text;
+    if (!files.read("act.meta", meta_text)) { fail("cannot open act.meta"); return false; }
+    std::istringstream meta(meta_text);
     std::string line;
     ActConfigDev& c = cfg_;
     while (std::getline(meta, line)) {
@@ -251,7 +244,7 @@ bool ActPolicy::load_transformer(const std::string& dir, int mask) {
         return false;
     }
     std::vector<float> data;
-    if (!read_floats(dir + "/act.bin", data)) { fail("cannot read act.bin"); return false; }
+    if (!files.read_floats("act.bin", data)) { fail("cannot read act.bin"); return false; }
     Cursor take{data};
     const int d = c.dim;
     // bits of ACT_INT8 (src/models/act/act_transformer.cpp:23-27)
@@ -355,10 +348,10 @@ bool ActPolicy::load_transformer(const std::string& dir, int mask) {
     return true;
 }
 
-bool ActPolicy::load_stats(const std::string& dir) {
+bool ActPolicy::load_stats(const ModelFiles& files) {
     std::vector<float> raw;
     const int sd = cfg_.state_dim, ad = cfg_.action_dim;
-    if (!read_floats(dir + "/stats.bin", raw) || raw.size() != (size_t)2 * sd + 2 * ad + (size_t)n_cams_ * 6) {
+    if (!files.read_floats("stats.bin", raw) || raw.size() != (size_t)2 * sd + 2 * ad + (size_t)n_cams_ * 6) {
         fail("stats.bin missing or wrong size");
         return false;
     }
@@ -464,11 +457,14 @@ bool ActPolicy::load(const std::string& dir) {
     i8_clip_ = env_clip();
     const int mask = env_int("ACT_INT8", 0);
 
-    if (!load_config(dir)) return false;
-    if (!load_backbone(dir, (mask & 32) != 0)) return false;
+    // a converted directory or a vla.simd GGUF (src/models/act/act_model.cpp:22-24 mounts it the same way)
+    ModelFiles files;
+    if (!files.open(dir)) { fail(files.error()); return false; }
+    if (!load_config(files)) return false;
+    if (!load_backbone(files, (mask & 32) != 0)) return false;
     if (!alloc_buffers()) return false;   // also fixes the feature map size
-    if (!load_transformer(dir, mask)) return false;
-    if (!load_stats(dir)) return false;
+    if (!load_transformer(files, mask)) return false;
+    if (!load_stats(files)) return false;
     if (env_int("ACT_PROFILE", 0) >= 2)
         std::fprintf(stderr, "[act] int8 GEMMs on device: %d\n", n_int8_);
 

@@ -19,6 +19,8 @@
 
 namespace vsb {
 
+class ModelFiles;
+
 struct DevBlock {
     DevConv conv1, conv2, down;
     bool has_down = false;
@@ -43,7 +45,8 @@ struct DecLayerDev {
 class ActPolicy {
   public:
     ~ActPolicy();
-    // Returns false (with a message in error()) on any load failure.
+    // Returns false (with a message in error()) on any load failure. `dir`: a
+    // converted directory or a vla.simd GGUF (model_files.h).
     bool load(const std::string& dir);
     const std::string& error() const { return err_; }
 
@@ -73,10 +76,10 @@ class ActPolicy {
     cudaError_t forward(cudaStream_t st, bool unnormalize);
 
   private:
-    bool load_config(const std::string& dir);
-    bool load_backbone(const std::string& dir, bool int8);
-    bool load_transformer(const std::string& dir, int mask);
-    bool load_stats(const std::string& dir);
+    bool load_config(const ModelFiles& files);
+    bool load_backbone(const ModelFiles& files, bool int8);
+    bool load_transformer(const ModelFiles& files, int mask);
+    bool load_stats(const ModelFiles& files);
     bool alloc_buffers();
     bool upload_linear(DevLinear& l, const float* W, const float* b, int N, int K, bool int8);
     cudaError_t run_linear(const DevLinear& l, const float* x_f32, const int8_t* xq, const float* xs,

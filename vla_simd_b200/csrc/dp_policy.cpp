@@ -3,6 +3,8 @@
 // query batch.
 #include "dp_policy.h"
 
+#include "model_files.h"
+
 #include "f32.h"
 #include "gemm_i8.h"
 #include "lm_ops.h"
@@ -45,18 +47,6 @@ bool shape_fits(std::initializer_list<long long> dims) {
         if (c > INT_MAX) return false;
     }
     return true;
-}
-
-bool read_floats(const std::string& path, std::vector<float>& out) {
-    std::ifstream f(path, std::ios::binary);
-    if (!f) return false;
-    f.seekg(0, std::ios::end);
-    const std::streamoff end = f.tellg();
-    f.seekg(0);
-    if (end < 0 || end % 4) return false;
-    out.resize(static_cast<size_t>(end) / 4);
-    f.read(reinterpret_cast<char*>(out.data()), end);
-    return static_cast<bool>(f);
 }
 
 struct Cursor {
@@ -140,9 +130,10 @@ void DpPolicy::mish_tail_host(void* p) {
 }
 
 // diffusion.meta as DiffusionModel::load reads it (src/models/diffusion/diffusion_model.cpp:25-103).
-bool DpPolicy::load_meta(const std::string& dir) {
-    std::ifstream meta(dir + "/diffusion.meta");
-    if (!meta) { fail("cannot open diffusion.meta"); return false; }
+bool DpPolicy::load_meta(const ModelFiles& files) {
+    std::string meta_text;
+    if (!files.read("diffusion.meta", meta_text)) { fail("cannot open diffusion.meta"); return false; }
+    std::istringstream meta(meta_text);
     DpConfigDev& c = cfg_;
     std::string line, sched = "DDPM";
     std::vector<int> dd;
@@ -265,11 +256,12 @@ bool DpPolicy::init_schedule() {
 // One observation encoder: "{name}_backbone.meta/.bin" (ResNet with
 // GroupNorm, src/models/act/resnet_backbone.cpp:50-151) and "{name}.bin"
 // (keypoint conv + output projection, src/models/diffusion/rgb_encoder.cpp:30-68).
-bool DpPolicy::load_encoder(const std::string& dir, int idx, bool int8) {
+bool DpPolicy::load_encoder(const ModelFiles& files, int idx, bool int8) {
     DpEncoderDev& e = enc_[idx];
     const std::string name = "rgb_encoder" + std::to_string(idx);
-    std::ifstream meta(dir + "/" + name + "_backbone.meta");
-    if (!meta) { fail("cannot open " + name + "_backbone.meta"); return false; }
+    std::string meta_text;
+    if (!files.read(name + "_backbone.meta", meta_text)) { fail("cannot open " + name + "_backbone.meta"); return false; }
+    std::istringstream meta(meta_text);
     struct BM { int cin, cout, stride, has_down; };
     std::vector<BM> bm;
     int in_ch = 3, gs = 0, block_k = 3;
@@ -300,7 +292,7 @@ bool DpPolicy::load_encoder(const std::string& dir, int idx, bool int8) {
     }
     e.gs = gs;
     std::vector<float> data;
-    if (!read_floats(dir + "/" + name + "_backbone.bin", data)) { fail("cannot read " + name + "_backbone.bin"); return false; }
+    if (!files.read_floats(name + "_backbone.bin", data)) { fail("cannot read " + name + "_backbone.bin"); return false; }
     Cursor take{data};
     const DevAlloc alloc = [this](size_t n) -> void* { return dalloc<char>(n); };
     auto dev_copy = [&](const float* src, size_t n) -> float* {
@@ -359,7 +351,7 @@ bool DpPolicy::load_encoder(const std::string& dir, int idx, bool int8) {
     e.fw = w;
 
     std::vector<float> head;
-    if (!read_floats(dir + "/" + name + ".bin", head)) { fail("cannot read " + name + ".bin"); return false; }
+    if (!files.read_floats(name + ".bin", head)) { fail("cannot read " + name + ".bin"); return false; }
     Cursor t2{head};
     const int K = cfg_.num_keypoints, F2 = 2 * K, C = e.C;
     const float* kw = t2((size_t)K * C);
@@ -382,7 +374,7 @@ bool DpPolicy::load_encoder(const std::string& dir, int idx, bool int8) {
 }
 
 // unet.bin in DPUNet1d::load order (src/models/diffusion/unet1d.cpp:18-160).
-bool DpPolicy::load_unet(const std::string& dir, bool int8) {
+bool DpPolicy::load_unet(const ModelFiles& files, bool int8) {
     const DpConfigDev& c = cfg_;
     const int ndown = static_cast<int>(c.down_dims.size());
     if (c.down_dims.empty() || ndown > 30 || c.n_groups <= 0 || c.step_embed_dim < 4 || c.step_embed_dim % 2 ||
@@ -402,7 +394,7 @@ bool DpPolicy::load_unet(const std::string& dir, bool int8) {
         return false;
     }
     std::vector<float> data;
-    if (!read_floats(dir + "/unet.bin", data)) { fail("cannot read unet.bin"); return false; }
+    if (!files.read_floats("unet.bin", data)) { fail("cannot read unet.bin"); return false; }
     Cursor take{data};
     const DevAlloc alloc = [this](size_t n) -> void* { return dalloc<char>(n); };
     const int A = c.action_dim, D = c.step_embed_dim, CD = c.cond_dim(), k = c.kernel_size;
@@ -485,10 +477,10 @@ bool DpPolicy::load_unet(const std::string& dir, bool int8) {
 
 // stats.bin: state min/max, action min/max, per camera image mean/std
 // (src/models/diffusion/diffusion_model.cpp:123-162), with the same refusals.
-bool DpPolicy::load_stats(const std::string& dir) {
+bool DpPolicy::load_stats(const ModelFiles& files) {
     const int sd = cfg_.state_dim, ad = cfg_.action_dim, N = cfg_.n_cams;
     std::vector<float> raw;
-    if (!read_floats(dir + "/stats.bin", raw) || raw.size() != (size_t)2 * sd + 2 * ad + (size_t)6 * N) {
+    if (!files.read_floats("stats.bin", raw) || raw.size() != (size_t)2 * sd + 2 * ad + (size_t)6 * N) {
         fail("stats.bin missing or wrong size");
         return false;
     }
@@ -711,14 +703,17 @@ bool DpPolicy::load(const std::string& dir, int max_batch) {
     // (src/models/diffusion/diffusion_model.cpp:110-121)
     const int i8 = env_int("DIFFUSION_INT8", 0);
 
-    if (!load_meta(dir) || !init_schedule()) return false;
+    // a converted directory or a vla.simd GGUF (src/models/diffusion/diffusion_model.cpp:25-27 mounts it the same way)
+    ModelFiles files;
+    if (!files.open(dir)) { fail(files.error()); return false; }
+    if (!load_meta(files) || !init_schedule()) return false;
     enc_.resize(cfg_.separate ? cfg_.n_cams : 1);
     for (size_t i = 0; i < enc_.size(); ++i)
-        if (!load_encoder(dir, static_cast<int>(i), (i8 & 2) != 0)) return false;
+        if (!load_encoder(files, static_cast<int>(i), (i8 & 2) != 0)) return false;
     for (const DpEncoderDev& e : enc_)
         if (e.C != enc_[0].C || e.fh != enc_[0].fh || e.fw != enc_[0].fw) { fail("encoders differ in shape"); return false; }
-    if (!load_unet(dir, (i8 & 1) != 0)) return false;
-    if (!load_stats(dir)) return false;
+    if (!load_unet(files, (i8 & 1) != 0)) return false;
+    if (!load_stats(files)) return false;
     if (!alloc_buffers()) return false;
     if (env_int("DP_PROFILE", 0) >= 1)
         std::fprintf(stderr, "[diffusion] int8 GEMMs on device: %d (DIFFUSION_INT8=%d)\n", n_int8_, i8);

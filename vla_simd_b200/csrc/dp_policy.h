@@ -24,6 +24,8 @@
 
 namespace vsb {
 
+class ModelFiles;
+
 struct DpGnConv {           // conv (no bias) followed by GroupNorm, or a conv with bias
     DevConv conv;
     float* gn_s = nullptr;      // null: no GroupNorm (BatchNorm folded into the conv)
@@ -95,7 +97,8 @@ struct DpConfigDev {
 class DpPolicy {
   public:
     ~DpPolicy();
-    // max_batch: the most queries one predict may carry (buffers are sized for it).
+    // max_batch: the most queries one predict may carry (buffers are sized for
+    // it). `dir`: a converted directory or a vla.simd GGUF (model_files.h).
     bool load(const std::string& dir, int max_batch = 1);
     const std::string& error() const { return err_; }
 
@@ -135,11 +138,11 @@ class DpPolicy {
     long long debug_map(float* out, long long cap);
 
   private:
-    bool load_meta(const std::string& dir);
+    bool load_meta(const ModelFiles& files);
     bool init_schedule();
-    bool load_encoder(const std::string& dir, int idx, bool int8);
-    bool load_unet(const std::string& dir, bool int8);
-    bool load_stats(const std::string& dir);
+    bool load_encoder(const ModelFiles& files, int idx, bool int8);
+    bool load_unet(const ModelFiles& files, bool int8);
+    bool load_stats(const ModelFiles& files);
     bool alloc_buffers();
     bool step_features();
     cudaError_t run_encoder(const DpEncoderDev& e, const float* img, int F, unsigned int* slots, float* feat,

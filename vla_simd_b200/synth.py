@@ -331,3 +331,55 @@ def dp_inputs(shape: DpShape = DP_BASELINE, seed: int = 1, batch: int = 0):
     state = rng.standard_normal(lead + (s.n_obs_steps, s.state_dim), dtype=np.float32)
     noise = rng.standard_normal(lead + (1 + s.num_inference_steps, s.horizon, s.action_dim), dtype=np.float32)
     return frames, state, noise
+
+
+# ---------------------------------------------------------------------------
+# vla.simd GGUF packing of a converted directory (the container the reference's
+# converters write by default; read back by src/io/gguf_vla_simd.cpp): GGUF v3,
+# key/value "general.architecture" = "vla-simd", "vla_simd.format" = 1, every
+# text file as the string "vla_simd.file.<name>", every .bin as one F32 tensor
+# named by the file, data aligned to 32 bytes.
+
+def _gguf_str(s: bytes) -> bytes:
+    import struct
+    return struct.pack("<Q", len(s)) + s
+
+
+def pack_gguf(model_dir: str, out_path: str, model: str) -> str:
+    """Pack the files of a converted directory into one vla.simd GGUF at out_path."""
+    import struct
+    align = 32
+    names = sorted(os.listdir(model_dir))
+    kv = [("general.architecture", 8, b"vla-simd"), ("general.name", 8, os.path.basename(out_path).encode()),
+          ("vla_simd.model", 8, model.encode()), ("vla_simd.format", 4, 1), ("vla_simd.source", 8, b"")]
+    bins = []
+    for n in names:
+        path = os.path.join(model_dir, n)
+        if not os.path.isfile(path):
+            continue
+        size = os.path.getsize(path)
+        if n.endswith(".bin") and size:
+            if size % 4:
+                raise ValueError(f"{n}: not a whole number of floats")
+            bins.append((n, path, size))
+        else:
+            kv.append((f"vla_simd.file.{n}", 8, open(path, "rb").read()))
+    head = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(bins), len(kv)))
+    for key, ty, val in kv:
+        head += _gguf_str(key.encode()) + struct.pack("<I", ty)
+        head += _gguf_str(val) if ty == 8 else struct.pack("<I", val)
+    offsets, off = [], 0
+    for n, _, size in bins:
+        off = (off + align - 1) // align * align
+        offsets.append(off)
+        head += _gguf_str(n.encode()) + struct.pack("<IQIQ", 1, size // 4, 0, off)   # 1-D F32
+        off += size
+    with open(out_path, "wb") as f:
+        f.write(head)
+        f.write(b"\0" * (-len(head) % align))
+        base = f.tell()
+        for (_, path, _), o in zip(bins, offsets):
+            f.write(b"\0" * (base + o - f.tell()))
+            with open(path, "rb") as src:
+                f.write(src.read())
+    return out_path
