@@ -42,7 +42,7 @@ ACT_CASES = [("small", synth.ACT_SMALL, 63), ("small", synth.ACT_SMALL, 0), ("sm
 # (seq_q, seq_k, n_q, n_kv): ACT encoder self, decoder self, decoder cross, GQA
 ATTN_CASES = [(602, 602, 8, 8), (100, 100, 8, 8), (100, 602, 8, 8), (50, 113, 15, 5), (3, 40, 4, 2)]
 LN_CASES = [(602, 512), (100, 512), (7, 960)]
-F32_LINEAR_CASES = [(1, 512, 6), (100, 6, 512), (5, 10, 37)]   # (seq, N, K): state_proj, head, odd
+F32_LINEAR_CASES = [(1, 512, 6), (100, 6, 512), (5, 10, 37), (640, 1024, 260), (37, 2048, 259)]   # (seq, N, K): state_proj, head, odd, DP cond (many rows)
 # (cfg, shape name, DIFFUSION_INT8, variant)
 DP_CASES = [("small", "DP_SMALL", 3, ""), ("small", "DP_SMALL", 0, ""), ("small", "DP_SMALL", 1, ""),
             ("small", "DP_SMALL", 3, "ddpm"), ("small", "DP_SMALL", 3, "nonoise"), ("base", "DP_BASELINE", 3, ""),

@@ -369,60 +369,225 @@ cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, in
 // k-1 down to 0, ci in order, zero inputs skipped (src/hal/common/conv.cpp:349-395).
 // That order is kept: every output is one fma chain, advanced tap slot by tap
 // slot (the j-th valid kt of the output, descending), and inside a slot over
-// ci. CTA = 8 output channels x 16 thread rows, a thread owns outputs
-// ot = row + 16i (OPT chains); ci advances in chunks of kCtCi whose W [kCtCi][k][8]
-// and x [T][kCtCi] values stream through a cp.async ring of kCtStages chunks,
-// so many weight bytes are in flight per SM while the chains run. Optional
-// per-row absmax of the output (atomicMax).
-constexpr int kCtCo = 8, kCtCi = 128, kCtRows = 16, kCtMaxK = 4, kCtStages = 4;
+// ci. CTA = CO output channels x all Tout time steps x SB samples; a thread
+// owns ST samples x OTP time steps x 4 channels. Chains of one time step share
+// their tap and input row, so per ci a thread loads one float4 of weights and
+// ST x values and issues ST x 4 fmas per time step. ci advances in chunks of
+// kCtCi whose W [kCtCi][k][CO] and x [SB][T][kCtCi] values stream through a
+// cp.async ring of kCtStages chunks. Optional per-row absmax (atomicMax).
+constexpr int kCtCi = 32, kCtMaxK = 4, kCtStages = 4, kCtThreads = 256;
 constexpr int kCtXs = kCtCi + 4;   // x row stride in shared memory: 16-byte rows, distinct banks per row
 
-__host__ __device__ constexpr size_t convt_stage_floats(int k, int T) {
-    return (size_t)kCtCi * k * kCtCo + (size_t)T * kCtXs;
+__host__ __device__ constexpr size_t convt_stage_floats(int k, int xrows, int co) {
+    return (size_t)kCtCi * k * co + (size_t)xrows * kCtXs;
+}
+
+template <int ST, int OTP, int CO>
+__global__ void __launch_bounds__(kCtThreads)
+conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                              const float* __restrict__ bias, float* __restrict__ out, int F, int T, int Cin,
+                              int Cout, int k, int stride, int pad, int Tout, int SB, int slots,
+                              unsigned int* __restrict__ rowmax) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    extern __shared__ __align__(16) float ct_smem[];
+    constexpr int NQ = CO / 4;                     // 4-channel groups per CTA
+    const int n_otg = Tout / OTP;                  // thread groups over time steps
+    const int cq = threadIdx.x % NQ;
+    const int otg = (threadIdx.x / NQ) % n_otg;
+    const int sg = (threadIdx.x / NQ) / n_otg;     // sample group
+    const int co0 = blockIdx.x * CO, f0 = blockIdx.y * SB;
+    const int sb = min(SB, F - f0);
+    const int co = co0 + 4 * cq;
+    const int xrows = SB * T;
+    const size_t stage_fl = convt_stage_floats(k, xrows, CO);
+    const int nchunk = (Cin + kCtCi - 1) / kCtCi;
+    const int iters = slots * nchunk;              // (slot, chunk) in chain order
+    const bool thread_live = sg * ST < sb;
+    float acc[OTP][ST][4];
+    #pragma unroll
+    for (int jo = 0; jo < OTP; ++jo)
+        #pragma unroll
+        for (int si = 0; si < ST; ++si)
+            #pragma unroll
+            for (int u = 0; u < 4; ++u) acc[jo][si][u] = (bias && co + u < Cout) ? bias[co + u] : 0.0f;
+    auto issue = [&](int it, int stg) {
+        const int c = it % nchunk;
+        float* sW = ct_smem + (size_t)stg * stage_fl;
+        float* sx = sW + (size_t)kCtCi * k * CO;
+        const int ci0 = c * kCtCi;
+        for (int e = threadIdx.x; e < kCtCi * k * NQ; e += blockDim.x) {
+            const int q = e % NQ, r = e / NQ, kt = r % k, ci = ci0 + r / k;
+            const bool ok = ci < Cin;
+            cp_async16(sW + (size_t)r * CO + 4 * q, W + ((long long)(ok ? ci : 0) * k + kt) * Cout + co0 + 4 * q,
+                       ok ? 16 : 0);
+        }
+        for (int e = threadIdx.x; e < xrows * (kCtCi / 4); e += blockDim.x) {
+            const int row = e / (kCtCi / 4), q = e - row * (kCtCi / 4), ci = ci0 + 4 * q;
+            const int s_ = row / T, t = row - s_ * T;
+            const bool ok = ci < Cin && s_ < sb;
+            cp_async16(sx + (size_t)row * kCtXs + 4 * q,
+                       x + ((long long)(ok ? f0 + s_ : 0) * T + t) * Cin + (ok ? ci : 0), ok ? 16 : 0);
+        }
+    };
+    for (int s0 = 0; s0 < kCtStages - 1; ++s0) {
+        if (s0 < iters) issue(s0, s0);
+        cp_async_commit();
+    }
+    int cur_slot = -1;
+    int kt_i[OTP], t_i[OTP];
+    for (int it = 0; it < iters; ++it) {
+        const int j = it / nchunk, c = it - j * nchunk;
+        if (j != cur_slot) {      // this slot's tap and input step per time step (-1: none)
+            cur_slot = j;
+            #pragma unroll
+            for (int jo = 0; jo < OTP; ++jo) {
+                const int ot = otg * OTP + jo;
+                kt_i[jo] = -1;
+                t_i[jo] = 0;
+                int seen = 0;
+                for (int kt = k - 1; kt >= 0; --kt) {
+                    const int num = ot + pad - kt;
+                    if (num < 0 || num % stride) continue;
+                    const int t = num / stride;
+                    if (t >= T) continue;
+                    if (seen++ == j) { kt_i[jo] = kt; t_i[jo] = t; break; }
+                }
+            }
+        }
+        asm volatile("cp.async.wait_group %0;" :: "n"(kCtStages - 2) : "memory");
+        __syncthreads();
+        // refill the stage the previous iteration read (every thread is past it)
+        if (it + kCtStages - 1 < iters) issue(it + kCtStages - 1, (it + kCtStages - 1) % kCtStages);
+        cp_async_commit();
+        if (!thread_live) continue;
+        const float* sW = ct_smem + (size_t)(it % kCtStages) * stage_fl;
+        const float* sx = sW + (size_t)kCtCi * k * CO;
+        const int cmax = min(kCtCi, Cin - c * kCtCi);
+        #pragma unroll
+        for (int jo = 0; jo < OTP; ++jo) {
+            if (kt_i[jo] < 0) continue;
+            const float* wrow = sW + (size_t)kt_i[jo] * CO + 4 * cq;
+            const float* xrow = sx + (size_t)(sg * ST * T + t_i[jo]) * kCtXs;
+            for (int ci = 0; ci < cmax; ++ci) {
+                const float4 w4 = *reinterpret_cast<const float4*>(wrow + (size_t)ci * k * CO);
+                #pragma unroll
+                for (int si = 0; si < ST; ++si) {
+                    const float v = xrow[(size_t)si * T * kCtXs + ci];
+                    if (v == 0.0f) continue;
+                    acc[jo][si][0] = __fmaf_rn(v, w4.x, acc[jo][si][0]);
+                    acc[jo][si][1] = __fmaf_rn(v, w4.y, acc[jo][si][1]);
+                    acc[jo][si][2] = __fmaf_rn(v, w4.z, acc[jo][si][2]);
+                    acc[jo][si][3] = __fmaf_rn(v, w4.w, acc[jo][si][3]);
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    #pragma unroll
+    for (int jo = 0; jo < OTP; ++jo) {
+        const int ot = otg * OTP + jo;
+        #pragma unroll
+        for (int si = 0; si < ST; ++si) {
+            const int sl = sg * ST + si;
+            const bool live = sl < sb;
+            const long long orow = (long long)(f0 + sl) * Tout + ot;
+            float m = 0.0f;
+            if (live) {
+                #pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (co + u < Cout) {
+                        out[orow * Cout + co + u] = acc[jo][si][u];
+                        m = fmaxf(m, fabsf(acc[jo][si][u]));
+                    }
+            }
+            if (rowmax) {
+                // the CO channels of this row sit in NQ consecutive lanes; every
+                // lane of the warp takes part in the shuffles
+                #pragma unroll
+                for (int off = NQ / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+                if (cq == 0 && live) atomicMax(&rowmax[orow], __float_as_uint(m));
+            }
+        }
+    }
+}
+
+template <int ST, int OTP, int CO>
+cudaError_t launch_convt(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
+                         int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax, cudaStream_t st) {
+    const int slots = (k + stride - 1) / stride;
+    const int per_group = (CO / 4) * (Tout / OTP);          // threads per sample group
+    const int groups = kCtThreads / per_group;
+    int SB = groups * ST;
+    if (SB > F) SB = F;
+    // whole warps (the row-absmax shuffles take every lane); extra threads own no chain
+    const int threads = (per_group * ((SB + ST - 1) / ST) + 31) & ~31;
+    const size_t smem = sizeof(float) * kCtStages * convt_stage_floats(k, SB * T, CO);
+    if (groups < 1 || smem > 200 * 1024 || Cout % CO) return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(conv_transpose1d_tiled_kernel<ST, OTP, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        attr = true;
+    }
+    return launch_k(conv_transpose1d_tiled_kernel<ST, OTP, CO>,
+                    dim3((unsigned)(Cout / CO), (unsigned)((F + SB - 1) / SB)), (unsigned)threads, smem, st, x, W,
+                    bias, out, F, T, Cin, Cout, k, stride, pad, Tout, SB, slots, rowmax);
+}
+
+// Few samples (batch 1): CTA = 8 output channels x 16 thread rows, a thread
+// owns OPT chains of one sample, ci in chunks of 128 through the same kind of
+// cp.async ring: more CTAs and threads per output than the tiled kernel above,
+// which is what a lone sample's latency needs. Same per-output order.
+constexpr int kChCo = 8, kChCi = 128, kChRows = 16, kChMaxK = 4, kChStages = 4;
+constexpr int kChXs = kChCi + 4;   // x row stride in shared memory: 16-byte rows, distinct banks per row
+
+__host__ __device__ constexpr size_t convt_chain_stage_floats(int k, int T) {
+    return (size_t)kChCi * k * kChCo + (size_t)T * kChXs;
 }
 
 template <int OPT>
 __global__ void __launch_bounds__(128)
-conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restrict__ W,
+conv_transpose1d_chain_kernel(const float* __restrict__ x, const float* __restrict__ W,
                               const float* __restrict__ bias, float* __restrict__ out, int T, int Cin, int Cout,
                               int k, int stride, int pad, int Tout, int slots, unsigned int* __restrict__ rowmax) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     extern __shared__ __align__(16) float ct_smem[];
-    const int tx = threadIdx.x & (kCtCo - 1), ty = threadIdx.x / kCtCo;
-    const int co0 = blockIdx.x * kCtCo, f = blockIdx.y;
+    const int tx = threadIdx.x & (kChCo - 1), ty = threadIdx.x / kChCo;
+    const int co0 = blockIdx.x * kChCo, f = blockIdx.y;
     const int co = co0 + tx;
     const float* xf = x + (long long)f * T * Cin;
-    const size_t stage_fl = convt_stage_floats(k, T);
-    const int nchunk = (Cin + kCtCi - 1) / kCtCi;
+    const size_t stage_fl = convt_chain_stage_floats(k, T);
+    const int nchunk = (Cin + kChCi - 1) / kChCi;
     const int iters = slots * nchunk;           // (slot, chunk) in chain order
     float acc[OPT];
     int ot[OPT];
     #pragma unroll
     for (int i = 0; i < OPT; ++i) {
-        ot[i] = ty + kCtRows * i;
+        ot[i] = ty + kChRows * i;
         acc[i] = (bias && co < Cout) ? bias[co] : 0.0f;
     }
     // cp.async of chunk c (ci block) into ring stage s: W rows (ci, kt) of 8
-    // floats (two 16-byte pieces) and x rows t of kCtCi floats; zero past Cin
+    // floats (two 16-byte pieces) and x rows t of kChCi floats; zero past Cin
     auto issue = [&](int it, int stg) {
         const int c = it % nchunk;
         float* sW = ct_smem + (size_t)stg * stage_fl;
-        float* sx = sW + (size_t)kCtCi * k * kCtCo;
-        const int ci0 = c * kCtCi;
-        for (int e = threadIdx.x; e < kCtCi * k * 2; e += blockDim.x) {
+        float* sx = sW + (size_t)kChCi * k * kChCo;
+        const int ci0 = c * kChCi;
+        for (int e = threadIdx.x; e < kChCi * k * 2; e += blockDim.x) {
             const int half = e & 1, r = e >> 1, kt = r % k, ci = ci0 + r / k;
             const bool ok = ci < Cin;
-            cp_async16(sW + (size_t)r * kCtCo + half * 4,
+            cp_async16(sW + (size_t)r * kChCo + half * 4,
                        W + ((long long)(ok ? ci : 0) * k + kt) * Cout + co0 + half * 4, ok ? 16 : 0);
         }
-        for (int e = threadIdx.x; e < T * (kCtCi / 4); e += blockDim.x) {
-            const int t = e / (kCtCi / 4), q = e - t * (kCtCi / 4), ci = ci0 + 4 * q;
+        for (int e = threadIdx.x; e < T * (kChCi / 4); e += blockDim.x) {
+            const int t = e / (kChCi / 4), q = e - t * (kChCi / 4), ci = ci0 + 4 * q;
             const bool ok = ci < Cin;
-            cp_async16(sx + (size_t)t * kCtXs + 4 * q, xf + (long long)t * Cin + (ok ? ci : 0), ok ? 16 : 0);
+            cp_async16(sx + (size_t)t * kChXs + 4 * q, xf + (long long)t * Cin + (ok ? ci : 0), ok ? 16 : 0);
         }
     };
-    for (int s0 = 0; s0 < kCtStages - 1; ++s0) {
+    for (int s0 = 0; s0 < kChStages - 1; ++s0) {
         if (s0 < iters) issue(s0, s0);
         cp_async_commit();
     }
@@ -447,23 +612,23 @@ conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restri
                 }
             }
         }
-        asm volatile("cp.async.wait_group %0;" :: "n"(kCtStages - 2) : "memory");
+        asm volatile("cp.async.wait_group %0;" :: "n"(kChStages - 2) : "memory");
         __syncthreads();
         // refill the stage the previous iteration read (every thread is past it)
-        if (it + kCtStages - 1 < iters) issue(it + kCtStages - 1, (it + kCtStages - 1) % kCtStages);
+        if (it + kChStages - 1 < iters) issue(it + kChStages - 1, (it + kChStages - 1) % kChStages);
         cp_async_commit();
-        const float* sW = ct_smem + (size_t)(it % kCtStages) * stage_fl;
-        const float* sx = sW + (size_t)kCtCi * k * kCtCo;
-        const int cmax = min(kCtCi, Cin - c * kCtCi);
+        const float* sW = ct_smem + (size_t)(it % kChStages) * stage_fl;
+        const float* sx = sW + (size_t)kChCi * k * kChCo;
+        const int cmax = min(kChCi, Cin - c * kChCi);
         #pragma unroll
         for (int i = 0; i < OPT; ++i) {
             if (kt_i[i] < 0) continue;
-            const float* xr = sx + (size_t)t_i[i] * kCtXs;
-            const float* wr = sW + (size_t)kt_i[i] * kCtCo + tx;
+            const float* xr = sx + (size_t)t_i[i] * kChXs;
+            const float* wr = sW + (size_t)kt_i[i] * kChCo + tx;
             for (int ci = 0; ci < cmax; ++ci) {
                 const float v = xr[ci];
                 if (v == 0.0f) continue;
-                acc[i] = __fmaf_rn(v, wr[(size_t)ci * k * kCtCo], acc[i]);
+                acc[i] = __fmaf_rn(v, wr[(size_t)ci * k * kChCo], acc[i]);
             }
         }
     }
@@ -484,33 +649,50 @@ conv_transpose1d_tiled_kernel(const float* __restrict__ x, const float* __restri
 }
 
 template <int OPT>
-cudaError_t launch_convt(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
+cudaError_t launch_convt_chain(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
                          int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax, cudaStream_t st) {
     const int slots = (k + stride - 1) / stride;
-    const size_t smem = sizeof(float) * kCtStages * convt_stage_floats(k, T);
+    const size_t smem = sizeof(float) * kChStages * convt_chain_stage_floats(k, T);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(conv_transpose1d_tiled_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(conv_transpose1d_chain_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              200 * 1024);
         attr = true;
     }
-    return launch_k(conv_transpose1d_tiled_kernel<OPT>, dim3((unsigned)(Cout / kCtCo), (unsigned)F), 128, smem, st,
+    return launch_k(conv_transpose1d_chain_kernel<OPT>, dim3((unsigned)(Cout / kChCo), (unsigned)F), 128, smem, st,
                     x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
 }
 
 cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
                                int Cout, int k, int stride, int pad, unsigned int* rowmax, cudaStream_t st) {
     const int Tout = (T - 1) * stride - 2 * pad + k;
-    // 16-byte cp.async rows: Cin and Cout multiples of 4 / 8 and aligned bases
+    // 16-byte cp.async rows; time steps spread over at most 256 / 8 thread groups x 4 per thread
     if (F <= 0 || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || k > kCtMaxK || stride <= 0 || pad < 0 || Tout <= 0 ||
-        Tout > 4 * kCtRows || Cin % 4 || Cout % kCtCo || F > 65535 ||
+        Tout > 4 * (kCtThreads / 8) || T > 64 || Cin % 4 || Cout % 8 || F > 65535 ||
         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W)) & 15))
         return cudaErrorInvalidValue;
+    const int OTP = Tout <= 32 ? 1 : Tout <= 64 ? 2 : 4;
+    if (Tout % OTP) return cudaErrorInvalidValue;
+    if (F < 4 && Tout <= 4 * kChRows && Cout % kChCo == 0) {
+        // a lone sample (or two, three): one sample per CTA row, one chain per thread
+        cudaError_t e2;
+        if (Tout <= kChRows) e2 = launch_convt_chain<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        else if (Tout <= 2 * kChRows) e2 = launch_convt_chain<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        else e2 = launch_convt_chain<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        if (e2 != cudaSuccess) return e2;
+        return cudaGetLastError();
+    }
+    // many samples: 32 channels x 4 samples per CTA tile (weights reused across
+    // the samples); otherwise 8 channels per CTA
+    const bool wide = F >= 4 && Cout % 32 == 0;
     cudaError_t e;
-    if (Tout <= kCtRows) e = launch_convt<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
-    else if (Tout <= 2 * kCtRows) e = launch_convt<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
-    else e = launch_convt<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    if (OTP == 1) e = wide ? launch_convt<4, 1, 32>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st)
+                           : launch_convt<1, 1, 8>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else if (OTP == 2) e = wide ? launch_convt<4, 2, 32>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st)
+                                : launch_convt<1, 2, 8>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+    else e = wide ? launch_convt<4, 4, 32>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st)
+                  : launch_convt<1, 4, 8>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -1115,9 +1115,108 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
     }
 }
 
+// The same outputs for many rows (N % 4 == 0: every output takes mm_block4's
+// order; K <= 512). CTA = 32 rows x 32 outputs with both operand tiles staged
+// whole in shared memory; a thread owns a 2 x 2 block of outputs and runs, per
+// output, the 16 lane chains (a[l] over k = 16s + l, b[l] over 16s + 8 + l),
+// the 8-wide step into a, t = a + b, hsum8, the fused scalar tail and + bias
+// in registers: bit for bit the warp kernel's arithmetic, with each staged
+// value feeding two outputs.
+constexpr int kLtRows = 32;
+
+__global__ void __launch_bounds__(256)
+linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ W,
+                        const float* __restrict__ bias, float* __restrict__ out, long long ldo, int M, int N, int K,
+                        const float* __restrict__ post_mul, const float* __restrict__ post_add) {
+    pdl_wait();     // inputs come from the previous kernel in the stream
+    pdl_trigger();
+    extern __shared__ __align__(16) float lt_smem[];
+    const int ldk = ((K + 3) & ~3) + 4;            // 16-byte rows, rows 4 banks apart
+    float* sx = lt_smem;
+    float* sw = lt_smem + kLtRows * ldk;
+    const int m0 = blockIdx.y * kLtRows, n0 = blockIdx.x * kLtRows;
+    for (int e = threadIdx.x; e < kLtRows * K; e += blockDim.x) {
+        const int r = e / K, c = e - r * K;
+        sx[r * ldk + c] = m0 + r < M ? x[(long long)(m0 + r) * ldx + c] : 0.0f;
+        sw[r * ldk + c] = n0 + r < N ? W[(long long)(n0 + r) * K + c] : 0.0f;
+    }
+    __syncthreads();
+    const int tm = threadIdx.x >> 4, tn = threadIdx.x & 15;
+    const float* xr[2] = {sx + tm * ldk, sx + (tm + 16) * ldk};
+    const float* wr[2] = {sw + tn * ldk, sw + (tn + 16) * ldk};
+    float acc[2][2][16];
+    #pragma unroll
+    for (int i = 0; i < 2; ++i)
+        #pragma unroll
+        for (int j = 0; j < 2; ++j)
+            #pragma unroll
+            for (int l = 0; l < 16; ++l) acc[i][j][l] = 0.0f;
+    const int K16 = K & ~15;
+    for (int k = 0; k < K16; k += 16) {
+        #pragma unroll
+        for (int q = 0; q < 4; ++q) {              // lanes 4q .. 4q+3 of the 16
+            const float4 x0 = *reinterpret_cast<const float4*>(xr[0] + k + 4 * q);
+            const float4 x1 = *reinterpret_cast<const float4*>(xr[1] + k + 4 * q);
+            const float4 w0 = *reinterpret_cast<const float4*>(wr[0] + k + 4 * q);
+            const float4 w1 = *reinterpret_cast<const float4*>(wr[1] + k + 4 * q);
+            const float xv[2][4] = {{x0.x, x0.y, x0.z, x0.w}, {x1.x, x1.y, x1.z, x1.w}};
+            const float wv[2][4] = {{w0.x, w0.y, w0.z, w0.w}, {w1.x, w1.y, w1.z, w1.w}};
+            #pragma unroll
+            for (int i = 0; i < 2; ++i)
+                #pragma unroll
+                for (int j = 0; j < 2; ++j)
+                    #pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        acc[i][j][4 * q + u] = __fmaf_rn(xv[i][u], wv[j][u], acc[i][j][4 * q + u]);
+        }
+    }
+    int kend = K16;
+    if (K - K16 >= 8) {                  // one 8-wide step into a
+        #pragma unroll
+        for (int i = 0; i < 2; ++i)
+            #pragma unroll
+            for (int j = 0; j < 2; ++j)
+                #pragma unroll
+                for (int l = 0; l < 8; ++l)
+                    acc[i][j][l] = __fmaf_rn(xr[i][K16 + l], wr[j][K16 + l], acc[i][j][l]);
+        kend = K16 + 8;
+    }
+    #pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        #pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int m = m0 + tm + 16 * i, n = n0 + tn + 16 * j;
+            float t[8];
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) t[l] = __fadd_rn(acc[i][j][l], acc[i][j][8 + l]);
+            float sum = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[4]), __fadd_rn(t[1], t[5])),
+                                  __fadd_rn(__fadd_rn(t[2], t[6]), __fadd_rn(t[3], t[7])));
+            for (int k = kend; k < K; ++k) sum = __fmaf_rn(xr[i][k], wr[j][k], sum);
+            if (m < M && n < N) {
+                float v = bias ? __fadd_rn(sum, bias[n]) : sum;
+                if (post_mul) v = __fmaf_rn(v, post_mul[n], post_add[n]);
+                out[(long long)m * ldo + n] = v;
+            }
+        }
+    }
+}
+
 cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
+    if (N % 4 == 0 && K <= 512 && M >= kLtRows && (long long)M * N >= (1LL << 16)) {
+        const size_t smem = sizeof(float) * 2 * kLtRows * (((K + 3) & ~3) + 4);
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(linear_f32_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            attr = true;
+        }
+        const dim3 grid((unsigned)((N + kLtRows - 1) / kLtRows), (unsigned)((M + kLtRows - 1) / kLtRows));
+        const cudaError_t le_ = launch_k(linear_f32_tiled_kernel, grid, 256, smem, st, x, ldx, W, bias, out, ldo, M,
+                                         N, K, post_mul, post_add);
+        if (le_ != cudaSuccess) return le_;
+        return cudaGetLastError();
+    }
     const long long threads = (long long)M * N * 32;
     {
         const cudaError_t le_ = launch_k(linear_f32_kernel, (int)((threads + 255) / 256), 256, 0, st,
