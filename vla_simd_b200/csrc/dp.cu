@@ -273,93 +273,31 @@ cudaError_t gn_apply(const float* x, const float* A, const float* B, float* out,
     return cudaGetLastError();
 }
 
-// --------------------------------------------------- 1D im2col + quantize
-// Block = one output row (sample f, time ot): the k*C fp32 patch values are
-// formed once in shared memory (zero for taps outside [0, T)), then the row
-// absmax, scale and int8 codes exactly as quantize_act_i8. Q8 = false writes
-// the fp32 row to colf [F*Tout][k*C] instead (fp32 layers).
-template <bool Q8>
-__global__ void __launch_bounds__(256)
-im2col1d_kernel(const float* __restrict__ x, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
-                const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ film,
-                long long ld_film, int film_scale, int8_t* __restrict__ q, long long ldq,
-                float* __restrict__ scale, float* __restrict__ colf) {
+// ------------------------------------------------------------ 1D im2col
+// fp32 im2col rows of F samples (fp32 U-Net layers): colf [F*Tout][k*C], row
+// (f, ot) = the k input rows ot*stride - pad + kt (zero outside [0, T))
+// (src/hal/common/conv.cpp:334-347).
+__global__ void im2col1d_f32_kernel(const float* __restrict__ x, int T, int C, long long ldx, int k, int stride,
+                                    int pad, int Tout, float* __restrict__ colf, long long total) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    extern __shared__ float row[];
-    __shared__ float sh[32];
-    const int r = blockIdx.x;
-    const int f = r / Tout, ot = r - f * Tout;
-    const int K = k * C;
-    const float* xf = x + (long long)f * T * ldx;
-    const float* Af = A ? A + (long long)f * C : nullptr;
-    const float* Bf = B ? B + (long long)f * C : nullptr;
-    const float* ff = film ? film + (long long)f * ld_film : nullptr;
-    float m = 0.0f;
-    for (int e = threadIdx.x; e < K; e += blockDim.x) {
+    const long long K = (long long)k * C;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / K;
+        const int e = static_cast<int>(i - r * K);
+        const int f = static_cast<int>(r / Tout), ot = static_cast<int>(r - (long long)f * Tout);
         const int kt = e / C, c = e - kt * C;
         const int t = ot * stride - pad + kt;
-        float v = 0.0f;
-        if (t >= 0 && t < T) {
-            v = xf[(long long)t * ldx + c];
-            if (Af) {
-                v = mish_lanes(__fmaf_rn(v, Af[c], Bf[c]));
-                if (ff) v = film_scale ? __fmaf_rn(ff[c], v, ff[C + c]) : __fadd_rn(v, ff[c]);
-            }
-        }
-        if (!Q8) {
-            colf[(long long)r * K + e] = v;
-            continue;
-        }
-        row[e] = v;
-        m = fmaxf(m, fabsf(v));
+        colf[i] = (t >= 0 && t < T) ? x[((long long)f * T + t) * ldx + c] : 0.0f;
     }
-    if (!Q8) return;
-    m = block_max_256(m, sh);    // (its barriers also order the row writes)
-    const float s = nn_row_scale(m), inv = __fdiv_rn(1.0f, s);
-    int8_t* qr = q + (long long)r * ldq;
-    for (int e4 = 4 * threadIdx.x; e4 < ldq; e4 += 4 * blockDim.x) {
-        char4 o;
-        o.x = e4 + 0 < K ? nn_q8(row[e4 + 0], inv) : 0;
-        o.y = e4 + 1 < K ? nn_q8(row[e4 + 1], inv) : 0;
-        o.z = e4 + 2 < K ? nn_q8(row[e4 + 2], inv) : 0;
-        o.w = e4 + 3 < K ? nn_q8(row[e4 + 3], inv) : 0;
-        *reinterpret_cast<char4*>(qr + e4) = o;
-    }
-    if (threadIdx.x == 0) scale[r] = s;
-}
-
-cudaError_t im2col1d_q8(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
-                        const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
-                        int8_t* q, long long ldq, float* scale, cudaStream_t st) {
-    const long long K = (long long)k * C;
-    if (F <= 0 || T <= 0 || C <= 0 || ldx < C || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0 || ldq < K ||
-        (ldq & 15) || (reinterpret_cast<uintptr_t>(q) & 15) || (A && !B) || (film && !A) ||
-        (long long)F * Tout > 2147483647LL)
-        return cudaErrorInvalidValue;
-    const size_t smem = (size_t)K * sizeof(float);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(im2col1d_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
-    const cudaError_t e = launch_k(im2col1d_kernel<true>, (unsigned)(F * Tout), 256, smem, st, x, T, C, ldx, k, stride,
-                                   pad, Tout, A, B, film, ld_film, film_scale ? 1 : 0, q, ldq, scale,
-                                   static_cast<float*>(nullptr));
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
 }
 
 cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
-                          const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
                           float* colf, cudaStream_t st) {
-    if (F <= 0 || T <= 0 || C <= 0 || ldx < C || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0 || (A && !B) ||
-        (film && !A) || (long long)F * Tout > 2147483647LL)
-        return cudaErrorInvalidValue;
-    const cudaError_t e = launch_k(im2col1d_kernel<false>, (unsigned)(F * Tout), 256, 0, st, x, T, C, ldx, k, stride,
-                                   pad, Tout, A, B, film, ld_film, film_scale ? 1 : 0, static_cast<int8_t*>(nullptr),
-                                   0LL, static_cast<float*>(nullptr), colf);
+    if (F <= 0 || T <= 0 || C <= 0 || ldx < C || k <= 0 || stride <= 0 || pad < 0 || Tout <= 0) return cudaErrorInvalidValue;
+    const long long total = (long long)F * Tout * k * C;
+    const cudaError_t e = launch_k(im2col1d_f32_kernel, (unsigned)grid_cap(total, 256, 148 * 8), 256, 0, st, x, T, C,
+                                   ldx, k, stride, pad, Tout, colf, total);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

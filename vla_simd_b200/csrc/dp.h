@@ -33,20 +33,9 @@ cudaError_t gn_affine(const float* x, int F, int npx, int C, long long ld, int g
 cudaError_t gn_apply(const float* x, const float* A, const float* B, float* out, int F, int npx, int C, long long ld,
                      int epi, const float* res, unsigned int* amax, cudaStream_t st);
 
-// Per-row int8 quantization of the 1D im2col of x [F][T][ldx] (C channels;
-// taps kt at ot*stride - pad + kt, zero outside [0, T)) ->
-// q [F*Tout][ldq], scale [F*Tout]: quantize_act_i8 of each fp32 im2col row
-// (src/hal/common/conv.cpp:334-347 then src/hal/common/gemm_i8.cpp:209-244).
-// With A/B non-null the taps read mish(fma(x, A, B)) (the GroupNorm + Mish of
-// the previous conv), then, with film non-null, FiLM: fma(sc, v, bi) with
-// sc = film[f][c], bi = film[f][C + c] (film_scale) or v + film[f][c].
-cudaError_t im2col1d_q8(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
-                        const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
-                        int8_t* q, long long ldq, float* scale, cudaStream_t st);
-
-// The same im2col with the fp32 rows written to colf [F*Tout][k*C] (fp32 layers).
+// fp32 1D im2col of F samples x [F][T][ldx] (C channels) -> colf [F*Tout][k*C]
+// (src/hal/common/conv.cpp:334-347), for the fp32 U-Net layers.
 cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, int k, int stride, int pad, int Tout,
-                          const float* A, const float* B, const float* film, long long ld_film, bool film_scale,
                           float* colf, cudaStream_t st);
 
 // cat [F][T][C1 + C2] = [a [F][T][C1] | b [F][T][C2]] per time step, with each

@@ -909,7 +909,7 @@ cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsi
         a.splitk_counters_n = ws_main_.n_counters;
         return gemm_i8(a, st);
     }
-    VSB_TRY(im2col1d_f32x(x, B, T, C, C, k, stride, pad, Tout, nullptr, nullptr, nullptr, 0, false, d_colf_, st));
+    VSB_TRY(im2col1d_f32x(x, B, T, C, C, k, stride, pad, Tout, d_colf_, st));
     return gemm_f32(d_colf_, l.K, l.W, l.K, l.bias, out, l.N, nullptr, 0, B * Tout, l.N, l.K, 0, rm_out, 1, st);
 }
 
