@@ -46,7 +46,8 @@ F32_LINEAR_CASES = [(1, 512, 6), (100, 6, 512), (5, 10, 37), (640, 1024, 260), (
 # (cfg, shape name, DIFFUSION_INT8, variant)
 DP_CASES = [("small", "DP_SMALL", 3, ""), ("small", "DP_SMALL", 0, ""), ("small", "DP_SMALL", 1, ""),
             ("small", "DP_SMALL", 3, "ddpm"), ("small", "DP_SMALL", 3, "nonoise"), ("base", "DP_BASELINE", 3, ""),
-            ("base", "DP_BASELINE", 0, "")]
+            ("base", "DP_BASELINE", 0, ""), ("edge", "DP_EDGE", 3, ""), ("edge", "DP_EDGE", 0, ""),
+            ("edge", "DP_EDGE", 2, ""), ("deep", "DP_DEEP", 3, ""), ("deep", "DP_DEEP", 0, "")]
 GEMM_SHAPES = [(1, 16, 3), (7, 48, 64), (13, 64, 17), (257, 96, 48), (50, 768, 1027), (602, 3200, 512),
                (602, 512, 3200), (300, 512, 512)]
 
@@ -115,7 +116,7 @@ def make_dp(digests):
                     "import dataclasses; sh = dataclasses.replace(sh, num_inference_steps=%d); "
                     "f, s, n = synth.dp_inputs(sh, seed=1); "
                     "np.save(%r, r.dp_predict(%r, f, s, %s))") % (
-                        ROOT, shape_name, 10, os.path.join(HERE, dp_fixture_name(cfg, mask, variant)), d,
+                        ROOT, shape_name, getattr(synth, shape_name).num_inference_steps, os.path.join(HERE, dp_fixture_name(cfg, mask, variant)), d,
                         "None" if variant == "nonoise" else "n")
             env = dict(os.environ, DIFFUSION_INT8=str(mask), OMP_NUM_THREADS="1")
             if variant == "ddpm":

@@ -82,6 +82,37 @@ def test_baseline_dp_matches_reference(tmp_path, monkeypatch, mask):
     pol.close()
 
 
+# (config, shape, DIFFUSION_INT8, the reference's int8 layer count on that checkpoint)
+EDGE_CASES = [("edge", synth.DP_EDGE, 3, 41), ("edge", synth.DP_EDGE, 0, 0), ("edge", synth.DP_EDGE, 2, 20),
+              ("deep", synth.DP_DEEP, 3, 63), ("deep", synth.DP_DEEP, 0, 0)]
+
+
+@pytest.mark.parametrize("cfg,shape,mask,n_int8", EDGE_CASES, ids=[f"{c[0]}-m{c[2]}" for c in EDGE_CASES])
+def test_edge_dp_matches_reference(tmp_path, monkeypatch, cfg, shape, mask, n_int8):
+    """Shared encoder over two cameras, no crop, folded-BatchNorm backbone,
+    bias-only FiLM, kernel 3, two U-Net levels, scaled_linear betas without
+    clipping (edge); one camera and observation step, a 1x1 feature map, four
+    U-Net levels on horizon 32, linear betas (deep)."""
+    pol = _policy(tmp_path, shape, mask, monkeypatch)
+    assert pol.int8_layers == n_int8
+    f, s, n = synth.dp_inputs(shape, seed=1)
+    got = pol.predict(f, s, n)
+    err = np.abs(got - _want(cfg, mask)).max()
+    print(f"DP {cfg} mask {mask} max-abs vs reference: {err:.3g}")
+    assert err <= TOL
+    pol.close()
+
+
+def test_shared_encoder_batch_equals_single_queries(tmp_path, monkeypatch):
+    B = 3
+    pol = _policy(tmp_path, synth.DP_EDGE, 3, monkeypatch, max_batch=B)
+    f, s, n = synth.dp_inputs(synth.DP_EDGE, seed=5, batch=B)
+    got = pol.predict_batch(f, s, n)
+    for b in range(B):
+        assert np.array_equal(got[b], pol.predict(f[b], s[b], n[b])), b
+    pol.close()
+
+
 def test_batch_equals_single_queries(tmp_path, monkeypatch):
     B = 3
     pol = _policy(tmp_path, synth.DP_SMALL, 3, monkeypatch, max_batch=4)

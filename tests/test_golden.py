@@ -39,7 +39,8 @@ def test_small_fixture_arrays_are_consistent():
 
 
 @pytest.mark.parametrize("cfg,shape", [("small", synth.ACT_SMALL), ("base", synth.ACT_BASELINE),
-                                       ("dp_small", synth.DP_SMALL), ("dp_base", synth.DP_BASELINE)])
+                                       ("dp_small", synth.DP_SMALL), ("dp_base", synth.DP_BASELINE),
+                                       ("dp_edge", synth.DP_EDGE), ("dp_deep", synth.DP_DEEP)])
 def test_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
     if cfg.startswith("dp_"):
         d = synth.write_dp_checkpoint(str(tmp_path / cfg), shape, seed=0)

@@ -214,6 +214,21 @@ DP_BASELINE = DpShape()
 DP_SMALL = DpShape(n_cams=2, img_h=40, img_w=48, crop_h=32, crop_w=40, state_dim=3, action_dim=4, horizon=16,
                    n_action_steps=6, num_keypoints=8, down_dims=(64, 128, 256), step_embed_dim=32,
                    stem_out=16, widths=(16, 32, 48, 64))
+# edge cases of the same code paths: one encoder shared by both cameras, no
+# crop, a folded-BatchNorm backbone (gn_group_size 0), bias-only FiLM, kernel 3,
+# a two-level U-Net on horizon 8 with channel counts that are not multiples of
+# 32 per group, scaled_linear betas over 50 training steps (DDIM ladder of 6),
+# no sample clipping
+DP_EDGE = DpShape(n_cams=2, separate_encoders=False, img_h=32, img_w=40, crop_h=0, crop_w=0, state_dim=5,
+                  action_dim=3, horizon=8, n_action_steps=4, num_keypoints=8, kernel_size=3, n_groups=8,
+                  step_embed_dim=16, film_scale=False, down_dims=(32, 48), num_train_timesteps=50,
+                  num_inference_steps=6, beta_schedule="scaled_linear", clip_sample=False, stem_out=16,
+                  widths=(16, 32, 48, 64), gn_group_size=0)
+# one camera, one observation step, a four-level U-Net on horizon 32, linear betas
+DP_DEEP = DpShape(n_obs_steps=1, n_cams=1, img_h=36, img_w=36, crop_h=28, crop_w=30, state_dim=2, action_dim=2,
+                  horizon=32, n_action_steps=12, num_keypoints=16, kernel_size=5, n_groups=4, step_embed_dim=24,
+                  down_dims=(16, 32, 64, 96), num_train_timesteps=100, num_inference_steps=8,
+                  beta_schedule="linear", stem_out=16, widths=(16, 32, 48, 64), gn_group_size=8)
 
 
 def write_dp_checkpoint(out_dir: str, shape: DpShape = DP_BASELINE, seed: int = 0) -> str:
@@ -231,19 +246,22 @@ def write_dp_checkpoint(out_dir: str, shape: DpShape = DP_BASELINE, seed: int = 
     def gn(c):
         return [(1.0 + normal((c,), 0.05)).astype(np.float32), normal((c,), 0.05)]
 
+    def norm(c):   # backbone GroupNorm scale/shift, or a folded BatchNorm's bias (gn_group_size 0)
+        return gn(c) if s.gn_group_size else [normal((c,), 0.05)]
+
     n_enc = s.n_cams if s.separate_encoders else 1
     ashape = ActShape(stem_out=s.stem_out, widths=s.widths)
     for e in range(n_enc):
         parts = []
         k = 7
-        parts += [normal((s.stem_out, k, k, 3), np.sqrt(2.0 / (k * k * 3)))] + gn(s.stem_out)
+        parts += [normal((s.stem_out, k, k, 3), np.sqrt(2.0 / (k * k * 3)))] + norm(s.stem_out)
         meta = ["in_ch 3", f"stem_out {s.stem_out}", f"stem_k {k}", "stem_stride 2", f"stem_pad {k // 2}",
                 "pool_k 3", "pool_stride 2", "pool_pad 1"]
         for cin, cout, stride, has_down in _block_table(ashape):
-            parts += [normal((cout, 3, 3, cin), np.sqrt(2.0 / (9 * cin)))] + gn(cout)
-            parts += [normal((cout, 3, 3, cout), np.sqrt(1.0 / (9 * cout)))] + gn(cout)
+            parts += [normal((cout, 3, 3, cin), np.sqrt(2.0 / (9 * cin)))] + norm(cout)
+            parts += [normal((cout, 3, 3, cout), np.sqrt(1.0 / (9 * cout)))] + norm(cout)
             if has_down:
-                parts += [normal((cout, 1, 1, cin), np.sqrt(1.0 / cin))] + gn(cout)
+                parts += [normal((cout, 1, 1, cin), np.sqrt(1.0 / cin))] + norm(cout)
             meta.append(f"block {cin} {cout} {stride} {has_down}")
         meta.append(f"gn_group_size {s.gn_group_size}")
         with open(os.path.join(out_dir, f"rgb_encoder{e}_backbone.meta"), "w") as f:
