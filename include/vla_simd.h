@@ -104,6 +104,39 @@ VLA_API int32_t vla_diffusion_predict(void* h, const uint8_t* frames, const floa
                                       int32_t unnormalize, float* actions,
                                       const float* noise);
 
+/* ----------------------------------------------------------------- Octo -----
+ * replaces reference include/vla_simd.h:121-144 (src/models/octo/octo_capi.cpp:19-58).
+ * model_dir: a converter directory (t5.meta/.bin, stem_primary.meta/.bin,
+ * stem_wrist.meta/.bin, octo.meta/.bin, head.meta/.bin,
+ * stats_action_{mean,std,mask}.bin) as written by tools/convert_octo.py, or
+ * its vla.simd GGUF; tok_dir holds the tokenizer's vocab.txt
+ * (tools/convert_t5_tokenizer.py). OCTO_INT8 (1 q/k/v/o, 2 MLP w1, 4 MLP w2,
+ * 8 token projections + stem embeddings, 16 stem convs, 32 diffusion head)
+ * keeps the reference's meaning. */
+VLA_API void* vla_octo_load(const char* model_dir, const char* tok_dir);
+VLA_API void  vla_octo_free(void* h);
+
+VLA_API int32_t vla_octo_horizon(void* h);
+VLA_API int32_t vla_octo_action_dim(void* h);
+VLA_API int32_t vla_octo_max_window(void* h);
+
+/* primary [wnd,256,256,3] and wrist [wnd,128,128,3] (or NULL) uint8 HWC;
+ * timestep_mask [wnd] (1 = real, 0 = history padding); wnd in
+ * [1, vla_octo_max_window]. The DDPM noise is drawn from `seed` as the
+ * reference draws it. actions out [horizon*action_dim]. */
+VLA_API int32_t vla_octo_predict(void* h, const uint8_t* primary, const uint8_t* wrist,
+                                 int32_t wnd, const uint8_t* timestep_mask,
+                                 const char* instruction, uint64_t seed,
+                                 int32_t unnormalize, float* actions);
+
+/* As vla_octo_predict with the noise supplied: noise [horizon*action_dim] is
+ * the initial x, z [steps*horizon*action_dim] the per-step draws. Both or neither. */
+VLA_API int32_t vla_octo_predict_ex(void* h, const uint8_t* primary, const uint8_t* wrist,
+                                    int32_t wnd, const uint8_t* timestep_mask,
+                                    const char* instruction, const float* noise,
+                                    const float* z, uint64_t seed,
+                                    int32_t unnormalize, float* actions);
+
 #ifdef __cplusplus
 }
 #endif

@@ -255,6 +255,43 @@ VLA_API int32_t vla_diffusion_int8_layers(void* h);
 VLA_API int64_t vla_diffusion_global_cond(void* h, float* out, int64_t cap);
 VLA_API int64_t vla_diffusion_debug_map(void* h, float* out, int64_t cap);
 
+/* --------------------------------------------------------- batched Octo
+ * No counterpart in the reference, whose vla_octo_predict_ex serves one query
+ * (src/models/octo/octo_capi.cpp:40-58): a handle loaded with max_batch serves
+ * up to that many queries of one window length in one call, each with its own
+ * instruction, timestep mask and noise; every query's actions equal a
+ * single-query predict of it. primary [batch][wnd][256][256][3], wrist
+ * [batch][wnd][128][128][3] or NULL (for all queries), timestep_mask
+ * [batch][wnd], instructions[batch]; noise [batch][horizon*action_dim] and z
+ * [batch][steps][horizon*action_dim], or both NULL with seeds[batch];
+ * actions [batch][horizon][action_dim]. */
+VLA_API void* vla_octo_load_batch(const char* model_dir, const char* tok_dir, int32_t max_batch);
+VLA_API int32_t vla_octo_predict_batch(void* h, int32_t batch, const uint8_t* primary, const uint8_t* wrist,
+                                       int32_t wnd, const uint8_t* timestep_mask,
+                                       const char* const* instructions, const float* noise, const float* z,
+                                       const uint64_t* seeds, int32_t unnormalize, float* actions);
+VLA_API int32_t vla_octo_num_steps(void* h);
+VLA_API int32_t vla_octo_embed_dim(void* h);
+VLA_API int32_t vla_octo_int8_layers(void* h);
+VLA_API int32_t vla_octo_kernels_per_step(void* h);
+/* how many distinct instructions the T5 encoder has run for (the cache's misses) */
+VLA_API int32_t vla_octo_t5_runs(void* h);
+/* device-resident stepping for throughput runs: the input buffers (sized for
+ * max_batch x max_window), vla_octo_set_instruction for query slot b, then
+ * vla_octo_enqueue of one graph on `stream` (no copies, no sync). */
+VLA_API int32_t vla_octo_device_buffers(void* h, uint8_t** primary, uint8_t** wrist, uint8_t** timestep_mask,
+                                        float** noise, float** z, const float** actions);
+VLA_API int32_t vla_octo_set_instruction(void* h, int32_t b, const char* instruction);
+VLA_API int32_t vla_octo_enqueue(void* h, int32_t batch, int32_t wnd, int32_t wrist, void* stream,
+                                 int32_t unnormalize);
+/* Parity tap: the last batch's readout embeddings [batch][embed_dim] (after the
+ * final LayerNorm, the diffusion head's input). Returns the element count, or -1. */
+VLA_API int64_t vla_octo_readout(void* h, float* out, int64_t cap);
+/* The host tokenizer Octo's handles use (no device work): ids [max_len] of
+ * `text` under the vocab.txt contents `vocab_text`, pieces truncated to
+ * max_len - 1, then </s>, then <pad> (src/tokenizer/t5_tokenizer.cpp:131-155). */
+VLA_API int32_t vla_t5_tokenize(const char* vocab_text, const char* text, int32_t max_len, int32_t* ids);
+
 #ifdef __cplusplus
 }
 #endif

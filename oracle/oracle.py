@@ -327,6 +327,61 @@ class Reference:
             l.vla_diffusion_free(h)
 
 
+    def octo_predict(self, model_dir, tok_dir, primary, wrist, tmask, instruction, noise, z, seed=0,
+                     unnormalize=True):
+        """The reference's vla_octo_predict_ex (src/models/octo/octo_capi.cpp:40-58) on one
+        query: primary [wnd, 256, 256, 3], wrist [wnd, 128, 128, 3] or None, tmask [wnd];
+        noise [flat] and z [steps, flat], or both None (drawn from seed);
+        returns actions [horizon, action_dim]."""
+        l = self.l
+        l.vla_octo_load.restype = VP
+        l.vla_octo_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+        l.vla_octo_free.argtypes = [VP]
+        for name in ("horizon", "action_dim"):
+            getattr(l, f"vla_octo_{name}").argtypes = [VP]
+        l.vla_octo_predict_ex.argtypes = [VP, VP, VP, I32, VP, ctypes.c_char_p, VP, VP, ctypes.c_uint64, I32, VP]
+        h = l.vla_octo_load(model_dir.encode(), tok_dir.encode())
+        if not h:
+            raise RuntimeError("reference vla_octo_load failed")
+        try:
+            out = np.zeros((l.vla_octo_horizon(h), l.vla_octo_action_dim(h)), np.float32)
+            p = np.ascontiguousarray(primary, np.uint8)
+            w = None if wrist is None else np.ascontiguousarray(wrist, np.uint8)
+            tm = np.ascontiguousarray(tmask, np.uint8)
+            nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+            zz = None if z is None else np.ascontiguousarray(z, np.float32)
+            rc = l.vla_octo_predict_ex(h, _ptr(p), _ptr(w), p.shape[0], _ptr(tm), instruction.encode(), _ptr(nz),
+                                       _ptr(zz), seed, 1 if unnormalize else 0, _ptr(out))
+            if rc != 0:
+                raise RuntimeError(f"reference vla_octo_predict_ex rc={rc}")
+            return out
+        finally:
+            l.vla_octo_free(h)
+
+    def octo_readout(self, model_dir, tok_dir, primary, wrist, tmask, instruction, d):
+        """The readout embedding [d] the reference's diffusion head reads (ref_octo_shim.cpp)."""
+        l = self.l
+        l.ref_octo_readout.argtypes = [ctypes.c_char_p, ctypes.c_char_p, VP, VP, I32, VP, ctypes.c_char_p, VP]
+        l.ref_octo_readout.restype = I32
+        out = np.zeros(d, np.float32)
+        p = np.ascontiguousarray(primary, np.uint8)
+        w = None if wrist is None else np.ascontiguousarray(wrist, np.uint8)
+        rc = l.ref_octo_readout(model_dir.encode(), tok_dir.encode(), _ptr(p), _ptr(w), p.shape[0],
+                                _ptr(np.ascontiguousarray(tmask, np.uint8)), instruction.encode(), _ptr(out))
+        if rc != 0:
+            raise RuntimeError("ref_octo_readout failed")
+        return out
+
+    def t5_tokenize(self, tok_dir, text, max_len=16):
+        """The reference tokenizer's ids of `text` (ref_octo_shim.cpp)."""
+        l = self.l
+        l.ref_t5_tokenize.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I32, VP]
+        l.ref_t5_tokenize.restype = I32
+        ids = np.zeros(max_len, np.int32)
+        if l.ref_t5_tokenize(tok_dir.encode(), text.encode(), max_len, _ptr(ids)) != 0:
+            raise RuntimeError("ref_t5_tokenize failed")
+        return ids
+
     def dp_global_cond(self, model_dir, frames, state):
         """The global conditioning vector the reference builds for one DP query (ref_dp_shim.cpp)."""
         l = self.l

@@ -55,6 +55,8 @@ GEMM_SHAPES = [(1, 16, 3), (7, 48, 64), (13, 64, 17), (257, 96, 48), (50, 768, 1
 def dir_digest(d):
     h = hashlib.sha256()
     for name in sorted(os.listdir(d)):
+        if not os.path.isfile(os.path.join(d, name)):
+            continue
         h.update(name.encode())
         with open(os.path.join(d, name), "rb") as f:
             h.update(f.read())
@@ -124,19 +126,81 @@ def make_dp(digests):
             subprocess.run([sys.executable, "-c", code], check=True, env=env)
 
 
+# (config, shape, OCTO_INT8, variant): "" the seeded query of octo_inputs(seed=1),
+# "nowrist" without the wrist camera, "pad" a 3-step window whose oldest step
+# is history padding, "w1" a 1-step window, "seed" the reference's own noise
+# draw from seed 7, "readout" the readout embedding instead of the actions
+OCTO_CASES = [("small", "OCTO_SMALL", 63, ""), ("small", "OCTO_SMALL", 0, ""), ("small", "OCTO_SMALL", 63, "readout"),
+              ("small", "OCTO_SMALL", 63, "nowrist"), ("small", "OCTO_SMALL", 63, "pad"),
+              ("small", "OCTO_SMALL", 63, "w1"), ("small", "OCTO_SMALL", 63, "seed"),
+              ("small", "OCTO_SMALL", 31, ""), ("base", "OCTO_BASELINE", 63, "")]
+# tokenizer cases: ids of each string under synth.octo_vocab()
+T5_TEXTS = ["", " ", "pick up the red block", "PICK up \u00b2\u00bd \u2026 \ufb01", "a\tb\nc  d",
+            "<extra_id_0> pick<extra_id_0>up", "x" * 40, "h\u00e9llo w\u00f6rld \u2603 \u65e5\u672c",
+            "\x01\x7fab\u2581cd", "\uff21\uff22\uff23 fullwidth", "<unk> <pad> </s>"]
+
+
+def octo_fixture_name(cfg, mask, variant):
+    return f"octo_{cfg}_m{mask}" + (f"_{variant}" if variant else "") + ".npy"
+
+
+def octo_query(shape, variant):
+    """The inputs of one Octo fixture case: (primary, wrist, tmask, instruction, noise, z, seed)."""
+    if variant == "pad":
+        p, w, tm, ins, n, z = synth.octo_inputs(shape, seed=2, wnd=3)
+        tm = np.array([0, 1, 1], np.uint8)
+    elif variant == "w1":
+        p, w, tm, ins, n, z = synth.octo_inputs(shape, seed=3, wnd=1)
+    else:
+        p, w, tm, ins, n, z = synth.octo_inputs(shape, seed=1)
+    if variant == "nowrist":
+        w = None
+    if variant == "seed":
+        n = z = None
+    return p, w, tm, ins, n, z, 7
+
+
+def make_octo(digests):
+    for cfg, shape_name, mask, variant in OCTO_CASES:
+        with tempfile.TemporaryDirectory() as d:
+            shape = getattr(synth, shape_name)
+            synth.write_octo_checkpoint(d, shape, seed=0)
+            digests["octo_" + cfg] = dir_digest(d) + dir_digest(os.path.join(d, "tok"))[:16]
+            call = ("r.octo_readout(d, d + '/tok', p, w, tm, ins, sh.d)" if variant == "readout"
+                    else "r.octo_predict(d, d + '/tok', p, w, tm, ins, n, z, seed)")
+            code = ("import sys,numpy as np; sys.path.insert(0, %r); sys.path.insert(0, %r); from oracle import oracle; "
+                    "from vla_simd_b200 import synth; import make_golden as mg; r = oracle.reference(); "
+                    "sh = synth.%s; d = %r; p, w, tm, ins, n, z, seed = mg.octo_query(sh, %r); "
+                    "np.save(%r, %s)") % (ROOT, HERE, shape_name, d, variant,
+                                          os.path.join(HERE, octo_fixture_name(cfg, mask, variant)), call)
+            # the reference reads OCTO_INT8 once per process
+            env = dict(os.environ, OCTO_INT8=str(mask), OMP_NUM_THREADS="1")
+            subprocess.run([sys.executable, "-c", code], check=True, env=env)
+    ref = oracle.reference()
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_octo_checkpoint(d, synth.OCTO_SMALL, seed=0)
+        ids = {t: ref.t5_tokenize(os.path.join(d, "tok"), t, 16).tolist() for t in T5_TEXTS}
+        ids.update({synth.octo_instruction(i): ref.t5_tokenize(os.path.join(d, "tok"), synth.octo_instruction(i),
+                                                               16).tolist() for i in range(20)})
+    with open(os.path.join(HERE, "t5_ids.json"), "w") as f:
+        json.dump(ids, f, indent=0, sort_keys=True)
+
+
 def main():
     ref = oracle.reference()
     if ref is None:
         sys.exit("oracle/_ref/libvla_ref.so missing: make -C oracle ref")
     digests = {}
-    if "--dp" in sys.argv:   # only the Diffusion Policy fixtures
-        path = os.path.join(HERE, "checkpoints.json")
-        digests = json.load(open(path))
-        make_dp(digests)
-        with open(path, "w") as f:
-            json.dump(digests, f, indent=1, sort_keys=True)
-        return
+    for flag, maker in (("--dp", make_dp), ("--octo", make_octo)):   # one family's fixtures only
+        if flag in sys.argv:
+            path = os.path.join(HERE, "checkpoints.json")
+            digests = json.load(open(path))
+            maker(digests)
+            with open(path, "w") as f:
+                json.dump(digests, f, indent=1, sort_keys=True)
+            return
     make_dp(digests)
+    make_octo(digests)
     for cfg, shape, mask in ACT_CASES:
         # the reference reads ACT_INT8 when it loads, so each mask runs in its own process
         with tempfile.TemporaryDirectory() as d:

@@ -49,6 +49,23 @@ def test_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
     assert dir_digest(d) == json.load(open(os.path.join(HERE, "checkpoints.json")))[cfg]
 
 
+@pytest.mark.parametrize("cfg,shape", [("octo_small", synth.OCTO_SMALL), ("octo_base", synth.OCTO_BASELINE)])
+def test_octo_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
+    d = synth.write_octo_checkpoint(str(tmp_path / cfg), shape, seed=0)
+    want = json.load(open(os.path.join(HERE, "checkpoints.json")))[cfg]
+    assert dir_digest(d) + dir_digest(os.path.join(d, "tok"))[:16] == want
+
+
+def test_reference_octo_fixture_is_current(tmp_path, reference, monkeypatch):
+    from make_golden import octo_query
+    monkeypatch.setenv("OCTO_INT8", "0")   # read once per process by the reference; 0 is its default
+    d = synth.write_octo_checkpoint(str(tmp_path / "octo"), synth.OCTO_SMALL, seed=0)
+    p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_SMALL, "")
+    got = reference.octo_predict(d, d + "/tok", p, w, tm, ins, n, z)
+    if os.environ.get("OCTO_INT8", "0") == "0":
+        assert np.array_equal(got, np.load(os.path.join(HERE, "octo_small_m0.npy")))
+
+
 def test_reference_policy_fixture_is_current(tmp_path, reference, monkeypatch):
     monkeypatch.setenv("ACT_INT8", "63")
     d = synth.write_act_checkpoint(str(tmp_path / "small"), synth.ACT_SMALL, seed=0)

@@ -9,6 +9,9 @@ it with ctypes and mirrors the reference's Python-side interface:
 * :class:`DiffusionPolicy` - the ``vla_diffusion_*`` ABI: an observation
   history (frames + states) and the sampler's noise in, an action chunk out;
   optionally a batch of independent queries per call.
+* :class:`OctoPolicy` - the ``vla_octo_*`` ABI: a window of primary / wrist
+  frames, a language instruction and the DDPM noise in, an action chunk out;
+  optionally a batch of independent queries per call.
 * ``ops`` - device-pointer wrappers over the op-level ABI taking torch CUDA
   tensors (torch is only the allocator / stream provider here).
 
@@ -113,6 +116,26 @@ SIGNATURES = {
     "vla_diffusion_int8_layers": (I32, [VP]),
     "vla_diffusion_global_cond": (I64, [VP, F32P, I64]),
     "vla_diffusion_debug_map": (I64, [VP, F32P, I64]),
+    "vla_octo_load": (VP, [ctypes.c_char_p, ctypes.c_char_p]),
+    "vla_octo_load_batch": (VP, [ctypes.c_char_p, ctypes.c_char_p, I32]),
+    "vla_octo_free": (None, [VP]),
+    "vla_octo_horizon": (I32, [VP]),
+    "vla_octo_action_dim": (I32, [VP]),
+    "vla_octo_max_window": (I32, [VP]),
+    "vla_octo_num_steps": (I32, [VP]),
+    "vla_octo_embed_dim": (I32, [VP]),
+    "vla_octo_int8_layers": (I32, [VP]),
+    "vla_octo_kernels_per_step": (I32, [VP]),
+    "vla_octo_t5_runs": (I32, [VP]),
+    "vla_octo_predict": (I32, [VP, U8P, U8P, I32, U8P, ctypes.c_char_p, ctypes.c_uint64, I32, F32P]),
+    "vla_octo_predict_ex": (I32, [VP, U8P, U8P, I32, U8P, ctypes.c_char_p, F32P, F32P, ctypes.c_uint64, I32, F32P]),
+    "vla_octo_predict_batch": (I32, [VP, I32, U8P, U8P, I32, U8P, ctypes.POINTER(ctypes.c_char_p), F32P, F32P,
+                                     ctypes.POINTER(ctypes.c_uint64), I32, F32P]),
+    "vla_octo_readout": (I64, [VP, F32P, I64]),
+    "vla_t5_tokenize": (I32, [ctypes.c_char_p, ctypes.c_char_p, I32, ctypes.POINTER(ctypes.c_int32)]),
+    "vla_octo_device_buffers": (I32, [VP, VP, VP, VP, VP, VP, VP]),
+    "vla_octo_set_instruction": (I32, [VP, I32, ctypes.c_char_p]),
+    "vla_octo_enqueue": (I32, [VP, I32, I32, I32, VP, I32]),
     "vla_act_device_buffers": (I32, [VP, VP, VP, VP]),
     "vla_act_enqueue": (I32, [VP, VP, I32]),
     "vla_act_kernels_per_step": (I32, [VP]),
@@ -192,6 +215,137 @@ class ActPolicy:
     def close(self) -> None:
         if self.h:
             self.lib.vla_act_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def t5_tokenize(vocab_text: str, text: str, max_len: int = 16) -> np.ndarray:
+    """Token ids of `text` under a T5 vocab.txt (the tokenizer Octo's handles
+    use; host code, no GPU needed)."""
+    ids = np.zeros(max_len, np.int32)
+    rc = lib().vla_t5_tokenize(vocab_text.encode(), text.encode(), int(max_len),
+                               ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+    check(rc, "vla_t5_tokenize")
+    return ids
+
+
+class OctoPolicy:
+    """ctypes binding of the Octo C ABI (include/vla_simd.h, the reference's
+    vla_octo_* at src/models/octo/octo_capi.cpp:19-58).
+
+    primary [wnd, 256, 256, 3] and wrist [wnd, 128, 128, 3] (or None) uint8,
+    timestep_mask [wnd], an instruction string, and either noise [horizon *
+    action_dim] with z [steps, horizon * action_dim] or a seed -> actions
+    [horizon, action_dim]. With max_batch > 1, predict_batch takes the arrays
+    with a leading batch axis and a list of instructions.
+    """
+
+    def __init__(self, model_dir: str, tok_dir: str | None = None, max_batch: int = 1):
+        self.lib = lib()
+        tok_dir = tok_dir or os.path.join(model_dir, "tok")
+        self.h = (self.lib.vla_octo_load(model_dir.encode(), tok_dir.encode()) if max_batch == 1
+                  else self.lib.vla_octo_load_batch(model_dir.encode(), tok_dir.encode(), int(max_batch)))
+        if not self.h:
+            raise RuntimeError(f"vla_octo_load failed for {model_dir}")
+        self.max_batch = int(max_batch)
+        for name in ("horizon", "action_dim", "max_window", "num_steps", "embed_dim"):
+            setattr(self, name, int(getattr(self.lib, f"vla_octo_{name}")(self.h)))
+        self.flat = self.horizon * self.action_dim
+
+    def _arrays(self, primary, wrist, tmask, noise, z, lead):
+        primary = np.ascontiguousarray(primary, np.uint8)
+        if primary.ndim != len(lead) + 4 or primary.shape[len(lead) + 1:] != (256, 256, 3):
+            raise ValueError(f"primary {primary.shape}")
+        wnd = primary.shape[len(lead)]
+        if wrist is not None:
+            wrist = np.ascontiguousarray(wrist, np.uint8)
+            if wrist.shape != lead + (wnd, 128, 128, 3):
+                raise ValueError(f"wrist {wrist.shape}")
+        tmask = np.ascontiguousarray(tmask, np.uint8)
+        if tmask.shape != lead + (wnd,):
+            raise ValueError(f"timestep mask {tmask.shape}")
+        if (noise is None) != (z is None):
+            raise ValueError("noise and z go together")
+        n = int(np.prod(lead, dtype=np.int64)) if lead else 1
+        if noise is not None:
+            noise = np.ascontiguousarray(noise, np.float32)
+            z = np.ascontiguousarray(z, np.float32)
+            if noise.size != n * self.flat or z.size != n * self.num_steps * self.flat:
+                raise ValueError("noise / z size")
+        return primary, wrist, tmask, noise, z, wnd
+
+    @staticmethod
+    def _p(a, t):
+        return None if a is None else a.ctypes.data_as(t)
+
+    def predict(self, primary, wrist, tmask, instruction: str, noise=None, z=None, seed: int = 0,
+                unnormalize: bool = True) -> np.ndarray:
+        primary, wrist, tmask, noise, z, wnd = self._arrays(primary, wrist, tmask, noise, z, ())
+        out = np.empty((self.horizon, self.action_dim), np.float32)
+        rc = self.lib.vla_octo_predict_ex(self.h, self._p(primary, U8P), self._p(wrist, U8P), wnd,
+                                          self._p(tmask, U8P), instruction.encode(), self._p(noise, F32P),
+                                          self._p(z, F32P), int(seed), 1 if unnormalize else 0,
+                                          out.ctypes.data_as(F32P))
+        check(rc, "vla_octo_predict_ex")
+        return out
+
+    def predict_batch(self, primary, wrist, tmask, instructions, noise=None, z=None, seeds=None,
+                      unnormalize: bool = True) -> np.ndarray:
+        b = int(np.asarray(primary).shape[0])
+        primary, wrist, tmask, noise, z, wnd = self._arrays(primary, wrist, tmask, noise, z, (b,))
+        if len(instructions) != b:
+            raise ValueError("one instruction per query")
+        ins = (ctypes.c_char_p * b)(*[s.encode() for s in instructions])
+        sd = None
+        if noise is None:
+            sd = (ctypes.c_uint64 * b)(*[int(v) for v in (seeds if seeds is not None else range(b))])
+        out = np.empty((b, self.horizon, self.action_dim), np.float32)
+        rc = self.lib.vla_octo_predict_batch(self.h, b, self._p(primary, U8P), self._p(wrist, U8P), wnd,
+                                             self._p(tmask, U8P), ins, self._p(noise, F32P), self._p(z, F32P), sd,
+                                             1 if unnormalize else 0, out.ctypes.data_as(F32P))
+        check(rc, "vla_octo_predict_batch")
+        return out
+
+    def readout(self) -> np.ndarray:
+        """The last query batch's readout embeddings [batch, embed_dim] (a parity tap)."""
+        out = np.empty(self.max_batch * self.embed_dim, np.float32)
+        n = int(self.lib.vla_octo_readout(self.h, out.ctypes.data_as(F32P), out.size))
+        if n < 0:
+            raise RuntimeError("vla_octo_readout failed")
+        return out[:n].reshape(-1, self.embed_dim).copy()
+
+    def device_buffers(self):
+        ptrs = [ctypes.c_void_p() for _ in range(6)]
+        check(self.lib.vla_octo_device_buffers(self.h, *[ctypes.byref(p) for p in ptrs]), "vla_octo_device_buffers")
+        return tuple(p.value for p in ptrs)
+
+    def set_instruction(self, b: int, instruction: str) -> None:
+        check(self.lib.vla_octo_set_instruction(self.h, int(b), instruction.encode()), "vla_octo_set_instruction")
+
+    def enqueue(self, batch: int, wnd: int, wrist: bool, stream_handle: int, unnormalize: bool = True) -> None:
+        check(self.lib.vla_octo_enqueue(self.h, int(batch), int(wnd), 1 if wrist else 0,
+                                        ctypes.c_void_p(stream_handle), 1 if unnormalize else 0), "vla_octo_enqueue")
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(self.lib.vla_octo_kernels_per_step(self.h))
+
+    @property
+    def int8_layers(self) -> int:
+        return int(self.lib.vla_octo_int8_layers(self.h))
+
+    @property
+    def t5_runs(self) -> int:
+        return int(self.lib.vla_octo_t5_runs(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.vla_octo_free(self.h)
             self.h = None
 
     def __del__(self):

@@ -6,6 +6,8 @@
 
 #include "act_policy.h"
 #include "dp_policy.h"
+#include "octo_policy.h"
+#include "t5_tokenizer.h"
 #include "gemm_i8.h"
 #include "host_quant.h"
 #include "lm_ops.h"
@@ -24,6 +26,7 @@
 
 using vsb::ActPolicy;
 using vsb::DpPolicy;
+using vsb::OctoPolicy;
 
 namespace {
 
@@ -234,6 +237,113 @@ int32_t vla_diffusion_enqueue(void* h, int32_t batch, void* stream, int32_t unno
     auto* m = static_cast<DpPolicy*>(h);
     if (batch < 1 || batch > m->max_batch()) return VLA_ERR_SHAPE;
     return status_of(m->enqueue(batch, as_stream(stream), unnormalize != 0));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+// ---------------------------------------------------------------- Octo
+
+void* vla_octo_load_batch(const char* model_dir, const char* tok_dir, int32_t max_batch) try {
+    if (!model_dir || !tok_dir || max_batch < 1) return nullptr;
+    auto m = std::make_unique<OctoPolicy>();
+    if (!m->load(model_dir, tok_dir, max_batch)) {
+        std::fprintf(stderr, "vla_octo_load: %s\n", m->error().c_str());
+        return nullptr;
+    }
+    return m.release();
+} catch (...) {
+    return nullptr;
+}
+
+void* vla_octo_load(const char* model_dir, const char* tok_dir) { return vla_octo_load_batch(model_dir, tok_dir, 1); }
+
+void vla_octo_free(void* h) { delete static_cast<OctoPolicy*>(h); }
+
+int32_t vla_octo_horizon(void* h) { return h ? static_cast<OctoPolicy*>(h)->config().horizon : 0; }
+int32_t vla_octo_action_dim(void* h) { return h ? static_cast<OctoPolicy*>(h)->config().action_dim : 0; }
+int32_t vla_octo_max_window(void* h) { return h ? static_cast<OctoPolicy*>(h)->config().max_horizon : 0; }
+int32_t vla_octo_num_steps(void* h) { return h ? static_cast<OctoPolicy*>(h)->config().steps : 0; }
+int32_t vla_octo_embed_dim(void* h) { return h ? static_cast<OctoPolicy*>(h)->config().d : 0; }
+int32_t vla_octo_int8_layers(void* h) { return h ? static_cast<OctoPolicy*>(h)->int8_layers() : 0; }
+int32_t vla_octo_kernels_per_step(void* h) { return h ? static_cast<OctoPolicy*>(h)->kernels_per_step() : 0; }
+int32_t vla_octo_t5_runs(void* h) { return h ? static_cast<OctoPolicy*>(h)->t5_runs() : 0; }
+
+int32_t vla_octo_predict_batch(void* h, int32_t batch, const uint8_t* primary, const uint8_t* wrist, int32_t wnd,
+                               const uint8_t* timestep_mask, const char* const* instructions, const float* noise,
+                               const float* z, const uint64_t* seeds, int32_t unnormalize, float* actions) try {
+    if (!h || !primary || !timestep_mask || !instructions || !actions) return VLA_ERR_ARG;
+    auto* m = static_cast<OctoPolicy*>(h);
+    if (batch < 1 || batch > m->max_batch()) return VLA_ERR_SHAPE;
+    // the position tables hold max_window steps (octo_capi.cpp:46-48)
+    if (wnd < 1 || wnd > m->config().max_horizon) return VLA_ERR_SHAPE;
+    if ((noise == nullptr) != (z == nullptr) || (!noise && !seeds)) return VLA_ERR_ARG;
+    for (int32_t b = 0; b < batch; ++b)
+        if (!instructions[b]) return VLA_ERR_ARG;
+    return status_of(m->predict(batch, primary, wrist, wnd, timestep_mask, instructions, noise, z, seeds,
+                                unnormalize != 0, actions));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_octo_predict_ex(void* h, const uint8_t* primary, const uint8_t* wrist, int32_t wnd,
+                            const uint8_t* timestep_mask, const char* instruction, const float* noise, const float* z,
+                            uint64_t seed, int32_t unnormalize, float* actions) {
+    if (!instruction) return VLA_ERR_ARG;
+    return vla_octo_predict_batch(h, 1, primary, wrist, wnd, timestep_mask, &instruction, noise, z, &seed,
+                                  unnormalize, actions);
+}
+
+int32_t vla_octo_predict(void* h, const uint8_t* primary, const uint8_t* wrist, int32_t wnd,
+                         const uint8_t* timestep_mask, const char* instruction, uint64_t seed, int32_t unnormalize,
+                         float* actions) {
+    return vla_octo_predict_ex(h, primary, wrist, wnd, timestep_mask, instruction, nullptr, nullptr, seed,
+                               unnormalize, actions);
+}
+
+int32_t vla_t5_tokenize(const char* vocab_text, const char* text, int32_t max_len, int32_t* ids) try {
+    if (!vocab_text || !text || !ids || max_len < 1) return VLA_ERR_ARG;
+    vsb::T5Tokenizer tok;
+    if (!tok.load_text(vocab_text)) return VLA_ERR_ARG;
+    const std::vector<int> v = tok.encode(text, max_len);
+    for (int32_t i = 0; i < max_len; ++i) ids[i] = v[static_cast<size_t>(i)];
+    return VLA_OK;
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int64_t vla_octo_readout(void* h, float* out, int64_t cap) try {
+    return h ? static_cast<OctoPolicy*>(h)->readout(out, cap) : -1;
+} catch (...) {
+    return -1;
+}
+
+int32_t vla_octo_device_buffers(void* h, uint8_t** primary, uint8_t** wrist, uint8_t** timestep_mask, float** noise,
+                                float** z, const float** actions) {
+    if (!h) return VLA_ERR_ARG;
+    auto* m = static_cast<OctoPolicy*>(h);
+    if (primary) *primary = m->device_primary();
+    if (wrist) *wrist = m->device_wrist();
+    if (timestep_mask) *timestep_mask = m->device_tmask();
+    if (noise) *noise = m->device_noise();
+    if (z) *z = m->device_z();
+    if (actions) *actions = m->device_actions();
+    return VLA_OK;
+}
+
+int32_t vla_octo_set_instruction(void* h, int32_t b, const char* instruction) try {
+    if (!h || !instruction) return VLA_ERR_ARG;
+    auto* m = static_cast<OctoPolicy*>(h);
+    if (b < 0 || b >= m->max_batch()) return VLA_ERR_SHAPE;
+    return status_of(m->set_instruction(b, instruction));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_octo_enqueue(void* h, int32_t batch, int32_t wnd, int32_t wrist, void* stream, int32_t unnormalize) try {
+    if (!h) return VLA_ERR_ARG;
+    auto* m = static_cast<OctoPolicy*>(h);
+    if (batch < 1 || batch > m->max_batch() || wnd < 1 || wnd > m->config().max_horizon) return VLA_ERR_SHAPE;
+    return status_of(m->enqueue(batch, wnd, wrist != 0, as_stream(stream), unnormalize != 0));
 } catch (...) {
     return VLA_ERR_EXCEPTION;
 }

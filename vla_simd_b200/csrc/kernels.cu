@@ -7,3 +7,4 @@
 #include "f32.cu"
 #include "lm_ops.cu"
 #include "dp.cu"
+#include "octo.cu"

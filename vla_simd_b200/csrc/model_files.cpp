@@ -268,14 +268,16 @@ bool ModelFiles::parse() {
     return true;
 }
 
-bool ModelFiles::disk(const std::string& rel, std::string& out) const {
-    std::ifstream f(dir_ + "/" + rel, std::ios::binary);
+bool ModelFiles::read_path(const std::string& path, std::string& out) {
+    std::ifstream f(path, std::ios::binary);
     if (!f) return false;
     std::ostringstream ss;
     ss << f.rdbuf();
     out = ss.str();
     return true;
 }
+
+bool ModelFiles::disk(const std::string& rel, std::string& out) const { return read_path(dir_ + "/" + rel, out); }
 
 bool ModelFiles::read(const std::string& rel, std::string& out) const {
     if (map_) {

@@ -36,6 +36,8 @@ class ModelFiles {
     bool read(const std::string& rel, std::string& out) const;
     // A .bin of little-endian fp32 values; false when absent or not a whole number of floats.
     bool read_floats(const std::string& rel, std::vector<float>& out) const;
+    // A whole file at an absolute or working-directory path, outside any model.
+    static bool read_path(const std::string& path, std::string& out);
 
   private:
     bool parse();

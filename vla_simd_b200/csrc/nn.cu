@@ -284,6 +284,17 @@ cudaError_t layernorm(const float* x, float* out, const float* w, const float* b
 constexpr int kAttD = 64;
 constexpr int kAttKT = 64;   // keys per shared K^T / V tile
 
+// Independent sequences of one launch (grid z): element strides between them.
+#define VSB_ATT_BATCH_OFFSET(bs)                 \
+    do {                                         \
+        const long long z_ = blockIdx.z;         \
+        Q += z_ * (bs).q;                        \
+        K += z_ * (bs).k;                        \
+        V += z_ * (bs).v;                        \
+        O += z_ * (bs).o;                        \
+        if (mask) mask += z_ * (bs).mask;        \
+    } while (0)
+
 // The reference's Cephes-style exp (src/hal/avx2/simd.h:72-95), lane for lane.
 __device__ __forceinline__ float ref_exp(float x) {
     const bool keep = !(x <= -87.0f);
@@ -323,7 +334,9 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(NT)
 attention_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                  const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
-                 int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
+                 int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask,
+                 AttBatch bs) {
+    VSB_ATT_BATCH_OFFSET(bs);
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     constexpr int QPT = QT / (NT / 32);    // queries per thread, score phase
@@ -524,7 +537,9 @@ template <int QPT>
 __global__ void __launch_bounds__(256, 1)
 attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                        const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
-                       int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask) {
+                       int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask,
+                       AttBatch bs) {
+    VSB_ATT_BATCH_OFFSET(bs);
     constexpr int QP = 8 * QPT;
     constexpr int kTile = kAttTK * kAttRS;
     extern __shared__ __align__(16) float att_smem[];
@@ -797,7 +812,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
 template <int QPT>
 cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                                    long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
-                                   float scale, const float* mask, cudaStream_t st) {
+                                   float scale, const float* mask, const AttBatch& bs, cudaStream_t st) {
     const size_t smem = att_tiled_smem(8 * QPT, seq_k);
     static int configured = 0;
     if ((int)smem > configured) {
@@ -806,9 +821,9 @@ cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K
         if (e != cudaSuccess) return e;
         configured = (int)smem;
     }
-    dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q);
+    dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q, bs.n);
     const cudaError_t e = launch_k(attention_tiled_kernel<QPT>, grid, 256, smem, st, Q, ldq, K, ldk, V, ldv, O, ldo,
-                                   seq_q, seq_k, n_q, n_kv, scale, mask);
+                                   seq_q, seq_k, n_q, n_kv, scale, mask, bs);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -816,7 +831,7 @@ cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K
 template <int QT, int NT>
 cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                              long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
-                             float scale, const float* mask, size_t smem, cudaStream_t st) {
+                             float scale, const float* mask, const AttBatch& bs, size_t smem, cudaStream_t st) {
     static int configured = 0;
     if ((int)smem > configured) {
         const cudaError_t e = cudaFuncSetAttribute(attention_kernel<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -824,11 +839,11 @@ cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long
         if (e != cudaSuccess) return e;
         configured = (int)smem;
     }
-    dim3 grid((seq_q + QT - 1) / QT, n_q);
+    dim3 grid((seq_q + QT - 1) / QT, n_q, bs.n);
     {
         const cudaError_t le_ = launch_k(attention_kernel<QT, NT>, grid, NT, smem, st,
                                          Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv,
-                                                          scale, mask);
+                                                          scale, mask, bs);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
@@ -837,8 +852,17 @@ cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long
 cudaError_t attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
                       float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, int head_dim, float scale,
                       const float* mask, cudaStream_t st) {
-    if (head_dim != kAttD || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv)
+    return attention_batched(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, head_dim, scale, mask,
+                             AttBatch{}, st);
+}
+
+cudaError_t attention_batched(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                              long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st) {
+    if (head_dim != kAttD || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv || bs.n < 1 ||
+        bs.n > 65535)
         return cudaErrorInvalidValue;
+    if (((bs.q | bs.k | bs.v | bs.o) & 3) != 0) return cudaErrorInvalidValue;
     // 16-byte vector loads of Q/K/V/O rows
     if (((ldq | ldk | ldv | ldo) & 3) ||
         ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V) |
@@ -860,10 +884,10 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
             if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
         }
         if (best_qpt == 5)
-            return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
+            return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
         if (best_qpt == 2)
-            return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
-        return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, st);
+            return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
+        return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
     }
     // Longer key ranges (> ~1100 keys): score rows of fewer queries per CTA.
     // 16 queries x 128 threads per CTA: measured fastest among 8..32 queries x
@@ -873,11 +897,11 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
     const long long ctas16 = (long long)((seq_q + 15) / 16) * n_q;
     const long long ctas8 = (long long)((seq_q + 7) / 8) * n_q;
     if (ctas16 >= 148 && need(16) <= 200 * 1024)
-        return launch_attention<16, 128>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(16), st);
+        return launch_attention<16, 128>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, need(16), st);
     if (ctas8 >= 148 && need(8) <= 220 * 1024)
-        return launch_attention<8, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(8), st);
+        return launch_attention<8, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, need(8), st);
     if (need(4) <= 220 * 1024)
-        return launch_attention<4, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, need(4), st);
+        return launch_attention<4, 64>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, need(4), st);
     return cudaErrorInvalidValue;   // > ~13000 keys: not a shape any policy here has
 }
 

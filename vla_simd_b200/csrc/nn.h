@@ -18,6 +18,16 @@ cudaError_t attention(const float* Q, long long ldq, const float* K, long long l
                       float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, int head_dim, float scale,
                       const float* mask, cudaStream_t st);
 
+// n independent sequences in one launch: sequence z reads Q + z*q, K + z*k,
+// V + z*v, mask + z*mask and writes O + z*o (element strides, multiples of 4).
+struct AttBatch {
+    int n = 1;
+    long long q = 0, k = 0, v = 0, o = 0, mask = 0;
+};
+cudaError_t attention_batched(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                              long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st);
+
 cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C, int k, int stride, int pad,
                          int Ho, int Wo, unsigned int* amax, cudaStream_t st);
 

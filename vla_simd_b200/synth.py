@@ -352,6 +352,221 @@ def dp_inputs(shape: DpShape = DP_BASELINE, seed: int = 1, batch: int = 0):
 
 
 # ---------------------------------------------------------------------------
+# Octo (tools/convert_octo.py's file set; random init)
+
+@dataclasses.dataclass(frozen=True)
+class OctoShape:
+    d: int = 768
+    n_layers: int = 12
+    heads: int = 12
+    mlp: int = 3072
+    max_horizon: int = 10
+    n_task: int = 16
+    stem_features: tuple = (32, 96, 192, 384)
+    stem_dim: int = 512
+    gn_groups: int = 32
+    t5_dim: int = 768
+    t5_layers: int = 12
+    t5_heads: int = 12
+    t5_ff: int = 3072
+    action_dim: int = 7
+    horizon: int = 4
+    time_dim: int = 32
+    num_blocks: int = 3
+    hidden: int = 256
+    steps: int = 20
+    max_action: float = 5.0
+    gelu_erf: bool = False
+    window: int = 2   # the query window the inputs are drawn for
+
+    def side(self, hw: int) -> int:
+        for _ in self.stem_features:
+            hw = (hw + 2 - 3) // 2 + 1
+        return hw
+
+    @property
+    def tok_primary(self) -> int:
+        return self.side(256) ** 2
+
+    @property
+    def tok_wrist(self) -> int:
+        return self.side(128) ** 2
+
+    @property
+    def flat(self) -> int:
+        return self.action_dim * self.horizon
+
+
+# BASELINE configs: Octo-base-shaped (12 layers, d 768, 12 heads, MLP 3072,
+# 256 + 64 patch tokens per frame on a 2-frame window, T5-base text tower over
+# 16 tokens, 20-step diffusion head, 4 x 7 chunk).
+OCTO_BASELINE = OctoShape()
+# reduced Octo for fast tests: five stem layers (8 x 8 + 4 x 4 tokens), narrow widths
+OCTO_SMALL = OctoShape(d=128, n_layers=3, heads=2, mlp=256, max_horizon=3, stem_features=(16, 16, 32, 32, 32),
+                       stem_dim=64, gn_groups=4, t5_dim=64, t5_layers=2, t5_heads=2, t5_ff=128, num_blocks=2,
+                       hidden=64)
+
+# A synthetic unigram vocabulary: the control pieces, every letter and digit
+# alone and after the word marker, and a few hundred made-up words.
+_SYLLABLES = ["pi", "ck", "up", "the", "red", "blo", "put", "in", "bo", "wl", "dra", "wer", "op", "en", "clo",
+              "se", "gr", "ab", "mu", "g", "sp", "oon", "tow", "el", "left", "righ", "t", "ca", "bi", "net"]
+
+
+def octo_vocab(seed: int = 7):
+    """[(piece, score)] of a synthetic vocab.txt; ids are list positions."""
+    rng = np.random.default_rng(seed)
+    mark = "▁"
+    pieces = [("<pad>", 0.0), ("</s>", 0.0), ("<unk>", 0.0)]
+    seen = {p for p, _ in pieces}
+
+    def add(p, sc):
+        if p not in seen:
+            seen.add(p)
+            pieces.append((p, sc))
+
+    add(mark, -3.0)
+    for ch in "abcdefghijklmnopqrstuvwxyz0123456789.,!?'-":
+        add(ch, -8.0 - float(rng.uniform(0, 2)))
+        add(mark + ch, -9.0 - float(rng.uniform(0, 2)))
+    for _ in range(400):
+        w = "".join(rng.choice(_SYLLABLES, size=int(rng.integers(1, 4))))
+        add((mark + w) if rng.uniform() < 0.7 else w, -float(rng.uniform(4.0, 12.0)))
+    add("<extra_id_0>", 0.0)
+    add("unused_placeholder", 0.0)   # score 0 and not <...>: keeps its id, never matched
+    return pieces
+
+
+def octo_instruction(seed: int, n_words: int = 8) -> str:
+    rng = np.random.default_rng(seed)
+    words = ["".join(rng.choice(_SYLLABLES, size=int(rng.integers(1, 4)))) for _ in range(n_words)]
+    return " ".join(words)
+
+
+def write_octo_checkpoint(out_dir: str, shape: OctoShape = OCTO_BASELINE, seed: int = 0) -> str:
+    """Write a random-init Octo checkpoint directory with its tokenizer in
+    out_dir/tok; returns out_dir."""
+    os.makedirs(os.path.join(out_dir, "tok"), exist_ok=True)
+    rng = np.random.default_rng(seed)
+    s = shape
+
+    def normal(shape_, std):
+        return (rng.standard_normal(shape_, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+    def save(name, parts):
+        np.concatenate([np.asarray(p, np.float32).reshape(-1) for p in parts]).astype(np.float32).tofile(
+            os.path.join(out_dir, name))
+
+    def scale_bias(c):
+        return [(1.0 + normal((c,), 0.05)).astype(np.float32), normal((c,), 0.05)]
+
+    vocab = octo_vocab()
+    with open(os.path.join(out_dir, "tok", "vocab.txt"), "w", encoding="utf-8") as f:
+        for p, sc in vocab:
+            f.write(f"{p}\t{sc!r}\n")
+
+    # T5 encoder: embedding, relative bias [32][heads], per layer ln1 q k v o ln2 wi wo, final ln
+    D5, hd5 = s.t5_dim, s.t5_dim // s.t5_heads
+    parts = [normal((len(vocab), D5), 1.0), normal((32, s.t5_heads), 0.5)]
+    for _ in range(s.t5_layers):
+        parts += [1.0 + normal((D5,), 0.05)]
+        parts += [normal((D5, D5), 1.0 / np.sqrt(D5 * hd5))]          # q (T5 folds 1/sqrt(d_kv) in)
+        parts += [normal((D5, D5), 1.0 / np.sqrt(D5)) for _ in range(3)]
+        parts += [1.0 + normal((D5,), 0.05), normal((s.t5_ff, D5), 1.0 / np.sqrt(D5)),
+                  normal((D5, s.t5_ff), 1.0 / np.sqrt(s.t5_ff))]
+    parts += [1.0 + normal((D5,), 0.05)]
+    save("t5.bin", parts)
+    with open(os.path.join(out_dir, "t5.meta"), "w") as f:
+        f.write(f"d_model {D5}\nn_layers {s.t5_layers}\nn_heads {s.t5_heads}\nd_kv {hd5}\nd_ff {s.t5_ff}\n"
+                f"vocab {len(vocab)}\nn_buckets 32\nmax_dist 128\neps 1e-6\nn_tokens {s.n_task}\n")
+
+    # SmallStems: per layer conv w [Cout][3][3][Cin], b, GroupNorm scale, bias; embed
+    for name in ("stem_primary", "stem_wrist"):
+        parts = []
+        cin = 6
+        for cout in s.stem_features:
+            parts += [normal((cout, 3, 3, cin), np.sqrt(2.0 / (9 * cin))), normal((cout,), 0.05)] + scale_bias(cout)
+            cin = cout
+        parts += [normal((s.stem_dim, cin), np.sqrt(1.0 / cin)), normal((s.stem_dim,), 0.02)]
+        save(f"{name}.bin", parts)
+        with open(os.path.join(out_dir, f"{name}.meta"), "w") as f:
+            f.write(f"in_ch 6\nn_layers {len(s.stem_features)}\nk 3\nstride 2\npad 1\n"
+                    "features " + " ".join(str(c) for c in s.stem_features) + "\n"
+                    f"embed_dim {s.stem_dim}\ngn_groups {s.gn_groups}\ngn_eps 1e-6\n")
+
+    # transformer: projections, position embeddings, blocks, final LayerNorm
+    D = s.d
+    parts = []
+
+    def lin(n, k, std=None):
+        parts.extend([normal((n, k), np.sqrt(1.0 / k) if std is None else std), normal((n,), 0.02)])
+
+    lin(D, s.t5_dim)
+    lin(D, s.stem_dim)
+    lin(D, s.stem_dim)
+    parts += [normal((s.n_task, D), 0.5), normal((s.max_horizon, s.tok_primary, D), 0.5),
+              normal((s.max_horizon, s.tok_wrist, D), 0.5), normal((s.max_horizon, 1, D), 0.5)]
+    for _ in range(s.n_layers):
+        parts += scale_bias(D)
+        for _ in range(4):
+            lin(D, D)
+        parts += scale_bias(D)
+        lin(s.mlp, D)
+        lin(D, s.mlp, 0.5 / np.sqrt(s.mlp))
+    parts += scale_bias(D)
+    save("octo.bin", parts)
+    with open(os.path.join(out_dir, "octo.meta"), "w") as f:
+        f.write(f"d {D}\nn_layers {s.n_layers}\nheads {s.heads}\nhead_dim {D // s.heads}\nmlp {s.mlp}\n"
+                f"max_horizon {s.max_horizon}\nn_task {s.n_task}\ntok_primary {s.tok_primary}\n"
+                f"tok_wrist {s.tok_wrist}\nn_readout 1\nt5_dim {s.t5_dim}\nstem_dim {s.stem_dim}\nln_eps 1e-6\n"
+                f"window {s.window}\ngelu_erf {int(s.gelu_erf)}\n")
+
+    # diffusion head: Fourier weights, cond MLP, score net, beta schedule
+    TD, H, FL = s.time_dim, s.hidden, s.flat
+    parts = [normal((TD // 2,), 0.2)]
+    lin(2 * TD, TD)
+    lin(TD, 2 * TD)
+    lin(H, TD + D + FL)
+    for _ in range(s.num_blocks):
+        parts += scale_bias(H)
+        lin(4 * H, H)
+        lin(H, 4 * H, 0.5 / np.sqrt(4 * H))
+    lin(FL, H)
+    # linear betas: a random-init score net would drive a cosine schedule's
+    # first steps into the +-max_action clamp and leave nothing to compare
+    betas = np.linspace(1e-4, 0.02, s.steps).astype(np.float32)
+    alphas = (1.0 - betas).astype(np.float32)
+    parts += [betas, alphas, np.cumprod(alphas).astype(np.float32)]
+    save("head.bin", parts)
+    with open(os.path.join(out_dir, "head.meta"), "w") as f:
+        f.write(f"emb {D}\naction_dim {s.action_dim}\nhorizon {s.horizon}\ntime_dim {TD}\n"
+                f"num_blocks {s.num_blocks}\nhidden {H}\nsteps {s.steps}\nmax_action {s.max_action!r}\n")
+
+    A = s.action_dim
+    normal((A,), 0.1).tofile(os.path.join(out_dir, "stats_action_mean.bin"))
+    rng.uniform(0.5, 1.5, A).astype(np.float32).tofile(os.path.join(out_dir, "stats_action_std.bin"))
+    np.array([1.0] * (A - 1) + [0.0], np.float32).tofile(os.path.join(out_dir, "stats_action_mask.bin"))
+    return out_dir
+
+
+def octo_inputs(shape: OctoShape = OCTO_BASELINE, seed: int = 1, batch: int = 0, wnd: int = 0):
+    """Seeded Octo query: primary [wnd, 256, 256, 3] and wrist [wnd, 128, 128, 3]
+    uint8 ~ U{0..255}, timestep mask [wnd] (all real), instruction string,
+    noise [flat] and z [steps, flat] ~ N(0, 1). With batch > 0 the arrays gain
+    a leading batch axis and the instruction becomes a list."""
+    rng = np.random.default_rng(seed)
+    s = shape
+    w = wnd or s.window
+    lead = (batch,) if batch else ()
+    primary = rng.integers(0, 256, size=lead + (w, 256, 256, 3), dtype=np.uint8)
+    wrist = rng.integers(0, 256, size=lead + (w, 128, 128, 3), dtype=np.uint8)
+    tmask = np.ones(lead + (w,), np.uint8)
+    noise = rng.standard_normal(lead + (s.flat,), dtype=np.float32)
+    z = rng.standard_normal(lead + (s.steps, s.flat), dtype=np.float32)
+    instr = [octo_instruction(seed * 131 + b) for b in range(batch)] if batch else octo_instruction(seed * 131)
+    return primary, wrist, tmask, instr, noise, z
+
+
+# ---------------------------------------------------------------------------
 # vla.simd GGUF packing of a converted directory (the container the reference's
 # converters write by default; read back by src/io/gguf_vla_simd.cpp): GGUF v3,
 # key/value "general.architecture" = "vla-simd", "vla_simd.format" = 1, every
