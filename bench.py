@@ -617,6 +617,178 @@ def run_dp(args):
     }), flush=True)
 
 
+OCTO_MASK = 63   # OCTO_INT8: every transformer / projection / stem / head GEMM in W8A8
+
+_OCTO_CPU_CHILD = r"""
+import ctypes, json, os, sys, time
+sys.path.insert(0, %(root)r)
+import numpy as np
+from vla_simd_b200 import synth
+budget, max_steps = %(budget)f, %(max_steps)d
+sh = synth.OCTO_BASELINE
+rng = np.random.default_rng(11)
+prim = rng.integers(0, 256, size=(max_steps + 2, 256, 256, 3), dtype=np.uint8)
+wrist = rng.integers(0, 256, size=(max_steps + 2, 128, 128, 3), dtype=np.uint8)
+tm = np.ones(sh.window, np.uint8)
+ins = synth.octo_instruction(1)
+from oracle import oracle
+r = oracle.reference()
+if r is None:
+    print(json.dumps({"unavailable": "oracle/_ref/libvla_ref.so (the reference's own build) not present"}))
+    sys.exit(0)
+l = r.l
+l.vla_octo_load.restype = ctypes.c_void_p
+l.vla_octo_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+l.vla_octo_predict.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int32, ctypes.c_void_p, ctypes.c_char_p,
+                                                       ctypes.c_uint64, ctypes.c_int32, ctypes.c_void_p]
+l.vla_octo_free.argtypes = [ctypes.c_void_p]
+h = l.vla_octo_load(%(ckpt)r.encode(), (%(ckpt)r + "/tok").encode())
+out = np.zeros((sh.horizon, sh.action_dim), np.float32)
+P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+def query(i):
+    # a control loop's sliding window: one new frame per call (the reference
+    # reuses the stem output of the frame it saw last call)
+    p = np.ascontiguousarray(prim[i:i + sh.window]); w = np.ascontiguousarray(wrist[i:i + sh.window])
+    return l.vla_octo_predict(h, P(p), P(w), sh.window, P(tm), ins.encode(), i, 1, P(out))
+query(0)
+times = []
+t_end = time.perf_counter() + budget
+while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+    t0 = time.perf_counter()
+    rc = query(len(times) + 1)
+    times.append(time.perf_counter() - t0)
+    assert rc == 0
+l.vla_octo_free(h)
+print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * float(np.median(times))}))
+"""
+
+
+def time_reference_octo_cpu(ckpt: str, budget_s: float, max_steps: int):
+    """The reference's own Octo query (oracle/_ref) in a fresh process, all host cores."""
+    cores = cpu_cores()
+    env = dict(os.environ, OCTO_INT8=str(OCTO_MASK), OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close",
+               CUDA_VISIBLE_DEVICES="")
+    code = _OCTO_CPU_CHILD % {"root": ROOT, "budget": budget_s, "max_steps": max_steps, "ckpt": ckpt}
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        return {"unavailable": f"reference CPU run failed: {r.stderr.strip().splitlines()[-1:]}"}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    if "unavailable" in d:
+        return d
+    d["cores"] = cores
+    d["chunks_per_s"] = d["steps"] / d["seconds"]
+    return d
+
+
+def run_octo(args):
+    """Octo-base-shaped policy: one query batch per step (2-frame window of a
+    256x256 primary and a 128x128 wrist camera, one instruction whose T5
+    encoding is cached, DDPM 20); replicas per GPU."""
+    import torch
+    rank, local_rank, world = _env_rank()
+    os.environ["VLA_CUDA_DEVICE"] = str(local_rank)
+    os.environ["OCTO_INT8"] = str(OCTO_MASK)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from vla_simd_b200 import OctoPolicy, synth
+    B = args.batch
+    sh = synth.OCTO_BASELINE
+    ckpt_root = tempfile.mkdtemp(prefix="vla_octo_")
+    ckpt = synth.write_octo_checkpoint(os.path.join(ckpt_root, "octo"), sh, seed=0)
+    pol = OctoPolicy(ckpt, max_batch=B)
+    p, w, tm, ins, noise, z = synth.octo_inputs(sh, seed=1 + rank, batch=B)
+    ins = [synth.octo_instruction(1)] * B
+    pol.predict_batch(p, w, tm, ins, noise, z)   # leaves the batch resident in the device input buffers
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        pol.enqueue(B, sh.window, True, stream.cuda_stream)
+    torch.cuda.synchronize()
+    kernels = pol.kernels_per_step
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            starts[i].record(stream)
+            pol.enqueue(B, sh.window, True, stream.cuda_stream)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    step_s = [s_.elapsed_time(e_) * 1e-3 for s_, e_ in zip(starts, ends)]
+    total_max = max_over_ranks(sum(step_s), dist, dev)
+    value = job_value(args.steps * B, world, total_max)
+    # end to end through the C ABI: host frames (a sliding window, a new frame
+    # per call), noise and z in, host actions out
+    n_e2e = max(args.steps, 10)
+    rng = np.random.default_rng(11 + rank)
+    seq_p = rng.integers(0, 256, size=(n_e2e + 3, B, 256, 256, 3), dtype=np.uint8)
+    seq_w = rng.integers(0, 256, size=(n_e2e + 3, B, 128, 128, 3), dtype=np.uint8)
+
+    def window(i):
+        return (np.ascontiguousarray(seq_p[i:i + sh.window].transpose(1, 0, 2, 3, 4)),
+                np.ascontiguousarray(seq_w[i:i + sh.window].transpose(1, 0, 2, 3, 4)))
+    wins = [window(i) for i in range(n_e2e + 2)]
+    for i in range(2):
+        pol.predict_batch(wins[i][0], wins[i][1], tm, ins, noise, z)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        pol.predict_batch(wins[i + 2][0], wins[i + 2][1], tm, ins, noise, z)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    e2e = {"value": job_value(n_e2e * B, world, e2e_s), "unit": "chunks/s",
+           "h2d_bytes_per_step": p.nbytes + w.nbytes + tm.nbytes + noise.nbytes + z.nbytes + 4 * B,
+           "d2h_bytes_per_step": B * sh.flat * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
+           "path": "vla_octo_predict_batch (C ABI), host frames + masks + noise -> host actions"}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = time_reference_octo_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
+    pol.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu_baseline = None
+    if cpu and "unavailable" not in cpu:
+        cpu_baseline = {"value": round(cpu["chunks_per_s"], 3), "unit": "chunks/s", "cores": cpu["cores"],
+                        "kind": "reference", "p50_ms": round(cpu["p50_ms"], 2),
+                        "sample": f"{cpu['steps']} single queries (same checkpoint, OCTO_INT8={OCTO_MASK}, a "
+                                  f"sliding 2-frame window) of the reference's own vla_octo_predict, "
+                                  f"OMP_NUM_THREADS={cpu['cores']}"}
+    elif cpu:
+        cpu_baseline = {"unavailable": cpu["unavailable"]}
+    print(json.dumps({
+        "metric": "Octo throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
+        "data": "synthetic (seeded random-init Octo weights, uniform uint8 frames, N(0,1) noise, a synthetic "
+                "T5 vocabulary)",
+        "config": {"workload": "Octo-base-shaped: 12 layers d768 12 heads MLP 3072, 2-frame window of 256x256 "
+                               "primary + 128x128 wrist (256 + 64 tokens per frame), T5-base text tower over 16 "
+                               "tokens (cached per instruction), 20-step DDPM head, 4x7 chunk",
+                   "batch_per_gpu": B, "int8_mask": OCTO_MASK, "parallelism": f"replicas x{world} (no collective)",
+                   "l2": "flushed between steps (256 MiB memset outside the timed events)"},
+        "latency_ms": {"p50": round(1e3 * statistics.median(step_s), 4),
+                       "p95": round(1e3 * float(np.percentile(step_s, 95)), 4)},
+        "cpu_baseline": cpu_baseline, "e2e": e2e, "gpu_launches": kernels * args.steps,
+        "kernels_per_step": kernels, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_reference(args):
     """Reference arm: the reference's own CPU implementation on this host (rank 0 only)."""
     rank, _, world = _env_rank()
@@ -656,9 +828,10 @@ def main():
     ap.add_argument("--op", default=None, help="time one op at its ACT shape (attention, gemm_qkv, gemm_w1, "
                                                "gemm_w2, layernorm, quantize, conv_layer1), or gemm_msweep "
                                                "(the FFN GEMM at M = 602 x {1, 8, 32, 128})")
-    ap.add_argument("--model", choices=["act", "dp"], default="act",
-                    help="act: the ACT step (the headline line); dp: Diffusion Policy (BASELINE configs[2])")
-    ap.add_argument("--batch", type=int, default=1, help="queries per step per GPU (--model dp)")
+    ap.add_argument("--model", choices=["act", "dp", "octo"], default="act",
+                    help="act: the ACT step (the headline line); dp: Diffusion Policy (BASELINE configs[2]); "
+                         "octo: the Octo-base-shaped policy")
+    ap.add_argument("--batch", type=int, default=1, help="queries per step per GPU (--model dp / octo)")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
     args = ap.parse_args()
@@ -673,6 +846,8 @@ def main():
         return
     if args.model == "dp" and args.impl != "reference":
         run_dp(args)
+    elif args.model == "octo" and args.impl != "reference":
+        run_octo(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

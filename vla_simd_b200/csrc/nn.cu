@@ -561,10 +561,34 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
     const float NINF = __int_as_float(0xff800000);
     const float* Kh = K + (long long)kvh * kAttD;
     const float* Vh = V + (long long)kvh * kAttD;
-    const int ntiles = (seq_k + kAttTK - 1) / kAttTK;
 
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
+
+    // Keys past every row's bound (trailing `lowest` mask entries, hal::row_bound)
+    // are never read: their probabilities are 0 and an fma with 0 leaves a chain
+    // unchanged, so the CTA stops at the largest bound of its rows (a fully
+    // blocked row keeps every key: it takes the uniform mean of V).
+    __shared__ int s_kend;
+    if (tid == 0) s_kend = mask ? 0 : seq_k;
+    __syncthreads();
+    if (mask) {
+        for (int r = warp; r < QP; r += 8) {
+            const int q = q0 + r;
+            if (q >= seq_q) continue;
+            const float* mr = mask + (long long)q * seq_k;
+            int last = -1;
+            for (int j = lane; j < seq_k; j += 32)
+                if (mr[j] != -FLT_MAX) last = j;
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
+            if (lane == 0) atomicMax(&s_kend, last < 0 ? seq_k : last + 1);
+        }
+    }
+    __syncthreads();
+    const int kend = s_kend;
+    const int skp_c = (kend + 7) & ~7;
+    const int ntiles = (kend + kAttTK - 1) / kAttTK;
 
     // kAttTK rows x 16 chunks of 16 bytes; rows past seq_k are zero-filled
     auto load_tile = [&](const float* base, long long ld, int k0, float* dst) {
@@ -665,7 +689,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         // shared-memory latency (and on the exp chain).
         // (branch-free bodies: selects, so the QPT rows' chains interleave)
         if (mask) {
-            for (int j = lane; j < skp; j += 32) {
+            for (int j = lane; j < skp_c; j += 32) {
                 float v[QPT];
                 #pragma unroll
                 for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
@@ -679,7 +703,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
                 for (int k = 0; k < QPT; ++k) srow[k][j] = v[k];
             }
         } else {
-            for (int j = lane; j < skp; j += 32) {
+            for (int j = lane; j < skp_c; j += 32) {
                 float v[QPT];
                 #pragma unroll
                 for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
@@ -699,7 +723,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xFFFFFFFFu, mx[k], off));
         const float u = __fdiv_rn(1.0f, (float)seq_k);
-        for (int j = lane; j < skp; j += 32) {
+        for (int j = lane; j < skp_c; j += 32) {
             float v[QPT];
             #pragma unroll
             for (int k = 0; k < QPT; ++k) v[k] = srow[k][j];
@@ -724,10 +748,10 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         const float* rowb = kk + 4 < QPT ? sS + (QPT * warp + kk + 4) * ss : nullptr;
         if (rowa && rowb) {
             #pragma unroll 4
-            for (int j = t; j < skp; j += 8) { s0 = __fadd_rn(s0, rowa[j]); s1 = __fadd_rn(s1, rowb[j]); }
+            for (int j = t; j < skp_c; j += 8) { s0 = __fadd_rn(s0, rowa[j]); s1 = __fadd_rn(s1, rowb[j]); }
         } else if (rowa) {
             #pragma unroll 8
-            for (int j = t; j < skp; j += 8) s0 = __fadd_rn(s0, rowa[j]);
+            for (int j = t; j < skp_c; j += 8) s0 = __fadd_rn(s0, rowa[j]);
         }
         float inv[QPT];
         #pragma unroll
@@ -739,8 +763,8 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
                                         __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
             inv[k] = __fdiv_rn(1.0f, sum);
         }
-        for (int j = lane; j < skp; j += 64) {
-            const bool two = j + 32 < skp;
+        for (int j = lane; j < skp_c; j += 64) {
+            const bool two = j + 32 < skp_c;
             float v[QPT], w[QPT];
             #pragma unroll
             for (int k = 0; k < QPT; ++k) {
@@ -768,7 +792,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         cp_async_wait_prev();
         __syncthreads();                // also: the softmax is done before tile 0
         const int k0 = t * kAttTK;
-        const int kn = min(kAttTK, seq_k - k0);
+        const int kn = min(kAttTK, kend - k0);
         const float* prow = sS + r0 * ss + k0;
         int j = 0;
         #pragma unroll 2
@@ -871,16 +895,26 @@ cudaError_t attention_batched(const float* Q, long long ldq, const float* K, lon
     const size_t ss = (size_t)att_row_stride(seq_k);
     auto need = [&](int qt) { return sizeof(float) * (qt * ss + (size_t)kAttD * qt + (size_t)kAttKT * kAttD); };
     // Register-tiled kernel: the query tile (8, 16 or 40 rows) that gives the
-    // busiest SM the fewest rows (ceil(CTAs / SMs) x rows; ties to the larger
-    // tile, which reuses each K/V tile more). 602 queries x 8 heads: 40 rows,
-    // 128 CTAs in one wave; the decoder's 100 queries: 8 rows, 104 CTAs.
+    // busiest SM the least work (ceil(CTAs / SMs) x rows x the tile's cost per
+    // row). 602 queries x 8 heads: 40 rows, 128 CTAs in one wave; the
+    // decoder's 100 queries: 8 rows, 104 CTAs; Octo's 690 x 12 heads: 40 rows.
     if (att_tiled_smem(8, seq_k) <= 227 * 1024) {
         int best_qpt = 0;
         long long best_rows = 0;
+        static const int forced = [] {
+            const char* e = std::getenv("VLA_ATT_QPT");   // tuning knob: 1, 2 or 5 query rows per warp
+            const int v = e ? std::atoi(e) : 0;
+            return v == 1 || v == 2 || v == 5 ? v : 0;
+        }();
         for (int qpt : {5, 2, 1}) {
             if (att_tiled_smem(8 * qpt, seq_k) > 227 * 1024) continue;
-            const long long ctas = (long long)((seq_q + 8 * qpt - 1) / (8 * qpt)) * n_q;
-            const long long rows = (ctas + 147) / 148 * 8 * qpt;
+            if (forced && qpt != forced) continue;
+            const long long ctas = (long long)((seq_q + 8 * qpt - 1) / (8 * qpt)) * n_q * bs.n;
+            // rows on the busiest SM, weighted by the measured cost of a row at
+            // each tile height (taller tiles reuse every K / V value more:
+            // 1.0 / 1.3 / 1.4 per row for 40 / 16 / 8 rows, Octo shapes)
+            const int w = qpt == 5 ? 10 : qpt == 2 ? 13 : 14;
+            const long long rows = (ctas + 147) / 148 * 8 * qpt * w;
             if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
         }
         if (best_qpt == 5)

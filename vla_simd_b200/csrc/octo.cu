@@ -306,6 +306,173 @@ __global__ void silu_exact_kernel(float* __restrict__ x, long long n) {
     }
 }
 
+// ------------------------------------------- activation + row quantization
+// One CTA per row: v = act(x) (kAct* kinds of lm_ops, or kActSiluLibm for
+// silu with the C library's expf), staged in shared memory, optionally written
+// back, then quantize_act_i8 of the row (the scale and codes of quantize_rows):
+// the activation and the next W8A8 layer's input quantization in one pass.
+__device__ __forceinline__ float act_any(int kind, float v) {
+    return kind == kActSiluLibm ? __fdiv_rn(v, __fadd_rn(1.0f, libm_expf(-v))) : act_eval(kind, v, 0.0f);
+}
+
+__global__ void __launch_bounds__(256) act_rows_q_kernel(int kind, float* __restrict__ x, int K, int keep,
+                                                          int8_t* __restrict__ q, long long ldq,
+                                                          float* __restrict__ scale) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float arow[];
+    __shared__ float red[8];
+    const long long row = blockIdx.x;
+    float* xr = x + row * K;
+    float m = 0.0f;
+    for (int k = threadIdx.x; k < K; k += 256) {
+        const float v = act_any(kind, xr[k]);
+        arow[k] = v;
+        m = fmaxf(m, fabsf(v));
+        if (keep) xr[k] = v;
+    }
+    m = block_max_256(m, red);
+    const float sc = row_scale(m), inv = __fdiv_rn(1.0f, sc);
+    int8_t* qr = q + row * ldq;
+    for (long long k = threadIdx.x; k < ldq; k += 256) qr[k] = k < K ? q8(arow[k], inv) : 0;
+    if (threadIdx.x == 0) scale[row] = sc;
+}
+
+cudaError_t act_rows_q(int kind, float* x, int M, int K, bool keep, int8_t* q, long long ldq, float* scale,
+                       cudaStream_t st) {
+    if (M <= 0 || K <= 0 || ldq < K || K > 12288) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (size_t)K;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        const cudaError_t e = cudaFuncSetAttribute(act_rows_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const cudaError_t e = launch_k(act_rows_q_kernel, (unsigned)M, 256, smem, st, kind, x, K, keep ? 1 : 0, q, ldq,
+                                   scale);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------- head step tail
+// One CTA (32 warps) per query: silu(h) -> eps = out_proj(.) with the exact
+// fp32 dense_linear order per output (mm_block4 for outputs in whole blocks
+// of 4, simd_dot for the rest; src/hal/avx2/gemm.cpp:33-122) -> the DDPM
+// update of x -> the next step's score-net input row [cond | emb | x] and its
+// int8 quantization. With x0 (the initial noise) instead of h: only the
+// first input row (and sample = x0).
+__device__ __forceinline__ float warp_dense_out(const float* __restrict__ xr, const float* __restrict__ wr, int K,
+                                                bool block4) {
+    const int lane = threadIdx.x & 31;
+    float acc = 0.0f;
+    int kend;
+    if (block4) {
+        const int K16 = K & ~15;
+        if (lane < 16)
+            for (int k = 0; k < K16; k += 16) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        kend = K16;
+        if (K - K16 >= 8) {
+            if (lane < 8) acc = __fmaf_rn(xr[K16 + lane], wr[K16 + lane], acc);
+            kend = K16 + 8;
+        }
+        acc = __fadd_rn(acc, __shfl_down_sync(0xFFFFFFFFu, acc, 8));
+    } else {
+        const int K32 = K & ~31;
+        for (int k = 0; k < K32; k += 32) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        kend = K32;
+        for (; kend + 8 <= K; kend += 8)
+            if (lane < 8) acc = __fmaf_rn(xr[kend + lane], wr[kend + lane], acc);
+        const float a1 = __shfl_down_sync(0xFFFFFFFFu, acc, 8);
+        const float a2 = __shfl_down_sync(0xFFFFFFFFu, acc, 16);
+        const float a3 = __shfl_down_sync(0xFFFFFFFFu, acc, 24);
+        acc = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+    }
+    float l[8];
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) l[i] = __shfl_sync(0xFFFFFFFFu, acc, i);
+    float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[4]), __fadd_rn(l[1], l[5])),
+                          __fadd_rn(__fadd_rn(l[2], l[6]), __fadd_rn(l[3], l[7])));
+    if (block4)
+        for (int k = kend; k < K; ++k) sum = __fmaf_rn(xr[k], wr[k], sum);
+    else
+        for (int k = kend; k < K; ++k) sum = __fadd_rn(sum, __fmul_rn(xr[k], wr[k]));
+    return sum;
+}
+
+__global__ void __launch_bounds__(1024) octo_head_tail_kernel(OctoHeadTail a) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float hsm[];
+    float* hs = hsm;                  // [H] silu(h)
+    float* xs = hs + a.H;             // [FL] updated sample
+    float* in = xs + a.FL;            // [IN] next input row
+    __shared__ float red[32];
+    const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int IN = a.TD + a.E + a.FL;
+    float* xb = a.sample + (long long)b * a.FL;
+    if (a.h) {
+        const float* hb = a.h + (long long)b * a.H;
+        for (int k = tid; k < a.H; k += blockDim.x) hs[k] = __fdiv_rn(hb[k], __fadd_rn(1.0f, libm_expf(-hb[k])));
+        __syncthreads();
+        const int nb4 = a.FL - a.FL % 4;
+        for (int n = warp; n < a.FL; n += blockDim.x >> 5) {
+            float e = warp_dense_out(hs, a.W + (long long)n * a.H, a.H, n < nb4);
+            e = a.bias ? __fadd_rn(e, a.bias[n]) : e;
+            if (lane == 0) {
+                const float zv = a.z ? a.z[(long long)b * a.z_stride + n] : 0.0f;
+                const float v = __fmaf_rn(__fmaf_rn(-a.a2, e, xb[n]), a.a1, __fmul_rn(a.sb, zv));
+                xs[n] = v < -a.max_action ? -a.max_action : v > a.max_action ? a.max_action : v;
+            }
+        }
+        __syncthreads();
+        for (int n = tid; n < a.FL; n += blockDim.x) xb[n] = xs[n];
+    } else {
+        for (int n = tid; n < a.FL; n += blockDim.x) {
+            xs[n] = a.x0[(long long)b * a.FL + n];
+            xb[n] = xs[n];
+        }
+        __syncthreads();
+    }
+    if (!a.cond_next) return;
+    float m = 0.0f;
+    for (int c = tid; c < IN; c += blockDim.x) {
+        const float v = c < a.TD ? a.cond_next[c] : c < a.TD + a.E ? a.emb[(long long)b * a.E + (c - a.TD)]
+                                                                   : xs[c - a.TD - a.E];
+        in[c] = v;
+        m = fmaxf(m, fabsf(v));
+        if (a.in_f32) a.in_f32[(long long)b * IN + c] = v;
+    }
+    if (!a.q) return;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    const float sc = row_scale(m), inv = __fdiv_rn(1.0f, sc);
+    int8_t* qr = a.q + (long long)b * a.ldq;
+    for (long long c = tid; c < a.ldq; c += blockDim.x) qr[c] = c < IN ? q8(in[c], inv) : 0;
+    if (tid == 0) a.qscale[b] = sc;
+}
+
+cudaError_t octo_head_tail(const OctoHeadTail& a, cudaStream_t st) {
+    if (a.B <= 0 || a.FL <= 0 || (!a.h && !a.x0) || (a.h && (!a.W || a.H <= 0))) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * ((size_t)a.H + a.FL + a.TD + a.E + a.FL);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        const cudaError_t e = cudaFuncSetAttribute(octo_head_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const cudaError_t e = launch_k(octo_head_tail_kernel, (unsigned)a.B, 1024, smem, st, a);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 cudaError_t silu_exact(float* x, long long n, cudaStream_t st) {
     if (n <= 0) return cudaErrorInvalidValue;
     const cudaError_t e = launch_k(silu_exact_kernel, (unsigned)grid_cap(n, 256, 148 * 4), 256, 0, st, x, n);

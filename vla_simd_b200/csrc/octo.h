@@ -49,6 +49,38 @@ cudaError_t octo_mask(const OctoSeq& s, const uint8_t* tmask, bool wrist, float*
 // Rows of n_rows queries: dst[b][0..n) = src[slot[b]][0..n) (the cached T5 outputs).
 cudaError_t gather_rows(const float* src, const int* slot, int n_rows, long long n, float* dst, cudaStream_t st);
 
+// Per-row activation then int8 quantization (quantize_act_i8's scale and
+// codes) of x [M][K]: kind is an lm_ops kAct* kind, or kActSiluLibm (silu with
+// the C library's expf). keep: also write the activation back into x.
+enum : int { kActSiluLibm = 100 };
+cudaError_t act_rows_q(int kind, float* x, int M, int K, bool keep, int8_t* q, long long ldq, float* scale,
+                       cudaStream_t st);
+
+// The tail of one score-net evaluation of B queries, fused: silu(h) ->
+// eps = out_proj (fp32, the reference's dense_linear order) -> DDPM update of
+// sample (a1, a2, sb as octo_ddpm_step; z [B][z_stride] or null) -> the next
+// step's input row [cond_next | emb | x] (in_f32 [B][IN] when set) and its
+// int8 quantization (q [B][ldq], qscale [B]) when q is set. With h null and
+// x0 set: sample = x0 and the first input row only.
+struct OctoHeadTail {
+    int B = 0, H = 0, FL = 0, TD = 0, E = 0;
+    const float* h = nullptr;      // [B][H] the score net's last hidden state (pre-silu)
+    const float* x0 = nullptr;     // [B][FL] initial noise (first call)
+    const float* W = nullptr;      // out_proj [FL][H]
+    const float* bias = nullptr;
+    float* sample = nullptr;       // [B][FL]
+    const float* z = nullptr;
+    long long z_stride = 0;
+    float a1 = 0, a2 = 0, sb = 0, max_action = 0;
+    const float* cond_next = nullptr;   // [TD] or null (last step)
+    const float* emb = nullptr;         // [B][E]
+    float* in_f32 = nullptr;
+    int8_t* q = nullptr;
+    long long ldq = 0;
+    float* qscale = nullptr;
+};
+cudaError_t octo_head_tail(const OctoHeadTail& a, cudaStream_t st);
+
 // x[i] = x[i] / (1 + expf(-x[i])) with the C library's expf (src/hal/common/eltwise.cpp:59-66).
 cudaError_t silu_exact(float* x, long long n, cudaStream_t st);
 

@@ -106,6 +106,37 @@ int t5_bucket(int rp, int num_buckets, int max_dist) {
     return base + b;
 }
 
+// The reference's seeded draw: std::normal_distribution<float> over
+// std::mt19937_64 (Marsaglia's polar method on generate_canonical uniforms,
+// the second value of each pair saved for the next call), with the one
+// contraction its -mfma -ffp-contract=fast build makes: r2 = fma(x, x, y*y)
+// (read from the compiled reference; x = 2u - 1 is exact either way).
+class PolarNormal {
+  public:
+    explicit PolarNormal(uint64_t seed) : rng_(seed) {}
+    float operator()() {
+        if (have_saved_) {
+            have_saved_ = false;
+            return saved_;
+        }
+        float x, y, r2;
+        do {
+            x = 2.0f * std::generate_canonical<float, 24>(rng_) - 1.0f;
+            y = 2.0f * std::generate_canonical<float, 24>(rng_) - 1.0f;
+            r2 = std::fma(x, x, y * y);
+        } while (r2 > 1.0f || r2 == 0.0f);
+        const float mult = std::sqrt(-2.0f * std::log(r2) / r2);
+        saved_ = x * mult;
+        have_saved_ = true;
+        return y * mult;
+    }
+
+  private:
+    std::mt19937_64 rng_;
+    float saved_ = 0.0f;
+    bool have_saved_ = false;
+};
+
 int grid_side(int s, int n_layers, int k, int stride, int pad) {
     for (int i = 0; i < n_layers; ++i) {
         const long long num = (long long)s + 2LL * pad - k;
@@ -850,8 +881,7 @@ cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, boo
             VSB_TRY(layernorm(d_x_, d_h_, L.ln2s, L.ln2b, static_cast<int>(rows), D, c.ln_eps, nullptr,
                               L.w1.int8 ? d_q_ : nullptr, L.w1.int8 ? d_qs_ : nullptr, nullptr, nullptr, ldq, st));
             VSB_TRY(linear_q(L.w1, d_q_, d_qs_, d_h_, D, static_cast<int>(rows), d_ff_, c.mlp, 0, nullptr, 0, st));
-            VSB_TRY(activation(act, d_ff_, d_ff_, nullptr, rows * c.mlp, st));
-            VSB_TRY(linear(L.w2, d_ff_, c.mlp, static_cast<int>(rows), d_x_, D, kEpiAdd, d_x_, D, st));
+            VSB_TRY(mlp_out(L, act, static_cast<int>(rows), d_x_, st));
         } else {
             // readout-only final layer (EncoderLayer::forward_last_row,
             // src/nn/encoder.cpp:80-111): K/V of every token, the rest for row ro
@@ -863,8 +893,7 @@ cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, boo
             VSB_TRY(layernorm(d_xr_, d_h_, L.ln2s, L.ln2b, B, D, c.ln_eps, nullptr, L.w1.int8 ? d_q_ : nullptr,
                               L.w1.int8 ? d_qs_ : nullptr, nullptr, nullptr, ldq, st));
             VSB_TRY(linear_q(L.w1, d_q_, d_qs_, d_h_, D, B, d_ff_, c.mlp, 0, nullptr, 0, st));
-            VSB_TRY(activation(act, d_ff_, d_ff_, nullptr, (long long)B * c.mlp, st));
-            VSB_TRY(linear(L.w2, d_ff_, c.mlp, B, d_xr_, D, kEpiAdd, d_xr_, D, st));
+            VSB_TRY(mlp_out(L, act, B, d_xr_, st));
         }
     }
     VSB_TRY(layernorm(d_xr_, d_emb_, final_s_, final_b_, B, D, c.ln_eps, nullptr, nullptr, nullptr, nullptr, nullptr,
@@ -872,30 +901,101 @@ cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, boo
 
     // DDPM over the score network (DiffusionHead::denoise, diffusion_head.cpp:172-191;
     // nn::DiffusionMlp::forward, src/nn/diffusion.cpp:15-36)
-    const int TD = c.time_dim, H = c.hidden, IN = TD + D + FL;
-    VSB_TRY(cudaMemcpyAsync(d_sample_, d_noise_, sizeof(float) * (size_t)B * FL, cudaMemcpyDeviceToDevice, st));
-    auto head_linear = [&](const DevLinear& l, const float* x, int K, float* out, int mode, const float* res) -> cudaError_t {
+    return run_head(B, st, unnormalize);
+}
+
+// The MLP's second half of M rows: gelu(ff) -> w2 -> x += . (src/nn/encoder.cpp:62-77).
+// An int8 w2 takes gelu and its row quantization in one pass.
+cudaError_t OctoPolicy::mlp_out(const OctoLayerDev& L, int act, int M, float* x, cudaStream_t st) {
+    const OctoConfigDev& c = cfg_;
+    if (L.w2.int8) {
+        VSB_TRY(act_rows_q(act, d_ff_, M, c.mlp, false, d_q_, round16(c.mlp), d_qs_, st));
+        return linear_q(L.w2, d_q_, d_qs_, nullptr, 0, M, x, c.d, kEpiAdd, x, c.d, st);
+    }
+    VSB_TRY(activation(act, d_ff_, d_ff_, nullptr, (long long)M * c.mlp, st));
+    return linear(L.w2, d_ff_, c.mlp, M, x, c.d, kEpiAdd, x, c.d, st);
+}
+
+// The diffusion head of B queries: per step in_proj -> blocks (LN -> d0 ->
+// silu -> d1, residual) -> the fused tail (silu, out_proj, DDPM update, next
+// input row and its quantization).
+cudaError_t OctoPolicy::run_head(int B, cudaStream_t st, bool unnormalize) {
+    const OctoConfigDev& c = cfg_;
+    const int D = c.d, FL = c.flat(), TD = c.time_dim, H = c.hidden, IN = TD + D + FL;
+    const bool fused_tail = !out_proj_.int8;   // the fp32 out_proj of a flat size that is not a multiple of 16
+    auto dense = [&](const DevLinear& l, const float* x, int K, float* out, int mode, const float* res) -> cudaError_t {
         if (l.int8) return linear(l, x, K, B, out, l.N, mode, res, l.N, st);
         // fp32 score-net layers are the reference's plain dense_linear (Role::Generic)
         VSB_TRY(linear_f32(x, K, l.W, l.bias, mode == kEpiAdd ? d_hn_ : out, l.N, B, l.N, K, nullptr, nullptr, st));
         if (mode == kEpiAdd) return add_f32(res, d_hn_, out, (long long)B * l.N, st);
         return cudaSuccess;
     };
+    auto input_row = [&](const float* h, const float* z, int t, int t_next) -> cudaError_t {
+        OctoHeadTail a;
+        a.B = B;
+        a.H = H;
+        a.FL = FL;
+        a.TD = TD;
+        a.E = D;
+        a.h = h;
+        a.x0 = h ? nullptr : d_noise_;
+        a.W = out_proj_.W;
+        a.bias = out_proj_.bias;
+        a.sample = d_sample_;
+        a.z = z;
+        a.z_stride = (long long)c.steps * FL;
+        if (t >= 0) {
+            a.a1 = a1_[t];
+            a.a2 = a2_[t];
+            a.sb = sb_[t];
+        }
+        a.max_action = c.max_action;
+        a.cond_next = t_next >= 0 ? d_cond_table_ + (size_t)t_next * TD : nullptr;
+        a.emb = d_emb_;
+        if (in_proj_.int8) {
+            a.q = d_q_;
+            a.ldq = round16(IN);
+            a.qscale = d_qs_;
+        } else {
+            a.in_f32 = d_hin_;
+        }
+        return octo_head_tail(a, st);
+    };
+    if (fused_tail) {
+        VSB_TRY(input_row(nullptr, nullptr, -1, c.steps - 1));
+    } else {
+        VSB_TRY(cudaMemcpyAsync(d_sample_, d_noise_, sizeof(float) * (size_t)B * FL, cudaMemcpyDeviceToDevice, st));
+    }
     for (int s = 0; s < c.steps; ++s) {
         const int t = c.steps - 1 - s;
-        VSB_TRY(octo_head_input(d_cond_table_ + (size_t)t * TD, TD, d_emb_, D, d_sample_, FL, B, d_hin_, st));
-        VSB_TRY(head_linear(in_proj_, d_hin_, IN, d_hh_, 0, nullptr));
-        for (const HeadBlock& hb : blocks_) {
-            VSB_TRY(layernorm(d_hh_, d_hn_, hb.ln_s, hb.ln_b, B, H, 1e-6f, nullptr, nullptr, nullptr, nullptr, nullptr,
-                              0, st));
-            VSB_TRY(head_linear(hb.d0, d_hn_, H, d_wide_, 0, nullptr));
-            VSB_TRY(silu_exact(d_wide_, (long long)B * 4 * H, st));
-            VSB_TRY(head_linear(hb.d1, d_wide_, 4 * H, d_hh_, kEpiAdd, d_hh_));
+        if (fused_tail) {
+            if (in_proj_.int8) VSB_TRY(linear_q(in_proj_, d_q_, d_qs_, nullptr, 0, B, d_hh_, H, 0, nullptr, 0, st));
+            else VSB_TRY(dense(in_proj_, d_hin_, IN, d_hh_, 0, nullptr));
+        } else {
+            VSB_TRY(octo_head_input(d_cond_table_ + (size_t)t * TD, TD, d_emb_, D, d_sample_, FL, B, d_hin_, st));
+            VSB_TRY(dense(in_proj_, d_hin_, IN, d_hh_, 0, nullptr));
         }
-        VSB_TRY(silu_exact(d_hh_, (long long)B * H, st));
-        VSB_TRY(head_linear(out_proj_, d_hh_, H, d_eps_, 0, nullptr));
-        VSB_TRY(octo_ddpm_step(d_sample_, d_eps_, d_z_ + (size_t)s * FL, (long long)c.steps * FL, B, FL, a1_[t], a2_[t],
-                               sb_[t], c.max_action, st));
+        for (const HeadBlock& hb : blocks_) {
+            VSB_TRY(layernorm(d_hh_, d_hn_, hb.ln_s, hb.ln_b, B, H, 1e-6f, nullptr, hb.d0.int8 ? d_q_ : nullptr,
+                              hb.d0.int8 ? d_qs_ : nullptr, nullptr, nullptr, round16(H), st));
+            if (hb.d0.int8) VSB_TRY(linear_q(hb.d0, d_q_, d_qs_, nullptr, 0, B, d_wide_, 4 * H, 0, nullptr, 0, st));
+            else VSB_TRY(dense(hb.d0, d_hn_, H, d_wide_, 0, nullptr));
+            if (hb.d1.int8) {
+                VSB_TRY(act_rows_q(kActSiluLibm, d_wide_, B, 4 * H, false, d_q_, round16(4 * H), d_qs_, st));
+                VSB_TRY(linear_q(hb.d1, d_q_, d_qs_, nullptr, 0, B, d_hh_, H, kEpiAdd, d_hh_, H, st));
+            } else {
+                VSB_TRY(silu_exact(d_wide_, (long long)B * 4 * H, st));
+                VSB_TRY(dense(hb.d1, d_wide_, 4 * H, d_hh_, kEpiAdd, d_hh_));
+            }
+        }
+        if (fused_tail) {
+            VSB_TRY(input_row(d_hh_, d_z_ + (size_t)s * FL, t, t > 0 ? t - 1 : -1));
+        } else {
+            VSB_TRY(silu_exact(d_hh_, (long long)B * H, st));
+            VSB_TRY(dense(out_proj_, d_hh_, H, d_eps_, 0, nullptr));
+            VSB_TRY(octo_ddpm_step(d_sample_, d_eps_, d_z_ + (size_t)s * FL, (long long)c.steps * FL, B, FL, a1_[t],
+                                   a2_[t], sb_[t], c.max_action, st));
+        }
     }
     return octo_actions(d_sample_, B, FL, c.action_dim, d_act_mean_, d_act_std_, d_act_mask_, unnormalize,
                         d_actions_, st);
@@ -975,10 +1075,9 @@ cudaError_t OctoPolicy::predict(int B, const uint8_t* primary, const uint8_t* wr
             float* hn = h_noise_;
             float* hz = h_noise_ + (size_t)B * FL;
             for (int b = 0; b < B; ++b) {
-                std::mt19937_64 rng(seeds[b]);
-                std::normal_distribution<float> N(0.0f, 1.0f);
-                for (int i = 0; i < FL; ++i) hn[(size_t)b * FL + i] = N(rng);
-                for (int i = 0; i < c.steps * FL; ++i) hz[(size_t)b * c.steps * FL + i] = N(rng);
+                PolarNormal N(seeds[b]);
+                for (int i = 0; i < FL; ++i) hn[(size_t)b * FL + i] = N();
+                for (int i = 0; i < c.steps * FL; ++i) hz[(size_t)b * c.steps * FL + i] = N();
             }
             VSB_TRY(cudaMemcpyAsync(d_noise_, hn, sizeof(float) * (size_t)B * FL, cudaMemcpyHostToDevice, stream_));
             VSB_TRY(cudaMemcpyAsync(d_z_, hz, sizeof(float) * (size_t)B * c.steps * FL, cudaMemcpyHostToDevice,

@@ -122,6 +122,8 @@ class OctoPolicy {
     int t5_slot(const std::string& instruction, cudaStream_t st, cudaError_t* err);
     cudaError_t run_t5(const std::vector<int>& ids, float* out, cudaStream_t st);
     cudaError_t run_stem(const OctoStemDev& s, const uint8_t* img, int F, float* tokens, cudaStream_t st);
+    cudaError_t mlp_out(const OctoLayerDev& L, int act, int M, float* x, cudaStream_t st);
+    cudaError_t run_head(int B, cudaStream_t st, bool unnormalize);
     cudaError_t linear(const DevLinear& l, const float* x, long long ldx, int M, float* out, long long ldo, int mode,
                        const float* res, long long ldr, cudaStream_t st);
     cudaError_t linear_q(const DevLinear& l, const int8_t* q, const float* qs, const float* x, long long ldx, int M,
