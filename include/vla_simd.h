@@ -104,6 +104,48 @@ VLA_API int32_t vla_diffusion_predict(void* h, const uint8_t* frames, const floa
                                       int32_t unnormalize, float* actions,
                                       const float* noise);
 
+/* -------------------------------------------------------------- SmolVLA -----
+ * replaces reference include/vla_simd.h:83-117 (src/models/smolvla/smolvla_capi.cpp:66-180).
+ * model_dir: a converter directory (vit / vlm / aex / heads .meta + .bin,
+ * emb.bin, stats_{state,action}_{mean,std}.bin, config.txt) as written by
+ * tools/convert_hf_safetensors.py, or its vla.simd GGUF; tok_dir holds the
+ * byte-level BPE tokenizer (vocab.txt, merges.txt). SMOLVLA_INT8 (1 vision
+ * q/k/v/o, 2 fc1, 4 fc2, 8 patch embedding + connector, 16 text tower, 32
+ * action expert) and SMOLVLA_NUM_STEPS keep the reference's meaning. */
+VLA_API void* vla_smolvla_load(const char* model_dir, const char* tok_dir);
+VLA_API void  vla_smolvla_free(void* h);
+
+VLA_API int32_t vla_smolvla_chunk(void* h);
+VLA_API int32_t vla_smolvla_action_dim(void* h);
+VLA_API int32_t vla_smolvla_state_dim(void* h);
+VLA_API int32_t vla_smolvla_n_views(void* h);
+VLA_API int32_t vla_smolvla_img_size(void* h);
+VLA_API int32_t vla_smolvla_tok_maxlen(void* h);
+
+/* ids / mask [tok_maxlen] of the instruction (a newline appended, the last
+ * tok_maxlen tokens kept, then pad); returns the token count. */
+VLA_API int32_t vla_smolvla_tokenize(void* h, const char* text, int32_t* ids, int32_t* mask);
+
+/* frames [n_views, height, width, 3] uint8 at the camera's resolution
+ * (resize-with-pad happens inside); lang tokens / mask [n_lang] from
+ * vla_smolvla_tokenize; state [state_dim] raw; noise [chunk, 32] or NULL
+ * (drawn from seed); actions out [chunk, action_dim]. */
+VLA_API int32_t vla_smolvla_predict(void* h, const uint8_t* frames, int32_t n_views,
+                                    int32_t height, int32_t width,
+                                    const int32_t* lang_tokens, const int32_t* lang_mask, int32_t n_lang,
+                                    const float* state, const float* noise, uint64_t seed,
+                                    float* actions);
+
+/* As vla_smolvla_predict with real-time-chunking guidance toward the previous
+ * chunk's first n_prev rows prev [n_prev, action_dim], weights [chunk],
+ * max_guidance > 0. */
+VLA_API int32_t vla_smolvla_predict_rtc(void* h, const uint8_t* frames, int32_t n_views,
+                                        int32_t height, int32_t width,
+                                        const int32_t* lang_tokens, const int32_t* lang_mask, int32_t n_lang,
+                                        const float* state, const float* noise, uint64_t seed,
+                                        float* actions, const float* prev, int32_t n_prev,
+                                        const float* weights, float max_guidance);
+
 /* ----------------------------------------------------------------- Octo -----
  * replaces reference include/vla_simd.h:121-144 (src/models/octo/octo_capi.cpp:19-58).
  * model_dir: a converter directory (t5.meta/.bin, stem_primary.meta/.bin,

@@ -292,6 +292,30 @@ VLA_API int64_t vla_octo_readout(void* h, float* out, int64_t cap);
  * max_len - 1, then </s>, then <pad> (src/tokenizer/t5_tokenizer.cpp:131-155). */
 VLA_API int32_t vla_t5_tokenize(const char* vocab_text, const char* text, int32_t max_len, int32_t* ids);
 
+/* --------------------------------------------------------- batched SmolVLA
+ * No counterpart in the reference, whose vla_smolvla_predict_rtc serves one
+ * query (src/models/smolvla/smolvla_capi.cpp:116-165): a handle loaded with
+ * max_batch serves up to that many queries of one frame size per call, each
+ * with its own prompt, state, noise (or seeds[b]) and guidance; every query's
+ * actions equal a single-query predict of it. frames [batch][n_views][h][w][3],
+ * lang tokens / mask [batch][n_lang], state [batch][state_dim], noise
+ * [batch][chunk][32] or NULL, prev [batch][n_prev][action_dim], weights
+ * [batch][chunk], actions [batch][chunk][action_dim]. */
+VLA_API void* vla_smolvla_load_batch(const char* model_dir, const char* tok_dir, int32_t max_batch);
+VLA_API int32_t vla_smolvla_predict_batch(void* h, int32_t batch, const uint8_t* frames, int32_t n_views,
+                                          int32_t height, int32_t width, const int32_t* lang_tokens,
+                                          const int32_t* lang_mask, int32_t n_lang, const float* state,
+                                          const float* noise, const uint64_t* seeds, float* actions,
+                                          const float* prev, int32_t n_prev, const float* weights,
+                                          float max_guidance);
+VLA_API int32_t vla_smolvla_int8_layers(void* h);
+VLA_API int32_t vla_smolvla_kernels_per_step(void* h);
+/* The byte-level BPE tokenizer SmolVLA's handles use (host code, no device
+ * work): ids of `text` (at most cap written; ids may be NULL when cap is 0)
+ * under the vocab.txt / merges.txt contents; returns the full token count. */
+VLA_API int32_t vla_bpe_tokenize(const char* vocab_text, const char* merges_text, const char* text, int32_t* ids,
+                                 int32_t cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -382,6 +382,64 @@ class Reference:
             raise RuntimeError("ref_t5_tokenize failed")
         return ids
 
+    def _smolvla_bind(self):
+        l = self.l
+        l.vla_smolvla_load.restype = VP
+        l.vla_smolvla_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+        l.vla_smolvla_free.argtypes = [VP]
+        for name in ("chunk", "action_dim", "tok_maxlen"):
+            getattr(l, f"vla_smolvla_{name}").argtypes = [VP]
+        l.vla_smolvla_tokenize.argtypes = [VP, ctypes.c_char_p, VP, VP]
+        l.vla_smolvla_predict_rtc.argtypes = [VP, VP, I32, I32, I32, VP, VP, I32, VP, VP, ctypes.c_uint64, VP, VP,
+                                              I32, VP, F32]
+        return l
+
+    def smolvla_predict(self, model_dir, frames, instruction, state, noise, seed=0, prev=None, weights=None,
+                        max_guidance=0.0):
+        """The reference's vla_smolvla_tokenize + vla_smolvla_predict_rtc
+        (src/models/smolvla/smolvla_capi.cpp:94-165) on one query: frames
+        [n_views, h, w, 3] uint8 at the camera's resolution, the instruction
+        string, raw state, noise [chunk, max_action_dim] or None (drawn from
+        seed), optional RTC guidance (prev [n_prev, action_dim], weights
+        [chunk]); returns actions [chunk, action_dim]."""
+        l = self._smolvla_bind()
+        h = l.vla_smolvla_load(model_dir.encode(), (model_dir + "/tok").encode())
+        if not h:
+            raise RuntimeError("reference vla_smolvla_load failed")
+        try:
+            n = l.vla_smolvla_tok_maxlen(h)
+            ids, mask = np.zeros(n, np.int32), np.zeros(n, np.int32)
+            if l.vla_smolvla_tokenize(h, instruction.encode(), _ptr(ids), _ptr(mask)) < 0:
+                raise RuntimeError("reference vla_smolvla_tokenize failed")
+            out = np.zeros((l.vla_smolvla_chunk(h), l.vla_smolvla_action_dim(h)), np.float32)
+            fr = np.ascontiguousarray(frames, np.uint8)
+            st = np.ascontiguousarray(state, np.float32)
+            nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+            pv = None if prev is None else np.ascontiguousarray(prev, np.float32)
+            wt = None if weights is None else np.ascontiguousarray(weights, np.float32)
+            rc = l.vla_smolvla_predict_rtc(h, _ptr(fr), fr.shape[0], fr.shape[1], fr.shape[2], _ptr(ids), _ptr(mask),
+                                           n, _ptr(st), _ptr(nz), seed, _ptr(out), _ptr(pv),
+                                           0 if pv is None else pv.shape[0], _ptr(wt), max_guidance)
+            if rc != 0:
+                raise RuntimeError(f"reference vla_smolvla_predict_rtc rc={rc}")
+            return out
+        finally:
+            l.vla_smolvla_free(h)
+
+    def smolvla_tokenize(self, model_dir, text):
+        """(ids, mask, n) of the reference's vla_smolvla_tokenize."""
+        l = self._smolvla_bind()
+        h = l.vla_smolvla_load(model_dir.encode(), (model_dir + "/tok").encode())
+        if not h:
+            raise RuntimeError("reference vla_smolvla_load failed")
+        try:
+            n = l.vla_smolvla_tok_maxlen(h)
+            ids, mask = np.zeros(n, np.int32), np.zeros(n, np.int32)
+            k = l.vla_smolvla_tokenize(h, text.encode(), _ptr(ids), _ptr(mask))
+            return ids, mask, k
+        finally:
+            l.vla_smolvla_free(h)
+
     def dp_global_cond(self, model_dir, frames, state):
         """The global conditioning vector the reference builds for one DP query (ref_dp_shim.cpp)."""
         l = self.l

@@ -186,12 +186,65 @@ def make_octo(digests):
         json.dump(ids, f, indent=0, sort_keys=True)
 
 
+# (config, shape, SMOLVLA_INT8, variant): "" the seeded query of smolvla_inputs(seed=1),
+# "rtc" with real-time-chunking guidance, "seed" the reference's own noise draw
+SMOLVLA_CASES = [("small", "SMOLVLA_SMALL", 63, ""), ("small", "SMOLVLA_SMALL", 0, ""),
+                 ("small", "SMOLVLA_SMALL", 63, "rtc"), ("small", "SMOLVLA_SMALL", 63, "seed"),
+                 ("small", "SMOLVLA_SMALL", 59, ""), ("base", "SMOLVLA_BASELINE", 63, "")]
+
+
+def smolvla_fixture_name(cfg, mask, variant):
+    return f"smolvla_{cfg}_m{mask}" + (f"_{variant}" if variant else "") + ".npy"
+
+
+def smolvla_query(shape, variant):
+    """The inputs of one SmolVLA fixture case: (frames, instruction, state, noise,
+    seed, prev, weights, max_guidance)."""
+    frames, ins, state, noise = synth.smolvla_inputs(shape, seed=1)
+    prev = weights = None
+    mg = 0.0
+    if variant == "rtc":
+        rng = np.random.default_rng(21)
+        prev = rng.standard_normal((3, shape.action_dim), dtype=np.float32)
+        weights = rng.uniform(0.0, 1.0, shape.chunk).astype(np.float32)
+        mg = 5.0
+    if variant == "seed":
+        noise = None
+    return frames, ins, state, noise, 9, prev, weights, mg
+
+
+def make_smolvla(digests):
+    for cfg, shape_name, mask, variant in SMOLVLA_CASES:
+        with tempfile.TemporaryDirectory() as d:
+            shape = getattr(synth, shape_name)
+            synth.write_smolvla_checkpoint(d, shape, seed=0)
+            digests["smolvla_" + cfg] = dir_digest(d) + dir_digest(os.path.join(d, "tok"))[:16]
+            code = ("import sys,numpy as np; sys.path.insert(0, %r); sys.path.insert(0, %r); from oracle import oracle; "
+                    "from vla_simd_b200 import synth; import make_golden as mg; r = oracle.reference(); "
+                    "sh = synth.%s; f, ins, st, nz, seed, pv, wt, g = mg.smolvla_query(sh, %r); "
+                    "np.save(%r, r.smolvla_predict(%r, f, ins, st, nz, seed, pv, wt, g))") % (
+                        ROOT, HERE, shape_name, variant, os.path.join(HERE, smolvla_fixture_name(cfg, mask, variant)),
+                        d)
+            env = dict(os.environ, SMOLVLA_INT8=str(mask), OMP_NUM_THREADS="1")
+            subprocess.run([sys.executable, "-c", code], check=True, env=env)
+    ref = oracle.reference()
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_smolvla_checkpoint(d, synth.SMOLVLA_SMALL, seed=0)
+        texts = T5_TEXTS + ["pick up the cube and place it in the bowl 3 times", "it's   done\n\n", "x1y22z333"]
+        ids = {}
+        for t in texts + [synth.octo_instruction(i) for i in range(20)]:
+            tok, mask, n = ref.smolvla_tokenize(d, t)
+            ids[t] = tok[:n].tolist()
+    with open(os.path.join(HERE, "bpe_ids.json"), "w") as f:
+        json.dump(ids, f, indent=0, sort_keys=True)
+
+
 def main():
     ref = oracle.reference()
     if ref is None:
         sys.exit("oracle/_ref/libvla_ref.so missing: make -C oracle ref")
     digests = {}
-    for flag, maker in (("--dp", make_dp), ("--octo", make_octo)):   # one family's fixtures only
+    for flag, maker in (("--dp", make_dp), ("--octo", make_octo), ("--smolvla", make_smolvla)):   # one family only
         if flag in sys.argv:
             path = os.path.join(HERE, "checkpoints.json")
             digests = json.load(open(path))
@@ -201,6 +254,7 @@ def main():
             return
     make_dp(digests)
     make_octo(digests)
+    make_smolvla(digests)
     for cfg, shape, mask in ACT_CASES:
         # the reference reads ACT_INT8 when it loads, so each mask runs in its own process
         with tempfile.TemporaryDirectory() as d:

@@ -1,0 +1,49 @@
+"""The host byte-level BPE tokenizer SmolVLA's handles use (vla_bpe_tokenize)
+against the reference's Tokenizer: the ids committed in
+tests/golden/bpe_ids.json (made by the reference's vla_smolvla_tokenize, which
+appends a newline and keeps the last tok_maxlen ids) and, when the reference
+build is present, random strings compared live. No GPU needed."""
+import json
+import os
+
+import numpy as np
+
+from vla_simd_b200 import bpe_tokenize, synth
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _files(tmp_path):
+    synth.smolvla_tokenizer_files(str(tmp_path / "tok"))
+    voc = (tmp_path / "tok" / "vocab.txt").read_text(encoding="utf-8")
+    mer = (tmp_path / "tok" / "merges.txt").read_text(encoding="utf-8")
+    return voc, mer
+
+
+def _as_handle(voc, mer, text, n):
+    s = text
+    while s.endswith("\n"):
+        s = s[:-1]
+    ids = bpe_tokenize(voc, mer, s + "\n")
+    return ids[-n:] if len(ids) > n else ids
+
+
+def test_bpe_matches_golden_ids(tmp_path):
+    voc, mer = _files(tmp_path)
+    ids = json.load(open(os.path.join(GOLDEN, "bpe_ids.json"), encoding="utf-8"))
+    assert len(ids) > 20
+    for s, want in ids.items():
+        assert _as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen).tolist() == want, repr(s)
+
+
+def test_bpe_matches_reference_live(tmp_path, reference):
+    d = synth.write_smolvla_checkpoint(str(tmp_path / "smol"), synth.SMOLVLA_SMALL, seed=0)
+    voc = open(os.path.join(d, "tok", "vocab.txt"), encoding="utf-8").read()
+    mer = open(os.path.join(d, "tok", "merges.txt"), encoding="utf-8").read()
+    rng = np.random.default_rng(7)
+    alphabet = list("abcdefghijklmnopqrstuvwxyz ABC.,!?'-\t\n0123456789") + [
+        "é", "…", "½", "ａ", "日", "\x01", "  ", "'s", "'ll", "٣", "²", " "]
+    for _ in range(120):
+        s = "".join(rng.choice(alphabet, size=int(rng.integers(0, 40))))
+        ids, mask, n = reference.smolvla_tokenize(d, s)
+        assert np.array_equal(_as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen), ids[:n]), repr(s)

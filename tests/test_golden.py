@@ -49,9 +49,11 @@ def test_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
     assert dir_digest(d) == json.load(open(os.path.join(HERE, "checkpoints.json")))[cfg]
 
 
-@pytest.mark.parametrize("cfg,shape", [("octo_small", synth.OCTO_SMALL), ("octo_base", synth.OCTO_BASELINE)])
+@pytest.mark.parametrize("cfg,shape", [("octo_small", synth.OCTO_SMALL), ("octo_base", synth.OCTO_BASELINE),
+                                       ("smolvla_small", synth.SMOLVLA_SMALL), ("smolvla_base", synth.SMOLVLA_BASELINE)])
 def test_octo_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
-    d = synth.write_octo_checkpoint(str(tmp_path / cfg), shape, seed=0)
+    writer = synth.write_smolvla_checkpoint if cfg.startswith("smolvla") else synth.write_octo_checkpoint
+    d = writer(str(tmp_path / cfg), shape, seed=0)
     want = json.load(open(os.path.join(HERE, "checkpoints.json")))[cfg]
     assert dir_digest(d) + dir_digest(os.path.join(d, "tok"))[:16] == want
 

@@ -9,6 +9,9 @@ it with ctypes and mirrors the reference's Python-side interface:
 * :class:`DiffusionPolicy` - the ``vla_diffusion_*`` ABI: an observation
   history (frames + states) and the sampler's noise in, an action chunk out;
   optionally a batch of independent queries per call.
+* :class:`SmolvlaPolicy` - the ``vla_smolvla_*`` ABI: camera frames, an
+  instruction, the robot state and the flow-matching noise in, an action chunk
+  out (optionally with real-time-chunking guidance, and batches of queries).
 * :class:`OctoPolicy` - the ``vla_octo_*`` ABI: a window of primary / wrist
   frames, a language instruction and the DDPM noise in, an action chunk out;
   optionally a batch of independent queries per call.
@@ -133,6 +136,24 @@ SIGNATURES = {
                                      ctypes.POINTER(ctypes.c_uint64), I32, F32P]),
     "vla_octo_readout": (I64, [VP, F32P, I64]),
     "vla_t5_tokenize": (I32, [ctypes.c_char_p, ctypes.c_char_p, I32, ctypes.POINTER(ctypes.c_int32)]),
+    "vla_smolvla_load": (VP, [ctypes.c_char_p, ctypes.c_char_p]),
+    "vla_smolvla_load_batch": (VP, [ctypes.c_char_p, ctypes.c_char_p, I32]),
+    "vla_smolvla_free": (None, [VP]),
+    "vla_smolvla_chunk": (I32, [VP]),
+    "vla_smolvla_action_dim": (I32, [VP]),
+    "vla_smolvla_state_dim": (I32, [VP]),
+    "vla_smolvla_n_views": (I32, [VP]),
+    "vla_smolvla_img_size": (I32, [VP]),
+    "vla_smolvla_tok_maxlen": (I32, [VP]),
+    "vla_smolvla_int8_layers": (I32, [VP]),
+    "vla_smolvla_kernels_per_step": (I32, [VP]),
+    "vla_smolvla_tokenize": (I32, [VP, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+    "vla_smolvla_predict": (I32, [VP, U8P, I32, I32, I32, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), I32, F32P, F32P, ctypes.c_uint64, F32P]),
+    "vla_smolvla_predict_rtc": (I32, [VP, U8P, I32, I32, I32, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), I32, F32P, F32P, ctypes.c_uint64, F32P,
+                                      F32P, I32, F32P, ctypes.c_float]),
+    "vla_smolvla_predict_batch": (I32, [VP, I32, U8P, I32, I32, I32, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), I32, F32P, F32P,
+                                        ctypes.POINTER(ctypes.c_uint64), F32P, F32P, I32, F32P, ctypes.c_float]),
+    "vla_bpe_tokenize": (I32, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32), I32]),
     "vla_octo_device_buffers": (I32, [VP, VP, VP, VP, VP, VP, VP]),
     "vla_octo_set_instruction": (I32, [VP, I32, ctypes.c_char_p]),
     "vla_octo_enqueue": (I32, [VP, I32, I32, I32, VP, I32]),
@@ -232,6 +253,101 @@ def t5_tokenize(vocab_text: str, text: str, max_len: int = 16) -> np.ndarray:
                                ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
     check(rc, "vla_t5_tokenize")
     return ids
+
+
+def bpe_tokenize(vocab_text: str, merges_text: str, text: str) -> np.ndarray:
+    """Token ids of `text` under a byte-level BPE vocab.txt / merges.txt (the
+    tokenizer SmolVLA's handles use; host code, no GPU needed)."""
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    n = lib().vla_bpe_tokenize(vocab_text.encode(), merges_text.encode(), text.encode(), None, 0)
+    check(min(int(n), 0), "vla_bpe_tokenize")
+    ids = np.zeros(max(int(n), 1), np.int32)
+    lib().vla_bpe_tokenize(vocab_text.encode(), merges_text.encode(), text.encode(), ids.ctypes.data_as(i32p),
+                           ids.size)
+    return ids[:int(n)]
+
+
+class SmolvlaPolicy:
+    """ctypes binding of the SmolVLA C ABI (include/vla_simd.h, the reference's
+    vla_smolvla_* at src/models/smolvla/smolvla_capi.cpp:66-180).
+
+    frames [n_views, h, w, 3] uint8 at the camera's resolution, an instruction
+    string (tokenized by the handle), raw state [state_dim], and noise [chunk,
+    32] or a seed -> actions [chunk, action_dim]; optional real-time-chunking
+    guidance (prev [n_prev, action_dim], weights [chunk], max_guidance). With
+    max_batch > 1, predict_batch takes the arrays with a leading batch axis.
+    """
+
+    def __init__(self, model_dir: str, tok_dir: str | None = None, max_batch: int = 1):
+        self.lib = lib()
+        tok_dir = tok_dir or os.path.join(model_dir, "tok")
+        self.h = (self.lib.vla_smolvla_load(model_dir.encode(), tok_dir.encode()) if max_batch == 1
+                  else self.lib.vla_smolvla_load_batch(model_dir.encode(), tok_dir.encode(), int(max_batch)))
+        if not self.h:
+            raise RuntimeError(f"vla_smolvla_load failed for {model_dir}")
+        self.max_batch = int(max_batch)
+        for name in ("chunk", "action_dim", "state_dim", "n_views", "img_size", "tok_maxlen"):
+            setattr(self, name, int(getattr(self.lib, f"vla_smolvla_{name}")(self.h)))
+
+    def tokenize(self, text: str):
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        ids = np.zeros(self.tok_maxlen, np.int32)
+        mask = np.zeros(self.tok_maxlen, np.int32)
+        n = self.lib.vla_smolvla_tokenize(self.h, text.encode(), ids.ctypes.data_as(i32p), mask.ctypes.data_as(i32p))
+        check(min(int(n), 0), "vla_smolvla_tokenize")
+        return ids, mask
+
+    def predict(self, frames, instruction: str, state, noise=None, seed: int = 0, prev=None, weights=None,
+                max_guidance: float = 0.0) -> np.ndarray:
+        return self.predict_batch(np.asarray(frames)[None], [instruction], np.asarray(state)[None],
+                                  None if noise is None else np.asarray(noise)[None], [seed],
+                                  None if prev is None else np.asarray(prev)[None],
+                                  None if weights is None else np.asarray(weights)[None], max_guidance)[0]
+
+    def predict_batch(self, frames, instructions, state, noise=None, seeds=None, prev=None, weights=None,
+                      max_guidance: float = 0.0) -> np.ndarray:
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        frames = np.ascontiguousarray(frames, np.uint8)
+        b = frames.shape[0]
+        if frames.ndim != 5 or frames.shape[1] != self.n_views or frames.shape[4] != 3:
+            raise ValueError(f"frames {frames.shape}")
+        toks = [self.tokenize(t) for t in instructions]
+        ids = np.ascontiguousarray(np.stack([t[0] for t in toks]))
+        mask = np.ascontiguousarray(np.stack([t[1] for t in toks]))
+        state = np.ascontiguousarray(state, np.float32).reshape(b, self.state_dim)
+        nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+        sd = (ctypes.c_uint64 * b)(*[int(v) for v in (seeds if seeds is not None else range(b))])
+        pv = None if prev is None else np.ascontiguousarray(prev, np.float32)
+        wt = None if weights is None else np.ascontiguousarray(weights, np.float32)
+        n_prev = 0 if pv is None else pv.shape[1]
+        out = np.empty((b, self.chunk, self.action_dim), np.float32)
+        p = lambda a, t: None if a is None else a.ctypes.data_as(t)
+        rc = self.lib.vla_smolvla_predict_batch(self.h, b, frames.ctypes.data_as(U8P), self.n_views, frames.shape[2],
+                                                frames.shape[3], ids.ctypes.data_as(i32p), mask.ctypes.data_as(i32p),
+                                                self.tok_maxlen, state.ctypes.data_as(F32P), p(nz, F32P), sd,
+                                                out.ctypes.data_as(F32P), p(pv, F32P), n_prev, p(wt, F32P),
+                                                float(max_guidance))
+        check(rc, "vla_smolvla_predict_batch")
+        return out
+
+    @property
+    def kernels_per_step(self) -> int:
+        return int(self.lib.vla_smolvla_kernels_per_step(self.h))
+
+    @property
+    def int8_layers(self) -> int:
+        return int(self.lib.vla_smolvla_int8_layers(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.vla_smolvla_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class OctoPolicy:

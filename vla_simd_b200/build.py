@@ -27,7 +27,8 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-
 CXX_FLAGS = ["-std=c++17", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
 
 CUDA_SOURCES = ["kernels.cu", "no_alloc.cu"]
-CXX_SOURCES = ["act_policy.cpp", "conv_exec.cpp", "dp_policy.cpp", "octo_policy.cpp", "t5_tokenizer.cpp",
+CXX_SOURCES = ["act_policy.cpp", "conv_exec.cpp", "dp_policy.cpp", "octo_policy.cpp", "t5_tokenizer.cpp", "smolvla_policy.cpp",
+               "bpe_tokenizer.cpp",
                "host_quant.cpp", "model_files.cpp", "capi.cpp"]
 
 

@@ -7,6 +7,8 @@
 #include "act_policy.h"
 #include "dp_policy.h"
 #include "octo_policy.h"
+#include "smolvla_policy.h"
+#include "bpe_tokenizer.h"
 #include "t5_tokenizer.h"
 #include "gemm_i8.h"
 #include "host_quant.h"
@@ -17,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -27,6 +30,7 @@
 using vsb::ActPolicy;
 using vsb::DpPolicy;
 using vsb::OctoPolicy;
+using vsb::SmolvlaPolicy;
 
 namespace {
 
@@ -344,6 +348,94 @@ int32_t vla_octo_enqueue(void* h, int32_t batch, int32_t wnd, int32_t wrist, voi
     auto* m = static_cast<OctoPolicy*>(h);
     if (batch < 1 || batch > m->max_batch() || wnd < 1 || wnd > m->config().max_horizon) return VLA_ERR_SHAPE;
     return status_of(m->enqueue(batch, wnd, wrist != 0, as_stream(stream), unnormalize != 0));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+// ------------------------------------------------------------- SmolVLA
+
+void* vla_smolvla_load_batch(const char* model_dir, const char* tok_dir, int32_t max_batch) try {
+    if (!model_dir || !tok_dir || max_batch < 1) return nullptr;
+    auto m = std::make_unique<SmolvlaPolicy>();
+    if (!m->load(model_dir, tok_dir, max_batch)) {
+        std::fprintf(stderr, "vla_smolvla_load: %s\n", m->error().c_str());
+        return nullptr;
+    }
+    return m.release();
+} catch (...) {
+    return nullptr;
+}
+
+void* vla_smolvla_load(const char* model_dir, const char* tok_dir) {
+    return vla_smolvla_load_batch(model_dir, tok_dir, 1);
+}
+
+void vla_smolvla_free(void* h) { delete static_cast<SmolvlaPolicy*>(h); }
+
+int32_t vla_smolvla_chunk(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().chunk : 0; }
+int32_t vla_smolvla_action_dim(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().ad : 0; }
+int32_t vla_smolvla_state_dim(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().sd : 0; }
+int32_t vla_smolvla_n_views(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().n_views : 0; }
+int32_t vla_smolvla_img_size(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().img : 0; }
+int32_t vla_smolvla_tok_maxlen(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->config().tok_maxlen : 0; }
+int32_t vla_smolvla_int8_layers(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->int8_layers() : 0; }
+int32_t vla_smolvla_kernels_per_step(void* h) { return h ? static_cast<SmolvlaPolicy*>(h)->kernels_per_step() : 0; }
+
+int32_t vla_smolvla_tokenize(void* h, const char* text, int32_t* ids, int32_t* mask) try {
+    if (!h || !text || !ids || !mask) return VLA_ERR_ARG;
+    return static_cast<SmolvlaPolicy*>(h)->tokenize(text, ids, mask);
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_smolvla_predict_batch(void* h, int32_t batch, const uint8_t* frames, int32_t n_views, int32_t height,
+                                  int32_t width, const int32_t* lang_tokens, const int32_t* lang_mask, int32_t n_lang,
+                                  const float* state, const float* noise, const uint64_t* seeds, float* actions,
+                                  const float* prev, int32_t n_prev, const float* weights, float max_guidance) try {
+    if (!h || !frames || !lang_tokens || !lang_mask || !state || !actions) return VLA_ERR_ARG;
+    if (height <= 0 || width <= 0 || n_lang < 0 || n_prev < 0) return VLA_ERR_ARG;
+    if (!noise && !seeds) return VLA_ERR_ARG;
+    if (!prev) n_prev = 0;
+    if (n_prev > 0 && (!weights || !(std::isfinite(max_guidance) && max_guidance > 0))) return VLA_ERR_ARG;
+    auto* m = static_cast<SmolvlaPolicy*>(h);
+    const vsb::SmolvlaConfigDev& c = m->config();
+    if (batch < 1 || batch > m->max_batch() || n_views != c.n_views || n_prev > c.chunk) return VLA_ERR_SHAPE;
+    if (n_lang != c.tok_maxlen) return VLA_ERR_SHAPE;
+    for (int64_t i = 0; n_prev > 0 && i < (int64_t)batch * c.chunk; i++)
+        if (!std::isfinite(weights[i])) return VLA_ERR_ARG;
+    for (int64_t i = 0; i < (int64_t)batch * n_prev * c.ad; i++)
+        if (!std::isfinite(prev[i])) return VLA_ERR_ARG;
+    for (int64_t i = 0; i < (int64_t)batch * n_lang; i++)   // a token past the vocab (smolvla_model.cpp:157-167)
+        if (lang_tokens[i] < 0 || lang_tokens[i] >= c.vocab) return VLA_ERR_SHAPE;
+    return status_of(m->predict(batch, frames, height, width, lang_tokens, lang_mask, n_lang, state, noise, seeds,
+                                prev, n_prev, weights, max_guidance, true, actions));
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_smolvla_predict_rtc(void* h, const uint8_t* frames, int32_t n_views, int32_t height, int32_t width,
+                                const int32_t* lang_tokens, const int32_t* lang_mask, int32_t n_lang,
+                                const float* state, const float* noise, uint64_t seed, float* actions,
+                                const float* prev, int32_t n_prev, const float* weights, float max_guidance) {
+    return vla_smolvla_predict_batch(h, 1, frames, n_views, height, width, lang_tokens, lang_mask, n_lang, state,
+                                     noise, &seed, actions, prev, n_prev, weights, max_guidance);
+}
+
+int32_t vla_smolvla_predict(void* h, const uint8_t* frames, int32_t n_views, int32_t height, int32_t width,
+                            const int32_t* lang_tokens, const int32_t* lang_mask, int32_t n_lang, const float* state,
+                            const float* noise, uint64_t seed, float* actions) {
+    return vla_smolvla_predict_rtc(h, frames, n_views, height, width, lang_tokens, lang_mask, n_lang, state, noise,
+                                   seed, actions, nullptr, 0, nullptr, 0.0f);
+}
+
+int32_t vla_bpe_tokenize(const char* vocab_text, const char* merges_text, const char* text, int32_t* ids,
+                         int32_t cap) try {
+    if (!vocab_text || !merges_text || !text || cap < 0 || (!ids && cap > 0)) return VLA_ERR_ARG;
+    vsb::BpeTokenizer tok;
+    if (!tok.load_text(vocab_text, merges_text)) return VLA_ERR_ARG;
+    const std::vector<int> v = tok.encode(text);
+    for (int32_t i = 0; i < cap && i < (int32_t)v.size(); ++i) ids[i] = v[static_cast<size_t>(i)];
+    return static_cast<int32_t>(v.size());
 } catch (...) {
     return VLA_ERR_EXCEPTION;
 }

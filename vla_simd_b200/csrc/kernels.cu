@@ -8,3 +8,4 @@
 #include "lm_ops.cu"
 #include "dp.cu"
 #include "octo.cu"
+#include "smolvla.cu"

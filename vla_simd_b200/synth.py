@@ -20,6 +20,7 @@ numpy's PCG64 stream makes the files identical on every machine for a seed.
 """
 from __future__ import annotations
 
+import collections
 import dataclasses
 import os
 
@@ -564,6 +565,227 @@ def octo_inputs(shape: OctoShape = OCTO_BASELINE, seed: int = 1, batch: int = 0,
     z = rng.standard_normal(lead + (s.steps, s.flat), dtype=np.float32)
     instr = [octo_instruction(seed * 131 + b) for b in range(batch)] if batch else octo_instruction(seed * 131)
     return primary, wrist, tmask, instr, noise, z
+
+
+# ---------------------------------------------------------------------------
+# SmolVLA (tools/convert_hf_safetensors.py's file set; random init, bf16 towers)
+
+@dataclasses.dataclass(frozen=True)
+class SmolvlaShape:
+    vit_hidden: int = 768
+    vit_heads: int = 12
+    vit_inter: int = 3072
+    vit_layers: int = 12
+    patch: int = 16
+    img: int = 512
+    scale_factor: int = 4
+    hidden: int = 960          # LM width (= the connector's output)
+    n_q: int = 15
+    n_kv: int = 5
+    ffn: int = 2560
+    vlm_layers: int = 16
+    expert_h: int = 720
+    expert_ffn: int = 1920
+    expert_layers: int = 16
+    self_attn_every_n: int = 2
+    chunk: int = 50
+    num_steps: int = 10
+    max_action_dim: int = 32
+    max_state_dim: int = 32
+    state_dim: int = 6
+    action_dim: int = 6
+    n_views: int = 2
+    tok_maxlen: int = 48
+    frame_h: int = 480         # the native camera frames the inputs are drawn at
+    frame_w: int = 640
+
+    @property
+    def n_patches(self) -> int:
+        return (self.img // self.patch) ** 2
+
+    @property
+    def n_img_tok(self) -> int:
+        return self.n_patches // (self.scale_factor ** 2)
+
+
+# SmolVLA-shaped (SigLIP 12 layers d768 at 512 px -> 64 tokens
+# per view after the pixel shuffle, 2 views; SmolLM2 16 layers h960, 15 / 5
+# heads of 64, FFN 2560; 48 prompt tokens + state; expert 16 layers h720; 10
+# Euler steps; 50 x 6 chunk).
+SMOLVLA_BASELINE = SmolvlaShape()
+# reduced SmolVLA for fast tests (same code paths; every int8-eligible width a multiple of 16)
+SMOLVLA_SMALL = SmolvlaShape(vit_hidden=128, vit_heads=2, vit_inter=256, vit_layers=2, img=128, scale_factor=2,
+                             hidden=128, n_q=2, n_kv=1, ffn=256, vlm_layers=3, expert_h=96, expert_ffn=192,
+                             expert_layers=3, chunk=10, num_steps=4, max_action_dim=8, max_state_dim=8,
+                             state_dim=5, action_dim=4, tok_maxlen=12, frame_h=96, frame_w=120)
+
+
+def _gpt2_byte_chars():
+    """The byte-level BPE alphabet: printable Latin-1 bytes map to themselves,
+    the other 68 bytes to code points 256.. in byte order."""
+    keep = list(range(33, 127)) + list(range(161, 173)) + list(range(174, 256))
+    table, extra = {}, 0
+    for b in range(256):
+        if b in keep:
+            table[b] = chr(b)
+        else:
+            table[b] = chr(256 + extra)
+            extra += 1
+    return table
+
+
+def smolvla_tokenizer_files(out_dir: str, n_merges: int = 120, seed: int = 5):
+    """A synthetic byte-level BPE tokenizer (vocab.txt "id<TAB>token", merges.txt
+    "a b") learned on the synthetic instruction corpus; returns the vocab size."""
+    bc = _gpt2_byte_chars()
+    corpus = [octo_instruction(seed * 1000 + i) for i in range(200)]
+    words = collections.Counter()
+    for line in corpus:
+        for i, w in enumerate(line.split(" ")):
+            words[tuple(bc[b] for b in ((" " if i else "") + w).encode())] += 1
+    merges = []
+    for _ in range(n_merges):
+        pairs = collections.Counter()
+        for w, c in words.items():
+            for a, b in zip(w, w[1:]):
+                pairs[(a, b)] += c
+        if not pairs:
+            break
+        best = max(sorted(pairs), key=lambda p: pairs[p])
+        merges.append(best)
+        new = collections.Counter()
+        for w, c in words.items():
+            out, i = [], 0
+            while i < len(w):
+                if i + 1 < len(w) and (w[i], w[i + 1]) == best:
+                    out.append(w[i] + w[i + 1])
+                    i += 2
+                else:
+                    out.append(w[i])
+                    i += 1
+            new[tuple(out)] += c
+        words = new
+    vocab = ["<|endoftext|>", "<|im_start|>", "<|im_end|>"] + [bc[b] for b in range(256)] + [a + b for a, b in merges]
+    os.makedirs(out_dir, exist_ok=True)
+    with open(os.path.join(out_dir, "vocab.txt"), "w", encoding="utf-8") as f:
+        for i, t in enumerate(vocab):
+            f.write(f"{i}\t{t}\n")
+    with open(os.path.join(out_dir, "merges.txt"), "w", encoding="utf-8") as f:
+        for a, b in merges:
+            f.write(f"{a} {b}\n")
+    return len(vocab)
+
+
+def _bf16(a):
+    """Round fp32 to bf16 (nearest even), as uint16."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def write_smolvla_checkpoint(out_dir: str, shape: SmolvlaShape = SMOLVLA_BASELINE, seed: int = 0) -> str:
+    """Write a random-init SmolVLA checkpoint directory (tokenizer in out_dir/tok); returns out_dir."""
+    os.makedirs(out_dir, exist_ok=True)
+    rng = np.random.default_rng(seed)
+    s = shape
+
+    def normal(shape_, std):
+        return (rng.standard_normal(shape_, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+    def norm_w(c):
+        return (1.0 + normal((c,), 0.05)).astype(np.float32)
+
+    vocab = smolvla_tokenizer_files(os.path.join(out_dir, "tok"))
+
+    # vision: fp32 region, then the bf16 region
+    H, I, P = s.vit_hidden, s.vit_inter, 3 * s.patch * s.patch
+    SD = H * s.scale_factor ** 2
+    f32 = [normal((H,), 0.02), normal((s.n_patches, H), 0.5)]
+    for _ in range(s.vit_layers):
+        f32 += [norm_w(H), normal((H,), 0.02)] + [normal((H,), 0.02) for _ in range(4)]
+        f32 += [norm_w(H), normal((H,), 0.02), normal((I,), 0.02), normal((H,), 0.02)]
+    f32 += [norm_w(H), normal((H,), 0.02)]
+    w = [normal((H, P), 1.0 / np.sqrt(P))]
+    for _ in range(s.vit_layers):
+        w += [normal((H, H), 1.0 / np.sqrt(H)) for _ in range(4)]
+        w += [normal((I, H), 1.0 / np.sqrt(H)), normal((H, I), 0.5 / np.sqrt(I))]
+    w += [normal((s.hidden, SD), 1.0 / np.sqrt(SD))]
+    with open(os.path.join(out_dir, "vit.bin"), "wb") as f:
+        np.concatenate([a.reshape(-1) for a in f32]).astype(np.float32).tofile(f)
+        _bf16(np.concatenate([a.reshape(-1) for a in w])).tofile(f)
+    with open(os.path.join(out_dir, "vit.meta"), "w") as f:
+        f.write(f"hidden {H}\nn_heads {s.vit_heads}\nhead_dim {H // s.vit_heads}\ninter {I}\n"
+                f"n_layers {s.vit_layers}\npatch {s.patch}\nimg {s.img}\nn_patches {s.n_patches}\n"
+                f"ln_eps 1e-06\nscale_factor {s.scale_factor}\nmm_out {s.hidden}\nn_img_tok {s.n_img_tok}\n")
+
+    # VLM text tower: per-layer norms + the output norm, then bf16 q k v o gate up down
+    D, QF, KV, F = s.hidden, s.n_q * 64, s.n_kv * 64, s.ffn
+    f32 = []
+    for _ in range(s.vlm_layers):
+        f32 += [norm_w(D), norm_w(D)]
+    f32 += [norm_w(D)]
+    w = []
+    for _ in range(s.vlm_layers):
+        w += [normal((QF, D), 1.0 / np.sqrt(D)), normal((KV, D), 1.0 / np.sqrt(D)), normal((KV, D), 1.0 / np.sqrt(D)),
+              normal((D, QF), 0.5 / np.sqrt(QF)), normal((F, D), 1.0 / np.sqrt(D)), normal((F, D), 1.0 / np.sqrt(D)),
+              normal((D, F), 0.5 / np.sqrt(F))]
+    with open(os.path.join(out_dir, "vlm.bin"), "wb") as f:
+        np.concatenate([a.reshape(-1) for a in f32]).astype(np.float32).tofile(f)
+        _bf16(np.concatenate([a.reshape(-1) for a in w])).tofile(f)
+    with open(os.path.join(out_dir, "vlm.meta"), "w") as f:
+        f.write(f"hidden {D}\nn_q {s.n_q}\nn_kv {s.n_kv}\nhead_dim 64\nffn {F}\neps 1e-05\nrope_base 10000\n"
+                f"n_layers {s.vlm_layers}\n")
+
+    # action expert (fp32): per layer ln_in q k v o ln_post gate up down; out norm; flow projections
+    EH, EF, MAD = s.expert_h, s.expert_ffn, s.max_action_dim
+    parts = []
+    for L in range(s.expert_layers):
+        self_attn = s.self_attn_every_n > 0 and L % s.self_attn_every_n == 0
+        kk = EH if self_attn else KV
+        parts += [norm_w(EH), normal((QF, EH), 1.0 / np.sqrt(EH)), normal((KV, kk), 1.0 / np.sqrt(kk)),
+                  normal((KV, kk), 1.0 / np.sqrt(kk)), normal((EH, QF), 0.5 / np.sqrt(QF)), norm_w(EH),
+                  normal((EF, EH), 1.0 / np.sqrt(EH)), normal((EF, EH), 1.0 / np.sqrt(EH)),
+                  normal((EH, EF), 0.5 / np.sqrt(EF))]
+    parts += [norm_w(EH), normal((EH, MAD), 1.0 / np.sqrt(MAD)), normal((EH,), 0.02),
+              normal((EH, 2 * EH), 1.0 / np.sqrt(2 * EH)), normal((EH,), 0.02), normal((EH, EH), 1.0 / np.sqrt(EH)),
+              normal((EH,), 0.02), normal((MAD, EH), 0.3 / np.sqrt(EH)), normal((MAD,), 0.02)]
+    np.concatenate([a.reshape(-1) for a in parts]).astype(np.float32).tofile(os.path.join(out_dir, "aex.bin"))
+    with open(os.path.join(out_dir, "aex.meta"), "w") as f:
+        f.write(f"expert_h {EH}\nexpert_ffn {EF}\nn_q {s.n_q}\nn_kv {s.n_kv}\nhead_dim 64\neps 1e-05\n"
+                f"rope_base 10000\nn_layers {s.expert_layers}\nself_attn_every_n {s.self_attn_every_n}\n"
+                f"chunk {s.chunk}\nnum_steps {s.num_steps}\nmax_action_dim {MAD}\nmin_period 0.004\n"
+                f"max_period 4.0\n")
+
+    # token embeddings (bf16), state projection, stats
+    _bf16(normal((vocab, D), 1.0 / np.sqrt(D))).tofile(os.path.join(out_dir, "emb.bin"))
+    np.concatenate([normal((D, s.max_state_dim), 1.0 / np.sqrt(s.max_state_dim)).reshape(-1),
+                    normal((D,), 0.02)]).tofile(os.path.join(out_dir, "heads.bin"))
+    with open(os.path.join(out_dir, "heads.meta"), "w") as f:
+        f.write(f"vocab {vocab}\nhidden {D}\nmax_state_dim {s.max_state_dim}\nreal_state_dim {s.state_dim}\n"
+                f"real_action_dim {s.action_dim}\nn_views {s.n_views}\n")
+    normal((s.state_dim,), 1.0).tofile(os.path.join(out_dir, "stats_state_mean.bin"))
+    rng.uniform(0.5, 2.0, s.state_dim).astype(np.float32).tofile(os.path.join(out_dir, "stats_state_std.bin"))
+    normal((s.action_dim,), 1.0).tofile(os.path.join(out_dir, "stats_action_mean.bin"))
+    rng.uniform(0.5, 2.0, s.action_dim).astype(np.float32).tofile(os.path.join(out_dir, "stats_action_std.bin"))
+    with open(os.path.join(out_dir, "config.txt"), "w") as f:
+        f.write(f"instruction {octo_instruction(1)}\ntokenizer_max_length {s.tok_maxlen}\npad_token_id 2\n"
+                f"chunk {s.chunk}\nnum_steps {s.num_steps}\nn_views {s.n_views}\n")
+    return out_dir
+
+
+def smolvla_inputs(shape: SmolvlaShape = SMOLVLA_BASELINE, seed: int = 1, batch: int = 0):
+    """Seeded SmolVLA query: frames [n_views, frame_h, frame_w, 3] uint8, an
+    instruction string, raw state [state_dim] ~ N(0, 1), noise [chunk,
+    max_action_dim] ~ N(0, 1). With batch > 0 the arrays gain a leading batch
+    axis and the instruction becomes a list."""
+    rng = np.random.default_rng(seed)
+    s = shape
+    lead = (batch,) if batch else ()
+    frames = rng.integers(0, 256, size=lead + (s.n_views, s.frame_h, s.frame_w, 3), dtype=np.uint8)
+    state = rng.standard_normal(lead + (s.state_dim,), dtype=np.float32)
+    noise = rng.standard_normal(lead + (s.chunk, s.max_action_dim), dtype=np.float32)
+    instr = [octo_instruction(seed * 17 + b) for b in range(batch)] if batch else octo_instruction(seed * 17)
+    return frames, instr, state, noise
 
 
 # ---------------------------------------------------------------------------
