@@ -789,6 +789,137 @@ def run_octo(args):
     }), flush=True)
 
 
+SMOLVLA_MASK = 63   # SMOLVLA_INT8: vision, text tower and action expert GEMMs in W8A8
+
+_SMOLVLA_CPU_CHILD = r"""
+import ctypes, json, os, sys, time
+sys.path.insert(0, %(root)r)
+import numpy as np
+from vla_simd_b200 import synth
+budget, max_steps = %(budget)f, %(max_steps)d
+sh = synth.SMOLVLA_BASELINE
+f, ins, st, nz = synth.smolvla_inputs(sh, seed=1)
+from oracle import oracle
+r = oracle.reference()
+if r is None:
+    print(json.dumps({"unavailable": "oracle/_ref/libvla_ref.so (the reference's own build) not present"}))
+    sys.exit(0)
+l = r._smolvla_bind()
+h = l.vla_smolvla_load(%(ckpt)r.encode(), (%(ckpt)r + "/tok").encode())
+n = l.vla_smolvla_tok_maxlen(h)
+ids, mask = np.zeros(n, np.int32), np.zeros(n, np.int32)
+l.vla_smolvla_tokenize(h, ins.encode(), ids.ctypes.data_as(ctypes.c_void_p), mask.ctypes.data_as(ctypes.c_void_p))
+out = np.zeros((sh.chunk, sh.action_dim), np.float32)
+P = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+def query():
+    return l.vla_smolvla_predict_rtc(h, P(f), sh.n_views, sh.frame_h, sh.frame_w, P(ids), P(mask), n, P(st), P(nz),
+                                     0, P(out), None, 0, None, 0.0)
+query()
+times = []
+t_end = time.perf_counter() + budget
+while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+    t0 = time.perf_counter()
+    rc = query()
+    times.append(time.perf_counter() - t0)
+    assert rc == 0
+l.vla_smolvla_free(h)
+print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * float(np.median(times))}))
+"""
+
+
+def run_smolvla(args):
+    """SmolVLA-shaped policy: one query batch per step (2 views of 480x640
+    camera frames resized and padded to 512, a 48-token prompt, state, 10
+    flow-matching steps); replicas per GPU. Device-timed value and C-ABI e2e."""
+    import torch
+    rank, local_rank, world = _env_rank()
+    os.environ["VLA_CUDA_DEVICE"] = str(local_rank)
+    os.environ["SMOLVLA_INT8"] = str(SMOLVLA_MASK)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from vla_simd_b200 import SmolvlaPolicy, synth
+    B = args.batch
+    sh = synth.SMOLVLA_BASELINE
+    ckpt_root = tempfile.mkdtemp(prefix="vla_smolvla_")
+    ckpt = synth.write_smolvla_checkpoint(os.path.join(ckpt_root, "smolvla"), sh, seed=0)
+    pol = SmolvlaPolicy(ckpt, max_batch=B)
+    f, ins, st, nz = synth.smolvla_inputs(sh, seed=1 + rank, batch=B)
+    for _ in range(max(args.warmup, 3)):
+        pol.predict_batch(f, ins, st, nz)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n = max(args.steps, 5)
+    step_s = []
+    with ClockSampler(local_rank) as clk:
+        for _ in range(n):
+            t0 = time.perf_counter()
+            pol.predict_batch(f, ins, st, nz)
+            step_s.append(time.perf_counter() - t0)
+    total = max_over_ranks(sum(step_s), dist, dev)
+    value = job_value(n * B, world, total)
+    kernels = pol.kernels_per_step
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = time_reference_generic(_SMOLVLA_CPU_CHILD, ckpt, "SMOLVLA_INT8", SMOLVLA_MASK, args.cpu_budget, 10)
+    pol.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu_baseline = None
+    if cpu and "unavailable" not in cpu:
+        cpu_baseline = {"value": round(cpu["chunks_per_s"], 3), "unit": "chunks/s", "cores": cpu["cores"],
+                        "kind": "reference", "p50_ms": round(cpu["p50_ms"], 2),
+                        "sample": f"{cpu['steps']} single queries (same checkpoint and inputs, SMOLVLA_INT8="
+                                  f"{SMOLVLA_MASK}) of the reference's own vla_smolvla_predict_rtc, "
+                                  f"OMP_NUM_THREADS={cpu['cores']}"}
+    elif cpu:
+        cpu_baseline = {"unavailable": cpu["unavailable"]}
+    print(json.dumps({
+        "metric": "SmolVLA throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 * total / n, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
+        "data": "synthetic (seeded random-init SmolVLA-shaped weights, uniform uint8 frames, N(0,1) state and noise, "
+                "a synthetic BPE vocabulary)",
+        "config": {"workload": "SmolVLA-shaped: SigLIP 12 layers d768 at 512 px -> 64 tokens per view x 2 views "
+                               "(480x640 frames resized with pad), SmolLM2 16 layers h960 15/5 heads, 48 prompt "
+                               "tokens + state, expert 16 layers h720, 10 flow-matching steps, 50 x 6 chunk",
+                   "batch_per_gpu": B, "int8_mask": SMOLVLA_MASK,
+                   "parallelism": f"replicas x{world} (no collective)",
+                   "timing": "wall clock per vla_smolvla_predict_batch call (host frames in, host actions out: "
+                             "this line's value is already end to end)"},
+        "latency_ms": {"p50": round(1e3 * statistics.median(step_s), 4)},
+        "cpu_baseline": cpu_baseline,
+        "e2e": {"value": round(value, 3), "unit": "chunks/s", "h2d_bytes_per_step": f.nbytes + st.nbytes + nz.nbytes,
+                "d2h_bytes_per_step": B * sh.chunk * sh.action_dim * 4},
+        "gpu_launches": kernels * n, "kernels_per_step": kernels, "clocks": clk.summary(),
+    }), flush=True)
+
+
+def time_reference_generic(child: str, ckpt: str, env_key: str, mask: int, budget_s: float, max_steps: int):
+    """A reference policy's own query (oracle/_ref) timed in a fresh process on all host cores."""
+    cores = cpu_cores()
+    env = dict(os.environ, OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close", CUDA_VISIBLE_DEVICES="")
+    env[env_key] = str(mask)
+    code = child % {"root": ROOT, "budget": budget_s, "max_steps": max_steps, "ckpt": ckpt}
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        return {"unavailable": f"reference CPU run failed: {r.stderr.strip().splitlines()[-1:]}"}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    if "unavailable" in d:
+        return d
+    d["cores"] = cores
+    d["chunks_per_s"] = d["steps"] / d["seconds"]
+    return d
+
+
 def run_reference(args):
     """Reference arm: the reference's own CPU implementation on this host (rank 0 only)."""
     rank, _, world = _env_rank()
@@ -828,9 +959,9 @@ def main():
     ap.add_argument("--op", default=None, help="time one op at its ACT shape (attention, gemm_qkv, gemm_w1, "
                                                "gemm_w2, layernorm, quantize, conv_layer1), or gemm_msweep "
                                                "(the FFN GEMM at M = 602 x {1, 8, 32, 128})")
-    ap.add_argument("--model", choices=["act", "dp", "octo"], default="act",
+    ap.add_argument("--model", choices=["act", "dp", "octo", "smolvla"], default="act",
                     help="act: the ACT step (the headline line); dp: Diffusion Policy (BASELINE configs[2]); "
-                         "octo: the Octo-base-shaped policy")
+                         "octo: the Octo-base-shaped policy; smolvla: the SmolVLA-shaped policy")
     ap.add_argument("--batch", type=int, default=1, help="queries per step per GPU (--model dp / octo)")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
@@ -848,6 +979,8 @@ def main():
         run_dp(args)
     elif args.model == "octo" and args.impl != "reference":
         run_octo(args)
+    elif args.model == "smolvla" and args.impl != "reference":
+        run_smolvla(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
