@@ -807,7 +807,7 @@ cudaError_t OctoPolicy::run_stem(const OctoStemDev& s, const uint8_t* img, int F
 // ------------------------------------------------------------ forward
 cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, bool unnormalize) {
     const OctoConfigDev& c = cfg_;
-    const int D = c.d, T = c.total(wnd), F = B * wnd, FL = c.flat();
+    const int D = c.d, T = c.total(wnd), F = B * wnd;
     const int ro = c.n_task + wnd * c.per_step() - 1;   // the last step's readout row (octo_transformer.h:61)
     const long long rows = (long long)B * T;
     VSB_TRY(cudaMemsetAsync(d_slots_, 0, sizeof(unsigned int) * n_slots_, st));
