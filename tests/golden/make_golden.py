@@ -133,7 +133,7 @@ def make_dp(digests):
 OCTO_CASES = [("small", "OCTO_SMALL", 63, ""), ("small", "OCTO_SMALL", 0, ""), ("small", "OCTO_SMALL", 63, "readout"),
               ("small", "OCTO_SMALL", 63, "nowrist"), ("small", "OCTO_SMALL", 63, "pad"),
               ("small", "OCTO_SMALL", 63, "w1"), ("small", "OCTO_SMALL", 63, "seed"),
-              ("small", "OCTO_SMALL", 31, ""), ("base", "OCTO_BASELINE", 63, "")]
+              ("small", "OCTO_SMALL", 31, ""), ("base", "OCTO_BASELINE", 63, ""), ("erf", "OCTO_ERF", 63, "")]
 # tokenizer cases: ids of each string under synth.octo_vocab()
 T5_TEXTS = ["", " ", "pick up the red block", "PICK up \u00b2\u00bd \u2026 \ufb01", "a\tb\nc  d",
             "<extra_id_0> pick<extra_id_0>up", "x" * 40, "h\u00e9llo w\u00f6rld \u2603 \u65e5\u672c",
@@ -190,7 +190,8 @@ def make_octo(digests):
 # "rtc" with real-time-chunking guidance, "seed" the reference's own noise draw
 SMOLVLA_CASES = [("small", "SMOLVLA_SMALL", 63, ""), ("small", "SMOLVLA_SMALL", 0, ""),
                  ("small", "SMOLVLA_SMALL", 63, "rtc"), ("small", "SMOLVLA_SMALL", 63, "seed"),
-                 ("small", "SMOLVLA_SMALL", 59, ""), ("base", "SMOLVLA_BASELINE", 63, "")]
+                 ("small", "SMOLVLA_SMALL", 59, ""), ("base", "SMOLVLA_BASELINE", 63, ""),
+                 ("edge", "SMOLVLA_EDGE", 63, "short"), ("edge", "SMOLVLA_EDGE", 0, "short")]
 
 
 def smolvla_fixture_name(cfg, mask, variant):
@@ -201,6 +202,8 @@ def smolvla_query(shape, variant):
     """The inputs of one SmolVLA fixture case: (frames, instruction, state, noise,
     seed, prev, weights, max_guidance)."""
     frames, ins, state, noise = synth.smolvla_inputs(shape, seed=1)
+    if variant == "short":   # fewer tokens than tok_maxlen: the rest are padding
+        ins = "pick up"
     prev = weights = None
     mg = 0.0
     if variant == "rtc":

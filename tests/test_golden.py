@@ -50,7 +50,8 @@ def test_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
 
 
 @pytest.mark.parametrize("cfg,shape", [("octo_small", synth.OCTO_SMALL), ("octo_base", synth.OCTO_BASELINE),
-                                       ("smolvla_small", synth.SMOLVLA_SMALL), ("smolvla_base", synth.SMOLVLA_BASELINE)])
+                                       ("smolvla_small", synth.SMOLVLA_SMALL), ("smolvla_base", synth.SMOLVLA_BASELINE),
+                                       ("smolvla_edge", synth.SMOLVLA_EDGE), ("octo_erf", synth.OCTO_ERF)])
 def test_octo_checkpoint_writer_matches_fixture_source(tmp_path, cfg, shape):
     writer = synth.write_smolvla_checkpoint if cfg.startswith("smolvla") else synth.write_octo_checkpoint
     d = writer(str(tmp_path / cfg), shape, seed=0)

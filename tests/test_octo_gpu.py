@@ -45,6 +45,17 @@ def test_small_octo_matches_reference(tmp_path, monkeypatch, mask, n_int8):
     pol.close()
 
 
+def test_erf_gelu_octo_matches_reference(tmp_path, monkeypatch):
+    """The torch-converted form (octo.meta gelu_erf 1: exact-erf GELU in every MLP)."""
+    pol = _policy(tmp_path, synth.OCTO_ERF, 63, monkeypatch)
+    assert pol.int8_layers == 38
+    p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_ERF, "")
+    err = np.abs(pol.predict(p, w, tm, ins, n, z) - _want("erf", 63)).max()
+    print(f"Octo erf-GELU max-abs vs reference: {err:.3g}")
+    assert err <= TOL
+    pol.close()
+
+
 def test_small_octo_readout_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.OCTO_SMALL, 63, monkeypatch)
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_SMALL, "")

@@ -44,6 +44,21 @@ def test_small_smolvla_matches_reference(tmp_path, monkeypatch, mask, n_int8, va
     pol.close()
 
 
+@pytest.mark.parametrize("mask,n_int8", [(63, 57), (0, 0)])
+def test_edge_smolvla_matches_reference(tmp_path, monkeypatch, mask, n_int8):
+    """One view from 50x100 frames, a two-token prompt padded to 20 (masked
+    prefix rows and keys), an expert shallower than the text tower with
+    self-attention every third layer, a 7-step chunk and 3 flow steps."""
+    pol = _policy(tmp_path, synth.SMOLVLA_EDGE, mask, monkeypatch)
+    assert pol.int8_layers == n_int8
+    f, ins, st, nz, seed, pv, wt, g = smolvla_query(synth.SMOLVLA_EDGE, "short")
+    got = pol.predict(f, ins, st, nz, seed, pv, wt, g)
+    err = np.abs(got - _want("edge", mask, "short")).max()
+    print(f"SmolVLA edge mask {mask} max-abs vs reference: {err:.3g}")
+    assert err <= TOL
+    pol.close()
+
+
 def test_baseline_smolvla_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.SMOLVLA_BASELINE, 63, monkeypatch)
     assert pol.int8_layers == 298

@@ -407,6 +407,9 @@ OCTO_SMALL = OctoShape(d=128, n_layers=3, heads=2, mlp=256, max_horizon=3, stem_
                        stem_dim=64, gn_groups=4, t5_dim=64, t5_layers=2, t5_heads=2, t5_ff=128, num_blocks=2,
                        hidden=64)
 
+# the torch-converted form: exact-erf GELU in the MLPs (octo.meta gelu_erf 1)
+OCTO_ERF = dataclasses.replace(OCTO_SMALL, gelu_erf=True)
+
 # A synthetic unigram vocabulary: the control pieces, every letter and digit
 # alone and after the word marker, and a few hundred made-up words.
 _SYLLABLES = ["pi", "ck", "up", "the", "red", "blo", "put", "in", "bo", "wl", "dra", "wer", "op", "en", "clo",
@@ -618,6 +621,17 @@ SMOLVLA_SMALL = SmolvlaShape(vit_hidden=128, vit_heads=2, vit_inter=256, vit_lay
                              hidden=128, n_q=2, n_kv=1, ffn=256, vlm_layers=3, expert_h=96, expert_ffn=192,
                              expert_layers=3, chunk=10, num_steps=4, max_action_dim=8, max_state_dim=8,
                              state_dim=5, action_dim=4, tok_maxlen=12, frame_h=96, frame_w=120)
+
+
+# edge cases of the same code paths: one view from small wide frames, a prompt
+# shorter than tok_maxlen (padded tokens masked out of the prefix), an expert
+# shallower than the text tower with self-attention every third layer, a
+# 7-step chunk and 3 flow steps
+SMOLVLA_EDGE = SmolvlaShape(vit_hidden=128, vit_heads=2, vit_inter=256, vit_layers=1, img=64, scale_factor=2,
+                            hidden=128, n_q=2, n_kv=1, ffn=256, vlm_layers=4, expert_h=64, expert_ffn=128,
+                            expert_layers=3, self_attn_every_n=3, chunk=7, num_steps=3, max_action_dim=8,
+                            max_state_dim=8, state_dim=3, action_dim=2, n_views=1, tok_maxlen=20, frame_h=50,
+                            frame_w=100)
 
 
 def _gpt2_byte_chars():
