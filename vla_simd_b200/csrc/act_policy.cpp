@@ -2,6 +2,8 @@
 // buffer planning, and the kernel sequence of one step.
 #include "act_policy.h"
 
+#include "host_util.h"
+
 #include "model_files.h"
 
 #include "f32.h"
@@ -22,44 +24,11 @@ namespace vsb {
 
 namespace {
 
-int env_int(const char* name, int dflt) {
-    const char* e = std::getenv(name);
-    if (!e || !*e) return dflt;
-    char* end = nullptr;
-    const long v = std::strtol(e, &end, 10);
-    return (end && *end == '\0') ? static_cast<int>(v) : dflt;
-}
-
-// TCPU_I8_CLIP semantics (src/hal/common/env.cpp:220-227): (0, 1], default 1.
-float env_clip() {
-    const char* e = std::getenv("TCPU_I8_CLIP");
-    const float f = e ? static_cast<float>(std::atof(e)) : 1.0f;
-    return f > 0.0f && f <= 1.0f ? f : 1.0f;
-}
-
-bool shape_fits(std::initializer_list<int> dims) {
-    long long c = 1;
-    for (int d : dims) {
-        if (d <= 0) return false;
-        c *= d;
-        if (c > INT_MAX) return false;
-    }
-    return true;
-}
-
-// Cursor over a float arena in the converter's order (src/models/arena.h:61-72).
-struct Cursor {
-    const std::vector<float>& d;
-    size_t off = 0;
-    bool ok = true;
-    const float* operator()(size_t n) {
-        if (!ok || n > d.size() - off) { ok = false; return nullptr; }
-        const float* p = d.data() + off;
-        off += n;
-        return p;
-    }
-    bool done() const { return ok && off == d.size(); }
-};
+using host::Cursor;
+using host::env_clip;
+using host::env_int;
+using host::round16;
+using host::shape_fits;
 
 int conv_out(int in, int k, int stride, int pad) {
     const long long num = (long long)in + 2LL * pad - k;
@@ -67,7 +36,6 @@ int conv_out(int in, int k, int stride, int pad) {
     return static_cast<int>(num / stride + 1);
 }
 
-long long round16(long long v) { return (v + 15) & ~15LL; }
 
 #define VSB_TRY(expr)                                  \
     do {                                               \

@@ -3,6 +3,8 @@
 // query batch.
 #include "dp_policy.h"
 
+#include "host_util.h"
+
 #include "model_files.h"
 
 #include "f32.h"
@@ -25,44 +27,11 @@ namespace {
 
 constexpr float kNormEps = 1e-8f;   // src/models/diffusion/diffusion_model.cpp:17
 
-int env_int(const char* name, int dflt) {
-    const char* e = std::getenv(name);
-    if (!e || !*e) return dflt;
-    char* end = nullptr;
-    const long v = std::strtol(e, &end, 10);
-    return (end && *end == '\0') ? static_cast<int>(v) : dflt;
-}
-
-float env_clip() {
-    const char* e = std::getenv("TCPU_I8_CLIP");
-    const float f = e ? static_cast<float>(std::atof(e)) : 1.0f;
-    return f > 0.0f && f <= 1.0f ? f : 1.0f;
-}
-
-bool shape_fits(std::initializer_list<long long> dims) {
-    long long c = 1;
-    for (long long d : dims) {
-        if (d <= 0) return false;
-        c *= d;
-        if (c > INT_MAX) return false;
-    }
-    return true;
-}
-
-struct Cursor {
-    const std::vector<float>& d;
-    size_t off = 0;
-    bool ok = true;
-    const float* operator()(size_t n) {
-        if (!ok || n > d.size() - off) { ok = false; return nullptr; }
-        const float* p = d.data() + off;
-        off += n;
-        return p;
-    }
-    bool done() const { return ok && off == d.size(); }
-};
-
-long long round16(long long v) { return (v + 15) & ~15LL; }
+using host::Cursor;
+using host::env_clip;
+using host::env_int;
+using host::round16;
+using host::shape_fits;
 
 // numpy's linspace as the reference builds the keypoint grid
 // (src/models/diffusion/rgb_encoder.cpp:22-28): start + step*i in double (its

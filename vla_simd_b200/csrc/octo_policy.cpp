@@ -2,6 +2,8 @@
 // buffer planning, the T5 cache and the kernel sequence of one query batch.
 #include "octo_policy.h"
 
+#include "host_util.h"
+
 #include "model_files.h"
 
 #include "dp.h"
@@ -26,72 +28,15 @@ namespace vsb {
 
 namespace {
 
-int env_int(const char* name, int dflt) {
-    const char* e = std::getenv(name);
-    if (!e || !*e) return dflt;
-    char* end = nullptr;
-    const long v = std::strtol(e, &end, 10);
-    return (end && *end == '\0') ? static_cast<int>(v) : dflt;
-}
+using host::Cursor;
+using host::env_clip;
+using host::env_int;
+using host::meta_int;
+using host::numeric_meta;
+using host::round16;
+using host::shape_fits;
 
-float env_clip() {
-    const char* e = std::getenv("TCPU_I8_CLIP");
-    const float f = e ? static_cast<float>(std::atof(e)) : 1.0f;
-    return f > 0.0f && f <= 1.0f ? f : 1.0f;
-}
-
-bool fits(std::initializer_list<long long> dims) {
-    long long c = 1;
-    for (long long d : dims) {
-        if (d <= 0) return false;
-        c *= d;
-        if (c > INT_MAX) return false;
-    }
-    return true;
-}
-
-struct Cursor {
-    const std::vector<float>& d;
-    size_t off = 0;
-    bool ok = true;
-    const float* operator()(size_t n) {
-        if (!ok || n > d.size() - off) { ok = false; return nullptr; }
-        const float* p = d.data() + off;
-        off += n;
-        return p;
-    }
-    bool done() const { return ok && off == d.size(); }
-};
-
-long long round16(long long v) { return (v + 15) & ~15LL; }
-
-// "key value" metadata where every value is a number (octo.meta, t5.meta,
-// head.meta; src/models/octo/octo_transformer.cpp:18-38): integers must be
-// whole and in range (src/models/arena.h:21-25). Unknown keys are skipped.
-bool parse_numeric_meta(const std::string& text, std::map<std::string, double>& kv) {
-    std::istringstream in(text);
-    std::string key;
-    double val;
-    while (in >> key) {
-        if (!(in >> val) || !std::isfinite(val)) return false;
-        kv[key] = val;
-    }
-    return true;
-}
-
-bool meta_int(const std::map<std::string, double>& kv, const char* key, int& out) {
-    const auto it = kv.find(key);
-    if (it == kv.end()) return true;
-    const double v = it->second;
-    if (v < INT_MIN || v > INT_MAX || v != std::trunc(v)) return false;
-    out = static_cast<int>(v);
-    return true;
-}
-
-void meta_float(const std::map<std::string, double>& kv, const char* key, float& out) {
-    const auto it = kv.find(key);
-    if (it != kv.end()) out = static_cast<float>(it->second);
-}
+void meta_float(const std::map<std::string, double>& kv, const char* key, float& out) { host::meta_real(kv, key, out); }
 
 // T5's bidirectional relative-position bucket of rp = key - query (the HF
 // relative_position_bucket: exact buckets below num_buckets/4, log-spaced up
@@ -158,7 +103,7 @@ OctoPolicy::~OctoPolicy() {
 bool OctoPolicy::load_t5(const ModelFiles& files) {
     std::string text;
     std::map<std::string, double> kv;
-    if (!files.read("t5.meta", text) || !parse_numeric_meta(text, kv)) { fail("cannot read t5.meta"); return false; }
+    if (!files.read("t5.meta", text) || !numeric_meta(text, kv)) { fail("cannot read t5.meta"); return false; }
     OctoConfigDev& c = cfg_;
     int d_model = c.t5_dim;
     if (!meta_int(kv, "d_model", d_model) || !meta_int(kv, "n_layers", c.t5_layers) ||
@@ -170,8 +115,8 @@ bool OctoPolicy::load_t5(const ModelFiles& files) {
     }
     meta_float(kv, "eps", c.t5_eps);
     const int D = d_model, FF = c.t5_ff;
-    if (!fits({D, D}) || !fits({D, FF}) || !fits({c.t5_vocab, D}) || !fits({c.t5_heads, c.t5_dkv}) ||
-        c.t5_heads * c.t5_dkv != D || c.t5_layers < 1 || !fits({c.t5_buckets, c.t5_heads}) || c.t5_buckets < 4 ||
+    if (!shape_fits({D, D}) || !shape_fits({D, FF}) || !shape_fits({c.t5_vocab, D}) || !shape_fits({c.t5_heads, c.t5_dkv}) ||
+        c.t5_heads * c.t5_dkv != D || c.t5_layers < 1 || !shape_fits({c.t5_buckets, c.t5_heads}) || c.t5_buckets < 4 ||
         c.t5_buckets % 2 || c.t5_max_dist <= c.t5_buckets / 4 || !std::isfinite(c.t5_eps) || c.t5_eps <= 0) {
         fail("unsupported t5.meta");
         return false;
@@ -242,7 +187,7 @@ bool OctoPolicy::load_stem(const ModelFiles& files, const std::string& name, int
     }
     int cin = in_ch;
     for (int i = 0; i < s.n_layers; ++i) {
-        if (!fits({feat[i], s.k, s.k, cin}) || feat[i] % s.gn_groups) { fail("unsupported " + name + ".meta"); return false; }
+        if (!shape_fits({feat[i], s.k, s.k, cin}) || feat[i] % s.gn_groups) { fail("unsupported " + name + ".meta"); return false; }
         cin = feat[i];
     }
     std::vector<float> data;
@@ -293,7 +238,7 @@ bool OctoPolicy::load_stem(const ModelFiles& files, const std::string& name, int
 bool OctoPolicy::load_transformer(const ModelFiles& files, int mask) {
     std::string text;
     std::map<std::string, double> kv;
-    if (!files.read("octo.meta", text) || !parse_numeric_meta(text, kv)) { fail("cannot read octo.meta"); return false; }
+    if (!files.read("octo.meta", text) || !numeric_meta(text, kv)) { fail("cannot read octo.meta"); return false; }
     OctoConfigDev& c = cfg_;
     int t5_dim = c.t5_dim;
     c.t5_dim = 768;
@@ -309,10 +254,10 @@ bool OctoPolicy::load_transformer(const ModelFiles& files, int mask) {
     meta_float(kv, "ln_eps", c.ln_eps);
     if (kv.count("gelu_erf")) c.gelu_erf = kv["gelu_erf"] != 0;
     const int D = c.d;
-    if (!fits({D, D}) || !fits({c.heads, c.head_dim}) || c.heads * c.head_dim != D || !fits({c.mlp, D}) ||
-        !fits({c.n_task, D}) || !fits({c.t5_dim, D}) || !fits({c.stem_dim, D}) ||
-        !fits({c.max_horizon, c.tok_primary, D}) || !fits({c.max_horizon, c.tok_wrist, D}) ||
-        !fits({c.max_horizon, c.n_readout, D}) || c.n_layers < 1 || !std::isfinite(c.ln_eps) || c.ln_eps <= 0) {
+    if (!shape_fits({D, D}) || !shape_fits({c.heads, c.head_dim}) || c.heads * c.head_dim != D || !shape_fits({c.mlp, D}) ||
+        !shape_fits({c.n_task, D}) || !shape_fits({c.t5_dim, D}) || !shape_fits({c.stem_dim, D}) ||
+        !shape_fits({c.max_horizon, c.tok_primary, D}) || !shape_fits({c.max_horizon, c.tok_wrist, D}) ||
+        !shape_fits({c.max_horizon, c.n_readout, D}) || c.n_layers < 1 || !std::isfinite(c.ln_eps) || c.ln_eps <= 0) {
         fail("unsupported octo.meta");
         return false;
     }
@@ -383,7 +328,7 @@ bool OctoPolicy::load_transformer(const ModelFiles& files, int mask) {
 bool OctoPolicy::load_head(const ModelFiles& files, bool int8) {
     std::string text;
     std::map<std::string, double> kv;
-    if (!files.read("head.meta", text) || !parse_numeric_meta(text, kv)) { fail("cannot read head.meta"); return false; }
+    if (!files.read("head.meta", text) || !numeric_meta(text, kv)) { fail("cannot read head.meta"); return false; }
     OctoConfigDev& c = cfg_;
     int emb = c.d;
     if (!meta_int(kv, "emb", emb) || !meta_int(kv, "action_dim", c.action_dim) ||
@@ -394,9 +339,9 @@ bool OctoPolicy::load_head(const ModelFiles& files, bool int8) {
         return false;
     }
     meta_float(kv, "max_action", c.max_action);
-    if (!fits({c.action_dim, c.horizon}) || !fits({2, c.time_dim, c.time_dim}) || c.time_dim % 2 ||
-        !fits({4, c.hidden, c.hidden}) || emb < 1 || c.num_blocks < 0 ||
-        (long long)c.time_dim + emb + c.flat() > INT_MAX || !fits({c.steps, c.time_dim}) ||
+    if (!shape_fits({c.action_dim, c.horizon}) || !shape_fits({2, c.time_dim, c.time_dim}) || c.time_dim % 2 ||
+        !shape_fits({4, c.hidden, c.hidden}) || emb < 1 || c.num_blocks < 0 ||
+        (long long)c.time_dim + emb + c.flat() > INT_MAX || !shape_fits({c.steps, c.time_dim}) ||
         !std::isfinite(c.max_action) || c.max_action <= 0) {
         fail("unsupported head.meta");
         return false;

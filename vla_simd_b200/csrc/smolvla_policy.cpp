@@ -3,6 +3,8 @@
 // and the kernel sequence of one query batch.
 #include "smolvla_policy.h"
 
+#include "host_util.h"
+
 #include "model_files.h"
 
 #include "f32.h"
@@ -26,51 +28,12 @@ namespace vsb {
 
 namespace {
 
-int env_int(const char* name, int dflt) {
-    const char* e = std::getenv(name);
-    if (!e || !*e) return dflt;
-    char* end = nullptr;
-    const long v = std::strtol(e, &end, 10);
-    return (end && *end == '\0') ? static_cast<int>(v) : dflt;
-}
-
-bool fits(std::initializer_list<long long> dims) {
-    long long c = 1;
-    for (long long d : dims) {
-        if (d <= 0) return false;
-        c *= d;
-        if (c > INT_MAX) return false;
-    }
-    return true;
-}
-
-long long round16(long long v) { return (v + 15) & ~15LL; }
-
-bool numeric_meta(const std::string& text, std::map<std::string, double>& kv) {
-    std::istringstream in(text);
-    std::string key;
-    double val;
-    while (in >> key) {
-        if (!(in >> val) || !std::isfinite(val)) return false;
-        kv[key] = val;
-    }
-    return true;
-}
-
-bool meta_int(const std::map<std::string, double>& kv, const char* key, int& out) {
-    const auto it = kv.find(key);
-    if (it == kv.end()) return true;
-    const double v = it->second;
-    if (v < INT_MIN || v > INT_MAX || v != std::trunc(v)) return false;
-    out = static_cast<int>(v);
-    return true;
-}
-
-template <class T>
-void meta_real(const std::map<std::string, double>& kv, const char* key, T& out) {
-    const auto it = kv.find(key);
-    if (it != kv.end()) out = static_cast<T>(it->second);
-}
+using host::env_int;
+using host::meta_int;
+using host::meta_real;
+using host::numeric_meta;
+using host::round16;
+using host::shape_fits;
 
 // fp32 values of bf16 words (exact: the bf16 bits are the top half)
 std::vector<float> widen(const uint16_t* p, size_t n) {
@@ -155,8 +118,8 @@ bool SmolvlaPolicy::load_vit(const ModelFiles& files, int mask) {
     }
     meta_real(kv, "ln_eps", c.v_eps);
     const int H = c.v_hidden, I = c.v_inter, PD = 3 * c.patch * c.patch, NP = c.n_patches, SD = H * c.sf * c.sf;
-    if (c.n_patches < 1 || !fits({c.img, c.img, 3}) || !fits({c.v_heads, c.v_hd}) || !fits({H, c.sf, c.sf}) ||
-        !fits({c.v_layers, H, H}) || !fits({c.v_layers, I, H}) || !fits({c.mm_out, SD}) ||
+    if (c.n_patches < 1 || !shape_fits({c.img, c.img, 3}) || !shape_fits({c.v_heads, c.v_hd}) || !shape_fits({H, c.sf, c.sf}) ||
+        !shape_fits({c.v_layers, H, H}) || !shape_fits({c.v_layers, I, H}) || !shape_fits({c.mm_out, SD}) ||
         !std::isfinite(c.v_eps) || c.v_eps <= 0) {
         fail("unsupported vit.meta");
         return false;
@@ -241,8 +204,8 @@ bool SmolvlaPolicy::load_vlm(const ModelFiles& files, bool int8) {
     }
     meta_real(kv, "eps", c.rms_eps);
     meta_real(kv, "rope_base", c.rope_base);
-    if (!fits({c.n_q, c.hd}) || !fits({c.n_kv, c.hd}) || c.n_q % c.n_kv || c.hd % 2 || c.qf() != c.hidden ||
-        !fits({c.vlm_layers, c.hidden, c.hidden}) || !fits({c.vlm_layers, c.ffn, c.hidden}) ||
+    if (!shape_fits({c.n_q, c.hd}) || !shape_fits({c.n_kv, c.hd}) || c.n_q % c.n_kv || c.hd % 2 || c.qf() != c.hidden ||
+        !shape_fits({c.vlm_layers, c.hidden, c.hidden}) || !shape_fits({c.vlm_layers, c.ffn, c.hidden}) ||
         !std::isfinite(c.rms_eps) || c.rms_eps <= 0 || !std::isfinite(c.rope_base) || c.rope_base <= 0) {
         fail("unsupported vlm.meta");
         return false;
@@ -310,9 +273,9 @@ bool SmolvlaPolicy::load_expert(const ModelFiles& files, bool int8) {
     const int steps = env_int("SMOLVLA_NUM_STEPS", 0);   // the reference's override (action_expert.cpp:71-76)
     if (steps > 0) c.num_steps = steps;
     const int QF = c.e_nq * c.e_hd, KV = c.e_nkv * c.e_hd, EH = c.eh, EF = c.ef, MAD = c.mad, NL = c.e_layers;
-    if (!fits({c.e_nq, c.e_hd}) || !fits({c.e_nkv, c.e_hd}) || c.e_nq % c.e_nkv || c.e_hd % 2 || EH % 2 ||
-        !fits({NL, EH, QF}) || !fits({NL, KV, KV}) || !fits({NL, EF, EH}) || !fits({2, EH, EH}) ||
-        !fits({c.chunk, MAD}) || !fits({EH, MAD}) || c.num_steps < 1 || c.san < 0 || !std::isfinite(c.e_eps) ||
+    if (!shape_fits({c.e_nq, c.e_hd}) || !shape_fits({c.e_nkv, c.e_hd}) || c.e_nq % c.e_nkv || c.e_hd % 2 || EH % 2 ||
+        !shape_fits({NL, EH, QF}) || !shape_fits({NL, KV, KV}) || !shape_fits({NL, EF, EH}) || !shape_fits({2, EH, EH}) ||
+        !shape_fits({c.chunk, MAD}) || !shape_fits({EH, MAD}) || c.num_steps < 1 || c.san < 0 || !std::isfinite(c.e_eps) ||
         c.e_eps <= 0 || !std::isfinite(c.e_rope_base) || c.e_rope_base <= 0 || !std::isfinite(c.min_period) ||
         !std::isfinite(c.max_period) || c.min_period <= 0 || c.max_period <= c.min_period) {
         fail("unsupported aex.meta");
@@ -392,7 +355,7 @@ bool SmolvlaPolicy::load_heads(const ModelFiles& files) {
         return false;
     }
     meta_real(kv, "norm_eps", c.norm_eps);
-    if (!fits({c.vocab, hidden}) || !fits({c.msd, hidden}) || c.n_views <= 0 || !std::isfinite(c.norm_eps) ||
+    if (!shape_fits({c.vocab, hidden}) || !shape_fits({c.msd, hidden}) || c.n_views <= 0 || !std::isfinite(c.norm_eps) ||
         c.norm_eps <= 0 || c.sd <= 0 || c.sd > c.msd || c.ad <= 0 || c.ad > c.mad || hidden != c.hidden ||
         hidden != c.mm_out || c.e_nkv * c.e_hd != c.kvf() || c.e_layers > c.vlm_layers) {
         fail("heads.meta is missing or malformed");
