@@ -47,3 +47,22 @@ def test_bpe_matches_reference_live(tmp_path, reference):
         s = "".join(rng.choice(alphabet, size=int(rng.integers(0, 40))))
         ids, mask, n = reference.smolvla_tokenize(d, s)
         assert np.array_equal(_as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen), ids[:n]), repr(s)
+
+
+def test_bpe_fuzz_matches_reference(tmp_path, reference):
+    """Random Unicode text (no surrogates, no NUL) through the handle's
+    tokenize path on both sides, 300 strings."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+    d = synth.write_smolvla_checkpoint(str(tmp_path / "smol"), synth.SMOLVLA_SMALL, seed=0)
+    voc = open(os.path.join(d, "tok", "vocab.txt"), encoding="utf-8").read()
+    mer = open(os.path.join(d, "tok", "merges.txt"), encoding="utf-8").read()
+    alphabet = st.characters(blacklist_categories=("Cs",), blacklist_characters="\x00")
+
+    @settings(max_examples=300, deadline=None, suppress_health_check=list(HealthCheck), derandomize=True)
+    @given(st.text(alphabet=alphabet, max_size=40))
+    def check(s):
+        ids, mask, n = reference.smolvla_tokenize(d, s)
+        assert np.array_equal(_as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen), ids[:n]), repr(s)
+
+    check()

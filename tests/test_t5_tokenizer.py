@@ -44,3 +44,21 @@ def test_tokenizer_matches_reference_live(tmp_path, reference):
     for s in cases:
         for n in (4, 16):
             assert np.array_equal(t5_tokenize(text, s, n), reference.t5_tokenize(str(tmp_path / "tok"), s, n)), repr(s)
+
+
+def test_tokenizer_fuzz_matches_reference(tmp_path, reference):
+    """Random Unicode text (no surrogates, no NUL), both tokenizers, 300 strings."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+    os.makedirs(tmp_path / "tok", exist_ok=True)
+    (tmp_path / "tok" / "vocab.txt").write_text(_vocab_text(), encoding="utf-8")
+    text = _vocab_text()
+    tok_dir = str(tmp_path / "tok")
+    alphabet = st.characters(blacklist_categories=("Cs",), blacklist_characters="\x00")
+
+    @settings(max_examples=300, deadline=None, suppress_health_check=list(HealthCheck), derandomize=True)
+    @given(st.text(alphabet=alphabet, max_size=40))
+    def check(s):
+        assert np.array_equal(t5_tokenize(text, s, 16), reference.t5_tokenize(tok_dir, s, 16)), repr(s)
+
+    check()
