@@ -2,7 +2,7 @@
  * vla_simd_cuda.h - op-level C ABI of libvla_simd_b200.so: the B200 kernels
  * behind the reference's portable op API (src/ops/quant_ops.h, lm_ops.h,
  * conv_ops.h), so a TCPU_HAL_CUDA backend of the reference can define its
- * tcpu:: functions on top of these (see INTEGRATION.md).
+ * tcpu:: functions on top of these.
  *
  * Two families:
  *   vla_cuda_*  DEVICE pointers, an explicit cudaStream_t (passed as void*),
@@ -80,7 +80,10 @@ VLA_API int32_t vla_cuda_dense_linear_i8(float* out, const float* x, const int8_
  * seq * ceil16(K) rounded up to 256 bytes, plus 4 * seq, at most 2 MiB (e.g.
  * 602 x 3200); larger calls return VLA_ERR_SHAPE with a message on stderr.
  * The first call on each device looks up the array's device address, so make
- * that first call before any stream capture. All calls share the one array:
+ * that first call before any stream capture (inside a capture it prints the
+ * reason and returns VLA_ERR_DEVICE). The address is valid per CUDA context:
+ * after cudaDeviceReset, or under another context made current through the
+ * driver API, the next call looks it up again. All calls share the one array:
  * calls that overlap on the GPU (different streams, or different host threads
  * on the same device) race; serialize them. */
 VLA_API int32_t vla_cuda_dense_linear_i8_noalloc(float* out, const float* x, const int8_t* Wq,

@@ -30,16 +30,25 @@ def _ptr(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
 
+def reference_dir() -> str | None:
+    """The reference checkout: $VLA_REF_DIR, else a checkout named ``reference``
+    beside this repository; None when neither holds the reference's sources."""
+    cand = os.environ.get("VLA_REF_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isfile(os.path.join(cand, "include", "vla_simd.h")) else None
+
+
 def build(reference: bool | None = None) -> None:
     """make the restatement (always) and the reference build (when its sources exist)."""
     targets = ["oracle"]
+    ref = reference_dir()
     if reference is None:
-        reference = os.path.isdir(os.environ.get("VLA_REF_DIR", "/root/reference"))
-    if reference:
-        targets.append("ref")
+        reference = ref is not None
     env = dict(os.environ)
-    if "VLA_REF_DIR" in env:
-        env["REF"] = env["VLA_REF_DIR"]
+    if reference:
+        if ref is None:
+            raise RuntimeError("the reference build needs its sources: set VLA_REF_DIR")
+        targets.append("ref")
+        env["REF"] = ref
     subprocess.run(["make", "-s", "-j8", "-C", HERE, *targets], check=True, env=env)
 
 

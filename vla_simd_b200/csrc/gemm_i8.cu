@@ -81,6 +81,8 @@ struct EpiParams {
     // int32 tiles [tile][split][M][BN] in ws, arrivals counted per tile
     int32_t* ws;
     unsigned int* counters;
+    // slab kernel (w8a8_slab_kernel): columns per CTA, CTAs per M tile, staging tiles per epilogue warp
+    int slab_bn, slab_groups, slab_nstg;
 };
 
 // Output row (index into out / res, and the absmax slot numerator) of tile
@@ -767,6 +769,8 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
 }
 
+#include "gemm_slab.cuh"
+
 // ------------------------------------------------------------------ SIMT path
 // Plain CUDA-core int8 GEMM (dp4a), used for operand strides TMA cannot
 // describe (lda/ldb not a multiple of 16) and as an independent GPU cross-check
@@ -1027,6 +1031,106 @@ cudaError_t launch_splitk_global(const CUtensorMap& ta, const CUtensorMap& tb, c
     return cudaGetLastError();
 }
 
+// fp32 [rows][cols] output map for TMA stores: box 32 x 32 (128-byte rows,
+// 128-byte swizzle, the slab kernel's staging layout).
+bool make_tmap_f32_out(CUtensorMap* map, const void* base, int rows, int cols, long long ld) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 3) || rows <= 0 || cols <= 0 || ld < cols) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+struct SlabPlan {
+    int bn = 0;        // columns per CTA (a multiple of sl)
+    int sl = 32;       // B slice rows = MMA N
+    int stages = 1;    // B slices in flight
+    int nstg = 2;      // staging tiles per epilogue warp
+};
+
+size_t slab_smem_bytes(int K, int bn, int sl, int stages, int nstg) {
+    const int nkb = (K + kBK - 1) / kBK;
+    return 1024 + (size_t)nkb * kBM * kBK + (size_t)stages * nkb * sl * kBK + (size_t)8 * nstg * kSlabStgFloats * 4 +
+           (size_t)2 * 4 * bn + 8 * (kSlabMaxKb + 2 * stages + kSlabMaxSlices + 1) + 16;
+}
+
+// Ring depth and staging tiles for a slab shape: as many B slices in flight
+// as fit (all of them when they do), two staging tiles per warp when a warp
+// stores more than one chunk. False when even one slice does not fit.
+bool slab_fit(int K, SlabPlan* sp) {
+    const int nsl = sp->bn / sp->sl;
+    const int chunks_per_warp = (sp->bn / 32 + 1) / 2;
+    for (int nstg = chunks_per_warp > 1 ? 2 : 1; nstg >= 1; --nstg) {
+        for (int st = nsl; st >= 1; --st) {
+            if (slab_smem_bytes(K, sp->bn, sp->sl, st, nstg) <= kMaxDynSmem) {
+                sp->stages = st;
+                sp->nstg = nstg;
+                return true;
+            }
+        }
+    }
+    return false;
+}
+
+// The slab kernel takes a plain GEMM (fp32 output through TMA stores, K <=
+// 1024) when its output fits one wave: the narrowest multiple of 32 columns
+// per CTA that needs at most one CTA per SM. VLA_GEMM_SLAB=0 turns it off,
+// VLA_GEMM_SLAB=<bn>:<sl>[:<stages>] forces a shape; VLA_GEMM_PLAN (a forced
+// persistent / split-K plan) also keeps GEMMs off it.
+bool slab_plan(int M, int N, int K, SlabPlan* sp) {
+    const int nkb = (K + kBK - 1) / kBK;
+    if (nkb > kSlabMaxKb || M <= 0 || N <= 0) return false;
+    const char* env = std::getenv("VLA_GEMM_SLAB");
+    if (env && env[0] == '0' && env[1] == '\0') return false;
+    const long long m_tiles = (M + kBM - 1) / kBM;
+    if (env) {
+        int bn = 0, sl = 0, st = 0;
+        const int n = std::sscanf(env, "%d:%d:%d", &bn, &sl, &st);
+        if (n >= 2 && (sl == 32 || sl == 64 || sl == 128) && bn >= sl && bn <= kSlabMaxBn && bn % sl == 0) {
+            sp->bn = bn;
+            sp->sl = sl;
+            if (!slab_fit(K, sp)) return false;
+            if (n == 3 && st >= 1 && st < sp->stages) sp->stages = st;
+            return m_tiles * ((N + bn - 1) / bn) <= 0x7FFFFFFF;
+        }
+        return false;
+    }
+    if (std::getenv("VLA_GEMM_PLAN")) return false;
+    const long long sms = sm_count();
+    for (int bn = 32; bn <= kSlabMaxBn; bn += 32) {
+        if (m_tiles * ((N + bn - 1) / bn) <= sms) {
+            sp->bn = bn;
+            sp->sl = 32;
+            return slab_fit(K, sp);
+        }
+    }
+    return false;
+}
+
+template <int SL>
+cudaError_t slab_ready() {
+    static std::atomic<unsigned long long> done{0};
+    return set_smem_attr_once(w8a8_slab_kernel<SL>, done);
+}
+
+template <int SL>
+cudaError_t launch_slab_sl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const EpiParams& p,
+                           const SlabPlan& sp, cudaStream_t st) {
+    cudaError_t e = slab_ready<SL>();
+    if (e != cudaSuccess) return e;
+    const long long grid = (long long)p.m_tiles * p.slab_groups;
+    e = launch_k(w8a8_slab_kernel<SL>, dim3(static_cast<unsigned>(grid)), kThreads,
+                 slab_smem_bytes(p.K, sp.bn, SL, sp.stages, sp.nstg), st, ta, tb, to, p, sp.stages);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 EpiParams make_epi(const GemmI8Args& a) {
     EpiParams p{};
     p.out = a.out;
@@ -1168,8 +1272,27 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
                         (a.lda & 15) == 0 && (a.ldb & 15) == 0;
     if (!a.force_simt && tma_ok) {
-        // operands TMA can describe always take the tensor-core kernel; a tensor
+        // operands TMA can describe always take the tensor-core kernels; a tensor
         // map the driver refuses is an error, never a silent detour
+        SlabPlan sp;
+        const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out);
+        if (!(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 && a.ldo >= a.N &&
+            slab_plan(a.M, a.N, a.K, &sp)) {
+            EpiParams p = make_epi(a);
+            p.slab_bn = sp.bn;
+            p.slab_groups = (a.N + sp.bn - 1) / sp.bn;
+            p.slab_nstg = sp.nstg;
+            CUtensorMap ta, tb, to;
+            if (!make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) ||
+                !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, sp.sl) ||
+                !make_tmap_f32_out(&to, a.out, a.M, a.N, a.ldo))
+                return cudaErrorInvalidConfiguration;
+            switch (sp.sl) {
+                case 64: return launch_slab_sl<64>(ta, tb, to, p, sp, st);
+                case 128: return launch_slab_sl<128>(ta, tb, to, p, sp, st);
+                default: return launch_slab_sl<32>(ta, tb, to, p, sp, st);
+            }
+        }
         GemmPlan plan = gemm_i8_plan(a.M, a.N, a.K);
         gemm_i8_skinny_plan(a, &plan);
         CUtensorMap ta, tb;
