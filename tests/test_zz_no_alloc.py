@@ -47,6 +47,59 @@ def test_noalloc_linear_equals_allocating_entry_point():
     assert ops.device_status() == 0
 
 
+def test_noalloc_at_the_scratch_limit():
+    """The largest call that fits the 2 MiB array runs and matches; one more row is refused.
+
+    Scratch need = seq * ceil16(K) rounded up to 256 bytes, plus 4 * seq. At
+    K = 512 that is 516 * seq: 4064 rows need 2,097,024 bytes (128 under the
+    limit), 4065 rows 2,097,540 (388 over). No (seq, K) needs exactly 2 MiB:
+    it would take 64 * a * (ceil16(K) + 4) == 2**21 with ceil16(K) + 4 four
+    times an odd number."""
+    import torch
+    from vla_simd_b200 import lib, ops
+    L = lib()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    seq, N, K = 4064, 64, 512
+    x, W, b = _case(torch, dev, seq + 1, N, K, 4)
+    wq, ws = ops.pack_weights_i8(W)
+    want = ops.dense_linear_i8(x[:seq], wq, ws, b)
+    out = torch.full((seq + 1, N), float("nan"), device=dev)
+    rc = L.vla_cuda_dense_linear_i8_noalloc(out.data_ptr(), x.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+                                            b.data_ptr(), seq, N, K, wq.stride(0), stream)
+    assert rc == VLA_OK
+    torch.cuda.synchronize()
+    assert torch.equal(out[:seq].view(torch.int32), want.view(torch.int32))
+    assert torch.isnan(out[seq]).all()
+    rc = L.vla_cuda_dense_linear_i8_noalloc(out.data_ptr(), x.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+                                            b.data_ptr(), seq + 1, N, K, wq.stride(0), stream)
+    assert rc == VLA_ERR_SHAPE
+
+
+def test_noalloc_on_a_second_device():
+    """Each device has its own copy of the array: a call on device 1 after device 0 matches too."""
+    import torch
+    from vla_simd_b200 import lib, ops
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one visible GPU")
+    L = lib()
+    for d in (0, 1, 0):
+        torch.cuda.set_device(d)
+        dev = torch.device("cuda", d)
+        stream = torch.cuda.current_stream().cuda_stream
+        x, W, b = _case(torch, dev, 100, 512, 512, 5 + d)
+        wq, ws = ops.pack_weights_i8(W)
+        want = ops.dense_linear_i8(x, wq, ws, b)
+        out = torch.empty((100, 512), device=dev)
+        rc = L.vla_cuda_dense_linear_i8_noalloc(out.data_ptr(), x.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+                                                b.data_ptr(), 100, 512, 512, wq.stride(0), stream)
+        assert rc == VLA_OK
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int32), want.view(torch.int32))
+    torch.cuda.set_device(0)
+
+
 def test_noalloc_rejects_calls_beyond_its_scratch():
     import ctypes
     from vla_simd_b200 import lib

@@ -1102,11 +1102,15 @@ bool slab_plan(int M, int N, int K, SlabPlan* sp) {
         return false;
     }
     if (std::getenv("VLA_GEMM_PLAN")) return false;
+    // One MMA chain per CTA (slice = the whole slab): measured on the B200,
+    // a 128 x 32 x 32 MMA chain runs at well under a quarter of the rate of a
+    // 128 x 128 x 32 one (each step waits for the previous accumulation), so
+    // narrow slices cost more in MMA time than their epilogue overlap returns.
     const long long sms = sm_count();
-    for (int bn = 32; bn <= kSlabMaxBn; bn += 32) {
+    for (int bn : {32, 64, 128}) {
         if (m_tiles * ((N + bn - 1) / bn) <= sms) {
             sp->bn = bn;
-            sp->sl = 32;
+            sp->sl = bn;
             return slab_fit(K, sp);
         }
     }

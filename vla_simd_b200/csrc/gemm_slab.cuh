@@ -70,8 +70,9 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    if (!p.static_weights) pdl_wait();
 
+    // On-chip set-up first: it touches nothing a predecessor kernel writes, so
+    // under programmatic dependent launch it overlaps the predecessor's tail.
     if (threadIdx.x == 0) {
         for (int kb = 0; kb < nkb; ++kb) mbar_init(&afull[kb], 1);
         for (int s = 0; s < stages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
@@ -89,7 +90,10 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // The TMEM columns are held: the next kernel may be scheduled now.
     pdl_trigger();
+    // weights that a predecessor kernel may still be writing: wait before any load
+    if (!p.static_weights) pdl_wait();
 
     int b_issued = 0;
     bool a_issued = false;
@@ -241,7 +245,7 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 bulk_commit();
             }
         }
-        if (lane == 0) bulk_wait_all();
+        if (lane == 0) bulk_wait_read<0>();   // the staging tiles must outlive the stores' reads
         __syncwarp();
         if (p.amax && quarter_live) {
             // one atomic per warp when its rows share a slot, else one per row

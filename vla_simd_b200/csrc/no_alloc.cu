@@ -30,13 +30,40 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device. In host code the
+// A __device__ variable's address belongs to a CUDA context, not to a device
+// number: after cudaDeviceReset, or under a non-primary context a host
+// framework made current through the driver API, the same device has a new
+// address. So the cache holds, per device, the context the address was looked
+// up in, and a call under any other context looks it up again.
+struct Cached {
+    void* ctx = nullptr;
+    void* addr = nullptr;
+};
+Cached g_cache[kMaxDevices];
+
+using CtxGetCurrentFn = int (*)(void**);   // cuCtxGetCurrent: CUresult (CUcontext*)
+
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(f);
+    });
+    return fn;
+}
+
+// Device address of g_noalloc_scratch in the current context. In host code the
 // array's name is only a stand-in for the device object, so the real address
-// is asked of the runtime once per device (with that device current) and
-// cached; the first call on each device does this.
-void* scratch_address(cudaError_t* err) {
+// is asked of the runtime (cudaGetSymbolAddress, which also creates the
+// device's primary context on first use) with the device current; this set-up
+// runs on the first call per device and context and is cached. It must not
+// run while `st` is being captured into a graph: the lookup is refused then.
+void* scratch_address(cudaStream_t st, cudaError_t* err) {
     int dev = 0;
     *err = cudaGetDevice(&dev);
     if (*err != cudaSuccess) return nullptr;
@@ -44,14 +71,36 @@ void* scratch_address(cudaError_t* err) {
         *err = cudaErrorInvalidDevice;
         return nullptr;
     }
+    void* ctx = nullptr;
+    CtxGetCurrentFn get = ctx_get_current();
+    const bool have_ctx = get && get(&ctx) == 0 && ctx;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
-        void* p = nullptr;
-        *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (*err != cudaSuccess) return nullptr;
-        g_addr[dev] = p;
+    Cached& c = g_cache[dev];
+    if (have_ctx && c.addr && c.ctx == ctx) return c.addr;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+        std::fprintf(stderr,
+                     "vla_cuda_dense_linear_i8_noalloc: the first call on a device (or in a new CUDA context) "
+                     "looks up the scratch array's address and cannot run inside stream capture; call it once "
+                     "before capturing\n");
+        *err = cudaErrorStreamCaptureUnsupported;
+        return nullptr;
     }
-    return g_addr[dev];
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    if (have_ctx) {
+        c.ctx = ctx;
+        c.addr = p;
+    } else if (get) {
+        // cudaGetSymbolAddress made the primary context current: key the cache by it
+        void* now = nullptr;
+        if (get(&now) == 0 && now) {
+            c.ctx = now;
+            c.addr = p;
+        }
+    }
+    return p;
 }
 
 }  // namespace
@@ -71,11 +120,11 @@ extern "C" int32_t vla_cuda_dense_linear_i8_noalloc(float* out, const float* x, 
         return VLA_ERR_SHAPE;
     }
     cudaError_t e = cudaSuccess;
-    unsigned char* base = static_cast<unsigned char*>(scratch_address(&e));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned char* base = static_cast<unsigned char*>(scratch_address(st, &e));
     if (!base) return VLA_ERR_DEVICE;
     int8_t* xq = reinterpret_cast<int8_t*>(base);
     float* ascale = reinterpret_cast<float*>(base + xq_bytes);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     // every byte of xq / ascale the GEMM reads is written by the quantizer first
     e = vsb::quantize_rows(x, K, nullptr, 0, seq, K, xq, ld, ascale, nullptr, 0, nullptr, st);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? VLA_ERR_ARG : VLA_ERR_DEVICE;
