@@ -66,3 +66,26 @@ def test_bpe_fuzz_matches_reference(tmp_path, reference):
         assert np.array_equal(_as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen), ids[:n]), repr(s)
 
     check()
+
+
+def test_bpe_split_rules_fuzz_matches_reference(tmp_path, reference):
+    """Text drawn from the characters the split rules single out (ASCII and
+    other whitespace, contraction letters after apostrophes, ASCII and other
+    digits, letters and symbols of several scripts), 500 strings."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+    d = synth.write_smolvla_checkpoint(str(tmp_path / "smol"), synth.SMOLVLA_SMALL, seed=0)
+    voc = open(os.path.join(d, "tok", "vocab.txt"), encoding="utf-8").read()
+    mer = open(os.path.join(d, "tok", "merges.txt"), encoding="utf-8").read()
+    pieces = [" ", "  ", "\t", "\n", "\r\n", " ", "　", " ", "'", "'s", "'re", "'ve", "'ll", "'d",
+              "'m", "'t", "'x", "0", "7", "42", "٣", "²", "５", "abc", "Robot", "été",
+              "中文", "аб", "!", "?!", ".", "-", "_", "€", "\U0001f916", "pick", " up"]
+
+    @settings(max_examples=500, deadline=None, suppress_health_check=list(HealthCheck), derandomize=True)
+    @given(st.lists(st.sampled_from(pieces), max_size=24))
+    def check(parts):
+        s = "".join(parts)
+        ids, mask, n = reference.smolvla_tokenize(d, s)
+        assert np.array_equal(_as_handle(voc, mer, s, synth.SMOLVLA_SMALL.tok_maxlen), ids[:n]), repr(s)
+
+    check()

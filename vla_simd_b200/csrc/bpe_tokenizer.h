@@ -5,10 +5,9 @@
 // vocab.txt: "id<TAB>token" per line (tokens in the byte-to-unicode alphabet);
 // merges.txt: "a b" per line, the line number is the merge's rank.
 #pragma once
-#include <map>
+#include <cstddef>
 #include <string>
 #include <unordered_map>
-#include <utility>
 #include <vector>
 
 namespace vsb {
@@ -20,11 +19,12 @@ class BpeTokenizer {
     std::vector<int> encode(const std::string& text) const;
 
   private:
-    std::vector<int> merge_piece(const std::string& bytes) const;
+    // ids of the piece text[begin, end) after merging
+    std::vector<int> merge_piece(const std::string& text, size_t begin, size_t end) const;
 
     std::unordered_map<std::string, int> vocab_;
-    std::map<std::pair<std::string, std::string>, int> rank_;
-    std::string byte_char_[256];
+    std::unordered_map<std::string, int> rank_;   // "left right" -> merge rank
+    std::string byte_char_[256];                  // byte -> its symbol (UTF-8)
 };
 
 }  // namespace vsb

@@ -1,60 +1,21 @@
 // T5 unigram tokenizer: the reference's normalization (a subset of NFKC plus
-// whitespace folding into the U+2581 word marker) and its Viterbi
-// segmentation over bytes, src/tokenizer/t5_tokenizer.cpp:13-129.
+// whitespace folding into the U+2581 word marker) and its best-score
+// segmentation over bytes, src/tokenizer/t5_tokenizer.cpp:13-155. Three steps:
+// normalize() rewrites the text; segment() scores every byte position from the
+// pieces that end there (the best score of the text up to each position);
+// encode() cuts the text at literal control pieces ("<extra_id_0>") and
+// segments what lies between them.
 #include "t5_tokenizer.h"
+
+#include "utf8.h"
 
 #include <algorithm>
 #include <limits>
 #include <sstream>
+#include <string_view>
 
 namespace vsb {
 namespace {
-
-// UTF-8 -> code points; a malformed or truncated sequence gives U+FFFD per
-// lead byte (src/tokenizer/bert_tokenizer.cpp:17-35).
-std::vector<uint32_t> decode_utf8(const std::string& s) {
-    std::vector<uint32_t> out;
-    out.reserve(s.size());
-    size_t i = 0;
-    while (i < s.size()) {
-        const unsigned lead = static_cast<unsigned char>(s[i++]);
-        int more;
-        if (lead < 0x80) more = 0;
-        else if (lead >= 0xC2 && lead < 0xE0) more = 1;
-        else if (lead >= 0xE0 && lead < 0xF0) more = 2;
-        else if (lead >= 0xF0 && lead < 0xF5) more = 3;
-        else { out.push_back(0xFFFD); continue; }
-        uint32_t cp = lead & (0x7Fu >> more);
-        // the first continuation byte's range excludes overlongs and surrogates
-        unsigned lo = 0x80, hi = 0xBF;
-        if (lead == 0xE0) lo = 0xA0;
-        if (lead == 0xF0) lo = 0x90;
-        if (lead == 0xED) hi = 0x9F;
-        if (lead == 0xF4) hi = 0x8F;
-        while (more > 0 && i < s.size()) {
-            const unsigned c = static_cast<unsigned char>(s[i]);
-            if (c < lo || c > hi) break;
-            cp = (cp << 6) | (c & 0x3Fu);
-            ++i;
-            --more;
-            lo = 0x80;
-            hi = 0xBF;
-        }
-        out.push_back(more ? 0xFFFD : cp);
-    }
-    return out;
-}
-
-void encode_utf8(std::string& out, uint32_t cp) {
-    if (cp < 0x80) {
-        out.push_back(static_cast<char>(cp));
-        return;
-    }
-    int n = cp < 0x800 ? 1 : cp < 0x10000 ? 2 : 3;   // continuation bytes
-    static const unsigned kLead[4] = {0, 0xC0, 0xE0, 0xF0};
-    out.push_back(static_cast<char>(kLead[n] | (cp >> (6 * n))));
-    while (n-- > 0) out.push_back(static_cast<char>(0x80 | ((cp >> (6 * n)) & 0x3F)));
-}
 
 // Compatibility decompositions the normalizer applies (the NFKC cases of
 // Latin-1 and General Punctuation that T5's normalizer rewrites):
@@ -103,15 +64,45 @@ bool blank(uint32_t cp) {
     }
 }
 
-int utf8_bytes(unsigned char c) {
-    if (c < 0x80) return 1;
-    if ((c & 0xE0) == 0xC0) return 2;
-    if ((c & 0xF0) == 0xE0) return 3;
-    if ((c & 0xF8) == 0xF0) return 4;
-    return 1;
+constexpr int kUnk = 2, kEos = 1, kPad = 0;
+
+const Compat* compat_of(uint32_t cp) {
+    const Compat* end = kCompat + sizeof(kCompat) / sizeof(kCompat[0]);
+    const Compat* it = std::lower_bound(kCompat, end, cp, [](const Compat& c, uint32_t v) { return c.cp < v; });
+    return it != end && it->cp == cp ? it : nullptr;
 }
 
-constexpr int kUnk = 2, kEos = 1, kPad = 0;
+// The normalizer: strict UTF-8 decoding (a bad sequence reads as U+FFFD),
+// dropped controls, fullwidth ASCII folded to ASCII, the compatibility
+// rewrites above, and every run of blanks before a word replaced by one U+2581
+// (blanks after the last word vanish).
+std::string normalize(const std::string& text) {
+    std::string out;
+    bool word_start = true;
+    auto put = [&](uint32_t cp) {
+        if (blank(cp)) {
+            word_start = true;
+            return;
+        }
+        if (word_start) utf8_put(out, 0x2581);
+        word_start = false;
+        utf8_put(out, cp);
+    };
+    for (size_t i = 0; i < text.size();) {
+        const Utf8Char u = utf8_strict(text.data() + i, text.size() - i);
+        i += u.len;
+        uint32_t cp = u.cp;
+        if (dropped(cp)) continue;
+        if (cp >= 0xFF01 && cp <= 0xFF5D) cp -= 0xFEE0;
+        if (const Compat* c = compat_of(cp)) {
+            for (uint32_t r : c->to)
+                if (r) put(r);
+        } else {
+            put(cp);
+        }
+    }
+    return out;
+}
 
 }  // namespace
 
@@ -144,92 +135,87 @@ bool T5Tokenizer::load_text(const std::string& text) {
 }
 
 void T5Tokenizer::segment(const std::string& text, std::vector<int>& ids) const {
-    // normalize: compatibility rewrites, fullwidth ASCII to ASCII, dropped
-    // controls, runs of blanks -> one U+2581 before the next word
-    std::string s;
-    bool at_word_start = true;
-    auto emit = [&](uint32_t cp) {
-        if (blank(cp)) {
-            at_word_start = true;
-            return;
-        }
-        if (at_word_start) {
-            s += "\xE2\x96\x81";
-            at_word_start = false;
-        }
-        encode_utf8(s, cp);
-    };
-    for (uint32_t cp : decode_utf8(text)) {
-        if (dropped(cp)) continue;
-        if (cp >= 0xFF01 && cp <= 0xFF5D) cp -= 0xFEE0;
-        const Compat* hit = nullptr;
-        for (const Compat& c : kCompat)
-            if (c.cp == cp) hit = &c;
-        if (!hit) {
-            emit(cp);
-            continue;
-        }
-        for (uint32_t r : hit->to) {
-            if (!r) break;
-            emit(r);
-        }
-    }
-
-    // best[i]: highest total score of a segmentation of s[0, i); ties keep the
-    // first candidate found (shorter pieces first, then the unknown fallback)
+    const std::string s = normalize(text);
     const int n = static_cast<int>(s.size());
-    const double kNone = -std::numeric_limits<double>::infinity();
+    // score[j]: best total score of a segmentation of s[0, j); start[j] / id[j]
+    // the last piece of that segmentation. Candidates for j are weighed in the
+    // order: start position ascending, and at one start the vocabulary piece
+    // before the one-character <unk>; a later candidate wins only with a
+    // strictly higher score, which fixes the ties.
+    const double kUnreachable = -std::numeric_limits<double>::infinity();
     const double unk_score = lowest_ - 10.0;
-    std::vector<double> best(n + 1, kNone);
-    std::vector<int> from(n + 1, -1), tok(n + 1, kUnk);
-    best[0] = 0.0;
+    std::vector<double> score(n + 1, kUnreachable);
+    std::vector<int> start(n + 1, -1), id(n + 1, kUnk);
+    std::vector<int> char_len(n, 1);     // UTF-8 length of the character starting at each byte
     for (int i = 0; i < n; ++i) {
-        if (best[i] == kNone) continue;
-        const int lmax = std::min(longest_, n - i);
-        for (int len = 1; len <= lmax; ++len) {
-            const auto it = piece_.find(s.substr(i, len));
-            if (it == piece_.end()) continue;
-            const double cand = best[i] + score_[it->second];
-            if (cand > best[i + len]) {
-                best[i + len] = cand;
-                from[i + len] = i;
-                tok[i + len] = it->second;
+        const unsigned c = static_cast<unsigned char>(s[i]);
+        char_len[i] = c < 0x80 ? 1 : (c & 0xE0) == 0xC0 ? 2 : (c & 0xF0) == 0xE0 ? 3 : (c & 0xF8) == 0xF0 ? 4 : 1;
+    }
+    score[0] = 0.0;
+    std::string_view sv(s);
+    const int reach = std::max(longest_, 4);   // the farthest start a piece or a character can have
+    for (int j = 1; j <= n; ++j) {
+        for (int i = std::max(0, j - reach); i < j; ++i) {
+            if (score[i] == kUnreachable) continue;
+            if (j - i <= longest_) {
+                const auto it = piece_.find(std::string(sv.substr(i, j - i)));
+                if (it != piece_.end() && score[i] + score_[it->second] > score[j]) {
+                    score[j] = score[i] + score_[it->second];
+                    start[j] = i;
+                    id[j] = it->second;
+                }
+            }
+            if (char_len[i] == j - i && score[i] + unk_score > score[j]) {
+                score[j] = score[i] + unk_score;
+                start[j] = i;
+                id[j] = kUnk;
             }
         }
-        // one whole UTF-8 character as <unk>
-        const int len = utf8_bytes(static_cast<unsigned char>(s[i]));
-        if (best[i] + unk_score > best[i + len]) {
-            best[i + len] = best[i] + unk_score;
-            from[i + len] = i;
-            tok[i + len] = kUnk;
-        }
     }
-    // walk back; consecutive unknowns collapse into one
-    std::vector<int> back;
-    for (int i = n; i > 0; i = from[i]) {
-        const bool repeat_unk = tok[i] == kUnk && !back.empty() && back.back() == kUnk;
-        if (!repeat_unk) back.push_back(tok[i]);
+    // the winning pieces front to back; a run of <unk> pieces emits one <unk>
+    std::vector<int> path;
+    for (int j = n; j > 0; j = start[j]) path.push_back(id[j]);
+    bool after_unk = false;
+    for (auto it = path.rbegin(); it != path.rend(); ++it) {
+        if (*it == kUnk && after_unk) continue;
+        after_unk = *it == kUnk;
+        ids.push_back(*it);
     }
-    ids.insert(ids.end(), back.rbegin(), back.rend());
+}
+
+std::vector<std::pair<size_t, size_t>> T5Tokenizer::control_pieces(const std::string& text) const {
+    // every '<' opens a candidate that ends at the next '>'; the candidate is a
+    // control piece when the vocabulary holds it with score 0 and it is shorter
+    // than the longest piece. Scanning resumes after a match (no control piece
+    // of a T5 vocabulary holds a second '<').
+    std::vector<std::pair<size_t, size_t>> hits;
+    size_t from = 0;
+    for (;;) {
+        const size_t open = text.find('<', from);
+        if (open == std::string::npos) break;
+        const size_t close = text.find('>', open);
+        if (close == std::string::npos) break;
+        from = open + 1;
+        if (close - open >= static_cast<size_t>(longest_)) continue;
+        const auto it = piece_.find(text.substr(open, close + 1 - open));
+        if (it == piece_.end() || score_[static_cast<size_t>(it->second)] != 0.0) continue;
+        hits.emplace_back(open, close + 1);
+        from = close + 1;
+    }
+    return hits;
 }
 
 std::vector<int> T5Tokenizer::encode(const std::string& text, int max_len) const {
     if (max_len < 1) return {};
     std::vector<int> ids;
-    // control pieces written literally ("<extra_id_0>") are kept whole; the
-    // text between them is segmented
     size_t done = 0;
-    for (size_t open = text.find('<'); open != std::string::npos; open = text.find('<', open + 1)) {
-        const size_t close = text.find('>', open);
-        if (close == std::string::npos) break;
-        if (close - open >= static_cast<size_t>(longest_)) continue;
-        const auto it = piece_.find(text.substr(open, close + 1 - open));
-        if (it == piece_.end() || score_[static_cast<size_t>(it->second)] != 0.0) continue;
-        segment(text.substr(done, open - done), ids);
-        ids.push_back(it->second);
-        done = close + 1;
+    for (const auto& [b, e] : control_pieces(text)) {
+        segment(text.substr(done, b - done), ids);
+        ids.push_back(piece_.at(text.substr(b, e - b)));
+        done = e;
     }
     segment(text.substr(done), ids);
+    // room for the eos, then padding to max_len
     if (static_cast<int>(ids.size()) > max_len - 1) ids.resize(static_cast<size_t>(max_len - 1));
     ids.push_back(kEos);
     ids.resize(static_cast<size_t>(max_len), kPad);

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <string>
 #include <unordered_map>
+#include <utility>
 #include <vector>
 
 namespace vsb {
@@ -26,7 +27,10 @@ class T5Tokenizer {
     int pad_id() const { return 0; }
 
   private:
+    // ids of `text` after normalization (no control pieces inside)
     void segment(const std::string& text, std::vector<int>& ids) const;
+    // [begin, end) of each literal control piece in `text`, in order
+    std::vector<std::pair<size_t, size_t>> control_pieces(const std::string& text) const;
 
     std::unordered_map<std::string, int> piece_;
     std::vector<double> score_;
