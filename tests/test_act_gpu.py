@@ -9,6 +9,8 @@ import pytest
 
 from vla_simd_b200 import synth
 
+from _parity import check_actions
+
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 TOL = 1e-3
@@ -28,7 +30,7 @@ def test_small_act_matches_reference(tmp_path, monkeypatch, mask):
     f, s = synth.act_inputs(synth.ACT_SMALL, seed=1)
     got = pol.predict(f, s)
     want = np.load(os.path.join(GOLDEN, f"act_small_m{mask}.npy"))
-    assert np.abs(got - want).max() <= TOL, np.abs(got - want).max()
+    check_actions(f"act-small-m{mask}", got, want, TOL)
     pol.close()
 
 
@@ -38,9 +40,7 @@ def test_baseline_act_matches_reference(tmp_path, monkeypatch):
     f, s = synth.act_inputs(synth.ACT_BASELINE, seed=1)
     got = pol.predict(f, s)
     want = np.load(os.path.join(GOLDEN, "act_base_m63.npy"))
-    err = np.abs(got - want).max()
-    print("ACT baseline max-abs vs reference:", err)
-    assert err <= TOL
+    check_actions("act-base-m63", got, want, TOL)
     again = pol.predict(f, s)
     assert np.array_equal(got, again), "step is not deterministic"
     assert pol.kernels_per_step > 50

@@ -18,6 +18,8 @@ import pytest
 
 from vla_simd_b200 import synth
 
+from _parity import check_actions
+
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 TOL = 1e-3
@@ -43,9 +45,7 @@ def test_small_dp_matches_reference(tmp_path, monkeypatch, mask, tol):
     pol = _policy(tmp_path, synth.DP_SMALL, mask, monkeypatch)
     f, s, n = synth.dp_inputs(synth.DP_SMALL, seed=1)
     got = pol.predict(f, s, n)
-    err = np.abs(got - _want("small", mask)).max()
-    print(f"DP small mask {mask} max-abs vs reference: {err:.3g}")
-    assert err <= tol
+    check_actions(f"dp-small-m{mask}", got, _want("small", mask), tol)
     pol.close()
 
 
@@ -53,17 +53,14 @@ def test_small_dp_ddpm_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.DP_SMALL, 3, monkeypatch, sched="DDPM")
     assert pol.is_ddim == 0 and pol.num_steps == 10
     f, s, n = synth.dp_inputs(synth.DP_SMALL, seed=1)
-    err = np.abs(pol.predict(f, s, n) - _want("small", 3, "ddpm")).max()
-    print("DP small DDPM max-abs vs reference:", err)
-    assert err <= TOL
+    check_actions("dp-small-m3-ddpm", pol.predict(f, s, n), _want("small", 3, "ddpm"), TOL)
     pol.close()
 
 
 def test_small_dp_without_noise_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.DP_SMALL, 3, monkeypatch)
     f, s, _ = synth.dp_inputs(synth.DP_SMALL, seed=1)
-    err = np.abs(pol.predict(f, s, None) - _want("small", 3, "nonoise")).max()
-    assert err <= TOL
+    check_actions("dp-small-m3-nonoise", pol.predict(f, s, None), _want("small", 3, "nonoise"), TOL)
     pol.close()
 
 
@@ -74,9 +71,7 @@ def test_baseline_dp_matches_reference(tmp_path, monkeypatch, mask):
         assert pol.int8_layers == 52   # the reference's count: U-Net GEMM layers + backbone convs
     f, s, n = synth.dp_inputs(synth.DP_BASELINE, seed=1)
     got = pol.predict(f, s, n)
-    err = np.abs(got - _want("base", mask)).max()
-    print(f"DP baseline mask {mask} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"dp-base-m{mask}", got, _want("base", mask), TOL)
     assert np.array_equal(got, pol.predict(f, s, n)), "query is not deterministic"
     assert pol.kernels_per_step > 100
     pol.close()
@@ -97,9 +92,7 @@ def test_edge_dp_matches_reference(tmp_path, monkeypatch, cfg, shape, mask, n_in
     assert pol.int8_layers == n_int8
     f, s, n = synth.dp_inputs(shape, seed=1)
     got = pol.predict(f, s, n)
-    err = np.abs(got - _want(cfg, mask)).max()
-    print(f"DP {cfg} mask {mask} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"dp-{cfg}-m{mask}", got, _want(cfg, mask), TOL)
     pol.close()
 
 

@@ -12,6 +12,8 @@ import pytest
 
 from vla_simd_b200 import synth
 
+from _parity import check_actions
+
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 TOL = 1e-3
@@ -39,9 +41,7 @@ def test_small_octo_matches_reference(tmp_path, monkeypatch, mask, n_int8):
     assert pol.int8_layers == n_int8   # the reference's count on this checkpoint
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_SMALL, "")
     got = pol.predict(p, w, tm, ins, n, z)
-    err = np.abs(got - _want("small", mask)).max()
-    print(f"Octo small mask {mask} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"octo-small-m{mask}", got, _want("small", mask), TOL)
     pol.close()
 
 
@@ -50,9 +50,7 @@ def test_erf_gelu_octo_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.OCTO_ERF, 63, monkeypatch)
     assert pol.int8_layers == 38
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_ERF, "")
-    err = np.abs(pol.predict(p, w, tm, ins, n, z) - _want("erf", 63)).max()
-    print(f"Octo erf-GELU max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions("octo-erf-m63", pol.predict(p, w, tm, ins, n, z), _want("erf", 63), TOL)
     pol.close()
 
 
@@ -60,9 +58,7 @@ def test_small_octo_readout_matches_reference(tmp_path, monkeypatch):
     pol = _policy(tmp_path, synth.OCTO_SMALL, 63, monkeypatch)
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_SMALL, "")
     pol.predict(p, w, tm, ins, n, z)
-    err = np.abs(pol.readout()[0] - _want("small", 63, "readout")).max()
-    print(f"Octo small readout max-abs vs reference: {err:.3g}")
-    assert err <= 1e-5
+    check_actions("octo-small-m63-readout", pol.readout()[0], _want("small", 63, "readout"), 1e-5)
     pol.close()
 
 
@@ -71,9 +67,7 @@ def test_small_octo_variants_match_reference(tmp_path, monkeypatch, variant):
     pol = _policy(tmp_path, synth.OCTO_SMALL, 63, monkeypatch)
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_SMALL, variant)
     got = pol.predict(p, w, tm, ins, n, z, seed=seed)
-    err = np.abs(got - _want("small", 63, variant)).max()
-    print(f"Octo small {variant} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"octo-small-m63-{variant}", got, _want("small", 63, variant), TOL)
     pol.close()
 
 
@@ -82,9 +76,7 @@ def test_baseline_octo_matches_reference(tmp_path, monkeypatch):
     assert pol.int8_layers == 92
     p, w, tm, ins, n, z, seed = octo_query(synth.OCTO_BASELINE, "")
     got = pol.predict(p, w, tm, ins, n, z)
-    err = np.abs(got - _want("base", 63)).max()
-    print(f"Octo baseline max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions("octo-base-m63", got, _want("base", 63), TOL)
     assert np.array_equal(got, pol.predict(p, w, tm, ins, n, z)), "query is not deterministic"
     assert pol.t5_runs == 2   # the warm-up's empty instruction, then this one once
     assert pol.kernels_per_step > 100

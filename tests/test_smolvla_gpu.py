@@ -12,6 +12,8 @@ import pytest
 
 from vla_simd_b200 import synth
 
+from _parity import check_actions
+
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 TOL = 1e-3
@@ -38,9 +40,7 @@ def test_small_smolvla_matches_reference(tmp_path, monkeypatch, mask, n_int8, va
     assert pol.int8_layers == n_int8   # the reference's count on this checkpoint
     f, ins, st, nz, seed, pv, wt, g = smolvla_query(synth.SMOLVLA_SMALL, variant)
     got = pol.predict(f, ins, st, nz, seed, pv, wt, g)
-    err = np.abs(got - _want("small", mask, variant)).max()
-    print(f"SmolVLA small mask {mask} {variant or 'plain'} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"smolvla-small-m{mask}-{variant or 'plain'}", got, _want("small", mask, variant), TOL)
     pol.close()
 
 
@@ -53,9 +53,7 @@ def test_edge_smolvla_matches_reference(tmp_path, monkeypatch, mask, n_int8):
     assert pol.int8_layers == n_int8
     f, ins, st, nz, seed, pv, wt, g = smolvla_query(synth.SMOLVLA_EDGE, "short")
     got = pol.predict(f, ins, st, nz, seed, pv, wt, g)
-    err = np.abs(got - _want("edge", mask, "short")).max()
-    print(f"SmolVLA edge mask {mask} max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions(f"smolvla-edge-m{mask}", got, _want("edge", mask, "short"), TOL)
     pol.close()
 
 
@@ -64,9 +62,7 @@ def test_baseline_smolvla_matches_reference(tmp_path, monkeypatch):
     assert pol.int8_layers == 298
     f, ins, st, nz, seed, pv, wt, g = smolvla_query(synth.SMOLVLA_BASELINE, "")
     got = pol.predict(f, ins, st, nz, seed)
-    err = np.abs(got - _want("base", 63)).max()
-    print(f"SmolVLA baseline max-abs vs reference: {err:.3g}")
-    assert err <= TOL
+    check_actions("smolvla-base-m63", got, _want("base", 63), TOL)
     assert np.array_equal(got, pol.predict(f, ins, st, nz, seed)), "query is not deterministic"
     pol.close()
 
