@@ -49,6 +49,11 @@ VLA_API int32_t vla_cuda_device_status(void);
 VLA_API int32_t vla_cuda_quantize_act_i8(const float* x, int8_t* xq, float* ascale,
                                          int32_t seq, int32_t K, int64_t ldq, void* stream);
 
+/* replaces tcpu::quantize_span_i8 (src/ops/quant_ops.h:80; gemm_i8.cpp:177-207):
+ * q[i] = rne(clamp(x[i] * inv, -127, 127)) for n elements, one shared scale
+ * (the conv per-tensor quantizer's arithmetic). */
+VLA_API int32_t vla_cuda_quantize_span_i8(const float* x, int8_t* q, int64_t n, float inv, void* stream);
+
 /* replaces tcpu::pack_weights_i8 (src/ops/quant_ops.h:58) in the device layout:
  * W [N][K] fp32 (device) -> Wq [N][ldw] int8 + wscale [N]. Same per-row math as
  * the activation quantizer. */
@@ -195,8 +200,13 @@ VLA_API int32_t vla_cuda_conv_transpose1d(float* out, const float* x, const floa
 VLA_API int32_t vla_tcpu_int8_gemm_available(void);          /* src/ops/quant_ops.h:41 */
 VLA_API int32_t vla_tcpu_i8_kpad(int32_t K);                 /* :45 */
 VLA_API uint64_t vla_tcpu_packed_i8_words(int32_t N, int32_t K); /* :57 */
-/* :58, the reference's CPU panel layout + int32 row sums (load time, host) */
+/* :58, the reference's CPU panel layout + int32 row sums (quantized and packed
+ * on the device, copied back) */
 VLA_API int32_t vla_tcpu_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K);
+/* :64, the row-sum table pack_weights_i8 stores after the panels */
+VLA_API const int32_t* vla_tcpu_i8_rowsums(const int8_t* Wq, int32_t N, int32_t K);
+/* :80, on the device */
+VLA_API int32_t vla_tcpu_quantize_span_i8(const float* x, int8_t* q, uint64_t n, float inv);
 /* :76 */
 VLA_API int32_t vla_tcpu_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int32_t seq, int32_t K);
 /* :83-85, Wq in the panel layout */
@@ -207,6 +217,11 @@ VLA_API int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const
 VLA_API int32_t vla_tcpu_dense_linear_i8(float* out, const float* x, const int8_t* Wq, const float* wscale,
                                          const float* bias, int32_t seq, int32_t N, int32_t K,
                                          int8_t* xq_scratch, float* ascale_scratch);
+/* :90-92, the backend's own reference for the same call: the CUDA-core
+ * (dp4a) kernel with the same epilogue, independent of the tensor-core path */
+VLA_API int32_t vla_tcpu_dense_linear_i8_ref(float* out, const int8_t* xq, const float* ascale,
+                                             const int8_t* Wq, const float* wscale, const float* bias,
+                                             int32_t seq, int32_t N, int32_t K);
 
 /* ------------------------------------------- device-resident ACT stepping
  * For throughput runs: inputs written straight into the handle's device

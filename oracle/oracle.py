@@ -22,6 +22,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 RESTATED_SO = os.path.join(HERE, "_build", "libi8_oracle.so")
 REFERENCE_SO = os.path.join(HERE, "_ref", "libvla_ref.so")
+# the reference's own sources with their int8 op API defined over this
+# repository's library (ref_cuda_backend.cpp): its models run their int8
+# layers on the GPU
+REFERENCE_CUDA_SO = os.path.join(HERE, "_ref", "libvla_ref_cuda.so")
+SERVER_PY = os.path.join(HERE, "_ref", "vla_simd", "policy_server.py")
 
 VP, I32, I64, F32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 
@@ -48,6 +53,9 @@ def build(reference: bool | None = None) -> None:
         if ref is None:
             raise RuntimeError("the reference build needs its sources: set VLA_REF_DIR")
         targets.append("ref")
+        # the reference over this repository's CUDA backend needs the product library
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "vla_simd_b200", "libvla_simd_b200.so")):
+            targets.append("refcuda")
         env["REF"] = ref
     subprocess.run(["make", "-s", "-j8", "-C", HERE, *targets], check=True, env=env)
 
@@ -121,10 +129,13 @@ class Restated:
 
 
 class Reference:
-    def __init__(self):
-        if not os.path.exists(REFERENCE_SO):
-            raise FileNotFoundError(REFERENCE_SO)
-        l = ctypes.CDLL(REFERENCE_SO)
+    def __init__(self, path: str = REFERENCE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        l = ctypes.CDLL(path)
+        self.path = path
+        l.ref_nn_linear_forward.restype = I32
+        l.ref_nn_linear_forward.argtypes = [VP, VP, I32, I32, VP, I32, VP, I32]
         l.ref_int8_gemm_available.restype = I32
         l.ref_i8_kpad.restype = I32
         l.ref_i8_kpad.argtypes = [I32]
@@ -162,6 +173,17 @@ class Reference:
 
     def kpad(self, K):
         return self.l.ref_i8_kpad(K)
+
+    def nn_linear_forward(self, W, bias, x, int8=True):
+        """The reference's nn::Linear (Role::Gemm): init, init_int8 when asked, forward.
+        Returns (out [seq, N], whether the layer took the int8 kernel)."""
+        W = np.ascontiguousarray(W, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        N, K = W.shape
+        out = np.zeros((x.shape[0], N), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        q = self.l.ref_nn_linear_forward(_ptr(W), _ptr(b), N, K, _ptr(x), x.shape[0], _ptr(out), 1 if int8 else 0)
+        return out, bool(q)
 
     def pack_weights_i8(self, W):
         W = np.ascontiguousarray(W, np.float32)
@@ -483,6 +505,14 @@ def reference() -> Reference | None:
     """The compiled reference, or None when oracle/_ref was not built here."""
     try:
         return Reference()
+    except (FileNotFoundError, OSError):
+        return None
+
+
+def reference_cuda() -> Reference | None:
+    """The reference over this repository's CUDA backend, or None when not built."""
+    try:
+        return Reference(REFERENCE_CUDA_SO)
     except (FileNotFoundError, OSError):
         return None
 

@@ -7,6 +7,7 @@
 #include "ops/conv_ops.h"
 #include "ops/lm_ops.h"
 #include "ops/quant_ops.h"
+#include "nn/linear.h"
 
 #include <cstdint>
 #include <vector>
@@ -54,6 +55,18 @@ void ref_maxpool2d_relu(float* out, const float* x, int H, int W, int C, int k, 
     tcpu::maxpool2d_relu(out, x, H, W, C, k, stride, pad);
 }
 void ref_relu(float* x, int n) { tcpu::relu(x, n); }
+
+// The reference's own layer object (src/nn/linear.cpp): init with fp32 W [N][K]
+// as a projection (Role::Gemm), optionally init_int8(), then forward(). Returns
+// 1 when the layer runs on the int8 kernel (init_int8 accepted it), else 0.
+int ref_nn_linear_forward(const float* W, const float* bias, int N, int K, const float* x, int seq, float* out,
+                          int int8) {
+    tcpu::nn::Linear l;
+    l.init(W, bias, N, K, tcpu::nn::Linear::Role::Gemm);
+    const int q = int8 && l.init_int8() ? 1 : 0;
+    l.forward(out, x, seq);
+    return q;
+}
 void ref_dense_linear(float* out, const float* x, const float* W, const float* bias, int seq, int N, int K) {
     tcpu::dense_linear(out, x, W, bias, seq, N, K);
 }

@@ -64,6 +64,7 @@ SIGNATURES = {
     "vla_cuda_i8_ld": (I64, [I32]),
     "vla_cuda_device_status": (I32, []),
     "vla_cuda_quantize_act_i8": (I32, [VP, VP, VP, I32, I32, I64, VP]),
+    "vla_cuda_quantize_span_i8": (I32, [VP, VP, I64, ctypes.c_float, VP]),
     "vla_cuda_pack_weights_i8": (I32, [VP, VP, VP, I32, I32, I64, VP]),
     "vla_cuda_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32, I64, I64, VP]),
     "vla_cuda_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP, VP, VP]),
@@ -95,6 +96,9 @@ SIGNATURES = {
     "vla_tcpu_i8_kpad": (I32, [I32]),
     "vla_tcpu_packed_i8_words": (ctypes.c_uint64, [I32, I32]),
     "vla_tcpu_pack_weights_i8": (I32, [VP, VP, VP, I32, I32]),
+    "vla_tcpu_i8_rowsums": (VP, [VP, I32, I32]),
+    "vla_tcpu_quantize_span_i8": (I32, [VP, VP, ctypes.c_uint64, ctypes.c_float]),
+    "vla_tcpu_dense_linear_i8_ref": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32]),
     "vla_tcpu_quantize_act_i8": (I32, [VP, VP, VP, I32, I32]),
     "vla_tcpu_dense_linear_i8_pre": (I32, [VP, VP, VP, VP, VP, VP, I32, I32, I32]),
     "vla_tcpu_dense_linear_i8": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, VP, VP]),

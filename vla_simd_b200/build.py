@@ -69,7 +69,10 @@ def build(verbose: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=4) as ex:
         objs = list(ex.map(lambda s: _compile(s, dep), CUDA_SOURCES + CXX_SOURCES))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = ["nvcc", *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lcuda"]
+        # -Bsymbolic: the library's own calls bind to its own definitions, so a
+        # process that also loads the reference's library (which exports the
+        # same model ABI names) cannot redirect them
+        cmd = ["nvcc", *ARCH, "-shared", "-cudart", "static", "-Xlinker", "-Bsymbolic", "-o", LIB, *objs, "-lcuda"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             # libcuda.so is only needed for the driver entry point query at

@@ -11,7 +11,6 @@
 #include "bpe_tokenizer.h"
 #include "t5_tokenizer.h"
 #include "gemm_i8.h"
-#include "host_quant.h"
 #include "lm_ops.h"
 #include "nn.h"
 #include "quant.h"
@@ -453,6 +452,11 @@ int32_t vla_cuda_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int3
                                         as_stream(stream)));
 }
 
+int32_t vla_cuda_quantize_span_i8(const float* x, int8_t* q, int64_t n, float inv, void* stream) {
+    if (n < 0 || (n > 0 && (!x || !q))) return VLA_ERR_ARG;
+    return status_of(vsb::quantize_span_i8(x, q, n, inv, as_stream(stream)));
+}
+
 int32_t vla_cuda_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K, int64_t ldw,
                                  void* stream) {
     if (!W || !Wq || !wscale || N <= 0 || K <= 0 || ldw < K) return VLA_ERR_ARG;
@@ -701,21 +705,44 @@ uint64_t vla_tcpu_packed_i8_words(int32_t N, int32_t K) {
 
 int32_t vla_tcpu_pack_weights_i8(const float* W, int8_t* Wq, float* wscale, int32_t N, int32_t K) try {
     if (!W || !Wq || !wscale || N <= 0 || N % 16 || K <= 0) return VLA_ERR_ARG;
-    const int Kp = vla_tcpu_i8_kpad(K), KG = Kp / 4;
-    std::vector<int8_t> rows((size_t)N * K);
-    vsb::quantize_rows_host(W, N, K, rows.data(), K, wscale);
-    std::memset(Wq, 0, (size_t)N * Kp);
-    int32_t* rowsum = reinterpret_cast<int32_t*>(Wq + (size_t)N * Kp);
-    for (int n = 0; n < N; ++n) {
-        int32_t s = 0;
-        for (int k = 0; k < K; ++k) {
-            const int8_t q = rows[(size_t)n * K + k];
-            Wq[((size_t)((n / 16) * KG + k / 4) * 16 + (n % 16)) * 4 + (k % 4)] = q;
-            s += q;
-        }
-        rowsum[n] = s;
-    }
-    return VLA_OK;
+    // quantize and pack on the device, then copy the reference's layout back
+    const int64_t ld = ld16(K);
+    const size_t packed = (size_t)N * vla_tcpu_i8_kpad(K) + sizeof(int32_t) * (size_t)N;
+    void* base = g_ws.get(carve_size({sizeof(float) * (size_t)N * K, (size_t)N * ld, sizeof(float) * N, packed}));
+    if (!base) return VLA_ERR_DEVICE;
+    Carver c{static_cast<char*>(base)};
+    float* dW = c.take<float>((size_t)N * K);
+    int8_t* dq = c.take<int8_t>((size_t)N * ld);
+    float* ds = c.take<float>(N);
+    int8_t* dp = c.take<int8_t>(packed);
+    cudaError_t e = cudaMemcpy(dW, W, sizeof(float) * (size_t)N * K, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = vsb::quantize_rows(dW, K, nullptr, 0, N, K, dq, ld, ds, nullptr, 0, nullptr, 0);
+    if (e == cudaSuccess) e = vsb::pack_panels_i8(dq, ld, N, K, dp, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(Wq, dp, packed, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(wscale, ds, sizeof(float) * N, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && vsb::device_status_take() != 0) e = cudaErrorLaunchFailure;
+    return status_of(e);
+} catch (...) {
+    return VLA_ERR_EXCEPTION;
+}
+
+const int32_t* vla_tcpu_i8_rowsums(const int8_t* Wq, int32_t N, int32_t K) {
+    if (!Wq || N <= 0 || K <= 0) return nullptr;
+    return reinterpret_cast<const int32_t*>(Wq + (size_t)N * vla_tcpu_i8_kpad(K));
+}
+
+int32_t vla_tcpu_quantize_span_i8(const float* x, int8_t* q, uint64_t n, float inv) try {
+    if (n == 0) return VLA_OK;
+    if (!x || !q) return VLA_ERR_ARG;
+    void* base = g_ws.get(carve_size({sizeof(float) * (size_t)n, (size_t)n}));
+    if (!base) return VLA_ERR_DEVICE;
+    Carver c{static_cast<char*>(base)};
+    float* dx = c.take<float>(n);
+    int8_t* dq = c.take<int8_t>(n);
+    cudaError_t e = cudaMemcpy(dx, x, sizeof(float) * n, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = vsb::quantize_span_i8(dx, dq, (long long)n, inv, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(q, dq, n, cudaMemcpyDeviceToHost);
+    return status_of(e);
 } catch (...) {
     return VLA_ERR_EXCEPTION;
 }
@@ -740,9 +767,9 @@ int32_t vla_tcpu_quantize_act_i8(const float* x, int8_t* xq, float* ascale, int3
     return VLA_ERR_EXCEPTION;
 }
 
-int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
-                                     const float* wscale, const float* bias, int32_t seq, int32_t N,
-                                     int32_t K) try {
+static int32_t tcpu_linear_pre(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
+                               const float* wscale, const float* bias, int32_t seq, int32_t N, int32_t K,
+                               int32_t force_simt) try {
     if (!out || !xq || !ascale || !Wq || !wscale || seq <= 0 || N <= 0 || N % 16 || !k_ok(K)) return VLA_ERR_ARG;
     const int64_t ld = ld16(K);
     const int Kp = vla_tcpu_i8_kpad(K);
@@ -766,13 +793,23 @@ int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const float* 
     if (e == cudaSuccess) e = vsb::unpack_panels_i8(dp, N, K, dw, ld, 0);
     if (e != cudaSuccess) return status_of(e);
     const int32_t r = vla_cuda_gemm_i8(dout, N, dq, ld, ds, 1, dw, ld, dws, bias ? db : nullptr, nullptr, 0, seq, N,
-                                       K, 0, nullptr, 1, 0, nullptr);
+                                       K, 0, nullptr, 1, force_simt, nullptr);
     if (r != VLA_OK) return r;
     e = cudaMemcpy(out, dout, sizeof(float) * (size_t)seq * N, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && vsb::device_status_take() != 0) e = cudaErrorLaunchFailure;
     return status_of(e);
 } catch (...) {
     return VLA_ERR_EXCEPTION;
+}
+
+int32_t vla_tcpu_dense_linear_i8_pre(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
+                                     const float* wscale, const float* bias, int32_t seq, int32_t N, int32_t K) {
+    return tcpu_linear_pre(out, xq, ascale, Wq, wscale, bias, seq, N, K, 0);
+}
+
+int32_t vla_tcpu_dense_linear_i8_ref(float* out, const int8_t* xq, const float* ascale, const int8_t* Wq,
+                                     const float* wscale, const float* bias, int32_t seq, int32_t N, int32_t K) {
+    return tcpu_linear_pre(out, xq, ascale, Wq, wscale, bias, seq, N, K, 1);
 }
 
 int32_t vla_tcpu_dense_linear_i8(float* out, const float* x, const int8_t* Wq, const float* wscale, const float* bias,

@@ -3,7 +3,6 @@
 
 #include "f32.h"
 #include "gemm_i8.h"
-#include "host_quant.h"
 #include "quant.h"
 
 #include <climits>
@@ -39,15 +38,22 @@ bool upload_linear(DevLinear& l, const float* W, const float* b, int N, int K, b
     if (b) cudaMemcpy(l.bias, b, sizeof(float) * N, cudaMemcpyHostToDevice);
     else cudaMemset(l.bias, 0, sizeof(float) * N);
     if (l.int8) {
+        // quantized on the device, by the same per-row kernel as the op API's
+        // pack (pack_weights_i8's arithmetic, src/hal/common/gemm_i8.cpp:56-89):
+        // the fp32 weights go up once to a staging buffer freed right after
         l.ldw = round16(K);
-        std::vector<int8_t> q((size_t)N * l.ldw);
-        std::vector<float> s(N);
-        quantize_rows_host(W, N, K, q.data(), l.ldw, s.data());
-        l.Wq = static_cast<int8_t*>(alloc(q.size()));
+        l.Wq = static_cast<int8_t*>(alloc((size_t)N * l.ldw));
         l.wscale = static_cast<float*>(alloc(sizeof(float) * N));
         if (!l.Wq || !l.wscale) return false;
-        cudaMemcpy(l.Wq, q.data(), q.size(), cudaMemcpyHostToDevice);
-        cudaMemcpy(l.wscale, s.data(), sizeof(float) * N, cudaMemcpyHostToDevice);
+        float* staging = nullptr;
+        if (cudaMalloc(&staging, sizeof(float) * (size_t)N * K) != cudaSuccess) return false;
+        cudaError_t e = cudaMemcpy(staging, W, sizeof(float) * (size_t)N * K, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(l.Wq, 0, (size_t)N * l.ldw);
+        if (e == cudaSuccess) e = quantize_rows(staging, K, nullptr, 0, N, K, l.Wq, l.ldw, l.wscale, nullptr, 0,
+                                                nullptr, 0);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+        cudaFree(staging);
+        if (e != cudaSuccess) return false;
         if (n_int8) ++*n_int8;
     } else {
         l.W = static_cast<float*>(alloc(sizeof(float) * (size_t)N * K));
@@ -65,8 +71,7 @@ bool make_dev_conv(DevConv& c, const float* w, const float* b, int cout, int k, 
         // the same int8 weights (quantization is deterministic), re-indexed
         // for the space-to-depth form of the conv
         std::vector<int8_t> wq((size_t)cout * c.lin.ldw), ws2d((size_t)cout * 64 * ((k + 1) / 2));
-        std::vector<float> sc(cout);
-        quantize_rows_host(w, cout, k * k * cin, wq.data(), c.lin.ldw, sc.data());
+        if (cudaMemcpy(wq.data(), c.lin.Wq, wq.size(), cudaMemcpyDeviceToHost) != cudaSuccess) return false;
         s2d_repack_weights_host(wq.data(), cout, k, cin, c.lin.ldw, ws2d.data());
         c.Wq_s2d = static_cast<int8_t*>(alloc(ws2d.size()));
         if (!c.Wq_s2d) return false;

@@ -1,31 +1,9 @@
 #include "host_quant.h"
 
-#include <algorithm>
 #include <cmath>
-#include <cstring>
-#include <limits>
 #include <vector>
 
 namespace vsb {
-
-void quantize_rows_host(const float* W, int N, int K, int8_t* q, long long ldq, float* scale) {
-    for (int n = 0; n < N; ++n) {
-        const float* wr = W + (long long)n * K;
-        float amax = 0.0f;
-        for (int k = 0; k < K; ++k) amax = std::max(amax, std::fabs(wr[k]));
-        // an all-zero row gets scale 1 (its int8 row is zero either way)
-        const float s = amax > 0.0f ? std::max(amax / 127.0f, std::numeric_limits<float>::min()) : 1.0f;
-        const float inv = 1.0f / s;
-        int8_t* qr = q + (long long)n * ldq;
-        std::memset(qr, 0, static_cast<size_t>(ldq));
-        for (int k = 0; k < K; ++k) {
-            long r = std::lrint(wr[k] * inv);   // round to nearest even
-            r = std::min(127L, std::max(-127L, r));
-            qr[k] = static_cast<int8_t>(r);
-        }
-        scale[n] = s;
-    }
-}
 
 void sinusoid_pos_2d_host(int fh, int fw, int dim, float* out) {
     const int half = dim / 2;

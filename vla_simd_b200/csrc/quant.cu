@@ -438,6 +438,67 @@ cudaError_t unpack_panels_i8(const int8_t* panels, int N, int K, int8_t* rows, l
     return cudaGetLastError();
 }
 
+// q[i] = q8_span(x[i], inv): tcpu::quantize_span_i8 over a flat span.
+__global__ void quantize_span_kernel(const float* __restrict__ x, int8_t* __restrict__ q, long long n, float inv) {
+    pdl_wait();
+    pdl_trigger();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        q[i] = q8_span(x[i], inv);
+}
+
+cudaError_t quantize_span_i8(const float* x, int8_t* q, long long n, float inv, cudaStream_t st) {
+    if (n < 0) return cudaErrorInvalidValue;
+    if (n == 0) return cudaSuccess;
+    long long blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    {
+        const cudaError_t le_ = launch_k(quantize_span_kernel, (int)blocks, 256, 0, st, x, q, n, inv);
+        if (le_ != cudaSuccess) return le_;
+    }
+    return cudaGetLastError();
+}
+
+// Device rows [N][ldw] -> the reference's CPU panel layout [N/16][Kp/4][16][4]
+// followed by the int32 row sums (src/hal/common/gemm_i8.cpp:30-43, :79-89):
+// thread = one 4-byte group (n, k/4) of the panels; group k/4 == 0 also sums
+// its row (the row sums are exact integer adds in any order).
+__global__ void pack_panels_kernel(const int8_t* __restrict__ rows, long long ldw, int N, int K,
+                                   int8_t* __restrict__ panels) {
+    pdl_wait();
+    pdl_trigger();
+    const int Kp = (K + 3) & ~3, KG = Kp / 4;
+    const long long groups = (long long)N * KG;
+    int32_t* rowsum = reinterpret_cast<int32_t*>(panels + (long long)N * Kp);
+    for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < groups;
+         g += (long long)gridDim.x * blockDim.x) {
+        const int n = static_cast<int>(g / KG), kg = static_cast<int>(g - (long long)n * KG);
+        const int8_t* r = rows + (long long)n * ldw;
+        char4 v;
+        v.x = 4 * kg + 0 < K ? r[4 * kg + 0] : 0;
+        v.y = 4 * kg + 1 < K ? r[4 * kg + 1] : 0;
+        v.z = 4 * kg + 2 < K ? r[4 * kg + 2] : 0;
+        v.w = 4 * kg + 3 < K ? r[4 * kg + 3] : 0;
+        *reinterpret_cast<char4*>(panels + ((long long)((n / 16) * KG + kg) * 16 + (n % 16)) * 4) = v;
+        if (kg == 0) {
+            int32_t sum = 0;
+            for (int k = 0; k < K; ++k) sum += r[k];
+            rowsum[n] = sum;
+        }
+    }
+}
+
+cudaError_t pack_panels_i8(const int8_t* rows, long long ldw, int N, int K, int8_t* panels, cudaStream_t st) {
+    if (N <= 0 || K <= 0 || N % 16 || ldw < K || (reinterpret_cast<uintptr_t>(panels) & 3)) return cudaErrorInvalidValue;
+    const long long groups = (long long)N * ((K + 3) / 4);
+    long long blocks = (groups + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    {
+        const cudaError_t le_ = launch_k(pack_panels_kernel, (int)blocks, 256, 0, st, rows, ldw, N, K, panels);
+        if (le_ != cudaSuccess) return le_;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t quantize_rows(const float* x, long long ldx, const float* addend, long long ld_add, int M, int K,
                           int8_t* q, long long ldq, float* scale, int8_t* q2, long long ldq2, float* scale2,
                           cudaStream_t st) {

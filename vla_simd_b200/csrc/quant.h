@@ -45,5 +45,10 @@ cudaError_t absmax_slots(const float* x, long long n, long long per_slot, unsign
 
 // Reference CPU panel layout [N/16][Kp/4][16][4] -> device rows [N][ldw].
 cudaError_t unpack_panels_i8(const int8_t* panels, int N, int K, int8_t* rows, long long ldw, cudaStream_t st);
+// q[i] = rne(clamp(x[i] * inv, +-127)) over n elements (tcpu::quantize_span_i8).
+cudaError_t quantize_span_i8(const float* x, int8_t* q, long long n, float inv, cudaStream_t st);
+// The inverse: device rows [N][ldw] -> panels [N/16][Kp/4][16][4] + int32 row
+// sums [N] right after them (the reference's pack_weights_i8 output layout).
+cudaError_t pack_panels_i8(const int8_t* rows, long long ldw, int N, int K, int8_t* panels, cudaStream_t st);
 
 }  // namespace vsb
