@@ -146,6 +146,27 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def cpu_model():
+    """The host CPU as lscpu names it: model name, physical cores (core ids per
+    socket), logical CPUs this process may use."""
+    model, cores = None, set()
+    try:
+        phys = None
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k, v = k.strip(), v.strip()
+                if k == "model name" and model is None:
+                    model = v
+                elif k == "physical id":
+                    phys = v
+                elif k == "core id":
+                    cores.add((phys, v))
+    except OSError:
+        pass
+    return {"model": model or "unknown", "physical_cores": len(cores) or None, "logical_cpus": cpu_cores()}
+
+
 # ----------------------------------------------------------------- CPU side
 
 _CPU_CHILD = r"""
@@ -178,9 +199,9 @@ print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * fl
 """
 
 
-def time_reference_cpu(ckpt: str, budget_s: float, max_steps: int):
-    """The reference's own ACT step (oracle/_ref) in a fresh process with all host cores."""
-    cores = cpu_cores()
+def time_reference_cpu(ckpt: str, budget_s: float, max_steps: int, threads: int | None = None):
+    """The reference's own ACT step (oracle/_ref) in a fresh process with all host cores (or `threads`)."""
+    cores = threads or cpu_cores()
     env = dict(os.environ, ACT_INT8=str(INT8_MASK), OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close",
                CUDA_VISIBLE_DEVICES="")
     code = _CPU_CHILD % {"root": ROOT, "kind": "reference", "budget": budget_s, "max_steps": max_steps,
@@ -423,9 +444,10 @@ def run_ours(args):
            "path": "vla_act_predict (C ABI), host uint8 frames + state -> host actions"}
 
     gemm = time_gemm(torch, dev) if rank == 0 else None
-    cpu = None
+    cpu = cpu1 = None
     if rank == 0 and not args.no_cpu_baseline:
         cpu = time_reference_cpu(ckpt, budget_s=args.cpu_budget, max_steps=40)
+        cpu1 = time_reference_cpu(ckpt, budget_s=min(args.cpu_budget, 8.0), max_steps=12, threads=1)
     pol.close()
     if dist:
         dist.barrier()
@@ -449,7 +471,11 @@ def run_ours(args):
         cpu_baseline = {"value": round(cpu["chunks_per_s"], 3), "unit": "chunks/s", "cores": cpu["cores"],
                         "kind": "reference", "p50_ms": round(cpu["p50_ms"], 2),
                         "sample": f"{cpu['steps']} ACT steps (same checkpoint, ACT_INT8=63) of the reference's "
-                                  f"own vla_act_predict, OMP_NUM_THREADS={cpu['cores']}"}
+                                  f"own vla_act_predict, OMP_NUM_THREADS={cpu['cores']}, OMP_PROC_BIND=close",
+                        "cpu": cpu_model()}
+        if cpu1 and "unavailable" not in cpu1:
+            cpu_baseline["one_thread"] = {"value": round(cpu1["chunks_per_s"], 3), "p50_ms": round(cpu1["p50_ms"], 2),
+                                          "steps": cpu1["steps"], "sample": "OMP_NUM_THREADS=1"}
     elif cpu:
         cpu_baseline = {"unavailable": cpu["unavailable"]}
     line = {
@@ -942,7 +968,7 @@ def run_reference(args):
         "config": {"workload": "ACT policy step, BASELINE configs[1] (same checkpoint and inputs as ours)",
                    "int8_mask": INT8_MASK, "parallelism": "CPU, OpenMP over all host cores"},
         "cpu_baseline": {"value": round(v, 3), "unit": "chunks/s", "cores": cpu["cores"], "kind": "reference",
-                         "sample": f"{cpu['steps']} steps of vla_act_predict from oracle/_ref"},
+                         "sample": f"{cpu['steps']} steps of vla_act_predict from oracle/_ref", "cpu": cpu_model()},
         "e2e": {"value": round(v, 3), "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "latency_ms": {"p50": round(cpu["p50_ms"], 3)},
     }), flush=True)
