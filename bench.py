@@ -445,7 +445,7 @@ def run_ours(args):
 
     gemm = time_gemm(torch, dev) if rank == 0 else None
     cpu = cpu1 = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_cpu(ckpt, budget_s=args.cpu_budget, max_steps=40)
         cpu1 = time_reference_cpu(ckpt, budget_s=min(args.cpu_budget, 8.0), max_steps=12, threads=1)
     pol.close()
@@ -609,7 +609,7 @@ def run_dp(args):
            "d2h_bytes_per_step": B * pol.chunk * pol.action_dim * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
            "path": "vla_diffusion_predict_batch (C ABI), host frames + state + noise -> host actions"}
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_dp_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
     pol.close()
     if dist:
@@ -779,7 +779,7 @@ def run_octo(args):
            "d2h_bytes_per_step": B * sh.flat * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
            "path": "vla_octo_predict_batch (C ABI), host frames + masks + noise -> host actions"}
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_octo_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
     pol.close()
     if dist:
@@ -891,7 +891,7 @@ def run_smolvla(args):
     value = job_value(n * B, world, total)
     kernels = pol.kernels_per_step
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_generic(_SMOLVLA_CPU_CHILD, ckpt, "SMOLVLA_INT8", SMOLVLA_MASK, args.cpu_budget, 10)
     pol.close()
     if dist:
