@@ -55,22 +55,55 @@ def test_rope_neox(dev, reference, seq, heads, hd, base):
 
 
 @pytest.mark.parametrize("name", ["relu", "silu_gate", "gelu_tanh", "gelu_erf", "mish", "silu"])
-@pytest.mark.parametrize("n", [1003, 4096])
+@pytest.mark.parametrize("n", [1003, 4096, 7])
 def test_activations(dev, reference, name, n):
+    """Bit-identical to the reference: its 8-lane bodies (Cephes exp) and, past
+    them, its scalar forms with the C library's float functions (restated);
+    silu is that scalar form everywhere. gelu_erf's tail stays within tolerance."""
     from vla_simd_b200 import ops
     rng = np.random.default_rng(n)
     x = (rng.standard_normal(n) * 4).astype(np.float32)
-    x[:8] = [0.0, -0.0, 25.0, -25.0, 90.0, -90.0, 1e-30, -1e-30]   # saturation, exp clamps, denormal range
+    specials = np.array([0.0, -0.0, 25.0, -25.0, 90.0, -90.0, 1e-30, -1e-30, 21.0, 19.9, -0.3, 1e-8],
+                        np.float32)
+    x[:min(n, 8)] = specials[:min(n, 8)]           # saturation, exp clamps, denormal range
+    x[-min(n, 4):] = specials[8:8 + min(n, 4)]     # and the scalar tail's branches
     u = rng.standard_normal(n).astype(np.float32)
     got = ops.activation(name, _t(x, dev), _t(u, dev) if name == "silu_gate" else None).cpu().numpy()
     want = reference.activation(name, x, u if name == "silu_gate" else None)
-    if name == "silu":
-        # the reference's silu is a scalar libm loop
-        assert np.allclose(got, want, rtol=2e-6, atol=2e-6)
+    if name == "gelu_erf":
+        body = n - n % 8
+        assert np.array_equal(_bits(got[:body]), _bits(want[:body])), name
+        assert np.allclose(got[body:], want[body:], rtol=2e-6, atol=2e-6)
         return
-    body = n - n % 8
-    assert np.array_equal(_bits(got[:body]), _bits(want[:body])), name
-    assert np.allclose(got[body:], want[body:], rtol=2e-6, atol=2e-6)
+    assert np.array_equal(_bits(got), _bits(want)), name
+
+
+def test_silu_libm_exp_on_many_inputs(dev, reference):
+    """silu = x / (1 + expf(-x)) over 2^22 inputs spread across the float range
+    (the restated expf on the device against the host library's)."""
+    from vla_simd_b200 import ops
+    rng = np.random.default_rng(11)
+    bits = rng.integers(0, 2**32, 1 << 22, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32).copy()
+    x[~np.isfinite(x)] = 1.0
+    x = np.concatenate([x, np.linspace(-100, 100, 1 << 20, dtype=np.float32)])
+    got = ops.activation("silu", _t(x, dev)).cpu().numpy()
+    want = reference.activation("silu", x)
+    same = (_bits(got) == _bits(want)) | (np.isnan(got) & np.isnan(want))
+    assert same.all(), x[~same][:5]
+
+
+def test_mish_tail_libm_on_many_inputs(dev, reference):
+    """The scalar Mish tail (expf, log1pf, tanhf restated) on 7-element calls,
+    where every element is past the 8-lane loop."""
+    from vla_simd_b200 import ops
+    rng = np.random.default_rng(12)
+    vals = np.concatenate([rng.standard_normal(700) * 8, np.linspace(-30, 30, 700)]).astype(np.float32)
+    for i in range(0, len(vals), 7):
+        x = vals[i:i + 7]
+        got = ops.activation("mish", _t(x, dev)).cpu().numpy()
+        want = reference.activation("mish", x)
+        assert np.array_equal(_bits(got), _bits(want)), x
 
 
 @pytest.mark.parametrize("P,C,groups,relu", [(100, 512, 8, False), (1764, 64, 8, True), (16, 2048, 32, False)])

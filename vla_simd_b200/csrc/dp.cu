@@ -10,6 +10,7 @@
 #include "sm100.cuh"
 #include "launch.cuh"
 #include "dp.h"
+#include "libm_f32.h"   // glibc's float expf / log1pf / expm1f / tanhf, restated
 
 namespace vsb {
 
@@ -23,42 +24,8 @@ __device__ __forceinline__ float mish_lanes(float v) {
     return __fmul_rn(v, __fdiv_rn(m, __fadd_rn(m, 2.0f)));
 }
 
-// The host C library's expf (glibc 2.39 on x86-64, the build the reference
-// links), restated from its published algorithm (ARM optimized-routines expf):
-// x*32/ln2 = k + r rounded with the 1.5*2^52 shift, exp(x) = 2^(k/32) *
-// (1 + c2 r + c1 r^2 + c0 r^3) in double, the 2^(i/32) table entries the
-// correctly rounded doubles with the exponent bits of i/32 removed, and the
-// fused multiply-adds of its FMA build. Identical to that expf on every
-// float (checked over all 2^32 inputs against the host library); the
-// spatial softmax needs it because its output feeds int8 quantizers, where
-// one ulp can move a rounding decision.
-__constant__ unsigned long long kExp2Tab32[32] = {
-    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
-    0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
-    0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
-    0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL,
-    0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL,
-    0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
-    0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
-    0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
-
-__device__ __forceinline__ float libm_expf(float x) {
-    if (x != x) return x + x;
-    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   // overflow: +inf
-    if (x < -0x1.9fe368p6f) return 0.0f;                        // underflow
-    const double xd = static_cast<double>(x);
-    const double inv_ln2_32 = 0x1.71547652b82fep+5, shift = 0x1.8p+52;
-    double kd = __fma_rn(inv_ln2_32, xd, shift);
-    const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
-    kd = __dsub_rn(kd, shift);
-    const double r = __fma_rn(inv_ln2_32, xd, -kd);
-    const double s = __longlong_as_double(static_cast<long long>(kExp2Tab32[ki & 31] + (ki << 47)));
-    const double z = __fma_rn(0x1.c6af84b912394p-20, r, 0x1.ebfce50fac4f3p-13);
-    const double r2 = __dmul_rn(r, r);
-    double y = __fma_rn(0x1.62e42ff0c52d6p-6, r, 1.0);
-    y = __fma_rn(z, r2, y);
-    return __double2float_rn(__dmul_rn(y, s));
-}
+// the host library's expf (libm_f32.h: bit-identical to it on all 2^32 inputs)
+__device__ __forceinline__ float libm_expf(float x) { return lf_expf(x); }
 
 __device__ __forceinline__ float block_max_256(float v, float* sh) {
     v = warp_max_f(v);
@@ -884,6 +851,26 @@ cudaError_t dp_cond_input(const float* stepfeat, int n_steps, int D, const float
         return cudaErrorInvalidValue;
     const cudaError_t e = launch_k(dp_cond_input_kernel, (unsigned)grid_cap((long long)n_steps * B * CD, 256, 148 * 4),
                                    256, 0, st, stepfeat, n_steps, D, gcond, tail, B, CD, gm);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// The scalar tail of the reference's Mish over the conditioning vector (the
+// last cond_dim % 8 entries its 8-lane loop leaves, src/hal/common/eltwise.cpp:244-248),
+// with the host library's float functions restated: tail[b][i] =
+// mish(gcond[b][G - n + i]).
+__global__ void dp_mish_tail_kernel(const float* __restrict__ gcond, int G, int n, int B, float* __restrict__ tail) {
+    pdl_wait();     // gcond comes from the previous kernel
+    pdl_trigger();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * n) return;
+    const int b = i / n, j = i - b * n;
+    tail[i] = lf_mish(gcond[(long long)b * G + (G - n) + j]);
+}
+
+cudaError_t dp_mish_tail(const float* gcond, int G, int n, int B, float* tail, cudaStream_t st) {
+    if (n <= 0 || n > G || B <= 0) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(dp_mish_tail_kernel, (unsigned)((B * n + 127) / 128), 128, 0, st, gcond, G, n, B, tail);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

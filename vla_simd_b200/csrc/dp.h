@@ -70,6 +70,9 @@ cudaError_t im2col1d_q8w(const float* x, int F, int T, int C, int k, int stride,
 // the cond encoder input of every denoising step (src/models/diffusion/unet1d.cpp:234-249).
 // The last CD % 8 elements of each row are taken from tail [B][CD % 8]
 // (mish's scalar libm tail, computed by the caller).
+// tail[b][i] = the reference's scalar Mish of gcond[b][G - n + i] (the host
+// library's expf / log1pf / tanhf restated), b < B, i < n.
+cudaError_t dp_mish_tail(const float* gcond, int G, int n, int B, float* tail, cudaStream_t st);
 cudaError_t dp_cond_input(const float* stepfeat, int n_steps, int D, const float* gcond, const float* tail, int B,
                           int CD, float* gm, cudaStream_t st);
 

@@ -82,20 +82,7 @@ DpPolicy::~DpPolicy() {
     for (void* p : allocs_) cudaFree(p);
     if (h_pinned_) cudaFreeHost(h_pinned_);
     if (h_status_pinned_) cudaFreeHost(h_status_pinned_);
-    if (h_tail_in_) cudaFreeHost(h_tail_in_);
-    if (h_tail_out_) cudaFreeHost(h_tail_out_);
     cudaSetDevice(prev);
-}
-
-// mish's scalar tail as the reference computes it (src/hal/common/eltwise.cpp:244-248),
-// on the host libm the reference calls: v * tanh(log1p(exp(v))), identity softplus above 20.
-void DpPolicy::mish_tail_host(void* p) {
-    const TailCtx* c = static_cast<const TailCtx*>(p);
-    for (int i = 0; i < c->n; ++i) {
-        const float v = c->in[i];
-        const float sp = v > 20.0f ? v : std::log1p(std::exp(v));
-        c->out[i] = v * std::tanh(sp);
-    }
 }
 
 // diffusion.meta as DiffusionModel::load reads it (src/models/diffusion/diffusion_model.cpp:25-103).
@@ -704,15 +691,7 @@ bool DpPolicy::load(const std::string& dir, int max_batch) {
     if (!d_status_) { fail("device status word"); return false; }
     tail_n_ = cfg_.cond_dim() % 8;
     if (tail_n_) {
-        const size_t nt = (size_t)max_batch_ * tail_n_;
-        if (cudaMallocHost(&h_tail_in_, sizeof(float) * nt) != cudaSuccess ||
-            cudaMallocHost(&h_tail_out_, sizeof(float) * nt) != cudaSuccess) {
-            fail("pinned host buffers");
-            return false;
-        }
-        d_tail_ = dalloc<float>(nt);
-        tail_ctx_.resize(max_batch_);
-        for (int b = 0; b < max_batch_; ++b) tail_ctx_[b] = TailCtx{h_tail_in_, h_tail_out_, (b + 1) * tail_n_};
+        d_tail_ = dalloc<float>((size_t)max_batch_ * tail_n_);
         if (!d_tail_) return false;
     }
     graphs_.assign((size_t)max_batch_ * 2, nullptr);
@@ -1025,12 +1004,8 @@ cudaError_t DpPolicy::forward(int B, cudaStream_t st, bool unnormalize) {
     }
     const int steps = num_steps(), CD = c.cond_dim(), D = c.step_embed_dim;
     if (tail_n_) {
-        // the cond input's libm tail: these gcond entries to the host, mish there, back
-        const int G = c.global_cond_dim();
-        VSB_TRY(cudaMemcpy2DAsync(h_tail_in_, sizeof(float) * tail_n_, d_gcond_ + (G - tail_n_), sizeof(float) * G,
-                                  sizeof(float) * tail_n_, B, cudaMemcpyDeviceToHost, st));
-        VSB_TRY(cudaLaunchHostFunc(st, &DpPolicy::mish_tail_host, &tail_ctx_[B - 1]));
-        VSB_TRY(cudaMemcpyAsync(d_tail_, h_tail_out_, sizeof(float) * B * tail_n_, cudaMemcpyHostToDevice, st));
+        // the cond input's scalar Mish tail, with the host library's functions restated on the device
+        VSB_TRY(dp_mish_tail(d_gcond_, c.global_cond_dim(), tail_n_, B, d_tail_, st));
     }
     VSB_TRY(dp_cond_input(d_stepfeat_, steps, D, d_gcond_, d_tail_, B, CD, d_gm_, st));
     VSB_TRY(linear_f32(d_gm_, CD, cond_all_.W, cond_all_.bias, d_film_, film_cols_, steps * B, (int)film_cols_, CD,

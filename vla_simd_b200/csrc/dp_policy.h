@@ -226,18 +226,12 @@ class DpPolicy {
     int8_t *d_q_ = nullptr, *d_q2_ = nullptr;
     float *d_qs_ = nullptr, *d_qs2_ = nullptr;
 
-    // Mish's scalar libm tail of the cond input (CD % 8 values per query, all
-    // from the global conditioning): evaluated by a host function inside the
-    // step with the host's libm, which the reference's values depend on.
-    struct TailCtx {
-        const float* in = nullptr;
-        float* out = nullptr;
-        int n = 0;
-    };
-    static void mish_tail_host(void* ctx);
+    // Mish's scalar tail of the cond input (CD % 8 values per query, all from
+    // the global conditioning), computed on the device with the host C
+    // library's float functions restated (libm_f32.h), which the reference's
+    // values depend on.
     int tail_n_ = 0;
-    float *h_tail_in_ = nullptr, *h_tail_out_ = nullptr, *d_tail_ = nullptr;
-    std::vector<TailCtx> tail_ctx_;   // one per batch size (captured graphs keep their pointer)
+    float* d_tail_ = nullptr;
 
     int debug_stage_ = -1;
     float* d_debug_ = nullptr;

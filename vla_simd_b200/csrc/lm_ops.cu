@@ -5,11 +5,16 @@
 //     sequential double sum, the SIMD bodies of the activations with their
 //     Cephes exp, GroupNorm's per-channel sweeps, conv_transpose1d's fixed
 //     accumulation order, im2col1d) the results are the reference's bits;
-//   - where the reference calls libm (the scalar tails of the activations,
-//     silu, spatial_softmax's expf, RoPE's double sin/cos) the device's own
-//     functions stand in and results agree to the reference tests' tolerances.
+//   - where the reference calls the C library's float functions (silu, and
+//     the scalar tails of silu_gate / gelu_tanh / mish past its 8-lane loops)
+//     they are glibc's expf / tanhf / log1pf restated (libm_f32.h, bit-equal
+//     to the host library on all 2^32 inputs), so those results are the
+//     reference's bits too;
+//   - spatial_softmax's expf and RoPE's double sin/cos use the device's own
+//     functions and agree to the reference tests' tolerances.
 // Compiled into kernels.cu after nn.cu (ref_exp, the reference's Cephes exp).
 #include "lm_ops.h"
+#include "libm_f32.h"
 
 namespace vsb {
 
@@ -82,20 +87,28 @@ cudaError_t rope_neox(float* x, const int* pos, int seq, int n_heads, int head_d
 // -------------------------------------------------------------- activations
 // The reference's SIMD bodies (src/hal/common/eltwise.cpp), element by
 // element: IEEE divisions, its fma contractions and its Cephes exp.
-__device__ __forceinline__ float act_eval(int kind, float v, float u) {
+// `tail`: the element lies past the reference's 8-lane loop, where it runs
+// its scalar form with the C library's float functions (eltwise.cpp:52-53,
+// :92-93, :244-248); silu is that scalar form everywhere (:67-73).
+__device__ __forceinline__ float act_eval(int kind, float v, float u, bool tail) {
     switch (kind) {
         case kActRelu:   // :209-214
             return v < 0.0f ? 0.0f : v;
         case kActSiluGate: {   // :29-47 x / (1 + exp(0 - x)) * u
-            const float e = ref_exp(__fsub_rn(0.0f, v));
+            const float e = tail ? lf_expf(-v) : ref_exp(__fsub_rn(0.0f, v));
             return __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, e)), u);
         }
-        case kActSilu: {   // :67-73 (a libm exp in the reference: tolerance class)
-            const float e = ref_exp(__fsub_rn(0.0f, v));
-            return __fdiv_rn(v, __fadd_rn(1.0f, e));
+        case kActSilu: {   // :67-73 x / (1 + expf(-x))
+            return __fdiv_rn(v, __fadd_rn(1.0f, lf_expf(-v)));
         }
-        case kActGeluTanh: {   // :75-91 v * sigmoid(2c (v + 0.044715 v^3))
+        case kActGeluTanh: {
             const float c = 0.7978845608028654f;
+            if (tail) {   // :92-93 0.5 v (1 + tanhf(c (v + 0.044715 v^3))), the add contracted
+                const float a = __fmul_rn(__fmul_rn(0.044715f, v), v);
+                const float t = lf_tanhf(__fmul_rn(c, __fmaf_rn(a, v, v)));
+                return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, t));
+            }
+            // :75-91 v * sigmoid(2c (v + 0.044715 v^3))
             const float v3 = __fmul_rn(__fmul_rn(v, v), v);
             const float y = __fmul_rn(2.0f * c, __fmaf_rn(0.044715f, v3, v));
             const float e = ref_exp(__fsub_rn(0.0f, y));
@@ -116,7 +129,9 @@ __device__ __forceinline__ float act_eval(int kind, float v, float u) {
             const float erf = __int_as_float(__float_as_int(erf_abs) | (__float_as_int(v) & 0x80000000));
             return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, erf));
         }
-        default: {   // kActMish, :224-243: v * tanh(softplus(v)) = v * m / (m + 2), m = e(e + 2)
+        default: {   // kActMish
+            if (tail) return lf_mish(v);   // :244-248 v * tanhf(log1pf(expf(v))), identity softplus above 20
+            // :224-243: v * tanh(softplus(v)) = v * m / (m + 2), m = e(e + 2)
             const float e = ref_exp(fminf(v, 20.0f));
             const float m = __fmul_rn(e, __fadd_rn(e, 2.0f));
             return __fmul_rn(v, __fdiv_rn(m, __fadd_rn(m, 2.0f)));
@@ -129,8 +144,9 @@ __global__ void activation_kernel(int kind, float* out, const float* x, const fl
     // read, then written, by the same thread
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
+    const long long body = n - n % 8;   // the reference's 8-lane loop covers [0, body)
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        out[i] = act_eval(kind, x[i], u ? u[i] : 0.0f);
+        out[i] = act_eval(kind, x[i], u ? u[i] : 0.0f, i >= body);
 }
 
 cudaError_t activation(int kind, float* out, const float* x, const float* u, long long n, cudaStream_t st) {

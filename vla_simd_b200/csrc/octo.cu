@@ -312,7 +312,7 @@ __global__ void silu_exact_kernel(float* __restrict__ x, long long n) {
 // back, then quantize_act_i8 of the row (the scale and codes of quantize_rows):
 // the activation and the next W8A8 layer's input quantization in one pass.
 __device__ __forceinline__ float act_any(int kind, float v) {
-    return kind == kActSiluLibm ? __fdiv_rn(v, __fadd_rn(1.0f, libm_expf(-v))) : act_eval(kind, v, 0.0f);
+    return kind == kActSiluLibm ? __fdiv_rn(v, __fadd_rn(1.0f, libm_expf(-v))) : act_eval(kind, v, 0.0f, false);
 }
 
 __global__ void __launch_bounds__(256) act_rows_q_kernel(int kind, float* __restrict__ x, int K, int keep,

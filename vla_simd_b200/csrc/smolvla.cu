@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(256) silu_gate_rows_kernel(const float* __rest
     const float* g = gu + row * 2 * F;
     float m = 0.0f;
     for (int k = threadIdx.x; k < F; k += 256) {
-        const float v = act_eval(kActSiluGate, g[k], g[F + k]);
+        const float v = act_eval(kActSiluGate, g[k], g[F + k], false);
         if (q) grow[k] = v;
         if (out) out[row * F + k] = v;
         m = fmaxf(m, fabsf(v));
