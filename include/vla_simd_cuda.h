@@ -134,6 +134,15 @@ VLA_API int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* 
                                        int32_t seq_q, int32_t seq_k, int32_t n_q, int32_t n_kv,
                                        int32_t head_dim, float scale, const float* mask, void* stream);
 
+/* The same attention on the tensor cores (tcgen05 kind::tf32, QK^T and PV each
+ * as three split-precision MMAs, online softmax): fp32-level accuracy but not
+ * the reference's summation order, so not bit-identical. The policies use it
+ * only when VLA_ATT_TC=1 is set before they load. Same arguments and rules
+ * (additive mask, fully blocked row -> mean of V). */
+VLA_API int32_t vla_cuda_gqa_attention_tc(float* out, const float* Q, const float* K, const float* V,
+                                          int32_t seq_q, int32_t seq_k, int32_t n_q, int32_t n_kv,
+                                          int32_t head_dim, float scale, const float* mask, void* stream);
+
 /* replaces tcpu::dense_linear (src/ops/lm_ops.h, src/hal/avx2/gemm.cpp:98-122) for
  * the small fp32 layers a policy keeps out of int8 (ACT's state projection and
  * action head), in the reference's exact summation order:

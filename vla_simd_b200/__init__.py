@@ -77,6 +77,7 @@ SIGNATURES = {
                                  VP, VP, VP]),
     "vla_cuda_layernorm": (I32, [VP, VP, VP, VP, I32, I32, F32, VP]),
     "vla_cuda_gqa_attention": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP, VP]),
+    "vla_cuda_gqa_attention_tc": (I32, [VP, VP, VP, VP, I32, I32, I32, I32, I32, F32, VP, VP]),
     "vla_cuda_maxpool2d_relu": (I32, [VP, VP, I32, I32, I32, I32, I32, I32, I32, VP]),
     "vla_cuda_rmsnorm": (I32, [VP, VP, VP, I32, I32, F32, VP]),
     "vla_cuda_rope_neox": (I32, [VP, VP, I32, I32, I32, F32, VP]),

@@ -610,6 +610,19 @@ int32_t vla_cuda_gqa_attention(float* out, const float* Q, const float* K, const
                                     n_kv, head_dim, scale, mask, as_stream(stream)));
 }
 
+int32_t vla_cuda_gqa_attention_tc(float* out, const float* Q, const float* K, const float* V, int32_t seq_q,
+                                  int32_t seq_k, int32_t n_q, int32_t n_kv, int32_t head_dim, float scale,
+                                  const float* mask, void* stream) {
+    if (!out || !Q || !K || !V || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv || head_dim != 64)
+        return VLA_ERR_ARG;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+                        reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(out);
+    if (a & 15) return VLA_ERR_ARG;
+    return status_of(vsb::attention_tc(Q, (long long)n_q * head_dim, K, (long long)n_kv * head_dim, V,
+                                       (long long)n_kv * head_dim, out, (long long)n_q * head_dim, seq_q, seq_k, n_q,
+                                       n_kv, scale, mask, vsb::AttBatch{}, as_stream(stream)));
+}
+
 int32_t vla_cuda_dense_linear_f32(float* out, const float* x, const float* W, const float* bias, int32_t seq,
                                   int32_t N, int32_t K, void* stream) {
     if (!out || !x || !W || seq <= 0 || N <= 0 || K <= 0) return VLA_ERR_ARG;

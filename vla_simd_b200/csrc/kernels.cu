@@ -4,6 +4,7 @@
 #include "gemm_i8.cu"
 #include "quant.cu"
 #include "nn.cu"
+#include "attn_tc.cu"
 #include "f32.cu"
 #include "lm_ops.cu"
 #include "dp.cu"

@@ -892,6 +892,8 @@ cudaError_t attention_batched(const float* Q, long long ldq, const float* K, lon
         ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V) |
           reinterpret_cast<uintptr_t>(O)) & 15))
         return cudaErrorInvalidValue;
+    if (attention_tc_enabled())
+        return attention_tc(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
     const size_t ss = (size_t)att_row_stride(seq_k);
     auto need = [&](int qt) { return sizeof(float) * (qt * ss + (size_t)kAttD * qt + (size_t)kAttKT * kAttD); };
     // Register-tiled kernel: the query tile (8, 16 or 40 rows) that gives the

@@ -28,6 +28,14 @@ cudaError_t attention_batched(const float* Q, long long ldq, const float* K, lon
                               long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
                               int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st);
 
+// The tensor-core attention (attn_tc.cu): 3xTF32 tcgen05 MMAs for QK^T and PV,
+// online softmax. Not bit-identical to the reference; attention_batched routes
+// to it only when VLA_ATT_TC=1 (read once).
+bool attention_tc_enabled();
+cudaError_t attention_tc(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
+                         float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, float scale,
+                         const float* mask, const AttBatch& bs, cudaStream_t st);
+
 cudaError_t maxpool_relu(const float* x, float* out, int F, int H, int W, int C, int k, int stride, int pad,
                          int Ho, int Wo, unsigned int* amax, cudaStream_t st);
 

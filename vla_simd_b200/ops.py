@@ -116,6 +116,16 @@ def gqa_attention(Q, K, V, n_q, n_kv, scale, mask=None, head_dim=64):
     return out
 
 
+def gqa_attention_tc(Q, K, V, n_q, n_kv, scale, mask=None, head_dim=64):
+    """The tensor-core (3xTF32 tcgen05) attention: same contract, not bit-identical."""
+    seq_q, seq_k = Q.shape[0], K.shape[0]
+    out = torch.empty((seq_q, n_q * head_dim), dtype=torch.float32, device=Q.device)
+    check(lib().vla_cuda_gqa_attention_tc(_p(out), _p(Q.contiguous()), _p(K.contiguous()), _p(V.contiguous()),
+                                          seq_q, seq_k, n_q, n_kv, head_dim, scale, _p(mask), _stream()),
+          "vla_cuda_gqa_attention_tc")
+    return out
+
+
 def maxpool2d_relu(x, k=3, stride=2, pad=1):
     F, H, W, C = x.shape
     Ho, Wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
