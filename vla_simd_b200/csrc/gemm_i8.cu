@@ -1047,6 +1047,24 @@ bool make_tmap_f32_out(CUtensorMap* map, const void* base, int rows, int cols, l
     return r == CUDA_SUCCESS;
 }
 
+// fp32 NHWC output [F][Ho][Wo][C] map for TMA stores: box {32 channels, 32
+// pixels, 1, 1} with the 128-byte swizzle (the same staging tile layout).
+bool make_tmap_f32_nhwc_out(CUtensorMap* map, const void* base, int F, int Ho, int Wo, int C) {
+    auto fn = get_encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (C & 3) || F <= 0 || Ho <= 0 || Wo <= 0 || C <= 0) return false;
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(Wo), static_cast<cuuint64_t>(Ho),
+                                static_cast<cuuint64_t>(F)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 4, static_cast<cuuint64_t>(Wo) * C * 4,
+                                   static_cast<cuuint64_t>(Ho) * Wo * C * 4};
+    const cuuint32_t box[4] = {32, 32, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 struct SlabPlan {
     int bn = 0;        // columns per CTA (a multiple of sl)
     int sl = 32;       // B slice rows = MMA N
@@ -1054,21 +1072,22 @@ struct SlabPlan {
     int nstg = 2;      // staging tiles per epilogue warp
 };
 
-size_t slab_smem_bytes(int K, int bn, int sl, int stages, int nstg) {
-    const int nkb = (K + kBK - 1) / kBK;
-    return 1024 + (size_t)nkb * kBM * kBK + (size_t)stages * nkb * sl * kBK + (size_t)8 * nstg * kSlabStgFloats * 4 +
+size_t slab_smem_bytes(int K, int bn, int sl, int stages, int nstg, int kbb = kBK) {
+    const int nkb = (K + kbb - 1) / kbb;
+    return 1024 + (size_t)nkb * kBM * kbb + (size_t)stages * nkb * sl * kbb + (size_t)8 * nstg * kSlabStgFloats * 4 +
            (size_t)2 * 4 * bn + 8 * (kSlabMaxKb + 2 * stages + kSlabMaxSlices + 1) + 16;
 }
 
 // Ring depth and staging tiles for a slab shape: as many B slices in flight
 // as fit (all of them when they do), two staging tiles per warp when a warp
 // stores more than one chunk. False when even one slice does not fit.
-bool slab_fit(int K, SlabPlan* sp) {
+bool slab_fit(int K, SlabPlan* sp, int kbb = kBK) {
+    if ((K + kbb - 1) / kbb > kSlabMaxKb) return false;
     const int nsl = sp->bn / sp->sl;
     const int chunks_per_warp = (sp->bn / 32 + 1) / 2;
     for (int nstg = chunks_per_warp > 1 ? 2 : 1; nstg >= 1; --nstg) {
         for (int st = nsl; st >= 1; --st) {
-            if (slab_smem_bytes(K, sp->bn, sp->sl, st, nstg) <= kMaxDynSmem) {
+            if (slab_smem_bytes(K, sp->bn, sp->sl, st, nstg, kbb) <= kMaxDynSmem) {
                 sp->stages = st;
                 sp->nstg = nstg;
                 return true;
@@ -1085,7 +1104,7 @@ bool slab_fit(int K, SlabPlan* sp) {
 // persistent / split-K plan) also keeps GEMMs off it.
 bool slab_plan(int M, int N, int K, SlabPlan* sp) {
     const int nkb = (K + kBK - 1) / kBK;
-    if (nkb > kSlabMaxKb || M <= 0 || N <= 0) return false;
+    if (nkb > 8 || M <= 0 || N <= 0) return false;   // plain GEMMs: K <= 1024
     const char* env = std::getenv("VLA_GEMM_SLAB");
     if (env && env[0] == '0' && env[1] == '\0') return false;
     const long long m_tiles = (M + kBM - 1) / kBM;
@@ -1117,20 +1136,20 @@ bool slab_plan(int M, int N, int K, SlabPlan* sp) {
     return false;
 }
 
-template <int SL>
+template <int SL, int KBB>
 cudaError_t slab_ready() {
     static std::atomic<unsigned long long> done{0};
-    return set_smem_attr_once(w8a8_slab_kernel<SL>, done);
+    return set_smem_attr_once(w8a8_slab_kernel<SL, KBB>, done);
 }
 
-template <int SL>
+template <int SL, int KBB = kBK>
 cudaError_t launch_slab_sl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const EpiParams& p,
                            const SlabPlan& sp, cudaStream_t st) {
-    cudaError_t e = slab_ready<SL>();
+    cudaError_t e = slab_ready<SL, KBB>();
     if (e != cudaSuccess) return e;
     const long long grid = (long long)p.m_tiles * p.slab_groups;
-    e = launch_k(w8a8_slab_kernel<SL>, dim3(static_cast<unsigned>(grid)), kThreads,
-                 slab_smem_bytes(p.K, sp.bn, SL, sp.stages, sp.nstg), st, ta, tb, to, p, sp.stages);
+    e = launch_k(w8a8_slab_kernel<SL, KBB>, dim3(static_cast<unsigned>(grid)), kThreads,
+                 slab_smem_bytes(p.K, sp.bn, SL, sp.stages, sp.nstg, KBB), st, ta, tb, to, p, sp.stages);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -1369,6 +1388,33 @@ cudaError_t conv_i8_implicit(const ConvI8Args& a, cudaStream_t st) {
     p.conv_pad = a.pad;
     p.conv_cb = a.C / kbb;
     p.m_tiles = a.F * p.conv_ty * p.conv_tx;
+    // 64-channel inputs with one wave or a few of output patches: the slab
+    // kernel (the whole tap set of the patch and all weights resident, TMA-store
+    // epilogue through a 4D output map; patch rows in runs of 32 pixels)
+    {
+        SlabPlan sp;
+        sp.bn = a.N <= 128 ? (a.N + 31) / 32 * 32 : 0;
+        sp.sl = sp.bn;
+        const char* env = std::getenv("VLA_GEMM_SLAB");
+        const bool off = (env && env[0] == '0') || std::getenv("VLA_GEMM_PLAN");
+        const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out);
+        if (!off && kbb == 64 && bw % 32 == 0 && (sp.bn == 32 || sp.bn == 64 || sp.bn == 128) && (a.N & 3) == 0 &&
+            (ob & 15) == 0 && !(a.mode & kEpiAcc) && p.m_tiles <= 3LL * sm_count() && slab_fit((int)K, &sp, 64)) {
+            p.slab_bn = sp.bn;
+            p.slab_groups = (a.N + sp.bn - 1) / sp.bn;
+            p.slab_nstg = sp.nstg;
+            CUtensorMap ta, tb, to;
+            if (!make_tmap_nhwc_i8(&ta, a.x, a.F, a.H, a.W, a.C, 64, bw, bh) ||
+                !make_tmap_i8_kmajor_kb(&tb, a.Wq, a.N, static_cast<int>(K), a.ldw, sp.sl, 64) ||
+                !make_tmap_f32_nhwc_out(&to, a.out, a.F, Ho, Wo, a.N))
+                return cudaErrorInvalidConfiguration;
+            switch (sp.sl) {
+                case 32: return launch_slab_sl<32, 64>(ta, tb, to, p, sp, st);
+                case 64: return launch_slab_sl<64, 64>(ta, tb, to, p, sp, st);
+                default: return launch_slab_sl<128, 64>(ta, tb, to, p, sp, st);
+            }
+        }
+    }
     GemmPlan plan;
     if (kbb == 64) {
         // 64-channel inputs: 64-byte k-blocks (one tap each), persistent kernel

@@ -22,25 +22,36 @@
 //   warp 1:        TMEM allocation; lane 0 issues the MMAs slice by slice
 //   warps 2-9:     epilogue; warp w takes TMEM lanes 32*(w%4).. and the
 //                  32-column chunks g with g % 2 == (w-2)/4
+//
+// Implicit convolutions (p.conv_bw > 0) run through the same kernel: the A
+// k-blocks are 4D tensor-map taps of the int8 NHWC input (load_a), a tile row
+// is a pixel of the tile's output patch (out_row), and the stores go through a
+// 4D output map [F][Ho][Wo][N] - each warp quarter's 32 tile rows are 32
+// consecutive pixels of one output row (the host requires patch widths that
+// are multiples of 32). KBB is the k-block width in bytes: 128 (128-byte
+// swizzle) or 64 (64-byte swizzle, for 64-channel convolution inputs).
 // Included by gemm_i8.cu inside its anonymous namespace (EpiParams, kBM, kBK,
-// kUmmaK, kThreads, row_ascale come from there).
+// kUmmaK, kThreads, row_ascale, out_row, load_a, kmajor_desc come from there).
 
-constexpr int kSlabMaxKb = 8;        // K <= 1024: the A tile stays resident
+constexpr int kSlabMaxKb = 16;       // k-blocks of the resident A tile (K <= 1024 for plain GEMMs)
 constexpr int kSlabMaxBn = 256;      // columns per CTA
 constexpr int kSlabMaxSlices = kSlabMaxBn / 32;
 constexpr int kSlabStgFloats = 32 * 32;   // one warp's staging tile: 32 rows x 128 bytes
 
-template <int SL>
+template <int SL, int KBB>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_out,
                  const EpiParams p, const int stages) {
     static_assert(SL == 32 || SL == 64 || SL == 128, "slice width");
+    static_assert(KBB == 64 || KBB == 128, "k-block bytes");
     constexpr uint32_t kIdesc = idesc_s8s8_s32(kBM, SL);
-    constexpr int kSliceKb = SL * kBK;          // bytes of one k-block of a B slice
-    constexpr int kAKb = kBM * kBK;             // bytes of one k-block of the A tile
-    const int nkb = (p.K + kBK - 1) / kBK;
+    constexpr int kSliceKb = SL * KBB;          // bytes of one k-block of a B slice
+    constexpr int kAKb = kBM * KBB;             // bytes of one k-block of the A tile
+    const int nkb = (p.K + KBB - 1) / KBB;
+    // bytes one A k-block brings in: a conv patch box may be under 128 rows
+    const uint32_t a_tx = p.conv_bw ? static_cast<uint32_t>(KBB * p.conv_bw * p.conv_bh) : static_cast<uint32_t>(kAKb);
     const int slice_bytes = nkb * kSliceKb;
     const int bn = p.slab_bn;
     const int mt = blockIdx.x / p.slab_groups, ng = blockIdx.x - mt * p.slab_groups;
@@ -102,15 +113,15 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
             auto load_slice = [&](int j, int s) {
                 mbar_arrive_expect_tx(&bfull[s], static_cast<uint32_t>(slice_bytes));
                 for (int kb = 0; kb < nkb; ++kb)
-                    tma_load_2d(sB + s * slice_bytes + kb * kSliceKb, &tmap_b, &bfull[s], kb * kBK, n0 + j * SL);
+                    tma_load_2d(sB + s * slice_bytes + kb * kSliceKb, &tmap_b, &bfull[s], kb * KBB, n0 + j * SL);
             };
             const int pre = nsl < stages ? nsl : stages;
             for (int j = 0; j < pre; ++j) load_slice(j, j);
             b_issued = pre;
             pdl_wait();   // A is the predecessor's output
             for (int kb = 0; kb < nkb; ++kb) {
-                mbar_arrive_expect_tx(&afull[kb], static_cast<uint32_t>(kAKb));
-                tma_load_2d(sA + kb * kAKb, &tmap_a, &afull[kb], kb * kBK, m0);
+                mbar_arrive_expect_tx(&afull[kb], a_tx);
+                load_a<KBB>(p, &tmap_a, sA + kb * kAKb, &afull[kb], mt, kb);
             }
             a_issued = true;
             for (int j = pre; j < nsl; ++j) {
@@ -138,9 +149,9 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     }
                     const uint32_t a_addr = smem_u32(sA + kb * kAKb);
                     #pragma unroll
-                    for (int k = 0; k < kBK / kUmmaK; ++k)
-                        umma_s8(d_tmem, sw128_kmajor_desc(a_addr + k * kUmmaK),
-                                sw128_kmajor_desc(b_addr + kb * kSliceKb + k * kUmmaK), kIdesc, (kb | k) != 0);
+                    for (int k = 0; k < KBB / kUmmaK; ++k)
+                        umma_s8(d_tmem, kmajor_desc<KBB>(a_addr + k * kUmmaK),
+                                kmajor_desc<KBB>(b_addr + kb * kSliceKb + k * kUmmaK), kIdesc, (kb | k) != 0);
                 }
                 if (fail) break;
                 if (j == 0) *s_adone = 1;
@@ -162,9 +173,22 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         named_sync(1, 256);
         pdl_wait();   // activation scales / residual: predecessor data
-        const int m = m0 + q * 32 + lane;
-        const bool row_ok = m < p.M;
-        const bool quarter_live = m0 + q * 32 < p.M;     // warp-uniform
+        // output row of this thread's tile row (-1: no output), and whether the
+        // quarter's first row has one (then the quarter's store is issued)
+        const int m = out_row(p, mt, q * 32 + lane);
+        const bool row_ok = m >= 0;
+        const bool quarter_live = __shfl_sync(0xFFFFFFFFu, m, 0) >= 0;   // warp-uniform
+        // store origin of the quarter: plain GEMM (n, row); convolution the
+        // pixel (ox, oy) of frame f of the quarter's first row
+        int st_x = 0, st_y = m0 + q * 32, st_f = 0;
+        if (p.conv_bw) {
+            const int m_first = __shfl_sync(0xFFFFFFFFu, m, 0);
+            const int per_f = p.conv_ho * p.conv_wo;
+            st_f = m_first / per_f;
+            const int rem = m_first - st_f * per_f;
+            st_y = rem / p.conv_wo;
+            st_x = rem - st_y * p.conv_wo;
+        }
         const float sa = row_ok ? row_ascale(p, m) : 0.0f;
         const int mode = p.mode;
         const bool has_res = (mode & (kEpiAdd | kEpiAddRelu)) != 0;
@@ -241,7 +265,8 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(&tmap_out, sb, n, m0 + q * 32);
+                if (p.conv_bw) tma_store_4d(&tmap_out, sb, n, st_x, st_y, st_f);
+                else tma_store_2d(&tmap_out, sb, n, st_y);
                 bulk_commit();
             }
         }

@@ -162,6 +162,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y) : "memory");
 }
 
+// 4D tile store (an NHWC fp32 output: {channels, W, H, frame}); the same rules.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y,
+                                             int32_t z, int32_t w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N of this thread's committed bulk groups still read shared memory.
