@@ -30,6 +30,13 @@
 // Finally o / l, or the mean of V for a row whose every key is blocked (the
 // reference's uniform-weights rule). Rows past seq_q and keys past seq_k are
 // zero tiles, the latter masked to -inf.
+//
+// Key split: a query tile's key blocks are divided among the `splits` CTAs
+// of a thread-block cluster (so a small head count still fills the SMs); each
+// CTA leaves its running (m, l, o) per row in shared memory and, after a
+// cluster barrier, finalizes rows r with r % splits == its rank by merging
+// the partial states through distributed shared memory:
+//   M = max m_i,  o = sum o_i exp(m_i - M),  l = sum l_i exp(m_i - M).
 #include "sm100.cuh"
 #include "launch.cuh"
 #include "nn.h"
@@ -84,7 +91,7 @@ __device__ __forceinline__ void put_split4(uint8_t* hi, uint8_t* lo, uint32_t of
 __global__ void __launch_bounds__(kTcThreads, 1)
 attention_tc_kernel(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
                     float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, float scale,
-                    const float* mask, const AttBatch bs) {
+                    const float* mask, const AttBatch bs, const int splits) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQh = sm;
@@ -99,7 +106,8 @@ attention_tc_kernel(const float* Q, long long ldq, const float* K, long long ldk
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int q0 = blockIdx.x * kTcRows, h = blockIdx.y, kvh = h / (n_q / n_kv);
+    const int rank = blockIdx.x % splits;                  // rank in the cluster (clusters run along x)
+    const int q0 = (blockIdx.x / splits) * kTcRows, h = blockIdx.y, kvh = h / (n_q / n_kv);
     VSB_ATT_BATCH_OFFSET(bs);
 
     if (tid == 0) {
@@ -133,8 +141,10 @@ attention_tc_kernel(const float* Q, long long ldq, const float* K, long long ldk
     float m = -INFINITY, l = 0.0f;
     uint32_t phase = 0;
     bool ok = true;
-    const int nblk = (seq_k + kTcKeys - 1) / kTcKeys;
-    for (int blk = 0; blk < nblk && ok; ++blk) {
+    const int nblk_all = (seq_k + kTcKeys - 1) / kTcKeys;
+    const int blk_lo = static_cast<int>((long long)nblk_all * rank / splits);
+    const int blk_hi = static_cast<int>((long long)nblk_all * (rank + 1) / splits);
+    for (int blk = blk_lo; blk < blk_hi && ok; ++blk) {
         const int k0 = blk * kTcKeys;
         // K block (row = key) and V^T block (row = d), split
         for (int i = tid; i < kTcKeys * (kAttD / 4); i += kTcThreads) {
@@ -255,7 +265,50 @@ attention_tc_kernel(const float* Q, long long ldq, const float* K, long long ldk
         __syncthreads();   // S / O columns and the K / V / P tiles are rewritten next block
     }
 
-    if (ok && row_ok) {
+    if (splits > 1) {
+        // this CTA's partial state per row -> shared memory (the P tiles are
+        // free: the last P.V MMA completed before the loop's final barrier)
+        constexpr int kPs = kAttD + 4;   // o[64], m, l, 2 pad: 16-byte rows
+        float* part = reinterpret_cast<float*>(sPh);
+        #pragma unroll
+        for (int c = 0; c < kAttD / 4; ++c)
+            *reinterpret_cast<float4*>(part + tid * kPs + 4 * c) = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        part[tid * kPs + kAttD] = m;
+        part[tid * kPs + kAttD + 1] = l;
+        cluster_sync();
+        if (tid % splits == rank) {
+            const uint32_t base = smem_u32(part + tid * kPs);
+            float mi[8], li[8];
+            float M = -INFINITY;
+            for (int i = 0; i < splits; ++i) {
+                const int4 ml = dsmem_ld_v4(dsmem_map(base + kAttD * 4, static_cast<uint32_t>(i)));
+                mi[i] = __int_as_float(ml.x);
+                li[i] = __int_as_float(ml.y);
+                M = fmaxf(M, mi[i]);
+            }
+            float L = 0.0f;
+            #pragma unroll
+            for (int d = 0; d < kAttD; ++d) o[d] = 0.0f;
+            if (M != -INFINITY) {
+                for (int i = 0; i < splits; ++i) {
+                    const float w = mi[i] == -INFINITY ? 0.0f : ref_exp(__fsub_rn(mi[i], M));
+                    L = __fmaf_rn(li[i], w, L);
+                    #pragma unroll
+                    for (int c = 0; c < kAttD / 4; ++c) {
+                        const int4 v = dsmem_ld_v4(dsmem_map(base + 16 * c, static_cast<uint32_t>(i)));
+                        o[4 * c] = __fmaf_rn(__int_as_float(v.x), w, o[4 * c]);
+                        o[4 * c + 1] = __fmaf_rn(__int_as_float(v.y), w, o[4 * c + 1]);
+                        o[4 * c + 2] = __fmaf_rn(__int_as_float(v.z), w, o[4 * c + 2]);
+                        o[4 * c + 3] = __fmaf_rn(__int_as_float(v.w), w, o[4 * c + 3]);
+                    }
+                }
+            }
+            m = M;
+            l = L;
+        }
+        cluster_sync();   // no CTA leaves while another still reads its partial rows
+    }
+    if (ok && row_ok && tid % splits == rank) {
         float* orow = O + (long long)row * ldo + h * kAttD;
         if (!(m > -FLT_MAX)) {
             // every key blocked: uniform weights over all keys (the mean of V)
@@ -308,9 +361,21 @@ cudaError_t attention_tc(const float* Q, long long ldq, const float* K, long lon
         if (e != cudaSuccess) return e;
         ready.fetch_or(bit);
     }
-    const dim3 grid((seq_q + kTcRows - 1) / kTcRows, n_q, bs.n);
-    e = launch_k(attention_tc_kernel, grid, kTcThreads, kTcSmem, st, Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k,
-                 n_q, n_kv, scale, mask, bs);
+    // key split: as many CTAs per query tile (a cluster, up to 8) as keep the
+    // grid within one CTA per SM, and at least one 64-key block each
+    const long long tiles = (long long)((seq_q + kTcRows - 1) / kTcRows) * n_q * bs.n;
+    const int nblk = (seq_k + kTcKeys - 1) / kTcKeys;
+    int splits = static_cast<int>(148 / (tiles > 0 ? tiles : 1));
+    if (splits > 8) splits = 8;
+    if (splits > nblk) splits = nblk;
+    if (splits < 1) splits = 1;
+    const dim3 grid(static_cast<unsigned>((seq_q + kTcRows - 1) / kTcRows * splits), n_q, bs.n);
+    if (splits > 1)
+        e = launch_k_cluster(attention_tc_kernel, grid, kTcThreads, dim3(splits, 1, 1), kTcSmem, st, Q, ldq, K, ldk,
+                             V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, splits);
+    else
+        e = launch_k(attention_tc_kernel, grid, kTcThreads, kTcSmem, st, Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k,
+                     n_q, n_kv, scale, mask, bs, splits);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
