@@ -458,7 +458,7 @@ def run_ours(args):
     bf16_peak, hbm_peak, peak_kind = _peaks()
     int8_peak = 2.0 * bf16_peak   # dense int8 runs at 2x the dense bf16 rate on B200
     achieved = gemm["tops_l2_warm"]
-    roofline = {"kernel": "w8a8_umma_kernel (ACT FFN 602x3200x512, L2-warm, back-to-back)", "bound": "tensor",
+    roofline = {"kernel": "w8a8_slab_kernel<128, 128> (ACT FFN 602x3200x512, L2-warm, back-to-back)", "bound": "tensor",
                 "achieved": round(achieved, 2), "peak": round(int8_peak, 1), "unit": "TOPS (int8)",
                 "frac": round(achieved / int8_peak, 4),
                 "peak_note": f"2x {peak_kind} bf16 dense ({bf16_peak} TFLOP/s, MEASURED_PEAKS.json)",
