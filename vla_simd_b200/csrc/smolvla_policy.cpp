@@ -536,7 +536,7 @@ bool SmolvlaPolicy::load(const std::string& dir, const std::string& tok_dir, int
     int major = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_);
     if (major != 10) { fail("needs an sm_100 (B200) device"); return false; }
-    if (max_batch < 1 || max_batch > 64) { fail("max_batch must be in [1, 64]"); return false; }
+    if (max_batch < 1 || max_batch > 256) { fail("max_batch must be in [1, 256]"); return false; }
     max_batch_ = max_batch;
     use_graph_ = env_int("VLA_CUDA_GRAPH", 1) != 0;
     const int mask = env_int("SMOLVLA_INT8", 0);
