@@ -23,8 +23,13 @@ namespace vsb {
 // inv = (float)(1/sqrt(ss/H + eps)), out = x*inv*w. One warp per row: the
 // lanes form the exact double products in shared memory, lane 0 adds them in
 // the reference's order.
+//
+// Optional fused output (q != nullptr): the per-row int8 quantization of the
+// normalized row for the next W8A8 GEMM (quantize_rows' arithmetic: absmax
+// scale, q8), so the GEMM needs no quantizer launch of its own.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
-                               int seq, int hidden, float eps) {
+                               int seq, int hidden, float eps, int8_t* __restrict__ q, long long ldq,
+                               float* __restrict__ qscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     extern __shared__ double rms_sq[];
@@ -39,12 +44,27 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     ss = __shfl_sync(0xFFFFFFFFu, ss, 0);
     const float inv = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hidden), (double)eps)));
     float* orow = out + (long long)t * hidden;
-    for (int h = lane; h < hidden; h += 32) orow[h] = __fmul_rn(__fmul_rn(xr[h], inv), w[h]);
+    float am = 0.0f;
+    for (int h = lane; h < hidden; h += 32) {
+        const float v = __fmul_rn(__fmul_rn(xr[h], inv), w[h]);
+        orow[h] = v;
+        am = fmaxf(am, fabsf(v));
+    }
+    if (!q) return;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+    const float sc = row_scale(am), iv = __fdiv_rn(1.0f, sc);
+    __syncwarp();   // this lane reads back only elements it wrote itself
+    int8_t* qr = q + (long long)t * ldq;
+    for (long long h = lane; h < ldq; h += 32) qr[h] = h < hidden ? q8(orow[h], iv) : 0;
+    if (lane == 0) qscale[t] = sc;
 }
 
-cudaError_t rmsnorm(const float* x, const float* w, float* out, int seq, int hidden, float eps, cudaStream_t st) {
-    if (seq <= 0 || hidden <= 0 || hidden > 6144) return cudaErrorInvalidValue;
-    const cudaError_t e = launch_k(rmsnorm_kernel, seq, 32, sizeof(double) * hidden, st, x, w, out, seq, hidden, eps);
+cudaError_t rmsnorm(const float* x, const float* w, float* out, int seq, int hidden, float eps, cudaStream_t st,
+                    int8_t* q, long long ldq, float* qscale) {
+    if (seq <= 0 || hidden <= 0 || hidden > 6144 || (q && (ldq < hidden || !qscale))) return cudaErrorInvalidValue;
+    const cudaError_t e = launch_k(rmsnorm_kernel, seq, 32, sizeof(double) * hidden, st, x, w, out, seq, hidden, eps,
+                                   q, ldq, qscale);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -7,7 +7,10 @@ namespace vsb {
 
 enum : int { kActRelu = 0, kActSiluGate = 1, kActSilu = 2, kActGeluTanh = 3, kActGeluErf = 4, kActMish = 5 };
 
-cudaError_t rmsnorm(const float* x, const float* w, float* out, int seq, int hidden, float eps, cudaStream_t st);
+// RMSNorm; with q, also the per-row int8 copy of out (q [seq][ldq], zero past
+// hidden) and its scales, as quantize_rows would make them.
+cudaError_t rmsnorm(const float* x, const float* w, float* out, int seq, int hidden, float eps, cudaStream_t st,
+                    int8_t* q = nullptr, long long ldq = 0, float* qscale = nullptr);
 cudaError_t rope_neox(float* x, const int* pos, int seq, int n_heads, int head_dim, float base, cudaStream_t st);
 // out = act(x) (u: silu_gate's second operand); out may alias x
 cudaError_t activation(int kind, float* out, const float* x, const float* u, long long n, cudaStream_t st);

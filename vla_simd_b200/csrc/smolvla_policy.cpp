@@ -596,6 +596,12 @@ cudaError_t SmolvlaPolicy::linear(const DevLinear& l, const float* x, long long 
     return linear_q(l, d_q_, d_qs_, x, ldx, M, out, ldo, mode, res, ldr, st);
 }
 
+cudaError_t SmolvlaPolicy::rmsnorm_for(const float* x, const float* w, float* xn, int rows, int K, float eps, bool int8,
+                                       cudaStream_t st) {
+    if (int8 && ((size_t)rows > q_rows_ || (size_t)rows * round16(K) > q_cap_)) return cudaErrorInvalidValue;
+    return rmsnorm(x, w, xn, rows, K, eps, st, int8 ? d_q_ : nullptr, round16(K), d_qs_);
+}
+
 cudaError_t SmolvlaPolicy::linear_q(const DevLinear& l, const int8_t* q, const float* qs, const float* x,
                                     long long ldx, int M, float* out, long long ldo, int mode, const float* res,
                                     long long ldr, cudaStream_t st) {
@@ -688,8 +694,8 @@ cudaError_t SmolvlaPolicy::run_vlm(int B, cudaStream_t st) {
     for (int L = 0; L < c.vlm_layers; ++L) {
         const SmolVlmLayerDev& w = vlm_[L];
         float* qkv = d_cache_[L];
-        VSB_TRY(rmsnorm(d_x_, w.ln_in, d_xn_, rows, D, c.rms_eps, st));
-        VSB_TRY(linear(w.wqkv, d_xn_, D, rows, qkv, LD, 0, nullptr, 0, st));
+        VSB_TRY(rmsnorm_for(d_x_, w.ln_in, d_xn_, rows, D, c.rms_eps, w.wqkv.int8, st));
+        VSB_TRY(linear_q(w.wqkv, d_q_, d_qs_, d_xn_, D, rows, qkv, LD, 0, nullptr, 0, st));
         VSB_TRY(rope_table(qkv + QF, LD, rows, c.n_kv, c.hd, d_pos_, rope_vlm_, max_pos_, d_status_, st));
         if (L + 1 == c.vlm_layers) break;
         VSB_TRY(rope_table(qkv, LD, rows, c.n_q, c.hd, d_pos_, rope_vlm_, max_pos_, d_status_, st));
@@ -701,8 +707,8 @@ cudaError_t SmolvlaPolicy::run_vlm(int B, cudaStream_t st) {
         VSB_TRY(attention_batched(qkv, LD, qkv + QF, LD, qkv + QF + KV, LD, d_att_, QF, np, np, c.n_q, c.n_kv, c.hd,
                                   scale, d_pmask_, bs, st));
         VSB_TRY(linear(w.wo, d_att_, QF, rows, d_x_, D, kEpiAdd, d_x_, D, st));
-        VSB_TRY(rmsnorm(d_x_, w.ln_post, d_xn_, rows, D, c.rms_eps, st));
-        VSB_TRY(linear(w.wgu, d_xn_, D, rows, d_gu_, 2 * F, 0, nullptr, 0, st));
+        VSB_TRY(rmsnorm_for(d_x_, w.ln_post, d_xn_, rows, D, c.rms_eps, w.wgu.int8, st));
+        VSB_TRY(linear_q(w.wgu, d_q_, d_qs_, d_xn_, D, rows, d_gu_, 2 * F, 0, nullptr, 0, st));
         if (w.wdown.int8) {
             VSB_TRY(silu_gate_rows(d_gu_, rows, F, nullptr, d_q_, round16(F), d_qs_, st));
             VSB_TRY(linear_q(w.wdown, d_q_, d_qs_, nullptr, 0, rows, d_x_, D, kEpiAdd, d_x_, D, st));
@@ -744,14 +750,16 @@ cudaError_t SmolvlaPolicy::run_expert(int B, bool guided, cudaStream_t st) {
         VSB_TRY(linear_f32(d_mlp1_, EH, at2_.W, at2_.bias, d_eh_, EH, rows, EH, EH, nullptr, nullptr, st));
         for (int L = 0; L < c.e_layers; ++L) {
             const SmolExpertLayerDev& w = aex_[L];
-            VSB_TRY(rmsnorm(d_eh_, w.ln_in, d_ehn_, rows, EH, c.e_eps, st));
-            VSB_TRY(linear(w.wq, d_ehn_, EH, rows, d_eq_, eQF, 0, nullptr, 0, st));
+            // one int8 copy of the normalized rows serves q and (self-attention) k / v
+            VSB_TRY(rmsnorm_for(d_eh_, w.ln_in, d_ehn_, rows, EH, c.e_eps, w.wq.int8 || (w.self_attn && w.wkv.int8),
+                                st));
+            VSB_TRY(linear_q(w.wq, d_q_, d_qs_, d_ehn_, EH, rows, d_eq_, eQF, 0, nullptr, 0, st));
             AttBatch bs;
             bs.n = B;
             bs.q = (long long)C * eQF;
             bs.o = (long long)C * eQF;
             if (w.self_attn) {
-                VSB_TRY(linear(w.wkv, d_ehn_, EH, rows, d_ekv_, 2 * KV, 0, nullptr, 0, st));
+                VSB_TRY(linear_q(w.wkv, d_q_, d_qs_, d_ehn_, EH, rows, d_ekv_, 2 * KV, 0, nullptr, 0, st));
                 VSB_TRY(rope_table(d_eq_, eQF, rows, c.e_nq, c.e_hd, d_pos_full_, rope_aex_, max_pos_, d_status_, st));
                 VSB_TRY(kv_scatter_rope(d_ekv_, B, C, KV, c.e_hd, d_pos_full_, rope_aex_, max_pos_, d_kvf_[L], np,
                                         d_status_, st));
@@ -767,8 +775,8 @@ cudaError_t SmolvlaPolicy::run_expert(int B, bool guided, cudaStream_t st) {
                                           c.e_nq, c.e_nkv, c.e_hd, scale, d_cmask_, bs, st));
             }
             VSB_TRY(linear(w.wo, d_eatt_, eQF, rows, d_eh_, EH, kEpiAdd, d_eh_, EH, st));
-            VSB_TRY(rmsnorm(d_eh_, w.ln_post, d_ehn_, rows, EH, c.e_eps, st));
-            VSB_TRY(linear(w.wgu, d_ehn_, EH, rows, d_egu_, 2 * EF, 0, nullptr, 0, st));
+            VSB_TRY(rmsnorm_for(d_eh_, w.ln_post, d_ehn_, rows, EH, c.e_eps, w.wgu.int8, st));
+            VSB_TRY(linear_q(w.wgu, d_q_, d_qs_, d_ehn_, EH, rows, d_egu_, 2 * EF, 0, nullptr, 0, st));
             if (w.wdown.int8) {
                 VSB_TRY(silu_gate_rows(d_egu_, rows, EF, nullptr, d_q_, round16(EF), d_qs_, st));
                 VSB_TRY(linear_q(w.wdown, d_q_, d_qs_, nullptr, 0, rows, d_eh_, EH, kEpiAdd, d_eh_, EH, st));

@@ -99,6 +99,10 @@ class SmolvlaPolicy {
     bool ensure_frames(int h, int w);
     cudaError_t linear(const DevLinear& l, const float* x, long long ldx, int M, float* out, long long ldo, int mode,
                        const float* res, long long ldr, cudaStream_t st);
+    // RMSNorm of x into xn; with int8, also the per-row int8 copy into the
+    // shared quantization buffer (d_q_ / d_qs_) for the linears that read xn.
+    cudaError_t rmsnorm_for(const float* x, const float* w, float* xn, int rows, int K, float eps, bool int8,
+                            cudaStream_t st);
     cudaError_t linear_q(const DevLinear& l, const int8_t* q, const float* qs, const float* x, long long ldx, int M,
                          float* out, long long ldo, int mode, const float* res, long long ldr, cudaStream_t st);
     cudaError_t run_vision(int F, int h, int w, cudaStream_t st);
