@@ -9,7 +9,7 @@ decoder -> head) on device-resident inputs, timed with CUDA events on the
 launching stream; L2 is flushed (256 MiB memset, outside the events) between
 steps. `value` = chunks/s of the whole job = N*K / max over ranks of the summed
 step time. `e2e` = the same metric through the C ABI (vla_act_predict) with
-host frames/state/actions, copies included, wall clock.
+pinned host frames/state in and host actions out, copies included, wall clock.
 
 Extra fields: per-step latency p50/p95, the W8A8 GEMM alone at the ACT FFN
 shape (602x3200x512; TOPS cold and L2-warm) as the
@@ -137,6 +137,31 @@ def max_over_ranks(seconds: float, dist=None, device=None) -> float:
 def job_value(steps_per_rank: int, world: int, seconds_max: float) -> float:
     """Whole-job chunks/s: every rank's steps over the slowest rank's time."""
     return world * steps_per_rank / seconds_max
+
+
+_PINNED = []   # page-locked tensors behind the numpy views pinned() hands out
+
+
+def pinned(torch, a):
+    """A copy of the numpy array `a` in page-locked host memory: the e2e legs
+    feed the C ABI from pinned buffers, as a serving loop that owns its camera
+    buffers does (the copies stay inside the timed region)."""
+    a = np.ascontiguousarray(a)
+    t = torch.empty(a.shape, dtype=torch.from_numpy(a).dtype, pin_memory=True)
+    _PINNED.append(t)
+    out = t.numpy()
+    out[...] = a
+    return out
+
+
+def timed_calls(fn, n: int):
+    """Wall-clock seconds of each of n calls of fn(i)."""
+    out = []
+    for i in range(n):
+        t0 = time.perf_counter()
+        fn(i)
+        out.append(time.perf_counter() - t0)
+    return out
 
 
 def cpu_cores():
@@ -431,17 +456,16 @@ def run_ours(args):
 
     # e2e through the C ABI with host buffers (copies inside), wall clock
     n_e2e = max(args.steps, 10)
+    frames_h, state_h = pinned(torch, frames), pinned(torch, state)
     for _ in range(3):
-        pol.predict(frames, state)
+        pol.predict(frames_h, state_h)
     if dist:
         dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(n_e2e):
-        pol.predict(frames, state)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    calls = timed_calls(lambda i: pol.predict(frames_h, state_h), n_e2e)
+    e2e_s = max_over_ranks(sum(calls), dist, dev)
     e2e = {"value": job_value(n_e2e, world, e2e_s), "unit": "chunks/s", "h2d_bytes_per_step": frames.nbytes + state.nbytes,
-           "d2h_bytes_per_step": 100 * 6 * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
-           "path": "vla_act_predict (C ABI), host uint8 frames + state -> host actions"}
+           "d2h_bytes_per_step": 100 * 6 * 4, "p50_ms_per_call": 1e3 * statistics.median(calls),
+           "path": "vla_act_predict (C ABI), pinned host uint8 frames + state -> host actions"}
 
     gemm = time_gemm(torch, dev) if rank == 0 else None
     cpu = cpu1 = None
@@ -596,18 +620,17 @@ def run_dp(args):
     total_max = max_over_ranks(sum(step_s), dist, dev)
     value = job_value(args.steps * B, world, total_max)
     n_e2e = max(args.steps, 10)
+    frames_h, state_h, noise_h = pinned(torch, frames), pinned(torch, state), pinned(torch, noise)
     for _ in range(2):
-        pol.predict_batch(frames, state, noise)
+        pol.predict_batch(frames_h, state_h, noise_h)
     if dist:
         dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(n_e2e):
-        pol.predict_batch(frames, state, noise)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    calls = timed_calls(lambda i: pol.predict_batch(frames_h, state_h, noise_h), n_e2e)
+    e2e_s = max_over_ranks(sum(calls), dist, dev)
     e2e = {"value": job_value(n_e2e * B, world, e2e_s), "unit": "chunks/s",
            "h2d_bytes_per_step": frames.nbytes + state.nbytes + noise.nbytes,
-           "d2h_bytes_per_step": B * pol.chunk * pol.action_dim * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
-           "path": "vla_diffusion_predict_batch (C ABI), host frames + state + noise -> host actions"}
+           "d2h_bytes_per_step": B * pol.chunk * pol.action_dim * 4, "p50_ms_per_call": 1e3 * statistics.median(calls),
+           "path": "vla_diffusion_predict_batch (C ABI), pinned host frames + state + noise -> host actions"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_dp_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
@@ -765,19 +788,18 @@ def run_octo(args):
     def window(i):
         return (np.ascontiguousarray(seq_p[i:i + sh.window].transpose(1, 0, 2, 3, 4)),
                 np.ascontiguousarray(seq_w[i:i + sh.window].transpose(1, 0, 2, 3, 4)))
-    wins = [window(i) for i in range(n_e2e + 2)]
+    wins = [tuple(pinned(torch, a) for a in window(i)) for i in range(n_e2e + 2)]
+    tm_h, noise_h, z_h = pinned(torch, tm), pinned(torch, noise), pinned(torch, z)
     for i in range(2):
-        pol.predict_batch(wins[i][0], wins[i][1], tm, ins, noise, z)
+        pol.predict_batch(wins[i][0], wins[i][1], tm_h, ins, noise_h, z_h)
     if dist:
         dist.barrier()
-    t0 = time.perf_counter()
-    for i in range(n_e2e):
-        pol.predict_batch(wins[i + 2][0], wins[i + 2][1], tm, ins, noise, z)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    calls = timed_calls(lambda i: pol.predict_batch(wins[i + 2][0], wins[i + 2][1], tm_h, ins, noise_h, z_h), n_e2e)
+    e2e_s = max_over_ranks(sum(calls), dist, dev)
     e2e = {"value": job_value(n_e2e * B, world, e2e_s), "unit": "chunks/s",
            "h2d_bytes_per_step": p.nbytes + w.nbytes + tm.nbytes + noise.nbytes + z.nbytes + 4 * B,
-           "d2h_bytes_per_step": B * sh.flat * 4, "p50_ms_per_call": 1e3 * e2e_s / n_e2e,
-           "path": "vla_octo_predict_batch (C ABI), host frames + masks + noise -> host actions"}
+           "d2h_bytes_per_step": B * sh.flat * 4, "p50_ms_per_call": 1e3 * statistics.median(calls),
+           "path": "vla_octo_predict_batch (C ABI), pinned host frames + masks + noise -> host actions"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the CPU baseline runs at N=1 only
         cpu = time_reference_octo_cpu(ckpt, budget_s=args.cpu_budget, max_steps=20)
@@ -875,6 +897,7 @@ def run_smolvla(args):
     ckpt = synth.write_smolvla_checkpoint(os.path.join(ckpt_root, "smolvla"), sh, seed=0)
     pol = SmolvlaPolicy(ckpt, max_batch=B)
     f, ins, st, nz = synth.smolvla_inputs(sh, seed=1 + rank, batch=B)
+    f, st, nz = pinned(torch, f), pinned(torch, st), pinned(torch, nz)
     for _ in range(max(args.warmup, 3)):
         pol.predict_batch(f, ins, st, nz)
     if dist:
@@ -919,8 +942,8 @@ def run_smolvla(args):
                                "tokens + state, expert 16 layers h720, 10 flow-matching steps, 50 x 6 chunk",
                    "batch_per_gpu": B, "int8_mask": SMOLVLA_MASK,
                    "parallelism": f"replicas x{world} (no collective)",
-                   "timing": "wall clock per vla_smolvla_predict_batch call (host frames in, host actions out: "
-                             "this line's value is already end to end)"},
+                   "timing": "wall clock per vla_smolvla_predict_batch call (pinned host frames in, host actions "
+                             "out: this line's value is already end to end)"},
         "latency_ms": {"p50": round(1e3 * statistics.median(step_s), 4)},
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": round(value, 3), "unit": "chunks/s", "h2d_bytes_per_step": f.nbytes + st.nbytes + nz.nbytes,

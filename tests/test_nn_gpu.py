@@ -118,6 +118,32 @@ def test_attention_matches_reference(dev, reference):
     assert np.abs(got - reference.attention(Q, K, V, n, n, 64, np.float32(0.125))).max() <= 2e-6
 
 
+@pytest.mark.parametrize("sq,sk,nq,nkv", [(1024, 1024, 12, 12), (690, 690, 12, 12), (50, 227, 15, 5)])
+def test_attention_tile_heights_vs_reference(dev, reference, sq, sk, nq, nkv):
+    """Shapes whose default query tile is 32 rows (SigLIP's 1024 keys, Octo's
+    690) or 8 rows (the SmolVLA expert's GQA): the reference's bits."""
+    from vla_simd_b200 import ops
+    g = XorShift(sq + sk)
+    Q = g.uniform(sq * nq * 64).reshape(sq, nq * 64)
+    K = g.uniform(sk * nkv * 64).reshape(sk, nkv * 64)
+    V = g.uniform(sk * nkv * 64).reshape(sk, nkv * 64)
+    got = ops.gqa_attention(_t(Q, dev), _t(K, dev), _t(V, dev), nq, nkv, 0.125).cpu().numpy()
+    assert np.array_equal(got, reference.attention(Q, K, V, nq, nkv, 64, np.float32(0.125)))
+
+
+@pytest.mark.parametrize("seq,N,K", [(50, 720, 1440), (50, 32, 720), (64, 720, 1040), (40, 96, 1037), (33, 4, 1000)])
+def test_dense_linear_f32_long_k_vs_reference(dev, reference, seq, N, K):
+    """The tiled fp32 linear streaming K > 512 through shared memory in
+    chunks (the SmolVLA expert's time MLP and projections): the reference's bits."""
+    from vla_simd_b200 import ops
+    rng = np.random.default_rng(seq * N + K)
+    x = rng.standard_normal((seq, K), dtype=np.float32)
+    W = (rng.standard_normal((N, K), dtype=np.float32) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N, dtype=np.float32)
+    got = ops.dense_linear_f32(_t(x, dev), _t(W, dev), _t(b, dev)).cpu().numpy()
+    assert np.array_equal(got, reference.dense_linear(x, W, b))
+
+
 @pytest.mark.parametrize("H,W,C", [(240, 320, 64), (7, 9, 16), (1, 1, 64)])
 def test_maxpool_relu_exact(dev, H, W, C):
     from vla_simd_b200 import ops

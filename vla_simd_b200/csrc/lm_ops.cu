@@ -20,50 +20,109 @@ namespace vsb {
 
 // ------------------------------------------------------------------ RMSNorm
 // src/hal/common/norms.cpp:19-35: ss = sum over h in order of (double)x*x,
-// inv = (float)(1/sqrt(ss/H + eps)), out = x*inv*w. One warp per row: the
-// lanes form the exact double products in shared memory, lane 0 adds them in
-// the reference's order.
+// inv = (float)(1/sqrt(ss/H + eps)), out = x*inv*w. One CTA per row: its
+// threads load the row and the weights once (every load issued before any is
+// used) and form the exact double products in shared memory; thread 0 adds
+// them in the reference's order, which is the row's critical path (H dependent
+// double adds).
 //
 // Optional fused output (q != nullptr): the per-row int8 quantization of the
 // normalized row for the next W8A8 GEMM (quantize_rows' arithmetic: absmax
 // scale, q8), so the GEMM needs no quantizer launch of its own.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
-                               int seq, int hidden, float eps, int8_t* __restrict__ q, long long ldq,
-                               float* __restrict__ qscale) {
+constexpr int kRmsThreads = 128;
+
+__global__ void __launch_bounds__(kRmsThreads)
+rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out, int seq,
+               int hidden, float eps, int8_t* __restrict__ q, long long ldq, float* __restrict__ qscale) {
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
-    extern __shared__ double rms_sq[];
-    const int t = blockIdx.x;
-    const int lane = threadIdx.x;
+    extern __shared__ double rms_sq[];                                  // [hidden] squares
+    float* xs = reinterpret_cast<float*>(rms_sq + hidden);              // [hidden] x, then the output row
+    float* ws = xs + hidden;                                            // [hidden] weights
+    __shared__ float s_red[kRmsThreads / 32];
+    __shared__ float s_inv;
+    const int t = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + (long long)t * hidden;
-    for (int h = lane; h < hidden; h += 32) rms_sq[h] = (double)xr[h] * (double)xr[h];
-    __syncwarp();
-    double ss = 0.0;
-    if (lane == 0)
-        for (int h = 0; h < hidden; ++h) ss = __dadd_rn(ss, rms_sq[h]);
-    ss = __shfl_sync(0xFFFFFFFFu, ss, 0);
-    const float inv = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hidden), (double)eps)));
+    if (hidden % 4 == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0) {
+        #pragma unroll 4
+        for (int h = 4 * tid; h < hidden; h += 4 * kRmsThreads) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + h);
+            const float4 g = *reinterpret_cast<const float4*>(w + h);
+            *reinterpret_cast<float4*>(xs + h) = v;
+            *reinterpret_cast<float4*>(ws + h) = g;
+            *reinterpret_cast<double2*>(rms_sq + h) = make_double2((double)v.x * (double)v.x, (double)v.y * (double)v.y);
+            *reinterpret_cast<double2*>(rms_sq + h + 2) =
+                make_double2((double)v.z * (double)v.z, (double)v.w * (double)v.w);
+        }
+    } else {
+        #pragma unroll 4
+        for (int h = tid; h < hidden; h += kRmsThreads) {
+            const float v = xr[h];
+            xs[h] = v;
+            ws[h] = w[h];
+            rms_sq[h] = (double)v * (double)v;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // the next 16 squares are loaded while the current 16 are added, so
+        // the chain runs at the double-add latency
+        double ss = 0.0;
+        int h = 0;
+        double2 cur[8], nxt[8];
+        const int h16 = hidden & ~15;
+        if (h16) {
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) cur[u] = reinterpret_cast<const double2*>(rms_sq)[u];
+        }
+        for (; h < h16; h += 16) {
+            if (h + 16 < h16) {
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) nxt[u] = reinterpret_cast<const double2*>(rms_sq + h + 16)[u];
+            }
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) { ss = __dadd_rn(ss, cur[u].x); ss = __dadd_rn(ss, cur[u].y); }
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+        }
+        for (; h < hidden; ++h) ss = __dadd_rn(ss, rms_sq[h]);
+        s_inv = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hidden), (double)eps)));
+    }
+    __syncthreads();
+    const float inv = s_inv;
     float* orow = out + (long long)t * hidden;
     float am = 0.0f;
-    for (int h = lane; h < hidden; h += 32) {
-        const float v = __fmul_rn(__fmul_rn(xr[h], inv), w[h]);
+    for (int h = tid; h < hidden; h += kRmsThreads) {
+        const float v = __fmul_rn(__fmul_rn(xs[h], inv), ws[h]);
         orow[h] = v;
+        xs[h] = v;          // read back below by this same thread only
         am = fmaxf(am, fabsf(v));
     }
     if (!q) return;
     #pragma unroll
     for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+    if ((tid & 31) == 0) s_red[tid >> 5] = am;
+    __syncthreads();
+    #pragma unroll
+    for (int i = 0; i < kRmsThreads / 32; ++i) am = fmaxf(am, s_red[i]);
     const float sc = row_scale(am), iv = __fdiv_rn(1.0f, sc);
-    __syncwarp();   // this lane reads back only elements it wrote itself
     int8_t* qr = q + (long long)t * ldq;
-    for (long long h = lane; h < ldq; h += 32) qr[h] = h < hidden ? q8(orow[h], iv) : 0;
-    if (lane == 0) qscale[t] = sc;
+    for (long long h = tid; h < ldq; h += kRmsThreads) qr[h] = h < hidden ? q8(xs[h], iv) : 0;
+    if (tid == 0) qscale[t] = sc;
 }
 
 cudaError_t rmsnorm(const float* x, const float* w, float* out, int seq, int hidden, float eps, cudaStream_t st,
                     int8_t* q, long long ldq, float* qscale) {
     if (seq <= 0 || hidden <= 0 || hidden > 6144 || (q && (ldq < hidden || !qscale))) return cudaErrorInvalidValue;
-    const cudaError_t e = launch_k(rmsnorm_kernel, seq, 32, sizeof(double) * hidden, st, x, w, out, seq, hidden, eps,
+    const size_t smem = (sizeof(double) + 2 * sizeof(float)) * (size_t)hidden;
+    static bool attr = false;
+    if (!attr && smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)((sizeof(double) + 2 * sizeof(float)) * 6144));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const cudaError_t e = launch_k(rmsnorm_kernel, seq, kRmsThreads, smem, st, x, w, out, seq, hidden, eps,
                                    q, ldq, qscale);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();

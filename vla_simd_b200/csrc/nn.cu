@@ -904,23 +904,26 @@ cudaError_t attention_batched(const float* Q, long long ldq, const float* K, lon
         int best_qpt = 0;
         long long best_rows = 0;
         static const int forced = [] {
-            const char* e = std::getenv("VLA_ATT_QPT");   // tuning knob: 1, 2 or 5 query rows per warp
+            const char* e = std::getenv("VLA_ATT_QPT");   // tuning knob: 1, 2, 4 or 5 query rows per warp
             const int v = e ? std::atoi(e) : 0;
-            return v == 1 || v == 2 || v == 5 ? v : 0;
+            return v == 1 || v == 2 || v == 4 || v == 5 ? v : 0;
         }();
-        for (int qpt : {5, 2, 1}) {
+        for (int qpt : {5, 4, 2, 1}) {
             if (att_tiled_smem(8 * qpt, seq_k) > 227 * 1024) continue;
             if (forced && qpt != forced) continue;
             const long long ctas = (long long)((seq_q + 8 * qpt - 1) / (8 * qpt)) * n_q * bs.n;
-            // rows on the busiest SM, weighted by the measured cost of a row at
-            // each tile height (taller tiles reuse every K / V value more:
-            // 1.0 / 1.3 / 1.4 per row for 40 / 16 / 8 rows, Octo shapes)
-            const int w = qpt == 5 ? 10 : qpt == 2 ? 13 : 14;
+            // rows on the busiest SM, weighted by the cost of a row at each
+            // tile height (taller tiles reuse every loaded K / V value more:
+            // 1.0 / 1.3 / 1.4 per row measured for 40 / 16 / 8 rows on Octo
+            // shapes; 32 rows placed by the shared-memory load count per fma)
+            const int w = qpt == 5 ? 10 : qpt == 4 ? 11 : qpt == 2 ? 13 : 14;
             const long long rows = (ctas + 147) / 148 * 8 * qpt * w;
             if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
         }
         if (best_qpt == 5)
             return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
+        if (best_qpt == 4)
+            return launch_attention_tiled<4>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
         if (best_qpt == 2)
             return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
         return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
@@ -1132,8 +1135,19 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
     if (block4) {
         // lanes 0-7: a[l] (k % 16 == l), lanes 8-15: b[l-8] (k % 16 == l); 16-wide steps
         const int K16 = K & ~15;
-        if (lane < 16)
-            for (int k = 0; k < K16; k += 16) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        if (lane < 16) {
+            // 8 steps' operands are loaded before their fmas: the chain waits
+            // on one round of load latency per 8 steps, not per step
+            int k = 0;
+            for (; k + 128 <= K16; k += 128) {
+                float xv[8], wv[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) { xv[u] = xr[k + 16 * u + lane]; wv[u] = wr[k + 16 * u + lane]; }
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) acc = __fmaf_rn(xv[u], wv[u], acc);
+            }
+            for (; k < K16; k += 16) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        }
         kend = K16;
         if (K - K16 >= 8) {                      // one 8-wide step into a
             if (lane < 8) acc = __fmaf_rn(xr[K16 + lane], wr[K16 + lane], acc);
@@ -1145,7 +1159,15 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
     } else {
         // lanes 8j+l: chain j of lane l, 32-wide steps; then 8-wide steps into chain 0
         const int K32 = K & ~31;
-        for (int k = 0; k < K32; k += 32) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
+        int k = 0;
+        for (; k + 256 <= K32; k += 256) {
+            float xv[8], wv[8];
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) { xv[u] = xr[k + 32 * u + lane]; wv[u] = wr[k + 32 * u + lane]; }
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) acc = __fmaf_rn(xv[u], wv[u], acc);
+        }
+        for (; k < K32; k += 32) acc = __fmaf_rn(xr[k + lane], wr[k + lane], acc);
         kend = K32;
         for (; kend + 8 <= K; kend += 8)
             if (lane < 8) acc = __fmaf_rn(xr[kend + lane], wr[kend + lane], acc);
@@ -1176,13 +1198,15 @@ __global__ void linear_f32_kernel(const float* __restrict__ x, long long ldx, co
 }
 
 // The same outputs for many rows (N % 4 == 0: every output takes mm_block4's
-// order; K <= 512). CTA = 32 rows x 32 outputs with both operand tiles staged
-// whole in shared memory; a thread owns a 2 x 2 block of outputs and runs, per
-// output, the 16 lane chains (a[l] over k = 16s + l, b[l] over 16s + 8 + l),
-// the 8-wide step into a, t = a + b, hsum8, the fused scalar tail and + bias
-// in registers: bit for bit the warp kernel's arithmetic, with each staged
-// value feeding two outputs.
+// order). CTA = 32 rows x 32 outputs; K streams through shared memory in
+// chunks of up to kLtK (both operand chunks staged whole); a thread owns a
+// 2 x 2 block of outputs and runs, per output, the 16 lane chains (a[l] over
+// k = 16s + l, b[l] over 16s + 8 + l) across the chunks in k order, then the
+// 8-wide step into a, t = a + b, hsum8, the fused scalar tail and + bias in
+// registers: bit for bit the warp kernel's arithmetic, with each staged value
+// feeding two outputs.
 constexpr int kLtRows = 32;
+constexpr int kLtK = 512;
 
 __global__ void __launch_bounds__(256)
 linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ W,
@@ -1191,16 +1215,11 @@ linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float*
     pdl_wait();     // inputs come from the previous kernel in the stream
     pdl_trigger();
     extern __shared__ __align__(16) float lt_smem[];
-    const int ldk = ((K + 3) & ~3) + 4;            // 16-byte rows, rows 4 banks apart
+    const int kc_max = K < kLtK ? K : kLtK;
+    const int ldk = ((kc_max + 3) & ~3) + 4;       // 16-byte rows, rows 4 banks apart
     float* sx = lt_smem;
     float* sw = lt_smem + kLtRows * ldk;
     const int m0 = blockIdx.y * kLtRows, n0 = blockIdx.x * kLtRows;
-    for (int e = threadIdx.x; e < kLtRows * K; e += blockDim.x) {
-        const int r = e / K, c = e - r * K;
-        sx[r * ldk + c] = m0 + r < M ? x[(long long)(m0 + r) * ldx + c] : 0.0f;
-        sw[r * ldk + c] = n0 + r < N ? W[(long long)(n0 + r) * K + c] : 0.0f;
-    }
-    __syncthreads();
     const int tm = threadIdx.x >> 4, tn = threadIdx.x & 15;
     const float* xr[2] = {sx + tm * ldk, sx + (tm + 16) * ldk};
     const float* wr[2] = {sw + tn * ldk, sw + (tn + 16) * ldk};
@@ -1212,25 +1231,55 @@ linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float*
             #pragma unroll
             for (int l = 0; l < 16; ++l) acc[i][j][l] = 0.0f;
     const int K16 = K & ~15;
-    for (int k = 0; k < K16; k += 16) {
-        #pragma unroll
-        for (int q = 0; q < 4; ++q) {              // lanes 4q .. 4q+3 of the 16
-            const float4 x0 = *reinterpret_cast<const float4*>(xr[0] + k + 4 * q);
-            const float4 x1 = *reinterpret_cast<const float4*>(xr[1] + k + 4 * q);
-            const float4 w0 = *reinterpret_cast<const float4*>(wr[0] + k + 4 * q);
-            const float4 w1 = *reinterpret_cast<const float4*>(wr[1] + k + 4 * q);
-            const float xv[2][4] = {{x0.x, x0.y, x0.z, x0.w}, {x1.x, x1.y, x1.z, x1.w}};
-            const float wv[2][4] = {{w0.x, w0.y, w0.z, w0.w}, {w1.x, w1.y, w1.z, w1.w}};
-            #pragma unroll
-            for (int i = 0; i < 2; ++i)
-                #pragma unroll
-                for (int j = 0; j < 2; ++j)
-                    #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        acc[i][j][4 * q + u] = __fmaf_rn(xv[i][u], wv[j][u], acc[i][j][4 * q + u]);
+    const bool vec = ((K | ldx) & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W)) & 15) == 0;
+    int kc0 = 0;
+    for (;;) {
+        const int kcl = K - kc0 < kLtK ? K - kc0 : kLtK;    // kLtK is a multiple of 16: chunks keep the 16-steps whole
+        if (vec) {                     // 16-byte loads, four rounds in flight per thread
+            const int c4 = kcl >> 2;
+            #pragma unroll 4
+            for (int e = threadIdx.x; e < kLtRows * c4; e += blockDim.x) {
+                const int r = e / c4, c = 4 * (e - r * c4);
+                const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                const float4 xv = m0 + r < M ? *reinterpret_cast<const float4*>(x + (long long)(m0 + r) * ldx + kc0 + c) : z;
+                const float4 wv = n0 + r < N ? *reinterpret_cast<const float4*>(W + (long long)(n0 + r) * K + kc0 + c) : z;
+                *reinterpret_cast<float4*>(sx + r * ldk + c) = xv;
+                *reinterpret_cast<float4*>(sw + r * ldk + c) = wv;
+            }
+        } else {
+            #pragma unroll 4
+            for (int e = threadIdx.x; e < kLtRows * kcl; e += blockDim.x) {
+                const int r = e / kcl, c = e - r * kcl;
+                sx[r * ldk + c] = m0 + r < M ? x[(long long)(m0 + r) * ldx + kc0 + c] : 0.0f;
+                sw[r * ldk + c] = n0 + r < N ? W[(long long)(n0 + r) * K + kc0 + c] : 0.0f;
+            }
         }
+        __syncthreads();
+        const int kend16 = (kc0 + kcl < K16 ? kc0 + kcl : K16) - kc0;
+        for (int k = 0; k < kend16; k += 16) {
+            #pragma unroll
+            for (int q = 0; q < 4; ++q) {              // lanes 4q .. 4q+3 of the 16
+                const float4 x0 = *reinterpret_cast<const float4*>(xr[0] + k + 4 * q);
+                const float4 x1 = *reinterpret_cast<const float4*>(xr[1] + k + 4 * q);
+                const float4 w0 = *reinterpret_cast<const float4*>(wr[0] + k + 4 * q);
+                const float4 w1 = *reinterpret_cast<const float4*>(wr[1] + k + 4 * q);
+                const float xv[2][4] = {{x0.x, x0.y, x0.z, x0.w}, {x1.x, x1.y, x1.z, x1.w}};
+                const float wv[2][4] = {{w0.x, w0.y, w0.z, w0.w}, {w1.x, w1.y, w1.z, w1.w}};
+                #pragma unroll
+                for (int i = 0; i < 2; ++i)
+                    #pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            acc[i][j][4 * q + u] = __fmaf_rn(xv[i][u], wv[j][u], acc[i][j][4 * q + u]);
+            }
+        }
+        if (kc0 + kcl >= K) break;     // the last chunk (it holds k >= K16) stays staged
+        kc0 += kcl;
+        __syncthreads();               // every thread is done with this chunk
     }
-    int kend = K16;
+    const int t16 = K16 - kc0;         // offset of K16 in the staged last chunk
+    int kend = t16;
     if (K - K16 >= 8) {                  // one 8-wide step into a
         #pragma unroll
         for (int i = 0; i < 2; ++i)
@@ -1238,8 +1287,8 @@ linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float*
             for (int j = 0; j < 2; ++j)
                 #pragma unroll
                 for (int l = 0; l < 8; ++l)
-                    acc[i][j][l] = __fmaf_rn(xr[i][K16 + l], wr[j][K16 + l], acc[i][j][l]);
-        kend = K16 + 8;
+                    acc[i][j][l] = __fmaf_rn(xr[i][t16 + l], wr[j][t16 + l], acc[i][j][l]);
+        kend = t16 + 8;
     }
     #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -1251,7 +1300,7 @@ linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float*
             for (int l = 0; l < 8; ++l) t[l] = __fadd_rn(acc[i][j][l], acc[i][j][8 + l]);
             float sum = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[4]), __fadd_rn(t[1], t[5])),
                                   __fadd_rn(__fadd_rn(t[2], t[6]), __fadd_rn(t[3], t[7])));
-            for (int k = kend; k < K; ++k) sum = __fmaf_rn(xr[i][k], wr[j][k], sum);
+            for (int k = kend; k < K - kc0; ++k) sum = __fmaf_rn(xr[i][k], wr[j][k], sum);
             if (m < M && n < N) {
                 float v = bias ? __fadd_rn(sum, bias[n]) : sum;
                 if (post_mul) v = __fmaf_rn(v, post_mul[n], post_add[n]);
@@ -1264,8 +1313,9 @@ linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx, const float*
 cudaError_t linear_f32(const float* x, long long ldx, const float* W, const float* bias, float* out, long long ldo,
                        int M, int N, int K, const float* post_mul, const float* post_add, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
-    if (N % 4 == 0 && K <= 512 && M >= kLtRows && (long long)M * N >= (1LL << 16)) {
-        const size_t smem = sizeof(float) * 2 * kLtRows * (((K + 3) & ~3) + 4);
+    if (N % 4 == 0 && M >= kLtRows && (long long)M * N >= (1LL << 16)) {
+        const int kc = K < kLtK ? K : kLtK;
+        const size_t smem = sizeof(float) * 2 * kLtRows * (((kc + 3) & ~3) + 4);
         static bool attr = false;
         if (!attr) {
             cudaFuncSetAttribute(linear_f32_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
