@@ -131,10 +131,12 @@ def test_attention_tile_heights_vs_reference(dev, reference, sq, sk, nq, nkv):
     assert np.array_equal(got, reference.attention(Q, K, V, nq, nkv, 64, np.float32(0.125)))
 
 
-@pytest.mark.parametrize("seq,N,K", [(50, 720, 1440), (50, 32, 720), (64, 720, 1040), (40, 96, 1037), (33, 4, 1000)])
+@pytest.mark.parametrize("seq,N,K", [(128, 720, 1440), (96, 720, 1037), (400, 720, 520), (50, 720, 1440),
+                                      (50, 32, 720), (33, 4, 1000)])
 def test_dense_linear_f32_long_k_vs_reference(dev, reference, seq, N, K):
-    """The tiled fp32 linear streaming K > 512 through shared memory in
-    chunks (the SmolVLA expert's time MLP and projections): the reference's bits."""
+    """K > 512 (the SmolVLA expert's time MLP and projections): the tiled
+    kernel streaming K through shared memory in chunks (rows x outputs >=
+    65536) and the warp-per-output kernel below that: the reference's bits."""
     from vla_simd_b200 import ops
     rng = np.random.default_rng(seq * N + K)
     x = rng.standard_normal((seq, K), dtype=np.float32)
