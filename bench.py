@@ -997,6 +997,68 @@ def run_reference(args):
     }), flush=True)
 
 
+def timeline_table(events, nsteps: int, top: int = 30):
+    """Per-kernel marginal device time of the profiled steps: kernels in order
+    of their end, each charged its end minus the latest earlier end (under
+    programmatic dependent launch a kernel starts before its predecessor ends,
+    so its own duration overstates what it adds to the step)."""
+    import collections
+    ks = sorted(events, key=lambda k: k[1])
+    inc = collections.defaultdict(lambda: [0, 0.0])
+    prev = ks[0][0]
+    for s_, e_, name in ks:
+        key = name.replace("(anonymous namespace)::", "").replace("vsb::", "").split("(")[0]
+        key = key[5:] if key.startswith("void ") else key
+        inc[key][0] += 1
+        inc[key][1] += max(0.0, e_ - prev)
+        prev = max(prev, e_)
+    total = sum(v[1] for v in inc.values())
+    rows = sorted(inc.items(), key=lambda x: -x[1][1])[:top]
+    return total / nsteps, [(k, c / nsteps, t / nsteps, t / c, t / total) for k, (c, t) in rows]
+
+
+def run_timeline(args):
+    """One GPU: profile graph replays of the ACT step (or SmolVLA queries) with
+    CUPTI (torch.profiler) and print each kernel's marginal time per step."""
+    import torch
+    from torch.profiler import profile, ProfilerActivity
+    torch.cuda.set_device(0)
+    n = max(args.steps, 1) if args.steps <= 20 else 5
+    if args.model == "smolvla":
+        os.environ["SMOLVLA_INT8"] = str(SMOLVLA_MASK)
+        from vla_simd_b200 import SmolvlaPolicy, synth
+        sh = synth.SMOLVLA_BASELINE
+        pol = SmolvlaPolicy(synth.write_smolvla_checkpoint(os.path.join(tempfile.mkdtemp(), "s"), sh, seed=0),
+                            max_batch=args.batch)
+        f, ins, st_, nz = synth.smolvla_inputs(sh, seed=1, batch=args.batch)
+        step = lambda: pol.predict_batch(f, ins, st_, nz)  # noqa: E731
+    else:
+        os.environ["ACT_INT8"] = str(INT8_MASK)
+        from vla_simd_b200 import ActPolicy, synth
+        pol = ActPolicy(synth.write_act_checkpoint(os.path.join(tempfile.mkdtemp(), "a"), synth.ACT_BASELINE, seed=0))
+        f, s_ = synth.act_inputs(synth.ACT_BASELINE, seed=1)
+        pol.predict(f, s_)
+        stream = torch.cuda.Stream()
+        step = lambda: pol.enqueue(stream.cuda_stream)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            step()
+        torch.cuda.synchronize()
+    ev = [(e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+          if e.device_type == torch.autograd.DeviceType.CUDA
+          and not any(w in e.name.lower() for w in ("memset", "memcpy"))]
+    per_step, rows = timeline_table(ev, n)
+    print(f"# {args.model} step timeline: {len(ev) / n:.0f} kernels per step, {per_step:.1f} us per step "
+          f"(marginal sum over {n} profiled steps, L2 warm)")
+    print("| kernel | launches / step | us / step | us / launch | share |\n|---|---:|---:|---:|---:|")
+    for k, c, t, tl, fr in rows:
+        print(f"| `{k}` | {c:.1f} | {t:.1f} | {tl:.2f} | {100 * fr:.1f}% |")
+    pol.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1014,7 +1076,12 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="queries per step per GPU (--model dp / octo)")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="profile a few steps (--model act or smolvla) and print each kernel's marginal time")
     args = ap.parse_args()
+    if args.timeline:
+        run_timeline(args)
+        return
     if args.op:
         run_op(args.op)
         return

@@ -463,6 +463,9 @@ bool ActPolicy::load(const std::string& dir) {
     d_sb_ = dalloc<float>(R);
     d_satt_ = dalloc<float>(R);
     d_sff_ = dalloc<float>(R);
+    d_att_cnt_ = dalloc<unsigned int>(kAttCounters);
+    if (d_att_cnt_ && cudaMemset(d_att_cnt_, 0, sizeof(unsigned int) * kAttCounters) != cudaSuccess)
+        fail("cudaMemset failed");
     d_xp_ = dalloc<float>((size_t)R * d);
     d_qea_ = dalloc<int8_t>((size_t)T * ldq_);
     d_qeb_ = dalloc<int8_t>((size_t)T * ldq_);
@@ -556,6 +559,18 @@ cudaError_t ActPolicy::join(cudaStream_t st) {
     return cudaStreamWaitEvent(st, ev_join_, 0);
 }
 
+// The attention output's int8 row copy (d_qatt_ / d_satt_), written by the
+// attention launch (nn.h AttQuant).
+AttQuant ActPolicy::att_quant() const {
+    AttQuant a;
+    a.q = d_qatt_;
+    a.ldq = ldq_;
+    a.scale = d_satt_;
+    a.counters = d_att_cnt_;
+    a.n_counters = kAttCounters;
+    return a;
+}
+
 cudaError_t ActPolicy::run_backbone(cudaStream_t st) {
     const int F = n_cams_;
     unsigned int* slot = d_amax_;
@@ -613,11 +628,10 @@ cudaError_t ActPolicy::run_encoder(cudaStream_t st) {
             VSB_TRY(run_linear(l.wqk, d_xp_, d_qa_, d_sa_, nullptr, T, d_qk_, 2 * d, 0, nullptr, 0, st));
             VSB_TRY(join(st));
         }
+        // the o-projection's int8 input comes out of the attention launch itself
+        const AttQuant aq = att_quant();
         VSB_TRY(attention(d_qk_, 2 * d, d_qk_ + d, 2 * d, d_v_, d, d_att_, d, T, T, cfg_.heads, cfg_.heads,
-                          cfg_.head_dim, scale, nullptr, st));
-        if (l.wo.int8) {
-            VSB_TRY(quantize_rows(d_att_, d, nullptr, 0, T, d, d_qatt_, ldq_, d_satt_, nullptr, 0, nullptr, st));
-        }
+                          cfg_.head_dim, scale, nullptr, st, l.wo.int8 ? &aq : nullptr));
         VSB_TRY(run_linear(l.wo, d_att_, d_qatt_, d_satt_, nullptr, T, d_x_, d, kEpiAdd, d_x_, d, st));
         VSB_TRY(layernorm(d_x_, d_x_, l.n1s, l.n1b, T, d, cfg_.ln_eps, nullptr, d_qa_, d_sa_, nullptr, nullptr, ldq_, st));
         VSB_TRY(run_linear(l.w1, d_x_, d_qa_, d_sa_, nullptr, T, d_ff_, cfg_.ff, kEpiRelu, nullptr, 0, st));
@@ -661,9 +675,9 @@ cudaError_t ActPolicy::run_decoder(cudaStream_t st, bool unnormalize) {
             VSB_TRY(decoder_self_block(l, st));
             VSB_TRY(decoder_cross_queries(l, d_qk_, st));
         }
+        const AttQuant aq = att_quant();
         VSB_TRY(attention(cq, d, d_ck_, d, d_cv_, d, d_att_, d, C, T, cfg_.heads, cfg_.heads, cfg_.head_dim,
-                          scale, nullptr, st));
-        VSB_TRY(quantize_rows(d_att_, d, nullptr, 0, C, d, d_qatt_, ldq_, d_satt_, nullptr, 0, nullptr, st));
+                          scale, nullptr, st, &aq));
         VSB_TRY(run_linear(l.c_wo, d_att_, d_qatt_, d_satt_, nullptr, C, d_dx_, d, kEpiAdd, d_dx_, d, st));
         VSB_TRY(layernorm(d_dx_, d_dx_, l.n2s, l.n2b, C, d, cfg_.ln_eps, nullptr, d_qatt_, d_satt_, nullptr, nullptr,
                           ldq_, st));
@@ -690,9 +704,9 @@ cudaError_t ActPolicy::decoder_self_block(const DecLayerDev& l, cudaStream_t st)
     if (!l.s_wqk.int8) VSB_TRY(add_f32(d_dx_, d_dec_pos_, d_xp_, (long long)C * d, st));
     VSB_TRY(run_linear(l.s_wqk, d_xp_, d_qatt_, d_satt_, nullptr, C, d_qk_, 2 * d, 0, nullptr, 0, st));
     VSB_TRY(run_linear(l.s_wv, d_dx_, d_qb_, d_sb_, nullptr, C, d_v_, d, 0, nullptr, 0, st));
+    const AttQuant aq = att_quant();
     VSB_TRY(attention(d_qk_, 2 * d, d_qk_ + d, 2 * d, d_v_, d, d_att_, d, C, C, cfg_.heads, cfg_.heads,
-                      cfg_.head_dim, scale, nullptr, st));
-    VSB_TRY(quantize_rows(d_att_, d, nullptr, 0, C, d, d_qatt_, ldq_, d_satt_, nullptr, 0, nullptr, st));
+                      cfg_.head_dim, scale, nullptr, st, &aq));
     VSB_TRY(run_linear(l.s_wo, d_att_, d_qatt_, d_satt_, nullptr, C, d_dx_, d, kEpiAdd, d_dx_, d, st));
     return layernorm(d_dx_, d_dx_, l.n1s, l.n1b, C, d, cfg_.ln_eps, d_dec_pos_, d_qatt_, d_satt_, nullptr, nullptr,
                      ldq_, st);

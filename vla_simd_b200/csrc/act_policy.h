@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include "conv_exec.h"
+#include "nn.h"
 
 #include <cstdint>
 #include <string>
@@ -143,6 +144,9 @@ class ActPolicy {
     float* d_col_f_ = nullptr;
     float* d_col_scale_ = nullptr;
     unsigned int* d_amax_ = nullptr;
+    static constexpr int kAttCounters = 4096;   // attention query-tile arrival counters (fused quantization)
+    unsigned int* d_att_cnt_ = nullptr;
+    AttQuant att_quant() const;
     int n_amax_ = 0;
     float *d_x_ = nullptr, *d_qk_ = nullptr, *d_v_ = nullptr, *d_att_ = nullptr, *d_ff_ = nullptr;
     float *d_dx_ = nullptr, *d_ck_ = nullptr, *d_cv_ = nullptr, *d_feat_ = nullptr;

@@ -5,6 +5,7 @@
 #include "sm100.cuh"
 #include "launch.cuh"
 #include "nn.h"
+#include "quant.h"
 
 #include <cfloat>
 #include <cmath>
@@ -533,12 +534,90 @@ __host__ __device__ constexpr size_t att_tiled_smem(int qp, int seq_k) {
     return sizeof(float) * ((size_t)qp * att_row_stride(seq_k) + (size_t)qp * kAttRS + 2 * kAttTK * kAttRS);
 }
 
+// Fused row quantization of a finished attention output tile (AttQuant): the
+// CTA's O stores are made visible, its arrival counted; the last CTA of the
+// query tile (one per head, gridDim.y of them) reads the tile's rows back
+// through L2 and quantizes them as quantize_rows does. Warp w takes rows
+// w + 8j (j < QPT); CH = 16-byte chunks per lane per row (rows of up to
+// 128*CH columns), and the loads of RB rows are issued before any is used.
+template <int QPT, int CH>
+__device__ __forceinline__ void att_quant_rows(const float* O, long long ldo, int q0, int seq_q, int kdim,
+                                               const AttQuant& qz) {
+    constexpr int RB = 20 / CH < QPT ? 20 / CH : QPT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int8_t* qb = qz.q + (long long)blockIdx.z * qz.zq;
+    float* sb = qz.scale + (long long)blockIdx.z * qz.zs;
+    for (int j0 = 0; j0 < QPT; j0 += RB) {
+        float4 v[RB][CH];
+        #pragma unroll
+        for (int b = 0; b < RB; ++b) {
+            const int q = q0 + warp + 8 * (j0 + b);
+            const bool ok = j0 + b < QPT && q < seq_q;
+            const float* orow = O + (long long)q * ldo;
+            #pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                const int k = 4 * lane + 128 * i;
+                v[b][i] = (ok && k < kdim) ? __ldcg(reinterpret_cast<const float4*>(orow + k))
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        #pragma unroll
+        for (int b = 0; b < RB; ++b) {
+            const int q = q0 + warp + 8 * (j0 + b);
+            if (!(j0 + b < QPT && q < seq_q)) continue;     // warp-uniform
+            float m = 0.0f;
+            #pragma unroll
+            for (int i = 0; i < CH; ++i)
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v[b][i].x), fabsf(v[b][i].y)), fmaxf(fabsf(v[b][i].z), fabsf(v[b][i].w))));
+            m = warp_max_f(m);
+            const float sc = nn_row_scale(m), inv = __fdiv_rn(1.0f, sc);
+            int8_t* qr = qb + (long long)q * qz.ldq;
+            #pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                const int k = 4 * lane + 128 * i;
+                if (k < kdim)
+                    *reinterpret_cast<char4*>(qr + k) = make_char4(nn_q8(v[b][i].x, inv), nn_q8(v[b][i].y, inv),
+                                                                   nn_q8(v[b][i].z, inv), nn_q8(v[b][i].w, inv));
+            }
+            for (long long k = kdim + 4 * lane; k < qz.ldq; k += 128)
+                *reinterpret_cast<char4*>(qr + k) = make_char4(0, 0, 0, 0);
+            if (lane == 0) sb[q] = sc;
+        }
+    }
+}
+
+template <int QPT>
+__device__ __forceinline__ void att_fused_quant(const float* O, long long ldo, int q0, int seq_q, int kdim,
+                                                const AttQuant& qz) {
+    // the barrier orders the CTA's stores before thread 0's fence, which makes
+    // them visible device-wide before its arrival is counted (the pattern of a
+    // cooperative grid barrier); the last arrival fences again before reading
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int* c = qz.counters + ((long long)blockIdx.z * gridDim.x + blockIdx.x);
+        __threadfence();
+        const unsigned int prev = atomicAdd(c, 1u);
+        const int last = prev + 1 == gridDim.y;
+        if (last) {
+            atomicExch(c, 0u);   // every head of the tile has arrived: ready for the next launch
+            __threadfence();
+        }
+        s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    if (kdim <= 512) att_quant_rows<QPT, 4>(O, ldo, q0, seq_q, kdim, qz);
+    else if (kdim <= 768) att_quant_rows<QPT, 6>(O, ldo, q0, seq_q, kdim, qz);
+    else att_quant_rows<QPT, 8>(O, ldo, q0, seq_q, kdim, qz);
+}
+
 template <int QPT>
 __global__ void __launch_bounds__(256, 1)
 attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                        const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
                        int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask,
-                       AttBatch bs) {
+                       AttBatch bs, AttQuant qz) {
     VSB_ATT_BATCH_OFFSET(bs);
     constexpr int QP = 8 * QPT;
     constexpr int kTile = kAttTK * kAttRS;
@@ -831,12 +910,14 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             *reinterpret_cast<float2*>(O + (long long)q * ldo + (long long)h * kAttD + d0) =
                 make_float2(o[a][0], o[a][1]);
     }
+    if (qz.q) att_fused_quant<QPT>(O, ldo, q0, seq_q, n_q * kAttD, qz);
 }
 
 template <int QPT>
 cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                                    long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
-                                   float scale, const float* mask, const AttBatch& bs, cudaStream_t st) {
+                                   float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
+                                   const AttQuant& qz = AttQuant{}) {
     const size_t smem = att_tiled_smem(8 * QPT, seq_k);
     static int configured = 0;
     if ((int)smem > configured) {
@@ -847,7 +928,7 @@ cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K
     }
     dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q, bs.n);
     const cudaError_t e = launch_k(attention_tiled_kernel<QPT>, grid, 256, smem, st, Q, ldq, K, ldk, V, ldv, O, ldo,
-                                   seq_q, seq_k, n_q, n_kv, scale, mask, bs);
+                                   seq_q, seq_k, n_q, n_kv, scale, mask, bs, qz);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -875,14 +956,45 @@ cudaError_t launch_attention(const float* Q, long long ldq, const float* K, long
 
 cudaError_t attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
                       float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, int head_dim, float scale,
-                      const float* mask, cudaStream_t st) {
+                      const float* mask, cudaStream_t st, const AttQuant* qz) {
     return attention_batched(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, head_dim, scale, mask,
-                             AttBatch{}, st);
+                             AttBatch{}, st, qz);
 }
+
+// The exact kernels: the register-tiled one where its score rows fit (it
+// fuses the row quantization when qz.q is set: *fused), else the one-pass
+// kernel; the tensor-core kernel when VLA_ATT_TC=1.
+static cudaError_t attention_select(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                                    long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                                    int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
+                                    const AttQuant& qz, bool* fused);
 
 cudaError_t attention_batched(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                               long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
-                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st) {
+                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
+                              const AttQuant* qz) {
+    const bool quant = qz && qz->q;
+    if (quant && (!qz->scale || qz->ldq < (long long)n_q * head_dim || (qz->ldq & 3) ||
+                  (reinterpret_cast<uintptr_t>(qz->q) & 3) || (qz->zq & 3)))
+        return cudaErrorInvalidValue;
+    // fusable: rows of at most 1024 columns and a counter per query tile
+    const bool fusable = quant && qz->counters && (long long)n_q * head_dim <= 1024 &&
+                         (long long)((seq_q + 7) / 8) * bs.n <= qz->n_counters;
+    bool fused = false;
+    cudaError_t e = attention_select(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, head_dim, scale, mask,
+                                     bs, st, fusable ? *qz : AttQuant{}, &fused);
+    if (e != cudaSuccess || !quant || fused) return e;
+    for (int z = 0; z < bs.n && e == cudaSuccess; ++z)
+        e = quantize_rows(O + z * bs.o, ldo, nullptr, 0, seq_q, n_q * head_dim, qz->q + z * qz->zq, qz->ldq,
+                          qz->scale + z * qz->zs, nullptr, 0, nullptr, st);
+    return e;
+}
+
+static cudaError_t attention_select(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
+                                    long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
+                                    int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
+                                    const AttQuant& qz, bool* fused) {
+    *fused = false;
     if (head_dim != kAttD || seq_q <= 0 || seq_k <= 0 || n_q <= 0 || n_kv <= 0 || n_q % n_kv || bs.n < 1 ||
         bs.n > 65535)
         return cudaErrorInvalidValue;
@@ -920,13 +1032,20 @@ cudaError_t attention_batched(const float* Q, long long ldq, const float* K, lon
             const long long rows = (ctas + 147) / 148 * 8 * qpt * w;
             if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
         }
+        // The fused quantization runs on one CTA per query tile after the
+        // tile's heads finish: measured against a separate quantize_rows
+        // launch in a graph, it saves 0.5-2 us at 8-16 rows per tile (the
+        // SmolVLA expert, ACT's decoder) and costs 1.3 us at 40 (ACT's
+        // encoder), where the separate launch spreads the rows over more SMs.
+        *fused = qz.q != nullptr && best_qpt <= 2;
+        const AttQuant none;
         if (best_qpt == 5)
-            return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
+            return launch_attention_tiled<5>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st, none);
         if (best_qpt == 4)
-            return launch_attention_tiled<4>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
+            return launch_attention_tiled<4>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st, none);
         if (best_qpt == 2)
-            return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
-        return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st);
+            return launch_attention_tiled<2>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st, qz);
+        return launch_attention_tiled<1>(Q, ldq, K, ldk, V, ldv, O, ldo, seq_q, seq_k, n_q, n_kv, scale, mask, bs, st, qz);
     }
     // Longer key ranges (> ~1100 keys): score rows of fewer queries per CTA.
     // 16 queries x 128 threads per CTA: measured fastest among 8..32 queries x

@@ -14,9 +14,24 @@ cudaError_t layernorm(const float* x, float* out, const float* w, const float* b
 
 // Multi-head attention, head_dim 64, rows of Q/K/V/O are tokens with the heads
 // side by side (token-major, [seq][heads*64] with leading dimensions).
+//
+// Optional fused output (AttQuant): the per-row int8 quantization of O for the
+// next W8A8 GEMM (quantize_rows' arithmetic over the n_q*64 columns of a row:
+// absmax scale, q8, zero past them up to ldq). The attention CTAs of one query
+// tile (one per head) count their arrivals in counters[tile]; the last one to
+// finish quantizes the tile's rows and sets the counter back to zero, so no
+// CTA waits on another and no quantizer launch follows.
+struct AttQuant {
+    int8_t* q = nullptr;                 // [rows][ldq]
+    long long ldq = 0;
+    float* scale = nullptr;              // [rows]
+    unsigned int* counters = nullptr;    // zero before first use; left zero
+    long long n_counters = 0;
+    long long zq = 0, zs = 0;            // per-sequence strides of q (bytes) and scale (floats)
+};
 cudaError_t attention(const float* Q, long long ldq, const float* K, long long ldk, const float* V, long long ldv,
                       float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, int head_dim, float scale,
-                      const float* mask, cudaStream_t st);
+                      const float* mask, cudaStream_t st, const AttQuant* qz = nullptr);
 
 // n independent sequences in one launch: sequence z reads Q + z*q, K + z*k,
 // V + z*v, mask + z*mask and writes O + z*o (element strides, multiples of 4).
@@ -26,7 +41,8 @@ struct AttBatch {
 };
 cudaError_t attention_batched(const float* Q, long long ldq, const float* K, long long ldk, const float* V,
                               long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
-                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st);
+                              int head_dim, float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
+                              const AttQuant* qz = nullptr);
 
 // The tensor-core attention (attn_tc.cu): 3xTF32 tcgen05 MMAs for QK^T and PV,
 // online softmax. Not bit-identical to the reference; attention_batched routes

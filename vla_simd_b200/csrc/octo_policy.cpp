@@ -526,8 +526,12 @@ bool OctoPolicy::alloc_buffers() {
                    (size_t)round16(TD5), (size_t)round16(c.time_dim + D + FL), (size_t)round16(4 * c.hidden)});
     qrows = std::max({qrows, (size_t)rows, (size_t)F * stem_w_.tokens(), (size_t)Bm * n});
     q_cap_ = qrows * qk;
+    q_rows_ = qrows;
     d_q_ = dalloc<int8_t>(q_cap_);
     d_qs_ = dalloc<float>(qrows);
+    d_att_cnt_ = dalloc<unsigned int>(kAttCounters);
+    if (d_att_cnt_ && cudaMemset(d_att_cnt_, 0, sizeof(unsigned int) * kAttCounters) != cudaSuccess)
+        fail("cudaMemset failed");
 
     // head
     d_cond_table_ = dalloc<float>((size_t)c.steps * c.time_dim);
@@ -690,6 +694,23 @@ cudaError_t OctoPolicy::set_instruction(int b, const char* instruction) {
 // ------------------------------------------------------------- layers
 // int8 layers: quantize_act_i8 of each row of x, then the W8A8 GEMM
 // (nn::Linear::forward, src/nn/linear.cpp:121-133); fp32 layers: the fp32 GEMM.
+// The int8 row copy (d_q_ / d_qs_) of an attention output of `rows` rows of K
+// columns, written by the attention launch itself (nn.h AttQuant); sequences
+// of seq_rows rows each. Null q when the scratch cannot hold it.
+AttQuant OctoPolicy::att_quant(int rows, int K, int seq_rows) const {
+    AttQuant a;
+    const long long ldq = round16(K);
+    if ((size_t)rows > q_rows_ || (size_t)rows * ldq > q_cap_) return a;
+    a.q = d_q_;
+    a.ldq = ldq;
+    a.scale = d_qs_;
+    a.counters = d_att_cnt_;
+    a.n_counters = kAttCounters;
+    a.zq = (long long)seq_rows * ldq;
+    a.zs = seq_rows;
+    return a;
+}
+
 cudaError_t OctoPolicy::linear(const DevLinear& l, const float* x, long long ldx, int M, float* out, long long ldo,
                                int mode, const float* res, long long ldr, cudaStream_t st) {
     if (l.int8) {
@@ -790,9 +811,12 @@ cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, boo
         bs.mask = (long long)T * T;
         if (!last) {
             bs.o = (long long)T * D;
+            // the o-projection's int8 input comes out of the attention launch
+            const AttQuant aq = att_quant(static_cast<int>(rows), D, T);
+            if (L.wo.int8 && !aq.q) return cudaErrorInvalidValue;
             VSB_TRY(attention_batched(d_qkv_, 3 * D, d_qkv_ + D, 3 * D, d_qkv_ + 2 * D, 3 * D, d_att_, D, T, T, c.heads,
-                                      c.heads, c.head_dim, scale, d_mask_, bs, st));
-            VSB_TRY(linear(L.wo, d_att_, D, static_cast<int>(rows), d_x_, D, kEpiAdd, d_x_, D, st));
+                                      c.heads, c.head_dim, scale, d_mask_, bs, st, L.wo.int8 ? &aq : nullptr));
+            VSB_TRY(linear_q(L.wo, d_q_, d_qs_, d_att_, D, static_cast<int>(rows), d_x_, D, kEpiAdd, d_x_, D, st));
             VSB_TRY(layernorm(d_x_, d_h_, L.ln2s, L.ln2b, static_cast<int>(rows), D, c.ln_eps, nullptr,
                               L.w1.int8 ? d_q_ : nullptr, L.w1.int8 ? d_qs_ : nullptr, nullptr, nullptr, ldq, st));
             VSB_TRY(linear_q(L.w1, d_q_, d_qs_, d_h_, D, static_cast<int>(rows), d_ff_, c.mlp, 0, nullptr, 0, st));
@@ -801,10 +825,13 @@ cudaError_t OctoPolicy::forward(int B, int wnd, bool wrist, cudaStream_t st, boo
             // readout-only final layer (EncoderLayer::forward_last_row,
             // src/nn/encoder.cpp:80-111): K/V of every token, the rest for row ro
             bs.o = D;
+            const AttQuant aq = att_quant(B, D, 1);
+            if (L.wo.int8 && !aq.q) return cudaErrorInvalidValue;
             VSB_TRY(attention_batched(d_qkv_ + (long long)ro * 3 * D, 3 * D, d_qkv_ + D, 3 * D, d_qkv_ + 2 * D, 3 * D,
                                       d_att_, D, 1, T, c.heads, c.heads, c.head_dim, scale,
-                                      d_mask_ + (long long)ro * T, bs, st));
-            VSB_TRY(linear(L.wo, d_att_, D, B, d_xr_, D, kEpiAdd, d_x_ + (long long)ro * D, (long long)T * D, st));
+                                      d_mask_ + (long long)ro * T, bs, st, L.wo.int8 ? &aq : nullptr));
+            VSB_TRY(linear_q(L.wo, d_q_, d_qs_, d_att_, D, B, d_xr_, D, kEpiAdd, d_x_ + (long long)ro * D,
+                             (long long)T * D, st));
             VSB_TRY(layernorm(d_xr_, d_h_, L.ln2s, L.ln2b, B, D, c.ln_eps, nullptr, L.w1.int8 ? d_q_ : nullptr,
                               L.w1.int8 ? d_qs_ : nullptr, nullptr, nullptr, ldq, st));
             VSB_TRY(linear_q(L.w1, d_q_, d_qs_, d_h_, D, B, d_ff_, c.mlp, 0, nullptr, 0, st));

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include "conv_exec.h"
+#include "nn.h"
 #include "t5_tokenizer.h"
 
 #include <cstdint>
@@ -195,7 +196,10 @@ class OctoPolicy {
     float *d_xr_ = nullptr, *d_emb_ = nullptr;
     int8_t* d_q_ = nullptr;
     float* d_qs_ = nullptr;
-    size_t q_cap_ = 0;
+    size_t q_cap_ = 0, q_rows_ = 0;
+    static constexpr int kAttCounters = 1 << 16;   // attention query-tile arrival counters (fused quantization)
+    unsigned int* d_att_cnt_ = nullptr;
+    AttQuant att_quant(int rows, int K, int seq_rows) const;
 
     // head
     float *d_hin_ = nullptr, *d_hh_ = nullptr, *d_hn_ = nullptr, *d_wide_ = nullptr, *d_eps_ = nullptr,

@@ -477,6 +477,9 @@ bool SmolvlaPolicy::alloc_buffers() {
     q_cap_ = rows_max * k_max;
     d_q_ = dalloc<int8_t>(q_cap_);
     d_qs_ = dalloc<float>(rows_max);
+    d_att_cnt_ = dalloc<unsigned int>(kAttCounters);
+    if (d_att_cnt_ && cudaMemset(d_att_cnt_, 0, sizeof(unsigned int) * kAttCounters) != cudaSuccess)
+        fail("cudaMemset failed");
     // RoPE tables: positions up to the prefix plus the chunk
     max_pos_ = np + C;
     {
@@ -596,6 +599,23 @@ cudaError_t SmolvlaPolicy::linear(const DevLinear& l, const float* x, long long 
     return linear_q(l, d_q_, d_qs_, x, ldx, M, out, ldo, mode, res, ldr, st);
 }
 
+// The int8 row copy (d_q_ / d_qs_) of an attention output of `rows` rows of K
+// columns, written by the attention launch itself (nn.h AttQuant); sequences
+// of seq_rows rows each. Null q when the scratch cannot hold it.
+AttQuant SmolvlaPolicy::att_quant(int rows, int K, int seq_rows) const {
+    AttQuant a;
+    const long long ldq = round16(K);
+    if ((size_t)rows > q_rows_ || (size_t)rows * ldq > q_cap_) return a;
+    a.q = d_q_;
+    a.ldq = ldq;
+    a.scale = d_qs_;
+    a.counters = d_att_cnt_;
+    a.n_counters = kAttCounters;
+    a.zq = (long long)seq_rows * ldq;
+    a.zs = seq_rows;
+    return a;
+}
+
 cudaError_t SmolvlaPolicy::rmsnorm_for(const float* x, const float* w, float* xn, int rows, int K, float eps, bool int8,
                                        cudaStream_t st) {
     if (int8 && ((size_t)rows > q_rows_ || (size_t)rows * round16(K) > q_cap_)) return cudaErrorInvalidValue;
@@ -662,9 +682,13 @@ cudaError_t SmolvlaPolicy::run_vision(int F, int h, int w, cudaStream_t st) {
         bs.n = F;
         bs.q = bs.k = bs.v = (long long)NP * 3 * H;
         bs.o = (long long)NP * H;
-        VSB_TRY(attention_batched(d_vqkv_, 3 * H, d_vqkv_ + H, 3 * H, d_vqkv_ + 2 * H, 3 * H, d_vatt_, H, NP, NP,
-                                  c.v_heads, c.v_heads, c.v_hd, scale, nullptr, bs, st));
-        VSB_TRY(linear(L.wo, d_vatt_, H, static_cast<int>(rows), d_vh_, H, kEpiAdd, d_vh_, H, st));
+        {   // the o-projection's int8 input comes out of the attention launch
+            const AttQuant aq = att_quant(static_cast<int>(rows), H, NP);
+            if (L.wo.int8 && !aq.q) return cudaErrorInvalidValue;
+            VSB_TRY(attention_batched(d_vqkv_, 3 * H, d_vqkv_ + H, 3 * H, d_vqkv_ + 2 * H, 3 * H, d_vatt_, H, NP, NP,
+                                      c.v_heads, c.v_heads, c.v_hd, scale, nullptr, bs, st, L.wo.int8 ? &aq : nullptr));
+            VSB_TRY(linear_q(L.wo, d_q_, d_qs_, d_vatt_, H, static_cast<int>(rows), d_vh_, H, kEpiAdd, d_vh_, H, st));
+        }
         VSB_TRY(layernorm(d_vh_, d_vn_, L.ln2s, L.ln2b, static_cast<int>(rows), H, c.v_eps, nullptr,
                           L.w1.int8 ? d_q_ : nullptr, L.w1.int8 ? d_qs_ : nullptr, nullptr, nullptr, ldq, st));
         VSB_TRY(linear_q(L.w1, d_q_, d_qs_, d_vn_, H, static_cast<int>(rows), d_vff_, I, 0, nullptr, 0, st));
@@ -704,9 +728,13 @@ cudaError_t SmolvlaPolicy::run_vlm(int B, cudaStream_t st) {
         bs.q = bs.k = bs.v = (long long)np * LD;
         bs.o = (long long)np * QF;
         bs.mask = (long long)np * np;
-        VSB_TRY(attention_batched(qkv, LD, qkv + QF, LD, qkv + QF + KV, LD, d_att_, QF, np, np, c.n_q, c.n_kv, c.hd,
-                                  scale, d_pmask_, bs, st));
-        VSB_TRY(linear(w.wo, d_att_, QF, rows, d_x_, D, kEpiAdd, d_x_, D, st));
+        {
+            const AttQuant aq = att_quant(rows, QF, np);
+            if (w.wo.int8 && !aq.q) return cudaErrorInvalidValue;
+            VSB_TRY(attention_batched(qkv, LD, qkv + QF, LD, qkv + QF + KV, LD, d_att_, QF, np, np, c.n_q, c.n_kv,
+                                      c.hd, scale, d_pmask_, bs, st, w.wo.int8 ? &aq : nullptr));
+            VSB_TRY(linear_q(w.wo, d_q_, d_qs_, d_att_, QF, rows, d_x_, D, kEpiAdd, d_x_, D, st));
+        }
         VSB_TRY(rmsnorm_for(d_x_, w.ln_post, d_xn_, rows, D, c.rms_eps, w.wgu.int8, st));
         VSB_TRY(linear_q(w.wgu, d_q_, d_qs_, d_xn_, D, rows, d_gu_, 2 * F, 0, nullptr, 0, st));
         if (w.wdown.int8) {
@@ -758,6 +786,8 @@ cudaError_t SmolvlaPolicy::run_expert(int B, bool guided, cudaStream_t st) {
             bs.n = B;
             bs.q = (long long)C * eQF;
             bs.o = (long long)C * eQF;
+            const AttQuant eq = att_quant(rows, eQF, C);   // the o-projection's int8 input, from the attention
+            if (w.wo.int8 && !eq.q) return cudaErrorInvalidValue;
             if (w.self_attn) {
                 VSB_TRY(linear_q(w.wkv, d_q_, d_qs_, d_ehn_, EH, rows, d_ekv_, 2 * KV, 0, nullptr, 0, st));
                 VSB_TRY(rope_table(d_eq_, eQF, rows, c.e_nq, c.e_hd, d_pos_full_, rope_aex_, max_pos_, d_status_, st));
@@ -766,15 +796,15 @@ cudaError_t SmolvlaPolicy::run_expert(int B, bool guided, cudaStream_t st) {
                 bs.k = bs.v = (long long)SK * 2 * KV;
                 bs.mask = (long long)C * SK;
                 VSB_TRY(attention_batched(d_eq_, eQF, d_kvf_[L], 2 * KV, d_kvf_[L] + KV, 2 * KV, d_eatt_, eQF, C, SK,
-                                          c.e_nq, c.e_nkv, c.e_hd, scale, d_dmask_, bs, st));
+                                          c.e_nq, c.e_nkv, c.e_hd, scale, d_dmask_, bs, st, w.wo.int8 ? &eq : nullptr));
             } else {
                 VSB_TRY(rope_table(d_eq_, eQF, rows, c.e_nq, c.e_hd, d_pos_reb_, rope_aex_, max_pos_, d_status_, st));
                 bs.k = bs.v = (long long)np * 2 * KV;
                 bs.mask = (long long)C * np;
                 VSB_TRY(attention_batched(d_eq_, eQF, d_ckv_[L], 2 * KV, d_ckv_[L] + KV, 2 * KV, d_eatt_, eQF, C, np,
-                                          c.e_nq, c.e_nkv, c.e_hd, scale, d_cmask_, bs, st));
+                                          c.e_nq, c.e_nkv, c.e_hd, scale, d_cmask_, bs, st, w.wo.int8 ? &eq : nullptr));
             }
-            VSB_TRY(linear(w.wo, d_eatt_, eQF, rows, d_eh_, EH, kEpiAdd, d_eh_, EH, st));
+            VSB_TRY(linear_q(w.wo, d_q_, d_qs_, d_eatt_, eQF, rows, d_eh_, EH, kEpiAdd, d_eh_, EH, st));
             VSB_TRY(rmsnorm_for(d_eh_, w.ln_post, d_ehn_, rows, EH, c.e_eps, w.wgu.int8, st));
             VSB_TRY(linear_q(w.wgu, d_q_, d_qs_, d_ehn_, EH, rows, d_egu_, 2 * EF, 0, nullptr, 0, st));
             if (w.wdown.int8) {

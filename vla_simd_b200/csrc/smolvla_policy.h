@@ -17,6 +17,7 @@
 
 #include "bpe_tokenizer.h"
 #include "conv_exec.h"
+#include "nn.h"
 
 #include <cstdint>
 #include <map>
@@ -169,6 +170,9 @@ class SmolvlaPolicy {
     int8_t* d_q_ = nullptr;
     float* d_qs_ = nullptr;
     size_t q_cap_ = 0, q_rows_ = 0;
+    static constexpr int kAttCounters = 1 << 17;   // attention query-tile arrival counters (fused quantization)
+    unsigned int* d_att_cnt_ = nullptr;
+    AttQuant att_quant(int rows, int K, int seq_rows) const;
 
     std::vector<void*> allocs_;
     float* h_pinned_ = nullptr;
