@@ -357,16 +357,44 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
         };
         const bool has_res = (p.mode & (kEpiAdd | kEpiAddRelu)) != 0;
+        // The tile-invariant part of each phase-B row's output position, once
+        // per CTA: the per-tile work below is then two divisions (conv) and a
+        // multiply-add per row instead of out_row's divisions per row, which
+        // measured ~6 K cycles per tile on the stem conv, longer than the
+        // tile's loads and MMAs.
+        int ly[8], lx[8];
+        #pragma unroll
+        for (int r8 = 0; r8 < 8; ++r8) {
+            const int r = quarter * 32 + rq + 4 * r8;
+            ly[r8] = p.conv_bw ? r / p.conv_bw : 0;
+            lx[r8] = p.conv_bw ? r - ly[r8] * p.conv_bw : r;
+        }
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int buf = i & 1;
             const int mt = t / n_tn, n0 = (t % n_tn) * BN;
             int mrow[8];                                                // phase B rows of this lane
             float asr[8];                                               // and their activation scales
-            #pragma unroll
-            for (int r8 = 0; r8 < 8; ++r8) {
-                mrow[r8] = out_row(p, mt, quarter * 32 + rq + 4 * r8);
-                asr[r8] = (mrow[r8] >= 0 && !acc_mode) ? row_ascale(p, mrow[r8]) : 0.0f;
+            if (p.conv_bw) {
+                // out_row: patch (f, ty, tx) of tile mt, pixel (ly, lx) of the patch
+                const int per_f = p.conv_ty * p.conv_tx;
+                const int f = mt / per_f, rem = mt - f * per_f;
+                const int ty = rem / p.conv_tx, tx = rem - ty * p.conv_tx;
+                const float fs = acc_mode ? 0.0f : p.ascale[f];        // row_ascale: one scale per frame
+                #pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8) {
+                    const int oy = ty * p.conv_bh + ly[r8], ox = tx * p.conv_bw + lx[r8];
+                    const bool ok = ly[r8] < p.conv_bh && oy < p.conv_ho && ox < p.conv_wo;
+                    mrow[r8] = ok ? (f * p.conv_ho + oy) * p.conv_wo + ox : -1;
+                    asr[r8] = ok ? fs : 0.0f;
+                }
+            } else {
+                #pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8) {
+                    const int m = mt * kBM + lx[r8];
+                    mrow[r8] = m < p.M ? m : -1;
+                    asr[r8] = (mrow[r8] >= 0 && !acc_mode) ? p.ascale[(long long)m * p.as_stride] : 0.0f;
+                }
             }
             // Everything the epilogue reads besides the accumulators is fetched
             // before waiting for them, so its latency hides behind the MMAs.
