@@ -714,10 +714,26 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         };
         const int r_first = GLOBAL ? 0 : rank, r_step = GLOBAL ? 1 : splits;
         const bool reduce_here = !GLOBAL || *s_last;
+        // Every load a row needs (its partial sums from the cluster's CTAs, its
+        // residual, its activation scale) is issued before any is used: with a
+        // load-then-add loop per source the row waited on one remote
+        // shared-memory latency per split, ~2/3 of this kernel's time.
         for (int j = rsub; reduce_here && r_first + r_step * j < kBM; j += kRPP) {
             const int r = r_first + r_step * j;
             const int m = out_row(p, mt, r);
             if (m < 0 || n >= p.N) continue;
+            float rv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (has_res && !acc_mode) {
+                const float* rr = p.res + (long long)m * p.ldr + n;
+                if (vec) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(rr);
+                    rv[0] = t4.x; rv[1] = t4.y; rv[2] = t4.z; rv[3] = t4.w;
+                } else {
+                    #pragma unroll
+                    for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
+                }
+            }
+            const float as = acc_mode ? 0.0f : row_ascale(p, m);
             int4 sum = make_int4(0, 0, 0, 0);
             if (GLOBAL) {
                 // eight slices' loads in flight at a time (integer sums: any order)
@@ -733,11 +749,14 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     for (int u = 0; u < 8; ++u) { sum.x += v[u].x; sum.y += v[u].y; sum.z += v[u].z; sum.w += v[u].w; }
                 }
             } else {
+                // the cluster's (at most 8) partial rows, all loads in flight (integer sums: any order)
                 const uint32_t off = part_s + static_cast<uint32_t>((r * kPS + 4 * q) * 4);
-                for (int src = 0; src < splits; ++src) {
-                    const int4 v = dsmem_ld_v4(dsmem_map(off, static_cast<uint32_t>(src)));
-                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-                }
+                int4 v[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    v[u] = u < splits ? dsmem_ld_v4(dsmem_map(off, static_cast<uint32_t>(u))) : make_int4(0, 0, 0, 0);
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) { sum.x += v[u].x; sum.y += v[u].y; sum.z += v[u].z; sum.w += v[u].w; }
             }
             const int32_t a4[4] = {sum.x, sum.y, sum.z, sum.w};
             if (acc_mode) {
@@ -747,18 +766,6 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     if (n + e < p.N) o[e] = a4[e];
                 continue;
             }
-            float rv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (has_res) {
-                const float* rr = p.res + (long long)m * p.ldr + n;
-                if (vec) {
-                    const float4 t4 = *reinterpret_cast<const float4*>(rr);
-                    rv[0] = t4.x; rv[1] = t4.y; rv[2] = t4.z; rv[3] = t4.w;
-                } else {
-                    #pragma unroll
-                    for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
-                }
-            }
-            const float as = row_ascale(p, m);
             float v[4];
             float lmax = 0.0f;
             #pragma unroll
