@@ -256,6 +256,23 @@ VLA_API int32_t vla_cuda_gemm_i8_splitk(void* out, int64_t ldo, const int8_t* xq
                                         int32_t* ws, int64_t ws_elems, uint32_t* counters,
                                         int32_t n_counters, void* stream);
 
+/* The W8A8 GEMM (+ ReLU when relu != 0) writing its output already quantized
+ * per row for the next W8A8 GEMM: q [M][ldq] int8 (ldq == N) and qscale [M],
+ * exactly what vla_cuda_gemm_i8 followed by vla_cuda_quantize_act_i8 of its
+ * fp32 output produce (the reference's dense_linear_i8 then quantize_act_i8,
+ * src/hal/common/gemm_i8.cpp:209-278), without the fp32 output. Caller-owned
+ * qamax [M] and qsync [2 * ceil(M / 128)] uint32, zero before the first call;
+ * every call leaves them zero; calls that may overlap on the GPU need separate
+ * ones. Shapes that are not one wave of slab CTAs (N % 32 != 0, K > 1024, too
+ * many rows) return VLA_ERR_SHAPE (vla_cuda_gemm_i8_rowq_supported says
+ * which). No counterpart in the reference. */
+VLA_API int32_t vla_cuda_gemm_i8_rowq_supported(int32_t M, int32_t N, int32_t K);
+VLA_API int32_t vla_cuda_gemm_i8_rowq(int8_t* q, int64_t ldq, float* qscale, const int8_t* xq, int64_t ldx,
+                                      const float* ascale, const int8_t* Wq, int64_t ldw,
+                                      const float* wscale, const float* bias, int32_t M, int32_t N,
+                                      int32_t K, int32_t relu, uint32_t* qamax, uint32_t* qsync,
+                                      void* stream);
+
 /* ------------------------------------------- batched Diffusion Policy
  * No counterpart in the reference, whose vla_diffusion_predict serves one query
  * (src/models/diffusion/diffusion_capi.cpp:57-72): a handle loaded with

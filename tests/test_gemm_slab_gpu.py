@@ -131,3 +131,32 @@ def test_default_plan_takes_the_slab_and_matches_forced_persistent(dev, monkeypa
     c = ops.gemm_i8(dq, ds, wq, ws, K, bias=_t(b, dev), mode=EPI_RELU)
     torch.cuda.synchronize()
     assert _bits_equal(a.cpu().numpy(), c.cpu().numpy())
+
+
+@pytest.mark.parametrize("M,N,K", [(602, 3200, 512), (100, 3200, 512), (1, 64, 129), (130, 96, 1024),
+                                   (333, 256, 1000)])
+@pytest.mark.parametrize("relu", [False, True])
+def test_rowq_output_equals_gemm_then_row_quantizer(dev, M, N, K, relu):
+    """The GEMM writing its output already quantized per row (the FFN
+    up-projection's int8 hidden for the down-projection) gives exactly the
+    int8 rows and scales that the fp32 GEMM followed by the row quantizer give;
+    twice in a row (its counters and absmax slots are left zero for the next
+    call)."""
+    import torch
+    from vla_simd_b200 import ops, EPI_RELU
+    if not ops.gemm_i8_rowq_supported(M, N, K):
+        pytest.skip("not one wave of slab CTAs on this device")
+    x, W, b, _ = _inputs(M, N, K, seed=3 * M + N + K)
+    wq, ws = ops.pack_weights_i8(_t(W, dev))
+    dq, ds = ops.quantize_act_i8(_t(x, dev))
+    y = ops.gemm_i8(dq, ds, wq, ws, K, bias=_t(b, dev), mode=EPI_RELU if relu else 0)
+    q_ref, s_ref = ops.quantize_act_i8(y, ld=N)
+    qamax = torch.zeros(M, dtype=torch.int32, device=dev)
+    qsync = torch.zeros(2 * ((M + 127) // 128), dtype=torch.int32, device=dev)
+    for _ in range(2):
+        q, s = ops.gemm_i8_rowq(dq, ds, wq, ws, K, qamax, qsync, bias=_t(b, dev), relu=relu)
+        torch.cuda.synchronize()
+        assert np.array_equal(q.cpu().numpy(), q_ref.cpu().numpy())
+        assert _bits_equal(s.cpu().numpy(), s_ref.cpu().numpy())
+        assert int(qamax.abs().sum()) == 0 and int(qsync.abs().sum()) == 0
+    assert ops.device_status() == 0

@@ -71,6 +71,8 @@ SIGNATURES = {
     "vla_cuda_dense_linear_i8_noalloc": (I32, [VP, VP, VP, VP, VP, I32, I32, I32, I64, VP]),
     "vla_cuda_gemm_i8": (I32, [VP, I64, VP, I64, VP, I32, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I32,
                                I32, VP]),
+    "vla_cuda_gemm_i8_rowq_supported": (I32, [I32, I32, I32]),
+    "vla_cuda_gemm_i8_rowq": (I32, [VP, I64, VP, VP, I64, VP, VP, I64, VP, VP, I32, I32, I32, I32, VP, VP, VP]),
     "vla_cuda_gemm_i8_splitk": (I32, [VP, I64, VP, I64, VP, VP, I64, VP, VP, VP, I64, I32, I32, I32, I32, VP, I64, VP,
                                       I32, VP]),
     "vla_cuda_conv2d_i8": (I32, [VP, VP, I32, I32, I32, I32, VP, I64, VP, VP, I32, I32, I32, I32, F32, I32, VP, VP,

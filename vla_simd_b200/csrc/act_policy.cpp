@@ -463,6 +463,12 @@ bool ActPolicy::load(const std::string& dir) {
     d_sb_ = dalloc<float>(R);
     d_satt_ = dalloc<float>(R);
     d_sff_ = dalloc<float>(R);
+    d_qamax_ = dalloc<unsigned int>(R);
+    d_qsync_ = dalloc<unsigned int>(2 * ((R + 127) / 128));
+    if (d_qamax_ && d_qsync_ &&
+        (cudaMemset(d_qamax_, 0, sizeof(unsigned int) * R) != cudaSuccess ||
+         cudaMemset(d_qsync_, 0, sizeof(unsigned int) * 2 * ((R + 127) / 128)) != cudaSuccess))
+        fail("cudaMemset failed");
     d_att_cnt_ = dalloc<unsigned int>(kAttCounters);
     if (d_att_cnt_ && cudaMemset(d_att_cnt_, 0, sizeof(unsigned int) * kAttCounters) != cudaSuccess)
         fail("cudaMemset failed");
@@ -559,6 +565,39 @@ cudaError_t ActPolicy::join(cudaStream_t st) {
     return cudaStreamWaitEvent(st, ev_join_, 0);
 }
 
+// FFN up-projection + ReLU straight to the down-projection's int8 input
+// (d_qff_ / d_sff_: the row quantization quantize_rows would make of the fp32
+// hidden, which is then never written), where the GEMM can do it (w1 and w2
+// both int8, one wave of slab CTAs); else the fp32 hidden and quantize_rows.
+cudaError_t ActPolicy::ffn_up(const DevLinear& w1, const DevLinear& w2, const int8_t* xq, const float* xs,
+                              const float* x_f32, int M, cudaStream_t st) {
+    if (w1.int8 && w2.int8 && d_qamax_ && gemm_i8_rowq_supported(M, w1.N, w1.K) && ldqff_ == w1.N) {
+        GemmI8Args a;
+        a.A = xq;
+        a.lda = round16(w1.K);
+        a.B = w1.Wq;
+        a.ldb = w1.ldw;
+        a.M = M;
+        a.N = w1.N;
+        a.K = w1.K;
+        a.ascale = xs;
+        a.wscale = w1.wscale;
+        a.bias = w1.bias;
+        a.mode = kEpiRelu;
+        a.static_weights = true;
+        a.qout = d_qff_;
+        a.ldq = ldqff_;
+        a.qscale = d_sff_;
+        a.qamax = d_qamax_;
+        a.qsync = d_qsync_;
+        return gemm_i8(a, st);
+    }
+    VSB_TRY(run_linear(w1, x_f32, xq, xs, nullptr, M, d_ff_, cfg_.ff, kEpiRelu, nullptr, 0, st));
+    if (w2.int8)
+        VSB_TRY(quantize_rows(d_ff_, cfg_.ff, nullptr, 0, M, cfg_.ff, d_qff_, ldqff_, d_sff_, nullptr, 0, nullptr, st));
+    return cudaSuccess;
+}
+
 // The attention output's int8 row copy (d_qatt_ / d_satt_), written by the
 // attention launch (nn.h AttQuant).
 AttQuant ActPolicy::att_quant() const {
@@ -634,10 +673,7 @@ cudaError_t ActPolicy::run_encoder(cudaStream_t st) {
                           cfg_.head_dim, scale, nullptr, st, l.wo.int8 ? &aq : nullptr));
         VSB_TRY(run_linear(l.wo, d_att_, d_qatt_, d_satt_, nullptr, T, d_x_, d, kEpiAdd, d_x_, d, st));
         VSB_TRY(layernorm(d_x_, d_x_, l.n1s, l.n1b, T, d, cfg_.ln_eps, nullptr, d_qa_, d_sa_, nullptr, nullptr, ldq_, st));
-        VSB_TRY(run_linear(l.w1, d_x_, d_qa_, d_sa_, nullptr, T, d_ff_, cfg_.ff, kEpiRelu, nullptr, 0, st));
-        if (l.w2.int8) {
-            VSB_TRY(quantize_rows(d_ff_, cfg_.ff, nullptr, 0, T, cfg_.ff, d_qff_, ldqff_, d_sff_, nullptr, 0, nullptr, st));
-        }
+        VSB_TRY(ffn_up(l.w1, l.w2, d_qa_, d_sa_, d_x_, T, st));
         VSB_TRY(run_linear(l.w2, d_ff_, d_qff_, d_sff_, nullptr, T, d_x_, d, kEpiAdd, d_x_, d, st));
         // LN2, then q(x + pos) and q(x) for the next layer (or for the decoder's
         // cross-attention keys / values after the last layer)
@@ -681,8 +717,7 @@ cudaError_t ActPolicy::run_decoder(cudaStream_t st, bool unnormalize) {
         VSB_TRY(run_linear(l.c_wo, d_att_, d_qatt_, d_satt_, nullptr, C, d_dx_, d, kEpiAdd, d_dx_, d, st));
         VSB_TRY(layernorm(d_dx_, d_dx_, l.n2s, l.n2b, C, d, cfg_.ln_eps, nullptr, d_qatt_, d_satt_, nullptr, nullptr,
                           ldq_, st));
-        VSB_TRY(run_linear(l.w1, d_dx_, d_qatt_, d_satt_, nullptr, C, d_ff_, cfg_.ff, kEpiRelu, nullptr, 0, st));
-        VSB_TRY(quantize_rows(d_ff_, cfg_.ff, nullptr, 0, C, cfg_.ff, d_qff_, ldqff_, d_sff_, nullptr, 0, nullptr, st));
+        VSB_TRY(ffn_up(l.w1, l.w2, d_qatt_, d_satt_, d_dx_, C, st));
         VSB_TRY(run_linear(l.w2, d_ff_, d_qff_, d_sff_, nullptr, C, d_dx_, d, kEpiAdd, d_dx_, d, st));
         VSB_TRY(layernorm(d_dx_, d_dx_, l.n3s, l.n3b, C, d, cfg_.ln_eps, nullptr, nullptr, nullptr, nullptr, nullptr,
                           0, st));

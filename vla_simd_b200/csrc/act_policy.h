@@ -147,6 +147,11 @@ class ActPolicy {
     static constexpr int kAttCounters = 4096;   // attention query-tile arrival counters (fused quantization)
     unsigned int* d_att_cnt_ = nullptr;
     AttQuant att_quant() const;
+    // row-quantized FFN hidden (GemmI8Args::qout): per-row absmax slots, tile counters
+    unsigned int* d_qamax_ = nullptr;
+    unsigned int* d_qsync_ = nullptr;
+    cudaError_t ffn_up(const DevLinear& w1, const DevLinear& w2, const int8_t* xq, const float* xs,
+                       const float* x_f32, int M, cudaStream_t st);
     int n_amax_ = 0;
     float *d_x_ = nullptr, *d_qk_ = nullptr, *d_v_ = nullptr, *d_att_ = nullptr, *d_ff_ = nullptr;
     float *d_dx_ = nullptr, *d_ck_ = nullptr, *d_cv_ = nullptr, *d_feat_ = nullptr;

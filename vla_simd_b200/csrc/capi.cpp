@@ -495,6 +495,38 @@ int32_t vla_cuda_gemm_i8(void* out, int64_t ldo, const int8_t* xq, int64_t ldx, 
     return status_of(vsb::gemm_i8(a, as_stream(stream)));
 }
 
+int32_t vla_cuda_gemm_i8_rowq_supported(int32_t M, int32_t N, int32_t K) {
+    return (M > 0 && N > 0 && k_ok(K) && vsb::gemm_i8_rowq_supported(M, N, K)) ? 1 : 0;
+}
+
+int32_t vla_cuda_gemm_i8_rowq(int8_t* q, int64_t ldq, float* qscale, const int8_t* xq, int64_t ldx,
+                              const float* ascale, const int8_t* Wq, int64_t ldw, const float* wscale,
+                              const float* bias, int32_t M, int32_t N, int32_t K, int32_t relu, uint32_t* qamax,
+                              uint32_t* qsync, void* stream) {
+    if (!q || !qscale || !xq || !ascale || !Wq || !wscale || !qamax || !qsync || M <= 0 || N <= 0 || !k_ok(K) ||
+        ldx < K || ldw < K || ldq != N)
+        return VLA_ERR_ARG;
+    if (!vsb::gemm_i8_rowq_supported(M, N, K)) return VLA_ERR_SHAPE;
+    vsb::GemmI8Args a;
+    a.A = xq;
+    a.lda = ldx;
+    a.B = Wq;
+    a.ldb = ldw;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.ascale = ascale;
+    a.wscale = wscale;
+    a.bias = bias;
+    a.mode = relu ? VLA_EPI_RELU : 0;
+    a.qout = q;
+    a.ldq = ldq;
+    a.qscale = qscale;
+    a.qamax = qamax;
+    a.qsync = qsync;
+    return status_of(vsb::gemm_i8(a, as_stream(stream)));
+}
+
 int32_t vla_cuda_gemm_i8_splitk(void* out, int64_t ldo, const int8_t* xq, int64_t ldx, const float* ascale,
                                 const int8_t* Wq, int64_t ldw, const float* wscale, const float* bias,
                                 const float* res, int64_t ldr, int32_t M, int32_t N, int32_t K, int32_t mode,

@@ -83,6 +83,12 @@ struct EpiParams {
     unsigned int* counters;
     // slab kernel (w8a8_slab_kernel): columns per CTA, CTAs per M tile, staging tiles per epilogue warp
     int slab_bn, slab_groups, slab_nstg;
+    // slab kernel, row-quantized output (GemmI8Args::qout)
+    int8_t* qout;
+    long long ldq;
+    float* qscale;
+    unsigned int* qamax;
+    unsigned int* qsync;
 };
 
 // Output row (index into out / res, and the absmax slot numerator) of tile
@@ -1110,7 +1116,7 @@ struct SlabPlan {
 size_t slab_smem_bytes(int K, int bn, int sl, int stages, int nstg, int kbb = kBK) {
     const int nkb = (K + kbb - 1) / kbb;
     return 1024 + (size_t)nkb * kBM * kbb + (size_t)stages * nkb * sl * kbb + (size_t)8 * nstg * kSlabStgFloats * 4 +
-           (size_t)2 * 4 * bn + 8 * (kSlabMaxKb + 2 * stages + kSlabMaxSlices + 1) + 16;
+           (size_t)2 * 4 * bn + 8 * (kSlabMaxKb + 2 * stages + kSlabMaxSlices + 1) + 16;   // TMEM slot, 3 flags
 }
 
 // Ring depth and staging tiles for a slab shape: as many B slices in flight
@@ -1183,8 +1189,31 @@ cudaError_t launch_slab_sl(const CUtensorMap& ta, const CUtensorMap& tb, const C
     cudaError_t e = slab_ready<SL, KBB>();
     if (e != cudaSuccess) return e;
     const long long grid = (long long)p.m_tiles * p.slab_groups;
-    e = launch_k(w8a8_slab_kernel<SL, KBB>, dim3(static_cast<unsigned>(grid)), kThreads,
-                 slab_smem_bytes(p.K, sp.bn, SL, sp.stages, sp.nstg, KBB), st, ta, tb, to, p, sp.stages);
+    const size_t smem = slab_smem_bytes(p.K, sp.bn, SL, sp.stages, sp.nstg, KBB);
+    if (p.qout) {
+        // the CTAs of an M tile wait for one another: a cooperative launch.
+        // Whether the driver takes it together with programmatic dependent
+        // launch is found on the first (uncaptured) launch and remembered.
+        static std::atomic<int> with_pdl{-1};
+        int wp = with_pdl.load(std::memory_order_relaxed);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (wp < 0 && cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone) {
+            e = launch_k_coop(w8a8_slab_kernel<SL, KBB>, dim3(static_cast<unsigned>(grid)), kThreads, smem, st, true,
+                              ta, tb, to, p, sp.stages);
+            if (e == cudaSuccess) {
+                with_pdl.store(1, std::memory_order_relaxed);
+                return cudaGetLastError();
+            }
+            cudaGetLastError();
+            with_pdl.store(0, std::memory_order_relaxed);
+            wp = 0;
+        }
+        e = launch_k_coop(w8a8_slab_kernel<SL, KBB>, dim3(static_cast<unsigned>(grid)), kThreads, smem, st, wp > 0,
+                          ta, tb, to, p, sp.stages);
+    } else {
+        e = launch_k(w8a8_slab_kernel<SL, KBB>, dim3(static_cast<unsigned>(grid)), kThreads, smem, st, ta, tb, to, p,
+                     sp.stages);
+    }
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -1207,6 +1236,11 @@ EpiParams make_epi(const GemmI8Args& a) {
     p.K = a.K;
     p.static_weights = a.static_weights ? 1 : 0;
     p.m_tiles = (a.M + kBM - 1) / kBM;
+    p.qout = a.qout;
+    p.ldq = a.ldq;
+    p.qscale = a.qscale;
+    p.qamax = a.qamax;
+    p.qsync = a.qsync;
     const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
     p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 &&
                (!a.res || ((rb & 15) == 0 && (a.ldr & 3) == 0));
@@ -1325,8 +1359,41 @@ bool gemm_i8_skinny_plan(const GemmI8Args& a, GemmPlan* plan) {
     return true;
 }
 
+bool gemm_i8_rowq_supported(int M, int N, int K) {
+    SlabPlan sp;
+    if (M <= 0 || N <= 0 || N % 32 || !slab_plan(M, N, K, &sp)) return false;
+    const long long grid = (long long)((M + kBM - 1) / kBM) * ((N + sp.bn - 1) / sp.bn);
+    return grid <= sm_count();
+}
+
+// The row-quantized output (GemmI8Args::qout) on the slab kernel.
+static cudaError_t gemm_i8_rowq(const GemmI8Args& a, cudaStream_t st) {
+    const uintptr_t qb = reinterpret_cast<uintptr_t>(a.qout);
+    if (!gemm_i8_rowq_supported(a.M, a.N, a.K) || a.ldq != a.N || (qb & 15) || (a.ldq & 15) || !a.qscale ||
+        !a.qamax || !a.qsync || a.res || a.amax || (a.mode & ~kEpiRelu) || !a.ascale_per_row || a.force_simt ||
+        ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) || (a.lda & 15) || (a.ldb & 15))
+        return cudaErrorInvalidValue;
+    SlabPlan sp;
+    slab_plan(a.M, a.N, a.K, &sp);
+    EpiParams p = make_epi(a);
+    p.out = nullptr;
+    p.slab_bn = sp.bn;
+    p.slab_groups = (a.N + sp.bn - 1) / sp.bn;
+    p.slab_nstg = sp.nstg;
+    CUtensorMap ta, tb;
+    if (!make_tmap_i8_kmajor(&ta, a.A, a.M, a.K, a.lda, kBM) || !make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, sp.sl))
+        return cudaErrorInvalidConfiguration;
+    // the fp32 output map is never used on this path: the A map stands in
+    switch (sp.sl) {
+        case 64: return launch_slab_sl<64>(ta, tb, ta, p, sp, st);
+        case 128: return launch_slab_sl<128>(ta, tb, ta, p, sp, st);
+        default: return launch_slab_sl<32>(ta, tb, ta, p, sp, st);
+    }
+}
+
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
+    if (a.qout) return gemm_i8_rowq(a, st);
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
                         (a.lda & 15) == 0 && (a.ldb & 15) == 0;
     if (!a.force_simt && tma_ok) {

@@ -43,7 +43,25 @@ struct GemmI8Args {
     long long splitk_ws_elems = 0;
     unsigned int* splitk_counters = nullptr;
     int splitk_counters_n = 0;
+    // Optional: the output as its per-row int8 quantization (quantize_rows'
+    // arithmetic over the row's N values) instead of fp32, for a GEMM whose
+    // only consumer is the next W8A8 GEMM: qout [M][ldq] (ldq == N), qscale
+    // [M]; `out` is not written. Each CTA folds the |values| of its columns into
+    // qamax [M] (float bits), the CTAs of one 128-row tile meet at a counter pair
+    // in qsync [2 * row tiles], then each quantizes its columns with the row's
+    // scale (a cooperative launch: the CTAs wait for one another). qamax and
+    // qsync must be zero before the first use; every launch leaves them zero.
+    // Calls that may run at the same time need separate qamax / qsync.
+    int8_t* qout = nullptr;
+    long long ldq = 0;
+    float* qscale = nullptr;
+    unsigned int* qamax = nullptr;
+    unsigned int* qsync = nullptr;
 };
+
+// Whether gemm_i8 can write the row-quantized output (GemmI8Args::qout) for
+// this shape on this device: one wave of slab CTAs, N % 32 == 0, K <= 1024.
+bool gemm_i8_rowq_supported(int M, int N, int K);
 
 // Launch on `st`. Tensor-core path when lda/ldb/A/B are 16-byte aligned,
 // otherwise the CUDA-core path (same results).

@@ -38,6 +38,106 @@ constexpr int kSlabMaxBn = 256;      // columns per CTA
 constexpr int kSlabMaxSlices = kSlabMaxBn / 32;
 constexpr int kSlabStgFloats = 32 * 32;   // one warp's staging tile: 32 rows x 128 bytes
 
+// Row-quantized output (EpiParams::qout; plain GEMMs, mode 0 or ReLU, N a
+// multiple of 32): pass 1 folds |v| of this thread's row over the CTA's columns
+// into qamax[m]; the CTAs of the M tile meet at qsync[2 mt] (a cooperative
+// launch: all are resident, the wait is bounded); pass 2 reloads the
+// accumulators, recomputes v bit for bit and writes
+// q = clamp(rne(v / s)), s = max(amax / 127, FLT_MIN) (quantize_rows'
+// arithmetic, src/hal/common/gemm_i8.cpp:209-244 over the row's N values).
+// The last CTA of the tile to leave (qsync[2 mt + 1]) zeroes the tile's qamax
+// slots and both counters for the next launch.
+__device__ __forceinline__ float rowq_scale(float amax) {
+    return amax > 0.0f ? fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN) : 1.0f;
+}
+__device__ __forceinline__ uint32_t rowq_q8(float v, float inv) {
+    float t = __fmul_rn(v, inv);
+    t = t != t ? 0.0f : fminf(fmaxf(t, -127.0f), 127.0f);
+    return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(f2i_rn_small(t))));
+}
+
+template <int SL>
+__device__ __forceinline__ void slab_rowq_epilogue(const EpiParams& p, uint64_t* accfull, uint32_t tmem_base,
+                                                   const float* s_ws, const float* s_bias, int q, int h, int lane,
+                                                   int m, bool row_ok, float sa, int mt, int ng, int nch,
+                                                   volatile int* s_qfail) {
+    const bool relu = (p.mode & kEpiRelu) != 0;
+    auto values = [&](int g, float (&v)[32]) -> bool {
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&accfull[(g * 32) / SL], 0))) return false;
+        tc_fence_after();
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + g * 32, acc);
+        tmem_ld_wait();
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const float t = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[e])), s_ws[g * 32 + e]), sa,
+                                      s_bias[g * 32 + e]);
+            v[e] = (relu && t < 0.0f) ? 0.0f : t;                     // tcpu::relu (eltwise.cpp:213-214)
+        }
+        return true;
+    };
+    bool ok = true;
+    float qmax = 0.0f;
+    for (int g = h; g < nch; g += 2) {
+        float v[32];
+        if (!(ok = values(g, v))) break;
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) qmax = fmaxf(qmax, fabsf(v[e]));
+    }
+    if (ok && row_ok) atomicMax(&p.qamax[m], __float_as_uint(qmax));
+    __syncwarp();
+    named_sync(1, 256);
+    if (threadIdx.x == 64) {
+        unsigned int* arrive = p.qsync + 2 * mt;
+        int fail = 0;
+        __threadfence();
+        atomicAdd(arrive, 1u);
+        const uint64_t t0 = globaltimer_ns();
+        while (*reinterpret_cast<volatile unsigned int*>(arrive) < static_cast<unsigned>(p.slab_groups)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_status(kStatusWaitTimeout);
+                fail = 1;
+                break;
+            }
+        }
+        __threadfence();
+        *s_qfail = fail;
+    }
+    __syncwarp();
+    named_sync(1, 256);
+    if (ok && !*s_qfail) {
+        const float sc = rowq_scale(row_ok ? __uint_as_float(__ldcg(p.qamax + m)) : 0.0f);
+        const float inv = __fdiv_rn(1.0f, sc);
+        const int n0 = ng * p.slab_bn;
+        for (int g = h; g < nch; g += 2) {
+            float v[32];
+            if (!values(g, v)) break;
+            if (!row_ok) continue;
+            uint32_t w[8];
+            #pragma unroll
+            for (int i = 0; i < 8; ++i)
+                w[i] = rowq_q8(v[4 * i], inv) | (rowq_q8(v[4 * i + 1], inv) << 8) |
+                       (rowq_q8(v[4 * i + 2], inv) << 16) | (rowq_q8(v[4 * i + 3], inv) << 24);
+            uint4* dst = reinterpret_cast<uint4*>(p.qout + (long long)m * p.ldq + n0 + g * 32);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        if (row_ok && ng == 0 && h == 0) p.qscale[m] = sc;
+    }
+    __syncwarp();
+    named_sync(1, 256);
+    if (threadIdx.x == 64) {
+        unsigned int* depart = p.qsync + 2 * mt + 1;
+        if (atomicAdd(depart, 1u) + 1 == static_cast<unsigned>(p.slab_groups)) {
+            // the tile's last CTA to leave: every CTA of it has read qamax
+            const int m0 = mt * kBM;
+            for (int r = 0; r < kBM && m0 + r < p.M; ++r) p.qamax[m0 + r] = 0u;
+            p.qsync[2 * mt] = 0u;
+            *depart = 0u;
+        }
+    }
+}
+
 template <int SL, int KBB>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -78,6 +178,7 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* s_bdone = reinterpret_cast<volatile int*>(tmem_slot + 1);   // B slices the MMA thread saw land
     volatile int* s_adone = s_bdone + 1;                                      // 1 once the whole A tile landed
+    volatile int* s_qfail = s_adone + 1;                                      // row-quantized output: the tile wait gave up
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -195,7 +296,8 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
         float* my_stg = stg + (warp - 2) * nstg * kSlabStgFloats;
         float rmax = 0.0f;
         int it = 0;
-        for (int g = h; quarter_live && g < nch; g += 2, ++it) {
+        if (p.qout) slab_rowq_epilogue<SL>(p, accfull, tmem_base, s_ws, s_bias, q, h, lane, m, row_ok, sa, mt, ng, nch, s_qfail);
+        for (int g = h; !p.qout && quarter_live && g < nch; g += 2, ++it) {
             const int n = n0 + g * 32;
             const int nv = p.N - n < 32 ? p.N - n : 32;     // valid columns of the chunk
             // the residual row segment goes out before the accumulator wait

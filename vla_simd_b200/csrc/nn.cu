@@ -648,7 +648,10 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
     // are never read: their probabilities are 0 and an fma with 0 leaves a chain
     // unchanged, so the CTA stops at the largest bound of its rows (a fully
     // blocked row keeps every key: it takes the uniform mean of V).
+    // Each row's bound is found once (kept for the softmax in s_rowlast), with
+    // four of a lane's mask loads in flight at a time.
     __shared__ int s_kend;
+    __shared__ int s_rowlast[QP];
     if (tid == 0) s_kend = mask ? 0 : seq_k;
     __syncthreads();
     if (mask) {
@@ -657,11 +660,15 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             if (q >= seq_q) continue;
             const float* mr = mask + (long long)q * seq_k;
             int last = -1;
+            #pragma unroll 4
             for (int j = lane; j < seq_k; j += 32)
                 if (mr[j] != -FLT_MAX) last = j;
             #pragma unroll
             for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
-            if (lane == 0) atomicMax(&s_kend, last < 0 ? seq_k : last + 1);
+            if (lane == 0) {
+                s_rowlast[r] = last;
+                atomicMax(&s_kend, last < 0 ? seq_k : last + 1);
+            }
         }
     }
     __syncthreads();
@@ -751,15 +758,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
             srow[k] = sS + r * ss;
             mrow[k] = (mask && q < seq_q) ? mask + (long long)q * seq_k : nullptr;
             // row bound: trailing `lowest` mask entries block keys (hal::row_bound)
-            int last = seq_k - 1;
-            if (mrow[k]) {
-                last = -1;
-                for (int j = lane; j < seq_k; j += 32)
-                    if (mrow[k][j] != -FLT_MAX) last = j;
-                #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xFFFFFFFFu, last, off));
-            }
-            jmax[k] = last + 1;
+            jmax[k] = mrow[k] ? s_rowlast[r] + 1 : seq_k;
             mx[k] = NINF;
         }
         // Each pass loads all of an iteration's elements before storing any:

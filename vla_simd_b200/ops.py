@@ -59,6 +59,23 @@ def gemm_i8(xq, ascale, Wq, wscale, K, bias=None, mode=0, res=None, out=None, am
     return out
 
 
+def gemm_i8_rowq_supported(M, N, K):
+    return bool(lib().vla_cuda_gemm_i8_rowq_supported(int(M), int(N), int(K)))
+
+
+def gemm_i8_rowq(xq, ascale, Wq, wscale, K, qamax, qsync, bias=None, relu=False):
+    """The W8A8 GEMM (+ ReLU) with its output quantized per row for the next
+    W8A8 GEMM (vla_cuda_gemm_i8_rowq): returns (q int8 [M, N], scale [M]).
+    qamax [M] and qsync [2 * ceil(M / 128)] int32 (zeroed) are the caller's."""
+    M, N = xq.shape[0], Wq.shape[0]
+    q = torch.empty((M, N), dtype=torch.int8, device=xq.device)
+    s = torch.empty(M, dtype=torch.float32, device=xq.device)
+    check(lib().vla_cuda_gemm_i8_rowq(_p(q), N, _p(s), _p(xq), xq.stride(0), _p(ascale), _p(Wq), Wq.stride(0),
+                                      _p(wscale), _p(bias), M, N, K, 1 if relu else 0, _p(qamax), _p(qsync),
+                                      _stream()), "vla_cuda_gemm_i8_rowq")
+    return q, s
+
+
 def gemm_i8_splitk(xq, ascale, Wq, wscale, K, ws, counters, bias=None, mode=0, res=None, out=None):
     """The W8A8 GEMM with K split over independent CTAs (vla_cuda_gemm_i8_splitk):
     M <= 128 rows; ws int32 and counters int32 (zeroed) are the caller's workspace."""
