@@ -199,7 +199,7 @@ import json, os, sys, time
 sys.path.insert(0, %(root)r)
 import numpy as np
 from vla_simd_b200 import synth
-kind, budget, max_steps = %(kind)r, %(budget)f, %(max_steps)d
+kind, budget, max_steps, warmup = %(kind)r, %(budget)f, %(max_steps)d, %(warmup)d
 f, s = synth.act_inputs(synth.ACT_BASELINE, seed=1)
 from oracle import oracle
 r = oracle.reference()
@@ -210,7 +210,7 @@ l = r.l
 h = l.vla_act_load(%(ckpt)r.encode())
 out = np.zeros((100, 6), np.float32)
 P = lambda a: a.ctypes.data_as(__import__("ctypes").c_void_p)
-for _ in range(2):
+for _ in range(warmup):
     l.vla_act_predict(h, P(f), P(s), 1, P(out))
 times = []
 t_end = time.perf_counter() + budget
@@ -224,13 +224,14 @@ print(json.dumps({"steps": len(times), "seconds": sum(times), "p50_ms": 1e3 * fl
 """
 
 
-def time_reference_cpu(ckpt: str, budget_s: float, max_steps: int, threads: int | None = None):
-    """The reference's own ACT step (oracle/_ref) in a fresh process with all host cores (or `threads`)."""
+def time_reference_cpu(ckpt: str, budget_s: float, max_steps: int, threads: int | None = None, warmup: int = 3):
+    """The reference's own ACT step (oracle/_ref) in a fresh process with all host cores (or `threads`),
+    after `warmup` untimed steps."""
     cores = threads or cpu_cores()
     env = dict(os.environ, ACT_INT8=str(INT8_MASK), OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close",
                CUDA_VISIBLE_DEVICES="")
     code = _CPU_CHILD % {"root": ROOT, "kind": "reference", "budget": budget_s, "max_steps": max_steps,
-                         "ckpt": ckpt}
+                         "ckpt": ckpt, "warmup": warmup}
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=900)
     if r.returncode != 0:
         return {"unavailable": f"reference CPU run failed: {r.stderr.strip().splitlines()[-1:]}"}
@@ -504,7 +505,7 @@ def run_ours(args):
         cpu_baseline = {"unavailable": cpu["unavailable"]}
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "chunks/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
         "data": "synthetic (seeded random-init ACT weights, uniform uint8 frames, N(0,1) state)",
         "config": {"workload": "ACT policy step, BASELINE configs[1]: 2x480x640 uint8 frames -> ResNet-18 -> "
@@ -650,7 +651,7 @@ def run_dp(args):
         cpu_baseline = {"unavailable": cpu["unavailable"]}
     print(json.dumps({
         "metric": "Diffusion Policy throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
         "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
         "data": "synthetic (seeded random-init DP weights, uniform uint8 frames, N(0,1) state and noise)",
@@ -820,7 +821,7 @@ def run_octo(args):
         cpu_baseline = {"unavailable": cpu["unavailable"]}
     print(json.dumps({
         "metric": "Octo throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
         "ms_per_step": round(1e3 * total_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
         "data": "synthetic (seeded random-init Octo weights, uniform uint8 frames, N(0,1) noise, a synthetic "
@@ -933,7 +934,7 @@ def run_smolvla(args):
         cpu_baseline = {"unavailable": cpu["unavailable"]}
     print(json.dumps({
         "metric": "SmolVLA throughput (chunks/s)", "value": round(value, 3), "unit": "chunks/s", "n_gpus": world,
-        "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 * total / n, 4), "higher_is_better": True,
+        "steps": n, "warmup": max(args.warmup, 3), "ms_per_step": round(1e3 * total / n, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8 GEMMs, int32 acc) + fp32",
         "data": "synthetic (seeded random-init SmolVLA-shaped weights, uniform uint8 frames, N(0,1) state and noise, "
                 "a synthetic BPE vocabulary)",
@@ -978,14 +979,15 @@ def run_reference(args):
     ckpt_root = tempfile.mkdtemp(prefix="vla_act_ref_")
     ckpt = synth.write_act_checkpoint(os.path.join(ckpt_root, "act"), synth.ACT_BASELINE, seed=0)
     steps = args.steps
-    cpu = time_reference_cpu(ckpt, budget_s=max(10.0, args.cpu_budget), max_steps=steps)
+    warmup = max(args.warmup, 3)
+    cpu = time_reference_cpu(ckpt, budget_s=max(10.0, args.cpu_budget), max_steps=steps, warmup=warmup)
     if "unavailable" in cpu:
         print(json.dumps({"impl": "reference", "unavailable": cpu["unavailable"]}), flush=True)
         return
     v = cpu["chunks_per_s"]
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "chunks/s", "n_gpus": world,
-        "steps": cpu["steps"], "warmup": 2, "ms_per_step": round(1e3 * cpu["seconds"] / cpu["steps"], 3),
+        "steps": cpu["steps"], "warmup": warmup, "ms_per_step": round(1e3 * cpu["seconds"] / cpu["steps"], 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8) + fp32 (CPU)",
         "data": "synthetic (seeded random-init ACT weights)",
         "config": {"workload": "ACT policy step, BASELINE configs[1] (same checkpoint and inputs as ours)",
