@@ -1034,6 +1034,25 @@ def run_timeline(args):
                             max_batch=args.batch)
         f, ins, st_, nz = synth.smolvla_inputs(sh, seed=1, batch=args.batch)
         step = lambda: pol.predict_batch(f, ins, st_, nz)  # noqa: E731
+    elif args.model == "dp":
+        os.environ["DIFFUSION_INT8"] = str(DP_MASK)
+        from vla_simd_b200 import DiffusionPolicy, synth
+        pol = DiffusionPolicy(synth.write_dp_checkpoint(os.path.join(tempfile.mkdtemp(), "d"), synth.DP_BASELINE,
+                                                        seed=0), max_batch=args.batch)
+        frames, state, noise = synth.dp_inputs(synth.DP_BASELINE, seed=1, batch=args.batch)
+        pol.predict_batch(frames, state, noise)
+        stream = torch.cuda.Stream()
+        step = lambda: pol.enqueue(args.batch, stream.cuda_stream)  # noqa: E731
+    elif args.model == "octo":
+        os.environ["OCTO_INT8"] = str(OCTO_MASK)
+        from vla_simd_b200 import OctoPolicy, synth
+        sh = synth.OCTO_BASELINE
+        pol = OctoPolicy(synth.write_octo_checkpoint(os.path.join(tempfile.mkdtemp(), "o"), sh, seed=0),
+                         max_batch=args.batch)
+        p_, w_, tm, ins, noise, z = synth.octo_inputs(sh, seed=1, batch=args.batch)
+        pol.predict_batch(p_, w_, tm, [synth.octo_instruction(1)] * args.batch, noise, z)
+        stream = torch.cuda.Stream()
+        step = lambda: pol.enqueue(args.batch, sh.window, True, stream.cuda_stream)  # noqa: E731
     else:
         os.environ["ACT_INT8"] = str(INT8_MASK)
         from vla_simd_b200 import ActPolicy, synth
@@ -1079,7 +1098,7 @@ def main():
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the W8A8 GEMM at the ACT FFN shape (a small case for ncu captures)")
     ap.add_argument("--timeline", action="store_true",
-                    help="profile a few steps (--model act or smolvla) and print each kernel's marginal time")
+                    help="profile a few steps (any --model, --batch) and print each kernel's marginal time")
     args = ap.parse_args()
     if args.timeline:
         run_timeline(args)

@@ -530,7 +530,21 @@ conv_transpose1d_chain_kernel(const float* __restrict__ x, const float* __restri
             if (kt_i[i] < 0) continue;
             const float* xr = sx + (size_t)t_i[i] * kChXs;
             const float* wr = sW + (size_t)kt_i[i] * kChCo + tx;
-            for (int ci = 0; ci < cmax; ++ci) {
+            // eight steps' operands are loaded before their fmas, so the chain
+            // runs at the fma latency rather than the shared-memory latency
+            int ci = 0;
+            for (; ci + 8 <= cmax; ci += 8) {
+                float xv[8], wv[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    xv[u] = xr[ci + u];
+                    wv[u] = wr[(size_t)(ci + u) * k * kChCo];
+                }
+                #pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (xv[u] != 0.0f) acc[i] = __fmaf_rn(xv[u], wv[u], acc[i]);
+            }
+            for (; ci < cmax; ++ci) {
                 const float v = xr[ci];
                 if (v == 0.0f) continue;
                 acc[i] = __fmaf_rn(v, wr[(size_t)ci * k * kChCo], acc[i]);

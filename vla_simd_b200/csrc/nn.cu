@@ -1019,14 +1019,20 @@ static cudaError_t attention_select(const float* Q, long long ldq, const float* 
             const int v = e ? std::atoi(e) : 0;
             return v == 1 || v == 2 || v == 4 || v == 5 ? v : 0;
         }();
+        const bool fits40 = att_tiled_smem(40, seq_k) <= 227 * 1024;
         for (int qpt : {5, 4, 2, 1}) {
             if (att_tiled_smem(8 * qpt, seq_k) > 227 * 1024) continue;
             if (forced && qpt != forced) continue;
+            // 32-row tiles only where 40 rows of scores do not fit (SigLIP's
+            // 1024 keys: 367 vs 465 us on 16-row tiles); where both fit, the
+            // 40-row tile measured faster (Octo's 690 keys: 3.01 vs 3.11 ms
+            // per query), each CTA streaming all keys whatever its rows
+            if (qpt == 4 && fits40 && !forced) continue;
             const long long ctas = (long long)((seq_q + 8 * qpt - 1) / (8 * qpt)) * n_q * bs.n;
             // rows on the busiest SM, weighted by the cost of a row at each
             // tile height (taller tiles reuse every loaded K / V value more:
             // 1.0 / 1.3 / 1.4 per row measured for 40 / 16 / 8 rows on Octo
-            // shapes; 32 rows placed by the shared-memory load count per fma)
+            // shapes; 32 rows between, by the shared-memory load count per fma)
             const int w = qpt == 5 ? 10 : qpt == 4 ? 11 : qpt == 2 ? 13 : 14;
             const long long rows = (ctas + 147) / 148 * 8 * qpt * w;
             if (!best_qpt || rows < best_rows) { best_qpt = qpt; best_rows = rows; }
