@@ -178,11 +178,14 @@ SPLITK_SHAPES = [(16, 2048, 10240), (16, 512, 2560), (8, 1024, 5120), (4, 1024, 
                  (1, 64, 1000), (77, 4096, 4096), (16, 16, 130)]
 
 
+@pytest.mark.parametrize("reducer", ["every_cta", "last_cta"])
 @pytest.mark.parametrize("M,N,K", SPLITK_SHAPES)
-def test_splitk_workspace_gemm_matches_oracle(dev, restated, M, N, K):
+def test_splitk_workspace_gemm_matches_oracle(dev, restated, M, N, K, reducer):
     """K split over independent CTAs (workspace reduction): the same int32 sums
     and fp32 outputs as the oracle and the ordinary kernels, every epilogue; the
-    counters are left zero, so a second call gives the same bits."""
+    counters are left zero, so a second call gives the same bits. With two
+    counters per output tile the CTAs (all resident, a cooperative launch) each
+    reduce rows after all have written; with one, the last to arrive reduces."""
     import torch
     from vla_simd_b200 import EPI_ACC, EPI_ADD, EPI_RELU, ops
     rng = np.random.default_rng(M * 31 + N * 7 + K)
@@ -193,7 +196,8 @@ def test_splitk_workspace_gemm_matches_oracle(dev, restated, M, N, K):
     wq, ws = ops.pack_weights_i8(_t(W, dev))
     xq, xs = ops.quantize_act_i8(_t(x, dev))
     work = torch.empty(148 * 128 * 128, dtype=torch.int32, device=dev)
-    counters = torch.zeros(4096, dtype=torch.int32, device=dev)
+    n_tiles = -(-N // (128 if N >= 1024 else 64 if N >= 256 else 32))
+    counters = torch.zeros(4096 if reducer == "every_cta" else n_tiles, dtype=torch.int32, device=dev)
     acc = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, mode=EPI_ACC)
     out = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev))
     relu = ops.gemm_i8_splitk(xq, xs, wq, ws, K, work, counters, bias=_t(b, dev), mode=EPI_RELU)

@@ -81,6 +81,7 @@ struct EpiParams {
     // int32 tiles [tile][split][M][BN] in ws, arrivals counted per tile
     int32_t* ws;
     unsigned int* counters;
+    int splitk_coop;              // GLOBAL split-K, co-resident: counters [2 * tiles], every CTA reduces rows
     // slab kernel (w8a8_slab_kernel): columns per CTA, CTAs per M tile, staging tiles per epilogue warp
     int slab_bn, slab_groups, slab_nstg;
     // slab kernel, row-quantized output (GemmI8Args::qout)
@@ -685,9 +686,28 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
-            const bool last = atomicAdd(&p.counters[blockIdx.y], 1u) == static_cast<unsigned>(splits - 1);
-            if (last) __threadfence();
-            *s_last = last ? 1 : 0;
+            if (p.splitk_coop) {
+                // every CTA of the grid is resident (cooperative launch): each
+                // waits (bounded) until the tile's slices are all written, then
+                // reduces its own interleaved rows, as the cluster form does
+                unsigned int* arrive = p.counters + 2 * blockIdx.y;
+                atomicAdd(arrive, 1u);
+                int ok = 1;
+                const uint64_t t0 = globaltimer_ns();
+                while (*reinterpret_cast<volatile unsigned int*>(arrive) < static_cast<unsigned>(splits)) {
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                        record_status(kStatusWaitTimeout);
+                        ok = 0;
+                        break;
+                    }
+                }
+                __threadfence();
+                *s_last = ok;
+            } else {
+                const bool last = atomicAdd(&p.counters[blockIdx.y], 1u) == static_cast<unsigned>(splits - 1);
+                if (last) __threadfence();
+                *s_last = last ? 1 : 0;
+            }
         }
         __syncthreads();
     }
@@ -718,8 +738,36 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (cur_key - key0 < 4u) atomicMax(&s_amax[cur_key - key0], __float_as_uint(cur_max));
             else atomicMax(&p.amax[cur_key], __float_as_uint(cur_max));
         };
-        const int r_first = GLOBAL ? 0 : rank, r_step = GLOBAL ? 1 : splits;
+        const bool one_reducer = GLOBAL && !p.splitk_coop;     // the last CTA to arrive sums every row
+        const int r_first = one_reducer ? 0 : rank, r_step = one_reducer ? 1 : splits;
         const bool reduce_here = !GLOBAL || *s_last;
+        // Over independent CTAs with at most two rows per thread (the batch-1
+        // policies' skinny GEMMs): both rows' slices are summed up front, 16
+        // loads in flight per thread, instead of eight per row in turn.
+        int4 gsum0 = make_int4(0, 0, 0, 0), gsum1 = make_int4(0, 0, 0, 0);
+        const bool gpre = one_reducer && reduce_here && p.M <= 2 * kRPP;
+        if (gpre) {
+            const long long sl = (long long)p.M * BN;
+            const int32_t* base = p.ws + (long long)blockIdx.y * splits * p.M * BN + 4 * q;
+            const bool ok0 = rsub < p.M && n < p.N, ok1 = rsub + kRPP < p.M && n < p.N;
+            for (int s0 = 0; s0 < splits; s0 += 8) {
+                int4 a[8], b[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const bool in = s0 + u < splits;
+                    a[u] = (in && ok0) ? __ldcg(reinterpret_cast<const int4*>(base + (long long)rsub * BN + (s0 + u) * sl))
+                                       : make_int4(0, 0, 0, 0);
+                    b[u] = (in && ok1) ? __ldcg(reinterpret_cast<const int4*>(base + (long long)(rsub + kRPP) * BN +
+                                                                               (s0 + u) * sl))
+                                       : make_int4(0, 0, 0, 0);
+                }
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    gsum0.x += a[u].x; gsum0.y += a[u].y; gsum0.z += a[u].z; gsum0.w += a[u].w;
+                    gsum1.x += b[u].x; gsum1.y += b[u].y; gsum1.z += b[u].z; gsum1.w += b[u].w;
+                }
+            }
+        }
         // Every load a row needs (its partial sums from the cluster's CTAs, its
         // residual, its activation scale) is issued before any is used, rather
         // than one remote load-then-add per split (the backbone convs' split-K
@@ -741,7 +789,9 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
             const float as = acc_mode ? 0.0f : row_ascale(p, m);
             int4 sum = make_int4(0, 0, 0, 0);
-            if (GLOBAL) {
+            if (gpre) {
+                sum = j == rsub ? gsum0 : gsum1;
+            } else if (GLOBAL) {
                 // eight slices' loads in flight at a time (integer sums: any order)
                 const int32_t* src0 = p.ws + (long long)blockIdx.y * splits * p.M * BN + (long long)r * BN + 4 * q;
                 const long long sl = (long long)p.M * BN;
@@ -801,6 +851,17 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     if (!GLOBAL) {
         cluster_sync();      // no CTA leaves while another still reads its partial tile
+    } else if (p.splitk_coop) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            // the tile's last CTA to leave: every CTA of it is past the wait and
+            // done reading the slices; both counters ready for the next launch
+            unsigned int* depart = p.counters + 2 * blockIdx.y + 1;
+            if (atomicAdd(depart, 1u) + 1 == static_cast<unsigned>(splits)) {
+                p.counters[2 * blockIdx.y] = 0u;
+                *depart = 0u;
+            }
+        }
     } else if (threadIdx.x == 0 && *s_last) {
         p.counters[blockIdx.y] = 0u;     // ready for the next launch (stream-ordered after this one)
     }
@@ -1066,8 +1127,30 @@ cudaError_t launch_splitk_global(const CUtensorMap& ta, const CUtensorMap& tb, c
     if (tiles > 65535 || splits < 2 || splits > kMaxGlobalSplits || !p.ws || !p.counters || p.m_tiles != 1 ||
         p.conv_bw)
         return cudaErrorInvalidValue;
-    e = launch_k(w8a8_splitk_kernel<BN, true>, dim3(splits, (unsigned)tiles), kThreads, splitk_smem_bytes(BN, stages),
-                 st, ta, tb, p, stages);
+    const size_t smem = splitk_smem_bytes(BN, stages);
+    if (p.splitk_coop) {
+        // every CTA reduces after all have written: a cooperative launch (whether
+        // the driver takes it with programmatic dependent launch as well is found
+        // on the first uncaptured launch and remembered)
+        static std::atomic<int> with_pdl{-1};
+        int wp = with_pdl.load(std::memory_order_relaxed);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (wp < 0 && cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone) {
+            e = launch_k_coop(w8a8_splitk_kernel<BN, true>, dim3(splits, (unsigned)tiles), kThreads, smem, st, true,
+                              ta, tb, p, stages);
+            if (e == cudaSuccess) {
+                with_pdl.store(1, std::memory_order_relaxed);
+                return cudaGetLastError();
+            }
+            cudaGetLastError();
+            with_pdl.store(0, std::memory_order_relaxed);
+            wp = 0;
+        }
+        e = launch_k_coop(w8a8_splitk_kernel<BN, true>, dim3(splits, (unsigned)tiles), kThreads, smem, st, wp > 0, ta,
+                          tb, p, stages);
+    } else {
+        e = launch_k(w8a8_splitk_kernel<BN, true>, dim3(splits, (unsigned)tiles), kThreads, smem, st, ta, tb, p, stages);
+    }
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -1313,6 +1396,10 @@ cudaError_t gemm_i8_umma(const GemmI8Args& a, const CUtensorMap& ta, const CUten
         EpiParams pg = p;
         pg.ws = a.splitk_ws;
         pg.counters = a.splitk_counters;
+        // co-resident form: two counters per tile, and the whole grid at once
+        // on the SMs (one CTA per SM at this ring depth)
+        const long long tiles = (long long)((a.N + bn - 1) / bn);
+        pg.splitk_coop = (2 * tiles <= a.splitk_counters_n && tiles * plan.splits <= sm_count()) ? 1 : 0;
         switch (bn) {
             case 32: return launch_splitk_global<32>(ta, tb, pg, plan.splits, plan.stages, st);
             case 64: return launch_splitk_global<64>(ta, tb, pg, plan.splits, plan.stages, st);
