@@ -106,10 +106,24 @@ def test_shared_encoder_batch_equals_single_queries(tmp_path, monkeypatch):
     pol.close()
 
 
-def test_batch_equals_single_queries(tmp_path, monkeypatch):
-    B = 3
-    pol = _policy(tmp_path, synth.DP_SMALL, 3, monkeypatch, max_batch=4)
+@pytest.mark.parametrize("B", [3, 8])
+def test_batch_equals_single_queries(tmp_path, monkeypatch, B):
+    """B = 8 on the small U-Net: its 256-channel convs split K five ways, so
+    the GroupNorm-ended GEMM's CTAs normalize more than one sample each."""
+    pol = _policy(tmp_path, synth.DP_SMALL, 3, monkeypatch, max_batch=8)
     f, s, n = synth.dp_inputs(synth.DP_SMALL, seed=5, batch=B)
+    got = pol.predict_batch(f, s, n)
+    for b in range(B):
+        assert np.array_equal(got[b], pol.predict(f[b], s[b], n[b])), b
+    pol.close()
+
+
+def test_baseline_batch_equals_single_queries(tmp_path, monkeypatch):
+    """The benchmark's batch of 8 against eight batch-1 queries (each of
+    those matches the reference bit for bit above)."""
+    B = 8
+    pol = _policy(tmp_path, synth.DP_BASELINE, 3, monkeypatch, max_batch=B)
+    f, s, n = synth.dp_inputs(synth.DP_BASELINE, seed=7, batch=B)
     got = pol.predict_batch(f, s, n)
     for b in range(B):
         assert np.array_equal(got[b], pol.predict(f[b], s[b], n[b])), b

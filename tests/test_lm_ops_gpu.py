@@ -136,8 +136,13 @@ def test_im2col1d_exact(dev, reference, T, Cin, k, stride, pad):
     assert np.array_equal(_bits(got), _bits(reference.im2col1d(x, k, stride, pad)))
 
 
+# the U-Net's two upsampling shapes (1024 and 512 channels: 16 and 8 weight
+# chunks resident in shared memory), a ragged last weight chunk and input
+# block (Cin 100) with four chains per thread (Tout 40), and Cin 3, which only
+# the general kernel takes
 @pytest.mark.parametrize("T,Cin,Cout,k,stride,pad,bias", [(16, 64, 32, 4, 2, 1, True), (8, 256, 128, 3, 1, 1, False),
-                                                          (5, 3, 70, 4, 2, 1, True)])
+                                                          (5, 3, 70, 4, 2, 1, True), (4, 1024, 1024, 4, 2, 1, True),
+                                                          (8, 512, 512, 4, 2, 1, False), (20, 100, 64, 4, 2, 1, False)])
 def test_conv_transpose1d_exact(dev, reference, T, Cin, Cout, k, stride, pad, bias):
     from vla_simd_b200 import ops
     rng = np.random.default_rng(T * Cin)

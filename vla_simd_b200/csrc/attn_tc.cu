@@ -93,7 +93,7 @@ attention_tc_kernel(const float* Q, long long ldq, const float* K, long long ldk
                     float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv, float scale,
                     const float* mask, const AttBatch bs, const int splits) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared-window pointer
     uint8_t* sQh = sm;
     uint8_t* sQl = sQh + kTcQBytes;
     uint8_t* sPh = sQl + kTcQBytes;

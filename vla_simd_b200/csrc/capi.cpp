@@ -6,6 +6,7 @@
 
 #include "act_policy.h"
 #include "dp_policy.h"
+#include "dp.h"
 #include "octo_policy.h"
 #include "smolvla_policy.h"
 #include "bpe_tokenizer.h"
@@ -734,7 +735,14 @@ int32_t vla_cuda_conv_transpose1d(float* out, const float* x, const float* W, co
     if (!out || !x || !W || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || stride <= 0 || pad < 0 ||
         (T - 1) * stride - 2 * pad + k <= 0)
         return VLA_ERR_ARG;
-    return status_of(vsb::conv_transpose1d(x, W, bias, out, T, Cin, Cout, k, stride, pad, as_stream(stream)));
+    // the U-Net's one-sample kernels where they take the shape, else the general one
+    cudaError_t e = vsb::conv_transpose1d_f(x, W, nullptr, bias, out, 1, T, Cin, Cout, k, stride, pad, nullptr,
+                                            as_stream(stream));
+    if (e == cudaErrorInvalidValue) {
+        cudaGetLastError();
+        e = vsb::conv_transpose1d(x, W, bias, out, T, Cin, Cout, k, stride, pad, as_stream(stream));
+    }
+    return status_of(e);
 }
 
 // ------------------------------------------------------ host-pointer shims

@@ -583,8 +583,372 @@ cudaError_t launch_convt_chain(const float* x, const float* W, const float* bias
                     x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
 }
 
-cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
-                               int Cout, int k, int stride, int pad, unsigned int* rowmax, cudaStream_t st) {
+// Few samples with the CTA's whole weight slice resident: the chain kernel's
+// CTA shape (8 output channels x 16 thread rows of one sample, OPT chains per
+// thread, same per-output order) with W[0:Cin][0:k][co0:co0+8] in shared
+// memory. The slice arrives as TMA tile loads of kRsBox (ci, tap) rows, one
+// mbarrier each, all issued before the wait on the previous kernel (weights
+// are load-time constants), so the first slot's chain starts on the first
+// chunk and every later slot reads only shared memory: the weights cross HBM
+// once per launch instead of once per slot.
+constexpr int kRsBox = 256;        // (ci, tap) rows per TMA chunk (the box height)
+constexpr int kRsMaxChunks = 64;
+
+__host__ __device__ constexpr size_t convt_rs_w_bytes(int nchunks, int box) { return (size_t)nchunks * box * kChCo * 4; }
+
+template <int OPT>
+__global__ void __launch_bounds__(128)
+conv_transpose1d_resident_kernel(const __grid_constant__ CUtensorMap tw, const float* __restrict__ x,
+                                 const float* __restrict__ bias, float* __restrict__ out, int T, int Cin, int Cout,
+                                 int k, int stride, int pad, int Tout, int slots, int box, int nchunks,
+                                 unsigned int* __restrict__ rowmax) {
+    // Pointers are offsets into the __shared__ array (never integer casts), so
+    // the compiler keeps them in the shared window: LDS, not generic loads.
+    extern __shared__ __align__(16) float rs_smem[];
+    float* sW = rs_smem + ((128u - (smem_u32(rs_smem) & 127u)) & 127u) / 4;    // 128-byte aligned TMA target
+    float* sx = sW + convt_rs_w_bytes(nchunks, box) / 4;                      // [T][Cin + 4]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sx + (size_t)T * (Cin + 4));  // [nchunks]
+    const int xs = Cin + 4;
+    const int tx = threadIdx.x & (kChCo - 1), ty = threadIdx.x / kChCo;
+    const int co0 = blockIdx.x * kChCo, f = blockIdx.y;
+    const int co = co0 + tx;
+    if (threadIdx.x == 0) {
+        for (int c = 0; c < nchunks; ++c) mbar_init(&bars[c], 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tw);
+        for (int c = 0; c < nchunks; ++c) {
+            mbar_arrive_expect_tx(&bars[c], static_cast<uint32_t>(box * kChCo * 4));
+            tma_load_2d(sW + (size_t)c * box * kChCo, &tw, &bars[c], co0, c * box);
+        }
+    }
+    pdl_wait();     // x comes from the previous kernel in the stream
+    pdl_trigger();
+    const float* xf = x + (long long)f * T * Cin;
+    for (int e = threadIdx.x; e < T * (Cin / 4); e += blockDim.x) {
+        const int t = e / (Cin / 4), q = e - t * (Cin / 4);
+        *reinterpret_cast<float4*>(sx + (size_t)t * xs + 4 * q) =
+            *reinterpret_cast<const float4*>(xf + (long long)t * Cin + 4 * q);
+    }
+    __syncthreads();     // x staged, barriers initialized
+    float acc[OPT];
+    int ot[OPT];
+    #pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+        ot[i] = ty + kChRows * i;
+        acc[i] = (bias && co < Cout) ? bias[co] : 0.0f;
+    }
+    int ready = 0;       // chunks this thread has seen arrive
+    bool ok = true;
+    for (int j = 0; j < slots && ok; ++j) {
+        int kt_i[OPT], t_i[OPT];
+        #pragma unroll
+        for (int i = 0; i < OPT; ++i) {      // this slot's tap and input row per output (-1: none)
+            kt_i[i] = -1;
+            t_i[i] = 0;
+            if (ot[i] >= Tout) continue;
+            int seen = 0;
+            for (int kt = k - 1; kt >= 0; --kt) {
+                const int num = ot[i] + pad - kt;
+                if (num < 0 || num % stride) continue;
+                const int t = num / stride;
+                if (t >= T) continue;
+                if (seen++ == j) { kt_i[i] = kt; t_i[i] = t; break; }
+            }
+        }
+        for (int ci0 = 0; ci0 < Cin && ok; ci0 += 64) {
+            const int cn = min(64, Cin - ci0);
+            // every (ci, tap) row of this block of 64 input channels has landed
+            const int need = ((ci0 + cn) * k - 1) / box + 1;
+            while (ready < need) {
+                if (!mbar_wait(&bars[ready], 0)) { ok = false; break; }
+                ++ready;
+            }
+            if (!ok) break;
+            #pragma unroll
+            for (int i = 0; i < OPT; ++i) {
+                if (kt_i[i] < 0) continue;
+                const float* xr = sx + (size_t)t_i[i] * xs + ci0;
+                const float* wr = sW + ((size_t)ci0 * k + kt_i[i]) * kChCo + tx;
+                if (cn == 64) {
+                    // the block's 64 steps unrolled: their operand loads run
+                    // ahead of the fma chain, which proceeds at fma latency
+                    #pragma unroll
+                    for (int u0 = 0; u0 < 64; u0 += 8) {
+                        float xv[8], wv[8];
+                        #pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            xv[u] = xr[u0 + u];
+                            wv[u] = wr[(size_t)(u0 + u) * k * kChCo];
+                        }
+                        #pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            if (xv[u] != 0.0f) acc[i] = __fmaf_rn(xv[u], wv[u], acc[i]);
+                    }
+                } else {
+                    for (int u = 0; u < cn; ++u) {
+                        const float v = xr[u];
+                        if (v == 0.0f) continue;
+                        acc[i] = __fmaf_rn(v, wr[(size_t)u * k * kChCo], acc[i]);
+                    }
+                }
+            }
+        }
+    }
+    // no copy may still be landing when the CTA leaves (after a timeout every
+    // wait is bounded again)
+    while (ok && ready < nchunks) {
+        if (!mbar_wait(&bars[ready], 0)) ok = false;
+        ++ready;
+    }
+    if (!ok) return;
+    #pragma unroll
+    for (int i = 0; i < OPT; ++i) {
+        const bool valid = ot[i] < Tout && co < Cout;
+        if (valid) out[((long long)f * Tout + ot[i]) * Cout + co] = acc[i];
+        if (rowmax) {
+            // the 8 channels of this row sit in 8 consecutive lanes; every lane
+            // of the warp takes part in the shuffles
+            float m = valid ? fabsf(acc[i]) : 0.0f;
+            #pragma unroll
+            for (int off = 4; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+            if (tx == 0 && ot[i] < Tout) atomicMax(&rowmax[f * Tout + ot[i]], __float_as_uint(m));
+        }
+    }
+}
+
+// fp32 [rows][cols] map with a {8, box_rows} box, no swizzle (the resident
+// transposed conv's weight chunks: 32-byte rows packed in shared memory)
+static bool make_tmap_f32_box8(CUtensorMap* map, const float* base, int rows, int cols, int box_rows) {
+    auto fn = get_encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (cols & 3) || rows <= 0 || cols < kChCo) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+    const cuuint32_t boxd[2] = {static_cast<cuuint32_t>(kChCo), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr size_t kRsMaxSmem = 220 * 1024;
+
+static size_t convt_rs_smem(int T, int Cin, int k, int* box, int* nchunks) {
+    const int rows = Cin * k;
+    *box = rows < kRsBox ? rows : kRsBox;
+    *nchunks = (rows + *box - 1) / *box;
+    return 128 + convt_rs_w_bytes(*nchunks, *box) + (size_t)T * (Cin + 4) * 4 + kRsMaxChunks * 8;
+}
+
+// cudaErrorNotSupported: the shape is not for this kernel (the caller takes another)
+template <int OPT>
+cudaError_t launch_convt_resident(const float* x, const float* W, const float* bias, float* out, int F, int T,
+                                  int Cin, int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax,
+                                  cudaStream_t st) {
+    int box = 0, nchunks = 0;
+    const size_t smem = convt_rs_smem(T, Cin, k, &box, &nchunks);
+    if (smem > kRsMaxSmem || nchunks > kRsMaxChunks || Cin % 4 || Cout % kChCo) return cudaErrorNotSupported;
+    CUtensorMap tw;
+    if (!make_tmap_f32_box8(&tw, W, Cin * k, Cout, box)) return cudaErrorNotSupported;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(conv_transpose1d_resident_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kRsMaxSmem);
+        attr = true;
+    }
+    const int slots = (k + stride - 1) / stride;
+    return launch_k(conv_transpose1d_resident_kernel<OPT>, dim3((unsigned)(Cout / kChCo), (unsigned)F), 128, smem,
+                    st, tw, x, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, box, nchunks, rowmax);
+}
+
+// Several samples: CTA = 8 output channels x all Tout time steps x SB
+// samples; a consumer thread owns one (channel, time step) of kBtSpt samples,
+// their chains interleaved. x of the CTA's samples stays in shared memory; the
+// weights stream from the transposed copy Wt [Cout][k][Cin] (ci contiguous)
+// through a ring of TMA stages of ci_st input channels x `stride` taps x 8
+// channels (128-byte swizzle: a warp's float4 reads of 8 rows hit 8 distinct
+// bank groups), loaded by a producer warp that starts before the wait on the
+// previous kernel. Pass p streams the taps [k - (p+1)*stride, k - p*stride):
+// an output has at most one tap in such a window (the one of its residue mod
+// stride), so the passes in order visit each output's taps in descending order
+// and ci ascending within a tap - the reference's per-output order - and every
+// weight is read once per CTA (the tiled kernel reads all k taps per slot).
+constexpr int kBtCo = 8, kBtBoxCi = 32, kBtStageCi = 128, kBtStages = 4, kBtSpt = 2, kBtMaxConsumers = 512;
+
+__host__ __device__ constexpr int convt_bt_stage_bytes(int ci_st, int stride) {
+    return (ci_st / kBtBoxCi) * kBtCo * stride * 128;
+}
+
+__global__ void __launch_bounds__(kBtMaxConsumers + 32)
+conv_transpose1d_batched_kernel(const __grid_constant__ CUtensorMap twt, const float* __restrict__ x,
+                                const float* __restrict__ bias, float* __restrict__ out, int F, int T, int Cin,
+                                int Cout, int k, int stride, int pad, int Tout, int SB, int ci_st,
+                                unsigned int* __restrict__ rowmax) {
+    extern __shared__ __align__(16) uint8_t bt_smem[];
+    uint8_t* ring = bt_smem + ((1024u - (smem_u32(bt_smem) & 1023u)) & 1023u);   // 128-byte swizzle: 1 KB aligned
+    const int nbox = ci_st / kBtBoxCi;
+    const int box_bytes = kBtCo * stride * 128;
+    const int stage_bytes = nbox * box_bytes;
+    const int xs = Cin + 4;                                          // 16-byte rows, distinct banks per row
+    float* sx = reinterpret_cast<float*>(ring + (size_t)kBtStages * stage_bytes);     // [SB][T][xs]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sx + (size_t)SB * T * xs);
+    uint64_t* empty = full + kBtStages;
+    const int NC = kBtCo * Tout * (SB / kBtSpt);                     // consumer threads (whole warps)
+    const int co0 = blockIdx.x * kBtCo, f0 = blockIdx.y * SB;
+    const int nci = Cin / ci_st;
+    const int G = ((k + stride - 1) / stride) * nci;                 // stages, pass-major
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBtStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NC / 32);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x >= NC) {
+        // producer: weights are load-time constants, so no wait on the previous kernel
+        if (threadIdx.x == NC) {
+            tma_prefetch_desc(&twt);
+            for (int g = 0; g < G; ++g) {
+                const int s = g % kBtStages;
+                if (g >= kBtStages && !mbar_wait(&empty[s], ((g / kBtStages) - 1) & 1)) break;
+                const int p = g / nci, c = g - p * nci;
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
+                for (int b = 0; b < nbox; ++b)
+                    tma_load_3d(ring + (size_t)s * stage_bytes + (size_t)b * box_bytes, &twt, &full[s],
+                                c * ci_st + b * kBtBoxCi, k - (p + 1) * stride, co0);
+            }
+        }
+        return;
+    }
+    pdl_wait();     // x comes from the previous kernel in the stream
+    pdl_trigger();
+    const int c4 = Cin / 4;
+    for (int e = threadIdx.x; e < SB * T * c4; e += NC) {
+        const int row = e / c4, q = e - row * c4;                   // row = sample * T + t
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (f0 + row / T < F) v = *reinterpret_cast<const float4*>(x + ((long long)f0 * T + row) * Cin + 4 * q);
+        *reinterpret_cast<float4*>(sx + (size_t)row * xs + 4 * q) = v;
+    }
+    asm volatile("bar.sync 1, %0;" :: "r"(NC) : "memory");          // consumers only
+    const int ot = threadIdx.x % Tout;
+    const int col = (threadIdx.x / Tout) % kBtCo;
+    const int sg = threadIdx.x / (Tout * kBtCo);
+    const int co = co0 + col;
+    float acc[kBtSpt];
+    #pragma unroll
+    for (int i = 0; i < kBtSpt; ++i) acc[i] = bias ? bias[co] : 0.0f;
+    int cur_p = -1, kt = -1, t = 0, wrow = 0;
+    bool ok = true;
+    for (int g = 0; g < G; ++g) {
+        const int s = g % kBtStages;
+        const int p = g / nci, c = g - p * nci;
+        if (p != cur_p) {      // this pass's tap of this output (-1: none)
+            cur_p = p;
+            const int kt_lo = k - (p + 1) * stride;
+            const int num_lo = ot + pad - kt_lo;
+            kt = kt_lo + ((num_lo % stride) + stride) % stride;
+            const int num = ot + pad - kt;
+            t = num >= 0 ? num / stride : -1;
+            if (kt < 0 || kt >= k || t < 0 || t >= T) kt = -1;
+            wrow = col * stride + (kt - kt_lo);
+        }
+        if (!mbar_wait(&full[s], (g / kBtStages) & 1)) { ok = false; break; }
+        if (kt >= 0) {
+            const uint8_t* wst = ring + (size_t)s * stage_bytes + wrow * 128;
+            const int sw = wrow & 7;
+            const float* xr = sx + ((size_t)sg * kBtSpt * T + t) * xs + c * ci_st;
+            for (int b = 0; b < nbox; ++b) {
+                #pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 w4 = *reinterpret_cast<const float4*>(wst + b * box_bytes + ((j ^ sw) << 4));
+                    #pragma unroll
+                    for (int i = 0; i < kBtSpt; ++i) {
+                        const float4 x4 =
+                            *reinterpret_cast<const float4*>(xr + (size_t)i * T * xs + b * kBtBoxCi + 4 * j);
+                        if (x4.x != 0.0f) acc[i] = __fmaf_rn(x4.x, w4.x, acc[i]);
+                        if (x4.y != 0.0f) acc[i] = __fmaf_rn(x4.y, w4.y, acc[i]);
+                        if (x4.z != 0.0f) acc[i] = __fmaf_rn(x4.z, w4.z, acc[i]);
+                        if (x4.w != 0.0f) acc[i] = __fmaf_rn(x4.w, w4.w, acc[i]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
+    }
+    if (!ok) return;
+    #pragma unroll
+    for (int i = 0; i < kBtSpt; ++i) {
+        const int sl = sg * kBtSpt + i;
+        const bool live = f0 + sl < F;
+        const long long orow = (long long)(f0 + sl) * Tout + ot;
+        if (live) out[orow * Cout + co] = acc[i];
+        if (rowmax) {
+            // lane ^ Tout, ^ 2 Tout, ... hold this time step's other channels
+            // of the CTA (Tout divides 32); every lane takes part
+            float m = live ? fabsf(acc[i]) : 0.0f;
+            for (int off = Tout; off < 32; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+            if ((threadIdx.x & 31) < Tout && live) atomicMax(&rowmax[orow], __float_as_uint(m));
+        }
+    }
+}
+
+// Wt [Cout][k][Cin] as a 3D map {Cin, k, Cout}, box {32, stride, 8}, 128-byte swizzle
+static bool make_tmap_convt_wt(CUtensorMap* map, const float* Wt, int Cin, int k, int Cout, int stride) {
+    auto fn = get_encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(Wt) & 15) || Cin % kBtBoxCi) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Cin), static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(Cout)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Cin) * 4, static_cast<cuuint64_t>(k) * Cin * 4};
+    const cuuint32_t boxd[3] = {static_cast<cuuint32_t>(kBtBoxCi), static_cast<cuuint32_t>(stride),
+                                static_cast<cuuint32_t>(kBtCo)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(Wt), dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static size_t convt_bt_smem(int SB, int T, int Cin, int ci_st, int stride) {
+    return 1024 + (size_t)kBtStages * convt_bt_stage_bytes(ci_st, stride) + (size_t)SB * T * (Cin + 4) * 4 +
+           2 * kBtStages * 8;
+}
+
+// cudaErrorNotSupported: the shape is not for this kernel (the caller takes another)
+cudaError_t launch_convt_batched(const float* x, const float* Wt, const float* bias, float* out, int F, int T,
+                                 int Cin, int Cout, int k, int stride, int pad, int Tout, unsigned int* rowmax,
+                                 cudaStream_t st) {
+    const bool tout_ok = Tout == 4 || Tout == 8 || Tout == 16 || Tout == 32;
+    const int ci_st = Cin <= kBtStageCi ? Cin : kBtStageCi;
+    if (!Wt || !tout_ok || Cin % kBtBoxCi || Cin % ci_st || Cout % kBtCo || stride > 32 || k > 256)
+        return cudaErrorNotSupported;
+    // samples per CTA: as many as the consumer threads allow, halved while the
+    // grid would leave SMs idle or the samples' x does not fit
+    const int groups_max = kBtMaxConsumers / (kBtCo * Tout);
+    int SB = kBtSpt * groups_max;
+    const int Fr = (F + kBtSpt - 1) / kBtSpt * kBtSpt;
+    while (SB > Fr) SB -= kBtSpt;
+    const long long co_blocks = Cout / kBtCo;
+    while (SB > kBtSpt && co_blocks * ((F + SB - 1) / SB) < 148) SB = (SB / 2 + kBtSpt - 1) / kBtSpt * kBtSpt;
+    const size_t limit = 220 * 1024;
+    while (SB > kBtSpt && convt_bt_smem(SB, T, Cin, ci_st, stride) > limit) SB -= kBtSpt;
+    const size_t smem = convt_bt_smem(SB, T, Cin, ci_st, stride);
+    if (smem > limit || (F + SB - 1) / SB > 65535) return cudaErrorNotSupported;
+    CUtensorMap twt;
+    if (!make_tmap_convt_wt(&twt, Wt, Cin, k, Cout, stride)) return cudaErrorNotSupported;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(conv_transpose1d_batched_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)limit);
+        attr = true;
+    }
+    const int threads = kBtCo * Tout * (SB / kBtSpt) + 32;
+    return launch_k(conv_transpose1d_batched_kernel, dim3((unsigned)co_blocks, (unsigned)((F + SB - 1) / SB)),
+                    (unsigned)threads, smem, st, twt, x, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, SB, ci_st,
+                    rowmax);
+}
+
+cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* Wt, const float* bias, float* out, int F,
+                               int T, int Cin, int Cout, int k, int stride, int pad, unsigned int* rowmax,
+                               cudaStream_t st) {
     const int Tout = (T - 1) * stride - 2 * pad + k;
     // 16-byte cp.async rows; time steps spread over at most 256 / 8 thread groups x 4 per thread
     if (F <= 0 || T <= 0 || Cin <= 0 || Cout <= 0 || k <= 0 || k > kCtMaxK || stride <= 0 || pad < 0 || Tout <= 0 ||
@@ -594,13 +958,28 @@ cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias
     const int OTP = Tout <= 32 ? 1 : Tout <= 64 ? 2 : 4;
     if (Tout % OTP) return cudaErrorInvalidValue;
     if (F < 4 && Tout <= 4 * kChRows && Cout % kChCo == 0) {
-        // a lone sample (or two, three): one sample per CTA row, one chain per thread
+        // a lone sample (or two, three): one sample per CTA row, one chain per
+        // thread; the weight slice resident in shared memory where it fits
         cudaError_t e2;
+        if (Tout <= kChRows) e2 = launch_convt_resident<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        else if (Tout <= 2 * kChRows) e2 = launch_convt_resident<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        else e2 = launch_convt_resident<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        if (e2 != cudaErrorNotSupported) {
+            if (e2 != cudaSuccess) return e2;
+            return cudaGetLastError();
+        }
         if (Tout <= kChRows) e2 = launch_convt_chain<1>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
         else if (Tout <= 2 * kChRows) e2 = launch_convt_chain<2>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
         else e2 = launch_convt_chain<4>(x, W, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
         if (e2 != cudaSuccess) return e2;
         return cudaGetLastError();
+    }
+    if (Wt) {
+        const cudaError_t e2 = launch_convt_batched(x, Wt, bias, out, F, T, Cin, Cout, k, stride, pad, Tout, rowmax, st);
+        if (e2 != cudaErrorNotSupported) {
+            if (e2 != cudaSuccess) return e2;
+            return cudaGetLastError();
+        }
     }
     // many samples: 32 channels x 4 samples per CTA tile (weights reused across
     // the samples); otherwise 8 channels per CTA

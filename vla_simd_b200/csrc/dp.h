@@ -46,8 +46,11 @@ cudaError_t concat_channels(const float* a, int C1, const float* b, int C2, floa
 // conv_transpose1d of F samples (x [F][T][Cin], W [Cin][k][Cout]) -> out [F][Tout][Cout],
 // the reference's per-output accumulation order (src/hal/common/conv.cpp:349-395);
 // optional per-row absmax of the output (atomicMax into rowmax [F*Tout], zeroed by the caller).
-cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* bias, float* out, int F, int T, int Cin,
-                               int Cout, int k, int stride, int pad, unsigned int* rowmax, cudaStream_t st);
+// Wt (optional): the same weights as [Cout][k][Cin], which the several-sample
+// kernel streams. cudaErrorInvalidValue: a shape no kernel here takes.
+cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* Wt, const float* bias, float* out, int F,
+                               int T, int Cin, int Cout, int k, int stride, int pad, unsigned int* rowmax,
+                               cudaStream_t st);
 
 // U-Net GroupNorm -> Mish -> epilogue over x [F][T][C] (out may alias x):
 // kUgMish nothing more, kUgFilmScale fma(film[f][c], v, film[f][C + c]),

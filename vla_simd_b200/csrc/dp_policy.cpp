@@ -420,6 +420,13 @@ bool DpPolicy::load_unet(const ModelFiles& files, bool int8) {
             const float* b = take(dim_out);
             if (!take.ok) { fail("unet.bin too short"); return false; }
             u.uw = dev_copy(w, (size_t)dim_out * 4 * dim_out);
+            // [Cout][k][Cin] copy for the several-sample kernel
+            std::vector<float> wt((size_t)dim_out * 4 * dim_out);
+            for (int ci = 0; ci < dim_out; ++ci)
+                for (int kt = 0; kt < 4; ++kt)
+                    for (int co = 0; co < dim_out; ++co)
+                        wt[((size_t)co * 4 + kt) * dim_out + ci] = w[((size_t)ci * 4 + kt) * dim_out + co];
+            u.uwt = dev_copy(wt.data(), wt.size());
             u.ub = dev_copy(b, dim_out);
         }
     }
@@ -950,7 +957,7 @@ cudaError_t DpPolicy::unet(int B, int step, cudaStream_t st) {
             const int Tout = (T - 1) * 2 - 2 + 4;
             unsigned int* rm_u = rm_take((long long)B * Tout);
             if (!rm_u) return cudaErrorInvalidValue;
-            VSB_TRY(conv_transpose1d_f(d_b_, u.uw, u.ub, d_x_, B, T, C, u.uc, 4, 2, 1, rm_u, st));
+            VSB_TRY(conv_transpose1d_f(d_b_, u.uw, u.uwt, u.ub, d_x_, B, T, C, u.uc, 4, 2, 1, rm_u, st));
             T = Tout;
             C = u.uc;
             x = d_x_;

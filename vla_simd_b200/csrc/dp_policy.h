@@ -65,7 +65,14 @@ struct DpResBlockDev {
 };
 
 struct DpDownDev { DpResBlockDev r1, r2; DevLinear ds; bool has = false; };
-struct DpUpDev { DpResBlockDev r1, r2; float* uw = nullptr; float* ub = nullptr; bool has = false; int uc = 0; };
+struct DpUpDev {
+    DpResBlockDev r1, r2;
+    float* uw = nullptr;    // [Cin][4][Cout]
+    float* uwt = nullptr;   // the same as [Cout][4][Cin]
+    float* ub = nullptr;
+    bool has = false;
+    int uc = 0;
+};
 
 // Workspace of the split-K GEMM path (GemmI8Args::splitk_ws / splitk_counters).
 struct DpSplitWs {

@@ -216,7 +216,7 @@ w8a8_umma_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
     extern __shared__ uint8_t smem_raw[];
     // SW128 tiles want 1024-byte alignment
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared-window pointer
     uint8_t* sA = smem;
     uint8_t* sB = smem + stages * kABytes;
     float* stg_all = reinterpret_cast<float*>(sB + stages * kBBytes);
@@ -553,7 +553,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // partial tile overlays the stage ring
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared-window pointer
     uint8_t* sA = smem;
     uint8_t* sB = smem + stages * kABytes;
     int32_t* part = reinterpret_cast<int32_t*>(smem);    // [kBM][kPS], once the ring is idle

@@ -164,7 +164,7 @@ w8a8_slab_kernel(const __grid_constant__ CUtensorMap tmap_a,
     while (tcols < bn) tcols <<= 1;
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared-window pointer
     uint8_t* sA = smem;                                            // nkb x 16 KB
     uint8_t* sB = sA + nkb * kAKb;                                 // stages x slice_bytes
     float* stg = reinterpret_cast<float*>(sB + stages * slice_bytes);   // 8 warps x nstg x 4 KB

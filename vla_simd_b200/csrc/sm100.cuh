@@ -139,6 +139,18 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// 3D tile load; x (innermost) a multiple of 16 bytes. y and z may start
+// outside the tensor (those rows read zeros).
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
+           "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // 4D tile load (implicit convolution: box {channels, W, H, 1} of an NHWC
 // tensor); x = channel offset, a multiple of 16 bytes. Coordinates past the
 // tensor (conv padding) read zeros.
