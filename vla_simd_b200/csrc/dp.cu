@@ -583,6 +583,47 @@ cudaError_t launch_convt_chain(const float* x, const float* W, const float* bias
                     x, W, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, rowmax);
 }
 
+// 64 steps of one output's chain: acc = fma(x[u], w[u * wstep], acc) for u
+// ascending, skipping x == 0 (the reference's skip) when SKIP. The next eight
+// steps' operands are loaded before the current eight fmas, so the chain runs
+// at the fma latency. Without zeros in x, SKIP = false gives the same bits.
+template <bool SKIP, int WS>      // WS: the weight stride when known at compile time (else 0: wstep_rt)
+__device__ __forceinline__ float convt_chain64(const float* xr, const float* wr, int wstep_rt, float acc) {
+    const int wstep = WS ? WS : wstep_rt;      // a constant stride makes every load offset an immediate
+    float xa[8], wa[8], xb[8], wb[8];
+    auto ld = [&](float* xv, float* wv, int u0) {
+        const float4 p = *reinterpret_cast<const float4*>(xr + u0);
+        const float4 q = *reinterpret_cast<const float4*>(xr + u0 + 4);
+        xv[0] = p.x; xv[1] = p.y; xv[2] = p.z; xv[3] = p.w;
+        xv[4] = q.x; xv[5] = q.y; xv[6] = q.z; xv[7] = q.w;
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) wv[u] = wr[(u0 + u) * wstep];
+    };
+    auto fm = [&](const float* xv, const float* wv) {
+        #pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (!SKIP || xv[u] != 0.0f) acc = __fmaf_rn(xv[u], wv[u], acc);
+    };
+    ld(xa, wa, 0);
+    #pragma unroll
+    for (int u0 = 0; u0 < 64; u0 += 16) {
+        ld(xb, wb, u0 + 8);
+        fm(xa, wa);
+        if (u0 + 16 < 64) ld(xa, wa, u0 + 16);
+        fm(xb, wb);
+    }
+    return acc;
+}
+
+// OR of v over the `n` threads that meet at named barrier `id` (whole warps)
+__device__ __forceinline__ bool bar_or(int id, int n, bool v) {
+    int r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\t"
+                 "bar.red.or.pred q, %2, %3, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"(v ? 1 : 0), "r"(id), "r"(n) : "memory");
+    return r != 0;
+}
+
 // Few samples with the CTA's whole weight slice resident: the chain kernel's
 // CTA shape (8 output channels x 16 thread rows of one sample, OPT chains per
 // thread, same per-output order) with W[0:Cin][0:k][co0:co0+8] in shared
@@ -596,12 +637,13 @@ constexpr int kRsMaxChunks = 64;
 
 __host__ __device__ constexpr size_t convt_rs_w_bytes(int nchunks, int box) { return (size_t)nchunks * box * kChCo * 4; }
 
-template <int OPT>
+template <int OPT, int KS>       // KS: the tap count when fixed at compile time (the U-Net's 4), else 0
 __global__ void __launch_bounds__(128)
 conv_transpose1d_resident_kernel(const __grid_constant__ CUtensorMap tw, const float* __restrict__ x,
                                  const float* __restrict__ bias, float* __restrict__ out, int T, int Cin, int Cout,
-                                 int k, int stride, int pad, int Tout, int slots, int box, int nchunks,
+                                 int k_rt, int stride, int pad, int Tout, int slots, int box, int nchunks,
                                  unsigned int* __restrict__ rowmax) {
+    const int k = KS ? KS : k_rt;
     // Pointers are offsets into the __shared__ array (never integer casts), so
     // the compiler keeps them in the shared window: LDS, not generic loads.
     extern __shared__ __align__(16) float rs_smem[];
@@ -624,12 +666,15 @@ conv_transpose1d_resident_kernel(const __grid_constant__ CUtensorMap tw, const f
     pdl_wait();     // x comes from the previous kernel in the stream
     pdl_trigger();
     const float* xf = x + (long long)f * T * Cin;
+    bool zero = false;
     for (int e = threadIdx.x; e < T * (Cin / 4); e += blockDim.x) {
         const int t = e / (Cin / 4), q = e - t * (Cin / 4);
-        *reinterpret_cast<float4*>(sx + (size_t)t * xs + 4 * q) =
-            *reinterpret_cast<const float4*>(xf + (long long)t * Cin + 4 * q);
+        const float4 v = *reinterpret_cast<const float4*>(xf + (long long)t * Cin + 4 * q);
+        zero |= v.x == 0.0f || v.y == 0.0f || v.z == 0.0f || v.w == 0.0f;
+        *reinterpret_cast<float4*>(sx + (size_t)t * xs + 4 * q) = v;
     }
-    __syncthreads();     // x staged, barriers initialized
+    // x staged, barriers initialized; does any input need the zero skip?
+    const bool any_zero = __syncthreads_or(zero) != 0;
     float acc[OPT];
     int ot[OPT];
     #pragma unroll
@@ -670,20 +715,8 @@ conv_transpose1d_resident_kernel(const __grid_constant__ CUtensorMap tw, const f
                 const float* xr = sx + (size_t)t_i[i] * xs + ci0;
                 const float* wr = sW + ((size_t)ci0 * k + kt_i[i]) * kChCo + tx;
                 if (cn == 64) {
-                    // the block's 64 steps unrolled: their operand loads run
-                    // ahead of the fma chain, which proceeds at fma latency
-                    #pragma unroll
-                    for (int u0 = 0; u0 < 64; u0 += 8) {
-                        float xv[8], wv[8];
-                        #pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            xv[u] = xr[u0 + u];
-                            wv[u] = wr[(size_t)(u0 + u) * k * kChCo];
-                        }
-                        #pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            if (xv[u] != 0.0f) acc[i] = __fmaf_rn(xv[u], wv[u], acc[i]);
-                    }
+                    acc[i] = any_zero ? convt_chain64<true, KS * kChCo>(xr, wr, k * kChCo, acc[i])
+                                      : convt_chain64<false, KS * kChCo>(xr, wr, k * kChCo, acc[i]);
                 } else {
                     for (int u = 0; u < cn; ++u) {
                         const float v = xr[u];
@@ -751,13 +784,19 @@ cudaError_t launch_convt_resident(const float* x, const float* W, const float* b
     if (!make_tmap_f32_box8(&tw, W, Cin * k, Cout, box)) return cudaErrorNotSupported;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(conv_transpose1d_resident_kernel<OPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(conv_transpose1d_resident_kernel<OPT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kRsMaxSmem);
+        cudaFuncSetAttribute(conv_transpose1d_resident_kernel<OPT, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kRsMaxSmem);
         attr = true;
     }
     const int slots = (k + stride - 1) / stride;
-    return launch_k(conv_transpose1d_resident_kernel<OPT>, dim3((unsigned)(Cout / kChCo), (unsigned)F), 128, smem,
-                    st, tw, x, bias, out, T, Cin, Cout, k, stride, pad, Tout, slots, box, nchunks, rowmax);
+    const dim3 grid((unsigned)(Cout / kChCo), (unsigned)F);
+    if (k == 4)
+        return launch_k(conv_transpose1d_resident_kernel<OPT, 4>, grid, 128, smem, st, tw, x, bias, out, T, Cin, Cout, k,
+                        stride, pad, Tout, slots, box, nchunks, rowmax);
+    return launch_k(conv_transpose1d_resident_kernel<OPT, 0>, grid, 128, smem, st, tw, x, bias, out, T, Cin, Cout, k,
+                    stride, pad, Tout, slots, box, nchunks, rowmax);
 }
 
 // Several samples: CTA = 8 output channels x all Tout time steps x SB
@@ -772,10 +811,37 @@ cudaError_t launch_convt_resident(const float* x, const float* W, const float* b
 // stride), so the passes in order visit each output's taps in descending order
 // and ci ascending within a tap - the reference's per-output order - and every
 // weight is read once per CTA (the tiled kernel reads all k taps per slot).
-constexpr int kBtCo = 8, kBtBoxCi = 32, kBtStageCi = 128, kBtStages = 4, kBtSpt = 2, kBtMaxConsumers = 512;
+// Eight 8 KB stages in flight per CTA: enough bytes to cover the TMA latency
+// at the rate the chains consume them (four left the consumers waiting).
+constexpr int kBtCo = 8, kBtBoxCi = 32, kBtStageCi = 128, kBtStages = 8, kBtSpt = 2, kBtMaxConsumers = 512;
 
 __host__ __device__ constexpr int convt_bt_stage_bytes(int ci_st, int stride) {
     return (ci_st / kBtBoxCi) * kBtCo * stride * 128;
+}
+
+// One ring stage of a consumer's kBtSpt chains: nbox boxes of 32 input
+// channels, the weight row `wrow` of each box (128-byte swizzled rows) against
+// the samples' x rows (xr, sample stride `ss`). SKIP: the reference's zero skip.
+template <bool SKIP>
+__device__ __forceinline__ void convt_bt_stage(const uint8_t* wst, int sw, int box_bytes, int nbox, const float* xr,
+                                               int ss, float (&acc)[kBtSpt]) {
+    #pragma unroll 1
+    for (int b = 0; b < nbox; ++b) {
+        const uint8_t* wb = wst + b * box_bytes;
+        const float* xb = xr + b * kBtBoxCi;
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 w4 = *reinterpret_cast<const float4*>(wb + ((j ^ sw) << 4));
+            #pragma unroll
+            for (int i = 0; i < kBtSpt; ++i) {
+                const float4 x4 = *reinterpret_cast<const float4*>(xb + i * ss + 4 * j);
+                if (!SKIP || x4.x != 0.0f) acc[i] = __fmaf_rn(x4.x, w4.x, acc[i]);
+                if (!SKIP || x4.y != 0.0f) acc[i] = __fmaf_rn(x4.y, w4.y, acc[i]);
+                if (!SKIP || x4.z != 0.0f) acc[i] = __fmaf_rn(x4.z, w4.z, acc[i]);
+                if (!SKIP || x4.w != 0.0f) acc[i] = __fmaf_rn(x4.w, w4.w, acc[i]);
+            }
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kBtMaxConsumers + 32)
@@ -823,13 +889,18 @@ conv_transpose1d_batched_kernel(const __grid_constant__ CUtensorMap twt, const f
     pdl_wait();     // x comes from the previous kernel in the stream
     pdl_trigger();
     const int c4 = Cin / 4;
+    bool zero = false;
     for (int e = threadIdx.x; e < SB * T * c4; e += NC) {
         const int row = e / c4, q = e - row * c4;                   // row = sample * T + t
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (f0 + row / T < F) v = *reinterpret_cast<const float4*>(x + ((long long)f0 * T + row) * Cin + 4 * q);
+        float4 v = make_float4(1.0f, 1.0f, 1.0f, 1.0f);            // samples past F: no zeros to skip
+        if (f0 + row / T < F) {
+            v = *reinterpret_cast<const float4*>(x + ((long long)f0 * T + row) * Cin + 4 * q);
+            zero |= v.x == 0.0f || v.y == 0.0f || v.z == 0.0f || v.w == 0.0f;
+        }
         *reinterpret_cast<float4*>(sx + (size_t)row * xs + 4 * q) = v;
     }
-    asm volatile("bar.sync 1, %0;" :: "r"(NC) : "memory");          // consumers only
+    // consumers only: x staged; without zeros in it the skip changes nothing
+    const bool any_zero = bar_or(1, NC, zero);
     const int ot = threadIdx.x % Tout;
     const int col = (threadIdx.x / Tout) % kBtCo;
     const int sg = threadIdx.x / (Tout * kBtCo);
@@ -855,23 +926,9 @@ conv_transpose1d_batched_kernel(const __grid_constant__ CUtensorMap twt, const f
         if (!mbar_wait(&full[s], (g / kBtStages) & 1)) { ok = false; break; }
         if (kt >= 0) {
             const uint8_t* wst = ring + (size_t)s * stage_bytes + wrow * 128;
-            const int sw = wrow & 7;
             const float* xr = sx + ((size_t)sg * kBtSpt * T + t) * xs + c * ci_st;
-            for (int b = 0; b < nbox; ++b) {
-                #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 w4 = *reinterpret_cast<const float4*>(wst + b * box_bytes + ((j ^ sw) << 4));
-                    #pragma unroll
-                    for (int i = 0; i < kBtSpt; ++i) {
-                        const float4 x4 =
-                            *reinterpret_cast<const float4*>(xr + (size_t)i * T * xs + b * kBtBoxCi + 4 * j);
-                        if (x4.x != 0.0f) acc[i] = __fmaf_rn(x4.x, w4.x, acc[i]);
-                        if (x4.y != 0.0f) acc[i] = __fmaf_rn(x4.y, w4.y, acc[i]);
-                        if (x4.z != 0.0f) acc[i] = __fmaf_rn(x4.z, w4.z, acc[i]);
-                        if (x4.w != 0.0f) acc[i] = __fmaf_rn(x4.w, w4.w, acc[i]);
-                    }
-                }
-            }
+            if (any_zero) convt_bt_stage<true>(wst, wrow & 7, box_bytes, nbox, xr, T * xs, acc);
+            else convt_bt_stage<false>(wst, wrow & 7, box_bytes, nbox, xr, T * xs, acc);
         }
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
@@ -920,18 +977,29 @@ cudaError_t launch_convt_batched(const float* x, const float* Wt, const float* b
     const int ci_st = Cin <= kBtStageCi ? Cin : kBtStageCi;
     if (!Wt || !tout_ok || Cin % kBtBoxCi || Cin % ci_st || Cout % kBtCo || stride > 32 || k > 256)
         return cudaErrorNotSupported;
-    // samples per CTA: as many as the consumer threads allow, halved while the
-    // grid would leave SMs idle or the samples' x does not fit
+    // samples per CTA: the fewest waves of CTAs (a CTA's time hardly depends on
+    // its sample count: more samples are more threads), then the most CTAs
     const int groups_max = kBtMaxConsumers / (kBtCo * Tout);
-    int SB = kBtSpt * groups_max;
-    const int Fr = (F + kBtSpt - 1) / kBtSpt * kBtSpt;
-    while (SB > Fr) SB -= kBtSpt;
     const long long co_blocks = Cout / kBtCo;
-    while (SB > kBtSpt && co_blocks * ((F + SB - 1) / SB) < 148) SB = (SB / 2 + kBtSpt - 1) / kBtSpt * kBtSpt;
     const size_t limit = 220 * 1024;
-    while (SB > kBtSpt && convt_bt_smem(SB, T, Cin, ci_st, stride) > limit) SB -= kBtSpt;
+    int SB = 0;
+    long long best_waves = 0, best_grid = 0;
+    for (int sb = kBtSpt; sb <= kBtSpt * groups_max; sb += kBtSpt) {
+        const size_t sm = convt_bt_smem(sb, T, Cin, ci_st, stride);
+        if (sm > limit) break;
+        const long long grid = co_blocks * ((F + sb - 1) / sb);
+        const long long per_sm = (long long)(228 * 1024) / (long long)(sm + 1024);
+        const long long waves = (grid + 148 * per_sm - 1) / (148 * per_sm);
+        if (!SB || waves < best_waves || (waves == best_waves && grid > best_grid)) {
+            SB = sb;
+            best_waves = waves;
+            best_grid = grid;
+        }
+        if (sb >= F) break;
+    }
+    if (!SB) return cudaErrorNotSupported;
     const size_t smem = convt_bt_smem(SB, T, Cin, ci_st, stride);
-    if (smem > limit || (F + SB - 1) / SB > 65535) return cudaErrorNotSupported;
+    if ((F + SB - 1) / SB > 65535) return cudaErrorNotSupported;
     CUtensorMap twt;
     if (!make_tmap_convt_wt(&twt, Wt, Cin, k, Cout, stride)) return cudaErrorNotSupported;
     static bool attr = false;
@@ -1005,7 +1073,7 @@ cudaError_t conv_transpose1d_f(const float* x, const float* W, const float* Wt, 
 __global__ void __launch_bounds__(256)
 unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float* __restrict__ scale,
                const float* __restrict__ bias, int epi, const float* __restrict__ film, long long ld_film,
-               const float* res, float* out, unsigned int* __restrict__ rowmax) {
+               const float* res, float* out, unsigned int* __restrict__ rowmax, int piece) {
     pdl_wait();     // x comes from the GEMM before
     pdl_trigger();
     extern __shared__ float ug_smem[];
@@ -1032,6 +1100,24 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
         }
     }
     for (int p = threadIdx.x; p < T; p += blockDim.x) srm[p] = 0u;
+    // the first epilogue pass's FiLM / residual operands, loaded now so their
+    // latency overlaps the statistics
+    const int e_lo = blockIdx.z * piece, e_hi = min(T * gc, e_lo + piece);
+    float pre_a = 0.0f, pre_b = 0.0f;
+    {
+        const int e = e_lo + threadIdx.x;
+        if (e < e_hi) {
+            const int p = e / gc, c = c0 + (e - p * gc);
+            if (epi == kUgFilmScale) {
+                pre_a = film[(long long)f * ld_film + c];
+                pre_b = film[(long long)f * ld_film + C + c];
+            } else if (epi == kUgFilmBias) {
+                pre_a = film[(long long)f * ld_film + c];
+            } else if (epi == kUgRes) {
+                pre_a = res[((long long)f * T + p) * C + c];
+            }
+        }
+    }
     __syncthreads();
     const double np = (double)T, n = np * gc;
     // per channel: shifted sums over the T steps (first step as the shift)
@@ -1068,25 +1154,28 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
     // a warp's 32 consecutive elements share a time step when gc % 32 == 0:
     // one shared-memory atomic per warp then, else one per element
     const bool warp_rows = (gc & 31) == 0;
-    for (int e0 = 0; e0 < T * gc; e0 += blockDim.x) {
+    // this CTA's piece of the (group, sample): elements [e_lo, e_hi) in whole
+    // 256-element passes (every CTA of it computed the same statistics)
+    for (int e0 = e_lo; e0 < e_hi; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
         float m = 0.0f;
         int p = 0;
-        if (e < T * gc) {
+        if (e < e_hi) {
             p = e / gc;
             const int cl = e - p * gc, c = c0 + cl;
             const long long i = ((long long)f * T + p) * C + c;
+            const bool first = e0 == e_lo;
             float v = mish_lanes(__fmaf_rn(sx[e], sA[cl], sB[cl]));
-            if (epi == kUgFilmScale) v = __fmaf_rn(ff[c], v, ff[C + c]);
-            else if (epi == kUgFilmBias) v = __fadd_rn(v, ff[c]);
-            else if (epi == kUgRes) v = __fadd_rn(v, res[i]);
+            if (epi == kUgFilmScale) v = __fmaf_rn(first ? pre_a : ff[c], v, first ? pre_b : ff[C + c]);
+            else if (epi == kUgFilmBias) v = __fadd_rn(v, first ? pre_a : ff[c]);
+            else if (epi == kUgRes) v = __fadd_rn(v, first ? pre_a : res[i]);
             out[i] = v;
             m = fabsf(v);
             if (rowmax && !warp_rows) atomicMax(&srm[p], __float_as_uint(m));
         }
-        if (rowmax && warp_rows) {   // every lane takes part (blockDim and T*gc are multiples of 32)
+        if (rowmax && warp_rows) {   // every lane takes part (blockDim, piece and T*gc are multiples of 32)
             m = warp_max_f(m);
-            if ((threadIdx.x & 31) == 0 && e < T * gc) atomicMax(&srm[p], __float_as_uint(m));
+            if ((threadIdx.x & 31) == 0 && e < e_hi) atomicMax(&srm[p], __float_as_uint(m));
         }
     }
     if (rowmax) {
@@ -1109,8 +1198,25 @@ cudaError_t unet_gn(const float* x, int F, int T, int C, int groups, float eps, 
         cudaFuncSetAttribute(unet_gn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         attr = true;
     }
-    const cudaError_t e = launch_k(unet_gn_kernel, dim3((unsigned)groups, (unsigned)F), 256, smem, st, x, T, C, groups,
-                                   eps, scale, bias, epi, film, ld_film, res, out, rowmax);
+    // With out apart from x, each (group, sample) spreads its elementwise
+    // epilogue (Mish and the rest) over up to `pieces` CTAs of one 256-element
+    // pass or more, each recomputing the group's statistics from the whole
+    // tile, until the grid is about two CTAs per SM. In place (out == x) a
+    // piece's writes could reach another CTA's tile before it is read: one CTA.
+    const int n = T * (C / groups);
+    int pieces = 1;
+    if (out != x) {
+        const long long gf = (long long)groups * F;
+        pieces = (n + 255) / 256;
+        const long long cap = (2LL * 148 + gf - 1) / gf;
+        if (pieces > cap) pieces = (int)cap;
+        if (pieces > 64) pieces = 64;
+        if (pieces < 1) pieces = 1;
+    }
+    const int piece = ((n + pieces - 1) / pieces + 255) / 256 * 256;
+    pieces = (n + piece - 1) / piece;
+    const cudaError_t e = launch_k(unet_gn_kernel, dim3((unsigned)groups, (unsigned)F, (unsigned)pieces), 256, smem, st,
+                                   x, T, C, groups, eps, scale, bias, epi, film, ld_film, res, out, rowmax, piece);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -892,10 +892,12 @@ unsigned int* DpPolicy::res_block(const DpResBlockDev& rb, const float* x, const
         }
         resp = d_r_;
     }
+    // conv1 into d_o_ and its GroupNorm out of place into d_h_ (lets unet_gn
+    // spread each group over several CTAs)
     if (e == cudaSuccess)
-        e = im2col_gemm(rb.c1.conv, x, rm_x, B, T, rb.cin, k, 1, k / 2, T, d_h_, nullptr, st);
+        e = im2col_gemm(rb.c1.conv, x, rm_x, B, T, rb.cin, k, 1, k / 2, T, d_o_, nullptr, st);
     if (e == cudaSuccess)
-        e = unet_gn(d_h_, B, T, rb.cout, G, cfg_.gn_eps, rb.c1.gn_s, rb.c1.gn_b,
+        e = unet_gn(d_o_, B, T, rb.cout, G, cfg_.gn_eps, rb.c1.gn_s, rb.c1.gn_b,
                     cfg_.film_scale ? kUgFilmScale : kUgFilmBias, film, film_cols_, nullptr, d_h_, rm_h, st);
     if (e == cudaSuccess)
         e = im2col_gemm(rb.c2.conv, d_h_, rm_h, B, T, rb.cout, k, 1, k / 2, T, d_o_, nullptr, st);
