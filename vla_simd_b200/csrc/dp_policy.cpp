@@ -841,7 +841,6 @@ cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsi
                                   cudaStream_t st) {
     if (l.int8) {
         const long long ldq = round16((long long)k * C);
-        VSB_TRY(im2col1d_q8w(x, B, T, C, k, stride, pad, Tout, rm_x, d_q_, ldq, d_qs_, st));
         GemmI8Args a;
         a.A = d_q_;
         a.lda = ldq;
@@ -862,6 +861,19 @@ cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsi
         a.splitk_ws_elems = ws_main_.elems;
         a.splitk_counters = ws_main_.counters;
         a.splitk_counters_n = ws_main_.n_counters;
+        // the GEMM quantizes the im2col rows itself where it can (one launch
+        // less); else im2col1d_q8w writes them first
+        a.im_x = x;
+        a.im_rowmax = rm_x;
+        a.im_T = T;
+        a.im_C = C;
+        a.im_k = k;
+        a.im_stride = stride;
+        a.im_pad = pad;
+        a.im_Tout = Tout;
+        if (gemm_i8_im2col_supported(a)) return gemm_i8(a, st);
+        a.im_x = nullptr;
+        VSB_TRY(im2col1d_q8w(x, B, T, C, k, stride, pad, Tout, rm_x, d_q_, ldq, d_qs_, st));
         return gemm_i8(a, st);
     }
     VSB_TRY(im2col1d_f32x(x, B, T, C, C, k, stride, pad, Tout, d_colf_, st));

@@ -90,7 +90,86 @@ struct EpiParams {
     float* qscale;
     unsigned int* qamax;
     unsigned int* qsync;
+    // GLOBAL split-K with the A operand computed in the kernel (GemmI8Args::im_x)
+    const float* im_x;
+    const unsigned int* im_rowmax;
+    int im_T, im_C, im_k, im_stride, im_pad, im_Tout;
 };
+
+// quantize_rows' arithmetic (src/hal/common/gemm_i8.cpp:209-244): the row
+// scale s = max(amax / 127, FLT_MIN) (1 for an all-zero row) and the byte of
+// q = clamp(rne(v / s)) from inv = 1 / s
+__device__ __forceinline__ float rowq_scale(float amax) {
+    return amax > 0.0f ? fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN) : 1.0f;
+}
+__device__ __forceinline__ uint32_t rowq_q8(float v, float inv) {
+    float t = __fmul_rn(v, inv);
+    t = t != t ? 0.0f : fminf(fmaxf(t, -127.0f), 127.0f);
+    return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(f2i_rn_small(t))));
+}
+__device__ __forceinline__ uint32_t rowq_pack4(float4 v, float inv) {
+    return rowq_q8(v.x, inv) | (rowq_q8(v.y, inv) << 8) | (rowq_q8(v.z, inv) << 16) | (rowq_q8(v.w, inv) << 24);
+}
+
+// The A operand of a 1D conv computed in the GEMM (the im2col1d_q8w kernel's
+// bytes, without its launch): the 256 epilogue threads (et 0-255, named
+// barrier 2) fill this CTA's k-block stages of the 128-byte-swizzled K-major A
+// ring. Row m = output step ot of sample f (m = f * Tout + ot); K index
+// kt * C + c reads x[f][ot * stride - pad + kt][c] (zero outside the input),
+// quantized with the row's scale from its k input rows' absmax (rowmax), kept
+// in s_sc [M] (also for the epilogue). Stages are filled as the ring frees
+// them (empty), each published with an async-proxy fence and one arrival on
+// full (whose other arrival carries the weight tile's bytes). Rows >= M are
+// left as they are: no output reads their accumulators. Returns false if a
+// wait ran out (recorded in the status word).
+__device__ __forceinline__ bool im2col_fill_a(const EpiParams& p, uint8_t* sA, uint64_t* full, uint64_t* empty,
+                                              int stages, int kb0, int my_kb, float* s_sc, int et) {
+    constexpr int kABytes = kBM * kBK;
+    const int M = p.M, C = p.im_C, T = p.im_T, Tout = p.im_Tout;
+    for (int m = et; m < M; m += 256) {
+        const int f = m / Tout, ot = m - f * Tout;
+        unsigned int mb = 0u;
+        for (int kt = 0; kt < p.im_k; ++kt) {
+            const int t = ot * p.im_stride - p.im_pad + kt;
+            if (t >= 0 && t < T) mb = max(mb, __ldcg(p.im_rowmax + (long long)f * T + t));
+        }
+        s_sc[m] = rowq_scale(__uint_as_float(mb));
+    }
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    const int per_kb = M * (kBK / 16);            // 16-byte chunks of one k-block
+    int i0 = 0;
+    while (i0 < my_kb) {
+        // the ring's first `stages` k-blocks in one sweep (every load in flight), then one at a time
+        const int i1 = i0 == 0 ? min(my_kb, stages) : i0 + 1;
+        if (i0 >= stages && !mbar_wait(&empty[i0 % stages], ((i0 / stages) - 1) & 1)) return false;
+        const int n_items = (i1 - i0) * per_kb;
+        #pragma unroll 4
+        for (int it = et; it < n_items; it += 256) {
+            const int di = it / per_kb, rem = it - di * per_kb;
+            const int m = rem >> 3, j = rem & 7;
+            const int e0 = (kb0 + i0 + di) * kBK + 16 * j;
+            uint4 w = make_uint4(0u, 0u, 0u, 0u);
+            if (e0 < p.K) {
+                const int kt = e0 / C, c = e0 - kt * C;
+                const int f = m / Tout, ot = m - f * Tout;
+                const int t = ot * p.im_stride - p.im_pad + kt;
+                if (t >= 0 && t < T) {
+                    const float4* src = reinterpret_cast<const float4*>(p.im_x + ((long long)f * T + t) * C + c);
+                    const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1), v2 = __ldcg(src + 2), v3 = __ldcg(src + 3);
+                    const float inv = __fdiv_rn(1.0f, s_sc[m]);
+                    w = make_uint4(rowq_pack4(v0, inv), rowq_pack4(v1, inv), rowq_pack4(v2, inv), rowq_pack4(v3, inv));
+                }
+            }
+            *reinterpret_cast<uint4*>(sA + (size_t)((i0 + di) % stages) * kABytes + m * kBK + ((j ^ (m & 7)) << 4)) = w;
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        if (et == 0)
+            for (int i = i0; i < i1; ++i) mbar_arrive(&full[i % stages]);
+        i0 = i1;
+    }
+    return true;
+}
 
 // Output row (index into out / res, and the absmax slot numerator) of tile
 // row r of M tile mt; -1 where the tile row maps to no output.
@@ -564,6 +643,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     volatile int* s_consumed = reinterpret_cast<volatile int*>(tmem_slot + 1);
     unsigned int* s_amax = reinterpret_cast<unsigned int*>(tmem_slot + 2);   // [4]
     volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 6);
+    float* s_imscale = reinterpret_cast<float*>(tmem_slot + 8);              // [kBM], GLOBAL with im_x
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -572,13 +652,14 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int n_tn = (p.N + BN - 1) / BN;
     const int mt = blockIdx.y / n_tn, n0 = (blockIdx.y % n_tn) * BN;
     const int nkb = (p.K + kBK - 1) / kBK;
-    const uint32_t stage_tx = (p.conv_bw ? kBK * p.conv_bw * p.conv_bh : kABytes) + kBBytes;
+    const bool im_a = GLOBAL && p.im_x != nullptr;   // A computed by the epilogue warps
+    const uint32_t stage_tx = (im_a ? 0u : p.conv_bw ? kBK * p.conv_bw * p.conv_bh : kABytes) + kBBytes;
     const int kb0 = static_cast<int>((long long)nkb * rank / splits);
     const int my_kb = static_cast<int>((long long)nkb * (rank + 1) / splits) - kb0;   // >= 1: splits <= nkb
     if (!p.static_weights) pdl_wait();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], im_a ? 2 : 1); mbar_init(&empty[s], 1); }
         mbar_init(acc_full, 1);
         *s_consumed = 0;
         for (int i = 0; i < 4; ++i) s_amax[i] = 0u;
@@ -609,7 +690,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     mbar_arrive_expect_tx(&full[s], stage_tx);
                     tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], (kb0 + i) * kBK, n0);
                 }
-                load_a<kBK>(p, &tmap_a, sA + s * kABytes, &full[s], mt, kb0 + i);
+                if (!im_a) load_a<kBK>(p, &tmap_a, sA + s * kABytes, &full[s], mt, kb0 + i);
                 issued = i + 1;
             }
             if (issued < pre) issued = pre;     // the weight halves went out regardless
@@ -636,6 +717,9 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
         __syncwarp();
     } else {
         pdl_wait();                 // activation scales / residual: predecessor data
+        // the conv input's im2col rows into the A stages (a timeout is recorded;
+        // the MMA warp's bounded waits then end the tile)
+        if (im_a) im2col_fill_a(p, sA, full, empty, stages, kb0, my_kb, s_imscale, threadIdx.x - 64);
         mbar_wait(acc_full, 0);     // a timeout is recorded in the status word
         tc_fence_after();
     }
@@ -787,7 +871,7 @@ w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? rr[e] : 0.0f;
                 }
             }
-            const float as = acc_mode ? 0.0f : row_ascale(p, m);
+            const float as = acc_mode ? 0.0f : im_a ? s_imscale[r] : row_ascale(p, m);
             int4 sum = make_int4(0, 0, 0, 0);
             if (gpre) {
                 sum = j == rsub ? gsum0 : gsum1;
@@ -981,7 +1065,8 @@ constexpr size_t umma_smem_bytes(int bn, int stages, int kbb = kBK) {
 }
 
 constexpr size_t splitk_smem_bytes(int bn, int stages) {
-    return 1024 + (size_t)stages * (kBM * kBK + bn * kBK) + (2 * stages + 1) * 8 + 32;
+    // ring, barriers, then 32 bytes of slots and the rows' im2col scales
+    return 1024 + (size_t)stages * (kBM * kBK + bn * kBK) + (2 * stages + 1) * 8 + 32 + kBM * 4;
 }
 
 // deepest ring that fits (capped at 8 stages)
@@ -1324,6 +1409,14 @@ EpiParams make_epi(const GemmI8Args& a) {
     p.qscale = a.qscale;
     p.qamax = a.qamax;
     p.qsync = a.qsync;
+    p.im_x = a.im_x;
+    p.im_rowmax = a.im_rowmax;
+    p.im_T = a.im_T;
+    p.im_C = a.im_C;
+    p.im_k = a.im_k;
+    p.im_stride = a.im_stride;
+    p.im_pad = a.im_pad;
+    p.im_Tout = a.im_Tout;
     const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out), rb = reinterpret_cast<uintptr_t>(a.res);
     p.vec_ok = !(a.mode & kEpiAcc) && (ob & 15) == 0 && (a.ldo & 3) == 0 &&
                (!a.res || ((rb & 15) == 0 && (a.ldr & 3) == 0));
@@ -1478,8 +1571,37 @@ static cudaError_t gemm_i8_rowq(const GemmI8Args& a, cudaStream_t st) {
     }
 }
 
+// Every N tile's CTAs quantize their own A rows, so the work repeats per N
+// tile: worth the saved launch only for few rows. Measured on the Diffusion
+// Policy U-Net: 16-row convs gain (batch 1: 5.10 -> 4.83 ms a query), 32-row
+// ones lose (13.1 vs 10.1 us per launch), 128-row ones more (6.6 vs 5.9 ms).
+constexpr int kIm2colMaxRows = 16;
+
+static bool im2col_plan(const GemmI8Args& a, GemmPlan* plan) {
+    if (!a.im_x || !a.im_rowmax || a.M > kIm2colMaxRows || a.im_C <= 0 || a.im_C % 16 || a.im_k <= 0 || a.im_T <= 0 || a.im_Tout <= 0 ||
+        a.im_stride <= 0 || a.im_pad < 0 || (long long)a.im_k * a.im_C != a.K || a.M % a.im_Tout ||
+        (a.mode & kEpiAcc) || a.qout || a.force_simt || (reinterpret_cast<uintptr_t>(a.im_x) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.B) & 15) || (a.ldb & 15))
+        return false;
+    *plan = gemm_i8_plan(a.M, a.N, a.K);
+    return gemm_i8_skinny_plan(a, plan) && plan->global;
+}
+
+bool gemm_i8_im2col_supported(const GemmI8Args& a) {
+    GemmPlan plan;
+    return a.M > 0 && a.N > 0 && a.K > 0 && im2col_plan(a, &plan);
+}
+
 cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
+    if (a.im_x) {
+        // the split-K kernel's epilogue warps build A; its map is never read
+        GemmPlan plan;
+        if (!im2col_plan(a, &plan)) return cudaErrorNotSupported;
+        CUtensorMap tb;
+        if (!make_tmap_i8_kmajor(&tb, a.B, a.N, a.K, a.ldb, plan.bn)) return cudaErrorInvalidConfiguration;
+        return gemm_i8_umma(a, tb, tb, plan, st);
+    }
     if (a.qout) return gemm_i8_rowq(a, st);
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
                         (a.lda & 15) == 0 && (a.ldb & 15) == 0;

@@ -57,7 +57,21 @@ struct GemmI8Args {
     float* qscale = nullptr;
     unsigned int* qamax = nullptr;
     unsigned int* qsync = nullptr;
+    // Optional: A is the int8 im2col of a 1D conv input x [F][im_T][im_C],
+    // computed inside the GEMM (the bytes and row scales im2col1d_q8w would
+    // write: row m = output step m % im_Tout of sample m / im_Tout, K index
+    // kt * im_C + c, each row quantized with the scale from its im_k input
+    // rows' absmax in im_rowmax [F * im_T]). A / lda / ascale are then unused.
+    // Only where gemm_i8_im2col_supported says so (else cudaErrorNotSupported).
+    const float* im_x = nullptr;
+    const unsigned int* im_rowmax = nullptr;
+    int im_T = 0, im_C = 0, im_k = 0, im_stride = 1, im_pad = 0, im_Tout = 0;
 };
+
+// Whether gemm_i8 can compute the im2col A operand itself (GemmI8Args::im_x):
+// at most 16 rows, K split across the SMs (the split-K workspace given), im_C
+// a multiple of 16, K == im_k * im_C.
+bool gemm_i8_im2col_supported(const GemmI8Args& a);
 
 // Whether gemm_i8 can write the row-quantized output (GemmI8Args::qout) for
 // this shape on this device: one wave of slab CTAs, N % 32 == 0, K <= 1024.

@@ -47,14 +47,7 @@ constexpr int kSlabStgFloats = 32 * 32;   // one warp's staging tile: 32 rows x 
 // arithmetic, src/hal/common/gemm_i8.cpp:209-244 over the row's N values).
 // The last CTA of the tile to leave (qsync[2 mt + 1]) zeroes the tile's qamax
 // slots and both counters for the next launch.
-__device__ __forceinline__ float rowq_scale(float amax) {
-    return amax > 0.0f ? fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN) : 1.0f;
-}
-__device__ __forceinline__ uint32_t rowq_q8(float v, float inv) {
-    float t = __fmul_rn(v, inv);
-    t = t != t ? 0.0f : fminf(fmaxf(t, -127.0f), 127.0f);
-    return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(f2i_rn_small(t))));
-}
+// (rowq_scale / rowq_q8: gemm_i8.cu)
 
 template <int SL>
 __device__ __forceinline__ void slab_rowq_epilogue(const EpiParams& p, uint64_t* accfull, uint32_t tmem_base,
