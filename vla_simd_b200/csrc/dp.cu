@@ -727,13 +727,17 @@ conv_transpose1d_resident_kernel(const __grid_constant__ CUtensorMap tw, const f
             }
         }
     }
-    // no copy may still be landing when the CTA leaves (after a timeout every
-    // wait is bounded again)
+    // no copy may still be landing when the CTA leaves: after a timeout the
+    // rest are waited for once more, under one more bounded interval
     while (ok && ready < nchunks) {
         if (!mbar_wait(&bars[ready], 0)) ok = false;
-        ++ready;
+        else ++ready;
     }
-    if (!ok) return;
+    if (!ok) {
+        const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+        for (int c = ready; c < nchunks; ++c) mbar_wait_until(&bars[c], 0, deadline);
+        return;
+    }
     #pragma unroll
     for (int i = 0; i < OPT; ++i) {
         const bool valid = ot[i] < Tout && co < Cout;
@@ -874,6 +878,7 @@ conv_transpose1d_batched_kernel(const __grid_constant__ CUtensorMap twt, const f
         // producer: weights are load-time constants, so no wait on the previous kernel
         if (threadIdx.x == NC) {
             tma_prefetch_desc(&twt);
+            int issued = 0;
             for (int g = 0; g < G; ++g) {
                 const int s = g % kBtStages;
                 if (g >= kBtStages && !mbar_wait(&empty[s], ((g / kBtStages) - 1) & 1)) break;
@@ -882,7 +887,13 @@ conv_transpose1d_batched_kernel(const __grid_constant__ CUtensorMap twt, const f
                 for (int b = 0; b < nbox; ++b)
                     tma_load_3d(ring + (size_t)s * stage_bytes + (size_t)b * box_bytes, &twt, &full[s],
                                 c * ci_st + b * kBtBoxCi, k - (p + 1) * stride, co0);
+                issued = g + 1;
             }
+            // the copies still in flight (at most the last kBtStages) land before
+            // this thread, and so the CTA, leaves, even if the consumers gave up
+            const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            for (int g = issued > kBtStages ? issued - kBtStages : 0; g < issued; ++g)
+                mbar_wait_until(&full[g % kBtStages], (g / kBtStages) & 1, deadline);
         }
         return;
     }

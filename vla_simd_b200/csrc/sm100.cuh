@@ -120,6 +120,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// The error path's wait: for a phase to complete or %globaltimer to pass
+// deadline_ns, whichever comes first (nothing more is recorded). Used to let a
+// CTA's own copies land before it leaves after another wait gave up.
+__device__ __forceinline__ void mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() > deadline_ns) return;
+}
+
 // ---------------------------------------------------------------------- TMA --
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
