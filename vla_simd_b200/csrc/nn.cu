@@ -529,9 +529,15 @@ __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc, int src
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __host__ __device__ constexpr size_t att_tiled_smem(int qp, int seq_k) {
     return sizeof(float) * ((size_t)qp * att_row_stride(seq_k) + (size_t)qp * kAttRS + 2 * kAttTK * kAttRS);
+}
+// the same with every K (then V) tile resident at once (kv_all)
+__host__ __device__ constexpr size_t att_tiled_smem_all(int qp, int seq_k) {
+    return sizeof(float) * ((size_t)qp * att_row_stride(seq_k) + (size_t)qp * kAttRS +
+                            (size_t)((seq_k + kAttTK - 1) / kAttTK) * kAttTK * kAttRS);
 }
 
 // Fused row quantization of a finished attention output tile (AttQuant): the
@@ -617,7 +623,7 @@ __global__ void __launch_bounds__(256, 1)
 attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* __restrict__ K, long long ldk,
                        const float* __restrict__ V, long long ldv, float* __restrict__ O, long long ldo,
                        int seq_q, int seq_k, int n_q, int n_kv, float scale, const float* __restrict__ mask,
-                       AttBatch bs, AttQuant qz) {
+                       AttBatch bs, AttQuant qz, int kv_all) {
     VSB_ATT_BATCH_OFFSET(bs);
     constexpr int QP = 8 * QPT;
     constexpr int kTile = kAttTK * kAttRS;
@@ -690,16 +696,29 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         cp_async16(sQ + r * kAttRS + c * 4, Q + (long long)(ok ? q0 + r : 0) * ldq + (long long)h * kAttD + c * 4,
                    ok ? 16 : 0);
     }
-    load_tile(Kh, ldk, 0, sKV);
+    // kv_all (short query tiles, whose per-tile work is too short for a
+    // double buffer to hide the next tile's load): every K tile in one group,
+    // one wait; then every V tile, issued before the softmax
+    if (kv_all) {
+        for (int t = 0; t < ntiles; ++t) load_tile(Kh, ldk, t * kAttTK, sKV + t * kTile);
+    } else {
+        load_tile(Kh, ldk, 0, sKV);
+    }
     cp_async_commit();
+    if (kv_all) {
+        cp_async_wait_all();
+        __syncthreads();
+    }
 
     // ---- scores
     for (int t = 0; t < ntiles; ++t) {
-        const float* cur = sKV + (t & 1) * kTile + (c0 + g) * kAttRS;
-        if (t + 1 < ntiles) load_tile(Kh, ldk, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
-        cp_async_commit();
-        cp_async_wait_prev();           // tile t (and Q) have landed
-        __syncthreads();
+        const float* cur = sKV + (kv_all ? t : (t & 1)) * kTile + (c0 + g) * kAttRS;
+        if (!kv_all) {
+            if (t + 1 < ntiles) load_tile(Kh, ldk, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
+            cp_async_commit();
+            cp_async_wait_prev();       // tile t (and Q) have landed
+            __syncthreads();
+        }
         float acc[QPT][4];
         #pragma unroll
         for (int a = 0; a < QPT; ++a)
@@ -739,9 +758,14 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
                 for (int a = 0; a < QPT; ++a) sS[(r0 + a) * ss + key] = __fmul_rn(acc[a][i], scale);
             }
         }
-        __syncthreads();                // the buffer is refilled two tiles on
+        if (!kv_all) __syncthreads();   // the buffer is refilled two tiles on
     }
-    load_tile(Vh, ldv, 0, sKV);         // V tile 0 streams in during the softmax
+    if (kv_all) {
+        __syncthreads();                // every K read done: V takes its place
+        for (int t = 0; t < ntiles; ++t) load_tile(Vh, ldv, t * kAttTK, sKV + t * kTile);
+    } else {
+        load_tile(Vh, ldv, 0, sKV);     // V tile 0 streams in during the softmax
+    }
     cp_async_commit();
 
     // ---- softmax: warp w takes rows QPT*w + k (k < QPT), processed together
@@ -863,12 +887,18 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
     float o[QPT][2];
     #pragma unroll
     for (int a = 0; a < QPT; ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
+    if (kv_all) {
+        cp_async_wait_all();
+        __syncthreads();                // also: the softmax is done
+    }
     for (int t = 0; t < ntiles; ++t) {
-        const float* cur = sKV + (t & 1) * kTile + d0;
-        if (t + 1 < ntiles) load_tile(Vh, ldv, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
-        cp_async_commit();
-        cp_async_wait_prev();
-        __syncthreads();                // also: the softmax is done before tile 0
+        const float* cur = sKV + (kv_all ? t : (t & 1)) * kTile + d0;
+        if (!kv_all) {
+            if (t + 1 < ntiles) load_tile(Vh, ldv, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
+            cp_async_commit();
+            cp_async_wait_prev();
+            __syncthreads();            // also: the softmax is done before tile 0
+        }
         const int k0 = t * kAttTK;
         const int kn = min(kAttTK, kend - k0);
         const float* prow = sS + r0 * ss + k0;
@@ -900,7 +930,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
                 o[a][1] = __fmaf_rn(pa, vv.y, o[a][1]);
             }
         }
-        __syncthreads();
+        if (!kv_all) __syncthreads();
     }
     #pragma unroll
     for (int a = 0; a < QPT; ++a) {
@@ -917,7 +947,18 @@ cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K
                                    long long ldv, float* O, long long ldo, int seq_q, int seq_k, int n_q, int n_kv,
                                    float scale, const float* mask, const AttBatch& bs, cudaStream_t st,
                                    const AttQuant& qz = AttQuant{}) {
-    const size_t smem = att_tiled_smem(8 * QPT, seq_k);
+    dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q, bs.n);
+    // K / V resident for short query tiles (8-16 rows) when the grid is one
+    // CTA per SM at most (the larger footprint costs no co-residency then)
+    static const int sms = [] {
+        int d = 0, n = 0;
+        cudaGetDevice(&d);
+        return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) == cudaSuccess ? n : 0;
+    }();
+    const long long ctas = (long long)grid.x * grid.y * grid.z;
+    const int kv_all = QPT <= 2 && seq_k > kAttTK && ctas <= sms &&
+                       att_tiled_smem_all(8 * QPT, seq_k) <= 227 * 1024 ? 1 : 0;
+    const size_t smem = kv_all ? att_tiled_smem_all(8 * QPT, seq_k) : att_tiled_smem(8 * QPT, seq_k);
     static int configured = 0;
     if ((int)smem > configured) {
         const cudaError_t e = cudaFuncSetAttribute(attention_tiled_kernel<QPT>,
@@ -925,9 +966,8 @@ cudaError_t launch_attention_tiled(const float* Q, long long ldq, const float* K
         if (e != cudaSuccess) return e;
         configured = (int)smem;
     }
-    dim3 grid((seq_q + 8 * QPT - 1) / (8 * QPT), n_q, bs.n);
     const cudaError_t e = launch_k(attention_tiled_kernel<QPT>, grid, 256, smem, st, Q, ldq, K, ldk, V, ldv, O, ldo,
-                                   seq_q, seq_k, n_q, n_kv, scale, mask, bs, qz);
+                                   seq_q, seq_k, n_q, n_kv, scale, mask, bs, qz, kv_all);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
