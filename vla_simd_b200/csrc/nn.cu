@@ -883,16 +883,27 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         }
     }
 
-    // ---- A*V
-    float o[QPT][2];
+    // ---- A*V. For 32- and 40-row tiles, 128 threads take QPT rows x 4 dims
+    // each (per 4 keys QPT + 4 16-byte loads feed 16*QPT fmas: 0.45 loaded
+    // floats per fma at QPT = 5, against 0.7 for QPT rows x 2 dims over 256
+    // threads); the other threads only load and synchronize. Shorter tiles:
+    // QPT rows x 2 dims over all 256 threads. Keys in order per output either way.
+    constexpr bool kPv4 = QPT >= 4;
+    constexpr int PC = kPv4 ? 4 : 2;
+    const bool pv_on = !kPv4 || tid < 128;
+    const int pr0 = kPv4 ? QPT * (tid >> 4) : r0;
+    const int pd0 = kPv4 ? 4 * (tid & 15) : d0;
+    float o[QPT][PC];
     #pragma unroll
-    for (int a = 0; a < QPT; ++a) { o[a][0] = 0.0f; o[a][1] = 0.0f; }
+    for (int a = 0; a < QPT; ++a)
+        #pragma unroll
+        for (int c = 0; c < PC; ++c) o[a][c] = 0.0f;
     if (kv_all) {
         cp_async_wait_all();
         __syncthreads();                // also: the softmax is done
     }
     for (int t = 0; t < ntiles; ++t) {
-        const float* cur = sKV + (kv_all ? t : (t & 1)) * kTile + d0;
+        const float* cur = sKV + (kv_all ? t : (t & 1)) * kTile + pd0;
         if (!kv_all) {
             if (t + 1 < ntiles) load_tile(Vh, ldv, (t + 1) * kAttTK, sKV + ((t + 1) & 1) * kTile);
             cp_async_commit();
@@ -901,43 +912,59 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         }
         const int k0 = t * kAttTK;
         const int kn = min(kAttTK, kend - k0);
-        const float* prow = sS + r0 * ss + k0;
-        int j = 0;
-        #pragma unroll 2
-        for (; j + 4 <= kn; j += 4) {
-            float4 pv[QPT];
-            float2 vv[4];
-            #pragma unroll
-            for (int a = 0; a < QPT; ++a) pv[a] = *reinterpret_cast<const float4*>(prow + a * ss + j);
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) vv[i] = *reinterpret_cast<const float2*>(cur + (j + i) * kAttRS);
-            // keys j..j+3 in order per output; 2*QPT independent chains per key
-            #pragma unroll
-            for (int i = 0; i < 4; ++i)
+        const float* prow = sS + pr0 * ss + k0;
+        if (pv_on) {
+            int j = 0;
+            #pragma unroll 2
+            for (; j + 4 <= kn; j += 4) {
+                float4 pv[QPT];
+                float vv[4][PC];
+                #pragma unroll
+                for (int a = 0; a < QPT; ++a) pv[a] = *reinterpret_cast<const float4*>(prow + a * ss + j);
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if constexpr (kPv4) {
+                        const float4 v4 = *reinterpret_cast<const float4*>(cur + (j + i) * kAttRS);
+                        vv[i][0] = v4.x; vv[i][1] = v4.y; vv[i][2] = v4.z; vv[i][3] = v4.w;
+                    } else {
+                        const float2 v2 = *reinterpret_cast<const float2*>(cur + (j + i) * kAttRS);
+                        vv[i][0] = v2.x; vv[i][1] = v2.y;
+                    }
+                }
+                // keys j..j+3 in order per output; PC*QPT independent chains per key
+                #pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    #pragma unroll
+                    for (int a = 0; a < QPT; ++a) {
+                        const float pa = i == 0 ? pv[a].x : i == 1 ? pv[a].y : i == 2 ? pv[a].z : pv[a].w;
+                        #pragma unroll
+                        for (int c = 0; c < PC; ++c) o[a][c] = __fmaf_rn(pa, vv[i][c], o[a][c]);
+                    }
+            }
+            for (; j < kn; ++j) {       // ragged tail: exactly seq_k keys enter each chain
+                float vv[PC];
+                #pragma unroll
+                for (int c = 0; c < PC; ++c) vv[c] = cur[j * kAttRS + c];
                 #pragma unroll
                 for (int a = 0; a < QPT; ++a) {
-                    const float pa = i == 0 ? pv[a].x : i == 1 ? pv[a].y : i == 2 ? pv[a].z : pv[a].w;
-                    o[a][0] = __fmaf_rn(pa, vv[i].x, o[a][0]);
-                    o[a][1] = __fmaf_rn(pa, vv[i].y, o[a][1]);
+                    const float pa = prow[a * ss + j];
+                    #pragma unroll
+                    for (int c = 0; c < PC; ++c) o[a][c] = __fmaf_rn(pa, vv[c], o[a][c]);
                 }
-        }
-        for (; j < kn; ++j) {           // ragged tail: exactly seq_k keys enter each chain
-            const float2 vv = *reinterpret_cast<const float2*>(cur + j * kAttRS);
-            #pragma unroll
-            for (int a = 0; a < QPT; ++a) {
-                const float pa = prow[a * ss + j];
-                o[a][0] = __fmaf_rn(pa, vv.x, o[a][0]);
-                o[a][1] = __fmaf_rn(pa, vv.y, o[a][1]);
             }
         }
         if (!kv_all) __syncthreads();
     }
-    #pragma unroll
-    for (int a = 0; a < QPT; ++a) {
-        const int q = q0 + r0 + a;
-        if (q < seq_q)
-            *reinterpret_cast<float2*>(O + (long long)q * ldo + (long long)h * kAttD + d0) =
-                make_float2(o[a][0], o[a][1]);
+    if (pv_on) {
+        #pragma unroll
+        for (int a = 0; a < QPT; ++a) {
+            const int q = q0 + pr0 + a;
+            if (q < seq_q) {
+                float* dst = O + (long long)q * ldo + (long long)h * kAttD + pd0;
+                #pragma unroll
+                for (int c = 0; c < PC; c += 2) *reinterpret_cast<float2*>(dst + c) = make_float2(o[a][c], o[a][c + 1]);
+            }
+        }
     }
     if (qz.q) att_fused_quant<QPT>(O, ldo, q0, seq_q, n_q * kAttD, qz);
 }
