@@ -724,7 +724,7 @@ attention_tiled_kernel(const float* __restrict__ Q, long long ldq, const float* 
         for (int a = 0; a < QPT; ++a)
             #pragma unroll
             for (int i = 0; i < 4; ++i) acc[a][i] = 0.0f;
-        #pragma unroll 2
+        #pragma unroll
         for (int d = 0; d < kAttD; d += 4) {
             float4 qv[QPT], kv[4];
             #pragma unroll
