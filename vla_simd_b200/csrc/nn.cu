@@ -71,14 +71,29 @@ layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const flo
     if (row >= M) return;
     const int H4 = H >> 2;
     const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * H);
-    float4 v[V4];
-    double sum = 0.0;
+    const float4* ar = addend ? reinterpret_cast<const float4*>(addend + (long long)row * H) : nullptr;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* b4 = b ? reinterpret_cast<const float4*>(b) : nullptr;
+    // the row, and (rows of up to 1024: registers allow) the affine / addend
+    // operands of the output pass, all requested up front so their latency
+    // overlaps the two reductions
+    constexpr bool kHoist = V4 <= 8;
+    constexpr int VH = kHoist ? V4 : 1;
+    float4 v[V4], wv[VH], bv[VH], av[VH];
     #pragma unroll
     for (int i = 0; i < V4; ++i) {
         const int g = lane + 32 * i;
-        v[i] = g < H4 ? xr[g] : make_float4(0.f, 0.f, 0.f, 0.f);
-        sum += (double)v[i].x + (double)v[i].y + (double)v[i].z + (double)v[i].w;
+        const bool in = g < H4;
+        v[i] = in ? xr[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (kHoist) {
+            wv[i] = in ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            bv[i] = (in && b4) ? b4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            av[i] = (in && ar) ? ar[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
+    double sum = 0.0;
+    #pragma unroll
+    for (int i = 0; i < V4; ++i) sum += (double)v[i].x + (double)v[i].y + (double)v[i].z + (double)v[i].w;
     const double mean = warp_sum_d(sum) / H;
     double var = 0.0;
     #pragma unroll
@@ -92,17 +107,14 @@ layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const flo
     var = warp_sum_d(var);
     const float inv = (float)(1.0 / sqrt(var / H + (double)eps));
     float4* orow = reinterpret_cast<float4*>(out + (long long)row * H);
-    const float4* ar = addend ? reinterpret_cast<const float4*>(addend + (long long)row * H) : nullptr;
-    const float4* w4 = reinterpret_cast<const float4*>(w);
-    const float4* b4 = b ? reinterpret_cast<const float4*>(b) : nullptr;
     float am1 = 0.0f, am2 = 0.0f;
     float4 a[V4];
     #pragma unroll
     for (int i = 0; i < V4; ++i) {
         const int g = lane + 32 * i;
         if (g < H4) {
-            const float4 ww = w4[g];
-            const float4 bb = b4 ? b4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 ww = kHoist ? wv[i % VH] : w4[g];
+            const float4 bb = kHoist ? bv[i % VH] : (b4 ? b4[g] : make_float4(0.f, 0.f, 0.f, 0.f));
             float* e = reinterpret_cast<float*>(&v[i]);
             const float* we = reinterpret_cast<const float*>(&ww);
             const float* be = reinterpret_cast<const float*>(&bb);
@@ -114,7 +126,7 @@ layernorm_kernel(const float* __restrict__ x, float* __restrict__ out, const flo
             }
             orow[g] = v[i];
             if (ar) {
-                const float4 t = ar[g];
+                const float4 t = kHoist ? av[i % VH] : ar[g];
                 a[i] = make_float4(__fadd_rn(v[i].x, t.x), __fadd_rn(v[i].y, t.y), __fadd_rn(v[i].z, t.z),
                                    __fadd_rn(v[i].w, t.w));
                 am1 = fmaxf(am1, fmaxf(fmaxf(fabsf(a[i].x), fabsf(a[i].y)), fmaxf(fabsf(a[i].z), fabsf(a[i].w))));
