@@ -1111,10 +1111,13 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
         }
     }
     for (int p = threadIdx.x; p < T; p += blockDim.x) srm[p] = 0u;
-    // the first epilogue pass's FiLM / residual operands, loaded now so their
-    // latency overlaps the statistics
+    // the first epilogue pass's FiLM / residual operands and this thread's
+    // first channel's scale and shift, loaded now so their latency overlaps
+    // the statistics
     const int e_lo = blockIdx.z * piece, e_hi = min(T * gc, e_lo + piece);
     float pre_a = 0.0f, pre_b = 0.0f;
+    const float sc0 = threadIdx.x < gc ? scale[c0 + threadIdx.x] : 0.0f;
+    const float bi0 = threadIdx.x < gc ? bias[c0 + threadIdx.x] : 0.0f;
     {
         const int e = e_lo + threadIdx.x;
         if (e < e_hi) {
@@ -1157,8 +1160,10 @@ unet_gn_kernel(const float* x, int T, int C, int groups, float eps, const float*
     const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, n), (double)eps)));
     const double mi = __dmul_rn(mean, inv);
     for (int cl = threadIdx.x; cl < gc; cl += blockDim.x) {
-        sA[cl] = (float)__dmul_rn(inv, (double)scale[c0 + cl]);
-        sB[cl] = (float)__fma_rn(-mi, (double)scale[c0 + cl], (double)bias[c0 + cl]);
+        const float scv = cl == (int)threadIdx.x ? sc0 : scale[c0 + cl];
+        const float biv = cl == (int)threadIdx.x ? bi0 : bias[c0 + cl];
+        sA[cl] = (float)__dmul_rn(inv, (double)scv);
+        sB[cl] = (float)__fma_rn(-mi, (double)scv, (double)biv);
     }
     __syncthreads();
     const float* ff = film ? film + (long long)f * ld_film : nullptr;
