@@ -988,6 +988,75 @@ __global__ void w8a8_simt_kernel(const int8_t* __restrict__ A, long long lda,
     if (p.amax) atomicMax(&p.amax[m / p.amax_rows], __float_as_uint(fabsf(v)));
 }
 
+// A few rows (1-4: the diffusion heads' one-query GEMMs): a warp per output
+// column n, its lanes over 16-byte chunks of the weight row (coalesced) and
+// of each A row, dp4a into int32 (exact: integer sums in any order), a warp
+// reduction, then the same fp32 epilogue. K % 16 == 0, 16-byte aligned rows.
+// The weights are load-time constants when static_weights: requested before
+// the wait on the previous kernel.
+constexpr int kGemvMaxRows = 4;
+
+__global__ void __launch_bounds__(256)
+w8a8_gemv_kernel(const int8_t* __restrict__ A, long long lda, const int8_t* __restrict__ B, long long ldb,
+                 const EpiParams p) {
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const bool live = n < p.N;
+    const int nch = p.K >> 4;                       // 16-byte chunks per row
+    const int4* b = reinterpret_cast<const int4*>(B + (long long)(live ? n : 0) * ldb);
+    // up to 4 chunks per lane (K <= 2048) in registers
+    int4 bw[4];
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = lane + 32 * i;
+        bw[i] = (live && c < nch && p.static_weights) ? b[c] : make_int4(0, 0, 0, 0);
+    }
+    pdl_wait();     // A (and the residual) come from the previous kernel
+    pdl_trigger();
+    if (!p.static_weights) {
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = lane + 32 * i;
+            bw[i] = (live && c < nch) ? b[c] : make_int4(0, 0, 0, 0);
+        }
+    }
+    int32_t acc[kGemvMaxRows];
+    #pragma unroll
+    for (int m = 0; m < kGemvMaxRows; ++m) {
+        acc[m] = 0;
+        if (m >= p.M) continue;
+        const int4* a = reinterpret_cast<const int4*>(A + (long long)m * lda);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nch) {
+                const int4 av = a[c];
+                acc[m] = __dp4a(av.x, bw[i].x, acc[m]);
+                acc[m] = __dp4a(av.y, bw[i].y, acc[m]);
+                acc[m] = __dp4a(av.z, bw[i].z, acc[m]);
+                acc[m] = __dp4a(av.w, bw[i].w, acc[m]);
+            }
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], off);
+    }
+    if (!live || lane >= p.M) return;
+    const int m = lane;
+    int32_t am = acc[0];
+    #pragma unroll
+    for (int i = 1; i < kGemvMaxRows; ++i)
+        if (m == i) am = acc[i];
+    if (p.mode & kEpiAcc) {
+        static_cast<int32_t*>(p.out)[(long long)m * p.ldo + n] = am;
+        return;
+    }
+    const float rv = p.res ? p.res[(long long)m * p.ldr + n] : 0.0f;
+    const float v = epi_value(am, p.wscale[n], p.ascale[(long long)m * p.as_stride], p.bias ? p.bias[n] : 0.0f,
+                              p.mode, &rv);
+    static_cast<float*>(p.out)[(long long)m * p.ldo + n] = v;
+    if (p.amax) atomicMax(&p.amax[m / p.amax_rows], __float_as_uint(fabsf(v)));
+}
+
 // ------------------------------------------------------------- tensor maps
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -1605,6 +1674,13 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.qout) return gemm_i8_rowq(a, st);
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
                         (a.lda & 15) == 0 && (a.ldb & 15) == 0;
+    if (!a.force_simt && tma_ok && a.M <= kGemvMaxRows && a.K % 16 == 0 && a.K <= 2048) {
+        // a few rows: the warp-per-column GEMV (latency: no tensor-core set-up)
+        const EpiParams p = make_epi(a);
+        const cudaError_t le_ = launch_k(w8a8_gemv_kernel, (a.N + 7) / 8, 256, 0, st, a.A, a.lda, a.B, a.ldb, p);
+        if (le_ != cudaSuccess) return le_;
+        return cudaGetLastError();
+    }
     if (!a.force_simt && tma_ok) {
         // operands TMA can describe always take the tensor-core kernels; a tensor
         // map the driver refuses is an error, never a silent detour
