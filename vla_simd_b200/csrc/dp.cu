@@ -1316,23 +1316,45 @@ cudaError_t im2col1d_q8w(const float* x, int F, int T, int C, int k, int stride,
     return cudaGetLastError();
 }
 
-// cat [F*T][C1 + C2] = [a | b] per row, with the row's absmax (float bits) into rowmax.
+// cat [F*T][C1 + C2] = [a | b] per row, with the row's absmax (float bits) into
+// rowmax. Row blockIdx.x, piece blockIdx.y: the pieces stride the row's
+// elements (float4 units when vec4), so a short U-Net row of 4096 channels is
+// one load per thread over several CTAs instead of a serial loop in one. With
+// more than one piece the partial maxima meet by atomicMax (absmax >= 0, so the
+// float bits order as unsigned), which needs the slots zeroed before the
+// launch; max is order-free, so the result is the same as one pass.
 __global__ void __launch_bounds__(256)
 concat_rows_kernel(const float* __restrict__ a, int C1, const float* __restrict__ b, int C2, float* __restrict__ cat,
-                   unsigned int* __restrict__ rowmax) {
+                   unsigned int* __restrict__ rowmax, int vec4) {
     pdl_wait();     // inputs come from earlier kernels in the stream
     pdl_trigger();
     __shared__ float sh[32];
     const long long r = blockIdx.x;
     const int Cc = C1 + C2;
+    const int first = blockIdx.y * blockDim.x + threadIdx.x, step = gridDim.y * blockDim.x;
     float m = 0.0f;
-    for (int c = threadIdx.x; c < Cc; c += blockDim.x) {
-        const float v = c < C1 ? a[r * C1 + c] : b[r * C2 + (c - C1)];
-        cat[r * Cc + c] = v;
-        m = fmaxf(m, fabsf(v));
+    if (vec4) {
+        const int n1 = C1 >> 2, n = Cc >> 2;
+        const float4* a4 = reinterpret_cast<const float4*>(a + r * C1);
+        const float4* b4 = reinterpret_cast<const float4*>(b + r * C2);
+        float4* c4 = reinterpret_cast<float4*>(cat + r * Cc);
+        for (int c = first; c < n; c += step) {
+            const float4 v = c < n1 ? a4[c] : b4[c - n1];
+            c4[c] = v;
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int c = first; c < Cc; c += step) {
+            const float v = c < C1 ? a[r * C1 + c] : b[r * C2 + (c - C1)];
+            cat[r * Cc + c] = v;
+            m = fmaxf(m, fabsf(v));
+        }
     }
     m = block_max_256(m, sh);
-    if (threadIdx.x == 0 && rowmax) rowmax[r] = __float_as_uint(m);
+    if (threadIdx.x == 0 && rowmax) {
+        if (gridDim.y == 1) rowmax[r] = __float_as_uint(m);
+        else atomicMax(rowmax + r, __float_as_uint(m));
+    }
 }
 
 // --------------------------------------------------- cond encoder input
@@ -1527,7 +1549,12 @@ __global__ void spatial_softmax_f_kernel(const float* __restrict__ x, const floa
 cudaError_t concat_channels(const float* a, int C1, const float* b, int C2, float* cat, int F, int T,
                             unsigned int* rowmax, cudaStream_t st) {
     if (F <= 0 || T <= 0 || C1 <= 0 || C2 <= 0 || (long long)F * T > 2147483647LL) return cudaErrorInvalidValue;
-    const cudaError_t e = launch_k(concat_rows_kernel, (unsigned)(F * T), 256, 0, st, a, C1, b, C2, cat, rowmax);
+    const int vec4 = ((C1 | C2) & 3) == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                                                reinterpret_cast<uintptr_t>(cat)) & 15) == 0;
+    const int units = vec4 ? (C1 + C2) / 4 : C1 + C2;
+    const int pieces = (units + 255) / 256 < 65535 ? (units + 255) / 256 : 65535;
+    const cudaError_t e = launch_k(concat_rows_kernel, dim3((unsigned)(F * T), (unsigned)pieces), 256, 0, st, a, C1, b,
+                                   C2, cat, rowmax, vec4);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -39,7 +39,9 @@ cudaError_t im2col1d_f32x(const float* x, int F, int T, int C, long long ldx, in
                           float* colf, cudaStream_t st);
 
 // cat [F][T][C1 + C2] = [a [F][T][C1] | b [F][T][C2]] per time step, with each
-// row's absmax (float bits) into rowmax [F*T] when given.
+// row's absmax (float bits) into rowmax [F*T] when given. Rows longer than 256
+// units (float4 units when C1, C2 and the pointers allow) are split over CTAs
+// that meet by atomicMax: rowmax must be zero before the launch.
 cudaError_t concat_channels(const float* a, int C1, const float* b, int C2, float* cat, int F, int T,
                             unsigned int* rowmax, cudaStream_t st);
 
