@@ -838,11 +838,16 @@ unsigned int* DpPolicy::rm_take(long long n) {
 // rm_out (optional): per-row absmax of the output, for the next conv.
 cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsigned int* rm_x, int B, int T, int C,
                                   int k, int stride, int pad, int Tout, float* out, unsigned int* rm_out,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, bool side) {
+    // side: the residual 1x1 conv on the forked stream, with its own A buffer
+    // and split-K workspace
+    int8_t* q = side ? d_q2_ : d_q_;
+    float* qs = side ? d_qs2_ : d_qs_;
+    const DpSplitWs& ws = side ? ws_side_ : ws_main_;
     if (l.int8) {
         const long long ldq = round16((long long)k * C);
         GemmI8Args a;
-        a.A = d_q_;
+        a.A = q;
         a.lda = ldq;
         a.B = l.Wq;
         a.ldb = l.ldw;
@@ -851,18 +856,20 @@ cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsi
         a.K = l.K;
         a.out = out;
         a.ldo = l.N;
-        a.ascale = d_qs_;
+        a.ascale = qs;
         a.wscale = l.wscale;
         a.bias = l.bias;
         a.amax = rm_out;
         a.amax_rows = 1;
         a.static_weights = true;   // uploaded once at load
-        a.splitk_ws = ws_main_.ws;
-        a.splitk_ws_elems = ws_main_.elems;
-        a.splitk_counters = ws_main_.counters;
-        a.splitk_counters_n = ws_main_.n_counters;
+        a.splitk_ws = ws.ws;
+        a.splitk_ws_elems = ws.elems;
+        a.splitk_counters = ws.counters;
+        a.splitk_counters_n = ws.n_counters;
         // the GEMM quantizes the im2col rows itself where it can (one launch
-        // less); else im2col1d_q8w writes them first
+        // less), except where a few short rows take the GEMV; else
+        // im2col1d_q8w writes them first
+        const bool gemv = gemm_i8_takes_gemv(a);
         a.im_x = x;
         a.im_rowmax = rm_x;
         a.im_T = T;
@@ -871,11 +878,12 @@ cudaError_t DpPolicy::im2col_gemm(const DevLinear& l, const float* x, const unsi
         a.im_stride = stride;
         a.im_pad = pad;
         a.im_Tout = Tout;
-        if (gemm_i8_im2col_supported(a)) return gemm_i8(a, st);
+        if (!gemv && gemm_i8_im2col_supported(a)) return gemm_i8(a, st);
         a.im_x = nullptr;
-        VSB_TRY(im2col1d_q8w(x, B, T, C, k, stride, pad, Tout, rm_x, d_q_, ldq, d_qs_, st));
+        VSB_TRY(im2col1d_q8w(x, B, T, C, k, stride, pad, Tout, rm_x, q, ldq, qs, st));
         return gemm_i8(a, st);
     }
+    if (side) return gemm_rows(l, nullptr, nullptr, x, B * T, out, ws, st);
     VSB_TRY(im2col1d_f32x(x, B, T, C, C, k, stride, pad, Tout, d_colf_, st));
     return gemm_f32(d_colf_, l.K, l.W, l.K, l.bias, out, l.N, nullptr, 0, B * Tout, l.N, l.K, 0, rm_out, 1, st);
 }
@@ -895,13 +903,10 @@ unsigned int* DpPolicy::res_block(const DpResBlockDev& rb, const float* x, const
     if (e == cudaSuccess && rb.has_res) {
         cudaStream_t sd = fork(st);
         if (!sd) e = cudaErrorUnknown;
-        if (e == cudaSuccess && rb.res.int8) {
-            e = quantize_rows(x, rb.cin, nullptr, 0, B * T, rb.cin, d_q2_, round16(rb.cin), d_qs2_, nullptr, 0,
-                              nullptr, sd);
-            if (e == cudaSuccess) e = gemm_rows(rb.res, d_q2_, d_qs2_, nullptr, B * T, d_r_, ws_side_, sd);
-        } else if (e == cudaSuccess) {
-            e = gemm_rows(rb.res, nullptr, nullptr, x, B * T, d_r_, ws_side_, sd);
-        }
+        // a 1x1 conv: the one-tap im2col, whose row scales come from x's
+        // absmax slots (the same per-row quantization as the reference's
+        // Linear over x)
+        if (e == cudaSuccess) e = im2col_gemm(rb.res, x, rm_x, B, T, rb.cin, 1, 1, 0, T, d_r_, nullptr, sd, true);
         resp = d_r_;
     }
     // conv1 into d_o_ and its GroupNorm out of place into d_h_ (lets unet_gn

@@ -163,7 +163,8 @@ class DpPolicy {
     cudaError_t gemm_rows(const DevLinear& l, const int8_t* q, const float* qs, const float* xf, int M, float* out,
                           const DpSplitWs& ws, cudaStream_t st);
     cudaError_t im2col_gemm(const DevLinear& l, const float* x, const unsigned int* rm_x, int B, int T, int C, int k,
-                            int stride, int pad, int Tout, float* out, unsigned int* rm_out, cudaStream_t st);
+                            int stride, int pad, int Tout, float* out, unsigned int* rm_out, cudaStream_t st,
+                            bool side = false);
     unsigned int* rm_take(long long n);
     cudaStream_t fork(cudaStream_t st);
     cudaError_t join(cudaStream_t st);

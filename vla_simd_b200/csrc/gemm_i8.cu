@@ -1656,6 +1656,13 @@ static bool im2col_plan(const GemmI8Args& a, GemmPlan* plan) {
     return gemm_i8_skinny_plan(a, plan) && plan->global;
 }
 
+bool gemm_i8_takes_gemv(const GemmI8Args& a) {
+    const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
+                        (a.lda & 15) == 0 && (a.ldb & 15) == 0;
+    return !a.im_x && !a.qout && !a.force_simt && tma_ok && a.M > 0 && a.M <= kGemvMaxRows && a.K % 16 == 0 &&
+           a.K <= 2048;
+}
+
 bool gemm_i8_im2col_supported(const GemmI8Args& a) {
     GemmPlan plan;
     return a.M > 0 && a.N > 0 && a.K > 0 && im2col_plan(a, &plan);
@@ -1674,7 +1681,7 @@ cudaError_t gemm_i8(const GemmI8Args& a, cudaStream_t st) {
     if (a.qout) return gemm_i8_rowq(a, st);
     const bool tma_ok = ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
                         (a.lda & 15) == 0 && (a.ldb & 15) == 0;
-    if (!a.force_simt && tma_ok && a.M <= kGemvMaxRows && a.K % 16 == 0 && a.K <= 2048) {
+    if (gemm_i8_takes_gemv(a)) {
         // a few rows: the warp-per-column GEMV (latency: no tensor-core set-up)
         const EpiParams p = make_epi(a);
         const cudaError_t le_ = launch_k(w8a8_gemv_kernel, (a.N + 7) / 8, 256, 0, st, a.A, a.lda, a.B, a.ldb, p);

@@ -73,6 +73,11 @@ struct GemmI8Args {
 // a multiple of 16, K == im_k * im_C.
 bool gemm_i8_im2col_supported(const GemmI8Args& a);
 
+// Whether gemm_i8 runs a (with im_x and qout unset) as the warp-per-column
+// GEMV: at most 4 rows, K a multiple of 16 and at most 2048, operands 16-byte
+// aligned.
+bool gemm_i8_takes_gemv(const GemmI8Args& a);
+
 // Whether gemm_i8 can write the row-quantized output (GemmI8Args::qout) for
 // this shape on this device: one wave of slab CTAs, N % 32 == 0, K <= 1024.
 bool gemm_i8_rowq_supported(int M, int N, int K);
