@@ -141,7 +141,21 @@ gn_affine_kernel(const float* __restrict__ x, int npx, int C, long long ld, int 
         const int cl = it % gc, sl = it / gc;
         const double K = (double)xf[cl];
         double s1 = 0.0, s2 = 0.0;
-        for (int p = sl; p < npx; p += nsl) {
+        int p = sl;
+        // eight pixels' loads in flight before their adds (the same order of
+        // additions as one pixel at a time)
+        for (; p + 7 * nsl < npx; p += 8 * nsl) {
+            float v[8];
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = xf[(long long)(p + u * nsl) * ld + cl];
+            #pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const double d = __dsub_rn((double)v[u], K);
+                s1 = __dadd_rn(s1, d);
+                s2 = __fma_rn(d, d, s2);
+            }
+        }
+        for (; p < npx; p += nsl) {
             const double d = __dsub_rn((double)xf[(long long)p * ld + cl], K);
             s1 = __dadd_rn(s1, d);
             s2 = __fma_rn(d, d, s2);
