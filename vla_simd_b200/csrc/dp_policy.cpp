@@ -905,7 +905,7 @@ unsigned int* DpPolicy::res_block(const DpResBlockDev& rb, const float* x, const
         if (!sd) e = cudaErrorUnknown;
         // a 1x1 conv: the one-tap im2col, whose row scales come from x's
         // absmax slots (the same per-row quantization as the reference's
-        // Linear over x)
+        // Linear over x, res.forward in src/models/diffusion/unet1d.cpp:188-191)
         if (e == cudaSuccess) e = im2col_gemm(rb.res, x, rm_x, B, T, rb.cin, 1, 1, 0, T, d_r_, nullptr, sd, true);
         resp = d_r_;
     }
